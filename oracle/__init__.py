@@ -1,0 +1,172 @@
+"""CPU oracle for the WKV-7 ClampW recurrence — TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
+``bench.py`` may import this package, and only as the checker (or as the timed
+CPU baseline).  The ``camoe_b200`` product path never imports it.
+
+Contents:
+
+* ``fwd`` / ``bwd`` — ctypes bindings of ``wkv7_oracle.c`` (a plain-C
+  restatement of ``camoe/backbone.py:264-294`` and of the gradient formulas of
+  ``camoe/cuda/rwkv7_clampw.cu:83-170``), in float64 (ground truth) or float32
+  (reference precision), OpenMP over (batch, head) chains.
+* ``RefOp`` — the reference's own ClampW CUDA op, compiled by
+  ``oracle/Makefile`` from the reference's sources into ``oracle/_ref/``; the
+  GPU parity tests call it with device pointers.
+* ``torch_reference`` — a float64 torch restatement of the same recurrence
+  whose gradients come from autograd; an independent cross-check of ``bwd``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_DIR = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_DIR, "_build", "libwkv7_oracle.so")
+_REF_DIR = os.path.join(_DIR, "_ref")
+
+W_SCALE = -0.6065306597126334  # -exp(-1/2), camoe/backbone.py:20
+
+_lib = None
+
+
+def build(ref: bool = False) -> None:
+    """Compile the oracle (and, with ``ref=True``, the reference op) via make."""
+    targets = ["all"] + (["ref"] if ref else [])
+    subprocess.run(["make", "-s", "-C", _DIR] + targets, check=True)
+
+
+def _load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH):
+        build()
+    lib = ctypes.CDLL(_LIB_PATH)
+    i64, fp, ci = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int
+    for suf in ("f64", "f32"):
+        f = getattr(lib, f"wkv7_oracle_fwd_{suf}")
+        f.argtypes = [i64] * 4 + [fp] * 8 + [ci]
+        f.restype = ci
+        g = getattr(lib, f"wkv7_oracle_bwd_{suf}")
+        g.argtypes = [i64] * 5 + [fp] * 14 + [ci]
+        g.restype = ci
+    lib.wkv7_oracle_decay.argtypes = [ctypes.c_double]
+    lib.wkv7_oracle_decay.restype = ctypes.c_double
+    _lib = lib
+    return lib
+
+
+def _f32(x) -> np.ndarray:
+    if hasattr(x, "detach"):  # torch tensor
+        x = x.detach().float().cpu().numpy()
+    return np.ascontiguousarray(x, dtype=np.float32)
+
+
+def _ptr(x: np.ndarray | None):
+    return None if x is None else x.ctypes.data_as(ctypes.c_void_p)
+
+
+def default_threads() -> int:
+    return max(1, len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count() or 1)
+
+
+def fwd(r, w, k, v, a, b, precision: str = "f64", threads: int | None = None):
+    """Forward recurrence.  Inputs [B,T,H,N] (numpy or torch); returns (y, sa) float32."""
+    r, w, k, v, a, b = (_f32(x) for x in (r, w, k, v, a, b))
+    B, T, H, N = r.shape
+    y = np.empty_like(r)
+    sa = np.empty_like(r)
+    fn = getattr(_load(), f"wkv7_oracle_fwd_{precision}")
+    rc = fn(B, T, H, N, *map(_ptr, (r, w, k, v, a, b, y, sa)), threads or default_threads())
+    if rc != 0:
+        raise RuntimeError(f"oracle forward failed with code {rc}")
+    return y, sa
+
+
+def bwd(r, w, k, v, a, b, dy, dsa=None, precision: str = "f64", ckpt: int = 64,
+        threads: int | None = None):
+    """Exact gradients (dr, dw, dk, dv, da, db) of sum(dy*y) + sum(dsa*sa), float32."""
+    r, w, k, v, a, b, dy = (_f32(x) for x in (r, w, k, v, a, b, dy))
+    dsa = None if dsa is None else _f32(dsa)
+    B, T, H, N = r.shape
+    outs = [np.empty_like(r) for _ in range(6)]
+    fn = getattr(_load(), f"wkv7_oracle_bwd_{precision}")
+    rc = fn(B, T, H, N, ckpt, *map(_ptr, (r, w, k, v, a, b, dy, dsa)), *map(_ptr, outs),
+            threads or default_threads())
+    if rc != 0:
+        raise RuntimeError(f"oracle backward failed with code {rc}")
+    return tuple(outs)
+
+
+def decay(w_in: float) -> float:
+    return _load().wkv7_oracle_decay(float(w_in))
+
+
+def torch_reference(r, w, k, v, a, b, dy=None, dsa=None):
+    """Float64 torch restatement of camoe/backbone.py:264-294 returning (y, sa);
+    with dy given, also the six input gradients from autograd (sa-gradient dsa
+    optional).  Small sizes only: it loops over time in Python."""
+    import torch
+
+    xs = [torch.as_tensor(np.asarray(_f32(x)), dtype=torch.float64).requires_grad_(dy is not None)
+          for x in (r, w, k, v, a, b)]
+    rr, ww, kk, vv, aa, bb = xs
+    B, T, H, N = rr.shape
+    dec = torch.exp(W_SCALE / (1.0 + torch.exp(-ww)))
+    S = torch.zeros(B, H, N, N, dtype=torch.float64)
+    ys, sas = [], []
+    for t in range(T):
+        sa = (S * aa[:, t].unsqueeze(-2)).sum(-1)
+        S = S * dec[:, t].unsqueeze(-2) + sa.unsqueeze(-1) * bb[:, t].unsqueeze(-2) \
+            + vv[:, t].unsqueeze(-1) * kk[:, t].unsqueeze(-2)
+        ys.append((S * rr[:, t].unsqueeze(-2)).sum(-1))
+        sas.append(sa)
+    y = torch.stack(ys, 1)
+    sa = torch.stack(sas, 1)
+    if dy is None:
+        return y.detach().numpy(), sa.detach().numpy()
+    loss = (y * torch.as_tensor(_f32(dy), dtype=torch.float64)).sum()
+    if dsa is not None:
+        loss = loss + (sa * torch.as_tensor(_f32(dsa), dtype=torch.float64)).sum()
+    grads = torch.autograd.grad(loss, xs)
+    return (y.detach().numpy(), sa.detach().numpy()) + tuple(g.numpy() for g in grads)
+
+
+class RefOp:
+    """The reference's ClampW CUDA op (built from its sources into oracle/_ref/),
+    called with device pointers.  It launches on the legacy default stream and
+    validates nothing, so callers synchronise and pass T % 16 == 0."""
+
+    def __init__(self, fp32: bool = False):
+        name = "librwkv7_clampw_ref_fp32.so" if fp32 else "librwkv7_clampw_ref_bf16.so"
+        path = os.path.join(_REF_DIR, name)
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
+        self.lib = ctypes.CDLL(path)
+        ci, fp = ctypes.c_int, ctypes.c_void_p
+        self.lib.ref_clampw_fwd.argtypes = [ci] * 3 + [fp] * 9
+        self.lib.ref_clampw_fwd.restype = ci
+        self.lib.ref_clampw_bwd.argtypes = [ci] * 3 + [fp] * 15
+        self.lib.ref_clampw_bwd.restype = ci
+
+    @staticmethod
+    def available(fp32: bool = False) -> bool:
+        name = "librwkv7_clampw_ref_fp32.so" if fp32 else "librwkv7_clampw_ref_bf16.so"
+        return os.path.exists(os.path.join(_REF_DIR, name))
+
+    def forward(self, r, w, k, v, a, b, y, s, sa):
+        B, T, H, _ = r.shape
+        rc = self.lib.ref_clampw_fwd(B, T, H, *[x.data_ptr() for x in (r, w, k, v, a, b, y, s, sa)])
+        if rc != 0:
+            raise RuntimeError(f"reference forward failed: cuda error {rc}")
+
+    def backward(self, r, w, k, v, a, b, dy, s, sa, dr, dw, dk, dv, da, db):
+        B, T, H, _ = r.shape
+        ptrs = [x.data_ptr() for x in (r, w, k, v, a, b, dy, s, sa, dr, dw, dk, dv, da, db)]
+        rc = self.lib.ref_clampw_bwd(B, T, H, *ptrs)
+        if rc != 0:
+            raise RuntimeError(f"reference backward failed: cuda error {rc}")

@@ -1,0 +1,87 @@
+"""The CPU oracle, pinned against the reference's own recurrence.
+
+The golden vectors were produced by the reference's fallback recurrence
+(camoe/backbone.py:250-294) with torch.autograd gradients
+(tests/golden/make_golden.py).  A second, independent restatement in float64
+torch (oracle.torch_reference) cross-checks the external-sa-gradient path,
+which the reference cannot exercise (its autograd backward drops dsa).
+"""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+from camoe_b200.inputs import make_inputs
+from helpers import GRADS, golden_cases, input_digest, load_golden, nrel
+
+CASES = golden_cases()
+
+
+def test_golden_cases_present():
+    assert len(CASES) >= 5
+
+
+@pytest.mark.parametrize("path", CASES, ids=lambda p: p.split("/")[-1][:-4])
+@pytest.mark.parametrize("precision", ["f64", "f32"])
+def test_oracle_matches_reference_golden(path, precision):
+    z, inp = load_golden(path)
+    assert input_digest(inp) == str(z["input_sha256"]), "input generator drifted"
+    args = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    y, _ = oracle.fwd(*args, precision=precision)
+    grads = oracle.bwd(*args, inp["dy"], precision=precision, ckpt=16)
+    # the golden values are float32 autograd through a float32 loop
+    tol = 2e-5
+    assert nrel(y, z["y"]) < tol
+    for n, g in zip(GRADS, grads):
+        assert nrel(g, z[n]) < tol, n
+
+
+def test_oracle_sa_and_dsa_against_torch_autograd():
+    inp = make_inputs(2, 24, 2, 64, seed=11, with_dsa=True)
+    args = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    ref = oracle.torch_reference(*args, dy=inp["dy"], dsa=inp["dsa"])
+    y, sa = oracle.fwd(*args)
+    grads = oracle.bwd(*args, inp["dy"], inp["dsa"], ckpt=5)
+    assert nrel(y, ref[0]) < 1e-6
+    assert nrel(sa, ref[1]) < 1e-6
+    for n, g, gr in zip(GRADS, grads, ref[2:]):
+        assert nrel(g, gr) < 1e-6, n
+
+
+@pytest.mark.parametrize("ckpt", [1, 3, 16, 64, 1000])
+def test_oracle_checkpoint_interval_does_not_change_gradients(ckpt):
+    inp = make_inputs(1, 50, 1, 64, seed=5, with_dsa=True)
+    args = [inp[n] for n in ("r", "w", "k", "v", "a", "b", "dy", "dsa")]
+    base = oracle.bwd(*args, ckpt=7)
+    other = oracle.bwd(*args, ckpt=ckpt)
+    for g0, g1 in zip(base, other):
+        np.testing.assert_array_equal(g0, g1)
+
+
+def test_oracle_decay_range():
+    # w = exp(-e^{-1/2} sigmoid(x)) lies in (exp(-e^{-1/2}), 1)
+    lo = math.exp(-math.exp(-0.5))
+    assert abs(oracle.decay(0.0) - math.exp(-math.exp(-0.5) / 2)) < 1e-15
+    assert lo < oracle.decay(30.0) < lo + 1e-9
+    assert 1 - 1e-9 < oracle.decay(-30.0) < 1.0
+
+
+def test_oracle_empty_inputs():
+    inp = make_inputs(1, 0, 1, 64, seed=0)
+    args = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    y, sa = oracle.fwd(*args)
+    assert y.shape == (1, 0, 1, 64)
+    grads = oracle.bwd(*args, inp["dy"])
+    assert all(g.shape == (1, 0, 1, 64) for g in grads)
+
+
+def test_oracle_chains_are_independent():
+    # results for (b, h) must not depend on the other chains in the batch
+    inp = make_inputs(2, 32, 3, 64, seed=9)
+    args = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    y, sa = oracle.fwd(*args)
+    one = [x[1:2, :, 2:3].contiguous() for x in args]
+    y1, sa1 = oracle.fwd(*one)
+    np.testing.assert_array_equal(y[1:2, :, 2:3], y1)
+    np.testing.assert_array_equal(sa[1:2, :, 2:3], sa1)
