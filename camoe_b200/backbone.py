@@ -1,0 +1,133 @@
+"""Drop-in replacement for the WKV-7 op section of the reference's
+``camoe/backbone.py`` (lines 14-131).
+
+Same module-level names and call contract:
+
+* ``HEAD_SIZE``, ``CHUNK_LEN``, ``W_SCALE``, ``USE_CUDA``, ``RUN_CUDA_RWKV7``,
+  ``CUDA_KERNEL_EXPECTS_FP32`` (camoe/backbone.py:15-20);
+* ``init_rwkv7_cuda()`` (camoe/backbone.py:22) — loads the prebuilt sm_100a
+  library instead of JIT-compiling, binds ``RUN_CUDA_RWKV7`` and registers the
+  reference's torch ops ``torch.ops.rwkv7_clampw.forward/backward`` with the
+  reference's argument lists (camoe/cuda/rwkv7_clampw.cpp:12-28).  Unlike the
+  reference (camoe/backbone.py:130-131) a failure raises: there is no silent
+  CPU fallback;
+* ``RWKV7_ClampW`` — the autograd Function (camoe/backbone.py:75-102):
+  ``forward(ctx, r, w, k, v, a, b) -> (y, sa)`` with the same assertions, and
+  ``backward(ctx, dy, dsa)``, which takes the gradient of both outputs (the
+  reference's ``backward(ctx, dy)`` cannot be called by autograd for a
+  two-output Function);
+* ``RUN_CUDA_RWKV7(r, w, k, v, a, b)`` on ``[B, T, C]`` tensors returning
+  ``(y, sa)`` in the caller's dtype (camoe/backbone.py:104-121).
+
+Environment flags read by ``init_rwkv7_cuda`` as in the reference:
+``CAMOE_FORCE_FP32_KERNEL=1`` selects fp32 inputs and the fp32-exact scan.
+``CAMOE_DISABLE_FAST_MATH`` is accepted and has no effect (the kernels always
+use accurate ``expf``).  ``CAMOE_WKV7_ALGO`` (auto|scan|chunked) picks the
+algorithm for bf16.
+"""
+from __future__ import annotations
+
+import math
+import os
+
+import torch
+
+from . import _lib, ops
+
+HEAD_SIZE = 64
+CHUNK_LEN = 16
+USE_CUDA = False
+RUN_CUDA_RWKV7 = None
+CUDA_KERNEL_EXPECTS_FP32 = False
+W_SCALE = -math.exp(-0.5)
+
+_ALGO = "auto"
+_TORCH_LIB = None
+
+
+class RWKV7_ClampW(torch.autograd.Function):
+    """y, sa = RWKV7_ClampW.apply(r, w, k, v, a, b) on [B, T, H, 64] tensors."""
+
+    @staticmethod
+    def forward(ctx, r, w, k, v, a, b):
+        B, T, H, C = r.shape
+        assert T % CHUNK_LEN == 0
+        expected_dtype = torch.float32 if CUDA_KERNEL_EXPECTS_FP32 else torch.bfloat16
+        assert all(i.dtype == expected_dtype for i in [r, w, k, v, a, b]), "RWKV7 kernel dtype mismatch"
+        assert all(i.is_contiguous() for i in [r, w, k, v, a, b]), "RWKV7 kernel needs contiguous tensors"
+        needs_ckpt = any(ctx.needs_input_grad)
+        y, sa, ckpt = ops.wkv7_forward(r, w, k, v, a, b, algo=_ALGO, save_ckpt=needs_ckpt)
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(r, w, k, v, a, b, ckpt)
+        return y, sa
+
+    @staticmethod
+    def backward(ctx, dy, dsa):
+        r, w, k, v, a, b, ckpt = ctx.saved_tensors
+        expected_dtype = r.dtype
+        if dy is None:
+            dy = torch.zeros_like(r)
+        assert dy.dtype == expected_dtype, "RWKV7 backward dtype mismatch"
+        dy = dy.contiguous()
+        if dsa is not None:
+            dsa = dsa.to(torch.float32).contiguous()
+        grads = ops.wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, algo=_ALGO)
+        return grads
+
+
+def _run_cuda(r, w, k, v, a, b):
+    B, T, HC = r.shape
+    H = HC // HEAD_SIZE
+    orig_dtype = r.dtype
+    target_dtype = torch.float32 if CUDA_KERNEL_EXPECTS_FP32 else torch.bfloat16
+    r, w, k, v, a, b = [x.to(dtype=target_dtype).contiguous().view(B, T, H, HEAD_SIZE)
+                        for x in [r, w, k, v, a, b]]
+    out, sa = RWKV7_ClampW.apply(r, w, k, v, a, b)
+    out = out.view(B, T, HC).to(orig_dtype)
+    sa = sa.view(B, T, HC).to(orig_dtype)
+    return out, sa
+
+
+def _register_torch_ops():
+    """torch.ops.rwkv7_clampw.forward/backward with the reference's arguments
+    (camoe/cuda/rwkv7_clampw.cpp:12-28): outputs preallocated by the caller and
+    written in place; ``s`` is the [B, H, T/16, 64, 64] fp32 checkpoint tensor
+    the reference allocates (camoe/backbone.py:87), used here as the
+    checkpoint buffer; ``sa`` is not read by backward (states are recomputed)."""
+    global _TORCH_LIB
+    if _TORCH_LIB is not None:
+        return
+    try:
+        lib = torch.library.Library("rwkv7_clampw", "DEF")
+    except RuntimeError:  # namespace already defined (e.g. by the reference extension)
+        return
+    lib.define("forward(Tensor r, Tensor w, Tensor k, Tensor v, Tensor a, Tensor b, "
+               "Tensor(a!) y, Tensor(b!) s, Tensor(c!) sa) -> ()")
+    lib.define("backward(Tensor r, Tensor w, Tensor k, Tensor v, Tensor a, Tensor b, Tensor dy, "
+               "Tensor s, Tensor sa, Tensor(a!) dr, Tensor(b!) dw, Tensor(c!) dk, Tensor(d!) dv, "
+               "Tensor(e!) da, Tensor(f!) db) -> ()")
+
+    def fwd_impl(r, w, k, v, a, b, y, s, sa):
+        ops.wkv7_forward(r, w, k, v, a, b, algo=_ALGO, y=y, sa=sa, ckpt=s.view(torch.uint8))
+
+    def bwd_impl(r, w, k, v, a, b, dy, s, sa, dr, dw, dk, dv, da, db):
+        ops.wkv7_backward(r, w, k, v, a, b, dy, None, s.view(torch.uint8), algo=_ALGO,
+                          grads=(dr, dw, dk, dv, da, db))
+
+    lib.impl("forward", fwd_impl, "CUDA")
+    lib.impl("backward", bwd_impl, "CUDA")
+    _TORCH_LIB = lib
+
+
+def init_rwkv7_cuda():
+    """Load the sm_100a WKV-7 library and bind ``RUN_CUDA_RWKV7``.  Raises on failure."""
+    global USE_CUDA, RUN_CUDA_RWKV7, CUDA_KERNEL_EXPECTS_FP32, _ALGO
+    force_fp32_kernel = os.environ.get("CAMOE_FORCE_FP32_KERNEL", "0") == "1"
+    _ALGO = os.environ.get("CAMOE_WKV7_ALGO", "auto")
+    if _ALGO not in _lib.ALGOS:
+        raise ValueError(f"CAMOE_WKV7_ALGO must be one of {sorted(_lib.ALGOS)}, got {_ALGO!r}")
+    _lib.lib()  # raises ImportError when the library is missing
+    _register_torch_ops()
+    CUDA_KERNEL_EXPECTS_FP32 = force_fp32_kernel
+    RUN_CUDA_RWKV7 = _run_cuda
+    USE_CUDA = True

@@ -1,0 +1,144 @@
+// C ABI of the WKV-7 ClampW operator (declared in include/camoe_wkv7.h):
+// argument validation, algorithm selection and kernel dispatch.  Nothing here
+// allocates or synchronises; every launch goes to the caller's stream.
+#include "camoe_wkv7.h"
+#include "wkv7_common.cuh"
+
+namespace camoe {
+namespace scan {
+template <typename Tin>
+cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream);
+template <typename Tin>
+cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream);
+}  // namespace scan
+namespace chunked {
+cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream);
+cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream);
+size_t ckpt_bytes(int64_t chains, int64_t T);
+}  // namespace chunked
+}  // namespace camoe
+
+namespace {
+
+thread_local int g_last_cuda_error = 0;
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// AUTO -> CHUNKED for bf16, SCAN for fp32; -1 for an invalid combination.
+int resolve_algo(int dtype, int algo) {
+  if (dtype != CAMOE_DTYPE_BF16 && dtype != CAMOE_DTYPE_FP32) return -1;
+  if (algo == CAMOE_ALGO_AUTO) return CAMOE_ALGO_SCAN;
+  if (algo == CAMOE_ALGO_SCAN) return algo;
+  if (algo == CAMOE_ALGO_CHUNKED) return dtype == CAMOE_DTYPE_BF16 ? algo : -1;
+  return -1;
+}
+
+size_t required_ckpt(int64_t B, int64_t T, int64_t hc, int algo) {
+  const int64_t chains = B * hc;
+  if (algo == CAMOE_ALGO_CHUNKED) return camoe::chunked::ckpt_bytes(chains, T);
+  const int64_t nchunk = (T + camoe::kChunk - 1) / camoe::kChunk;
+  return static_cast<size_t>(chains * nchunk) * camoe::kN * camoe::kN * sizeof(float);
+}
+
+int check_geometry(int64_t B, int64_t T, int64_t H, int64_t h0, int64_t hc, int N) {
+  if (N != camoe::kN) return CAMOE_ERR_UNSUPPORTED;
+  if (B < 0 || T < 0 || H < 0 || h0 < 0 || hc < 0 || h0 + hc > H) return CAMOE_ERR_INVALID_ARG;
+  if (B * hc > 0x7fffffffLL) return CAMOE_ERR_INVALID_ARG;  // grid size
+  return CAMOE_OK;
+}
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return CAMOE_OK;
+  g_last_cuda_error = static_cast<int>(e);
+  return CAMOE_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+int camoe_wkv7_version(void) { return 10000; }
+
+const char* camoe_wkv7_strerror(int code) {
+  switch (code) {
+    case CAMOE_OK: return "ok";
+    case CAMOE_ERR_INVALID_ARG: return "invalid argument (null pointer, negative size or head range outside H_total)";
+    case CAMOE_ERR_UNSUPPORTED: return "unsupported configuration (N must be 64; CHUNKED needs bf16)";
+    case CAMOE_ERR_SHAPE: return "unsupported shape";
+    case CAMOE_ERR_ALIGNMENT: return "a pointer is not 16-byte aligned";
+    case CAMOE_ERR_WORKSPACE: return "checkpoint buffer too small (see camoe_wkv7_ckpt_bytes)";
+    case CAMOE_ERR_CUDA: return "CUDA launch failed (see camoe_wkv7_last_cuda_error)";
+    default: return "unknown status code";
+  }
+}
+
+int camoe_wkv7_last_cuda_error(void) { return g_last_cuda_error; }
+
+size_t camoe_wkv7_ckpt_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype, int algo) {
+  const int al = resolve_algo(dtype, algo);
+  if (al < 0 || N != camoe::kN || B < 0 || T < 0 || h_count < 0) return 0;
+  return required_ckpt(B, T, h_count, al);
+}
+
+int camoe_wkv7_fwd(const void* r, const void* w, const void* k, const void* v, const void* a,
+                   const void* b, void* y, float* sa, void* ckpt, size_t ckpt_bytes, int64_t B,
+                   int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
+                   int algo, void* stream) {
+  int st = check_geometry(B, T, H_total, h0, h_count, N);
+  if (st != CAMOE_OK) return st;
+  const int al = resolve_algo(dtype, algo);
+  if (al < 0) return CAMOE_ERR_UNSUPPORTED;
+  if (B * h_count == 0 || T == 0) return CAMOE_OK;
+  const void* ptrs[] = {r, w, k, v, a, b, y, sa};
+  for (const void* p : ptrs) {
+    if (p == nullptr) return CAMOE_ERR_INVALID_ARG;
+    if (!aligned16(p)) return CAMOE_ERR_ALIGNMENT;
+  }
+  if (ckpt != nullptr) {
+    if (!aligned16(ckpt)) return CAMOE_ERR_ALIGNMENT;
+    if (ckpt_bytes < required_ckpt(B, T, h_count, al)) return CAMOE_ERR_WORKSPACE;
+  }
+  camoe::FwdArgs p;
+  p.r = r; p.w = w; p.k = k; p.v = v; p.a = a; p.b = b;
+  p.y = y; p.sa = sa; p.ckpt = static_cast<float*>(ckpt);
+  p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_fwd(p, s));
+  if (dtype == CAMOE_DTYPE_BF16) return cuda_status(camoe::scan::launch_fwd<camoe::bf16>(p, s));
+  return cuda_status(camoe::scan::launch_fwd<float>(p, s));
+}
+
+int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v, const void* a,
+                   const void* b, const void* dy, const float* dsa, const void* ckpt,
+                   size_t ckpt_bytes, void* dr, void* dw, void* dk, void* dv, void* da, void* db,
+                   int64_t B, int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N,
+                   int dtype, int algo, void* stream) {
+  int st = check_geometry(B, T, H_total, h0, h_count, N);
+  if (st != CAMOE_OK) return st;
+  const int al = resolve_algo(dtype, algo);
+  if (al < 0) return CAMOE_ERR_UNSUPPORTED;
+  if (B * h_count == 0 || T == 0) return CAMOE_OK;
+  const void* ptrs[] = {r, w, k, v, a, b, dy, dr, dw, dk, dv, da, db};
+  for (const void* p : ptrs) {
+    if (p == nullptr) return CAMOE_ERR_INVALID_ARG;
+    if (!aligned16(p)) return CAMOE_ERR_ALIGNMENT;
+  }
+  if (dsa != nullptr && !aligned16(dsa)) return CAMOE_ERR_ALIGNMENT;
+  const size_t need = required_ckpt(B, T, h_count, al);
+  if (need > 0) {
+    if (ckpt == nullptr) return CAMOE_ERR_INVALID_ARG;
+    if (!aligned16(ckpt)) return CAMOE_ERR_ALIGNMENT;
+    if (ckpt_bytes < need) return CAMOE_ERR_WORKSPACE;
+  }
+  camoe::BwdArgs p;
+  p.r = r; p.w = w; p.k = k; p.v = v; p.a = a; p.b = b; p.dy = dy;
+  p.dsa = dsa; p.ckpt = static_cast<const float*>(ckpt);
+  p.dr = dr; p.dw = dw; p.dk = dk; p.dv = dv; p.da = da; p.db = db;
+  p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_bwd(p, s));
+  if (dtype == CAMOE_DTYPE_BF16) return cuda_status(camoe::scan::launch_bwd<camoe::bf16>(p, s));
+  return cuda_status(camoe::scan::launch_bwd<float>(p, s));
+}
+
+}  // extern "C"

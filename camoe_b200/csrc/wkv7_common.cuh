@@ -1,0 +1,74 @@
+// Shared definitions of the WKV-7 ClampW kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace camoe {
+
+constexpr int kN = 64;      // head size (state is kN x kN)
+constexpr int kChunk = 16;  // steps per chunk / checkpoint interval
+// -exp(-1/2): the ClampW decay is w = exp(kWScale * sigmoid(w_in)),
+// camoe/cuda/rwkv7_clampw.cu:16,42.
+constexpr float kWScale = -0.6065306597126334f;
+
+using bf16 = __nv_bfloat16;
+
+// Geometry of one call: heads [h0, h0 + hc) of [B, T, H, kN] arrays.
+struct Geom {
+  int64_t B, T, H, h0, hc;
+  int64_t nchunk;  // ceil(T / kChunk)
+  __host__ __device__ int64_t chains() const { return B * hc; }
+  // offset of element (t, i) of chain `ch`
+  __device__ __forceinline__ int64_t off(int64_t ch, int64_t t, int i) const {
+    const int64_t b = ch / hc, h = h0 + ch % hc;
+    return ((b * T + t) * H + h) * kN + i;
+  }
+  // stride between consecutive time steps of one chain, in elements
+  __host__ __device__ int64_t tstride() const { return H * kN; }
+};
+
+struct FwdArgs {
+  const void *r, *w, *k, *v, *a, *b;
+  void* y;
+  float* sa;
+  float* ckpt;  // may be null
+  Geom g;
+};
+
+struct BwdArgs {
+  const void *r, *w, *k, *v, *a, *b, *dy;
+  const float* dsa;   // may be null
+  const float* ckpt;  // written by the matching forward
+  void *dr, *dw, *dk, *dv, *da, *db;
+  Geom g;
+};
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(bf16 x) { return __bfloat162float(x); }
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ bf16 from_f32<bf16>(float x) { return __float2bfloat16_rn(x); }
+
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// ---- cp.async (16-byte, L2-only) helpers ----------------------------------
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  const int n = pred ? 16 : 0;  // n == 0 zero-fills the destination
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+}  // namespace camoe

@@ -1,0 +1,109 @@
+"""Torch-level calls of the WKV-7 ClampW C ABI.
+
+These functions take [B, T, H, 64] CUDA tensors, allocate the outputs with
+torch (the C ABI itself allocates nothing) and launch on the current CUDA
+stream.  Heads [h0, h0 + h_count) of the given tensors are processed in
+place; the rest of the outputs is left unwritten (zero-filled when
+``zero_rest`` is set), which is how the multi-GPU launcher shards heads
+without copies.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import ALGO_AUTO, ALGOS, DTYPE_BF16, DTYPE_FP32, check
+
+HEAD_SIZE = 64
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return DTYPE_BF16
+    if dt == torch.float32:
+        return DTYPE_FP32
+    raise TypeError(f"WKV-7 op supports bfloat16 and float32 inputs, got {dt}")
+
+
+def algo_code(algo) -> int:
+    if isinstance(algo, str):
+        return ALGOS[algo]
+    return int(algo)
+
+
+def _check_inputs(xs, names):
+    ref = xs[0]
+    if ref.dim() != 4 or ref.shape[-1] != HEAD_SIZE:
+        raise ValueError(f"expected [B, T, H, {HEAD_SIZE}] tensors, got {tuple(ref.shape)}")
+    for x, n in zip(xs, names):
+        if not x.is_cuda:
+            raise ValueError(f"{n} must be a CUDA tensor (the op has no CPU path)")
+        if x.shape != ref.shape:
+            raise ValueError(f"{n} has shape {tuple(x.shape)}, expected {tuple(ref.shape)}")
+        if x.dtype != ref.dtype:
+            raise TypeError(f"{n} has dtype {x.dtype}, expected {ref.dtype}")
+        if not x.is_contiguous():
+            raise ValueError(f"{n} must be contiguous")
+        if x.device != ref.device:
+            raise ValueError(f"{n} is on {x.device}, expected {ref.device}")
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ckpt_bytes(B: int, T: int, h_count: int, dtype: torch.dtype, algo="auto") -> int:
+    return int(_lib.lib().camoe_wkv7_ckpt_bytes(B, T, h_count, HEAD_SIZE, dtype_code(dtype),
+                                                algo_code(algo)))
+
+
+def wkv7_forward(r, w, k, v, a, b, *, algo="auto", save_ckpt: bool = True, h0: int = 0,
+                 h_count: int | None = None, y=None, sa=None, ckpt=None, zero_rest=False):
+    """Forward.  Returns (y, sa, ckpt); ckpt is None when save_ckpt is False."""
+    _check_inputs((r, w, k, v, a, b), "rwkvab")
+    B, T, H, N = r.shape
+    hc = H - h0 if h_count is None else h_count
+    alloc = torch.zeros if zero_rest else torch.empty
+    if y is None:
+        y = alloc(B, T, H, N, dtype=r.dtype, device=r.device)
+    if sa is None:
+        sa = alloc(B, T, H, N, dtype=torch.float32, device=r.device)
+    nbytes = 0
+    if save_ckpt:
+        nbytes = ckpt_bytes(B, T, hc, r.dtype, algo)
+        if ckpt is None:
+            ckpt = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=r.device)
+        else:
+            nbytes = ckpt.numel() * ckpt.element_size()
+    else:
+        ckpt = None
+    st = _lib.lib().camoe_wkv7_fwd(
+        r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(),
+        y.data_ptr(), sa.data_ptr(), None if ckpt is None else ckpt.data_ptr(), nbytes,
+        B, T, H, h0, hc, N, dtype_code(r.dtype), algo_code(algo), _stream_ptr(r.device))
+    check(st)
+    return y, sa, ckpt
+
+
+def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
+                  h_count: int | None = None, grads=None, zero_rest=False):
+    """Backward.  ``dsa`` (fp32) may be None.  Returns (dr, dw, dk, dv, da, db)."""
+    _check_inputs((r, w, k, v, a, b, dy), "rwkvab" + "y")
+    B, T, H, N = r.shape
+    hc = H - h0 if h_count is None else h_count
+    if dsa is not None:
+        if dsa.dtype != torch.float32 or dsa.shape != r.shape or not dsa.is_contiguous() \
+                or dsa.device != r.device:
+            raise ValueError("dsa must be a contiguous float32 tensor shaped like the inputs")
+    if grads is None:
+        alloc = torch.zeros if zero_rest else torch.empty
+        grads = tuple(alloc(B, T, H, N, dtype=r.dtype, device=r.device) for _ in range(6))
+    nbytes = 0 if ckpt is None else ckpt.numel() * ckpt.element_size()
+    st = _lib.lib().camoe_wkv7_bwd(
+        r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(),
+        dy.data_ptr(), None if dsa is None else dsa.data_ptr(),
+        None if ckpt is None else ckpt.data_ptr(), nbytes,
+        *(g.data_ptr() for g in grads), B, T, H, h0, hc, N, dtype_code(r.dtype),
+        algo_code(algo), _stream_ptr(r.device))
+    check(st)
+    return grads

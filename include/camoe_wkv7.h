@@ -1,0 +1,104 @@
+/*
+ * camoe_wkv7.h — C ABI of the B200 (sm_100a) WKV-7 "ClampW" operator.
+ *
+ * The operator computes, independently for every (batch b, head h) chain,
+ *     w_t  = exp(-exp(-1/2) * sigmoid(w_in_t))            (per element)
+ *     sa_t = S_{t-1} a_t
+ *     S_t  = S_{t-1} diag(w_t) + sa_t b_t^T + v_t k_t^T    (S_{-1} = 0, N x N, fp32)
+ *     y_t  = S_t r_t
+ * and the gradients of sum(dy*y) + sum(dsa*sa) with respect to r, w_in, k,
+ * v, a and b.
+ *
+ * Every tensor argument is a [B, T, H_total, N] contiguous array (element
+ * ((b*T + t)*H_total + h)*N + i), N = 64.  A call processes the heads
+ * [h0, h0 + h_count) of those arrays in place, so a head-sharded launcher
+ * passes slices without copies.  r, w, k, v, a, b, y, dy and the six
+ * gradients have the element type `dtype` (bf16 or fp32); sa and dsa are
+ * always fp32.  The caller owns every buffer; nothing is allocated.  All
+ * pointers must be 16-byte aligned device pointers.
+ *
+ * The forward writes a per-chain state checkpoint that the backward reads.
+ * Its size comes from camoe_wkv7_ckpt_bytes(); it never exceeds the
+ * reference's [B, H, T/16, N, N] fp32 checkpoint tensor, so that tensor can
+ * be passed as the buffer.  The forward and backward of one pair must use
+ * the same dtype, algo and shape.  Passing ckpt = NULL to the forward skips
+ * the checkpoint (inference).
+ *
+ * Calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy default
+ * stream), keep no global state and may run concurrently on different
+ * streams.  They return CAMOE_OK or an error code; no call aborts or traps.
+ *
+ * Reference interfaces these replace:
+ *   torch.ops.rwkv7_clampw.forward(r,w,k,v,a,b,y,s,sa)
+ *       camoe/cuda/rwkv7_clampw.cpp:12-15, launcher rwkv7_clampw.cu:76-79
+ *   torch.ops.rwkv7_clampw.backward(r,w,k,v,a,b,dy,s,sa,dr,dw,dk,dv,da,db)
+ *       camoe/cuda/rwkv7_clampw.cpp:19-23, launcher rwkv7_clampw.cu:172-176
+ *   checkpoint tensor s = empty(B, H, T/16, N, N, fp32)   camoe/backbone.py:87
+ */
+#ifndef CAMOE_WKV7_H
+#define CAMOE_WKV7_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define CAMOE_DTYPE_BF16 0
+#define CAMOE_DTYPE_FP32 1
+
+/* algorithms: AUTO = CHUNKED for bf16, SCAN for fp32 */
+#define CAMOE_ALGO_AUTO 0
+#define CAMOE_ALGO_SCAN 1    /* per-step fp32 SIMT scan, the fp32-exact path */
+#define CAMOE_ALGO_CHUNKED 2 /* 16-step chunks on the tensor cores, bf16 only */
+
+/* status codes */
+#define CAMOE_OK 0
+#define CAMOE_ERR_INVALID_ARG 1  /* NULL required pointer, negative size, bad head range */
+#define CAMOE_ERR_UNSUPPORTED 2  /* N != 64, unknown dtype/algo, fp32 with CHUNKED */
+#define CAMOE_ERR_SHAPE 3        /* T not a multiple of 16 */
+#define CAMOE_ERR_ALIGNMENT 4    /* a pointer is not 16-byte aligned */
+#define CAMOE_ERR_WORKSPACE 5    /* ckpt_bytes smaller than camoe_wkv7_ckpt_bytes() */
+#define CAMOE_ERR_CUDA 6         /* a CUDA launch failed; see camoe_wkv7_last_cuda_error() */
+
+/* Version of this ABI (major*10000 + minor*100 + patch). */
+int camoe_wkv7_version(void);
+
+/* Static description of a status code. */
+const char* camoe_wkv7_strerror(int code);
+
+/* The cudaError_t of the most recent CAMOE_ERR_CUDA on the calling thread. */
+int camoe_wkv7_last_cuda_error(void);
+
+/* Bytes of state checkpoint a forward/backward pair needs for B x h_count
+ * chains of length T (0 when there is nothing to store).  Returns 0 for
+ * invalid arguments as well; the fwd/bwd calls report those. */
+size_t camoe_wkv7_ckpt_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype,
+                             int algo);
+
+/* Forward.  Writes y (dtype) and sa (fp32) for heads [h0, h0+h_count) and,
+ * when ckpt != NULL, the state checkpoint.  Replaces
+ * torch.ops.rwkv7_clampw.forward (camoe/cuda/rwkv7_clampw.cpp:12-15). */
+int camoe_wkv7_fwd(const void* r, const void* w, const void* k, const void* v,
+                   const void* a, const void* b, void* y, float* sa, void* ckpt,
+                   size_t ckpt_bytes, int64_t B, int64_t T, int64_t H_total, int64_t h0,
+                   int64_t h_count, int N, int dtype, int algo, void* stream);
+
+/* Backward.  Reads the checkpoint written by the matching forward, dy
+ * (dtype) and, when non-NULL, dsa (fp32, the gradient of sa); writes the six
+ * input gradients (dtype).  Replaces torch.ops.rwkv7_clampw.backward
+ * (camoe/cuda/rwkv7_clampw.cpp:19-23), whose autograd wrapper took no sa
+ * gradient (camoe/backbone.py:95). */
+int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v,
+                   const void* a, const void* b, const void* dy, const float* dsa,
+                   const void* ckpt, size_t ckpt_bytes, void* dr, void* dw, void* dk,
+                   void* dv, void* da, void* db, int64_t B, int64_t T, int64_t H_total,
+                   int64_t h0, int64_t h_count, int N, int dtype, int algo, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CAMOE_WKV7_H */

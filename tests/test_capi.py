@@ -1,0 +1,101 @@
+"""C ABI checks that need no GPU: the library loads, exports every function
+the header declares, and rejects bad arguments before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from camoe_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "camoe_wkv7.h")
+
+
+def header_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(camoe_wkv7_\w+)\s*\(", src)))
+
+
+def test_header_declares_expected_entry_points():
+    names = header_functions()
+    for n in _lib.EXPORTS:
+        assert n in names
+
+
+def test_library_exports_every_header_function():
+    lib = _lib.lib()
+    for name in header_functions():
+        assert hasattr(lib, name), name
+
+
+def test_version_and_strerror():
+    lib = _lib.lib()
+    assert lib.camoe_wkv7_version() >= 10000
+    for code in range(7):
+        assert lib.camoe_wkv7_strerror(code)
+    assert b"unknown" in lib.camoe_wkv7_strerror(99)
+
+
+def test_ckpt_bytes_fits_the_reference_checkpoint_tensor():
+    lib = _lib.lib()
+    for dtype in (_lib.DTYPE_BF16, _lib.DTYPE_FP32):
+        for algo in (_lib.ALGO_AUTO, _lib.ALGO_SCAN, _lib.ALGO_CHUNKED):
+            if dtype == _lib.DTYPE_FP32 and algo == _lib.ALGO_CHUNKED:
+                assert lib.camoe_wkv7_ckpt_bytes(4, 4096, 16, 64, dtype, algo) == 0
+                continue
+            for B, T, H in ((1, 64, 2), (8, 1024, 16), (4, 4096, 16), (2, 65536, 32)):
+                got = lib.camoe_wkv7_ckpt_bytes(B, T, H, 64, dtype, algo)
+                ref = B * H * (T // 16) * 64 * 64 * 4  # camoe/backbone.py:87
+                assert 0 < got <= ref
+    assert lib.camoe_wkv7_ckpt_bytes(1, 64, 1, 32, 0, 0) == 0   # N != 64
+    assert lib.camoe_wkv7_ckpt_bytes(1, 64, 1, 64, 7, 0) == 0   # bad dtype
+    assert lib.camoe_wkv7_ckpt_bytes(0, 64, 1, 64, 0, 0) == 0   # empty
+
+
+def _fwd(B=1, T=16, H=1, h0=0, hc=1, N=64, dtype=0, algo=0, ptr=16, ckpt=None, nbytes=0):
+    lib = _lib.lib()
+    p = ctypes.c_void_p(ptr)
+    return lib.camoe_wkv7_fwd(p, p, p, p, p, p, p, p, ckpt, nbytes, B, T, H, h0, hc, N,
+                              dtype, algo, None)
+
+
+def test_fwd_argument_errors_need_no_device():
+    assert _fwd(N=32) == _lib.ERR_UNSUPPORTED
+    assert _fwd(B=-1) == _lib.ERR_INVALID_ARG
+    assert _fwd(H=2, h0=1, hc=2) == _lib.ERR_INVALID_ARG     # head range past H_total
+    assert _fwd(dtype=5) == _lib.ERR_UNSUPPORTED
+    assert _fwd(dtype=1, algo=2) == _lib.ERR_UNSUPPORTED     # chunked is bf16 only
+    assert _fwd(algo=9) == _lib.ERR_UNSUPPORTED
+    assert _fwd(ptr=0) == _lib.ERR_INVALID_ARG               # null pointers
+    assert _fwd(ptr=24) == _lib.ERR_ALIGNMENT                # 8-byte aligned only
+    assert _fwd(ckpt=ctypes.c_void_p(16), nbytes=10) == _lib.ERR_WORKSPACE
+    # empty work returns before any device call
+    assert _fwd(B=0) == _lib.OK
+    assert _fwd(T=0) == _lib.OK
+    assert _fwd(hc=0) == _lib.OK
+
+
+def test_bwd_argument_errors_need_no_device():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+
+    def bwd(ckpt=p, nbytes=1 << 40, dsa=None, **kw):
+        g = dict(B=1, T=32, H=1, h0=0, hc=1, N=64, dtype=0, algo=0)
+        g.update(kw)
+        return lib.camoe_wkv7_bwd(p, p, p, p, p, p, p, dsa, ckpt, nbytes, p, p, p, p, p, p,
+                                  g["B"], g["T"], g["H"], g["h0"], g["hc"], g["N"], g["dtype"],
+                                  g["algo"], None)
+
+    assert bwd(ckpt=None) == _lib.ERR_INVALID_ARG
+    assert bwd(nbytes=100) == _lib.ERR_WORKSPACE
+    assert bwd(dsa=ctypes.c_void_p(20)) == _lib.ERR_ALIGNMENT
+    assert bwd(N=128) == _lib.ERR_UNSUPPORTED
+    assert bwd(B=0) == _lib.OK
+
+
+def test_error_raises_camoe_error():
+    with pytest.raises(_lib.CamoeError) as ei:
+        _lib.check(_lib.ERR_ALIGNMENT)
+    assert ei.value.status == _lib.ERR_ALIGNMENT
