@@ -27,7 +27,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // AUTO -> CHUNKED for bf16, SCAN for fp32; -1 for an invalid combination.
 int resolve_algo(int dtype, int algo) {
   if (dtype != CAMOE_DTYPE_BF16 && dtype != CAMOE_DTYPE_FP32) return -1;
-  if (algo == CAMOE_ALGO_AUTO) return CAMOE_ALGO_SCAN;
+  if (algo == CAMOE_ALGO_AUTO) return dtype == CAMOE_DTYPE_BF16 ? CAMOE_ALGO_CHUNKED : CAMOE_ALGO_SCAN;
   if (algo == CAMOE_ALGO_SCAN) return algo;
   if (algo == CAMOE_ALGO_CHUNKED) return dtype == CAMOE_DTYPE_BF16 ? algo : -1;
   return -1;

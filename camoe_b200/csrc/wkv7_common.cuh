@@ -25,6 +25,11 @@ struct Geom {
     const int64_t b = ch / hc, h = h0 + ch % hc;
     return ((b * T + t) * H + h) * kN + i;
   }
+  // offset of element (0, 0) of chain `ch`; element (t, i) is at base + t * tstride() + i
+  __device__ __forceinline__ int64_t base(int64_t ch) const {
+    const int64_t b = ch / hc, h = h0 + ch % hc;
+    return (b * T * H + h) * kN;
+  }
   // stride between consecutive time steps of one chain, in elements
   __host__ __device__ int64_t tstride() const { return H * kN; }
 };
