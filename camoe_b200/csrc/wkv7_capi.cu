@@ -55,6 +55,12 @@ int cuda_status(cudaError_t e) {
 
 }  // namespace
 
+namespace camoe {
+// lets other translation units of the library report a CUDA error through
+// camoe_wkv7_last_cuda_error()
+void set_last_cuda_error(int e) { g_last_cuda_error = e; }
+}  // namespace camoe
+
 extern "C" {
 
 int camoe_wkv7_version(void) { return 10000; }

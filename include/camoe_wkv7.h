@@ -25,8 +25,9 @@
  * the checkpoint (inference).
  *
  * Calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy default
- * stream), keep no global state and may run concurrently on different
- * streams.  They return CAMOE_OK or an error code; no call aborts or traps.
+ * stream); all but camoe_wkv7_fwd_bwd_noalloc keep no global state and may
+ * run concurrently on different streams.  They return CAMOE_OK or an error
+ * code; no call aborts or traps.
  *
  * Reference interfaces these replace:
  *   torch.ops.rwkv7_clampw.forward(r,w,k,v,a,b,y,s,sa)
@@ -96,6 +97,29 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v,
                    const void* ckpt, size_t ckpt_bytes, void* dr, void* dw, void* dk,
                    void* dv, void* da, void* db, int64_t B, int64_t T, int64_t H_total,
                    int64_t h0, int64_t h_count, int N, int dtype, int algo, void* stream);
+
+/* Size of the library-owned checkpoint scratch used by
+ * camoe_wkv7_fwd_bwd_noalloc (64 MiB per GPU that loads the library). */
+#define CAMOE_WKV7_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+
+/* Forward and backward in one call that allocates nothing, for callers that
+ * cannot allocate device memory (a host whose device memory belongs to
+ * another runtime's pooled allocator, or a training step that must not let
+ * cudaMalloc synchronise the device).  No counterpart in the reference.
+ * Writes y, sa and the six gradients like camoe_wkv7_fwd followed by
+ * camoe_wkv7_bwd, with the state checkpoint kept in a library-owned device
+ * array of CAMOE_WKV7_NOALLOC_SCRATCH_BYTES instead of a caller buffer.
+ * Returns CAMOE_ERR_WORKSPACE when camoe_wkv7_ckpt_bytes() of the problem
+ * exceeds that size (e.g. at most 4096 chains x 16-step chunks).  The first
+ * call on a device looks up the array's address (cudaGetSymbolAddress); make
+ * it before any stream capture.  All calls share the array: calls whose work
+ * overlaps on the GPU race. */
+int camoe_wkv7_fwd_bwd_noalloc(const void* r, const void* w, const void* k, const void* v,
+                               const void* a, const void* b, const void* dy, const float* dsa,
+                               void* y, float* sa, void* dr, void* dw, void* dk, void* dv,
+                               void* da, void* db, int64_t B, int64_t T, int64_t H_total,
+                               int64_t h0, int64_t h_count, int N, int dtype, int algo,
+                               void* stream);
 
 #ifdef __cplusplus
 }
