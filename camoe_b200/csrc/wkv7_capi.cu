@@ -12,6 +12,7 @@ template <typename Tin>
 cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream);
 }  // namespace scan
 namespace chunked {
+unsigned int fwd_timeouts();
 cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream);
 size_t ckpt_bytes(int64_t chains, int64_t T);
@@ -79,6 +80,11 @@ const char* camoe_wkv7_strerror(int code) {
 }
 
 int camoe_wkv7_last_cuda_error(void) { return g_last_cuda_error; }
+
+unsigned int camoe_wkv7_device_errors(void) {
+  const unsigned int a = camoe::chunked::fwd_timeouts();
+  return a;
+}
 
 size_t camoe_wkv7_ckpt_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype, int algo) {
   const int al = resolve_algo(dtype, algo);

@@ -266,117 +266,12 @@ __device__ __forceinline__ void keyside_forward(KeySide& ks, const bf16 (*raw)[L
   __syncthreads();
 }
 
-// checkpoint slot of chunk c (state at the chunk's start), fragment order:
-// float4 index ((warp * 8 + ntile) * 32 + lane)
-__device__ __forceinline__ float4* ckpt_slot(float* base, int64_t ch, int64_t nchunk, int64_t c) {
-  return reinterpret_cast<float4*>(base + (ch * nchunk + c) * (kN * kN));
-}
-
-__global__ void __launch_bounds__(kThreads) chunked_fwd_kernel(FwdArgs p) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  FwdSmem& sm = *reinterpret_cast<FwdSmem*>(smem_raw);
-  KeySide& ks = sm.ks;
-  const int tid = threadIdx.x, lane = tid & 31, wq = tid >> 5;
-  const int g = lane >> 2, q = lane & 3;
-  const int64_t ch = blockIdx.x;
-  const int64_t nchunk = p.g.nchunk, T = p.g.T, ts = p.g.tstride();
-  const int64_t cbase = p.g.base(ch);
-  const int i0 = 16 * wq;
-  auto get = [&](int t) { return in_ptr(p, t); };
-
-  float S[8][4];
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
-
-#pragma unroll
-  for (int s = 0; s < NST - 1; ++s) {
-    if (s < nchunk) issue_tiles(sm.raw[s], kNumIn, get, cbase, ts, T, s, tid, kThreads);
-    cp_async_commit();
-  }
-  for (int64_t c = 0; c < nchunk; ++c) {
-    const int st = c % NST;
-    if (c + NST - 1 < nchunk)
-      issue_tiles(sm.raw[(c + NST - 1) % NST], kNumIn, get, cbase, ts, T, c + NST - 1, tid, kThreads);
-    cp_async_commit();
-    cp_async_wait<NST - 1>();
-    __syncthreads();
-    keyside_forward(ks, sm.raw[st], tid, wq, lane);
-
-    if (p.ckpt != nullptr && c > 0) {
-      float4* dst = ckpt_slot(p.ckpt, ch, nchunk, c);
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-        dst[(wq * 8 + nt) * 32 + lane] = make_float4(S[nt][0], S[nt][1], S[nt][2], S[nt][3]);
-    }
-
-    uint32_t sA[4][4], vA[4], b[4];
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) acc_to_a(sA[kk], S[2 * kk], S[2 * kk + 1]);
-    lda_colmajor(vA, &sm.raw[st][IN_V][0][0], LD, i0, 0, lane);
-    float sa[2][4] = {}, yv[2][4] = {};
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      ldb_nk(b, &ks.W[0][0], LD, 0, 16 * kk, lane);
-      mma16816(sa[0], sA[kk], b[0], b[1]);
-      mma16816(sa[1], sA[kk], b[2], b[3]);
-      ldb_nk(b, &ks.Qy[0][0], LD, 0, 16 * kk, lane);
-      mma16816(yv[0], sA[kk], b[0], b[1]);
-      mma16816(yv[1], sA[kk], b[2], b[3]);
-    }
-    ldb_nk(b, &ks.Q[0][0], LDS, 0, 0, lane);
-    mma16816(sa[0], vA, b[0], b[1]);
-    mma16816(sa[1], vA, b[2], b[3]);
-    ldb_nk(b, &ks.P[0][0], LDS, 0, 0, lane);
-    mma16816(yv[0], vA, b[0], b[1]);
-    mma16816(yv[1], vA, b[2], b[3]);
-
-    // outputs: element (i = i0 + g (+8), t = 8 nt + 2q (+1))
-    {
-      bf16* yp = static_cast<bf16*>(p.y);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i = i0 + g + (e >= 2 ? 8 : 0);
-          const int64_t t = c * L + 8 * nt + 2 * q + (e & 1);
-          if (t < T) {
-            const int64_t o = cbase + t * ts + i;
-            p.sa[o] = sa[nt][e];
-            yp[o] = __float2bfloat16_rn(yv[nt][e]);
-          }
-        }
-    }
-
-    // S' = S diag(lam) + SA^T Bh + V^T Kh
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const float l0 = ks.lam[8 * nt + 2 * q], l1 = ks.lam[8 * nt + 2 * q + 1];
-      S[nt][0] *= l0; S[nt][1] *= l1; S[nt][2] *= l0; S[nt][3] *= l1;
-    }
-    uint32_t saA[4];
-    acc_to_a(saA, sa[0], sa[1]);
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      ldb_kn(b, &ks.Bh[0][0], LD, 16 * m, 0, lane);
-      mma16816(S[2 * m], saA, b[0], b[1]);
-      mma16816(S[2 * m + 1], saA, b[2], b[3]);
-      ldb_kn(b, &ks.Kh[0][0], LD, 16 * m, 0, lane);
-      mma16816(S[2 * m], vA, b[0], b[1]);
-      mma16816(S[2 * m + 1], vA, b[2], b[3]);
-    }
-    __syncthreads();
-  }
-}
-
-cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
-  const size_t smem = sizeof(FwdSmem);
-  cudaError_t e = cudaFuncSetAttribute(chunked_fwd_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  chunked_fwd_kernel<<<(unsigned)p.g.chains(), kThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+// checkpoint slot of chunk c (state at the chunk's start, bf16 A fragments):
+// uint4 index ((warp * 4 + kstep) * 32 + lane)
+__device__ __forceinline__ const uint4* ckpt_slot(const float* base, int64_t ch, int64_t nchunk,
+                                                  int64_t c) {
+  return reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(base) +
+                                        (ch * nchunk + c) * (kN * kN * 2));
 }
 
 // ---------------------------------------------------------------------------
@@ -506,11 +401,18 @@ __global__ void __launch_bounds__(kThreads) chunked_bwd_kernel(BwdArgs p) {
     // ---------------- value side (rows i0..i0+15) ----------------
     float Sin[8][4];
     if (c > 0) {
-      const float4* src = ckpt_slot(const_cast<float*>(p.ckpt), ch, nchunk, c);
+      const uint4* src = ckpt_slot(p.ckpt, ch, nchunk, c);
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const float4 x = src[(wq * 8 + nt) * 32 + lane];
-        Sin[nt][0] = x.x; Sin[nt][1] = x.y; Sin[nt][2] = x.z; Sin[nt][3] = x.w;
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint4 x = src[(wq * 4 + kk) * 32 + lane];
+        const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[h]));
+          float* dst = h < 2 ? Sin[2 * kk] : Sin[2 * kk + 1];
+          dst[2 * (h & 1)] = f.x;
+          dst[2 * (h & 1) + 1] = f.y;
+        }
       }
     } else {
 #pragma unroll
@@ -789,8 +691,9 @@ cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// one bf16 64 x 64 state per chunk and chain
 size_t ckpt_bytes(int64_t chains, int64_t T) {
-  return static_cast<size_t>(chains * ((T + kChunk - 1) / kChunk)) * kN * kN * sizeof(float);
+  return static_cast<size_t>(chains * ((T + kChunk - 1) / kChunk)) * kN * kN * 2;
 }
 
 }  // namespace chunked

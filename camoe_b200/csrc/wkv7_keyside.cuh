@@ -1,0 +1,241 @@
+// Key-side phases of one 16-step chunk, shared by the chunked forward and
+// backward kernels.  "Key side" = everything that depends on r, w, k, a, b
+// only (not on the state or v); see wkv7_chunked_fwd.cu for the algebra.
+//
+// All functions are executed by one group of 4 warps (gw = warp index within
+// the group, gtid = thread index within the group); the caller separates the
+// phases with a group-wide named barrier.
+#pragma once
+
+#include "wkv7_common.cuh"
+#include "wkv7_mma.cuh"
+#include "wkv7_tma.cuh"
+
+namespace camoe {
+namespace ks {
+
+using namespace camoe::mma;
+
+constexpr int L = kChunk;  // 16
+constexpr int LD = 72;     // padded row stride of 16 x 64 bf16 tiles (144 B: conflict-free ldmatrix)
+constexpr int LDS = 24;    // padded row stride of 16 x 16 bf16 tiles
+
+using Tile = bf16[L][LD];
+using Tile16 = bf16[L][LDS];
+
+// Phase 1 (SIMT): per column pair (2p, 2p+1) and time quarter tq, the
+// log-decays lw = -e^{-1/2} sigmoid(w_in), their inclusive prefix cum inside
+// the chunk (scan over the 4 quarter lanes), Lam = exp(cum), and the scaled
+// operands At = a exp(cum - lw), Rt = r Lam, Kb = k / Lam, Bb = b / Lam.
+// lam (the decay over the whole chunk) = Lam of the last step.
+// Thread layout: p = gtid / 4, tq = gtid % 4 (quarter lanes adjacent).
+// With `cum_out`/`sig_out` non-null, the fp32 prefixes and sigmoids are kept
+// for the backward.  The input tiles are 16 x 64 bf16, either row-major with
+// stride LD (SWZ = false) or as landed by a swizzled TMA load (SWZ = true).
+template <bool SWZ>
+__device__ __forceinline__ int raw_idx(int u, int j) {
+  return SWZ ? tma::swz(u, j) : u * LD + j;
+}
+
+template <bool SWZ>
+__device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf16* kk,
+                                       const bf16* aa, const bf16* bb, Tile& At, Tile& Rt,
+                                       Tile& Kb, Tile& Bb, float* lam, float (*cum_out)[kN],
+                                       float (*sig_out)[kN], int gtid) {
+  const int p = gtid >> 2, tq = gtid & 3, j = 2 * p;
+  const int lane = gtid & 31;
+  float lw0[4], lw1[4], c0[4], c1[4];
+  float run0 = 0.f, run1 = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int u = 4 * tq + e;
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ww + raw_idx<SWZ>(u, j)));
+    const float s0 = __fdividef(1.0f, 1.0f + __expf(-x.x));
+    const float s1 = __fdividef(1.0f, 1.0f + __expf(-x.y));
+    if (sig_out != nullptr) *reinterpret_cast<float2*>(&sig_out[u][j]) = make_float2(s0, s1);
+    lw0[e] = kWScale * s0;
+    lw1[e] = kWScale * s1;
+    run0 += lw0[e];
+    run1 += lw1[e];
+    c0[e] = run0;
+    c1[e] = run1;
+  }
+  // exclusive prefix of the quarter totals over the 4 quarter lanes
+  float s0 = run0, s1 = run1;
+#pragma unroll
+  for (int d = 1; d < 4; d <<= 1) {
+    const float t0 = __shfl_up_sync(0xffffffffu, s0, d);
+    const float t1 = __shfl_up_sync(0xffffffffu, s1, d);
+    if (tq >= d) {
+      s0 += t0;
+      s1 += t1;
+    }
+  }
+  const float off0 = s0 - run0, off1 = s1 - run1;
+  (void)lane;
+  float px0 = __expf(off0), px1 = __expf(off1);  // exp(cum) before the quarter's first step
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int u = 4 * tq + e;
+    const float cu0 = off0 + c0[e], cu1 = off1 + c1[e];
+    if (cum_out != nullptr) *reinterpret_cast<float2*>(&cum_out[u][j]) = make_float2(cu0, cu1);
+    const float L0 = __expf(cu0), L1 = __expf(cu1);
+    const float i0 = __expf(-cu0), i1 = __expf(-cu1);
+    const int o = raw_idx<SWZ>(u, j);
+    const float2 r = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(rr + o));
+    const float2 k = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kk + o));
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(aa + o));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bb + o));
+    *reinterpret_cast<__nv_bfloat162*>(&At[u][j]) = __floats2bfloat162_rn(a.x * px0, a.y * px1);
+    *reinterpret_cast<__nv_bfloat162*>(&Rt[u][j]) = __floats2bfloat162_rn(r.x * L0, r.y * L1);
+    *reinterpret_cast<__nv_bfloat162*>(&Kb[u][j]) = __floats2bfloat162_rn(k.x * i0, k.y * i1);
+    *reinterpret_cast<__nv_bfloat162*>(&Bb[u][j]) = __floats2bfloat162_rn(b.x * i0, b.y * i1);
+    px0 = L0;
+    px1 = L1;
+  }
+  if (tq == 3) *reinterpret_cast<float2*>(&lam[j]) = make_float2(px0, px1);
+}
+
+// Phase 2 (tensor cores): the four 16x16 Gram blocks, warp gw computes block gw:
+//   0: Ga = strict(At Bb^T) (fp32)   1: Bm = strict(At Kb^T)
+//   2: Cm = lower(Rt Bb^T)           3: Dm = lower(Rt Kb^T)
+__device__ __forceinline__ void grams(const Tile& At, const Tile& Rt, const Tile& Bb,
+                                      const Tile& Kb, float (*Ga)[L + 1], Tile16& Bm, Tile16& Cm,
+                                      Tile16& Dm, int gw, int lane) {
+  const bf16* Am = (gw >> 1) ? &Rt[0][0] : &At[0][0];
+  const bf16* Bn = (gw & 1) ? &Kb[0][0] : &Bb[0][0];
+  float acc[2][4] = {};
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    uint32_t a[4], b[4];
+    lda_rowmajor(a, Am, LD, 0, kk * 16, lane);
+    ldb_nk(b, Bn, LD, 0, kk * 16, lane);
+    mma16816(acc[0], a, b[0], b[1]);
+    mma16816(acc[1], a, b[2], b[3]);
+  }
+  const int g = lane >> 2, q = lane & 3;
+  const bool strict = gw < 2;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int t = g + (e >= 2 ? 8 : 0), s = 8 * nt + 2 * q + (e & 1);
+      const bool keep = strict ? (s < t) : (s <= t);
+      acc[nt][e] = keep ? acc[nt][e] : 0.f;
+    }
+  if (gw == 0) {
+    store_acc_f32(&Ga[0][0], L + 1, 0, 0, acc[0], lane);
+    store_acc_f32(&Ga[0][0], L + 1, 0, 8, acc[1], lane);
+  } else {
+    bf16* dst = gw == 1 ? &Bm[0][0] : gw == 2 ? &Cm[0][0] : &Dm[0][0];
+    store_acc_bf16(dst, LDS, 0, 0, acc[0], lane);
+    store_acc_bf16(dst, LDS, 0, 8, acc[1], lane);
+  }
+}
+
+// Phase 3 (one warp): Tf = (I - Ga)^{-1} (lower unitriangular) by 8x8 blocks
+// in fp32 (forward substitution per column, then T21 = T22 A21 T11), Ti = bf16(Tf).
+__device__ __forceinline__ void inverse(const float (*Ga)[L + 1], float (*Tf)[L + 1],
+                                        float (*Mf)[9], Tile16& Ti, int lane) {
+  if (lane < 16) {
+    const int o = (lane >> 3) * 8, c = lane & 7;
+    float x[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      float acc = (r == c) ? 1.f : 0.f;
+#pragma unroll
+      for (int s = 0; s < r; ++s) acc += Ga[o + r][o + s] * x[s];
+      x[r] = acc;  // x[s] == 0 for s < c: the column starts at its diagonal
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) Tf[o + r][o + c] = x[r];
+  }
+  __syncwarp();
+#pragma unroll
+  for (int e2 = 0; e2 < 2; ++e2) {  // M = A21 T11
+    const int e = lane + 32 * e2, r = e >> 3, c = e & 7;
+    float acc = 0.f;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) acc += Ga[8 + r][s] * Tf[s][c];
+    Mf[r][c] = acc;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int e2 = 0; e2 < 2; ++e2) {  // T21 = T22 M
+    const int e = lane + 32 * e2, r = e >> 3, c = e & 7;
+    float acc = 0.f;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) acc += Tf[8 + r][8 + m] * Mf[m][c];
+    Tf[8 + r][c] = acc;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int e8 = 0; e8 < 8; ++e8) {
+    const int e = lane + 32 * e8, r = e >> 4, c = e & 15;
+    const bool upper = c > r;
+    const float v = upper ? 0.f : Tf[r][c];
+    if (upper) Tf[r][c] = 0.f;
+    Ti[r][c] = __float2bfloat16_rn(v);
+  }
+}
+
+// Phase 4a: W = Ti At (warp gw: columns 16gw..16gw+15); Q = Ti Bm (warp 3).
+__device__ __forceinline__ void w_and_q(const Tile16& Ti, const Tile& At, const Tile16& Bm,
+                                        Tile& W, Tile16& Q, int gw, int lane) {
+  uint32_t a[4], b[4];
+  lda_rowmajor(a, &Ti[0][0], LDS, 0, 0, lane);
+  ldb_kn(b, &At[0][0], LD, 16 * gw, 0, lane);
+  float acc[2][4] = {};
+  mma16816(acc[0], a, b[0], b[1]);
+  mma16816(acc[1], a, b[2], b[3]);
+  store_acc_bf16(&W[0][0], LD, 0, 16 * gw, acc[0], lane);
+  store_acc_bf16(&W[0][0], LD, 0, 16 * gw + 8, acc[1], lane);
+  if (gw == 3) {
+    float qa[2][4] = {};
+    ldb_kn(b, &Bm[0][0], LDS, 0, 0, lane);
+    mma16816(qa[0], a, b[0], b[1]);
+    mma16816(qa[1], a, b[2], b[3]);
+    store_acc_bf16(&Q[0][0], LDS, 0, 0, qa[0], lane);
+    store_acc_bf16(&Q[0][0], LDS, 0, 8, qa[1], lane);
+  }
+}
+
+// accumulator pair initialised from a bf16 [m][n] tile at (m0, n0)
+__device__ __forceinline__ void acc_from_bf16(float (&c)[4], const bf16* tile, int ld, int m0,
+                                              int n0, int lane) {
+  const int g = lane >> 2, q = lane & 3;
+  const float2 lo = __bfloat1622float2(
+      *reinterpret_cast<const __nv_bfloat162*>(tile + (m0 + g) * ld + n0 + 2 * q));
+  const float2 hi = __bfloat1622float2(
+      *reinterpret_cast<const __nv_bfloat162*>(tile + (m0 + g + 8) * ld + n0 + 2 * q));
+  c[0] = lo.x; c[1] = lo.y; c[2] = hi.x; c[3] = hi.y;
+}
+
+// Phase 4b: Qy = Rt + Cm W (warp gw: columns 16gw..); P = Cm Q + Dm (warp 2).
+__device__ __forceinline__ void qy_and_p(const Tile16& Cm, const Tile& W, const Tile& Rt,
+                                         const Tile16& Q, const Tile16& Dm, Tile& Qy, Tile16& P,
+                                         int gw, int lane) {
+  uint32_t a[4], b[4];
+  lda_rowmajor(a, &Cm[0][0], LDS, 0, 0, lane);
+  ldb_kn(b, &W[0][0], LD, 16 * gw, 0, lane);
+  float acc[2][4];
+  acc_from_bf16(acc[0], &Rt[0][0], LD, 0, 16 * gw, lane);
+  acc_from_bf16(acc[1], &Rt[0][0], LD, 0, 16 * gw + 8, lane);
+  mma16816(acc[0], a, b[0], b[1]);
+  mma16816(acc[1], a, b[2], b[3]);
+  store_acc_bf16(&Qy[0][0], LD, 0, 16 * gw, acc[0], lane);
+  store_acc_bf16(&Qy[0][0], LD, 0, 16 * gw + 8, acc[1], lane);
+  if (gw == 2) {
+    float pa[2][4];
+    acc_from_bf16(pa[0], &Dm[0][0], LDS, 0, 0, lane);
+    acc_from_bf16(pa[1], &Dm[0][0], LDS, 0, 8, lane);
+    ldb_kn(b, &Q[0][0], LDS, 0, 0, lane);
+    mma16816(pa[0], a, b[0], b[1]);
+    mma16816(pa[1], a, b[2], b[3]);
+    store_acc_bf16(&P[0][0], LDS, 0, 0, pa[0], lane);
+    store_acc_bf16(&P[0][0], LDS, 0, 8, pa[1], lane);
+  }
+}
+
+}  // namespace ks
+}  // namespace camoe

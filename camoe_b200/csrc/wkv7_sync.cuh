@@ -1,0 +1,94 @@
+// mbarrier, named-barrier and bulk-copy helpers with bounded waits.
+//
+// Every wait on an mbarrier gives up after kWaitLimitCycles (about a second
+// at 1.9 GHz), counts the event in g_wkv7_timeouts and reports failure, so a
+// logic error can never leave a GPU spinning.  Callers stop their loops on a
+// failed wait.  The counter is per translation unit (static); each kernel
+// file exposes a host reader, summed by camoe_wkv7_device_errors().
+#pragma once
+
+#include <stdint.h>
+
+namespace camoe {
+
+static __device__ unsigned int g_wkv7_timeouts = 0;
+
+constexpr long long kWaitLimitCycles = 2000000000LL;
+
+__device__ __forceinline__ uint32_t sm_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(sm_addr(bar)), "r"(count) : "memory");
+}
+
+// make barrier initialisation visible to the async proxy (bulk copies)
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];\n" ::"r"(sm_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;\n" ::"r"(sm_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(sm_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Wait for the phase with the given parity to complete; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      atomicAdd(&g_wkv7_timeouts, 1u);
+      return false;
+    }
+  }
+}
+
+// 1-D bulk copy global -> shared of `bytes` (multiple of 16, both ends
+// 16-byte aligned), completing on `bar` (complete_tx).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          sm_addr(dst)),
+      "l"(src), "r"(bytes), "r"(sm_addr(bar))
+      : "memory");
+}
+
+// Named barrier over `count` threads (a multiple of 32) of this CTA.
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
+// Named barrier that also ANDs `pred` over the participating threads, so a
+// group leaves a loop together when any member's wait has failed.
+__device__ __forceinline__ bool named_sync_and(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+}  // namespace camoe

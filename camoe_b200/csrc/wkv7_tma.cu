@@ -1,0 +1,50 @@
+// Host-side tensor-map encoding for the TMA tile loads (see wkv7_tma.cuh).
+// cuTensorMapEncodeTiled is a driver API function; it is resolved once
+// through the runtime's driver entry-point query, so the library needs no
+// link-time dependency on libcuda.
+#include <mutex>
+
+#include "wkv7_tma.cuh"
+
+namespace camoe {
+namespace tma {
+namespace {
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+bool encode_bhtn(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H) {
+  const EncodeFn fn = encode_fn();
+  if (fn == nullptr || B <= 0 || T <= 0 || H <= 0) return false;
+  const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(T),
+                              static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(kRowBytes),
+                                 static_cast<cuuint64_t>(H) * kRowBytes,
+                                 static_cast<cuuint64_t>(T) * H * kRowBytes};
+  const cuuint32_t box[4] = {64, 1, 16, 1};
+  const cuuint32_t estride[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+            box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace tma
+}  // namespace camoe

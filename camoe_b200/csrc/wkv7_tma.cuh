@@ -1,0 +1,43 @@
+// TMA (cp.async.bulk.tensor) helpers: host-side tensor-map encoding for the
+// [B, T, H, N] operand arrays and the device-side tile load.
+//
+// Each operand is described to the TMA unit as a 4-D tensor (N, H, T, B)
+// with N innermost, so one 16-step chunk of one head is a {64, 1, 16, 1} box:
+// 16 rows of 128 bytes.  Rows past T are out of bounds in the T dimension and
+// arrive zero-filled.  The box lands in shared memory with the 128-byte
+// swizzle: the 16-byte piece k of row r is stored at piece k ^ (r & 7), which
+// keeps row-parallel shared-memory reads free of bank conflicts.  Every load
+// starts at x = 0 (16-byte aligned) and never writes global memory.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace camoe {
+namespace tma {
+
+constexpr int kRowBytes = 128;             // 64 bf16
+constexpr int kTileBytes = 16 * kRowBytes;  // one 16-step chunk of one head
+
+// element offset of (row r, column c) inside a swizzled 16 x 64 bf16 tile
+__host__ __device__ __forceinline__ int swz(int r, int c) {
+  return r * 64 + ((((c >> 3) ^ (r & 7))) << 3) + (c & 7);
+}
+
+// Encode the (N, H, T, B) map of a bf16 [B, T, H, 64] array; returns false on failure.
+bool encode_bhtn(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H);
+
+__device__ __forceinline__ void load_tile(void* dst_smem, const CUtensorMap* map, int h,
+                                          int t0, int b, uint64_t* bar) {
+  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem));
+  const uint32_t mb = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(h), "r"(t0), "r"(b), "r"(mb)
+      : "memory");
+}
+
+}  // namespace tma
+}  // namespace camoe

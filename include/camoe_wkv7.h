@@ -73,6 +73,12 @@ const char* camoe_wkv7_strerror(int code);
 /* The cudaError_t of the most recent CAMOE_ERR_CUDA on the calling thread. */
 int camoe_wkv7_last_cuda_error(void);
 
+/* Number of bounded device-side waits that timed out on the current device
+ * since the library was loaded (0 in correct operation; a timed-out kernel
+ * stops early and leaves its outputs incomplete).  Synchronises the device.
+ * Returns UINT_MAX if the count cannot be read. */
+unsigned int camoe_wkv7_device_errors(void);
+
 /* Bytes of state checkpoint a forward/backward pair needs for B x h_count
  * chains of length T (0 when there is nothing to store).  Returns 0 for
  * invalid arguments as well; the fwd/bwd calls report those. */

@@ -16,6 +16,15 @@ from helpers import GRADS, TOL_BF16, TOL_FP32, nrel
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True)
+def _no_device_timeouts():
+    """Every bounded device-side wait must have completed (no timed-out kernel)."""
+    from camoe_b200 import _lib
+    before = _lib.lib().camoe_wkv7_device_errors()
+    yield
+    assert _lib.lib().camoe_wkv7_device_errors() == before
+
 NAMES = ("r", "w", "k", "v", "a", "b")
 # (dtype, algo) pairs of the product path
 PATHS = [(torch.float32, "scan"), (torch.bfloat16, "scan"), (torch.bfloat16, "chunked")]
@@ -27,6 +36,7 @@ SHAPES = {
     "ragged_t40": (2, 40, 1, 2, 0.0, 1.0),
     "single_chunk": (3, 16, 1, 3, 0.0, 1.0),
     "t17": (1, 17, 2, 6, 0.0, 1.0),
+    "t5": (2, 5, 3, 7, 0.0, 1.0),
     "extreme_decay": (1, 48, 1, 4, 0.0, 6.0),
     "slow_decay": (1, 256, 2, 1, 2.0, 0.5),
     "layer_b8_t1024": (8, 1024, 16, 0, 0.0, 1.0),
