@@ -98,7 +98,8 @@ __device__ __forceinline__ void issue_raw(RawTile* buf, uint64_t* bar, const Par
 
 __global__ void __launch_bounds__(kThreads, 1) chunked_fwd_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // round up to 1 KiB with pointer arithmetic (keeps the shared address space visible)
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
   const FwdArgs& p = P.a;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t ch = blockIdx.x;
