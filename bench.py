@@ -213,7 +213,9 @@ def main():
 
     # preallocated outputs: the timed step is exactly one fwd + one bwd launch pair
     y, sa, ckpt = ops.wkv7_forward(*xs, algo=args.algo)
-    grads = ops.wkv7_backward(*xs, dy, None, ckpt, algo=args.algo)
+    wb = ops.work_bytes(B, T, H, torch.bfloat16, args.algo)
+    work = torch.empty(max(wb, 16), dtype=torch.uint8, device=dev)
+    grads = ops.wkv7_backward(*xs, dy, None, ckpt, algo=args.algo, work=work)
 
     def step(ev=None):
         if ev is not None:
@@ -221,7 +223,7 @@ def main():
         ops.wkv7_forward(*xs, algo=args.algo, y=y, sa=sa, ckpt=ckpt)
         if ev is not None:
             ev[1].record(stream)
-        ops.wkv7_backward(*xs, dy, None, ckpt, algo=args.algo, grads=grads)
+        ops.wkv7_backward(*xs, dy, None, ckpt, algo=args.algo, grads=grads, work=work)
         if ev is not None:
             ev[2].record(stream)
 
@@ -257,7 +259,11 @@ def main():
     achieved = k_bytes / (k_ms / 1e3) / 1e9
     step_ms = ms / args.steps
     step_gbs = (FWD_BYTES + BWD_BYTES) * elems / (step_ms / 1e3) / 1e9
-    roofline = {"bound": "hbm", "kernel": f"wkv7 {kern} ({args.algo})", "achieved": achieved,
+    kname = {"fwd": "forward (keyside_kernel + value_fwd_kernel)",
+             "bwd": "backward (value_bwd_kernel + keyside_bwd_kernel)"}[kern]
+    if args.algo == "scan":
+        kname = f"scan_{kern}_kernel"
+    roofline = {"bound": "hbm", "kernel": kname, "achieved": achieved,
                 "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
                 "traffic": None, "algorithmic_bytes_per_launch": k_bytes,
                 "launch_ms": k_ms, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
@@ -280,7 +286,7 @@ def main():
                                          "workloads)",
                 "config": config_of(args, wl, world), "roofline": roofline,
                 "cpu_baseline": cb, "clocks": clk, "e2e": e2e,
-                "gpu_launches": 2 * args.steps,
+                "gpu_launches": (4 if args.algo in ("auto", "chunked") else 2) * args.steps,
                 "tokens_per_s_per_gpu": value / world}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -13,9 +13,11 @@ cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream);
 }  // namespace scan
 namespace chunked {
 unsigned int fwd_timeouts();
+unsigned int bwd_timeouts();
 cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream);
-cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream);
+cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream);
 size_t ckpt_bytes(int64_t chains, int64_t T);
+size_t work_bytes(int64_t chains, int64_t T);
 }  // namespace chunked
 }  // namespace camoe
 
@@ -39,6 +41,10 @@ size_t required_ckpt(int64_t B, int64_t T, int64_t hc, int algo) {
   if (algo == CAMOE_ALGO_CHUNKED) return camoe::chunked::ckpt_bytes(chains, T);
   const int64_t nchunk = (T + camoe::kChunk - 1) / camoe::kChunk;
   return static_cast<size_t>(chains * nchunk) * camoe::kN * camoe::kN * sizeof(float);
+}
+
+size_t required_work(int64_t B, int64_t T, int64_t hc, int algo) {
+  return algo == CAMOE_ALGO_CHUNKED ? camoe::chunked::work_bytes(B * hc, T) : 0;
 }
 
 int check_geometry(int64_t B, int64_t T, int64_t H, int64_t h0, int64_t hc, int N) {
@@ -82,14 +88,21 @@ const char* camoe_wkv7_strerror(int code) {
 int camoe_wkv7_last_cuda_error(void) { return g_last_cuda_error; }
 
 unsigned int camoe_wkv7_device_errors(void) {
-  const unsigned int a = camoe::chunked::fwd_timeouts();
-  return a;
+  const unsigned int a = camoe::chunked::fwd_timeouts(), b = camoe::chunked::bwd_timeouts();
+  if (a == ~0u || b == ~0u) return ~0u;
+  return a + b;
 }
 
 size_t camoe_wkv7_ckpt_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype, int algo) {
   const int al = resolve_algo(dtype, algo);
   if (al < 0 || N != camoe::kN || B < 0 || T < 0 || h_count < 0) return 0;
   return required_ckpt(B, T, h_count, al);
+}
+
+size_t camoe_wkv7_work_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype, int algo) {
+  const int al = resolve_algo(dtype, algo);
+  if (al < 0 || N != camoe::kN || B < 0 || T < 0 || h_count < 0) return 0;
+  return required_work(B, T, h_count, al);
 }
 
 int camoe_wkv7_fwd(const void* r, const void* w, const void* k, const void* v, const void* a,
@@ -122,9 +135,9 @@ int camoe_wkv7_fwd(const void* r, const void* w, const void* k, const void* v, c
 
 int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v, const void* a,
                    const void* b, const void* dy, const float* dsa, const void* ckpt,
-                   size_t ckpt_bytes, void* dr, void* dw, void* dk, void* dv, void* da, void* db,
-                   int64_t B, int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N,
-                   int dtype, int algo, void* stream) {
+                   size_t ckpt_bytes, void* work, size_t work_bytes, void* dr, void* dw, void* dk,
+                   void* dv, void* da, void* db, int64_t B, int64_t T, int64_t H_total,
+                   int64_t h0, int64_t h_count, int N, int dtype, int algo, void* stream) {
   int st = check_geometry(B, T, H_total, h0, h_count, N);
   if (st != CAMOE_OK) return st;
   const int al = resolve_algo(dtype, algo);
@@ -142,13 +155,19 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v, c
     if (!aligned16(ckpt)) return CAMOE_ERR_ALIGNMENT;
     if (ckpt_bytes < need) return CAMOE_ERR_WORKSPACE;
   }
+  const size_t wneed = required_work(B, T, h_count, al);
+  if (wneed > 0) {
+    if (work == nullptr) return CAMOE_ERR_INVALID_ARG;
+    if (!aligned16(work)) return CAMOE_ERR_ALIGNMENT;
+    if (work_bytes < wneed) return CAMOE_ERR_WORKSPACE;
+  }
   camoe::BwdArgs p;
   p.r = r; p.w = w; p.k = k; p.v = v; p.a = a; p.b = b; p.dy = dy;
   p.dsa = dsa; p.ckpt = static_cast<const float*>(ckpt);
   p.dr = dr; p.dw = dw; p.dk = dk; p.dv = dv; p.da = da; p.db = db;
   p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_bwd(p, s));
+  if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_bwd(p, work, s));
   if (dtype == CAMOE_DTYPE_BF16) return cuda_status(camoe::scan::launch_bwd<camoe::bf16>(p, s));
   return cuda_status(camoe::scan::launch_bwd<float>(p, s));
 }

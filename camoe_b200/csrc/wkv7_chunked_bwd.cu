@@ -1,0 +1,750 @@
+// Chunked WKV-7 ClampW backward on the tensor cores: two kernels.
+//
+// With the forward of one chunk written (wkv7_chunked_fwd.cu) as
+//     SA = W S^T + Q V,   Y = Qy S^T + P V,   S' = (S + SA^T Bb + V^T Kb) diag(lam),
+// and G = dL/dS' the gradient carried in from the following chunk, G'' = G diag(lam):
+//     dSA  = dSA_ext + Bb G''^T
+//     dS   = G'' + dY^T Qy + dSA^T W                (carried to the previous chunk)
+//     dV   = Kb G''^T + P^T dY + Q^T dSA
+// and the key-side gradients need, summed over the 64 state rows i,
+//     dW = dSA S,  dQy = dY S,  dBb = SA G'',  dKb = V G'',
+//     dQ = strict(dSA V^T),  dP = lower(dY V^T),  dll = colsum(G o S')
+// (dll is d(lam) * lam: lam scales the chunk's end state S').
+//
+// value_bwd_kernel (one CTA per chain, chunks in reverse): 4 value warps carry
+// G and run the recurrence; 4 cross warps form the row sums above from the
+// value warps' bf16 copies of S, G'', SA and dSA and write them as a
+// rec::ProdRec to the workspace; a producer warp streams each chunk's KeyRec,
+// v, dy, dSA_ext tiles and (even chunks) the checkpointed state.  Chunks are
+// taken in (even, odd) pairs: the state at the start of the odd chunk is
+// recomputed from the even chunk's checkpoint.
+//
+// keyside_bwd_kernel (chunk-parallel, every SM): recomputes a chunk's key side
+// from r, w, k, a, b and turns its ProdRec into dr, dw, dk, da, db:
+//     dW += Cm^T dQy,  dQ += Cm^T dP,  dCm = lower(dQy W^T + dP Q^T)
+//     dTi = dW At^T + dQ Bm^T,  dA = strict(Ti^T dTi Ti^T),  dBm = strict(Ti^T dQ)
+//     dAt = Ti^T dW + dA Bb + dBm Kb,   dRt = dQy + dCm Bb + dP Kb
+//     dBb += dA^T At + dCm^T Rt,        dKb += dBm^T At + dP^T Rt
+//     da = dAt Lamx, dr = dRt Lam, dk = dKb / Lam, db = dBb / Lam
+//     dcum = dRt o Rt - dKb o Kb - dBb o Bb (+ dll at the last step), dcumx = dAt o At
+//     dlw_s = sum_{t>=s} dcum_t + sum_{t>s} dcumx_t,  dw_in = dlw (-e^{-1/2}) sig (1 - sig)
+// (the chain rule of the forward algebra; per-element it is the gradient of
+// camoe/cuda/rwkv7_clampw.cu:83-170 summed over a chunk).
+#include "wkv7_common.cuh"
+#include "wkv7_keyside.cuh"
+#include "wkv7_mma.cuh"
+#include "wkv7_record.cuh"
+#include "wkv7_sync.cuh"
+#include "wkv7_tma.cuh"
+
+namespace camoe {
+namespace chunked {
+
+using namespace camoe::mma;
+using ks::L;
+using ks::LD;
+using ks::LDS;
+using ks::Tile;
+using ks::Tile16;
+
+namespace vb {
+
+constexpr int NS = 4;
+constexpr int kThreads = 288;  // value warps 0-3, cross warps 4-7, producer warp 8
+
+struct alignas(1024) Slot {
+  bf16 v[L * kN];   // TMA 128-byte swizzled
+  bf16 dy[L * kN];  // TMA 128-byte swizzled
+  float dsa[L][kN];
+  rec::KeyRec k;
+  uint4 S[512];  // state at the chunk start (even chunks >= 2), A-fragment order
+};
+
+struct XBuf {  // value warps -> cross warps, one chunk
+  bf16 S[kN][LD], G[kN][LD];      // rows i
+  bf16 SAT[kN][LDS], dSAT[kN][LDS];
+  float dll[4][kN];               // per value warp column sums
+};
+
+struct Smem {
+  Slot slot[NS];
+  XBuf xb[2];
+  uint64_t full[NS], empty[NS], xfull[2], xempty[2];
+};
+
+struct Params {
+  CUtensorMap map_v, map_dy, map_dsa;
+  BwdArgs a;
+  void* work;
+};
+
+// Chunks are taken from the end in groups: one lone even chunk first when
+// nchunk is odd, then (even, odd) pairs.  Returns lo, hi (hi == lo for a lone
+// chunk) and the load index of lo.
+__device__ __forceinline__ void group_of(int64_t nchunk, int64_t gi, int64_t& lo, int64_t& hi,
+                                         int64_t& idx_lo) {
+  if (nchunk & 1) {
+    if (gi == 0) { lo = hi = nchunk - 1; idx_lo = 0; return; }
+    lo = nchunk - 1 - 2 * gi;
+    idx_lo = 1 + 2 * (gi - 1);
+  } else {
+    lo = nchunk - 2 - 2 * gi;
+    idx_lo = 2 * gi;
+  }
+  hi = lo + 1;
+}
+
+__device__ __forceinline__ int64_t num_groups(int64_t nchunk) { return (nchunk + 1) / 2; }
+
+__global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_constant__ Params P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
+  const BwdArgs& p = P.a;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t ch = blockIdx.x;
+  const int64_t nchunk = p.g.nchunk, T = p.g.T, ts = p.g.tstride();
+  const int64_t cbase = p.g.base(ch), chains = p.g.chains();
+  const int64_t ngroups = num_groups(nchunk);
+  const bool has_dsa = p.dsa != nullptr;
+
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 8);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&sm.xfull[x], 4);
+      mbar_init(&sm.xempty[x], 4);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == 8) {
+    // ------------------------------ producer ------------------------------
+    if (lane != 0) return;
+    const int hh = static_cast<int>(p.g.h0 + ch % p.g.hc), bb = static_cast<int>(ch / p.g.hc);
+    int64_t issued = 0;
+    bool ok = true;
+    for (int64_t gi = 0; gi < ngroups && ok; ++gi) {
+      int64_t lo, hi, idx;
+      group_of(nchunk, gi, lo, hi, idx);
+      for (int64_t c = lo; c <= hi && ok; ++c, ++idx) {
+        const int s = static_cast<int>(idx % NS);
+        if (idx >= NS) ok = mbar_wait(&sm.empty[s], static_cast<uint32_t>((idx / NS - 1) & 1));
+        if (!ok) break;
+        const bool with_state = c == lo && lo >= 2;
+        const uint32_t bytes = sizeof(rec::KeyRec) + 2 * tma::kTileBytes +
+                               (has_dsa ? L * kN * 4 : 0) + (with_state ? 8192 : 0);
+        Slot& sl = sm.slot[s];
+        mbar_arrive_expect_tx(&sm.full[s], bytes);
+        bulk_g2s(&sl.k, rec::keyrec(const_cast<float*>(p.ckpt), ch, nchunk, c), sizeof(rec::KeyRec), &sm.full[s]);
+        tma::load_tile(sl.v, &P.map_v, hh, static_cast<int>(c * L), bb, &sm.full[s]);
+        tma::load_tile(sl.dy, &P.map_dy, hh, static_cast<int>(c * L), bb, &sm.full[s]);
+        if (has_dsa) tma::load_tile(&sl.dsa[0][0], &P.map_dsa, hh, static_cast<int>(c * L), bb, &sm.full[s]);
+        if (with_state)
+          bulk_g2s(sl.S, rec::state_ptr(const_cast<float*>(p.ckpt), chains, ch, nchunk, lo), 8192, &sm.full[s]);
+        ++issued;
+      }
+    }
+    if (!ok)  // stopped on a timeout: let the copies in flight land
+      for (int64_t i = issued > NS ? issued - NS : 0; i < issued; ++i)
+        mbar_wait(&sm.full[i % NS], static_cast<uint32_t>((i / NS) & 1));
+    return;
+  }
+
+  if (warp >= 4) {
+    // ------------------------------ cross warps ------------------------------
+    const int cw = warp - 4, j0 = 16 * cw, g = lane >> 2, q = lane & 3;
+    int64_t done = 0;  // chunks processed (cross-buffer index = done & 1)
+    for (int64_t gi = 0; gi < ngroups; ++gi) {
+      int64_t lo, hi, idx_lo;
+      group_of(nchunk, gi, lo, hi, idx_lo);
+      for (int64_t c = hi; c >= lo; --c, ++done) {
+        const int xb = static_cast<int>(done & 1);
+        const int64_t idx = idx_lo + (c - lo);
+        const int s = static_cast<int>(idx % NS);
+        if (!mbar_wait(&sm.xfull[xb], static_cast<uint32_t>((done >> 1) & 1))) return;
+        const XBuf& X = sm.xb[xb];
+        const Slot& sl = sm.slot[s];
+        float dW[2][4] = {}, dQy[2][4] = {}, dBb[2][4] = {}, dKb[2][4] = {};
+        mm16<true, true, 4>(dW, &X.dSAT[0][0], Padded{LDS}, &X.S[0][0], Padded{LD}, j0, lane);
+        mm16<false, true, 4>(dQy, sl.dy, Swz64{}, &X.S[0][0], Padded{LD}, j0, lane);
+        mm16<true, true, 4>(dBb, &X.SAT[0][0], Padded{LDS}, &X.G[0][0], Padded{LD}, j0, lane);
+        mm16<false, true, 4>(dKb, sl.v, Swz64{}, &X.G[0][0], Padded{LD}, j0, lane);
+        rec::ProdRec* pr = rec::prodrec(P.work, ch, nchunk, c);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const int t = g + 8 * hf, j = j0 + 8 * nt + 2 * q;
+            *reinterpret_cast<float2*>(&pr->dW[t * kN + j]) = make_float2(dW[nt][2 * hf], dW[nt][2 * hf + 1]);
+            *reinterpret_cast<float2*>(&pr->dQy[t * kN + j]) = make_float2(dQy[nt][2 * hf], dQy[nt][2 * hf + 1]);
+            *reinterpret_cast<float2*>(&pr->dBb[t * kN + j]) = make_float2(dBb[nt][2 * hf], dBb[nt][2 * hf + 1]);
+            *reinterpret_cast<float2*>(&pr->dKb[t * kN + j]) = make_float2(dKb[nt][2 * hf], dKb[nt][2 * hf + 1]);
+          }
+        if (cw < 2) {  // cw 0: dQ = strict(dSA V^T), cw 1: dP = lower(dY V^T)
+          float acc[2][4] = {};
+          if (cw == 0) mm16<true, false, 4>(acc, &X.dSAT[0][0], Padded{LDS}, sl.v, Swz64{}, 0, lane);
+          else mm16<false, false, 4>(acc, sl.dy, Swz64{}, sl.v, Swz64{}, 0, lane);
+          float* dst = cw == 0 ? pr->dQ : pr->dP;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int t = g + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
+              const bool keep = cw == 0 ? (u < t) : (u <= t);
+              dst[t * L + u] = keep ? acc[nt][e] : 0.f;
+            }
+        } else if (cw == 2) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = lane + 32 * e;
+            pr->dll[j] = X.dll[0][j] + X.dll[1][j] + X.dll[2][j] + X.dll[3][j];
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sm.xempty[xb]);
+          mbar_arrive(&sm.empty[s]);
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------ value warps ------------------------------
+  const int wq = warp, g = lane >> 2, q = lane & 3, i0 = 16 * wq;
+  float G[8][4];  // dL/dS' of the chunk being processed
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) G[nt][e] = 0.f;
+  float dll[8][2];  // colsum(G o S') of the next chunk to process (lanes g == 0)
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) dll[nt][0] = dll[nt][1] = 0.f;
+  bf16* dvp = static_cast<bf16*>(p.dv);
+  int64_t done = 0;
+  for (int64_t gi = 0; gi < ngroups; ++gi) {
+    int64_t lo, hi, idx_lo;
+    group_of(nchunk, gi, lo, hi, idx_lo);
+    const int s_lo = static_cast<int>(idx_lo % NS);
+    const int s_hi = static_cast<int>((idx_lo + 1) % NS);
+    if (!mbar_wait(&sm.full[s_lo], static_cast<uint32_t>((idx_lo / NS) & 1))) return;
+    if (hi != lo && !mbar_wait(&sm.full[s_hi], static_cast<uint32_t>(((idx_lo + 1) / NS) & 1))) return;
+
+    // state at the start of lo (A fragments)
+    uint32_t sLo[4][4];
+    if (lo >= 2) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint4 x = sm.slot[s_lo].S[(wq * 4 + kk) * 32 + lane];
+        sLo[kk][0] = x.x; sLo[kk][1] = x.y; sLo[kk][2] = x.z; sLo[kk][3] = x.w;
+      }
+    } else {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) sLo[kk][0] = sLo[kk][1] = sLo[kk][2] = sLo[kk][3] = 0u;
+    }
+    // SA of lo (needed by lo's backward, and by the recompute of hi's start state)
+    float satLo[2][4] = {};
+    uint32_t vA[4], b[4];
+    {
+      const rec::KeyRec& kr = sm.slot[s_lo].k;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
+        mma16816(satLo[0], sLo[kk], b[0], b[1]);
+        mma16816(satLo[1], sLo[kk], b[2], b[3]);
+      }
+      lda_cm(vA, sm.slot[s_lo].v, Swz64{}, i0, 0, lane);
+      ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
+      mma16816(satLo[0], vA, b[0], b[1]);
+      mma16816(satLo[1], vA, b[2], b[3]);
+    }
+    uint32_t sHi[4][4] = {};
+    if (hi != lo) {  // S(hi) = (S(lo) + SA^T Bb + V^T Kb) diag(lam), from chunk lo
+      const rec::KeyRec& kr = sm.slot[s_lo].k;
+      float Sf[8][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sLo[kk][h]));
+          const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sLo[kk][2 + h]));
+          // sLo[kk] = A fragment of n8 tiles (2kk, 2kk+1): regs 0,1 -> tile 2kk, regs 2,3 -> 2kk+1
+          Sf[2 * kk][2 * h] = a0.x;
+          Sf[2 * kk][2 * h + 1] = a0.y;
+          Sf[2 * kk + 1][2 * h] = a1.x;
+          Sf[2 * kk + 1][2 * h + 1] = a1.y;
+        }
+      uint32_t saA[4];
+      acc_to_a(saA, satLo[0], satLo[1]);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        ldb_kn(b, kr.Bb, Swz64{}, 16 * m, 0, lane);
+        mma16816(Sf[2 * m], saA, b[0], b[1]);
+        mma16816(Sf[2 * m + 1], saA, b[2], b[3]);
+        ldb_kn(b, kr.Kb, Swz64{}, 16 * m, 0, lane);
+        mma16816(Sf[2 * m], vA, b[0], b[1]);
+        mma16816(Sf[2 * m + 1], vA, b[2], b[3]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
+        Sf[nt][0] *= l.x; Sf[nt][1] *= l.y; Sf[nt][2] *= l.x; Sf[nt][3] *= l.y;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) acc_to_a(sHi[kk], Sf[2 * kk], Sf[2 * kk + 1]);
+    }
+
+    for (int64_t c = hi; c >= lo; --c, ++done) {
+      const bool is_lo = c == lo;
+      const int s = is_lo ? s_lo : s_hi;
+      const int xb = static_cast<int>(done & 1);
+      const Slot& sl = sm.slot[s];
+      const rec::KeyRec& kr = sl.k;
+      uint32_t sA[4][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) sA[kk][r] = is_lo ? sLo[kk][r] : sHi[kk][r];
+
+      // G'' = G diag(lam)
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
+        G[nt][0] *= l.x; G[nt][1] *= l.y; G[nt][2] *= l.x; G[nt][3] *= l.y;
+      }
+      uint32_t gA[4][4], dyA[4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) acc_to_a(gA[kk], G[2 * kk], G[2 * kk + 1]);
+      lda_cm(vA, sl.v, Swz64{}, i0, 0, lane);
+      lda_cm(dyA, sl.dy, Swz64{}, i0, 0, lane);
+
+      float sat[2][4], dsat[2][4];
+      if (is_lo) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sat[nt][e] = satLo[nt][e];
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sat[nt][e] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
+          mma16816(sat[0], sA[kk], b[0], b[1]);
+          mma16816(sat[1], sA[kk], b[2], b[3]);
+        }
+        ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
+        mma16816(sat[0], vA, b[0], b[1]);
+        mma16816(sat[1], vA, b[2], b[3]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          dsat[nt][e] = has_dsa ? sl.dsa[8 * nt + 2 * q + (e & 1)][i0 + g + (e >= 2 ? 8 : 0)] : 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        ldb_nk(b, kr.Bb, Swz64{}, 0, 16 * kk, lane);
+        mma16816(dsat[0], gA[kk], b[0], b[1]);
+        mma16816(dsat[1], gA[kk], b[2], b[3]);
+      }
+      uint32_t dsaA[4];
+      acc_to_a(dsaA, dsat[0], dsat[1]);
+
+      // dV^T = G'' Kb^T + dY^T P + dSA^T Q
+      {
+        float dvt[2][4] = {};
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          ldb_nk(b, kr.Kb, Swz64{}, 0, 16 * kk, lane);
+          mma16816(dvt[0], gA[kk], b[0], b[1]);
+          mma16816(dvt[1], gA[kk], b[2], b[3]);
+        }
+        ldb_kn(b, kr.P, Swz16{}, 0, 0, lane);
+        mma16816(dvt[0], dyA, b[0], b[1]);
+        mma16816(dvt[1], dyA, b[2], b[3]);
+        ldb_kn(b, kr.Q, Swz16{}, 0, 0, lane);
+        mma16816(dvt[0], dsaA, b[0], b[1]);
+        mma16816(dvt[1], dsaA, b[2], b[3]);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int64_t t = c * L + 8 * nt + 2 * q + (e & 1);
+            if (t < T) dvp[cbase + t * ts + i0 + g + (e >= 2 ? 8 : 0)] = __float2bfloat16_rn(dvt[nt][e]);
+          }
+      }
+
+      // hand S, G'', SA, dSA (bf16) and dll of this chunk to the cross warps
+      if (done >= 2 && !mbar_wait(&sm.xempty[xb], static_cast<uint32_t>(((done >> 1) - 1) & 1))) return;
+      XBuf& X = sm.xb[xb];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // A fragment regs -> rows g / g+8, cols 16kk + 2q (+8)
+          const int col = 16 * kk + 2 * q + 8 * h;
+          *reinterpret_cast<uint32_t*>(&X.S[i0 + g][col]) = sA[kk][2 * h];
+          *reinterpret_cast<uint32_t*>(&X.S[i0 + g + 8][col]) = sA[kk][2 * h + 1];
+          *reinterpret_cast<uint32_t*>(&X.G[i0 + g][col]) = gA[kk][2 * h];
+          *reinterpret_cast<uint32_t*>(&X.G[i0 + g + 8][col]) = gA[kk][2 * h + 1];
+        }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        store_acc_bf16(&X.SAT[0][0], LDS, i0, 8 * nt, sat[nt], lane);
+        store_acc_bf16(&X.dSAT[0][0], LDS, i0, 8 * nt, dsat[nt], lane);
+      }
+      if (g == 0) {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+          *reinterpret_cast<float2*>(&X.dll[wq][8 * nt + 2 * q]) = make_float2(dll[nt][0], dll[nt][1]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.xfull[xb]);
+
+      // dS = G'' + dY^T Qy + dSA^T W  -> G of the previous chunk
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        ldb_kn(b, kr.Qy, Swz64{}, 16 * m, 0, lane);
+        mma16816(G[2 * m], dyA, b[0], b[1]);
+        mma16816(G[2 * m + 1], dyA, b[2], b[3]);
+        ldb_kn(b, kr.W, Swz64{}, 16 * m, 0, lane);
+        mma16816(G[2 * m], dsaA, b[0], b[1]);
+        mma16816(G[2 * m + 1], dsaA, b[2], b[3]);
+      }
+      // dll of the previous chunk: colsum over rows of G o S, S = this chunk's start state
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const uint32_t lo2 = sA[nt >> 1][2 * (nt & 1)], hi2 = sA[nt >> 1][2 * (nt & 1) + 1];
+        const float2 s0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo2));
+        const float2 s1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi2));
+        float p0 = G[nt][0] * s0.x + G[nt][2] * s1.x;
+        float p1 = G[nt][1] * s0.y + G[nt][3] * s1.y;
+#pragma unroll
+        for (int m = 4; m < 32; m <<= 1) {
+          p0 += __shfl_xor_sync(0xffffffffu, p0, m);
+          p1 += __shfl_xor_sync(0xffffffffu, p1, m);
+        }
+        dll[nt][0] = p0;
+        dll[nt][1] = p1;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[s]);
+    }
+  }
+}
+
+}  // namespace vb
+
+namespace kb {
+
+constexpr int NR = 2;
+constexpr int kThreads = 128;  // one group of 4 warps per CTA
+
+struct alignas(1024) KGroup {
+  bf16 raw[NR][5][L * kN];  // r, w, k, a, b as landed by TMA (1 KiB aligned)
+  rec::ProdRec prod[NR];
+  Tile At, Rt, W, Bb, Kb;
+  Tile16 Bm, Cm, Dm, Ti, Q, P;
+  float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
+  float lam[kN], cum[L][kN], sig[L][kN];
+  bf16 dQyb[L][LD], dW2b[L][LD];
+  bf16 dPb[L][LDS], dQ2b[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
+  float dTf[L][L + 1], dM1[L][L + 1];
+  float dcum[L][kN], dcumx[L][kN];
+  bf16 dwt[L][LD];
+  uint64_t bar[NR];
+};
+
+struct Params {
+  CUtensorMap maps[5];  // r, w, k, a, b
+  BwdArgs a;
+  void* work;
+};
+
+__device__ __forceinline__ void issue(KGroup& G, int rb, const Params& P, int64_t item) {
+  const Geom& g = P.a.g;
+  const int64_t ch = item / g.nchunk, c = item % g.nchunk;
+  const int h = static_cast<int>(g.h0 + ch % g.hc), b = static_cast<int>(ch / g.hc);
+  mbar_arrive_expect_tx(&G.bar[rb], 5 * tma::kTileBytes + sizeof(rec::ProdRec));
+#pragma unroll
+  for (int t = 0; t < 5; ++t) tma::load_tile(G.raw[rb][t], &P.maps[t], h, static_cast<int>(c * L), b, &G.bar[rb]);
+  bulk_g2s(&G.prod[rb], rec::prodrec(P.work, ch, g.nchunk, c), sizeof(rec::ProdRec), &G.bar[rb]);
+}
+
+__global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_constant__ Params P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  KGroup& G = *reinterpret_cast<KGroup*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
+  const BwdArgs& p = P.a;
+  const int tid = threadIdx.x, lane = tid & 31, gw = tid >> 5, gq = lane >> 2, q = lane & 3;
+  const int j0 = 16 * gw;
+  if (tid == 0) {
+    for (int i = 0; i < NR; ++i) mbar_init(&G.bar[i], 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  const int64_t nchunk = p.g.nchunk, T = p.g.T, ts = p.g.tstride();
+  const int64_t total = p.g.chains() * nchunk;
+  if (tid == 0)
+    for (int i = 0; i < NR; ++i)
+      if (blockIdx.x + static_cast<int64_t>(i) * gridDim.x < total) issue(G, i, P, blockIdx.x + static_cast<int64_t>(i) * gridDim.x);
+  int64_t j = 0;
+  for (;; ++j) {
+    const int64_t item = blockIdx.x + j * gridDim.x;
+    if (item >= total) break;
+    const int rb = static_cast<int>(j % NR);
+    bool ok = mbar_wait(&G.bar[rb], static_cast<uint32_t>((j / NR) & 1));
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    const int64_t ch = item / nchunk, c = item % nchunk;
+    const int64_t cbase = p.g.base(ch);
+    const bf16* raw_r = G.raw[rb][0];
+    const bf16* raw_k = G.raw[rb][2];
+    const bf16* raw_a = G.raw[rb][3];
+    const bf16* raw_b = G.raw[rb][4];
+    const rec::ProdRec& pr = G.prod[rb];
+
+    // ---- key side of the chunk (forward recompute) ----
+    ks::decays<true>(raw_r, G.raw[rb][1], raw_k, raw_a, raw_b, G.At, G.Rt, G.Kb, G.Bb, G.lam,
+                     G.cum, G.sig, tid);
+    __syncthreads();
+    ks::grams(G.At, G.Rt, G.Bb, G.Kb, G.Ga, G.Bm, G.Cm, G.Dm, gw, lane);
+    __syncthreads();
+    if (gw == 0) ks::inverse(G.Ga, G.Tf, G.Mf, G.Ti, lane);
+    __syncthreads();
+    ks::w_and_q(G.Ti, G.At, G.Bm, G.W, G.Q, gw, lane);
+
+    // ---- dW += Cm^T dQy (own columns), bf16 copies of dQy and dP ----
+    for (int e = lane; e < L * 8; e += 32) {  // 16 rows x 8 pairs of own columns
+      const int t = e >> 3, jj = j0 + 2 * (e & 7);
+      const float2 v = *reinterpret_cast<const float2*>(&pr.dQy[t * kN + jj]);
+      *reinterpret_cast<__nv_bfloat162*>(&G.dQyb[t][jj]) = __floats2bfloat162_rn(v.x, v.y);
+    }
+    if (gw == 1)
+      for (int e = lane; e < L * L; e += 32) G.dPb[e >> 4][e & 15] = __float2bfloat16_rn(pr.dP[e]);
+    __syncwarp();
+    float dW2[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const float2 v = *reinterpret_cast<const float2*>(&pr.dW[(gq + 8 * hf) * kN + j0 + 8 * nt + 2 * q]);
+        dW2[nt][2 * hf] = v.x;
+        dW2[nt][2 * hf + 1] = v.y;
+      }
+    __syncthreads();  // W, Q ready (w_and_q) and dPb visible
+    mm16<true, true, 1>(dW2, &G.Cm[0][0], Padded{LDS}, &G.dQyb[0][0], Padded{LD}, j0, lane);
+    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW2[0], lane);
+    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW2[1], lane);
+    __syncthreads();
+
+    // ---- 16x16 pieces ----
+    if (gw == 0) {  // dCm = lower(dQy W^T + dP Q^T)
+      float dcm[2][4] = {};
+      mm16<false, false, 4>(dcm, &G.dQyb[0][0], Padded{LD}, &G.W[0][0], Padded{LD}, 0, lane);
+      mm16<false, false, 1>(dcm, &G.dPb[0][0], Padded{LDS}, &G.Q[0][0], Padded{LDS}, 0, lane);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
+          if (u > t) dcm[nt][e] = 0.f;
+        }
+      store_acc_bf16(&G.dCmb[0][0], LDS, 0, 0, dcm[0], lane);
+      store_acc_bf16(&G.dCmb[0][0], LDS, 0, 8, dcm[1], lane);
+    } else if (gw == 1) {  // dQ += Cm^T dP;  dTi = dW At^T + dQ Bm^T
+      float dq[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          dq[nt][e] = pr.dQ[(gq + (e >= 2 ? 8 : 0)) * L + 8 * nt + 2 * q + (e & 1)];
+      mm16<true, true, 1>(dq, &G.Cm[0][0], Padded{LDS}, &G.dPb[0][0], Padded{LDS}, 0, lane);
+      store_acc_bf16(&G.dQ2b[0][0], LDS, 0, 0, dq[0], lane);
+      store_acc_bf16(&G.dQ2b[0][0], LDS, 0, 8, dq[1], lane);
+      __syncwarp();
+      float dti[2][4] = {};
+      mm16<false, false, 4>(dti, &G.dW2b[0][0], Padded{LD}, &G.At[0][0], Padded{LD}, 0, lane);
+      mm16<false, false, 1>(dti, &G.dQ2b[0][0], Padded{LDS}, &G.Bm[0][0], Padded{LDS}, 0, lane);
+      store_acc_f32(&G.dTf[0][0], L + 1, 0, 0, dti[0], lane);
+      store_acc_f32(&G.dTf[0][0], L + 1, 0, 8, dti[1], lane);
+    }
+    float dAt[2][4] = {};  // Ti^T dW (own columns)
+    mm16<true, true, 1>(dAt, &G.Ti[0][0], Padded{LDS}, &G.dW2b[0][0], Padded{LD}, j0, lane);
+    __syncthreads();
+    if (gw == 0) {  // dA = strict(Ti^T dTi Ti^T), fp32
+#pragma unroll
+      for (int e8 = 0; e8 < 8; ++e8) {
+        const int e = lane + 32 * e8, t = e >> 4, u = e & 15;
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < L; ++m) acc += G.dTf[t][m] * G.Tf[u][m];
+        G.dM1[t][u] = acc;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int e8 = 0; e8 < 8; ++e8) {
+        const int e = lane + 32 * e8, t = e >> 4, u = e & 15;
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < L; ++m) acc += G.Tf[m][t] * G.dM1[m][u];
+        G.dAb[t][u] = __float2bfloat16_rn(u < t ? acc : 0.f);
+      }
+    } else if (gw == 1) {  // dBm = strict(Ti^T dQ)
+      float dbm[2][4] = {};
+      mm16<true, true, 1>(dbm, &G.Ti[0][0], Padded{LDS}, &G.dQ2b[0][0], Padded{LDS}, 0, lane);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
+          if (u >= t) dbm[nt][e] = 0.f;
+        }
+      store_acc_bf16(&G.dBmb[0][0], LDS, 0, 0, dbm[0], lane);
+      store_acc_bf16(&G.dBmb[0][0], LDS, 0, 8, dbm[1], lane);
+    }
+    __syncthreads();
+
+    // ---- column-indexed gradients (own columns) ----
+    mm16<false, true, 1>(dAt, &G.dAb[0][0], Padded{LDS}, &G.Bb[0][0], Padded{LD}, j0, lane);
+    mm16<false, true, 1>(dAt, &G.dBmb[0][0], Padded{LDS}, &G.Kb[0][0], Padded{LD}, j0, lane);
+    float dBb[2][4] = {}, dKb[2][4] = {}, dRt[2][4] = {};
+    mm16<true, true, 1>(dBb, &G.dAb[0][0], Padded{LDS}, &G.At[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dBb, &G.dCmb[0][0], Padded{LDS}, &G.Rt[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dKb, &G.dBmb[0][0], Padded{LDS}, &G.At[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dKb, &G.dPb[0][0], Padded{LDS}, &G.Rt[0][0], Padded{LD}, j0, lane);
+    mm16<false, true, 1>(dRt, &G.dCmb[0][0], Padded{LDS}, &G.Bb[0][0], Padded{LD}, j0, lane);
+    mm16<false, true, 1>(dRt, &G.dPb[0][0], Padded{LDS}, &G.Kb[0][0], Padded{LD}, j0, lane);
+    bf16* dap = static_cast<bf16*>(p.da);
+    bf16* drp = static_cast<bf16*>(p.dr);
+    bf16* dkp = static_cast<bf16*>(p.dk);
+    bf16* dbp = static_cast<bf16*>(p.db);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int t = gq + 8 * hf, jj = j0 + 8 * nt + 2 * q;
+        const float2 cm = *reinterpret_cast<const float2*>(&G.cum[t][jj]);
+        const float2 sg = *reinterpret_cast<const float2*>(&G.sig[t][jj]);
+        const float2 qy = *reinterpret_cast<const float2*>(&pr.dQy[t * kN + jj]);
+        const float2 pb = *reinterpret_cast<const float2*>(&pr.dBb[t * kN + jj]);
+        const float2 pk = *reinterpret_cast<const float2*>(&pr.dKb[t * kN + jj]);
+        const float2 rr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_r + tma::swz(t, jj)));
+        const float2 kk = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_k + tma::swz(t, jj)));
+        const float2 aa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_a + tma::swz(t, jj)));
+        const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_b + tma::swz(t, jj)));
+        const float cmv[2] = {cm.x, cm.y}, sgv[2] = {sg.x, sg.y}, qyv[2] = {qy.x, qy.y};
+        const float pbv[2] = {pb.x, pb.y}, pkv[2] = {pk.x, pk.y};
+        const float rv[2] = {rr.x, rr.y}, kv[2] = {kk.x, kk.y}, av[2] = {aa.x, aa.y}, bv[2] = {bb.x, bb.y};
+        float oda[2], odr[2], odk[2], odb[2];
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const int e = 2 * hf + x;
+          const float Lam = __expf(cmv[x]), Lamx = __expf(cmv[x] - kWScale * sgv[x]), iLam = __expf(-cmv[x]);
+          const float dat = dAt[nt][e], drt = dRt[nt][e] + qyv[x];
+          const float dbb = dBb[nt][e] + pbv[x], dkb = dKb[nt][e] + pkv[x];
+          oda[x] = dat * Lamx;
+          odr[x] = drt * Lam;
+          odk[x] = dkb * iLam;
+          odb[x] = dbb * iLam;
+          G.dcum[t][jj + x] = drt * rv[x] * Lam - dkb * kv[x] * iLam - dbb * bv[x] * iLam;
+          G.dcumx[t][jj + x] = dat * av[x] * Lamx;
+        }
+        const int64_t tg = c * L + t;
+        if (tg < T) {
+          const int64_t o = cbase + tg * ts + jj;
+          *reinterpret_cast<__nv_bfloat162*>(dap + o) = __floats2bfloat162_rn(oda[0], oda[1]);
+          *reinterpret_cast<__nv_bfloat162*>(drp + o) = __floats2bfloat162_rn(odr[0], odr[1]);
+          *reinterpret_cast<__nv_bfloat162*>(dkp + o) = __floats2bfloat162_rn(odk[0], odk[1]);
+          *reinterpret_cast<__nv_bfloat162*>(dbp + o) = __floats2bfloat162_rn(odb[0], odb[1]);
+        }
+      }
+    __syncwarp();
+    if (lane < 16) {  // reverse scans along t of column j
+      const int jj = j0 + lane;
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+      for (int t = L - 1; t >= 0; --t) {
+        float dc = G.dcum[t][jj];
+        if (t == L - 1) dc += pr.dll[jj];
+        s1 += dc;
+        const float dlw = s1 + s2;
+        s2 += G.dcumx[t][jj];
+        const float sg = G.sig[t][jj];
+        G.dwt[t][jj] = __float2bfloat16_rn(dlw * kWScale * sg * (1.0f - sg));
+      }
+    }
+    __syncthreads();
+    {  // dw tile: 16 rows x 8 pieces of 16 bytes
+      const int t = tid >> 3, part = tid & 7;
+      const int64_t tg = c * L + t;
+      if (tg < T)
+        *reinterpret_cast<uint4*>(static_cast<bf16*>(p.dw) + cbase + tg * ts + part * 8) =
+            *reinterpret_cast<const uint4*>(&G.dwt[t][part * 8]);
+    }
+    __syncthreads();  // raw, prod and scratch free
+    if (tid == 0 && item + NR * static_cast<int64_t>(gridDim.x) < total)
+      issue(G, rb, P, item + NR * static_cast<int64_t>(gridDim.x));
+  }
+  if (tid == 0)  // after a timeout, let loads in flight land before the CTA exits
+    for (int64_t jj = j; jj < j + NR; ++jj)
+      if (blockIdx.x + jj * gridDim.x < total) mbar_wait(&G.bar[jj % NR], static_cast<uint32_t>((jj / NR) & 1));
+}
+
+}  // namespace kb
+
+unsigned int bwd_timeouts() {
+  unsigned int n = 0;
+  if (cudaMemcpyFromSymbol(&n, g_wkv7_timeouts, sizeof(n)) != cudaSuccess) return ~0u;
+  return n;
+}
+
+size_t ckpt_bytes(int64_t chains, int64_t T) {
+  return rec::ckpt_bytes(chains, (T + kChunk - 1) / kChunk);
+}
+
+size_t work_bytes(int64_t chains, int64_t T) {
+  return rec::work_bytes(chains, (T + kChunk - 1) / kChunk);
+}
+
+cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
+  vb::Params V;
+  V.a = p;
+  V.work = work;
+  if (!tma::encode_bhtn(&V.map_v, p.v, p.g.B, p.g.T, p.g.H) ||
+      !tma::encode_bhtn(&V.map_dy, p.dy, p.g.B, p.g.T, p.g.H))
+    return cudaErrorInvalidValue;
+  if (p.dsa != nullptr && !tma::encode_bhtn_f32(&V.map_dsa, p.dsa, p.g.B, p.g.T, p.g.H))
+    return cudaErrorInvalidValue;
+  const size_t vsmem = sizeof(vb::Smem) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(vb::value_bwd_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vsmem);
+  if (e != cudaSuccess) return e;
+  vb::value_bwd_kernel<<<(unsigned)p.g.chains(), vb::kThreads, vsmem, stream>>>(V);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+
+  kb::Params K;
+  K.a = p;
+  K.work = work;
+  const void* src[5] = {p.r, p.w, p.k, p.a, p.b};
+  for (int t = 0; t < 5; ++t)
+    if (!tma::encode_bhtn(&K.maps[t], src[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t ksmem = sizeof(kb::KGroup) + 1024;
+  e = cudaFuncSetAttribute(kb::keyside_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)ksmem);
+  if (e != cudaSuccess) return e;
+  const int64_t items = p.g.chains() * p.g.nchunk;
+  const int64_t kgrid = items < 2LL * sms ? items : 2LL * sms;
+  kb::keyside_bwd_kernel<<<(unsigned)kgrid, kb::kThreads, ksmem, stream>>>(K);
+  return cudaGetLastError();
+}
+
+}  // namespace chunked
+}  // namespace camoe

@@ -39,6 +39,7 @@
 #include "wkv7_common.cuh"
 #include "wkv7_keyside.cuh"
 #include "wkv7_mma.cuh"
+#include "wkv7_record.cuh"
 #include "wkv7_sync.cuh"
 #include "wkv7_tma.cuh"
 
@@ -135,13 +136,6 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_fwd_kernel(const __grid_c
       uint32_t sA[4][4], vA[4], b[4];
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) acc_to_a(sA[kk], S[2 * kk], S[2 * kk + 1]);
-      if (p.ckpt != nullptr && c > 0) {
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.ckpt) +
-                                              (ch * nchunk + c) * (kN * kN * 2));
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          dst[(wq * 4 + kk) * 32 + lane] = make_uint4(sA[kk][0], sA[kk][1], sA[kk][2], sA[kk][3]);
-      }
       lda_colmajor(vA, &sl.v[0][0], LD, i0, 0, lane);
       float sa[2][4] = {}, yv[2][4] = {};
 #pragma unroll
@@ -244,6 +238,263 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_fwd_kernel(const __grid_c
 
 }  // namespace fwd
 
+// ===========================================================================
+// Forward with a checkpoint: two kernels.
+//
+// keyside_kernel (chunk-parallel, every SM): for every (chain, chunk) the key
+// side matrices W, Qy, Bb, Kb, Q, P and lam, written as one rec::KeyRec into
+// the checkpoint buffer.  Groups of 4 warps work on independent chunks; two
+// groups per CTA, grid-stride over all chunks, TMA loads one chunk ahead.
+//
+// value_fwd_kernel (one CTA per chain): 4 value warps hold the state rows as
+// mma accumulators and walk the chunks in order; a producer warp streams each
+// chunk's KeyRec (one bulk copy) and v tile (TMA) into a ring of NS slots.
+// The value warps write y, sa and, at the start of every even chunk >= 2, the
+// bf16 state (rec::state_ptr) for the backward.
+// ===========================================================================
+
+namespace ka {
+
+constexpr int kGroups = 2;
+constexpr int kThreads = 128 * kGroups;
+constexpr int NR = 2;  // input buffers per group
+
+struct alignas(1024) Group {
+  bf16 raw[NR][5][L * kN];  // r, w, k, a, b tiles as landed by TMA (1 KiB aligned)
+  rec::KeyRec out;          // staging of the record for the bulk store
+  Tile At, Rt, W, Qy, Bb, Kb;
+  Tile16 Bm, Cm, Dm, Ti, Q, P;
+  float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
+  float lam[kN];
+  uint64_t rawbar[NR];
+};
+
+struct Params {
+  CUtensorMap maps[5];  // r, w, k, a, b
+  Geom g;
+  void* ckpt;
+};
+
+__device__ __forceinline__ void issue(Group& G, int rb, const Params& P, int64_t item) {
+  const int64_t ch = item / P.g.nchunk, c = item % P.g.nchunk;
+  const int h = static_cast<int>(P.g.h0 + ch % P.g.hc), b = static_cast<int>(ch / P.g.hc);
+  mbar_arrive_expect_tx(&G.rawbar[rb], 5 * tma::kTileBytes);
+#pragma unroll
+  for (int t = 0; t < 5; ++t) tma::load_tile(G.raw[rb][t], &P.maps[t], h, static_cast<int>(c * L), b, &G.rawbar[rb]);
+}
+
+__global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant__ Params P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Group* groups = reinterpret_cast<Group*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = warp >> 2, gw = warp & 3, gtid = tid & 127, bar_id = 1 + grp;
+  Group& G = groups[grp];
+  if (gtid == 0) {
+    for (int i = 0; i < NR; ++i) mbar_init(&G.rawbar[i], 1);
+    mbar_fence_init();
+  }
+  named_sync(bar_id, 128);
+  const int64_t total = P.g.chains() * P.g.nchunk;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * kGroups + grp;
+  const int64_t ngroups = static_cast<int64_t>(gridDim.x) * kGroups;
+  if (gtid == 0)
+    for (int i = 0; i < NR; ++i)
+      if (gid + i * ngroups < total) issue(G, i, P, gid + i * ngroups);
+  int64_t j = 0;
+  for (;; ++j) {
+    const int64_t item = gid + j * ngroups;
+    if (item >= total) break;
+    const int rb = static_cast<int>(j % NR);
+    bool ok = mbar_wait(&G.rawbar[rb], static_cast<uint32_t>((j / NR) & 1));
+    ok = named_sync_and(bar_id, 128, ok);
+    if (!ok) break;
+    ks::decays<true>(G.raw[rb][0], G.raw[rb][1], G.raw[rb][2], G.raw[rb][3], G.raw[rb][4], G.At,
+                     G.Rt, G.Kb, G.Bb, G.lam, nullptr, nullptr, gtid);
+    named_sync(bar_id, 128);
+    if (gtid == 0 && item + NR * ngroups < total) issue(G, rb, P, item + NR * ngroups);
+    ks::grams(G.At, G.Rt, G.Bb, G.Kb, G.Ga, G.Bm, G.Cm, G.Dm, gw, lane);
+    named_sync(bar_id, 128);
+    if (gw == 0) ks::inverse(G.Ga, G.Tf, G.Mf, G.Ti, lane);
+    named_sync(bar_id, 128);
+    ks::w_and_q(G.Ti, G.At, G.Bm, G.W, G.Q, gw, lane);
+    named_sync(bar_id, 128);
+    ks::qy_and_p(G.Cm, G.W, G.Rt, G.Q, G.Dm, G.Qy, G.P, gw, lane);
+    if (gtid == 0) bulk_wait_read();  // the previous record has left `out`
+    named_sync(bar_id, 128);
+    // pack W, Qy, Bb, Kb, Q, P, lam into the record (16-byte pieces, swizzled layouts)
+    for (int pc = gtid; pc < 592; pc += 128) {
+      uint4 v;
+      void* dst;
+      if (pc < 512) {
+        const int t = pc >> 7, r = (pc >> 3) & 15, k = pc & 7;
+        const Tile& src = t == 0 ? G.W : t == 1 ? G.Qy : t == 2 ? G.Bb : G.Kb;
+        bf16* d = t == 0 ? G.out.W : t == 1 ? G.out.Qy : t == 2 ? G.out.Bb : G.out.Kb;
+        v = *reinterpret_cast<const uint4*>(&src[r][8 * k]);
+        dst = d + Swz64{}(r, 8 * k);
+      } else if (pc < 576) {
+        const int t = (pc - 512) >> 5, r = ((pc - 512) >> 1) & 15, k = pc & 1;
+        const Tile16& src = t == 0 ? G.Q : G.P;
+        v = *reinterpret_cast<const uint4*>(&src[r][8 * k]);
+        dst = (t == 0 ? G.out.Q : G.out.P) + Swz16{}(r, 8 * k);
+      } else {
+        v = *reinterpret_cast<const uint4*>(&G.lam[4 * (pc - 576)]);
+        dst = &G.out.lam[4 * (pc - 576)];
+      }
+      *reinterpret_cast<uint4*>(dst) = v;
+    }
+    fence_proxy_async();
+    named_sync(bar_id, 128);
+    if (gtid == 0) {
+      const int64_t ch = item / P.g.nchunk, c = item % P.g.nchunk;
+      bulk_s2g(rec::keyrec(P.ckpt, ch, P.g.nchunk, c), &G.out, sizeof(rec::KeyRec));
+      bulk_commit();
+    }
+  }
+  if (gtid == 0) {
+    bulk_wait_all();
+    // after a timeout, let loads in flight land before the CTA exits
+    for (int64_t jj = j; jj < j + NR; ++jj)
+      if (gid + jj * ngroups < total) mbar_wait(&G.rawbar[jj % NR], static_cast<uint32_t>((jj / NR) & 1));
+  }
+}
+
+}  // namespace ka
+
+namespace vf {
+
+constexpr int NS = 6;
+constexpr int kThreads = 160;  // 4 value warps + 1 producer warp
+
+struct alignas(1024) Slot {
+  bf16 v[L * kN];  // v tile as landed by TMA (1 KiB aligned)
+  rec::KeyRec k;
+};
+
+struct Smem {
+  Slot slot[NS];
+  uint64_t full[NS], empty[NS];
+};
+
+struct Params {
+  CUtensorMap map_v;
+  FwdArgs a;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) value_fwd_kernel(const __grid_constant__ Params P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
+  const FwdArgs& p = P.a;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t ch = blockIdx.x;
+  const int64_t nchunk = p.g.nchunk, T = p.g.T, ts = p.g.tstride();
+  const int64_t cbase = p.g.base(ch);
+
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 4);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == 4) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      const int hh = static_cast<int>(p.g.h0 + ch % p.g.hc), bb = static_cast<int>(ch / p.g.hc);
+      int64_t c = 0;
+      for (; c < nchunk; ++c) {
+        const int s = static_cast<int>(c % NS);
+        if (c >= NS && !mbar_wait(&sm.empty[s], static_cast<uint32_t>((c / NS - 1) & 1))) break;
+        mbar_arrive_expect_tx(&sm.full[s], sizeof(rec::KeyRec) + tma::kTileBytes);
+        bulk_g2s(&sm.slot[s].k, rec::keyrec(p.ckpt, ch, nchunk, c), sizeof(rec::KeyRec), &sm.full[s]);
+        tma::load_tile(sm.slot[s].v, &P.map_v, hh, static_cast<int>(c * L), bb, &sm.full[s]);
+      }
+      if (c < nchunk)  // stopped on a timeout: let the copies in flight land
+        for (int64_t cc = c > NS ? c - NS : 0; cc < c; ++cc)
+          mbar_wait(&sm.full[cc % NS], static_cast<uint32_t>((cc / NS) & 1));
+    }
+    return;
+  }
+
+  // ------------------------------ value warps ------------------------------
+  const int wq = warp, g = lane >> 2, q = lane & 3, i0 = 16 * wq;
+  const int64_t chains = p.g.chains();
+  float S[8][4];
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
+  bf16* yp = static_cast<bf16*>(p.y);
+  for (int64_t c = 0; c < nchunk; ++c) {
+    const int s = static_cast<int>(c % NS);
+    if (!mbar_wait(&sm.full[s], static_cast<uint32_t>((c / NS) & 1))) break;
+    const rec::KeyRec& kr = sm.slot[s].k;
+
+    uint32_t sA[4][4], vA[4], b[4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) acc_to_a(sA[kk], S[2 * kk], S[2 * kk + 1]);
+    if ((c & 1) == 0 && c >= 2) {
+      uint4* dst = reinterpret_cast<uint4*>(rec::state_ptr(p.ckpt, chains, ch, nchunk, c));
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        dst[(wq * 4 + kk) * 32 + lane] = make_uint4(sA[kk][0], sA[kk][1], sA[kk][2], sA[kk][3]);
+    }
+    lda_cm(vA, sm.slot[s].v, Swz64{}, i0, 0, lane);
+    float sa[2][4] = {}, yv[2][4] = {};
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
+      mma16816(sa[0], sA[kk], b[0], b[1]);
+      mma16816(sa[1], sA[kk], b[2], b[3]);
+      ldb_nk(b, kr.Qy, Swz64{}, 0, 16 * kk, lane);
+      mma16816(yv[0], sA[kk], b[0], b[1]);
+      mma16816(yv[1], sA[kk], b[2], b[3]);
+    }
+    ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
+    mma16816(sa[0], vA, b[0], b[1]);
+    mma16816(sa[1], vA, b[2], b[3]);
+    ldb_nk(b, kr.P, Swz16{}, 0, 0, lane);
+    mma16816(yv[0], vA, b[0], b[1]);
+    mma16816(yv[1], vA, b[2], b[3]);
+
+    uint32_t saA[4];
+    acc_to_a(saA, sa[0], sa[1]);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      ldb_kn(b, kr.Bb, Swz64{}, 16 * m, 0, lane);
+      mma16816(S[2 * m], saA, b[0], b[1]);
+      mma16816(S[2 * m + 1], saA, b[2], b[3]);
+      ldb_kn(b, kr.Kb, Swz64{}, 16 * m, 0, lane);
+      mma16816(S[2 * m], vA, b[0], b[1]);
+      mma16816(S[2 * m + 1], vA, b[2], b[3]);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
+      S[nt][0] *= l.x; S[nt][1] *= l.y; S[nt][2] *= l.x; S[nt][3] *= l.y;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[s]);
+
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = i0 + g + (e >= 2 ? 8 : 0);
+        const int64_t t = c * L + 8 * nt + 2 * q + (e & 1);
+        if (t < T) {
+          const int64_t o = cbase + t * ts + i;
+          p.sa[o] = sa[nt][e];
+          yp[o] = __float2bfloat16_rn(yv[nt][e]);
+        }
+      }
+  }
+}
+
+}  // namespace vf
+
+
 // wait timeouts recorded by this file's kernels on the current device
 unsigned int fwd_timeouts() {
   unsigned int n = 0;
@@ -252,16 +503,48 @@ unsigned int fwd_timeouts() {
 }
 
 cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
-  fwd::Params P;
-  P.a = p;
-  const void* src[fwd::kNumRaw] = {p.r, p.w, p.k, p.a, p.b, p.v};
-  for (int t = 0; t < fwd::kNumRaw; ++t)
-    if (!tma::encode_bhtn(&P.maps[t], src[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
-  const size_t smem = sizeof(fwd::Smem) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(fwd::chunked_fwd_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (p.ckpt == nullptr) {  // inference: one fused kernel, nothing stored
+    fwd::Params P;
+    P.a = p;
+    const void* src[fwd::kNumRaw] = {p.r, p.w, p.k, p.a, p.b, p.v};
+    for (int t = 0; t < fwd::kNumRaw; ++t)
+      if (!tma::encode_bhtn(&P.maps[t], src[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(fwd::Smem) + 1024;
+    cudaError_t e = cudaFuncSetAttribute(fwd::chunked_fwd_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    fwd::chunked_fwd_kernel<<<(unsigned)p.g.chains(), fwd::kThreads, smem, stream>>>(P);
+    return cudaGetLastError();
+  }
+  // training: key-side records over all SMs, then the sequential value pass
+  ka::Params K;
+  K.g = p.g;
+  K.ckpt = p.ckpt;
+  const void* ksrc[5] = {p.r, p.w, p.k, p.a, p.b};
+  for (int t = 0; t < 5; ++t)
+    if (!tma::encode_bhtn(&K.maps[t], ksrc[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
+  vf::Params V;
+  V.a = p;
+  if (!tma::encode_bhtn(&V.map_v, p.v, p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
+
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t ksmem = ka::kGroups * sizeof(ka::Group) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(ka::keyside_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ksmem);
   if (e != cudaSuccess) return e;
-  fwd::chunked_fwd_kernel<<<(unsigned)p.g.chains(), fwd::kThreads, smem, stream>>>(P);
+  const int64_t items = p.g.chains() * p.g.nchunk;
+  const int64_t want = (items + ka::kGroups - 1) / ka::kGroups;
+  const int64_t kgrid = want < 2LL * sms ? want : 2LL * sms;
+  ka::keyside_kernel<<<(unsigned)kgrid, ka::kThreads, ksmem, stream>>>(K);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+
+  const size_t vsmem = sizeof(vf::Smem) + 1024;
+  e = cudaFuncSetAttribute(vf::value_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)vsmem);
+  if (e != cudaSuccess) return e;
+  vf::value_fwd_kernel<<<(unsigned)p.g.chains(), vf::kThreads, vsmem, stream>>>(V);
   return cudaGetLastError();
 }
 

@@ -122,5 +122,59 @@ __device__ __forceinline__ void store_acc_f32(float* tile, int ld, int m0, int n
   tile[(m0 + g + 8) * ld + n0 + 2 * q + 1] = c[3];
 }
 
+// ---- layout-generic loaders --------------------------------------------------
+// A layout maps (row, column) of a bf16 tile to an element offset; row starts
+// of 8-column (16-byte) pieces must be 16-byte aligned.
+struct Padded {  // row-major with padded row stride
+  int ld;
+  __device__ __forceinline__ int operator()(int r, int c) const { return r * ld + c; }
+};
+struct Swz64 {  // 64 columns, 128-byte rows, 16-byte pieces XOR-swizzled by (row & 7)
+  __device__ __forceinline__ int operator()(int r, int c) const {
+    return r * 64 + ((((c >> 3) ^ (r & 7))) << 3) + (c & 7);
+  }
+};
+struct Swz16 {  // 16 columns, 32-byte rows, the two pieces swizzled by bit 2 of the row
+  __device__ __forceinline__ int operator()(int r, int c) const {
+    return r * 16 + ((((c >> 3) ^ ((r >> 2) & 1))) << 3) + (c & 7);
+  }
+};
+
+template <typename Lay>
+__device__ __forceinline__ void lda_rm(uint32_t (&a)[4], const __nv_bfloat16* tile, Lay lay,
+                                       int m0, int k0, int lane) {
+  ldsm_x4(a, tile + lay(m0 + (lane & 7) + ((lane >> 3) & 1) * 8, k0 + (lane >> 4) * 8));
+}
+template <typename Lay>
+__device__ __forceinline__ void lda_cm(uint32_t (&a)[4], const __nv_bfloat16* tile, Lay lay,
+                                       int m0, int k0, int lane) {
+  ldsm_x4_t(a, tile + lay(k0 + (lane & 7) + (lane >> 4) * 8, m0 + ((lane >> 3) & 1) * 8));
+}
+template <typename Lay>
+__device__ __forceinline__ void ldb_nk(uint32_t (&b)[4], const __nv_bfloat16* tile, Lay lay,
+                                       int n0, int k0, int lane) {
+  ldsm_x4(b, tile + lay(n0 + (lane & 7) + (lane >> 4) * 8, k0 + ((lane >> 3) & 1) * 8));
+}
+template <typename Lay>
+__device__ __forceinline__ void ldb_kn(uint32_t (&b)[4], const __nv_bfloat16* tile, Lay lay,
+                                       int n0, int k0, int lane) {
+  ldsm_x4_t(b, tile + lay(k0 + (lane & 7) + ((lane >> 3) & 1) * 8, n0 + (lane >> 4) * 8));
+}
+
+// acc (16 x 16 output at columns n0) += A (16 x 16*KS) B;
+// AT: A stored [k][m] (else [m][k]); BT: B stored [k][n] (else [n][k]).
+template <bool AT, bool BT, int KS, typename LA, typename LB>
+__device__ __forceinline__ void mm16(float (&acc)[2][4], const __nv_bfloat16* A, LA la,
+                                     const __nv_bfloat16* B, LB lb, int n0, int lane) {
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk) {
+    uint32_t a[4], b[4];
+    if (AT) lda_cm(a, A, la, 0, 16 * kk, lane); else lda_rm(a, A, la, 0, 16 * kk, lane);
+    if (BT) ldb_kn(b, B, lb, n0, 16 * kk, lane); else ldb_nk(b, B, lb, n0, 16 * kk, lane);
+    mma16816(acc[0], a, b[0], b[1]);
+    mma16816(acc[1], a, b[2], b[3]);
+  }
+}
+
 }  // namespace mma
 }  // namespace camoe

@@ -21,7 +21,8 @@
 //
 // The array is shared by every call and keeps the last call's contents.
 // Nothing in it needs to start at zero: the forward writes every checkpoint
-// slot that the backward of the same call reads.  Calls whose work overlaps
+// record that the backward of the same call reads, and the backward writes
+// its workspace records before reading them.  Calls whose work overlaps
 // on the GPU (different streams, or several host threads) race on the array.
 #include <mutex>
 
@@ -38,8 +39,7 @@ cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream);
 }  // namespace scan
 namespace chunked {
 cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream);
-cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream);
-size_t ckpt_bytes(int64_t chains, int64_t T);
+cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream);
 }  // namespace chunked
 }  // namespace camoe
 
@@ -99,8 +99,11 @@ extern "C" int camoe_wkv7_fwd_bwd_noalloc(
     if (!aligned16(p)) return CAMOE_ERR_ALIGNMENT;
   }
   if (dsa != nullptr && !aligned16(dsa)) return CAMOE_ERR_ALIGNMENT;
+  // the scratch holds the checkpoint, then the backward workspace
   const size_t need = camoe_wkv7_ckpt_bytes(B, T, h_count, N, dtype, al);
-  if (need > CAMOE_WKV7_NOALLOC_SCRATCH_BYTES) return CAMOE_ERR_WORKSPACE;
+  const size_t wneed = camoe_wkv7_work_bytes(B, T, h_count, N, dtype, al);
+  const size_t wofs = (need + 255) & ~static_cast<size_t>(255);
+  if (wofs + wneed > CAMOE_WKV7_NOALLOC_SCRATCH_BYTES) return CAMOE_ERR_WORKSPACE;
 
   void* scratch = nullptr;
   const int st = scratch_address(&scratch);
@@ -118,7 +121,7 @@ extern "C" int camoe_wkv7_fwd_bwd_noalloc(
   cudaError_t e;
   if (al == CAMOE_ALGO_CHUNKED) {
     e = camoe::chunked::launch_fwd(f, s);
-    if (e == cudaSuccess) e = camoe::chunked::launch_bwd(p, s);
+    if (e == cudaSuccess) e = camoe::chunked::launch_bwd(p, static_cast<char*>(scratch) + wofs, s);
   } else if (dtype == CAMOE_DTYPE_BF16) {
     e = camoe::scan::launch_fwd<camoe::bf16>(f, s);
     if (e == cudaSuccess) e = camoe::scan::launch_bwd<camoe::bf16>(p, s);

@@ -1,0 +1,70 @@
+// Per-chunk records that the chunked kernels exchange through global memory,
+// and the state checkpoint, all inside the caller's checkpoint buffer or the
+// backward workspace.
+//
+// Checkpoint buffer (written by the forward, read by the backward), for
+// `chains` chains of `nchunk` 16-step chunks:
+//   [chains][nchunk] KeyRec      key-side matrices of every chunk
+//   [chains][nstate] state       bf16 64x64 state at the start of chunks
+//                                2, 4, 6, ... (mma A-fragment order)
+// nstate = (nchunk - 1) / 2; the state at the start of odd chunks is
+// recomputed from the preceding even one, chunk 0 starts from zero.  Per
+// chunk this is 9472 + 4096 bytes, below the 16 KiB per chunk of the
+// reference's [B, H, T/16, 64, 64] fp32 checkpoint tensor.
+//
+// Backward workspace: [chains][nchunk] ProdRec.
+#pragma once
+
+#include "wkv7_common.cuh"
+
+namespace camoe {
+namespace rec {
+
+// 16 x 64 bf16 tiles are stored Swz64, 16 x 16 tiles Swz16 (see wkv7_mma.cuh),
+// so a bulk copy lands them in shared memory ready for conflict-free ldmatrix.
+struct KeyRec {
+  bf16 W[16 * 64], Qy[16 * 64], Bb[16 * 64], Kb[16 * 64];
+  bf16 Q[16 * 16], P[16 * 16];
+  float lam[64];
+};
+static_assert(sizeof(KeyRec) == 9472, "KeyRec layout");
+
+// sums over the 64 state rows that the key-side backward needs (plain row-major)
+struct ProdRec {
+  float dW[16 * 64];   // dSA S
+  float dQy[16 * 64];  // dY S
+  float dBb[16 * 64];  // SA (dS' diag lam)
+  float dKb[16 * 64];  // V (dS' diag lam)
+  float dQ[16 * 16];   // strict(dSA V^T)
+  float dP[16 * 16];   // lower(dY V^T)
+  float dll[64];       // colsum(dS' o S') over the chunk's end state
+};
+static_assert(sizeof(ProdRec) % 16 == 0, "ProdRec size");
+
+constexpr int64_t kStateBytes = 64 * 64 * 2;
+
+__host__ __device__ __forceinline__ int64_t nstate(int64_t nchunk) {
+  return nchunk > 0 ? (nchunk - 1) / 2 : 0;
+}
+__host__ __device__ __forceinline__ size_t ckpt_bytes(int64_t chains, int64_t nchunk) {
+  return static_cast<size_t>(chains * nchunk) * sizeof(KeyRec) +
+         static_cast<size_t>(chains * nstate(nchunk)) * kStateBytes;
+}
+__host__ __device__ __forceinline__ size_t work_bytes(int64_t chains, int64_t nchunk) {
+  return static_cast<size_t>(chains * nchunk) * sizeof(ProdRec);
+}
+__device__ __forceinline__ KeyRec* keyrec(void* ckpt, int64_t ch, int64_t nchunk, int64_t c) {
+  return reinterpret_cast<KeyRec*>(ckpt) + (ch * nchunk + c);
+}
+// state at the start of even chunk c >= 2
+__device__ __forceinline__ char* state_ptr(void* ckpt, int64_t chains, int64_t ch,
+                                           int64_t nchunk, int64_t c) {
+  char* base = reinterpret_cast<char*>(ckpt) + chains * nchunk * sizeof(KeyRec);
+  return base + (ch * nstate(nchunk) + (c / 2 - 1)) * kStateBytes;
+}
+__device__ __forceinline__ ProdRec* prodrec(void* work, int64_t ch, int64_t nchunk, int64_t c) {
+  return reinterpret_cast<ProdRec*>(work) + (ch * nchunk + c);
+}
+
+}  // namespace rec
+}  // namespace camoe

@@ -27,6 +27,8 @@ __host__ __device__ __forceinline__ int swz(int r, int c) {
 
 // Encode the (N, H, T, B) map of a bf16 [B, T, H, 64] array; returns false on failure.
 bool encode_bhtn(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H);
+// Same for an fp32 array, without swizzle: a chunk lands as a plain [16][64] fp32 tile.
+bool encode_bhtn_f32(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H);
 
 __device__ __forceinline__ void load_tile(void* dst_smem, const CUtensorMap* map, int h,
                                           int t0, int b, uint64_t* bar) {

@@ -57,6 +57,11 @@ def ckpt_bytes(B: int, T: int, h_count: int, dtype: torch.dtype, algo="auto") ->
                                                 algo_code(algo)))
 
 
+def work_bytes(B: int, T: int, h_count: int, dtype: torch.dtype, algo="auto") -> int:
+    return int(_lib.lib().camoe_wkv7_work_bytes(B, T, h_count, HEAD_SIZE, dtype_code(dtype),
+                                                algo_code(algo)))
+
+
 def wkv7_forward(r, w, k, v, a, b, *, algo="auto", save_ckpt: bool = True, h0: int = 0,
                  h_count: int | None = None, y=None, sa=None, ckpt=None, zero_rest=False):
     """Forward.  Returns (y, sa, ckpt); ckpt is None when save_ckpt is False."""
@@ -86,8 +91,9 @@ def wkv7_forward(r, w, k, v, a, b, *, algo="auto", save_ckpt: bool = True, h0: i
 
 
 def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
-                  h_count: int | None = None, grads=None, zero_rest=False):
-    """Backward.  ``dsa`` (fp32) may be None.  Returns (dr, dw, dk, dv, da, db)."""
+                  h_count: int | None = None, grads=None, zero_rest=False, work=None):
+    """Backward.  ``dsa`` (fp32) may be None.  Returns (dr, dw, dk, dv, da, db).
+    ``work`` is the scratch workspace (allocated here when not given)."""
     _check_inputs((r, w, k, v, a, b, dy), "rwkvab" + "y")
     B, T, H, N = r.shape
     hc = H - h0 if h_count is None else h_count
@@ -99,10 +105,15 @@ def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
         alloc = torch.zeros if zero_rest else torch.empty
         grads = tuple(alloc(B, T, H, N, dtype=r.dtype, device=r.device) for _ in range(6))
     nbytes = 0 if ckpt is None else ckpt.numel() * ckpt.element_size()
+    wneed = work_bytes(B, T, hc, r.dtype, algo)
+    if work is None and wneed > 0:
+        work = torch.empty(wneed, dtype=torch.uint8, device=r.device)
+    wbytes = 0 if work is None else work.numel() * work.element_size()
     st = _lib.lib().camoe_wkv7_bwd(
         r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(),
         dy.data_ptr(), None if dsa is None else dsa.data_ptr(),
         None if ckpt is None else ckpt.data_ptr(), nbytes,
+        None if work is None else work.data_ptr(), wbytes,
         *(g.data_ptr() for g in grads), B, T, H, h0, hc, N, dtype_code(r.dtype),
         algo_code(algo), _stream_ptr(r.device))
     check(st)

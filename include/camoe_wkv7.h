@@ -17,12 +17,14 @@
  * always fp32.  The caller owns every buffer; nothing is allocated.  All
  * pointers must be 16-byte aligned device pointers.
  *
- * The forward writes a per-chain state checkpoint that the backward reads.
- * Its size comes from camoe_wkv7_ckpt_bytes(); it never exceeds the
- * reference's [B, H, T/16, N, N] fp32 checkpoint tensor, so that tensor can
- * be passed as the buffer.  The forward and backward of one pair must use
- * the same dtype, algo and shape.  Passing ckpt = NULL to the forward skips
- * the checkpoint (inference).
+ * The forward writes a per-chain checkpoint that the backward reads.  Its
+ * size comes from camoe_wkv7_ckpt_bytes(); it never exceeds the reference's
+ * [B, H, T/16, N, N] fp32 checkpoint tensor, so that tensor can be passed as
+ * the buffer.  The forward and backward of one pair must use the same dtype,
+ * algo and shape.  Passing ckpt = NULL to the forward skips the checkpoint
+ * (inference).  The backward also takes a scratch workspace of
+ * camoe_wkv7_work_bytes() bytes (0 for the scan algorithm); the checkpoint is
+ * only read, so a backward can be repeated.
  *
  * Calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy default
  * stream); all but camoe_wkv7_fwd_bwd_noalloc keep no global state and may
@@ -61,7 +63,7 @@ extern "C" {
 #define CAMOE_ERR_UNSUPPORTED 2  /* N != 64, unknown dtype/algo, fp32 with CHUNKED */
 #define CAMOE_ERR_SHAPE 3        /* T not a multiple of 16 */
 #define CAMOE_ERR_ALIGNMENT 4    /* a pointer is not 16-byte aligned */
-#define CAMOE_ERR_WORKSPACE 5    /* ckpt_bytes smaller than camoe_wkv7_ckpt_bytes() */
+#define CAMOE_ERR_WORKSPACE 5    /* checkpoint or workspace smaller than required */
 #define CAMOE_ERR_CUDA 6         /* a CUDA launch failed; see camoe_wkv7_last_cuda_error() */
 
 /* Version of this ABI (major*10000 + minor*100 + patch). */
@@ -85,6 +87,10 @@ unsigned int camoe_wkv7_device_errors(void);
 size_t camoe_wkv7_ckpt_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype,
                              int algo);
 
+/* Bytes of backward workspace for the same problem (0 when none is needed). */
+size_t camoe_wkv7_work_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype,
+                             int algo);
+
 /* Forward.  Writes y (dtype) and sa (fp32) for heads [h0, h0+h_count) and,
  * when ckpt != NULL, the state checkpoint.  Replaces
  * torch.ops.rwkv7_clampw.forward (camoe/cuda/rwkv7_clampw.cpp:12-15). */
@@ -100,9 +106,10 @@ int camoe_wkv7_fwd(const void* r, const void* w, const void* k, const void* v,
  * gradient (camoe/backbone.py:95). */
 int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v,
                    const void* a, const void* b, const void* dy, const float* dsa,
-                   const void* ckpt, size_t ckpt_bytes, void* dr, void* dw, void* dk,
-                   void* dv, void* da, void* db, int64_t B, int64_t T, int64_t H_total,
-                   int64_t h0, int64_t h_count, int N, int dtype, int algo, void* stream);
+                   const void* ckpt, size_t ckpt_bytes, void* work, size_t work_bytes,
+                   void* dr, void* dw, void* dk, void* dv, void* da, void* db, int64_t B,
+                   int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
+                   int algo, void* stream);
 
 /* Size of the library-owned checkpoint scratch used by
  * camoe_wkv7_fwd_bwd_noalloc (64 MiB per GPU that loads the library). */
@@ -115,8 +122,9 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v,
  * Writes y, sa and the six gradients like camoe_wkv7_fwd followed by
  * camoe_wkv7_bwd, with the state checkpoint kept in a library-owned device
  * array of CAMOE_WKV7_NOALLOC_SCRATCH_BYTES instead of a caller buffer.
- * Returns CAMOE_ERR_WORKSPACE when camoe_wkv7_ckpt_bytes() of the problem
- * exceeds that size (e.g. at most 4096 chains x 16-step chunks).  The first
+ * Returns CAMOE_ERR_WORKSPACE when camoe_wkv7_ckpt_bytes() plus
+ * camoe_wkv7_work_bytes() of the problem exceed that size (about 2200 chains x
+ * 16-step chunks for the chunked algorithm, 4096 for the scan).  The first
  * call on a device looks up the array's address (cudaGetSymbolAddress); make
  * it before any stream capture.  All calls share the array: calls whose work
  * overlaps on the GPU race. */

@@ -61,6 +61,13 @@ def _fwd(B=1, T=16, H=1, h0=0, hc=1, N=64, dtype=0, algo=0, ptr=16, ckpt=None, n
                               dtype, algo, None)
 
 
+def test_work_bytes():
+    lib = _lib.lib()
+    assert lib.camoe_wkv7_work_bytes(4, 4096, 16, 64, _lib.DTYPE_FP32, _lib.ALGO_SCAN) == 0
+    assert lib.camoe_wkv7_work_bytes(4, 4096, 16, 64, _lib.DTYPE_BF16, _lib.ALGO_CHUNKED) > 0
+    assert lib.camoe_wkv7_work_bytes(4, 4096, 16, 32, _lib.DTYPE_BF16, _lib.ALGO_CHUNKED) == 0
+
+
 def test_fwd_argument_errors_need_no_device():
     assert _fwd(N=32) == _lib.ERR_UNSUPPORTED
     assert _fwd(B=-1) == _lib.ERR_INVALID_ARG
@@ -81,15 +88,18 @@ def test_bwd_argument_errors_need_no_device():
     lib = _lib.lib()
     p = ctypes.c_void_p(16)
 
-    def bwd(ckpt=p, nbytes=1 << 40, dsa=None, **kw):
+    def bwd(ckpt=p, nbytes=1 << 40, dsa=None, work=p, wbytes=1 << 40, **kw):
         g = dict(B=1, T=32, H=1, h0=0, hc=1, N=64, dtype=0, algo=0)
         g.update(kw)
-        return lib.camoe_wkv7_bwd(p, p, p, p, p, p, p, dsa, ckpt, nbytes, p, p, p, p, p, p,
-                                  g["B"], g["T"], g["H"], g["h0"], g["hc"], g["N"], g["dtype"],
-                                  g["algo"], None)
+        return lib.camoe_wkv7_bwd(p, p, p, p, p, p, p, dsa, ckpt, nbytes, work, wbytes,
+                                  p, p, p, p, p, p, g["B"], g["T"], g["H"], g["h0"], g["hc"],
+                                  g["N"], g["dtype"], g["algo"], None)
 
     assert bwd(ckpt=None) == _lib.ERR_INVALID_ARG
     assert bwd(nbytes=100) == _lib.ERR_WORKSPACE
+    assert bwd(work=None) == _lib.ERR_INVALID_ARG            # chunked needs a workspace
+    assert bwd(wbytes=100) == _lib.ERR_WORKSPACE
+    assert bwd(work=ctypes.c_void_p(24)) == _lib.ERR_ALIGNMENT
     assert bwd(dsa=ctypes.c_void_p(20)) == _lib.ERR_ALIGNMENT
     assert bwd(N=128) == _lib.ERR_UNSUPPORTED
     assert bwd(B=0) == _lib.OK
