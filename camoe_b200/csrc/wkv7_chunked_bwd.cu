@@ -49,7 +49,7 @@ using ks::Tile16;
 
 namespace vb {
 
-constexpr int NS = 4;
+constexpr int NS = 6;
 constexpr int kThreads = 288;  // value warps 0-3, cross warps 4-7, producer warp 8
 
 struct alignas(1024) Slot {
@@ -95,6 +95,150 @@ __device__ __forceinline__ void group_of(int64_t nchunk, int64_t gi, int64_t& lo
 }
 
 __device__ __forceinline__ int64_t num_groups(int64_t nchunk) { return (nchunk + 1) / 2; }
+
+// One chunk of the value-warp backward (warp wq owns state rows 16wq..16wq+15):
+// G'' = G diag(lam); SA (or the precomputed satPre); dSA; dV -> global; the bf16
+// copies of S, G'', SA, dSA -> cross buffer (done & 1); G <- dS; the column sums
+// of G o S for the next chunk -> next cross buffer.  False on a timeout.
+__device__ __forceinline__ bool value_chunk(Smem& sm, const BwdArgs& p, int64_t c, int s,
+                                            int64_t done, int64_t nchunk,
+                                            const uint32_t (&sA)[4][4], const float (&satPre)[2][4],
+                                            bool have_sat, float (&G)[8][4], int wq, int lane,
+                                            int64_t cbase, int64_t ts, int64_t T, bool has_dsa) {
+  const int g = lane >> 2, q = lane & 3, i0 = 16 * wq;
+  const int xb = static_cast<int>(done & 1);
+  const Slot& sl = sm.slot[s];
+  const rec::KeyRec& kr = sl.k;
+  uint32_t b[4], vA[4], dyA[4];
+
+  // G'' = G diag(lam)
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
+    G[nt][0] *= l.x; G[nt][1] *= l.y; G[nt][2] *= l.x; G[nt][3] *= l.y;
+  }
+  uint32_t gA[4][4];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) acc_to_a(gA[kk], G[2 * kk], G[2 * kk + 1]);
+  lda_cm(vA, sl.v, Swz64{}, i0, 0, lane);
+  lda_cm(dyA, sl.dy, Swz64{}, i0, 0, lane);
+
+  float sat[2][4], dsat[2][4];
+  if (have_sat) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sat[nt][e] = satPre[nt][e];
+  } else {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sat[nt][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
+      mma16816(sat[0], sA[kk], b[0], b[1]);
+      mma16816(sat[1], sA[kk], b[2], b[3]);
+    }
+    ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
+    mma16816(sat[0], vA, b[0], b[1]);
+    mma16816(sat[1], vA, b[2], b[3]);
+  }
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      dsat[nt][e] = has_dsa ? sl.dsa[8 * nt + 2 * q + (e & 1)][i0 + g + (e >= 2 ? 8 : 0)] : 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    ldb_nk(b, kr.Bb, Swz64{}, 0, 16 * kk, lane);
+    mma16816(dsat[0], gA[kk], b[0], b[1]);
+    mma16816(dsat[1], gA[kk], b[2], b[3]);
+  }
+  uint32_t dsaA[4];
+  acc_to_a(dsaA, dsat[0], dsat[1]);
+
+  // bf16 copies of S, G'', SA, dSA for the cross warps (buffer freed at the previous chunk)
+  XBuf& X = sm.xb[xb];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {  // A fragment regs -> rows g / g+8, cols 16kk + 2q (+8)
+      const int col = 16 * kk + 2 * q + 8 * h;
+      *reinterpret_cast<uint32_t*>(&X.S[i0 + g][col]) = sA[kk][2 * h];
+      *reinterpret_cast<uint32_t*>(&X.S[i0 + g + 8][col]) = sA[kk][2 * h + 1];
+      *reinterpret_cast<uint32_t*>(&X.G[i0 + g][col]) = gA[kk][2 * h];
+      *reinterpret_cast<uint32_t*>(&X.G[i0 + g + 8][col]) = gA[kk][2 * h + 1];
+    }
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    store_acc_bf16(&X.SAT[0][0], LDS, i0, 8 * nt, sat[nt], lane);
+    store_acc_bf16(&X.dSAT[0][0], LDS, i0, 8 * nt, dsat[nt], lane);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&sm.xfull[xb]);
+
+  // dV^T = G'' Kb^T + dY^T P + dSA^T Q
+  {
+    float dvt[2][4] = {};
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      ldb_nk(b, kr.Kb, Swz64{}, 0, 16 * kk, lane);
+      mma16816(dvt[0], gA[kk], b[0], b[1]);
+      mma16816(dvt[1], gA[kk], b[2], b[3]);
+    }
+    ldb_kn(b, kr.P, Swz16{}, 0, 0, lane);
+    mma16816(dvt[0], dyA, b[0], b[1]);
+    mma16816(dvt[1], dyA, b[2], b[3]);
+    ldb_kn(b, kr.Q, Swz16{}, 0, 0, lane);
+    mma16816(dvt[0], dsaA, b[0], b[1]);
+    mma16816(dvt[1], dsaA, b[2], b[3]);
+    bf16* dvp = static_cast<bf16*>(p.dv);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t t = c * L + 8 * nt + 2 * q + (e & 1);
+        if (t < T) dvp[cbase + t * ts + i0 + g + (e >= 2 ? 8 : 0)] = __float2bfloat16_rn(dvt[nt][e]);
+      }
+  }
+
+  // dS = G'' + dY^T Qy + dSA^T W  -> G of the previous chunk
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    ldb_kn(b, kr.Qy, Swz64{}, 16 * m, 0, lane);
+    mma16816(G[2 * m], dyA, b[0], b[1]);
+    mma16816(G[2 * m + 1], dyA, b[2], b[3]);
+    ldb_kn(b, kr.W, Swz64{}, 16 * m, 0, lane);
+    mma16816(G[2 * m], dsaA, b[0], b[1]);
+    mma16816(G[2 * m + 1], dsaA, b[2], b[3]);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&sm.empty[s]);
+
+  // dll of the next chunk to process: colsum over rows of G o S (S = this chunk's start state)
+  if (done + 1 < nchunk) {
+    const int nx = static_cast<int>((done + 1) & 1);
+    if (done + 1 >= 2 &&
+        !mbar_wait(&sm.xempty[nx], static_cast<uint32_t>((((done + 1) >> 1) - 1) & 1)))
+      return false;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const uint32_t lo2 = sA[nt >> 1][2 * (nt & 1)], hi2 = sA[nt >> 1][2 * (nt & 1) + 1];
+      const float2 s0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo2));
+      const float2 s1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi2));
+      float p0 = G[nt][0] * s0.x + G[nt][2] * s1.x;
+      float p1 = G[nt][1] * s0.y + G[nt][3] * s1.y;
+#pragma unroll
+      for (int m = 4; m < 32; m <<= 1) {
+        p0 += __shfl_xor_sync(0xffffffffu, p0, m);
+        p1 += __shfl_xor_sync(0xffffffffu, p1, m);
+      }
+      if (g == 0) *reinterpret_cast<float2*>(&sm.xb[nx].dll[wq][8 * nt + 2 * q]) = make_float2(p0, p1);
+    }
+  }
+  return true;
+}
 
 __global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -214,16 +358,16 @@ __global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_con
   }
 
   // ------------------------------ value warps ------------------------------
-  const int wq = warp, g = lane >> 2, q = lane & 3, i0 = 16 * wq;
+  const int wq = warp, i0 = 16 * wq, q = lane & 3;
   float G[8][4];  // dL/dS' of the chunk being processed
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) G[nt][e] = 0.f;
-  float dll[8][2];  // colsum(G o S') of the next chunk to process (lanes g == 0)
+  if ((lane >> 2) == 0)  // the first chunk processed has no following chunk: dll = 0
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) dll[nt][0] = dll[nt][1] = 0.f;
-  bf16* dvp = static_cast<bf16*>(p.dv);
+    for (int nt = 0; nt < 8; ++nt)
+      *reinterpret_cast<float2*>(&sm.xb[0].dll[wq][8 * nt + 2 * q]) = make_float2(0.f, 0.f);
   int64_t done = 0;
   for (int64_t gi = 0; gi < ngroups; ++gi) {
     int64_t lo, hi, idx_lo;
@@ -247,9 +391,9 @@ __global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_con
     }
     // SA of lo (needed by lo's backward, and by the recompute of hi's start state)
     float satLo[2][4] = {};
-    uint32_t vA[4], b[4];
     {
       const rec::KeyRec& kr = sm.slot[s_lo].k;
+      uint32_t vA[4], b[4];
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
@@ -260,181 +404,51 @@ __global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_con
       ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
       mma16816(satLo[0], vA, b[0], b[1]);
       mma16816(satLo[1], vA, b[2], b[3]);
-    }
-    uint32_t sHi[4][4] = {};
-    if (hi != lo) {  // S(hi) = (S(lo) + SA^T Bb + V^T Kb) diag(lam), from chunk lo
-      const rec::KeyRec& kr = sm.slot[s_lo].k;
-      float Sf[8][4];
+      if (hi != lo) {  // S(hi) = (S(lo) + SA^T Bb + V^T Kb) diag(lam), from chunk lo
+        uint32_t sHi[4][4];
+        {
+          float Sf[8][4];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
+          for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sLo[kk][h]));
-          const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sLo[kk][2 + h]));
-          // sLo[kk] = A fragment of n8 tiles (2kk, 2kk+1): regs 0,1 -> tile 2kk, regs 2,3 -> 2kk+1
-          Sf[2 * kk][2 * h] = a0.x;
-          Sf[2 * kk][2 * h + 1] = a0.y;
-          Sf[2 * kk + 1][2 * h] = a1.x;
-          Sf[2 * kk + 1][2 * h + 1] = a1.y;
-        }
-      uint32_t saA[4];
-      acc_to_a(saA, satLo[0], satLo[1]);
+            for (int h = 0; h < 2; ++h) {
+              // sLo[kk] is the A fragment of n8 tiles (2kk, 2kk+1): regs 0,1 -> 2kk, 2,3 -> 2kk+1
+              const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sLo[kk][h]));
+              const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sLo[kk][2 + h]));
+              Sf[2 * kk][2 * h] = a0.x;
+              Sf[2 * kk][2 * h + 1] = a0.y;
+              Sf[2 * kk + 1][2 * h] = a1.x;
+              Sf[2 * kk + 1][2 * h + 1] = a1.y;
+            }
+          uint32_t saA[4];
+          acc_to_a(saA, satLo[0], satLo[1]);
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        ldb_kn(b, kr.Bb, Swz64{}, 16 * m, 0, lane);
-        mma16816(Sf[2 * m], saA, b[0], b[1]);
-        mma16816(Sf[2 * m + 1], saA, b[2], b[3]);
-        ldb_kn(b, kr.Kb, Swz64{}, 16 * m, 0, lane);
-        mma16816(Sf[2 * m], vA, b[0], b[1]);
-        mma16816(Sf[2 * m + 1], vA, b[2], b[3]);
-      }
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
-        Sf[nt][0] *= l.x; Sf[nt][1] *= l.y; Sf[nt][2] *= l.x; Sf[nt][3] *= l.y;
-      }
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) acc_to_a(sHi[kk], Sf[2 * kk], Sf[2 * kk + 1]);
-    }
-
-    for (int64_t c = hi; c >= lo; --c, ++done) {
-      const bool is_lo = c == lo;
-      const int s = is_lo ? s_lo : s_hi;
-      const int xb = static_cast<int>(done & 1);
-      const Slot& sl = sm.slot[s];
-      const rec::KeyRec& kr = sl.k;
-      uint32_t sA[4][4];
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) sA[kk][r] = is_lo ? sLo[kk][r] : sHi[kk][r];
-
-      // G'' = G diag(lam)
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
-        G[nt][0] *= l.x; G[nt][1] *= l.y; G[nt][2] *= l.x; G[nt][3] *= l.y;
-      }
-      uint32_t gA[4][4], dyA[4];
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) acc_to_a(gA[kk], G[2 * kk], G[2 * kk + 1]);
-      lda_cm(vA, sl.v, Swz64{}, i0, 0, lane);
-      lda_cm(dyA, sl.dy, Swz64{}, i0, 0, lane);
-
-      float sat[2][4], dsat[2][4];
-      if (is_lo) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sat[nt][e] = satLo[nt][e];
-      } else {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sat[nt][e] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
-          mma16816(sat[0], sA[kk], b[0], b[1]);
-          mma16816(sat[1], sA[kk], b[2], b[3]);
-        }
-        ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
-        mma16816(sat[0], vA, b[0], b[1]);
-        mma16816(sat[1], vA, b[2], b[3]);
-      }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          dsat[nt][e] = has_dsa ? sl.dsa[8 * nt + 2 * q + (e & 1)][i0 + g + (e >= 2 ? 8 : 0)] : 0.f;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        ldb_nk(b, kr.Bb, Swz64{}, 0, 16 * kk, lane);
-        mma16816(dsat[0], gA[kk], b[0], b[1]);
-        mma16816(dsat[1], gA[kk], b[2], b[3]);
-      }
-      uint32_t dsaA[4];
-      acc_to_a(dsaA, dsat[0], dsat[1]);
-
-      // dV^T = G'' Kb^T + dY^T P + dSA^T Q
-      {
-        float dvt[2][4] = {};
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          ldb_nk(b, kr.Kb, Swz64{}, 0, 16 * kk, lane);
-          mma16816(dvt[0], gA[kk], b[0], b[1]);
-          mma16816(dvt[1], gA[kk], b[2], b[3]);
-        }
-        ldb_kn(b, kr.P, Swz16{}, 0, 0, lane);
-        mma16816(dvt[0], dyA, b[0], b[1]);
-        mma16816(dvt[1], dyA, b[2], b[3]);
-        ldb_kn(b, kr.Q, Swz16{}, 0, 0, lane);
-        mma16816(dvt[0], dsaA, b[0], b[1]);
-        mma16816(dvt[1], dsaA, b[2], b[3]);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int64_t t = c * L + 8 * nt + 2 * q + (e & 1);
-            if (t < T) dvp[cbase + t * ts + i0 + g + (e >= 2 ? 8 : 0)] = __float2bfloat16_rn(dvt[nt][e]);
+          for (int m = 0; m < 4; ++m) {
+            ldb_kn(b, kr.Bb, Swz64{}, 16 * m, 0, lane);
+            mma16816(Sf[2 * m], saA, b[0], b[1]);
+            mma16816(Sf[2 * m + 1], saA, b[2], b[3]);
+            ldb_kn(b, kr.Kb, Swz64{}, 16 * m, 0, lane);
+            mma16816(Sf[2 * m], vA, b[0], b[1]);
+            mma16816(Sf[2 * m + 1], vA, b[2], b[3]);
           }
-      }
-
-      // hand S, G'', SA, dSA (bf16) and dll of this chunk to the cross warps
-      if (done >= 2 && !mbar_wait(&sm.xempty[xb], static_cast<uint32_t>(((done >> 1) - 1) & 1))) return;
-      XBuf& X = sm.xb[xb];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
+          for (int nt = 0; nt < 8; ++nt) {
+            const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
+            Sf[nt][0] *= l.x; Sf[nt][1] *= l.y; Sf[nt][2] *= l.x; Sf[nt][3] *= l.y;
+          }
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {  // A fragment regs -> rows g / g+8, cols 16kk + 2q (+8)
-          const int col = 16 * kk + 2 * q + 8 * h;
-          *reinterpret_cast<uint32_t*>(&X.S[i0 + g][col]) = sA[kk][2 * h];
-          *reinterpret_cast<uint32_t*>(&X.S[i0 + g + 8][col]) = sA[kk][2 * h + 1];
-          *reinterpret_cast<uint32_t*>(&X.G[i0 + g][col]) = gA[kk][2 * h];
-          *reinterpret_cast<uint32_t*>(&X.G[i0 + g + 8][col]) = gA[kk][2 * h + 1];
+          for (int kk = 0; kk < 4; ++kk) acc_to_a(sHi[kk], Sf[2 * kk], Sf[2 * kk + 1]);
         }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        store_acc_bf16(&X.SAT[0][0], LDS, i0, 8 * nt, sat[nt], lane);
-        store_acc_bf16(&X.dSAT[0][0], LDS, i0, 8 * nt, dsat[nt], lane);
+        if (!value_chunk(sm, p, hi, s_hi, done, nchunk, sHi, satLo, false, G, wq, lane, cbase,
+                         ts, T, has_dsa))
+          return;
+        ++done;
       }
-      if (g == 0) {
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-          *reinterpret_cast<float2*>(&X.dll[wq][8 * nt + 2 * q]) = make_float2(dll[nt][0], dll[nt][1]);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.xfull[xb]);
-
-      // dS = G'' + dY^T Qy + dSA^T W  -> G of the previous chunk
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        ldb_kn(b, kr.Qy, Swz64{}, 16 * m, 0, lane);
-        mma16816(G[2 * m], dyA, b[0], b[1]);
-        mma16816(G[2 * m + 1], dyA, b[2], b[3]);
-        ldb_kn(b, kr.W, Swz64{}, 16 * m, 0, lane);
-        mma16816(G[2 * m], dsaA, b[0], b[1]);
-        mma16816(G[2 * m + 1], dsaA, b[2], b[3]);
-      }
-      // dll of the previous chunk: colsum over rows of G o S, S = this chunk's start state
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const uint32_t lo2 = sA[nt >> 1][2 * (nt & 1)], hi2 = sA[nt >> 1][2 * (nt & 1) + 1];
-        const float2 s0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo2));
-        const float2 s1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi2));
-        float p0 = G[nt][0] * s0.x + G[nt][2] * s1.x;
-        float p1 = G[nt][1] * s0.y + G[nt][3] * s1.y;
-#pragma unroll
-        for (int m = 4; m < 32; m <<= 1) {
-          p0 += __shfl_xor_sync(0xffffffffu, p0, m);
-          p1 += __shfl_xor_sync(0xffffffffu, p1, m);
-        }
-        dll[nt][0] = p0;
-        dll[nt][1] = p1;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.empty[s]);
     }
+    if (!value_chunk(sm, p, lo, s_lo, done, nchunk, sLo, satLo, true, G, wq, lane, cbase, ts, T,
+                     has_dsa))
+      return;
+    ++done;
   }
 }
 
@@ -576,25 +590,17 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
     float dAt[2][4] = {};  // Ti^T dW (own columns)
     mm16<true, true, 1>(dAt, &G.Ti[0][0], Padded{LDS}, &G.dW2b[0][0], Padded{LD}, j0, lane);
     __syncthreads();
-    if (gw == 0) {  // dA = strict(Ti^T dTi Ti^T), fp32
+    // dA = strict(Ti^T dTi Ti^T) in fp32, 2 entries per thread and product;
+    // dBm = strict(Ti^T dQ) on warp 1 in between
 #pragma unroll
-      for (int e8 = 0; e8 < 8; ++e8) {
-        const int e = lane + 32 * e8, t = e >> 4, u = e & 15;
-        float acc = 0.f;
+    for (int e2 = 0; e2 < 2; ++e2) {  // M1 = dTi Ti^T
+      const int e = tid + 128 * e2, t = e >> 4, u = e & 15;
+      float acc = 0.f;
 #pragma unroll
-        for (int m = 0; m < L; ++m) acc += G.dTf[t][m] * G.Tf[u][m];
-        G.dM1[t][u] = acc;
-      }
-      __syncwarp();
-#pragma unroll
-      for (int e8 = 0; e8 < 8; ++e8) {
-        const int e = lane + 32 * e8, t = e >> 4, u = e & 15;
-        float acc = 0.f;
-#pragma unroll
-        for (int m = 0; m < L; ++m) acc += G.Tf[m][t] * G.dM1[m][u];
-        G.dAb[t][u] = __float2bfloat16_rn(u < t ? acc : 0.f);
-      }
-    } else if (gw == 1) {  // dBm = strict(Ti^T dQ)
+      for (int m = 0; m < L; ++m) acc += G.dTf[t][m] * G.Tf[u][m];
+      G.dM1[t][u] = acc;
+    }
+    if (gw == 1) {
       float dbm[2][4] = {};
       mm16<true, true, 1>(dbm, &G.Ti[0][0], Padded{LDS}, &G.dQ2b[0][0], Padded{LDS}, 0, lane);
 #pragma unroll
@@ -606,6 +612,15 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
         }
       store_acc_bf16(&G.dBmb[0][0], LDS, 0, 0, dbm[0], lane);
       store_acc_bf16(&G.dBmb[0][0], LDS, 0, 8, dbm[1], lane);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int e2 = 0; e2 < 2; ++e2) {  // dA = Ti^T M1, strictly lower part
+      const int e = tid + 128 * e2, t = e >> 4, u = e & 15;
+      float acc = 0.f;
+#pragma unroll
+      for (int m = 0; m < L; ++m) acc += G.Tf[m][t] * G.dM1[m][u];
+      G.dAb[t][u] = __float2bfloat16_rn(u < t ? acc : 0.f);
     }
     __syncthreads();
 

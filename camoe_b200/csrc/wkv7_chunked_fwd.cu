@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
 
 namespace vf {
 
-constexpr int NS = 6;
+constexpr int NS = 12;
 constexpr int kThreads = 160;  // 4 value warps + 1 producer warp
 
 struct alignas(1024) Slot {

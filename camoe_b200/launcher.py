@@ -1,0 +1,150 @@
+"""One-process-per-GPU sharding of the WKV-7 op.
+
+The op is independent per (batch, head) chain, so a multi-GPU job is a
+partition of the B x H chains with no exchange on the data path:
+
+* batch shards when B is a multiple of the world size (contiguous batch
+  slices, every head): e.g. B=32 over 8 GPUs -> 4 sequences per GPU;
+* (batch, head-group) shards when the world size is a multiple of B and H
+  divides evenly: e.g. B=2, H=32 over 8 GPUs -> 1 sequence x 8 heads per GPU,
+  processed in place through the C ABI's head range (no copy).
+
+``run`` spawns one process per rank (torch.multiprocessing, ``spawn``), sets
+up a process group (NCCL on GPUs, gloo on CPU) with a short timeout, runs the
+per-shard function and gathers every shard's outputs back to the caller on
+the host (outside any timed region).  A rank that raises or does not finish
+within ``timeout`` makes ``run`` raise instead of hanging.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import queue
+import socket
+import traceback
+from dataclasses import dataclass
+
+import torch
+
+NAMES = ("r", "w", "k", "v", "a", "b")
+OUT_NAMES = ("y", "sa", "dr", "dw", "dk", "dv", "da", "db")
+
+
+@dataclass(frozen=True)
+class Shard:
+    b0: int
+    b1: int  # batch range [b0, b1)
+    h0: int
+    h1: int  # head range [h0, h1)
+
+    @property
+    def chains(self) -> int:
+        return (self.b1 - self.b0) * (self.h1 - self.h0)
+
+
+def plan_shards(B: int, H: int, world: int) -> list[Shard]:
+    """Partition B x H chains over `world` ranks (equal sizes, no collective)."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    if B % world == 0:
+        per = B // world
+        return [Shard(r * per, (r + 1) * per, 0, H) for r in range(world)]
+    if world % B == 0 and H % (world // B) == 0:
+        groups = world // B
+        hp = H // groups
+        return [Shard(r // groups, r // groups + 1, (r % groups) * hp, (r % groups + 1) * hp)
+                for r in range(world)]
+    raise ValueError(f"cannot split B={B} x H={H} chains evenly over {world} ranks")
+
+
+def cuda_shard_fn(inputs: dict, shard: Shard, device: torch.device) -> dict:
+    """Forward + backward of one shard on `device` through the C ABI (head range in place)."""
+    from . import ops
+
+    sl = slice(shard.b0, shard.b1)
+    xs = [inputs[n][sl].to(device) for n in NAMES]
+    dy = inputs["dy"][sl].to(device)
+    dsa = inputs["dsa"][sl].to(device) if inputs.get("dsa") is not None else None
+    hc = shard.h1 - shard.h0
+    y, sa, ck = ops.wkv7_forward(*xs, h0=shard.h0, h_count=hc, zero_rest=True)
+    grads = ops.wkv7_backward(*xs, dy, dsa, ck, h0=shard.h0, h_count=hc, zero_rest=True)
+    torch.cuda.synchronize(device)
+    hs = slice(shard.h0, shard.h1)
+    out = {"y": y, "sa": sa}
+    out.update(dict(zip(OUT_NAMES[2:], grads)))
+    return {n: t[:, :, hs].cpu() for n, t in out.items()}
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, backend, inputs, shards, shard_fn, results, timeout_s):
+    import torch.distributed as dist
+    try:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        if backend == "nccl":
+            torch.cuda.set_device(rank)
+            device = torch.device("cuda", rank)
+        else:
+            device = torch.device("cpu")
+        dist.init_process_group(backend, init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+        out = shard_fn(inputs, shards[rank], device)
+        dist.barrier()  # every rank finished its shard
+        results.put((rank, "ok", out))
+        dist.destroy_process_group()
+    except Exception:  # reported to the parent, which raises
+        results.put((rank, "error", traceback.format_exc()))
+
+
+def run(inputs: dict, world: int, backend: str = "nccl", shard_fn=None,
+        timeout: float = 120.0) -> dict:
+    """Run `shard_fn` (default: the CUDA op) on `world` ranks and gather the outputs.
+
+    `inputs` holds CPU tensors r, w, k, v, a, b, dy [, dsa] of shape [B, T, H, 64].
+    Returns dict of full [B, T, H, 64] CPU tensors y, sa, dr, dw, dk, dv, da, db.
+    """
+    import torch.multiprocessing as mp
+
+    B, T, H, N = inputs["r"].shape
+    shards = plan_shards(B, H, world)
+    fn = shard_fn or cuda_shard_fn
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, backend, inputs, shards, fn,
+                                                 results, timeout), daemon=True)
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got, errors = {}, []
+    deadline = timeout + 10.0
+    try:
+        while len(got) + len(errors) < world:
+            try:
+                rank, status, payload = results.get(timeout=deadline)
+            except queue.Empty:
+                raise TimeoutError(f"ranks {sorted(set(range(world)) - set(got))} did not finish "
+                                   f"within {deadline:.0f} s")
+            if status == "ok":
+                got[rank] = payload
+            else:
+                errors.append((rank, payload))
+                break
+    finally:
+        for p in procs:
+            p.join(timeout=5.0)
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=5.0)
+    if errors:
+        rank, tb = errors[0]
+        raise RuntimeError(f"rank {rank} failed:\n{tb}")
+    full = {n: torch.zeros(B, T, H, N, dtype=got[0][n].dtype) for n in OUT_NAMES}
+    for rank, sh in enumerate(shards):
+        for n in OUT_NAMES:
+            full[n][sh.b0:sh.b1, :, sh.h0:sh.h1] = got[rank][n]
+    return full
