@@ -222,20 +222,36 @@ __device__ __forceinline__ bool value_chunk(Smem& sm, const BwdArgs& p, int64_t 
     if (done + 1 >= 2 &&
         !mbar_wait(&sm.xempty[nx], static_cast<uint32_t>((((done + 1) >> 1) - 1) & 1)))
       return false;
+    // per-thread partial sums over rows g, g+8 of columns 8nt + 2q + x, as v[2nt + x]
+    float v[16];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       const uint32_t lo2 = sA[nt >> 1][2 * (nt & 1)], hi2 = sA[nt >> 1][2 * (nt & 1) + 1];
       const float2 s0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo2));
       const float2 s1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi2));
-      float p0 = G[nt][0] * s0.x + G[nt][2] * s1.x;
-      float p1 = G[nt][1] * s0.y + G[nt][3] * s1.y;
-#pragma unroll
-      for (int m = 4; m < 32; m <<= 1) {
-        p0 += __shfl_xor_sync(0xffffffffu, p0, m);
-        p1 += __shfl_xor_sync(0xffffffffu, p1, m);
-      }
-      if (g == 0) *reinterpret_cast<float2*>(&sm.xb[nx].dll[wq][8 * nt + 2 * q]) = make_float2(p0, p1);
+      v[2 * nt] = G[nt][0] * s0.x + G[nt][2] * s1.x;
+      v[2 * nt + 1] = G[nt][1] * s0.y + G[nt][3] * s1.y;
     }
+    // reduce-scatter over the 8 row lanes (lane bits 4, 3, 2): lane g keeps v[2g], v[2g+1]
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const bool up = lane & 16;
+      const float send = up ? v[m] : v[m + 8], keep = up ? v[m + 8] : v[m];
+      v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const bool up = lane & 8;
+      const float send = up ? v[m] : v[m + 4], keep = up ? v[m + 4] : v[m];
+      v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const bool up = lane & 4;
+      const float send = up ? v[m] : v[m + 2], keep = up ? v[m + 2] : v[m];
+      v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    *reinterpret_cast<float2*>(&sm.xb[nx].dll[wq][8 * g + 2 * q]) = make_float2(v[0], v[1]);
   }
   return true;
 }
@@ -456,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_con
 
 namespace kb {
 
-constexpr int NR = 2;
+constexpr int NR = 1;           // inputs single-buffered: 3 CTAs per SM overlap the loads
 constexpr int kThreads = 128;  // one group of 4 warps per CTA
 
 struct alignas(1024) KGroup {
@@ -468,8 +484,7 @@ struct alignas(1024) KGroup {
   float lam[kN], cum[L][kN], sig[L][kN];
   bf16 dQyb[L][LD], dW2b[L][LD];
   bf16 dPb[L][LDS], dQ2b[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
-  float dTf[L][L + 1], dM1[L][L + 1];
-  float dcum[L][kN], dcumx[L][kN];
+  float dTf[L][L + 1];
   bf16 dwt[L][LD];
   uint64_t bar[NR];
 };
@@ -479,6 +494,36 @@ struct Params {
   BwdArgs a;
   void* work;
 };
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// acc (16 x 16) = A (16 x 16) B (16 x 16) with tf32 operands, one warp;
+// A(m, k) and B(k, n) are element accessors.
+template <typename FA, typename FB>
+__device__ __forceinline__ void mm16_tf32(float (&acc)[2][4], FA A, FB B, int lane) {
+  const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int k0 = 0; k0 < 16; k0 += 8) {
+    const uint32_t a[4] = {to_tf32(A(g, k0 + q)), to_tf32(A(g + 8, k0 + q)),
+                           to_tf32(A(g, k0 + q + 4)), to_tf32(A(g + 8, k0 + q + 4))};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+      mma_tf32(acc[nt], a, to_tf32(B(k0 + q, 8 * nt + g)), to_tf32(B(k0 + q + 4, 8 * nt + g)));
+  }
+}
 
 __device__ __forceinline__ void issue(KGroup& G, int rb, const Params& P, int64_t item) {
   const Geom& g = P.a.g;
@@ -520,7 +565,11 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
     const bf16* raw_k = G.raw[rb][2];
     const bf16* raw_a = G.raw[rb][3];
     const bf16* raw_b = G.raw[rb][4];
-    const rec::ProdRec& pr = G.prod[rb];
+    rec::ProdRec& pr = G.prod[rb];
+    // scan scratch aliases ProdRec fields: dW is consumed before the element
+    // phase, dQy is read at each position by the thread that then overwrites it
+    float(*dcum)[kN] = reinterpret_cast<float(*)[kN]>(pr.dW);
+    float(*dcumx)[kN] = reinterpret_cast<float(*)[kN]>(pr.dQy);
 
     // ---- key side of the chunk (forward recompute) ----
     ks::decays<true>(raw_r, G.raw[rb][1], raw_k, raw_a, raw_b, G.At, G.Rt, G.Kb, G.Bb, G.lam,
@@ -590,17 +639,27 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
     float dAt[2][4] = {};  // Ti^T dW (own columns)
     mm16<true, true, 1>(dAt, &G.Ti[0][0], Padded{LDS}, &G.dW2b[0][0], Padded{LD}, j0, lane);
     __syncthreads();
-    // dA = strict(Ti^T dTi Ti^T) in fp32, 2 entries per thread and product;
-    // dBm = strict(Ti^T dQ) on warp 1 in between
+    // dA = strict(Ti^T dTi Ti^T) with tf32 operands on warp 0; dBm = strict(Ti^T dQ) on warp 1
+    if (gw == 0) {
+      float m1[2][4] = {};  // M1 = dTi Ti^T
+      mm16_tf32(m1, [&](int m, int k) { return G.dTf[m][k]; },
+                [&](int k, int n) { return G.Tf[n][k]; }, lane);
+      store_acc_f32(&G.Ga[0][0], L + 1, 0, 0, m1[0], lane);  // Ga is free after the inverse
+      store_acc_f32(&G.Ga[0][0], L + 1, 0, 8, m1[1], lane);
+      __syncwarp();
+      float da[2][4] = {};  // dA = Ti^T M1
+      mm16_tf32(da, [&](int m, int k) { return G.Tf[k][m]; },
+                [&](int k, int n) { return G.Ga[k][n]; }, lane);
 #pragma unroll
-    for (int e2 = 0; e2 < 2; ++e2) {  // M1 = dTi Ti^T
-      const int e = tid + 128 * e2, t = e >> 4, u = e & 15;
-      float acc = 0.f;
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int m = 0; m < L; ++m) acc += G.dTf[t][m] * G.Tf[u][m];
-      G.dM1[t][u] = acc;
-    }
-    if (gw == 1) {
+        for (int e = 0; e < 4; ++e) {
+          const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
+          if (u >= t) da[nt][e] = 0.f;
+        }
+      store_acc_bf16(&G.dAb[0][0], LDS, 0, 0, da[0], lane);
+      store_acc_bf16(&G.dAb[0][0], LDS, 0, 8, da[1], lane);
+    } else if (gw == 1) {
       float dbm[2][4] = {};
       mm16<true, true, 1>(dbm, &G.Ti[0][0], Padded{LDS}, &G.dQ2b[0][0], Padded{LDS}, 0, lane);
 #pragma unroll
@@ -612,15 +671,6 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
         }
       store_acc_bf16(&G.dBmb[0][0], LDS, 0, 0, dbm[0], lane);
       store_acc_bf16(&G.dBmb[0][0], LDS, 0, 8, dbm[1], lane);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int e2 = 0; e2 < 2; ++e2) {  // dA = Ti^T M1, strictly lower part
-      const int e = tid + 128 * e2, t = e >> 4, u = e & 15;
-      float acc = 0.f;
-#pragma unroll
-      for (int m = 0; m < L; ++m) acc += G.Tf[m][t] * G.dM1[m][u];
-      G.dAb[t][u] = __float2bfloat16_rn(u < t ? acc : 0.f);
     }
     __syncthreads();
 
@@ -666,8 +716,8 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
           odr[x] = drt * Lam;
           odk[x] = dkb * iLam;
           odb[x] = dbb * iLam;
-          G.dcum[t][jj + x] = drt * rv[x] * Lam - dkb * kv[x] * iLam - dbb * bv[x] * iLam;
-          G.dcumx[t][jj + x] = dat * av[x] * Lamx;
+          dcum[t][jj + x] = drt * rv[x] * Lam - dkb * kv[x] * iLam - dbb * bv[x] * iLam;
+          dcumx[t][jj + x] = dat * av[x] * Lamx;
         }
         const int64_t tg = c * L + t;
         if (tg < T) {
@@ -684,11 +734,11 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
       float s1 = 0.f, s2 = 0.f;
 #pragma unroll
       for (int t = L - 1; t >= 0; --t) {
-        float dc = G.dcum[t][jj];
+        float dc = dcum[t][jj];
         if (t == L - 1) dc += pr.dll[jj];
         s1 += dc;
         const float dlw = s1 + s2;
-        s2 += G.dcumx[t][jj];
+        s2 += dcumx[t][jj];
         const float sg = G.sig[t][jj];
         G.dwt[t][jj] = __float2bfloat16_rn(dlw * kWScale * sg * (1.0f - sg));
       }
@@ -756,7 +806,7 @@ cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
                            (int)ksmem);
   if (e != cudaSuccess) return e;
   const int64_t items = p.g.chains() * p.g.nchunk;
-  const int64_t kgrid = items < 2LL * sms ? items : 2LL * sms;
+  const int64_t kgrid = items < 3LL * sms ? items : 3LL * sms;  // 3 CTAs per SM
   kb::keyside_bwd_kernel<<<(unsigned)kgrid, kb::kThreads, ksmem, stream>>>(K);
   return cudaGetLastError();
 }
