@@ -12,15 +12,15 @@
 // (dll is d(lam) * lam: lam scales the chunk's end state S').
 //
 // value_bwd_kernel (one CTA per chain, chunks in reverse): 4 value warps carry
-// G and run the recurrence; 4 cross warps form the row sums above from the
-// value warps' bf16 copies of S, G'', SA and dSA and write them as a
-// rec::ProdRec to the workspace; a producer warp streams each chunk's KeyRec,
-// v, dy, dSA_ext tiles and (even chunks) the checkpointed state.  Chunks are
-// taken in (even, odd) pairs: the state at the start of the odd chunk is
-// recomputed from the even chunk's checkpoint.
+// G and run the recurrence, writing dv and, per chunk, a rec::XRec (bf16 S,
+// G'', SA^T, dSA^T and the column sums for dll) to the workspace; a producer
+// warp streams each chunk's KeyRec, v, dy, dSA_ext tiles and (even chunks) the
+// checkpointed state.  Chunks are taken in (even, odd) pairs: the state at the
+// start of the odd chunk is recomputed from the even chunk's checkpoint.
 //
-// keyside_bwd_kernel (chunk-parallel, every SM): recomputes a chunk's key side
-// from r, w, k, a, b and turns its ProdRec into dr, dw, dk, da, db:
+// keyside_bwd_kernel (chunk-parallel, every SM): forms the row sums above from
+// the chunk's XRec and its v, dy tiles, recomputes the chunk's key side from
+// r, w, k, a, b and turns both into dr, dw, dk, da, db:
 //     dW += Cm^T dQy,  dQ += Cm^T dP,  dCm = lower(dQy W^T + dP Q^T)
 //     dTi = dW At^T + dQ Bm^T,  dA = strict(Ti^T dTi Ti^T),  dBm = strict(Ti^T dQ)
 //     dAt = Ti^T dW + dA Bb + dBm Kb,   dRt = dQy + dCm Bb + dP Kb
@@ -49,8 +49,8 @@ using ks::Tile16;
 
 namespace vb {
 
-constexpr int NS = 6;
-constexpr int kThreads = 288;  // value warps 0-3, cross warps 4-7, producer warp 8
+constexpr int NS = 8;
+constexpr int kThreads = 160;  // value warps 0-3, producer warp 4
 
 struct alignas(1024) Slot {
   bf16 v[L * kN];   // TMA 128-byte swizzled
@@ -60,16 +60,9 @@ struct alignas(1024) Slot {
   uint4 S[512];  // state at the chunk start (even chunks >= 2), A-fragment order
 };
 
-struct XBuf {  // value warps -> cross warps, one chunk
-  bf16 S[kN][LD], G[kN][LD];      // rows i
-  bf16 SAT[kN][LDS], dSAT[kN][LDS];
-  float dll[4][kN];               // per value warp column sums
-};
-
 struct Smem {
   Slot slot[NS];
-  XBuf xb[2];
-  uint64_t full[NS], empty[NS], xfull[2], xempty[2];
+  uint64_t full[NS], empty[NS];
 };
 
 struct Params {
@@ -96,18 +89,16 @@ __device__ __forceinline__ void group_of(int64_t nchunk, int64_t gi, int64_t& lo
 
 __device__ __forceinline__ int64_t num_groups(int64_t nchunk) { return (nchunk + 1) / 2; }
 
-// One chunk of the value-warp backward (warp wq owns state rows 16wq..16wq+15):
+// One chunk c of the value-warp backward (warp wq owns state rows 16wq..16wq+15):
 // G'' = G diag(lam); SA (or the precomputed satPre); dSA; dV -> global; the bf16
-// copies of S, G'', SA, dSA -> cross buffer (done & 1); G <- dS; the column sums
-// of G o S for the next chunk -> next cross buffer.  False on a timeout.
-__device__ __forceinline__ bool value_chunk(Smem& sm, const BwdArgs& p, int64_t c, int s,
-                                            int64_t done, int64_t nchunk,
-                                            const uint32_t (&sA)[4][4], const float (&satPre)[2][4],
-                                            bool have_sat, float (&G)[8][4], int wq, int lane,
-                                            int64_t cbase, int64_t ts, int64_t T, bool has_dsa) {
+// S, G'', SA^T, dSA^T rows of this warp -> the chunk's XRec; G <- dS; the column
+// sums of G o S over this warp's rows -> dll of chunk c - 1.
+__device__ __forceinline__ void value_chunk(const Slot& sl, const BwdArgs& p, rec::XRec* xr,
+                                            int64_t c, const uint32_t (&sA)[4][4],
+                                            const float (&satPre)[2][4], bool have_sat,
+                                            float (&G)[8][4], int wq, int lane, int64_t cbase,
+                                            int64_t ts, int64_t T, bool has_dsa) {
   const int g = lane >> 2, q = lane & 3, i0 = 16 * wq;
-  const int xb = static_cast<int>(done & 1);
-  const Slot& sl = sm.slot[s];
   const rec::KeyRec& kr = sl.k;
   uint32_t b[4], vA[4], dyA[4];
 
@@ -158,25 +149,17 @@ __device__ __forceinline__ bool value_chunk(Smem& sm, const BwdArgs& p, int64_t 
   uint32_t dsaA[4];
   acc_to_a(dsaA, dsat[0], dsat[1]);
 
-  // bf16 copies of S, G'', SA, dSA for the cross warps (buffer freed at the previous chunk)
-  XBuf& X = sm.xb[xb];
+  // this warp's rows of S, G'', SA^T, dSA^T for the key-side backward
 #pragma unroll
-  for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {  // A fragment regs -> rows g / g+8, cols 16kk + 2q (+8)
-      const int col = 16 * kk + 2 * q + 8 * h;
-      *reinterpret_cast<uint32_t*>(&X.S[i0 + g][col]) = sA[kk][2 * h];
-      *reinterpret_cast<uint32_t*>(&X.S[i0 + g + 8][col]) = sA[kk][2 * h + 1];
-      *reinterpret_cast<uint32_t*>(&X.G[i0 + g][col]) = gA[kk][2 * h];
-      *reinterpret_cast<uint32_t*>(&X.G[i0 + g + 8][col]) = gA[kk][2 * h + 1];
-    }
+  for (int kk = 0; kk < 4; ++kk) {
+    store_a_lay(xr->S, Swz64{}, i0, 16 * kk, sA[kk], lane);
+    store_a_lay(xr->G, Swz64{}, i0, 16 * kk, gA[kk], lane);
+  }
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
-    store_acc_bf16(&X.SAT[0][0], LDS, i0, 8 * nt, sat[nt], lane);
-    store_acc_bf16(&X.dSAT[0][0], LDS, i0, 8 * nt, dsat[nt], lane);
+    store_acc_lay(xr->SAT, Swz16{}, i0, 8 * nt, sat[nt], lane);
+    store_acc_lay(xr->dSAT, Swz16{}, i0, 8 * nt, dsat[nt], lane);
   }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(&sm.xfull[xb]);
 
   // dV^T = G'' Kb^T + dY^T P + dSA^T Q
   {
@@ -213,15 +196,9 @@ __device__ __forceinline__ bool value_chunk(Smem& sm, const BwdArgs& p, int64_t 
     mma16816(G[2 * m], dsaA, b[0], b[1]);
     mma16816(G[2 * m + 1], dsaA, b[2], b[3]);
   }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(&sm.empty[s]);
 
-  // dll of the next chunk to process: colsum over rows of G o S (S = this chunk's start state)
-  if (done + 1 < nchunk) {
-    const int nx = static_cast<int>((done + 1) & 1);
-    if (done + 1 >= 2 &&
-        !mbar_wait(&sm.xempty[nx], static_cast<uint32_t>((((done + 1) >> 1) - 1) & 1)))
-      return false;
+  // dll of chunk c - 1: column sums over this warp's rows of G o S (S = its end state)
+  if (c >= 1) {
     // per-thread partial sums over rows g, g+8 of columns 8nt + 2q + x, as v[2nt + x]
     float v[16];
 #pragma unroll
@@ -251,9 +228,8 @@ __device__ __forceinline__ bool value_chunk(Smem& sm, const BwdArgs& p, int64_t 
       const float send = up ? v[m] : v[m + 2], keep = up ? v[m + 2] : v[m];
       v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
     }
-    *reinterpret_cast<float2*>(&sm.xb[nx].dll[wq][8 * g + 2 * q]) = make_float2(v[0], v[1]);
+    *reinterpret_cast<float2*>(&(xr - 1)->dll[wq][8 * g + 2 * q]) = make_float2(v[0], v[1]);
   }
-  return true;
 }
 
 __global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_constant__ Params P) {
@@ -270,17 +246,13 @@ __global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_con
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 8);
-    }
-    for (int x = 0; x < 2; ++x) {
-      mbar_init(&sm.xfull[x], 4);
-      mbar_init(&sm.xempty[x], 4);
+      mbar_init(&sm.empty[s], 4);
     }
     mbar_fence_init();
   }
   __syncthreads();
 
-  if (warp == 8) {
+  if (warp == 4) {
     // ------------------------------ producer ------------------------------
     if (lane != 0) return;
     const int hh = static_cast<int>(p.g.h0 + ch % p.g.hc), bb = static_cast<int>(ch / p.g.hc);
@@ -313,66 +285,6 @@ __global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_con
     return;
   }
 
-  if (warp >= 4) {
-    // ------------------------------ cross warps ------------------------------
-    const int cw = warp - 4, j0 = 16 * cw, g = lane >> 2, q = lane & 3;
-    int64_t done = 0;  // chunks processed (cross-buffer index = done & 1)
-    for (int64_t gi = 0; gi < ngroups; ++gi) {
-      int64_t lo, hi, idx_lo;
-      group_of(nchunk, gi, lo, hi, idx_lo);
-      for (int64_t c = hi; c >= lo; --c, ++done) {
-        const int xb = static_cast<int>(done & 1);
-        const int64_t idx = idx_lo + (c - lo);
-        const int s = static_cast<int>(idx % NS);
-        if (!mbar_wait(&sm.xfull[xb], static_cast<uint32_t>((done >> 1) & 1))) return;
-        const XBuf& X = sm.xb[xb];
-        const Slot& sl = sm.slot[s];
-        float dW[2][4] = {}, dQy[2][4] = {}, dBb[2][4] = {}, dKb[2][4] = {};
-        mm16<true, true, 4>(dW, &X.dSAT[0][0], Padded{LDS}, &X.S[0][0], Padded{LD}, j0, lane);
-        mm16<false, true, 4>(dQy, sl.dy, Swz64{}, &X.S[0][0], Padded{LD}, j0, lane);
-        mm16<true, true, 4>(dBb, &X.SAT[0][0], Padded{LDS}, &X.G[0][0], Padded{LD}, j0, lane);
-        mm16<false, true, 4>(dKb, sl.v, Swz64{}, &X.G[0][0], Padded{LD}, j0, lane);
-        rec::ProdRec* pr = rec::prodrec(P.work, ch, nchunk, c);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            const int t = g + 8 * hf, j = j0 + 8 * nt + 2 * q;
-            *reinterpret_cast<float2*>(&pr->dW[t * kN + j]) = make_float2(dW[nt][2 * hf], dW[nt][2 * hf + 1]);
-            *reinterpret_cast<float2*>(&pr->dQy[t * kN + j]) = make_float2(dQy[nt][2 * hf], dQy[nt][2 * hf + 1]);
-            *reinterpret_cast<float2*>(&pr->dBb[t * kN + j]) = make_float2(dBb[nt][2 * hf], dBb[nt][2 * hf + 1]);
-            *reinterpret_cast<float2*>(&pr->dKb[t * kN + j]) = make_float2(dKb[nt][2 * hf], dKb[nt][2 * hf + 1]);
-          }
-        if (cw < 2) {  // cw 0: dQ = strict(dSA V^T), cw 1: dP = lower(dY V^T)
-          float acc[2][4] = {};
-          if (cw == 0) mm16<true, false, 4>(acc, &X.dSAT[0][0], Padded{LDS}, sl.v, Swz64{}, 0, lane);
-          else mm16<false, false, 4>(acc, sl.dy, Swz64{}, sl.v, Swz64{}, 0, lane);
-          float* dst = cw == 0 ? pr->dQ : pr->dP;
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int t = g + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
-              const bool keep = cw == 0 ? (u < t) : (u <= t);
-              dst[t * L + u] = keep ? acc[nt][e] : 0.f;
-            }
-        } else if (cw == 2) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int j = lane + 32 * e;
-            pr->dll[j] = X.dll[0][j] + X.dll[1][j] + X.dll[2][j] + X.dll[3][j];
-          }
-        }
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sm.xempty[xb]);
-          mbar_arrive(&sm.empty[s]);
-        }
-      }
-    }
-    return;
-  }
-
   // ------------------------------ value warps ------------------------------
   const int wq = warp, i0 = 16 * wq, q = lane & 3;
   float G[8][4];  // dL/dS' of the chunk being processed
@@ -380,11 +292,9 @@ __global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_con
   for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) G[nt][e] = 0.f;
-  if ((lane >> 2) == 0)  // the first chunk processed has no following chunk: dll = 0
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-      *reinterpret_cast<float2*>(&sm.xb[0].dll[wq][8 * nt + 2 * q]) = make_float2(0.f, 0.f);
-  int64_t done = 0;
+  if (nchunk > 0)  // the last chunk has no following chunk: dll = 0
+    *reinterpret_cast<float2*>(&rec::xrec(P.work, ch, nchunk, nchunk - 1)->dll[wq][2 * lane]) =
+        make_float2(0.f, 0.f);
   for (int64_t gi = 0; gi < ngroups; ++gi) {
     int64_t lo, hi, idx_lo;
     group_of(nchunk, gi, lo, hi, idx_lo);
@@ -455,16 +365,16 @@ __global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_con
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) acc_to_a(sHi[kk], Sf[2 * kk], Sf[2 * kk + 1]);
         }
-        if (!value_chunk(sm, p, hi, s_hi, done, nchunk, sHi, satLo, false, G, wq, lane, cbase,
-                         ts, T, has_dsa))
-          return;
-        ++done;
+        value_chunk(sm.slot[s_hi], p, rec::xrec(P.work, ch, nchunk, hi), hi, sHi, satLo, false,
+                    G, wq, lane, cbase, ts, T, has_dsa);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[s_hi]);
       }
     }
-    if (!value_chunk(sm, p, lo, s_lo, done, nchunk, sLo, satLo, true, G, wq, lane, cbase, ts, T,
-                     has_dsa))
-      return;
-    ++done;
+    value_chunk(sm.slot[s_lo], p, rec::xrec(P.work, ch, nchunk, lo), lo, sLo, satLo, true, G,
+                wq, lane, cbase, ts, T, has_dsa);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[s_lo]);
   }
 }
 
@@ -476,21 +386,22 @@ constexpr int NR = 1;           // inputs single-buffered: 3 CTAs per SM overlap
 constexpr int kThreads = 128;  // one group of 4 warps per CTA
 
 struct alignas(1024) KGroup {
-  bf16 raw[NR][5][L * kN];  // r, w, k, a, b as landed by TMA (1 KiB aligned)
-  rec::ProdRec prod[NR];
+  bf16 raw[NR][7][L * kN];  // r, w, k, a, b, v, dy as landed by TMA (1 KiB aligned)
+  rec::XRec x[NR];          // S and G are reused as scratch once the row sums are formed
   Tile At, Rt, W, Bb, Kb;
   Tile16 Bm, Cm, Dm, Ti, Q, P;
   float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
-  float lam[kN], cum[L][kN], sig[L][kN];
-  bf16 dQyb[L][LD], dW2b[L][LD];
+  float lam[kN], cum[L][kN], sig[L][kN], dll[kN];
   bf16 dPb[L][LDS], dQ2b[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
   float dTf[L][L + 1];
-  bf16 dwt[L][LD];
   uint64_t bar[NR];
 };
+// scratch inside the XRec: dcum, dcumx (fp32 16 x 64) in S; dQyb, dW2b, dwt in G
+static_assert(2 * L * kN * sizeof(float) <= sizeof(rec::XRec::S), "dcum scratch");
+static_assert(3 * sizeof(Tile) <= sizeof(rec::XRec::G), "tile scratch");
 
 struct Params {
-  CUtensorMap maps[5];  // r, w, k, a, b
+  CUtensorMap maps[7];  // r, w, k, a, b, v, dy
   BwdArgs a;
   void* work;
 };
@@ -529,13 +440,13 @@ __device__ __forceinline__ void issue(KGroup& G, int rb, const Params& P, int64_
   const Geom& g = P.a.g;
   const int64_t ch = item / g.nchunk, c = item % g.nchunk;
   const int h = static_cast<int>(g.h0 + ch % g.hc), b = static_cast<int>(ch / g.hc);
-  mbar_arrive_expect_tx(&G.bar[rb], 5 * tma::kTileBytes + sizeof(rec::ProdRec));
+  mbar_arrive_expect_tx(&G.bar[rb], 7 * tma::kTileBytes + sizeof(rec::XRec));
 #pragma unroll
-  for (int t = 0; t < 5; ++t) tma::load_tile(G.raw[rb][t], &P.maps[t], h, static_cast<int>(c * L), b, &G.bar[rb]);
-  bulk_g2s(&G.prod[rb], rec::prodrec(P.work, ch, g.nchunk, c), sizeof(rec::ProdRec), &G.bar[rb]);
+  for (int t = 0; t < 7; ++t) tma::load_tile(G.raw[rb][t], &P.maps[t], h, static_cast<int>(c * L), b, &G.bar[rb]);
+  bulk_g2s(&G.x[rb], rec::xrec(P.work, ch, g.nchunk, c), sizeof(rec::XRec), &G.bar[rb]);
 }
 
-__global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   KGroup& G = *reinterpret_cast<KGroup*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
   const BwdArgs& p = P.a;
@@ -565,50 +476,73 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
     const bf16* raw_k = G.raw[rb][2];
     const bf16* raw_a = G.raw[rb][3];
     const bf16* raw_b = G.raw[rb][4];
-    rec::ProdRec& pr = G.prod[rb];
-    // scan scratch aliases ProdRec fields: dW is consumed before the element
-    // phase, dQy is read at each position by the thread that then overwrites it
-    float(*dcum)[kN] = reinterpret_cast<float(*)[kN]>(pr.dW);
-    float(*dcumx)[kN] = reinterpret_cast<float(*)[kN]>(pr.dQy);
+    const bf16* raw_v = G.raw[rb][5];
+    const bf16* raw_dy = G.raw[rb][6];
+    rec::XRec& xr = G.x[rb];
+    float(*dcum)[kN] = reinterpret_cast<float(*)[kN]>(&xr.S[0]);
+    float(*dcumx)[kN] = dcum + L;
+    Tile& dQyb = *reinterpret_cast<Tile*>(&xr.G[0]);
+    Tile& dW2b = *(&dQyb + 1);
+    Tile& dwt = *(&dQyb + 2);
 
-    // ---- key side of the chunk (forward recompute) ----
+    // ---- row sums over the 64 state rows (own columns), and the key side ----
+    //   dW = dSA S, dQy = dY S, dBb = SA G'', dKb = V G'';  dP = lower(dY V^T) (warp 2),
+    //   dQ = strict(dSA V^T) (warp 1, kept in registers), dll (warp 3)
+    float dW[2][4] = {}, dQy[2][4] = {}, dBp[2][4] = {}, dKp[2][4] = {}, dq[2][4] = {};
+    mm16<true, true, 4>(dW, xr.dSAT, Swz16{}, xr.S, Swz64{}, j0, lane);
+    mm16<false, true, 4>(dQy, raw_dy, Swz64{}, xr.S, Swz64{}, j0, lane);
+    mm16<true, true, 4>(dBp, xr.SAT, Swz16{}, xr.G, Swz64{}, j0, lane);
+    mm16<false, true, 4>(dKp, raw_v, Swz64{}, xr.G, Swz64{}, j0, lane);
+    if (gw == 1) {
+      mm16<true, false, 4>(dq, xr.dSAT, Swz16{}, raw_v, Swz64{}, 0, lane);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
+          if (u >= t) dq[nt][e] = 0.f;
+        }
+    } else if (gw == 2) {
+      float dp[2][4] = {};
+      mm16<false, false, 4>(dp, raw_dy, Swz64{}, raw_v, Swz64{}, 0, lane);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
+          if (u > t) dp[nt][e] = 0.f;
+        }
+      store_acc_bf16(&G.dPb[0][0], LDS, 0, 0, dp[0], lane);
+      store_acc_bf16(&G.dPb[0][0], LDS, 0, 8, dp[1], lane);
+    } else if (gw == 3) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int jj = lane + 32 * e;
+        G.dll[jj] = xr.dll[0][jj] + xr.dll[1][jj] + xr.dll[2][jj] + xr.dll[3][jj];
+      }
+    }
     ks::decays<true>(raw_r, G.raw[rb][1], raw_k, raw_a, raw_b, G.At, G.Rt, G.Kb, G.Bb, G.lam,
                      G.cum, G.sig, tid);
-    __syncthreads();
+    __syncthreads();  // XRec S and G free from here on
     ks::grams(G.At, G.Rt, G.Bb, G.Kb, G.Ga, G.Bm, G.Cm, G.Dm, gw, lane);
+    store_acc_bf16(&dQyb[0][0], LD, 0, j0, dQy[0], lane);
+    store_acc_bf16(&dQyb[0][0], LD, 0, j0 + 8, dQy[1], lane);
     __syncthreads();
     if (gw == 0) ks::inverse(G.Ga, G.Tf, G.Mf, G.Ti, lane);
     __syncthreads();
     ks::w_and_q(G.Ti, G.At, G.Bm, G.W, G.Q, gw, lane);
+    __syncthreads();  // W, Q ready
 
-    // ---- dW += Cm^T dQy (own columns), bf16 copies of dQy and dP ----
-    for (int e = lane; e < L * 8; e += 32) {  // 16 rows x 8 pairs of own columns
-      const int t = e >> 3, jj = j0 + 2 * (e & 7);
-      const float2 v = *reinterpret_cast<const float2*>(&pr.dQy[t * kN + jj]);
-      *reinterpret_cast<__nv_bfloat162*>(&G.dQyb[t][jj]) = __floats2bfloat162_rn(v.x, v.y);
-    }
-    if (gw == 1)
-      for (int e = lane; e < L * L; e += 32) G.dPb[e >> 4][e & 15] = __float2bfloat16_rn(pr.dP[e]);
-    __syncwarp();
-    float dW2[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const float2 v = *reinterpret_cast<const float2*>(&pr.dW[(gq + 8 * hf) * kN + j0 + 8 * nt + 2 * q]);
-        dW2[nt][2 * hf] = v.x;
-        dW2[nt][2 * hf + 1] = v.y;
-      }
-    __syncthreads();  // W, Q ready (w_and_q) and dPb visible
-    mm16<true, true, 1>(dW2, &G.Cm[0][0], Padded{LDS}, &G.dQyb[0][0], Padded{LD}, j0, lane);
-    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW2[0], lane);
-    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW2[1], lane);
+    // ---- dW += Cm^T dQy (own columns) ----
+    mm16<true, true, 1>(dW, &G.Cm[0][0], Padded{LDS}, &dQyb[0][0], Padded{LD}, j0, lane);
+    store_acc_bf16(&dW2b[0][0], LD, 0, j0, dW[0], lane);
+    store_acc_bf16(&dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
     __syncthreads();
 
     // ---- 16x16 pieces ----
     if (gw == 0) {  // dCm = lower(dQy W^T + dP Q^T)
       float dcm[2][4] = {};
-      mm16<false, false, 4>(dcm, &G.dQyb[0][0], Padded{LD}, &G.W[0][0], Padded{LD}, 0, lane);
+      mm16<false, false, 4>(dcm, &dQyb[0][0], Padded{LD}, &G.W[0][0], Padded{LD}, 0, lane);
       mm16<false, false, 1>(dcm, &G.dPb[0][0], Padded{LDS}, &G.Q[0][0], Padded{LDS}, 0, lane);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
@@ -620,24 +554,18 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
       store_acc_bf16(&G.dCmb[0][0], LDS, 0, 0, dcm[0], lane);
       store_acc_bf16(&G.dCmb[0][0], LDS, 0, 8, dcm[1], lane);
     } else if (gw == 1) {  // dQ += Cm^T dP;  dTi = dW At^T + dQ Bm^T
-      float dq[2][4];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          dq[nt][e] = pr.dQ[(gq + (e >= 2 ? 8 : 0)) * L + 8 * nt + 2 * q + (e & 1)];
       mm16<true, true, 1>(dq, &G.Cm[0][0], Padded{LDS}, &G.dPb[0][0], Padded{LDS}, 0, lane);
       store_acc_bf16(&G.dQ2b[0][0], LDS, 0, 0, dq[0], lane);
       store_acc_bf16(&G.dQ2b[0][0], LDS, 0, 8, dq[1], lane);
       __syncwarp();
       float dti[2][4] = {};
-      mm16<false, false, 4>(dti, &G.dW2b[0][0], Padded{LD}, &G.At[0][0], Padded{LD}, 0, lane);
+      mm16<false, false, 4>(dti, &dW2b[0][0], Padded{LD}, &G.At[0][0], Padded{LD}, 0, lane);
       mm16<false, false, 1>(dti, &G.dQ2b[0][0], Padded{LDS}, &G.Bm[0][0], Padded{LDS}, 0, lane);
       store_acc_f32(&G.dTf[0][0], L + 1, 0, 0, dti[0], lane);
       store_acc_f32(&G.dTf[0][0], L + 1, 0, 8, dti[1], lane);
     }
     float dAt[2][4] = {};  // Ti^T dW (own columns)
-    mm16<true, true, 1>(dAt, &G.Ti[0][0], Padded{LDS}, &G.dW2b[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dAt, &G.Ti[0][0], Padded{LDS}, &dW2b[0][0], Padded{LD}, j0, lane);
     __syncthreads();
     // dA = strict(Ti^T dTi Ti^T) with tf32 operands on warp 0; dBm = strict(Ti^T dQ) on warp 1
     if (gw == 0) {
@@ -695,23 +623,19 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
         const int t = gq + 8 * hf, jj = j0 + 8 * nt + 2 * q;
         const float2 cm = *reinterpret_cast<const float2*>(&G.cum[t][jj]);
         const float2 sg = *reinterpret_cast<const float2*>(&G.sig[t][jj]);
-        const float2 qy = *reinterpret_cast<const float2*>(&pr.dQy[t * kN + jj]);
-        const float2 pb = *reinterpret_cast<const float2*>(&pr.dBb[t * kN + jj]);
-        const float2 pk = *reinterpret_cast<const float2*>(&pr.dKb[t * kN + jj]);
         const float2 rr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_r + tma::swz(t, jj)));
         const float2 kk = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_k + tma::swz(t, jj)));
         const float2 aa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_a + tma::swz(t, jj)));
         const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_b + tma::swz(t, jj)));
-        const float cmv[2] = {cm.x, cm.y}, sgv[2] = {sg.x, sg.y}, qyv[2] = {qy.x, qy.y};
-        const float pbv[2] = {pb.x, pb.y}, pkv[2] = {pk.x, pk.y};
+        const float cmv[2] = {cm.x, cm.y}, sgv[2] = {sg.x, sg.y};
         const float rv[2] = {rr.x, rr.y}, kv[2] = {kk.x, kk.y}, av[2] = {aa.x, aa.y}, bv[2] = {bb.x, bb.y};
         float oda[2], odr[2], odk[2], odb[2];
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           const int e = 2 * hf + x;
           const float Lam = __expf(cmv[x]), Lamx = __expf(cmv[x] - kWScale * sgv[x]), iLam = __expf(-cmv[x]);
-          const float dat = dAt[nt][e], drt = dRt[nt][e] + qyv[x];
-          const float dbb = dBb[nt][e] + pbv[x], dkb = dKb[nt][e] + pkv[x];
+          const float dat = dAt[nt][e], drt = dRt[nt][e] + dQy[nt][e];
+          const float dbb = dBb[nt][e] + dBp[nt][e], dkb = dKb[nt][e] + dKp[nt][e];
           oda[x] = dat * Lamx;
           odr[x] = drt * Lam;
           odk[x] = dkb * iLam;
@@ -735,12 +659,12 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
 #pragma unroll
       for (int t = L - 1; t >= 0; --t) {
         float dc = dcum[t][jj];
-        if (t == L - 1) dc += pr.dll[jj];
+        if (t == L - 1) dc += G.dll[jj];
         s1 += dc;
         const float dlw = s1 + s2;
         s2 += dcumx[t][jj];
         const float sg = G.sig[t][jj];
-        G.dwt[t][jj] = __float2bfloat16_rn(dlw * kWScale * sg * (1.0f - sg));
+        dwt[t][jj] = __float2bfloat16_rn(dlw * kWScale * sg * (1.0f - sg));
       }
     }
     __syncthreads();
@@ -749,9 +673,10 @@ __global__ void __launch_bounds__(kThreads) keyside_bwd_kernel(const __grid_cons
       const int64_t tg = c * L + t;
       if (tg < T)
         *reinterpret_cast<uint4*>(static_cast<bf16*>(p.dw) + cbase + tg * ts + part * 8) =
-            *reinterpret_cast<const uint4*>(&G.dwt[t][part * 8]);
+            *reinterpret_cast<const uint4*>(&dwt[t][part * 8]);
     }
-    __syncthreads();  // raw, prod and scratch free
+    fence_proxy_async();  // generic writes to the XRec scratch before the next bulk load lands there
+    __syncthreads();  // raw, XRec and scratch free
     if (tid == 0 && item + NR * static_cast<int64_t>(gridDim.x) < total)
       issue(G, rb, P, item + NR * static_cast<int64_t>(gridDim.x));
   }
@@ -796,8 +721,8 @@ cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
   kb::Params K;
   K.a = p;
   K.work = work;
-  const void* src[5] = {p.r, p.w, p.k, p.a, p.b};
-  for (int t = 0; t < 5; ++t)
+  const void* src[7] = {p.r, p.w, p.k, p.a, p.b, p.v, p.dy};
+  for (int t = 0; t < 7; ++t)
     if (!tma::encode_bhtn(&K.maps[t], src[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -161,6 +161,29 @@ __device__ __forceinline__ void ldb_kn(uint32_t (&b)[4], const __nv_bfloat16* ti
   ldsm_x4_t(b, tile + lay(k0 + (lane & 7) + ((lane >> 3) & 1) * 8, n0 + (lane >> 4) * 8));
 }
 
+// Store an accumulator tile (16 x 8 at rows m0, cols n0) as bf16 through a layout
+// (shared or global memory).
+template <typename Lay>
+__device__ __forceinline__ void store_acc_lay(__nv_bfloat16* tile, Lay lay, int m0, int n0,
+                                              const float (&c)[4], int lane) {
+  const int g = lane >> 2, q = lane & 3;
+  *reinterpret_cast<__nv_bfloat162*>(tile + lay(m0 + g, n0 + 2 * q)) =
+      __floats2bfloat162_rn(c[0], c[1]);
+  *reinterpret_cast<__nv_bfloat162*>(tile + lay(m0 + g + 8, n0 + 2 * q)) =
+      __floats2bfloat162_rn(c[2], c[3]);
+}
+
+// Store a bf16 A fragment (16 x 16 at rows m0, cols k0) through a layout.
+template <typename Lay>
+__device__ __forceinline__ void store_a_lay(__nv_bfloat16* tile, Lay lay, int m0, int k0,
+                                            const uint32_t (&a)[4], int lane) {
+  const int g = lane >> 2, q = lane & 3;
+  *reinterpret_cast<uint32_t*>(tile + lay(m0 + g, k0 + 2 * q)) = a[0];
+  *reinterpret_cast<uint32_t*>(tile + lay(m0 + g + 8, k0 + 2 * q)) = a[1];
+  *reinterpret_cast<uint32_t*>(tile + lay(m0 + g, k0 + 8 + 2 * q)) = a[2];
+  *reinterpret_cast<uint32_t*>(tile + lay(m0 + g + 8, k0 + 8 + 2 * q)) = a[3];
+}
+
 // acc (16 x 16 output at columns n0) += A (16 x 16*KS) B;
 // AT: A stored [k][m] (else [m][k]); BT: B stored [k][n] (else [n][k]).
 template <bool AT, bool BT, int KS, typename LA, typename LB>

@@ -12,7 +12,7 @@
 // chunk this is 9472 + 4096 bytes, below the 16 KiB per chunk of the
 // reference's [B, H, T/16, 64, 64] fp32 checkpoint tensor.
 //
-// Backward workspace: [chains][nchunk] ProdRec.
+// Backward workspace: [chains][nchunk] XRec.
 #pragma once
 
 #include "wkv7_common.cuh"
@@ -29,17 +29,18 @@ struct KeyRec {
 };
 static_assert(sizeof(KeyRec) == 9472, "KeyRec layout");
 
-// sums over the 64 state rows that the key-side backward needs (plain row-major)
-struct ProdRec {
-  float dW[16 * 64];   // dSA S
-  float dQy[16 * 64];  // dY S
-  float dBb[16 * 64];  // SA (dS' diag lam)
-  float dKb[16 * 64];  // V (dS' diag lam)
-  float dQ[16 * 16];   // strict(dSA V^T)
-  float dP[16 * 16];   // lower(dY V^T)
-  float dll[64];       // colsum(dS' o S') over the chunk's end state
+// What the value-side backward hands to the key-side backward for one chunk:
+// bf16 copies of the chunk's start state S, of G'' = dL/dS' diag(lam), of SA^T
+// and dSA^T (rows = state row i), and per value warp the column sums over its
+// 16 rows of dL/dS' o S' (summed by the reader, so the result is deterministic).
+struct XRec {
+  bf16 S[64 * 64];     // Swz64 layout over 64 rows
+  bf16 G[64 * 64];     // Swz64
+  bf16 SAT[64 * 16];   // Swz16 layout over 64 rows
+  bf16 dSAT[64 * 16];  // Swz16
+  float dll[4][64];
 };
-static_assert(sizeof(ProdRec) % 16 == 0, "ProdRec size");
+static_assert(sizeof(XRec) % 16 == 0, "XRec size");
 
 constexpr int64_t kStateBytes = 64 * 64 * 2;
 
@@ -51,7 +52,7 @@ __host__ __device__ __forceinline__ size_t ckpt_bytes(int64_t chains, int64_t nc
          static_cast<size_t>(chains * nstate(nchunk)) * kStateBytes;
 }
 __host__ __device__ __forceinline__ size_t work_bytes(int64_t chains, int64_t nchunk) {
-  return static_cast<size_t>(chains * nchunk) * sizeof(ProdRec);
+  return static_cast<size_t>(chains * nchunk) * sizeof(XRec);
 }
 __device__ __forceinline__ KeyRec* keyrec(void* ckpt, int64_t ch, int64_t nchunk, int64_t c) {
   return reinterpret_cast<KeyRec*>(ckpt) + (ch * nchunk + c);
@@ -62,8 +63,8 @@ __device__ __forceinline__ char* state_ptr(void* ckpt, int64_t chains, int64_t c
   char* base = reinterpret_cast<char*>(ckpt) + chains * nchunk * sizeof(KeyRec);
   return base + (ch * nstate(nchunk) + (c / 2 - 1)) * kStateBytes;
 }
-__device__ __forceinline__ ProdRec* prodrec(void* work, int64_t ch, int64_t nchunk, int64_t c) {
-  return reinterpret_cast<ProdRec*>(work) + (ch * nchunk + c);
+__device__ __forceinline__ XRec* xrec(void* work, int64_t ch, int64_t nchunk, int64_t c) {
+  return reinterpret_cast<XRec*>(work) + (ch * nchunk + c);
 }
 
 }  // namespace rec
