@@ -49,33 +49,52 @@ using ks::Tile16;
 
 namespace vb {
 
-constexpr int NS = 8;
-constexpr int kThreads = 160;  // value warps 0-3, producer warp 4
+// The state rows are independent in the recurrence (the transition acts on the
+// key dimension), so a chain's 64 rows are split over 4 / RB CTAs of RB row
+// blocks (16 rows) each.  Per row block a CTA runs a G warp (the gradient
+// recurrence), a state warp (start states, SA, dll) and a dV warp; a producer
+// warp streams the inputs and a store warp writes the staged outputs (the
+// chunk's XRec rows and the dv tile) with bulk copies.
+constexpr int NS = 4;  // input slots (power of two)
+constexpr int NX = 4;  // output stages (power of two)
 
+template <int RB>
 struct alignas(1024) Slot {
-  bf16 v[L * kN];   // TMA 128-byte swizzled
+  bf16 v[L * kN];   // TMA 128-byte swizzled, all 64 columns
   bf16 dy[L * kN];  // TMA 128-byte swizzled
   float dsa[L][kN];
   rec::KeyRec k;
-  uint4 S[512];  // state at the chunk start (even chunks >= 2), A-fragment order
+  uint4 S[RB][4][32];  // this CTA's rows of the state at the chunk start (even chunks >= 2)
 };
 
+template <int RB>
+struct alignas(1024) Stage {
+  bf16 dv[L][16 * RB];   // dV tile [t][i] of this CTA's rows (TMA store)
+  bf16 S[16 * RB * kN];  // Swz64, this CTA's rows of the XRec tiles
+  bf16 G[16 * RB * kN];  // Swz64
+  bf16 SAT[16 * RB * L];   // Swz16
+  bf16 dSAT[16 * RB * L];  // Swz16
+  float dll[RB][kN];
+};
+
+template <int RB>
 struct Smem {
-  Slot slot[NS];
-  uint64_t full[NS], empty[NS];
+  Slot<RB> slot[NS];
+  Stage<RB> st[NX];
+  uint64_t full[NS], empty[NS], gfull[NX], sfull[NX], sempty[NX];
 };
 
 struct Params {
-  CUtensorMap map_v, map_dy, map_dsa;
+  CUtensorMap map_v, map_dy, map_dsa, map_dv;
   BwdArgs a;
   void* work;
 };
 
 // Chunks are taken from the end in groups: one lone even chunk first when
-// nchunk is odd, then (even, odd) pairs.  Returns lo, hi (hi == lo for a lone
-// chunk) and the load index of lo.
-__device__ __forceinline__ void group_of(int64_t nchunk, int64_t gi, int64_t& lo, int64_t& hi,
-                                         int64_t& idx_lo) {
+// nchunk is odd, then (even, odd) pairs; lo is loaded before hi, hi is
+// processed before lo.  Returns lo, hi (hi == lo for a lone chunk) and the
+// load index of lo.
+__device__ __forceinline__ void group_of(int nchunk, int gi, int& lo, int& hi, int& idx_lo) {
   if (nchunk & 1) {
     if (gi == 0) { lo = hi = nchunk - 1; idx_lo = 0; return; }
     lo = nchunk - 1 - 2 * gi;
@@ -87,295 +106,390 @@ __device__ __forceinline__ void group_of(int64_t nchunk, int64_t gi, int64_t& lo
   hi = lo + 1;
 }
 
-__device__ __forceinline__ int64_t num_groups(int64_t nchunk) { return (nchunk + 1) / 2; }
+// Load index (slot order) of chunk c; its processing index is nchunk - 1 - c.
+__device__ __forceinline__ int load_idx(int nchunk, int c) {
+  if ((nchunk & 1) && c == nchunk - 1) return 0;
+  return (c & 1) ? nchunk - c : nchunk - 2 - c;
+}
 
-// One chunk c of the value-warp backward (warp wq owns state rows 16wq..16wq+15):
-// G'' = G diag(lam); SA (or the precomputed satPre); dSA; dV -> global; the bf16
-// S, G'', SA^T, dSA^T rows of this warp -> the chunk's XRec; G <- dS; the column
-// sums of G o S over this warp's rows -> dll of chunk c - 1.
-__device__ __forceinline__ void value_chunk(const Slot& sl, const BwdArgs& p, rec::XRec* xr,
-                                            int64_t c, const uint32_t (&sA)[4][4],
-                                            const float (&satPre)[2][4], bool have_sat,
-                                            float (&G)[8][4], int wq, int lane, int64_t cbase,
-                                            int64_t ts, int64_t T, bool has_dsa) {
-  const int g = lane >> 2, q = lane & 3, i0 = 16 * wq;
-  const rec::KeyRec& kr = sl.k;
-  uint32_t b[4], vA[4], dyA[4];
+__device__ __forceinline__ uint32_t par(int idx, int n) { return static_cast<uint32_t>((idx / n) & 1); }
 
-  // G'' = G diag(lam)
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
-    G[nt][0] *= l.x; G[nt][1] *= l.y; G[nt][2] *= l.x; G[nt][3] *= l.y;
-  }
-  uint32_t gA[4][4];
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) acc_to_a(gA[kk], G[2 * kk], G[2 * kk + 1]);
-  lda_cm(vA, sl.v, Swz64{}, i0, 0, lane);
-  lda_cm(dyA, sl.dy, Swz64{}, i0, 0, lane);
-
-  float sat[2][4], dsat[2][4];
-  if (have_sat) {
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sat[nt][e] = satPre[nt][e];
-  } else {
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sat[nt][e] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
-      mma16816(sat[0], sA[kk], b[0], b[1]);
-      mma16816(sat[1], sA[kk], b[2], b[3]);
-    }
-    ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
-    mma16816(sat[0], vA, b[0], b[1]);
-    mma16816(sat[1], vA, b[2], b[3]);
-  }
+// SA^T fragments (rows = one row block, cols = t) of a chunk: S W^T + V Q^T.
+__device__ __forceinline__ void sa_of(float (&sat)[2][4], const rec::KeyRec& kr,
+                                      const uint32_t (&sA)[4][4], const uint32_t (&vA)[4], int lane) {
+  uint32_t b[4];
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
-      dsat[nt][e] = has_dsa ? sl.dsa[8 * nt + 2 * q + (e & 1)][i0 + g + (e >= 2 ? 8 : 0)] : 0.f;
+    for (int e = 0; e < 4; ++e) sat[nt][e] = 0.f;
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
-    ldb_nk(b, kr.Bb, Swz64{}, 0, 16 * kk, lane);
-    mma16816(dsat[0], gA[kk], b[0], b[1]);
-    mma16816(dsat[1], gA[kk], b[2], b[3]);
+    ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
+    mma16816(sat[0], sA[kk], b[0], b[1]);
+    mma16816(sat[1], sA[kk], b[2], b[3]);
   }
-  uint32_t dsaA[4];
-  acc_to_a(dsaA, dsat[0], dsat[1]);
-
-  // this warp's rows of S, G'', SA^T, dSA^T for the key-side backward
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    store_a_lay(xr->S, Swz64{}, i0, 16 * kk, sA[kk], lane);
-    store_a_lay(xr->G, Swz64{}, i0, 16 * kk, gA[kk], lane);
-  }
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    store_acc_lay(xr->SAT, Swz16{}, i0, 8 * nt, sat[nt], lane);
-    store_acc_lay(xr->dSAT, Swz16{}, i0, 8 * nt, dsat[nt], lane);
-  }
-
-  // dV^T = G'' Kb^T + dY^T P + dSA^T Q
-  {
-    float dvt[2][4] = {};
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      ldb_nk(b, kr.Kb, Swz64{}, 0, 16 * kk, lane);
-      mma16816(dvt[0], gA[kk], b[0], b[1]);
-      mma16816(dvt[1], gA[kk], b[2], b[3]);
-    }
-    ldb_kn(b, kr.P, Swz16{}, 0, 0, lane);
-    mma16816(dvt[0], dyA, b[0], b[1]);
-    mma16816(dvt[1], dyA, b[2], b[3]);
-    ldb_kn(b, kr.Q, Swz16{}, 0, 0, lane);
-    mma16816(dvt[0], dsaA, b[0], b[1]);
-    mma16816(dvt[1], dsaA, b[2], b[3]);
-    bf16* dvp = static_cast<bf16*>(p.dv);
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int64_t t = c * L + 8 * nt + 2 * q + (e & 1);
-        if (t < T) dvp[cbase + t * ts + i0 + g + (e >= 2 ? 8 : 0)] = __float2bfloat16_rn(dvt[nt][e]);
-      }
-  }
-
-  // dS = G'' + dY^T Qy + dSA^T W  -> G of the previous chunk
-#pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    ldb_kn(b, kr.Qy, Swz64{}, 16 * m, 0, lane);
-    mma16816(G[2 * m], dyA, b[0], b[1]);
-    mma16816(G[2 * m + 1], dyA, b[2], b[3]);
-    ldb_kn(b, kr.W, Swz64{}, 16 * m, 0, lane);
-    mma16816(G[2 * m], dsaA, b[0], b[1]);
-    mma16816(G[2 * m + 1], dsaA, b[2], b[3]);
-  }
-
-  // dll of chunk c - 1: column sums over this warp's rows of G o S (S = its end state)
-  if (c >= 1) {
-    // per-thread partial sums over rows g, g+8 of columns 8nt + 2q + x, as v[2nt + x]
-    float v[16];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const uint32_t lo2 = sA[nt >> 1][2 * (nt & 1)], hi2 = sA[nt >> 1][2 * (nt & 1) + 1];
-      const float2 s0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo2));
-      const float2 s1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi2));
-      v[2 * nt] = G[nt][0] * s0.x + G[nt][2] * s1.x;
-      v[2 * nt + 1] = G[nt][1] * s0.y + G[nt][3] * s1.y;
-    }
-    // reduce-scatter over the 8 row lanes (lane bits 4, 3, 2): lane g keeps v[2g], v[2g+1]
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      const bool up = lane & 16;
-      const float send = up ? v[m] : v[m + 8], keep = up ? v[m + 8] : v[m];
-      v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const bool up = lane & 8;
-      const float send = up ? v[m] : v[m + 4], keep = up ? v[m + 4] : v[m];
-      v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-#pragma unroll
-    for (int m = 0; m < 2; ++m) {
-      const bool up = lane & 4;
-      const float send = up ? v[m] : v[m + 2], keep = up ? v[m + 2] : v[m];
-      v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-    *reinterpret_cast<float2*>(&(xr - 1)->dll[wq][8 * g + 2 * q]) = make_float2(v[0], v[1]);
-  }
+  ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
+  mma16816(sat[0], vA, b[0], b[1]);
+  mma16816(sat[1], vA, b[2], b[3]);
 }
 
-__global__ void __launch_bounds__(kThreads, 1) value_bwd_kernel(const __grid_constant__ Params P) {
+// State warp, one chunk: its S and SA^T rows -> stage; the stage's dll row =
+// column sums over its rows of G'' o S' (S' = sNext, the start state of the
+// following chunk, zero for the last chunk), i.e. lam * dL/dlam.
+template <int RB>
+__device__ __forceinline__ void s_chunk(Stage<RB>& st, const uint32_t (&sA)[4][4],
+                                        const float (&sat)[2][4], const uint32_t (&sNext)[4][4],
+                                        int r, int lane) {
+  const int g = lane >> 2, q = lane & 3, il = 16 * r;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) sta_rm(st.S, Swz64{}, il, 16 * kk, sA[kk], lane);
+  uint32_t saA[4];
+  acc_to_a(saA, sat[0], sat[1]);
+  sta_rm(st.SAT, Swz16{}, il, 0, saA, lane);
+  // per-thread partial sums over rows g, g+8 of columns 16kk + 8h + 2q + x, as v[4kk + 2h + x]
+  float v[16];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    uint32_t gr[4];
+    lda_rm(gr, st.G, Swz64{}, il, 16 * kk, lane);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {  // regs (2h, 2h+1): rows g, g+8 of columns 16kk + 8h + 2q
+      const float2 g0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr[2 * h]));
+      const float2 g1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr[2 * h + 1]));
+      const float2 s0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sNext[kk][2 * h]));
+      const float2 s1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sNext[kk][2 * h + 1]));
+      v[4 * kk + 2 * h] = g0.x * s0.x + g1.x * s1.x;
+      v[4 * kk + 2 * h + 1] = g0.y * s0.y + g1.y * s1.y;
+    }
+  }
+  // v[2n + x] is column 8n + 2q + x; reduce-scatter over the 8 row lanes
+  // (lane bits 4, 3, 2): lane g keeps v[2g], v[2g+1]
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const bool up = lane & 16;
+    const float send = up ? v[m] : v[m + 8], keep = up ? v[m + 8] : v[m];
+    v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const bool up = lane & 8;
+    const float send = up ? v[m] : v[m + 4], keep = up ? v[m + 4] : v[m];
+    v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    const bool up = lane & 4;
+    const float send = up ? v[m] : v[m + 2], keep = up ? v[m + 2] : v[m];
+    v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  *reinterpret_cast<float2*>(&st.dll[r][8 * g + 2 * q]) = make_float2(v[0], v[1]);
+}
+
+template <int RB>
+__global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
+  Smem<RB>& sm = *reinterpret_cast<Smem<RB>*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
+  constexpr int NRG = 4 / RB;  // CTAs per chain
   const BwdArgs& p = P.a;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t ch = blockIdx.x;
-  const int64_t nchunk = p.g.nchunk, T = p.g.T, ts = p.g.tstride();
-  const int64_t cbase = p.g.base(ch), chains = p.g.chains();
-  const int64_t ngroups = num_groups(nchunk);
+  const int64_t ch = blockIdx.x / NRG;
+  const int row0 = 16 * RB * static_cast<int>(blockIdx.x % NRG);  // first state row of this CTA
+  const int nchunk = static_cast<int>(p.g.nchunk);
+  const int ngroups = (nchunk + 1) / 2;
   const bool has_dsa = p.dsa != nullptr;
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 4);
+      mbar_init(&sm.empty[s], 3 * RB);
+    }
+    for (int x = 0; x < NX; ++x) {
+      mbar_init(&sm.gfull[x], RB);
+      mbar_init(&sm.sfull[x], 2 * RB);
+      mbar_init(&sm.sempty[x], 1);
     }
     mbar_fence_init();
   }
   __syncthreads();
 
-  if (warp == 4) {
+  const int hh = static_cast<int>(p.g.h0 + ch % p.g.hc), bb = static_cast<int>(ch / p.g.hc);
+  if (warp == 3 * RB) {
     // ------------------------------ producer ------------------------------
     if (lane != 0) return;
-    const int hh = static_cast<int>(p.g.h0 + ch % p.g.hc), bb = static_cast<int>(ch / p.g.hc);
-    int64_t issued = 0;
+    const int64_t chains = p.g.chains();
+    int issued = 0;
     bool ok = true;
-    for (int64_t gi = 0; gi < ngroups && ok; ++gi) {
-      int64_t lo, hi, idx;
+    for (int gi = 0; gi < ngroups && ok; ++gi) {
+      int lo, hi, idx;
       group_of(nchunk, gi, lo, hi, idx);
-      for (int64_t c = lo; c <= hi && ok; ++c, ++idx) {
-        const int s = static_cast<int>(idx % NS);
-        if (idx >= NS) ok = mbar_wait(&sm.empty[s], static_cast<uint32_t>((idx / NS - 1) & 1));
+      for (int c = lo; c <= hi && ok; ++c, ++idx) {
+        const int s = idx & (NS - 1);
+        if (idx >= NS) ok = mbar_wait(&sm.empty[s], par(idx - NS, NS));
         if (!ok) break;
         const bool with_state = c == lo && lo >= 2;
         const uint32_t bytes = sizeof(rec::KeyRec) + 2 * tma::kTileBytes +
-                               (has_dsa ? L * kN * 4 : 0) + (with_state ? 8192 : 0);
-        Slot& sl = sm.slot[s];
+                               (has_dsa ? L * kN * 4 : 0) + (with_state ? 2048 * RB : 0);
+        Slot<RB>& sl = sm.slot[s];
         mbar_arrive_expect_tx(&sm.full[s], bytes);
         bulk_g2s(&sl.k, rec::keyrec(const_cast<float*>(p.ckpt), ch, nchunk, c), sizeof(rec::KeyRec), &sm.full[s]);
-        tma::load_tile(sl.v, &P.map_v, hh, static_cast<int>(c * L), bb, &sm.full[s]);
-        tma::load_tile(sl.dy, &P.map_dy, hh, static_cast<int>(c * L), bb, &sm.full[s]);
-        if (has_dsa) tma::load_tile(&sl.dsa[0][0], &P.map_dsa, hh, static_cast<int>(c * L), bb, &sm.full[s]);
+        tma::load_tile(sl.v, &P.map_v, hh, c * L, bb, &sm.full[s]);
+        tma::load_tile(sl.dy, &P.map_dy, hh, c * L, bb, &sm.full[s]);
+        if (has_dsa) tma::load_tile(&sl.dsa[0][0], &P.map_dsa, hh, c * L, bb, &sm.full[s]);
         if (with_state)
-          bulk_g2s(sl.S, rec::state_ptr(const_cast<float*>(p.ckpt), chains, ch, nchunk, lo), 8192, &sm.full[s]);
+          bulk_g2s(sl.S, rec::state_ptr(const_cast<float*>(p.ckpt), chains, ch, nchunk, lo) + row0 * 128,
+                   2048 * RB, &sm.full[s]);
         ++issued;
       }
     }
     if (!ok)  // stopped on a timeout: let the copies in flight land
-      for (int64_t i = issued > NS ? issued - NS : 0; i < issued; ++i)
-        mbar_wait(&sm.full[i % NS], static_cast<uint32_t>((i / NS) & 1));
+      for (int i = issued > NS ? issued - NS : 0; i < issued; ++i)
+        mbar_wait(&sm.full[i & (NS - 1)], par(i, NS));
     return;
   }
 
-  // ------------------------------ value warps ------------------------------
-  const int wq = warp, i0 = 16 * wq, q = lane & 3;
-  float G[8][4];  // dL/dS' of the chunk being processed
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) G[nt][e] = 0.f;
-  if (nchunk > 0)  // the last chunk has no following chunk: dll = 0
-    *reinterpret_cast<float2*>(&rec::xrec(P.work, ch, nchunk, nchunk - 1)->dll[wq][2 * lane]) =
-        make_float2(0.f, 0.f);
-  for (int64_t gi = 0; gi < ngroups; ++gi) {
-    int64_t lo, hi, idx_lo;
-    group_of(nchunk, gi, lo, hi, idx_lo);
-    const int s_lo = static_cast<int>(idx_lo % NS);
-    const int s_hi = static_cast<int>((idx_lo + 1) % NS);
-    if (!mbar_wait(&sm.full[s_lo], static_cast<uint32_t>((idx_lo / NS) & 1))) return;
-    if (hi != lo && !mbar_wait(&sm.full[s_hi], static_cast<uint32_t>(((idx_lo + 1) / NS) & 1))) return;
+  if (warp == 3 * RB + 1) {
+    // ------------------------------ store warp ------------------------------
+    if (lane != 0) return;
+    for (int pi = 0; pi < nchunk; ++pi) {
+      const int c = nchunk - 1 - pi, x = pi & (NX - 1);
+      if (!mbar_wait(&sm.sfull[x], par(pi, NX))) break;
+      const Stage<RB>& st = sm.st[x];
+      rec::XRec* xr = rec::xrec(P.work, ch, nchunk, c);
+      bulk_s2g(xr->S + row0 * kN, st.S, 2048 * RB);
+      bulk_s2g(xr->G + row0 * kN, st.G, 2048 * RB);
+      bulk_s2g(xr->SAT + row0 * L, st.SAT, 512 * RB);
+      bulk_s2g(xr->dSAT + row0 * L, st.dSAT, 512 * RB);
+      bulk_s2g(&xr->dll[row0 / 16][0], &st.dll[0][0], 256 * RB);
+      tma::store_tile(&P.map_dv, &st.dv[0][0], row0, hh, c * L, bb);
+      bulk_commit();
+      bulk_wait_read();
+      mbar_arrive(&sm.sempty[x]);
+    }
+    bulk_wait_all();
+    return;
+  }
 
-    // state at the start of lo (A fragments)
-    uint32_t sLo[4][4];
+  const int role = warp / RB, r = warp % RB;
+  const int il = 16 * r, i0 = row0 + il;  // local and global first row of this warp's block
+  const int q = lane & 3, g = lane >> 2;
+  if (role == 0) {
+    // ------------------------------ G warp: the gradient recurrence ------------------------------
+    float G[8][4];  // dL/dS' of the chunk being processed
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) G[nt][e] = 0.f;
+    for (int pi = 0; pi < nchunk; ++pi) {
+      const int c = nchunk - 1 - pi, li = load_idx(nchunk, c);
+      const int s = li & (NS - 1), x = pi & (NX - 1);
+      if (!mbar_wait(&sm.full[s], par(li, NS))) return;
+      if (pi >= NX && !mbar_wait(&sm.sempty[x], par(pi - NX, NX))) return;
+      const Slot<RB>& sl = sm.slot[s];
+      Stage<RB>& st = sm.st[x];
+      const rec::KeyRec& kr = sl.k;
+      uint32_t b[4], dyA[4];
+      // G'' = G diag(lam)
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
+        G[nt][0] *= l.x; G[nt][1] *= l.y; G[nt][2] *= l.x; G[nt][3] *= l.y;
+      }
+      uint32_t gA[4][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) acc_to_a(gA[kk], G[2 * kk], G[2 * kk + 1]);
+      // dSA = dSA_ext + Bb G''^T (rows i, cols t)
+      float dsat[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          dsat[nt][e] = has_dsa ? sl.dsa[8 * nt + 2 * q + (e & 1)][i0 + g + (e >= 2 ? 8 : 0)] : 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        ldb_nk(b, kr.Bb, Swz64{}, 0, 16 * kk, lane);
+        mma16816(dsat[0], gA[kk], b[0], b[1]);
+        mma16816(dsat[1], gA[kk], b[2], b[3]);
+      }
+      uint32_t dsaA[4];
+      acc_to_a(dsaA, dsat[0], dsat[1]);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) sta_rm(st.G, Swz64{}, il, 16 * kk, gA[kk], lane);
+      sta_rm(st.dSAT, Swz16{}, il, 0, dsaA, lane);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.gfull[x]);
+      // dS = G'' + dY^T Qy + dSA^T W  -> G of the previous chunk
+      lda_cm(dyA, sl.dy, Swz64{}, i0, 0, lane);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        ldb_kn(b, kr.Qy, Swz64{}, 16 * m, 0, lane);
+        mma16816(G[2 * m], dyA, b[0], b[1]);
+        mma16816(G[2 * m + 1], dyA, b[2], b[3]);
+        ldb_kn(b, kr.W, Swz64{}, 16 * m, 0, lane);
+        mma16816(G[2 * m], dsaA, b[0], b[1]);
+        mma16816(G[2 * m + 1], dsaA, b[2], b[3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[s]);
+    }
+    return;
+  }
+
+  if (role == 2) {
+    // ------------------------------ dV warp ------------------------------
+    for (int pi = 0; pi < nchunk; ++pi) {
+      const int c = nchunk - 1 - pi, li = load_idx(nchunk, c);
+      const int s = li & (NS - 1), x = pi & (NX - 1);
+      if (!mbar_wait(&sm.full[s], par(li, NS))) return;
+      if (!mbar_wait(&sm.gfull[x], par(pi, NX))) return;
+      const Slot<RB>& sl = sm.slot[s];
+      Stage<RB>& st = sm.st[x];
+      const rec::KeyRec& kr = sl.k;
+      uint32_t b[4], dyA[4], dsaA[4], gA[4][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) lda_rm(gA[kk], st.G, Swz64{}, il, 16 * kk, lane);
+      lda_rm(dsaA, st.dSAT, Swz16{}, il, 0, lane);
+      lda_cm(dyA, sl.dy, Swz64{}, i0, 0, lane);
+      // dV^T = G'' Kb^T + dY^T P + dSA^T Q
+      float dvt[2][4] = {};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        ldb_nk(b, kr.Kb, Swz64{}, 0, 16 * kk, lane);
+        mma16816(dvt[0], gA[kk], b[0], b[1]);
+        mma16816(dvt[1], gA[kk], b[2], b[3]);
+      }
+      ldb_kn(b, kr.P, Swz16{}, 0, 0, lane);
+      mma16816(dvt[0], dyA, b[0], b[1]);
+      mma16816(dvt[1], dyA, b[2], b[3]);
+      ldb_kn(b, kr.Q, Swz16{}, 0, 0, lane);
+      mma16816(dvt[0], dsaA, b[0], b[1]);
+      mma16816(dvt[1], dsaA, b[2], b[3]);
+      uint32_t dvA[4];
+      acc_to_a(dvA, dvt[0], dvt[1]);
+      sta_cm(&st.dv[0][0], Padded{16 * RB}, il, 0, dvA, lane);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.sfull[x]);
+        mbar_arrive(&sm.empty[s]);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------ state warp ------------------------------
+  uint32_t sNext[4][4];  // start state of the chunk after the one being processed
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) sNext[kk][0] = sNext[kk][1] = sNext[kk][2] = sNext[kk][3] = 0u;
+  for (int gi = 0; gi < ngroups; ++gi) {
+    int lo, hi, idx_lo;
+    group_of(nchunk, gi, lo, hi, idx_lo);
+    const int s_lo = idx_lo & (NS - 1), s_hi = (idx_lo + 1) & (NS - 1);
+    if (!mbar_wait(&sm.full[s_lo], par(idx_lo, NS))) return;
+    if (hi != lo && !mbar_wait(&sm.full[s_hi], par(idx_lo + 1, NS))) return;
+    const Slot<RB>& slo = sm.slot[s_lo];
+    const rec::KeyRec& kr = slo.k;
+
+    uint32_t sLo[4][4], vA[4];
     if (lo >= 2) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const uint4 x = sm.slot[s_lo].S[(wq * 4 + kk) * 32 + lane];
-        sLo[kk][0] = x.x; sLo[kk][1] = x.y; sLo[kk][2] = x.z; sLo[kk][3] = x.w;
+        const uint4 xv = slo.S[r][kk][lane];
+        sLo[kk][0] = xv.x; sLo[kk][1] = xv.y; sLo[kk][2] = xv.z; sLo[kk][3] = xv.w;
       }
     } else {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) sLo[kk][0] = sLo[kk][1] = sLo[kk][2] = sLo[kk][3] = 0u;
     }
-    // SA of lo (needed by lo's backward, and by the recompute of hi's start state)
-    float satLo[2][4] = {};
-    {
-      const rec::KeyRec& kr = sm.slot[s_lo].k;
-      uint32_t vA[4], b[4];
+    lda_cm(vA, slo.v, Swz64{}, i0, 0, lane);
+    float satLo[2][4];
+    sa_of(satLo, kr, sLo, vA, lane);
+    if (hi != lo) {
+      // S(hi) = (S(lo) + SA^T Bb + V^T Kb) diag(lam), from chunk lo
+      uint32_t sHi[4][4], b[4];
+      {
+        float Sf[8][4];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
-        mma16816(satLo[0], sLo[kk], b[0], b[1]);
-        mma16816(satLo[1], sLo[kk], b[2], b[3]);
-      }
-      lda_cm(vA, sm.slot[s_lo].v, Swz64{}, i0, 0, lane);
-      ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
-      mma16816(satLo[0], vA, b[0], b[1]);
-      mma16816(satLo[1], vA, b[2], b[3]);
-      if (hi != lo) {  // S(hi) = (S(lo) + SA^T Bb + V^T Kb) diag(lam), from chunk lo
-        uint32_t sHi[4][4];
-        {
-          float Sf[8][4];
+        for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              // sLo[kk] is the A fragment of n8 tiles (2kk, 2kk+1): regs 0,1 -> 2kk, 2,3 -> 2kk+1
-              const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sLo[kk][h]));
-              const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sLo[kk][2 + h]));
-              Sf[2 * kk][2 * h] = a0.x;
-              Sf[2 * kk][2 * h + 1] = a0.y;
-              Sf[2 * kk + 1][2 * h] = a1.x;
-              Sf[2 * kk + 1][2 * h + 1] = a1.y;
-            }
-          uint32_t saA[4];
-          acc_to_a(saA, satLo[0], satLo[1]);
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            ldb_kn(b, kr.Bb, Swz64{}, 16 * m, 0, lane);
-            mma16816(Sf[2 * m], saA, b[0], b[1]);
-            mma16816(Sf[2 * m + 1], saA, b[2], b[3]);
-            ldb_kn(b, kr.Kb, Swz64{}, 16 * m, 0, lane);
-            mma16816(Sf[2 * m], vA, b[0], b[1]);
-            mma16816(Sf[2 * m + 1], vA, b[2], b[3]);
+          for (int h = 0; h < 2; ++h) {
+            // sLo[kk] is the A fragment of n8 tiles (2kk, 2kk+1): regs 0,1 -> 2kk, 2,3 -> 2kk+1
+            const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sLo[kk][h]));
+            const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sLo[kk][2 + h]));
+            Sf[2 * kk][2 * h] = a0.x;
+            Sf[2 * kk][2 * h + 1] = a0.y;
+            Sf[2 * kk + 1][2 * h] = a1.x;
+            Sf[2 * kk + 1][2 * h + 1] = a1.y;
           }
+        uint32_t saA[4];
+        acc_to_a(saA, satLo[0], satLo[1]);
 #pragma unroll
-          for (int nt = 0; nt < 8; ++nt) {
-            const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
-            Sf[nt][0] *= l.x; Sf[nt][1] *= l.y; Sf[nt][2] *= l.x; Sf[nt][3] *= l.y;
-          }
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) acc_to_a(sHi[kk], Sf[2 * kk], Sf[2 * kk + 1]);
+        for (int m = 0; m < 4; ++m) {
+          ldb_kn(b, kr.Bb, Swz64{}, 16 * m, 0, lane);
+          mma16816(Sf[2 * m], saA, b[0], b[1]);
+          mma16816(Sf[2 * m + 1], saA, b[2], b[3]);
+          ldb_kn(b, kr.Kb, Swz64{}, 16 * m, 0, lane);
+          mma16816(Sf[2 * m], vA, b[0], b[1]);
+          mma16816(Sf[2 * m + 1], vA, b[2], b[3]);
         }
-        value_chunk(sm.slot[s_hi], p, rec::xrec(P.work, ch, nchunk, hi), hi, sHi, satLo, false,
-                    G, wq, lane, cbase, ts, T, has_dsa);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.empty[s_hi]);
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
+          Sf[nt][0] *= l.x; Sf[nt][1] *= l.y; Sf[nt][2] *= l.x; Sf[nt][3] *= l.y;
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) acc_to_a(sHi[kk], Sf[2 * kk], Sf[2 * kk + 1]);
       }
+      const Slot<RB>& shi = sm.slot[s_hi];
+      uint32_t vHi[4];
+      lda_cm(vHi, shi.v, Swz64{}, i0, 0, lane);
+      float satHi[2][4];
+      sa_of(satHi, shi.k, sHi, vHi, lane);
+      const int pi = nchunk - 1 - hi, x = pi & (NX - 1);
+      if (!mbar_wait(&sm.gfull[x], par(pi, NX))) return;
+      s_chunk(sm.st[x], sHi, satHi, sNext, r, lane);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.sfull[x]);
+        mbar_arrive(&sm.empty[s_hi]);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sNext[kk][e] = sHi[kk][e];
     }
-    value_chunk(sm.slot[s_lo], p, rec::xrec(P.work, ch, nchunk, lo), lo, sLo, satLo, true, G,
-                wq, lane, cbase, ts, T, has_dsa);
+    const int pi = nchunk - 1 - lo, x = pi & (NX - 1);
+    if (!mbar_wait(&sm.gfull[x], par(pi, NX))) return;
+    s_chunk(sm.st[x], sLo, satLo, sNext, r, lane);
+    fence_proxy_async();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[s_lo]);
+    if (lane == 0) {
+      mbar_arrive(&sm.sfull[x]);
+      mbar_arrive(&sm.empty[s_lo]);
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sNext[kk][e] = sLo[kk][e];
   }
+}
+
+template <int RB>
+cudaError_t launch(const Params& V, int64_t chains, cudaStream_t stream) {
+  const size_t smem = sizeof(Smem<RB>) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(value_bwd_kernel<RB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  value_bwd_kernel<RB><<<static_cast<unsigned>(chains * (4 / RB)), 32 * (3 * RB + 2), smem, stream>>>(V);
+  return cudaGetLastError();
+}
+
+// Row blocks per CTA: split chains over as many CTAs as the SMs can hold at once.
+inline int rows_per_cta(int64_t chains, int sms) {
+  if (chains * 4 <= sms) return 1;
+  if (chains * 2 <= sms) return 2;
+  return 4;
 }
 
 }  // namespace vb
@@ -659,7 +773,7 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
 #pragma unroll
       for (int t = L - 1; t >= 0; --t) {
         float dc = dcum[t][jj];
-        if (t == L - 1) dc += G.dll[jj];
+        if (t == L - 1) dc += G.dll[jj] / G.lam[jj];  // the XRec holds colsum(G'' o S') = lam dll
         s1 += dc;
         const float dlw = s1 + s2;
         s2 += dcumx[t][jj];
@@ -702,20 +816,21 @@ size_t work_bytes(int64_t chains, int64_t T) {
 }
 
 cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int rb = vb::rows_per_cta(p.g.chains(), sms);
   vb::Params V;
   V.a = p;
   V.work = work;
   if (!tma::encode_bhtn(&V.map_v, p.v, p.g.B, p.g.T, p.g.H) ||
-      !tma::encode_bhtn(&V.map_dy, p.dy, p.g.B, p.g.T, p.g.H))
+      !tma::encode_bhtn(&V.map_dy, p.dy, p.g.B, p.g.T, p.g.H) ||
+      !tma::encode_bhtn_cols(&V.map_dv, p.dv, p.g.B, p.g.T, p.g.H, 16 * rb))
     return cudaErrorInvalidValue;
   if (p.dsa != nullptr && !tma::encode_bhtn_f32(&V.map_dsa, p.dsa, p.g.B, p.g.T, p.g.H))
     return cudaErrorInvalidValue;
-  const size_t vsmem = sizeof(vb::Smem) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(vb::value_bwd_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vsmem);
-  if (e != cudaSuccess) return e;
-  vb::value_bwd_kernel<<<(unsigned)p.g.chains(), vb::kThreads, vsmem, stream>>>(V);
-  e = cudaGetLastError();
+  cudaError_t e = rb == 1 ? vb::launch<1>(V, p.g.chains(), stream)
+                : rb == 2 ? vb::launch<2>(V, p.g.chains(), stream)
+                          : vb::launch<4>(V, p.g.chains(), stream);
   if (e != cudaSuccess) return e;
 
   kb::Params K;
@@ -724,8 +839,6 @@ cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
   const void* src[7] = {p.r, p.w, p.k, p.a, p.b, p.v, p.dy};
   for (int t = 0; t < 7; ++t)
     if (!tma::encode_bhtn(&K.maps[t], src[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const size_t ksmem = sizeof(kb::KGroup) + 1024;
   e = cudaFuncSetAttribute(kb::keyside_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)ksmem);

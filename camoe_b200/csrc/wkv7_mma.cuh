@@ -45,6 +45,17 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
                : "r"(smem_u32(p)));
 }
 
+__device__ __forceinline__ void stsm_x4(void* p, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1,%2,%3,%4};\n" ::"r"(smem_u32(p)),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+__device__ __forceinline__ void stsm_x4_t(void* p, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1,%2,%3,%4};\n" ::"r"(smem_u32(p)),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -182,6 +193,19 @@ __device__ __forceinline__ void store_a_lay(__nv_bfloat16* tile, Lay lay, int m0
   *reinterpret_cast<uint32_t*>(tile + lay(m0 + g + 8, k0 + 2 * q)) = a[1];
   *reinterpret_cast<uint32_t*>(tile + lay(m0 + g, k0 + 8 + 2 * q)) = a[2];
   *reinterpret_cast<uint32_t*>(tile + lay(m0 + g + 8, k0 + 8 + 2 * q)) = a[3];
+}
+
+// Inverses of lda_rm / lda_cm: store a bf16 A fragment (16 x 16 at rows m0,
+// cols k0) into a [m][k] tile, or transposed into a [k][m] tile (stmatrix).
+template <typename Lay>
+__device__ __forceinline__ void sta_rm(__nv_bfloat16* tile, Lay lay, int m0, int k0,
+                                       const uint32_t (&a)[4], int lane) {
+  stsm_x4(tile + lay(m0 + (lane & 7) + ((lane >> 3) & 1) * 8, k0 + (lane >> 4) * 8), a);
+}
+template <typename Lay>
+__device__ __forceinline__ void sta_cm(__nv_bfloat16* tile, Lay lay, int m0, int k0,
+                                       const uint32_t (&a)[4], int lane) {
+  stsm_x4_t(tile + lay(k0 + (lane & 7) + (lane >> 4) * 8, m0 + ((lane >> 3) & 1) * 8), a);
 }
 
 // acc (16 x 16 output at columns n0) += A (16 x 16*KS) B;

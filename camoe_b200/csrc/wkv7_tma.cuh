@@ -30,6 +30,12 @@ bool encode_bhtn(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64
 // Same for an fp32 array, without swizzle: a chunk lands as a plain [16][64] fp32 tile.
 bool encode_bhtn_f32(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H);
 
+// Map of a bf16 [B, T, H, 64] array with a {n_box, 1, 16, 1} box and no
+// swizzle (rows of n_box columns, row-major in shared memory), for stores of
+// a column range of one chunk.
+bool encode_bhtn_cols(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H,
+                      int n_box);
+
 __device__ __forceinline__ void load_tile(void* dst_smem, const CUtensorMap* map, int h,
                                           int t0, int b, uint64_t* bar) {
   const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem));
@@ -38,6 +44,18 @@ __device__ __forceinline__ void load_tile(void* dst_smem, const CUtensorMap* map
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(h), "r"(t0), "r"(b), "r"(mb)
+      : "memory");
+}
+
+// Store one chunk box from shared memory at columns n0.. of head h, steps
+// t0.., batch b (bulk-group completion; rows past T are not written).
+__device__ __forceinline__ void store_tile(const CUtensorMap* map, const void* src_smem, int n0,
+                                           int h, int t0, int b) {
+  const uint32_t src = static_cast<uint32_t>(__cvta_generic_to_shared(src_smem));
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];\n" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(n0), "r"(h), "r"(t0), "r"(b), "r"(src)
       : "memory");
 }
 

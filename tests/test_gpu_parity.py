@@ -40,6 +40,8 @@ SHAPES = {
     "extreme_decay": (1, 48, 1, 4, 0.0, 6.0),
     "slow_decay": (1, 256, 2, 1, 2.0, 0.5),
     "layer_b8_t1024": (8, 1024, 16, 0, 0.0, 1.0),
+    # 64 chains: the chunked backward splits each chain's state rows over two CTAs
+    "rows_split2_b4_t200": (4, 200, 16, 8, 0.0, 1.0),
 }
 
 
@@ -81,8 +83,10 @@ def test_matches_oracle(shape, dtype, algo):
 
 
 @pytest.mark.parametrize("dtype,algo", PATHS, ids=PATH_IDS)
-def test_external_sa_gradient(dtype, algo):
-    inp = make_inputs(2, 96, 3, 64, seed=21, with_dsa=True)
+@pytest.mark.parametrize("B,T,H", [(2, 96, 3), (4, 80, 16), (8, 67, 16)],
+                         ids=["rows_split4", "rows_split2", "rows_whole"])
+def test_external_sa_gradient(dtype, algo, B, T, H):
+    inp = make_inputs(B, T, H, 64, seed=21, with_dsa=True)
     compare(run_op(inp, dtype, algo, with_dsa=True), oracle_outputs(inp, dtype, True),
             tol_for(dtype), "dsa")
 
