@@ -64,7 +64,7 @@ struct alignas(1024) Slot {
   bf16 dy[L * kN];  // TMA 128-byte swizzled
   float dsa[L][kN];
   rec::KeyRec k;
-  uint4 S[RB][4][32];  // this CTA's rows of the state at the chunk start (even chunks >= 2)
+  bf16 S[16 * RB * kN];  // Swz64: this CTA's rows of the state at the chunk start (even chunks >= 2)
 };
 
 template <int RB>
@@ -393,10 +393,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
     uint32_t sLo[4][4], vA[4];
     if (lo >= 2) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint4 xv = slo.S[r][kk][lane];
-        sLo[kk][0] = xv.x; sLo[kk][1] = xv.y; sLo[kk][2] = xv.z; sLo[kk][3] = xv.w;
-      }
+      for (int kk = 0; kk < 4; ++kk) lda_rm(sLo[kk], slo.S, Swz64{}, il, 16 * kk, lane);
     } else {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) sLo[kk][0] = sLo[kk][1] = sLo[kk][2] = sLo[kk][3] = 0u;
@@ -483,13 +480,6 @@ cudaError_t launch(const Params& V, int64_t chains, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   value_bwd_kernel<RB><<<static_cast<unsigned>(chains * (4 / RB)), 32 * (3 * RB + 2), smem, stream>>>(V);
   return cudaGetLastError();
-}
-
-// Row blocks per CTA: split chains over as many CTAs as the SMs can hold at once.
-inline int rows_per_cta(int64_t chains, int sms) {
-  if (chains * 4 <= sms) return 1;
-  if (chains * 2 <= sms) return 2;
-  return 4;
 }
 
 }  // namespace vb
@@ -818,13 +808,13 @@ size_t work_bytes(int64_t chains, int64_t T) {
 cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int rb = vb::rows_per_cta(p.g.chains(), sms);
+  const int rb = rows_per_cta(p.g.chains(), sms);
   vb::Params V;
   V.a = p;
   V.work = work;
   if (!tma::encode_bhtn(&V.map_v, p.v, p.g.B, p.g.T, p.g.H) ||
       !tma::encode_bhtn(&V.map_dy, p.dy, p.g.B, p.g.T, p.g.H) ||
-      !tma::encode_bhtn_cols(&V.map_dv, p.dv, p.g.B, p.g.T, p.g.H, 16 * rb))
+      !tma::encode_bhtn_cols(&V.map_dv, p.dv, p.g.B, p.g.T, p.g.H, 16 * rb, false))
     return cudaErrorInvalidValue;
   if (p.dsa != nullptr && !tma::encode_bhtn_f32(&V.map_dsa, p.dsa, p.g.B, p.g.T, p.g.H))
     return cudaErrorInvalidValue;

@@ -362,134 +362,210 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
 
 namespace vf {
 
-constexpr int NS = 12;
-constexpr int kThreads = 160;  // 4 value warps + 1 producer warp
+// As in the backward (wkv7_chunked_bwd.cu), a chain's 64 state rows are split
+// over 4 / RB CTAs of RB row blocks.  Per row block an S warp carries the fp32
+// state through the sequence (SA and the update, the critical path) and
+// publishes the chunk's start state; a Y warp forms Y from it; a producer warp
+// streams each chunk's KeyRec and v tile and a store warp writes the staged
+// y, sa tiles (TMA tile stores) and the even-chunk checkpoints (bulk copies).
+constexpr int NS = 8;  // input slots (power of two)
+constexpr int NX = 4;  // output stages (power of two)
 
 struct alignas(1024) Slot {
   bf16 v[L * kN];  // v tile as landed by TMA (1 KiB aligned)
   rec::KeyRec k;
 };
 
+template <int RB>
+struct alignas(1024) Stage {
+  float sa[L][16 * RB];   // [t][i] of this CTA's rows (TMA store)
+  bf16 y[L][16 * RB];     // [t][i] (TMA store)
+  bf16 S[16 * RB * kN];   // Swz64 rows: the chunk's start state
+};
+
+template <int RB>
 struct Smem {
   Slot slot[NS];
-  uint64_t full[NS], empty[NS];
+  Stage<RB> st[NX];
+  uint64_t full[NS], empty[NS], sfull[NX], done[NX], sempty[NX];
 };
 
 struct Params {
-  CUtensorMap map_v;
+  CUtensorMap map_v, map_y, map_sa;
   FwdArgs a;
 };
 
-__global__ void __launch_bounds__(kThreads, 1) value_fwd_kernel(const __grid_constant__ Params P) {
+template <int RB>
+__global__ void __launch_bounds__(32 * (2 * RB + 2), 1) value_fwd_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
+  Smem<RB>& sm = *reinterpret_cast<Smem<RB>*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
+  constexpr int NRG = 4 / RB;  // CTAs per chain
   const FwdArgs& p = P.a;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t ch = blockIdx.x;
-  const int64_t nchunk = p.g.nchunk, T = p.g.T, ts = p.g.tstride();
-  const int64_t cbase = p.g.base(ch);
+  const int64_t ch = blockIdx.x / NRG;
+  const int row0 = 16 * RB * static_cast<int>(blockIdx.x % NRG);
+  const int nchunk = static_cast<int>(p.g.nchunk);
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 4);
+      mbar_init(&sm.empty[s], 2 * RB);
+    }
+    for (int x = 0; x < NX; ++x) {
+      mbar_init(&sm.sfull[x], RB);
+      mbar_init(&sm.done[x], 2 * RB);
+      mbar_init(&sm.sempty[x], 1);
     }
     mbar_fence_init();
   }
   __syncthreads();
 
-  if (warp == 4) {
+  const int hh = static_cast<int>(p.g.h0 + ch % p.g.hc), bb = static_cast<int>(ch / p.g.hc);
+  if (warp == 2 * RB) {
     // ------------------------------ producer ------------------------------
-    if (lane == 0) {
-      const int hh = static_cast<int>(p.g.h0 + ch % p.g.hc), bb = static_cast<int>(ch / p.g.hc);
-      int64_t c = 0;
-      for (; c < nchunk; ++c) {
-        const int s = static_cast<int>(c % NS);
-        if (c >= NS && !mbar_wait(&sm.empty[s], static_cast<uint32_t>((c / NS - 1) & 1))) break;
-        mbar_arrive_expect_tx(&sm.full[s], sizeof(rec::KeyRec) + tma::kTileBytes);
-        bulk_g2s(&sm.slot[s].k, rec::keyrec(p.ckpt, ch, nchunk, c), sizeof(rec::KeyRec), &sm.full[s]);
-        tma::load_tile(sm.slot[s].v, &P.map_v, hh, static_cast<int>(c * L), bb, &sm.full[s]);
+    if (lane != 0) return;
+    int c = 0;
+    for (; c < nchunk; ++c) {
+      const int s = c & (NS - 1);
+      if (c >= NS && !mbar_wait(&sm.empty[s], static_cast<uint32_t>(((c - NS) / NS) & 1))) break;
+      mbar_arrive_expect_tx(&sm.full[s], sizeof(rec::KeyRec) + tma::kTileBytes);
+      bulk_g2s(&sm.slot[s].k, rec::keyrec(p.ckpt, ch, nchunk, c), sizeof(rec::KeyRec), &sm.full[s]);
+      tma::load_tile(sm.slot[s].v, &P.map_v, hh, c * L, bb, &sm.full[s]);
+    }
+    if (c < nchunk)  // stopped on a timeout: let the copies in flight land
+      for (int cc = c > NS ? c - NS : 0; cc < c; ++cc)
+        mbar_wait(&sm.full[cc & (NS - 1)], static_cast<uint32_t>((cc / NS) & 1));
+    return;
+  }
+
+  if (warp == 2 * RB + 1) {
+    // ------------------------------ store warp ------------------------------
+    if (lane != 0) return;
+    const int64_t chains = p.g.chains();
+    for (int c = 0; c < nchunk; ++c) {
+      const int x = c & (NX - 1);
+      if (!mbar_wait(&sm.done[x], static_cast<uint32_t>((c / NX) & 1))) break;
+      const Stage<RB>& st = sm.st[x];
+      tma::store_tile(&P.map_sa, &st.sa[0][0], row0, hh, c * L, bb);
+      tma::store_tile(&P.map_y, &st.y[0][0], row0, hh, c * L, bb);
+      if (c >= 2 && (c & 1) == 0)
+        bulk_s2g(rec::state_ptr(p.ckpt, chains, ch, nchunk, c) + row0 * 128, st.S, 2048 * RB);
+      bulk_commit();
+      bulk_wait_read();
+      mbar_arrive(&sm.sempty[x]);
+    }
+    bulk_wait_all();
+    return;
+  }
+
+  const int role = warp / RB, r = warp % RB;
+  const int il = 16 * r, i0 = row0 + il;
+  const int g = lane >> 2, q = lane & 3;
+  if (role == 0) {
+    // ------------------------------ S warp: the state recurrence ------------------------------
+    float S[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
+    for (int c = 0; c < nchunk; ++c) {
+      const int s = c & (NS - 1), x = c & (NX - 1);
+      if (!mbar_wait(&sm.full[s], static_cast<uint32_t>((c / NS) & 1))) return;
+      if (c >= NX && !mbar_wait(&sm.sempty[x], static_cast<uint32_t>(((c - NX) / NX) & 1))) return;
+      const rec::KeyRec& kr = sm.slot[s].k;
+      Stage<RB>& st = sm.st[x];
+      uint32_t sA[4][4], vA[4], b[4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        acc_to_a(sA[kk], S[2 * kk], S[2 * kk + 1]);
+        sta_rm(st.S, Swz64{}, il, 16 * kk, sA[kk], lane);
       }
-      if (c < nchunk)  // stopped on a timeout: let the copies in flight land
-        for (int64_t cc = c > NS ? c - NS : 0; cc < c; ++cc)
-          mbar_wait(&sm.full[cc % NS], static_cast<uint32_t>((cc / NS) & 1));
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.sfull[x]);
+      lda_cm(vA, sm.slot[s].v, Swz64{}, i0, 0, lane);
+      float sa[2][4] = {};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
+        mma16816(sa[0], sA[kk], b[0], b[1]);
+        mma16816(sa[1], sA[kk], b[2], b[3]);
+      }
+      ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
+      mma16816(sa[0], vA, b[0], b[1]);
+      mma16816(sa[1], vA, b[2], b[3]);
+      uint32_t saA[4];
+      acc_to_a(saA, sa[0], sa[1]);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        ldb_kn(b, kr.Bb, Swz64{}, 16 * m, 0, lane);
+        mma16816(S[2 * m], saA, b[0], b[1]);
+        mma16816(S[2 * m + 1], saA, b[2], b[3]);
+        ldb_kn(b, kr.Kb, Swz64{}, 16 * m, 0, lane);
+        mma16816(S[2 * m], vA, b[0], b[1]);
+        mma16816(S[2 * m + 1], vA, b[2], b[3]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
+        S[nt][0] *= l.x; S[nt][1] *= l.y; S[nt][2] *= l.x; S[nt][3] *= l.y;
+      }
+      // sa (rows i, cols t) -> stage [t][i]
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          st.sa[8 * nt + 2 * q + (e & 1)][il + g + (e >= 2 ? 8 : 0)] = sa[nt][e];
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.done[x]);
+        mbar_arrive(&sm.empty[s]);
+      }
     }
     return;
   }
 
-  // ------------------------------ value warps ------------------------------
-  const int wq = warp, g = lane >> 2, q = lane & 3, i0 = 16 * wq;
-  const int64_t chains = p.g.chains();
-  float S[8][4];
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
-  bf16* yp = static_cast<bf16*>(p.y);
-  for (int64_t c = 0; c < nchunk; ++c) {
-    const int s = static_cast<int>(c % NS);
-    if (!mbar_wait(&sm.full[s], static_cast<uint32_t>((c / NS) & 1))) break;
+  // ------------------------------ Y warp ------------------------------
+  for (int c = 0; c < nchunk; ++c) {
+    const int s = c & (NS - 1), x = c & (NX - 1);
+    if (!mbar_wait(&sm.full[s], static_cast<uint32_t>((c / NS) & 1))) return;
+    if (!mbar_wait(&sm.sfull[x], static_cast<uint32_t>((c / NX) & 1))) return;
     const rec::KeyRec& kr = sm.slot[s].k;
-
-    uint32_t sA[4][4], vA[4], b[4];
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) acc_to_a(sA[kk], S[2 * kk], S[2 * kk + 1]);
-    if ((c & 1) == 0 && c >= 2) {
-      uint4* dst = reinterpret_cast<uint4*>(rec::state_ptr(p.ckpt, chains, ch, nchunk, c));
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        dst[(wq * 4 + kk) * 32 + lane] = make_uint4(sA[kk][0], sA[kk][1], sA[kk][2], sA[kk][3]);
-    }
-    lda_cm(vA, sm.slot[s].v, Swz64{}, i0, 0, lane);
-    float sa[2][4] = {}, yv[2][4] = {};
+    Stage<RB>& st = sm.st[x];
+    uint32_t sA[4], vA[4], b[4];
+    float yv[2][4] = {};
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
-      mma16816(sa[0], sA[kk], b[0], b[1]);
-      mma16816(sa[1], sA[kk], b[2], b[3]);
+      lda_rm(sA, st.S, Swz64{}, il, 16 * kk, lane);
       ldb_nk(b, kr.Qy, Swz64{}, 0, 16 * kk, lane);
-      mma16816(yv[0], sA[kk], b[0], b[1]);
-      mma16816(yv[1], sA[kk], b[2], b[3]);
+      mma16816(yv[0], sA, b[0], b[1]);
+      mma16816(yv[1], sA, b[2], b[3]);
     }
-    ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
-    mma16816(sa[0], vA, b[0], b[1]);
-    mma16816(sa[1], vA, b[2], b[3]);
+    lda_cm(vA, sm.slot[s].v, Swz64{}, i0, 0, lane);
     ldb_nk(b, kr.P, Swz16{}, 0, 0, lane);
     mma16816(yv[0], vA, b[0], b[1]);
     mma16816(yv[1], vA, b[2], b[3]);
-
-    uint32_t saA[4];
-    acc_to_a(saA, sa[0], sa[1]);
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      ldb_kn(b, kr.Bb, Swz64{}, 16 * m, 0, lane);
-      mma16816(S[2 * m], saA, b[0], b[1]);
-      mma16816(S[2 * m + 1], saA, b[2], b[3]);
-      ldb_kn(b, kr.Kb, Swz64{}, 16 * m, 0, lane);
-      mma16816(S[2 * m], vA, b[0], b[1]);
-      mma16816(S[2 * m + 1], vA, b[2], b[3]);
-    }
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
-      S[nt][0] *= l.x; S[nt][1] *= l.y; S[nt][2] *= l.x; S[nt][3] *= l.y;
-    }
+    uint32_t yA[4];
+    acc_to_a(yA, yv[0], yv[1]);
+    sta_cm(&st.y[0][0], Padded{16 * RB}, il, 0, yA, lane);
+    fence_proxy_async();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[s]);
-
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = i0 + g + (e >= 2 ? 8 : 0);
-        const int64_t t = c * L + 8 * nt + 2 * q + (e & 1);
-        if (t < T) {
-          const int64_t o = cbase + t * ts + i;
-          p.sa[o] = sa[nt][e];
-          yp[o] = __float2bfloat16_rn(yv[nt][e]);
-        }
-      }
+    if (lane == 0) {
+      mbar_arrive(&sm.done[x]);
+      mbar_arrive(&sm.empty[s]);
+    }
   }
+}
+
+template <int RB>
+cudaError_t launch(const Params& V, int64_t chains, cudaStream_t stream) {
+  const size_t smem = sizeof(Smem<RB>) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(value_fwd_kernel<RB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  value_fwd_kernel<RB><<<static_cast<unsigned>(chains * (4 / RB)), 32 * (2 * RB + 2), smem, stream>>>(V);
+  return cudaGetLastError();
 }
 
 }  // namespace vf
@@ -523,12 +599,15 @@ cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
   const void* ksrc[5] = {p.r, p.w, p.k, p.a, p.b};
   for (int t = 0; t < 5; ++t)
     if (!tma::encode_bhtn(&K.maps[t], ksrc[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
-  vf::Params V;
-  V.a = p;
-  if (!tma::encode_bhtn(&V.map_v, p.v, p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
-
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int rb = rows_per_cta(p.g.chains(), sms);
+  vf::Params V;
+  V.a = p;
+  if (!tma::encode_bhtn(&V.map_v, p.v, p.g.B, p.g.T, p.g.H) ||
+      !tma::encode_bhtn_cols(&V.map_y, p.y, p.g.B, p.g.T, p.g.H, 16 * rb, false) ||
+      !tma::encode_bhtn_cols(&V.map_sa, p.sa, p.g.B, p.g.T, p.g.H, 16 * rb, true))
+    return cudaErrorInvalidValue;
   const size_t ksmem = ka::kGroups * sizeof(ka::Group) + 1024;
   cudaError_t e = cudaFuncSetAttribute(ka::keyside_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ksmem);
@@ -540,12 +619,9 @@ cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  const size_t vsmem = sizeof(vf::Smem) + 1024;
-  e = cudaFuncSetAttribute(vf::value_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)vsmem);
-  if (e != cudaSuccess) return e;
-  vf::value_fwd_kernel<<<(unsigned)p.g.chains(), vf::kThreads, vsmem, stream>>>(V);
-  return cudaGetLastError();
+  return rb == 1 ? vf::launch<1>(V, p.g.chains(), stream)
+       : rb == 2 ? vf::launch<2>(V, p.g.chains(), stream)
+                 : vf::launch<4>(V, p.g.chains(), stream);
 }
 
 }  // namespace chunked

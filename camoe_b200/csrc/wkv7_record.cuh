@@ -6,7 +6,8 @@
 // `chains` chains of `nchunk` 16-step chunks:
 //   [chains][nchunk] KeyRec      key-side matrices of every chunk
 //   [chains][nstate] state       bf16 64x64 state at the start of chunks
-//                                2, 4, 6, ... (mma A-fragment order)
+//                                2, 4, 6, ... (rows of 128 bytes, 16-byte
+//                                pieces swizzled by row & 7)
 // nstate = (nchunk - 1) / 2; the state at the start of odd chunks is
 // recomputed from the preceding even one, chunk 0 starts from zero.  Per
 // chunk this is 9472 + 4096 bytes, below the 16 KiB per chunk of the
@@ -68,4 +69,13 @@ __device__ __forceinline__ XRec* xrec(void* work, int64_t ch, int64_t nchunk, in
 }
 
 }  // namespace rec
+
+// The sequential value kernels split a chain's 64 state rows (independent in
+// the recurrence) over 4 / RB CTAs of RB 16-row blocks: as many CTAs as the
+// SMs hold at once, at most 4 per chain.
+inline int rows_per_cta(int64_t chains, int sms) {
+  if (chains * 4 <= sms) return 1;
+  if (chains * 2 <= sms) return 2;
+  return 4;
+}
 }  // namespace camoe

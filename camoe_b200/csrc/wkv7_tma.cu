@@ -61,20 +61,21 @@ bool encode_bhtn_f32(CUtensorMap* map, const void* base, int64_t B, int64_t T, i
 }
 
 bool encode_bhtn_cols(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H,
-                      int n_box) {
+                      int n_box, bool f32) {
   const EncodeFn fn = encode_fn();
   if (fn == nullptr || B <= 0 || T <= 0 || H <= 0 || n_box <= 0 || n_box > 64 || n_box % 8 != 0)
     return false;
+  const cuuint64_t row = f32 ? 256 : kRowBytes;
   const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(T),
                               static_cast<cuuint64_t>(B)};
-  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(kRowBytes),
-                                 static_cast<cuuint64_t>(H) * kRowBytes,
-                                 static_cast<cuuint64_t>(T) * H * kRowBytes};
+  const cuuint64_t strides[3] = {row, static_cast<cuuint64_t>(H) * row,
+                                 static_cast<cuuint64_t>(T) * H * row};
   const cuuint32_t box[4] = {static_cast<cuuint32_t>(n_box), 1, 16, 1};
   const cuuint32_t estride[4] = {1, 1, 1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
-            box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+            const_cast<void*>(base), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace tma

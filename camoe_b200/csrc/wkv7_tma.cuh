@@ -30,11 +30,11 @@ bool encode_bhtn(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64
 // Same for an fp32 array, without swizzle: a chunk lands as a plain [16][64] fp32 tile.
 bool encode_bhtn_f32(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H);
 
-// Map of a bf16 [B, T, H, 64] array with a {n_box, 1, 16, 1} box and no
-// swizzle (rows of n_box columns, row-major in shared memory), for stores of
-// a column range of one chunk.
+// Map of a bf16 (or, with f32, fp32) [B, T, H, 64] array with a
+// {n_box, 1, 16, 1} box and no swizzle (rows of n_box columns, row-major in
+// shared memory), for stores of a column range of one chunk.
 bool encode_bhtn_cols(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H,
-                      int n_box);
+                      int n_box, bool f32);
 
 __device__ __forceinline__ void load_tile(void* dst_smem, const CUtensorMap* map, int h,
                                           int t0, int b, uint64_t* bar) {
