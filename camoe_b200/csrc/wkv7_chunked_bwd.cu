@@ -11,16 +11,16 @@
 //     dQ = strict(dSA V^T),  dP = lower(dY V^T),  dll = colsum(G o S')
 // (dll is d(lam) * lam: lam scales the chunk's end state S').
 //
-// value_bwd_kernel (one CTA per chain, chunks in reverse): 4 value warps carry
-// G and run the recurrence, writing dv and, per chunk, a rec::XRec (bf16 S,
-// G'', SA^T, dSA^T and the column sums for dll) to the workspace; a producer
-// warp streams each chunk's KeyRec, v, dy, dSA_ext tiles and (even chunks) the
-// checkpointed state.  Chunks are taken in (even, odd) pairs: the state at the
-// start of the odd chunk is recomputed from the even chunk's checkpoint.
+// value_bwd_kernel (chunks in reverse, one to four CTAs per chain): carries G
+// through the recurrence, writing dv and, per chunk, a rec::XRec (bf16 S, G'',
+// SA^T, dSA^T) to the workspace; the state at the start of every chunk comes
+// from the checkpoint (even chunks) or is recomputed from the preceding even
+// chunk (odd chunks).
 //
 // keyside_bwd_kernel (chunk-parallel, every SM): forms the row sums above from
-// the chunk's XRec and its v, dy tiles, recomputes the chunk's key side from
-// r, w, k, a, b and turns both into dr, dw, dk, da, db:
+// the chunk's XRec, its v, dy tiles and the next chunk's start state (for
+// dll), recomputes the chunk's key side from r, w, k, a, b and turns both into
+// dr, dw, dk, da, db:
 //     dW += Cm^T dQy,  dQ += Cm^T dP,  dCm = lower(dQy W^T + dP Q^T)
 //     dTi = dW At^T + dQ Bm^T,  dA = strict(Ti^T dTi Ti^T),  dBm = strict(Ti^T dQ)
 //     dAt = Ti^T dW + dA Bb + dBm Kb,   dRt = dQy + dCm Bb + dP Kb
@@ -51,12 +51,21 @@ namespace vb {
 
 // The state rows are independent in the recurrence (the transition acts on the
 // key dimension), so a chain's 64 rows are split over 4 / RB CTAs of RB row
-// blocks (16 rows) each.  Per row block a CTA runs a G warp (the gradient
-// recurrence), a state warp (start states, SA, dll) and a dV warp; a producer
-// warp streams the inputs and a store warp writes the staged outputs (the
-// chunk's XRec rows and the dv tile) with bulk copies.
-constexpr int NS = 4;  // input slots (power of two)
-constexpr int NX = 4;  // output stages (power of two)
+// blocks (16 rows) each.  Per row block:
+//   G warp      the gradient recurrence G -> G'' -> dSA -> dS (the critical
+//               path).  It loads all of a chunk's operand fragments before
+//               its mma chains and publishes G'' and dSA in a small ring only
+//               after them, so no shared-memory store sits in front of its
+//               loads; no fences, no output stores;
+//   dV warp     reads them, forms dV and stages dv and the G'', dSA^T rows of
+//               the chunk's XRec;
+//   state warp  start states (checkpointed or recomputed), SA; stages the S
+//               and SA^T rows of the XRec.
+// A producer warp streams the inputs and a store warp writes the staged rows
+// and the dv tile with bulk copies, KEEP groups in flight.
+constexpr int NS = 4;    // input slots (power of two)
+constexpr int NX = 4;    // output stages (power of two)
+constexpr int KEEP = 2;  // store groups still reading shared memory, < NX
 
 template <int RB>
 struct alignas(1024) Slot {
@@ -68,20 +77,27 @@ struct alignas(1024) Slot {
 };
 
 template <int RB>
+struct alignas(128) GPub {  // G warp -> dV warp, one chunk
+  bf16 G[16 * RB * kN];     // Swz64
+  bf16 dSAT[16 * RB * L];   // Swz16
+};
+
+template <int RB>
 struct alignas(1024) Stage {
-  bf16 dv[L][16 * RB];   // dV tile [t][i] of this CTA's rows (TMA store)
-  bf16 S[16 * RB * kN];  // Swz64, this CTA's rows of the XRec tiles
-  bf16 G[16 * RB * kN];  // Swz64
+  bf16 dv[L][16 * RB];     // dV tile [t][i] of this CTA's rows (TMA store)
+  bf16 S[16 * RB * kN];    // Swz64, this CTA's rows of the XRec tiles
+  bf16 G[16 * RB * kN];    // Swz64
   bf16 SAT[16 * RB * L];   // Swz16
   bf16 dSAT[16 * RB * L];  // Swz16
-  float dll[RB][kN];
 };
 
 template <int RB>
 struct Smem {
+  static constexpr int NG = RB == 4 ? 2 : 4;  // G'' / dSA ring (power of two)
   Slot<RB> slot[NS];
   Stage<RB> st[NX];
-  uint64_t full[NS], empty[NS], gfull[NX], sfull[NX], sempty[NX];
+  GPub<RB> gp[NG];
+  uint64_t full[NS], empty[NS], gfull[NG], gfree[NG], sfull[NX], sempty[NX];
 };
 
 struct Params {
@@ -117,72 +133,32 @@ __device__ __forceinline__ uint32_t par(int idx, int n) { return static_cast<uin
 // SA^T fragments (rows = one row block, cols = t) of a chunk: S W^T + V Q^T.
 __device__ __forceinline__ void sa_of(float (&sat)[2][4], const rec::KeyRec& kr,
                                       const uint32_t (&sA)[4][4], const uint32_t (&vA)[4], int lane) {
-  uint32_t b[4];
+  uint32_t bW[4][4], bQ[4];
 #pragma unroll
-  for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) sat[nt][e] = 0.f;
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
-    mma16816(sat[0], sA[kk], b[0], b[1]);
-    mma16816(sat[1], sA[kk], b[2], b[3]);
-  }
-  ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
-  mma16816(sat[0], vA, b[0], b[1]);
-  mma16816(sat[1], vA, b[2], b[3]);
+  for (int kk = 0; kk < 4; ++kk) ldb_nk(bW[kk], kr.W, Swz64{}, 0, 16 * kk, lane);
+  ldb_nk(bQ, kr.Q, Swz16{}, 0, 0, lane);
+  mma_k64_k16(sat, sA, vA, bW, bQ);
 }
 
-// State warp, one chunk: its S and SA^T rows -> stage; the stage's dll row =
-// column sums over its rows of G'' o S' (S' = sNext, the start state of the
-// following chunk, zero for the last chunk), i.e. lam * dL/dlam.
+// State warp, one chunk (processing index pi): stage its S and SA^T rows.
 template <int RB>
-__device__ __forceinline__ void s_chunk(Stage<RB>& st, const uint32_t (&sA)[4][4],
-                                        const float (&sat)[2][4], const uint32_t (&sNext)[4][4],
-                                        int r, int lane) {
-  const int g = lane >> 2, q = lane & 3, il = 16 * r;
+__device__ __forceinline__ bool s_chunk(Smem<RB>& sm, int pi, int s, const uint32_t (&sA)[4][4],
+                                        const float (&sat)[2][4], int il, int lane) {
+  const int x = pi & (NX - 1);
+  if (pi >= NX && !mbar_wait(&sm.sempty[x], par(pi - NX, NX))) return false;
+  Stage<RB>& st = sm.st[x];
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) sta_rm(st.S, Swz64{}, il, 16 * kk, sA[kk], lane);
   uint32_t saA[4];
   acc_to_a(saA, sat[0], sat[1]);
   sta_rm(st.SAT, Swz16{}, il, 0, saA, lane);
-  // per-thread partial sums over rows g, g+8 of columns 16kk + 8h + 2q + x, as v[4kk + 2h + x]
-  float v[16];
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    uint32_t gr[4];
-    lda_rm(gr, st.G, Swz64{}, il, 16 * kk, lane);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {  // regs (2h, 2h+1): rows g, g+8 of columns 16kk + 8h + 2q
-      const float2 g0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr[2 * h]));
-      const float2 g1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr[2 * h + 1]));
-      const float2 s0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sNext[kk][2 * h]));
-      const float2 s1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sNext[kk][2 * h + 1]));
-      v[4 * kk + 2 * h] = g0.x * s0.x + g1.x * s1.x;
-      v[4 * kk + 2 * h + 1] = g0.y * s0.y + g1.y * s1.y;
-    }
+  fence_proxy_async();
+  __syncwarp();
+  if (lane == 0) {
+    mbar_arrive(&sm.sfull[x]);
+    mbar_arrive(&sm.empty[s]);
   }
-  // v[2n + x] is column 8n + 2q + x; reduce-scatter over the 8 row lanes
-  // (lane bits 4, 3, 2): lane g keeps v[2g], v[2g+1]
-#pragma unroll
-  for (int m = 0; m < 8; ++m) {
-    const bool up = lane & 16;
-    const float send = up ? v[m] : v[m + 8], keep = up ? v[m + 8] : v[m];
-    v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const bool up = lane & 8;
-    const float send = up ? v[m] : v[m + 4], keep = up ? v[m + 4] : v[m];
-    v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-#pragma unroll
-  for (int m = 0; m < 2; ++m) {
-    const bool up = lane & 4;
-    const float send = up ? v[m] : v[m + 2], keep = up ? v[m + 2] : v[m];
-    v[m] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-  *reinterpret_cast<float2*>(&st.dll[r][8 * g + 2 * q]) = make_float2(v[0], v[1]);
+  return true;
 }
 
 template <int RB>
@@ -190,8 +166,9 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Smem<RB>& sm = *reinterpret_cast<Smem<RB>*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
   constexpr int NRG = 4 / RB;  // CTAs per chain
+  constexpr int NG = Smem<RB>::NG;
   const BwdArgs& p = P.a;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = role_warp<RB>(tid >> 5);
   const int64_t ch = blockIdx.x / NRG;
   const int row0 = 16 * RB * static_cast<int>(blockIdx.x % NRG);  // first state row of this CTA
   const int nchunk = static_cast<int>(p.g.nchunk);
@@ -203,8 +180,11 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 3 * RB);
     }
-    for (int x = 0; x < NX; ++x) {
+    for (int x = 0; x < NG; ++x) {
       mbar_init(&sm.gfull[x], RB);
+      mbar_init(&sm.gfree[x], RB);
+    }
+    for (int x = 0; x < NX; ++x) {
       mbar_init(&sm.sfull[x], 2 * RB);
       mbar_init(&sm.sempty[x], 1);
     }
@@ -259,11 +239,10 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
       bulk_s2g(xr->G + row0 * kN, st.G, 2048 * RB);
       bulk_s2g(xr->SAT + row0 * L, st.SAT, 512 * RB);
       bulk_s2g(xr->dSAT + row0 * L, st.dSAT, 512 * RB);
-      bulk_s2g(&xr->dll[row0 / 16][0], &st.dll[0][0], 256 * RB);
       tma::store_tile(&P.map_dv, &st.dv[0][0], row0, hh, c * L, bb);
       bulk_commit();
-      bulk_wait_read();
-      mbar_arrive(&sm.sempty[x]);
+      bulk_wait_read_n<KEEP>();
+      if (pi >= KEEP) mbar_arrive(&sm.sempty[(pi - KEEP) & (NX - 1)]);
     }
     bulk_wait_all();
     return;
@@ -279,93 +258,137 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
     for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) G[nt][e] = 0.f;
+    if (nchunk > 0) {
+      const int li0 = load_idx(nchunk, nchunk - 1);
+      if (!mbar_wait(&sm.full[li0 & (NS - 1)], par(li0, NS))) return;
+    }
     for (int pi = 0; pi < nchunk; ++pi) {
       const int c = nchunk - 1 - pi, li = load_idx(nchunk, c);
-      const int s = li & (NS - 1), x = pi & (NX - 1);
-      if (!mbar_wait(&sm.full[s], par(li, NS))) return;
-      if (pi >= NX && !mbar_wait(&sm.sempty[x], par(pi - NX, NX))) return;
+      const int s = li & (NS - 1), xg = pi & (NG - 1);
+      const int lin = c >= 1 ? load_idx(nchunk, c - 1) : 0, sn = lin & (NS - 1);
+      // barrier tests for the end of this chunk and the next one, answered while the chunk computes
+      const bool next_ready = c == 0 || mbar_test(&sm.full[sn], par(lin, NS));
+      const bool pub_ready = pi < NG || mbar_test(&sm.gfree[xg], par(pi - NG, NG));
       const Slot<RB>& sl = sm.slot[s];
-      Stage<RB>& st = sm.st[x];
       const rec::KeyRec& kr = sl.k;
-      uint32_t b[4], dyA[4];
+      // all operand fragments of the chunk first
+      uint32_t bB[4][4], bQy[4][4], bW[4][4], dyA[4];
+      float2 lam[8];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        ldb_nk(bB[kk], kr.Bb, Swz64{}, 0, 16 * kk, lane);
+        ldb_kn(bQy[kk], kr.Qy, Swz64{}, 16 * kk, 0, lane);
+        ldb_kn(bW[kk], kr.W, Swz64{}, 16 * kk, 0, lane);
+      }
+      lda_cm(dyA, sl.dy, Swz64{}, i0, 0, lane);
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) lam[nt] = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
+      float dsat[2][4], dso[2][4];  // dSA = dSA_ext + Bb G''^T (rows i, cols t), odd k-steps apart
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          dsat[nt][e] = has_dsa ? sl.dsa[8 * nt + 2 * q + (e & 1)][i0 + g + (e >= 2 ? 8 : 0)] : 0.f;
+          dso[nt][e] = 0.f;
+        }
       // G'' = G diag(lam)
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-        const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
-        G[nt][0] *= l.x; G[nt][1] *= l.y; G[nt][2] *= l.x; G[nt][3] *= l.y;
+        G[nt][0] *= lam[nt].x; G[nt][1] *= lam[nt].y; G[nt][2] *= lam[nt].x; G[nt][3] *= lam[nt].y;
       }
       uint32_t gA[4][4];
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) acc_to_a(gA[kk], G[2 * kk], G[2 * kk + 1]);
-      // dSA = dSA_ext + Bb G''^T (rows i, cols t)
-      float dsat[2][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; kk += 2) {
+        mma16816(dsat[0], gA[kk], bB[kk][0], bB[kk][1]);
+        mma16816(dsat[1], gA[kk], bB[kk][2], bB[kk][3]);
+        mma16816(dso[0], gA[kk + 1], bB[kk + 1][0], bB[kk + 1][1]);
+        mma16816(dso[1], gA[kk + 1], bB[kk + 1][2], bB[kk + 1][3]);
+      }
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          dsat[nt][e] = has_dsa ? sl.dsa[8 * nt + 2 * q + (e & 1)][i0 + g + (e >= 2 ? 8 : 0)] : 0.f;
+        for (int e = 0; e < 4; ++e) dsat[nt][e] += dso[nt][e];
+      // dS = G'' + dY^T Qy + dSA^T W  -> G of the previous chunk
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        ldb_nk(b, kr.Bb, Swz64{}, 0, 16 * kk, lane);
-        mma16816(dsat[0], gA[kk], b[0], b[1]);
-        mma16816(dsat[1], gA[kk], b[2], b[3]);
+      for (int m = 0; m < 4; ++m) {
+        mma16816(G[2 * m], dyA, bQy[m][0], bQy[m][1]);
+        mma16816(G[2 * m + 1], dyA, bQy[m][2], bQy[m][3]);
       }
       uint32_t dsaA[4];
       acc_to_a(dsaA, dsat[0], dsat[1]);
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) sta_rm(st.G, Swz64{}, il, 16 * kk, gA[kk], lane);
-      sta_rm(st.dSAT, Swz16{}, il, 0, dsaA, lane);
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.gfull[x]);
-      // dS = G'' + dY^T Qy + dSA^T W  -> G of the previous chunk
-      lda_cm(dyA, sl.dy, Swz64{}, i0, 0, lane);
-#pragma unroll
       for (int m = 0; m < 4; ++m) {
-        ldb_kn(b, kr.Qy, Swz64{}, 16 * m, 0, lane);
-        mma16816(G[2 * m], dyA, b[0], b[1]);
-        mma16816(G[2 * m + 1], dyA, b[2], b[3]);
-        ldb_kn(b, kr.W, Swz64{}, 16 * m, 0, lane);
-        mma16816(G[2 * m], dsaA, b[0], b[1]);
-        mma16816(G[2 * m + 1], dsaA, b[2], b[3]);
+        mma16816(G[2 * m], dsaA, bW[m][0], bW[m][1]);
+        mma16816(G[2 * m + 1], dsaA, bW[m][2], bW[m][3]);
       }
+      // publish G'' and dSA
+      if (!pub_ready && !mbar_wait(&sm.gfree[xg], par(pi - NG, NG))) return;
+      GPub<RB>& gp = sm.gp[xg];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) sta_rm(gp.G, Swz64{}, il, 16 * kk, gA[kk], lane);
+      sta_rm(gp.dSAT, Swz16{}, il, 0, dsaA, lane);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.empty[s]);
+      if (lane == 0) {
+        mbar_arrive(&sm.gfull[xg]);
+        mbar_arrive(&sm.empty[s]);
+      }
+      if (!next_ready && !mbar_wait(&sm.full[sn], par(lin, NS))) return;
     }
     return;
   }
 
   if (role == 2) {
     // ------------------------------ dV warp ------------------------------
+    if (nchunk > 0) {
+      const int li0 = load_idx(nchunk, nchunk - 1);
+      if (!mbar_wait(&sm.full[li0 & (NS - 1)], par(li0, NS))) return;
+    }
     for (int pi = 0; pi < nchunk; ++pi) {
       const int c = nchunk - 1 - pi, li = load_idx(nchunk, c);
-      const int s = li & (NS - 1), x = pi & (NX - 1);
-      if (!mbar_wait(&sm.full[s], par(li, NS))) return;
-      if (!mbar_wait(&sm.gfull[x], par(pi, NX))) return;
+      const int s = li & (NS - 1), xg = pi & (NG - 1), x = pi & (NX - 1);
+      const int lin = c >= 1 ? load_idx(nchunk, c - 1) : 0, sn = lin & (NS - 1);
+      const bool next_ready = c == 0 || mbar_test(&sm.full[sn], par(lin, NS));
+      const bool st_ready = pi < NX || mbar_test(&sm.sempty[x], par(pi - NX, NX));
       const Slot<RB>& sl = sm.slot[s];
-      Stage<RB>& st = sm.st[x];
       const rec::KeyRec& kr = sl.k;
-      uint32_t b[4], dyA[4], dsaA[4], gA[4][4];
+      uint32_t bK[4][4], bP[4], bQ[4], dyA[4], dsaA[4], gA[4][4];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) lda_rm(gA[kk], st.G, Swz64{}, il, 16 * kk, lane);
-      lda_rm(dsaA, st.dSAT, Swz16{}, il, 0, lane);
+      for (int kk = 0; kk < 4; ++kk) ldb_nk(bK[kk], kr.Kb, Swz64{}, 0, 16 * kk, lane);
+      ldb_kn(bP, kr.P, Swz16{}, 0, 0, lane);
+      ldb_kn(bQ, kr.Q, Swz16{}, 0, 0, lane);
       lda_cm(dyA, sl.dy, Swz64{}, i0, 0, lane);
-      // dV^T = G'' Kb^T + dY^T P + dSA^T Q
-      float dvt[2][4] = {};
+      if (!mbar_wait(&sm.gfull[xg], par(pi, NG))) return;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        ldb_nk(b, kr.Kb, Swz64{}, 0, 16 * kk, lane);
-        mma16816(dvt[0], gA[kk], b[0], b[1]);
-        mma16816(dvt[1], gA[kk], b[2], b[3]);
+      for (int kk = 0; kk < 4; ++kk) lda_rm(gA[kk], sm.gp[xg].G, Swz64{}, il, 16 * kk, lane);
+      lda_rm(dsaA, sm.gp[xg].dSAT, Swz16{}, il, 0, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.gfree[xg]);
+      // dV^T = G'' Kb^T + dY^T P + dSA^T Q (two accumulator chains, summed)
+      float dvt[2][4] = {}, dvo[2][4] = {};
+      mma16816(dvt[0], dyA, bP[0], bP[1]);
+      mma16816(dvt[1], dyA, bP[2], bP[3]);
+      mma16816(dvo[0], dsaA, bQ[0], bQ[1]);
+      mma16816(dvo[1], dsaA, bQ[2], bQ[3]);
+#pragma unroll
+      for (int kk = 0; kk < 4; kk += 2) {
+        mma16816(dvt[0], gA[kk], bK[kk][0], bK[kk][1]);
+        mma16816(dvt[1], gA[kk], bK[kk][2], bK[kk][3]);
+        mma16816(dvo[0], gA[kk + 1], bK[kk + 1][0], bK[kk + 1][1]);
+        mma16816(dvo[1], gA[kk + 1], bK[kk + 1][2], bK[kk + 1][3]);
       }
-      ldb_kn(b, kr.P, Swz16{}, 0, 0, lane);
-      mma16816(dvt[0], dyA, b[0], b[1]);
-      mma16816(dvt[1], dyA, b[2], b[3]);
-      ldb_kn(b, kr.Q, Swz16{}, 0, 0, lane);
-      mma16816(dvt[0], dsaA, b[0], b[1]);
-      mma16816(dvt[1], dsaA, b[2], b[3]);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dvt[nt][e] += dvo[nt][e];
       uint32_t dvA[4];
       acc_to_a(dvA, dvt[0], dvt[1]);
+      if (!st_ready && !mbar_wait(&sm.sempty[x], par(pi - NX, NX))) return;
+      Stage<RB>& st = sm.st[x];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) sta_rm(st.G, Swz64{}, il, 16 * kk, gA[kk], lane);
+      sta_rm(st.dSAT, Swz16{}, il, 0, dsaA, lane);
       sta_cm(&st.dv[0][0], Padded{16 * RB}, il, 0, dvA, lane);
       fence_proxy_async();
       __syncwarp();
@@ -373,14 +396,12 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
         mbar_arrive(&sm.sfull[x]);
         mbar_arrive(&sm.empty[s]);
       }
+      if (!next_ready && !mbar_wait(&sm.full[sn], par(lin, NS))) return;
     }
     return;
   }
 
   // ------------------------------ state warp ------------------------------
-  uint32_t sNext[4][4];  // start state of the chunk after the one being processed
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) sNext[kk][0] = sNext[kk][1] = sNext[kk][2] = sNext[kk][3] = 0u;
   for (int gi = 0; gi < ngroups; ++gi) {
     int lo, hi, idx_lo;
     group_of(nchunk, gi, lo, hi, idx_lo);
@@ -442,33 +463,9 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
       lda_cm(vHi, shi.v, Swz64{}, i0, 0, lane);
       float satHi[2][4];
       sa_of(satHi, shi.k, sHi, vHi, lane);
-      const int pi = nchunk - 1 - hi, x = pi & (NX - 1);
-      if (!mbar_wait(&sm.gfull[x], par(pi, NX))) return;
-      s_chunk(sm.st[x], sHi, satHi, sNext, r, lane);
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&sm.sfull[x]);
-        mbar_arrive(&sm.empty[s_hi]);
-      }
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) sNext[kk][e] = sHi[kk][e];
+      if (!s_chunk(sm, nchunk - 1 - hi, s_hi, sHi, satHi, il, lane)) return;
     }
-    const int pi = nchunk - 1 - lo, x = pi & (NX - 1);
-    if (!mbar_wait(&sm.gfull[x], par(pi, NX))) return;
-    s_chunk(sm.st[x], sLo, satLo, sNext, r, lane);
-    fence_proxy_async();
-    __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&sm.sfull[x]);
-      mbar_arrive(&sm.empty[s_lo]);
-    }
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sNext[kk][e] = sLo[kk][e];
+    if (!s_chunk(sm, nchunk - 1 - lo, s_lo, sLo, satLo, il, lane)) return;
   }
 }
 
@@ -492,12 +489,20 @@ constexpr int kThreads = 128;  // one group of 4 warps per CTA
 struct alignas(1024) KGroup {
   bf16 raw[NR][7][L * kN];  // r, w, k, a, b, v, dy as landed by TMA (1 KiB aligned)
   rec::XRec x[NR];          // S and G are reused as scratch once the row sums are formed
-  Tile At, Rt, W, Bb, Kb;
-  Tile16 Bm, Cm, Dm, Ti, Q, P;
-  float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
-  float lam[kN], cum[L][kN], sig[L][kN], dll[kN];
-  bf16 dPb[L][LDS], dQ2b[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
-  float dTf[L][L + 1];
+  Tile At, Rt, Bb, Kb;
+  float lam[kN], cum[L][kN], sig[L][kN];
+  float dllp[4][kN], dll[kN];
+  bf16 dPb[L][LDS];
+  union {
+    bf16 Snext[64 * 64];  // first phase only: Swz64 start state of the next chunk
+    struct {              // later phases
+      Tile W;
+      Tile16 Bm, Cm, Dm, Ti, Q, P;
+      float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
+      bf16 dQ2b[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
+      float dTf[L][L + 1];
+    };
+  };
   uint64_t bar[NR];
 };
 // scratch inside the XRec: dcum, dcumx (fp32 16 x 64) in S; dQyb, dW2b, dwt in G
@@ -544,10 +549,12 @@ __device__ __forceinline__ void issue(KGroup& G, int rb, const Params& P, int64_
   const Geom& g = P.a.g;
   const int64_t ch = item / g.nchunk, c = item % g.nchunk;
   const int h = static_cast<int>(g.h0 + ch % g.hc), b = static_cast<int>(ch / g.hc);
-  mbar_arrive_expect_tx(&G.bar[rb], 7 * tma::kTileBytes + sizeof(rec::XRec));
+  const bool next = c + 1 < g.nchunk;
+  mbar_arrive_expect_tx(&G.bar[rb], 7 * tma::kTileBytes + sizeof(rec::XRec) + (next ? 8192 : 0));
 #pragma unroll
   for (int t = 0; t < 7; ++t) tma::load_tile(G.raw[rb][t], &P.maps[t], h, static_cast<int>(c * L), b, &G.bar[rb]);
   bulk_g2s(&G.x[rb], rec::xrec(P.work, ch, g.nchunk, c), sizeof(rec::XRec), &G.bar[rb]);
+  if (next) bulk_g2s(G.Snext, rec::xrec(P.work, ch, g.nchunk, c + 1)->S, 8192, &G.bar[rb]);
 }
 
 __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_constant__ Params P) {
@@ -591,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
 
     // ---- row sums over the 64 state rows (own columns), and the key side ----
     //   dW = dSA S, dQy = dY S, dBb = SA G'', dKb = V G'';  dP = lower(dY V^T) (warp 2),
-    //   dQ = strict(dSA V^T) (warp 1, kept in registers), dll (warp 3)
+    //   dQ = strict(dSA V^T) (warp 1, kept in registers), lam dll (16 rows per warp)
     float dW[2][4] = {}, dQy[2][4] = {}, dBp[2][4] = {}, dKp[2][4] = {}, dq[2][4] = {};
     mm16<true, true, 4>(dW, xr.dSAT, Swz16{}, xr.S, Swz64{}, j0, lane);
     mm16<false, true, 4>(dQy, raw_dy, Swz64{}, xr.S, Swz64{}, j0, lane);
@@ -618,17 +625,26 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
         }
       store_acc_bf16(&G.dPb[0][0], LDS, 0, 0, dp[0], lane);
       store_acc_bf16(&G.dPb[0][0], LDS, 0, 8, dp[1], lane);
-    } else if (gw == 3) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int jj = lane + 32 * e;
-        G.dll[jj] = xr.dll[0][jj] + xr.dll[1][jj] + xr.dll[2][jj] + xr.dll[3][jj];
+    }
+    {  // lam dll = colsum(G'' o S'), S' = start state of the next chunk (rows 16gw.., cols 2lane, 2lane+1)
+      float2 acc = make_float2(0.f, 0.f);
+      if (c + 1 < nchunk) {
+#pragma unroll 4
+        for (int i = 16 * gw; i < 16 * gw + 16; ++i) {
+          const int o = Swz64{}(i, 2 * lane);
+          const float2 gv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xr.G[o]));
+          const float2 sv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&G.Snext[o]));
+          acc.x += gv.x * sv.x;
+          acc.y += gv.y * sv.y;
+        }
       }
+      *reinterpret_cast<float2*>(&G.dllp[gw][2 * lane]) = acc;
     }
     ks::decays<true>(raw_r, G.raw[rb][1], raw_k, raw_a, raw_b, G.At, G.Rt, G.Kb, G.Bb, G.lam,
                      G.cum, G.sig, tid);
-    __syncthreads();  // XRec S and G free from here on
+    __syncthreads();  // XRec S and G and the next chunk's state free from here on
     ks::grams(G.At, G.Rt, G.Bb, G.Kb, G.Ga, G.Bm, G.Cm, G.Dm, gw, lane);
+    if (tid < kN) G.dll[tid] = G.dllp[0][tid] + G.dllp[1][tid] + G.dllp[2][tid] + G.dllp[3][tid];
     store_acc_bf16(&dQyb[0][0], LD, 0, j0, dQy[0], lane);
     store_acc_bf16(&dQyb[0][0], LD, 0, j0 + 8, dQy[1], lane);
     __syncthreads();

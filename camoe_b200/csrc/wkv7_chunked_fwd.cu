@@ -363,13 +363,22 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
 namespace vf {
 
 // As in the backward (wkv7_chunked_bwd.cu), a chain's 64 state rows are split
-// over 4 / RB CTAs of RB row blocks.  Per row block an S warp carries the fp32
-// state through the sequence (SA and the update, the critical path) and
-// publishes the chunk's start state; a Y warp forms Y from it; a producer warp
-// streams each chunk's KeyRec and v tile and a store warp writes the staged
-// y, sa tiles (TMA tile stores) and the even-chunk checkpoints (bulk copies).
-constexpr int NS = 8;  // input slots (power of two)
-constexpr int NX = 4;  // output stages (power of two)
+// over 4 / RB CTAs of RB row blocks.  Per row block:
+//   S warp   carries the fp32 state through the sequence (SA and the update:
+//            the critical path).  It loads all of a chunk's operand fragments
+//            before its mma chains and publishes the chunk's start state in a
+//            small ring only after them, so no shared-memory store sits in
+//            front of its loads; it issues no fence and no output store;
+//   Y warp   reads the published start state, forms Y and stages y and (even
+//            chunks) the checkpoint copy of the start state;
+//   A warp   the same for SA (recomputed with the S warp's operands and
+//            order) and sa.
+// A producer warp streams each chunk's KeyRec and v tile; a store warp writes
+// the staged tiles (TMA tile stores, bulk copies) with KEEP groups in flight.
+constexpr int NS = 8;    // input slots (power of two)
+constexpr int NP = 4;    // start-state ring (power of two)
+constexpr int NX = 4;    // output stages (power of two)
+constexpr int KEEP = 2;  // store groups still reading shared memory, < NX
 
 struct alignas(1024) Slot {
   bf16 v[L * kN];  // v tile as landed by TMA (1 KiB aligned)
@@ -377,17 +386,23 @@ struct alignas(1024) Slot {
 };
 
 template <int RB>
+struct alignas(128) Pub {
+  bf16 S[16 * RB * kN];  // Swz64 rows: a chunk's start state
+};
+
+template <int RB>
 struct alignas(1024) Stage {
-  float sa[L][16 * RB];   // [t][i] of this CTA's rows (TMA store)
-  bf16 y[L][16 * RB];     // [t][i] (TMA store)
-  bf16 S[16 * RB * kN];   // Swz64 rows: the chunk's start state
+  float sa[L][16 * RB];  // [t][i] of this CTA's rows (TMA store)
+  bf16 y[L][16 * RB];    // [t][i] (TMA store)
+  bf16 S[16 * RB * kN];  // Swz64 rows: checkpoint copy of the start state
 };
 
 template <int RB>
 struct Smem {
   Slot slot[NS];
   Stage<RB> st[NX];
-  uint64_t full[NS], empty[NS], sfull[NX], done[NX], sempty[NX];
+  Pub<RB> pub[NP];
+  uint64_t full[NS], empty[NS], pfull[NP], pfree[NP], done[NX], sempty[NX];
 };
 
 struct Params {
@@ -395,13 +410,15 @@ struct Params {
   FwdArgs a;
 };
 
+__device__ __forceinline__ uint32_t par(int idx, int n) { return static_cast<uint32_t>((idx / n) & 1); }
+
 template <int RB>
-__global__ void __launch_bounds__(32 * (2 * RB + 2), 1) value_fwd_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Smem<RB>& sm = *reinterpret_cast<Smem<RB>*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
   constexpr int NRG = 4 / RB;  // CTAs per chain
   const FwdArgs& p = P.a;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = role_warp<RB>(tid >> 5);
   const int64_t ch = blockIdx.x / NRG;
   const int row0 = 16 * RB * static_cast<int>(blockIdx.x % NRG);
   const int nchunk = static_cast<int>(p.g.nchunk);
@@ -409,10 +426,13 @@ __global__ void __launch_bounds__(32 * (2 * RB + 2), 1) value_fwd_kernel(const _
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 2 * RB);
+      mbar_init(&sm.empty[s], 3 * RB);
+    }
+    for (int x = 0; x < NP; ++x) {
+      mbar_init(&sm.pfull[x], RB);
+      mbar_init(&sm.pfree[x], 2 * RB);
     }
     for (int x = 0; x < NX; ++x) {
-      mbar_init(&sm.sfull[x], RB);
       mbar_init(&sm.done[x], 2 * RB);
       mbar_init(&sm.sempty[x], 1);
     }
@@ -421,38 +441,37 @@ __global__ void __launch_bounds__(32 * (2 * RB + 2), 1) value_fwd_kernel(const _
   __syncthreads();
 
   const int hh = static_cast<int>(p.g.h0 + ch % p.g.hc), bb = static_cast<int>(ch / p.g.hc);
-  if (warp == 2 * RB) {
+  if (warp == 3 * RB) {
     // ------------------------------ producer ------------------------------
     if (lane != 0) return;
     int c = 0;
     for (; c < nchunk; ++c) {
       const int s = c & (NS - 1);
-      if (c >= NS && !mbar_wait(&sm.empty[s], static_cast<uint32_t>(((c - NS) / NS) & 1))) break;
+      if (c >= NS && !mbar_wait(&sm.empty[s], par(c - NS, NS))) break;
       mbar_arrive_expect_tx(&sm.full[s], sizeof(rec::KeyRec) + tma::kTileBytes);
       bulk_g2s(&sm.slot[s].k, rec::keyrec(p.ckpt, ch, nchunk, c), sizeof(rec::KeyRec), &sm.full[s]);
       tma::load_tile(sm.slot[s].v, &P.map_v, hh, c * L, bb, &sm.full[s]);
     }
     if (c < nchunk)  // stopped on a timeout: let the copies in flight land
-      for (int cc = c > NS ? c - NS : 0; cc < c; ++cc)
-        mbar_wait(&sm.full[cc & (NS - 1)], static_cast<uint32_t>((cc / NS) & 1));
+      for (int cc = c > NS ? c - NS : 0; cc < c; ++cc) mbar_wait(&sm.full[cc & (NS - 1)], par(cc, NS));
     return;
   }
 
-  if (warp == 2 * RB + 1) {
+  if (warp == 3 * RB + 1) {
     // ------------------------------ store warp ------------------------------
     if (lane != 0) return;
     const int64_t chains = p.g.chains();
     for (int c = 0; c < nchunk; ++c) {
       const int x = c & (NX - 1);
-      if (!mbar_wait(&sm.done[x], static_cast<uint32_t>((c / NX) & 1))) break;
+      if (!mbar_wait(&sm.done[x], par(c, NX))) break;
       const Stage<RB>& st = sm.st[x];
       tma::store_tile(&P.map_sa, &st.sa[0][0], row0, hh, c * L, bb);
       tma::store_tile(&P.map_y, &st.y[0][0], row0, hh, c * L, bb);
       if (c >= 2 && (c & 1) == 0)
         bulk_s2g(rec::state_ptr(p.ckpt, chains, ch, nchunk, c) + row0 * 128, st.S, 2048 * RB);
       bulk_commit();
-      bulk_wait_read();
-      mbar_arrive(&sm.sempty[x]);
+      bulk_wait_read_n<KEEP>();
+      if (c >= KEEP) mbar_arrive(&sm.sempty[(c - KEEP) & (NX - 1)]);
     }
     bulk_wait_all();
     return;
@@ -468,93 +487,106 @@ __global__ void __launch_bounds__(32 * (2 * RB + 2), 1) value_fwd_kernel(const _
     for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
+    if (nchunk > 0 && !mbar_wait(&sm.full[0], 0)) return;
     for (int c = 0; c < nchunk; ++c) {
-      const int s = c & (NS - 1), x = c & (NX - 1);
-      if (!mbar_wait(&sm.full[s], static_cast<uint32_t>((c / NS) & 1))) return;
-      if (c >= NX && !mbar_wait(&sm.sempty[x], static_cast<uint32_t>(((c - NX) / NX) & 1))) return;
+      const int s = c & (NS - 1), xp = c & (NP - 1), sn = (c + 1) & (NS - 1);
+      // barrier tests for the end of this chunk and the next one, answered while the chunk computes
+      const bool next_ready = c + 1 >= nchunk || mbar_test(&sm.full[sn], par(c + 1, NS));
+      const bool pub_ready = c < NP || mbar_test(&sm.pfree[xp], par(c - NP, NP));
       const rec::KeyRec& kr = sm.slot[s].k;
-      Stage<RB>& st = sm.st[x];
-      uint32_t sA[4][4], vA[4], b[4];
+      uint32_t bW[4][4], bQ[4], bB[4][4], bK[4][4], vA[4];
+      float2 lam[8];
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        acc_to_a(sA[kk], S[2 * kk], S[2 * kk + 1]);
-        sta_rm(st.S, Swz64{}, il, 16 * kk, sA[kk], lane);
+        ldb_nk(bW[kk], kr.W, Swz64{}, 0, 16 * kk, lane);
+        ldb_kn(bB[kk], kr.Bb, Swz64{}, 16 * kk, 0, lane);
+        ldb_kn(bK[kk], kr.Kb, Swz64{}, 16 * kk, 0, lane);
       }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.sfull[x]);
+      ldb_nk(bQ, kr.Q, Swz16{}, 0, 0, lane);
       lda_cm(vA, sm.slot[s].v, Swz64{}, i0, 0, lane);
-      float sa[2][4] = {};
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        ldb_nk(b, kr.W, Swz64{}, 0, 16 * kk, lane);
-        mma16816(sa[0], sA[kk], b[0], b[1]);
-        mma16816(sa[1], sA[kk], b[2], b[3]);
+      for (int nt = 0; nt < 8; ++nt) lam[nt] = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
+      uint32_t sA[4][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) acc_to_a(sA[kk], S[2 * kk], S[2 * kk + 1]);
+      float sa[2][4];
+      mma_k64_k16(sa, sA, vA, bW, bQ);
+      // S' = (S + SA^T Bb + V^T Kb) diag(lam)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        mma16816(S[2 * m], vA, bK[m][0], bK[m][1]);
+        mma16816(S[2 * m + 1], vA, bK[m][2], bK[m][3]);
       }
-      ldb_nk(b, kr.Q, Swz16{}, 0, 0, lane);
-      mma16816(sa[0], vA, b[0], b[1]);
-      mma16816(sa[1], vA, b[2], b[3]);
       uint32_t saA[4];
       acc_to_a(saA, sa[0], sa[1]);
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        ldb_kn(b, kr.Bb, Swz64{}, 16 * m, 0, lane);
-        mma16816(S[2 * m], saA, b[0], b[1]);
-        mma16816(S[2 * m + 1], saA, b[2], b[3]);
-        ldb_kn(b, kr.Kb, Swz64{}, 16 * m, 0, lane);
-        mma16816(S[2 * m], vA, b[0], b[1]);
-        mma16816(S[2 * m + 1], vA, b[2], b[3]);
+        mma16816(S[2 * m], saA, bB[m][0], bB[m][1]);
+        mma16816(S[2 * m + 1], saA, bB[m][2], bB[m][3]);
       }
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-        const float2 l = *reinterpret_cast<const float2*>(&kr.lam[8 * nt + 2 * q]);
-        S[nt][0] *= l.x; S[nt][1] *= l.y; S[nt][2] *= l.x; S[nt][3] *= l.y;
+        S[nt][0] *= lam[nt].x; S[nt][1] *= lam[nt].y; S[nt][2] *= lam[nt].x; S[nt][3] *= lam[nt].y;
       }
-      // sa (rows i, cols t) -> stage [t][i]
+      // publish the chunk's start state
+      if (!pub_ready && !mbar_wait(&sm.pfree[xp], par(c - NP, NP))) return;
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          st.sa[8 * nt + 2 * q + (e & 1)][il + g + (e >= 2 ? 8 : 0)] = sa[nt][e];
-      fence_proxy_async();
+      for (int kk = 0; kk < 4; ++kk) sta_rm(sm.pub[xp].S, Swz64{}, il, 16 * kk, sA[kk], lane);
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&sm.done[x]);
+        mbar_arrive(&sm.pfull[xp]);
         mbar_arrive(&sm.empty[s]);
       }
+      if (!next_ready && !mbar_wait(&sm.full[sn], par(c + 1, NS))) return;
     }
     return;
   }
 
-  // ------------------------------ Y warp ------------------------------
+  // ------------------------------ Y warp (role 1) / A warp (role 2) ------------------------------
+  if (nchunk > 0 && !mbar_wait(&sm.full[0], 0)) return;
   for (int c = 0; c < nchunk; ++c) {
-    const int s = c & (NS - 1), x = c & (NX - 1);
-    if (!mbar_wait(&sm.full[s], static_cast<uint32_t>((c / NS) & 1))) return;
-    if (!mbar_wait(&sm.sfull[x], static_cast<uint32_t>((c / NX) & 1))) return;
+    const int s = c & (NS - 1), xp = c & (NP - 1), x = c & (NX - 1), sn = (c + 1) & (NS - 1);
+    const bool next_ready = c + 1 >= nchunk || mbar_test(&sm.full[sn], par(c + 1, NS));
+    const bool st_ready = c < NX || mbar_test(&sm.sempty[x], par(c - NX, NX));
     const rec::KeyRec& kr = sm.slot[s].k;
-    Stage<RB>& st = sm.st[x];
-    uint32_t sA[4], vA[4], b[4];
-    float yv[2][4] = {};
+    uint32_t bM[4][4], bV[4], vA[4];
+    const bf16* mk = role == 1 ? kr.Qy : kr.W;
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      lda_rm(sA, st.S, Swz64{}, il, 16 * kk, lane);
-      ldb_nk(b, kr.Qy, Swz64{}, 0, 16 * kk, lane);
-      mma16816(yv[0], sA, b[0], b[1]);
-      mma16816(yv[1], sA, b[2], b[3]);
-    }
+    for (int kk = 0; kk < 4; ++kk) ldb_nk(bM[kk], mk, Swz64{}, 0, 16 * kk, lane);
+    ldb_nk(bV, role == 1 ? kr.P : kr.Q, Swz16{}, 0, 0, lane);
     lda_cm(vA, sm.slot[s].v, Swz64{}, i0, 0, lane);
-    ldb_nk(b, kr.P, Swz16{}, 0, 0, lane);
-    mma16816(yv[0], vA, b[0], b[1]);
-    mma16816(yv[1], vA, b[2], b[3]);
-    uint32_t yA[4];
-    acc_to_a(yA, yv[0], yv[1]);
-    sta_cm(&st.y[0][0], Padded{16 * RB}, il, 0, yA, lane);
+    if (!mbar_wait(&sm.pfull[xp], par(c, NP))) return;
+    uint32_t sA[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) lda_rm(sA[kk], sm.pub[xp].S, Swz64{}, il, 16 * kk, lane);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.pfree[xp]);
+    // role 1: Y = Qy S^T + P V;  role 2: SA = W S^T + Q V (the S warp's operands and order)
+    float acc[2][4];
+    mma_k64_k16(acc, sA, vA, bM, bV);
+    if (!st_ready && !mbar_wait(&sm.sempty[x], par(c - NX, NX))) return;
+    Stage<RB>& st = sm.st[x];
+    if (role == 1) {
+      uint32_t yA[4];
+      acc_to_a(yA, acc[0], acc[1]);
+      sta_cm(&st.y[0][0], Padded{16 * RB}, il, 0, yA, lane);
+      if (c >= 2 && (c & 1) == 0)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) sta_rm(st.S, Swz64{}, il, 16 * kk, sA[kk], lane);
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          st.sa[8 * nt + 2 * q + (e & 1)][il + g + (e >= 2 ? 8 : 0)] = acc[nt][e];
+    }
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) {
       mbar_arrive(&sm.done[x]);
       mbar_arrive(&sm.empty[s]);
     }
+    if (!next_ready && !mbar_wait(&sm.full[sn], par(c + 1, NS))) return;
   }
 }
 
@@ -564,7 +596,7 @@ cudaError_t launch(const Params& V, int64_t chains, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(value_fwd_kernel<RB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  value_fwd_kernel<RB><<<static_cast<unsigned>(chains * (4 / RB)), 32 * (2 * RB + 2), smem, stream>>>(V);
+  value_fwd_kernel<RB><<<static_cast<unsigned>(chains * (4 / RB)), 32 * (3 * RB + 2), smem, stream>>>(V);
   return cudaGetLastError();
 }
 

@@ -208,6 +208,32 @@ __device__ __forceinline__ void sta_cm(__nv_bfloat16* tile, Lay lay, int m0, int
   stsm_x4_t(tile + lay(k0 + (lane & 7) + (lane >> 4) * 8, m0 + ((lane >> 3) & 1) * 8), a);
 }
 
+// acc (16 x 16) = A (16 x 64, four k-step fragments) M + V (16 x 16) N, with
+// M and N given as B fragments.  Even and odd k-steps accumulate separately
+// (two dependent chains of depth 3 instead of one of depth 5) and are summed.
+__device__ __forceinline__ void mma_k64_k16(float (&acc)[2][4], const uint32_t (&a)[4][4],
+                                            const uint32_t (&v)[4], const uint32_t (&bM)[4][4],
+                                            const uint32_t (&bN)[4]) {
+  float o[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nt][e] = o[nt][e] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 4; kk += 2) {
+    mma16816(acc[0], a[kk], bM[kk][0], bM[kk][1]);
+    mma16816(acc[1], a[kk], bM[kk][2], bM[kk][3]);
+    mma16816(o[0], a[kk + 1], bM[kk + 1][0], bM[kk + 1][1]);
+    mma16816(o[1], a[kk + 1], bM[kk + 1][2], bM[kk + 1][3]);
+  }
+  mma16816(o[0], v, bN[0], bN[1]);
+  mma16816(o[1], v, bN[2], bN[3]);
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nt][e] += o[nt][e];
+}
+
 // acc (16 x 16 output at columns n0) += A (16 x 16*KS) B;
 // AT: A stored [k][m] (else [m][k]); BT: B stored [k][n] (else [n][k]).
 template <bool AT, bool BT, int KS, typename LA, typename LB>

@@ -32,14 +32,12 @@ static_assert(sizeof(KeyRec) == 9472, "KeyRec layout");
 
 // What the value-side backward hands to the key-side backward for one chunk:
 // bf16 copies of the chunk's start state S, of G'' = dL/dS' diag(lam), of SA^T
-// and dSA^T (rows = state row i), and per value warp the column sums over its
-// 16 rows of dL/dS' o S' (summed by the reader, so the result is deterministic).
+// and dSA^T (rows = state row i).
 struct XRec {
   bf16 S[64 * 64];     // Swz64 layout over 64 rows
   bf16 G[64 * 64];     // Swz64
   bf16 SAT[64 * 16];   // Swz16 layout over 64 rows
   bf16 dSAT[64 * 16];  // Swz16
-  float dll[4][64];
 };
 static_assert(sizeof(XRec) % 16 == 0, "XRec size");
 
@@ -73,6 +71,16 @@ __device__ __forceinline__ XRec* xrec(void* work, int64_t ch, int64_t nchunk, in
 // The sequential value kernels split a chain's 64 state rows (independent in
 // the recurrence) over 4 / RB CTAs of RB 16-row blocks: as many CTAs as the
 // SMs hold at once, at most 4 per chain.
+// Role index of hardware warp w in the value kernels, whose roles are laid
+// out as [3 RB compute warps][producer][store].  Warp w runs on SMSP w % 4;
+// with RB == 2 the producer and store roles move to warps 4 and 5, so the two
+// recurrence warps (0, 1) share their SMSPs only with those light warps.
+template <int RB>
+__device__ __forceinline__ int role_warp(int w) {
+  if (RB != 2) return w;
+  return w < 4 ? w : (w < 6 ? w + 2 : w - 2);
+}
+
 inline int rows_per_cta(int64_t chains, int sms) {
   if (chains * 4 <= sms) return 1;
   if (chains * 2 <= sms) return 2;

@@ -50,6 +50,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// Non-blocking test of the phase with the given parity: issued early, its
+// result is read later, so the round trip overlaps other work.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(sm_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Wait for the phase with the given parity to complete; false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -107,6 +120,12 @@ __device__ __forceinline__ void bulk_commit() {
 // wait until the issuing thread's bulk stores have finished reading shared memory
 __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+}
+// wait until at most N of the issuing thread's most recent bulk-store groups
+// are still reading shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read_n() {
+  asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
 }
 // wait until the issuing thread's bulk stores have completed
 __device__ __forceinline__ void bulk_wait_all() {
