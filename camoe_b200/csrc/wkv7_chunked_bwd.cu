@@ -483,37 +483,69 @@ cudaError_t launch(const Params& V, int64_t chains, cudaStream_t stream) {
 
 namespace kb {
 
-constexpr int NR = 1;           // inputs single-buffered: 3 CTAs per SM overlap the loads
-constexpr int kThreads = 128;  // one group of 4 warps per CTA
+constexpr int kThreads = 128;  // one group of 4 warps per CTA, 3 CTAs per SM
 
+// Inputs are single-buffered and loaded in two parts: v, dy and the XRec of
+// the next item as soon as the first phase of this one has consumed them
+// (part A), r, w, k, a, b once this item's outputs, staged in place in those
+// tiles, have been read by the TMA stores (part B).
 struct alignas(1024) KGroup {
-  bf16 raw[NR][7][L * kN];  // r, w, k, a, b, v, dy as landed by TMA (1 KiB aligned)
-  rec::XRec x[NR];          // S and G are reused as scratch once the row sums are formed
+  bf16 raw[7][L * kN];  // r, w, k, a, b, v, dy as landed by TMA (1 KiB aligned);
+                        // r, w, k, a, b then hold dr, dw, dk, da, db for the TMA stores
+  rec::XRec x;
+  Tile dQyb, dW2b;
   Tile At, Rt, Bb, Kb;
   float lam[kN], cum[L][kN], sig[L][kN];
   float dllp[4][kN], dll[kN];
-  bf16 dPb[L][LDS];
+  bf16 dPb[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
   union {
-    bf16 Snext[64 * 64];  // first phase only: Swz64 start state of the next chunk
-    struct {              // later phases
+    struct {  // key-side recompute and the 16 x 16 pieces
       Tile W;
       Tile16 Bm, Cm, Dm, Ti, Q, P;
       float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
-      bf16 dQ2b[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
+      bf16 dQ2b[L][LDS];
       float dTf[L][L + 1];
     };
+    struct {  // column phase and the reverse scans
+      float dcum[L][kN], dcumx[L][kN];
+    };
   };
-  uint64_t bar[NR];
+  uint64_t barA, barB;
 };
-// scratch inside the XRec: dcum, dcumx (fp32 16 x 64) in S; dQyb, dW2b, dwt in G
-static_assert(2 * L * kN * sizeof(float) <= sizeof(rec::XRec::S), "dcum scratch");
-static_assert(3 * sizeof(Tile) <= sizeof(rec::XRec::G), "tile scratch");
 
 struct Params {
-  CUtensorMap maps[7];  // r, w, k, a, b, v, dy
+  CUtensorMap in[7];   // r, w, k, a, b, v, dy
+  CUtensorMap out[5];  // dr, dw, dk, da, db
   BwdArgs a;
   void* work;
 };
+
+__device__ __forceinline__ void item_pos(const Geom& g, int64_t item, int64_t& ch, int64_t& c, int& h,
+                                         int& b) {
+  ch = item / g.nchunk;
+  c = item % g.nchunk;
+  h = static_cast<int>(g.h0 + ch % g.hc);
+  b = static_cast<int>(ch / g.hc);
+}
+
+__device__ __forceinline__ void issue_a(KGroup& G, const Params& P, int64_t item) {
+  int64_t ch, c;
+  int h, b;
+  item_pos(P.a.g, item, ch, c, h, b);
+  mbar_arrive_expect_tx(&G.barA, 2 * tma::kTileBytes + sizeof(rec::XRec));
+  tma::load_tile(G.raw[5], &P.in[5], h, static_cast<int>(c * L), b, &G.barA);
+  tma::load_tile(G.raw[6], &P.in[6], h, static_cast<int>(c * L), b, &G.barA);
+  bulk_g2s(&G.x, rec::xrec(P.work, ch, P.a.g.nchunk, c), sizeof(rec::XRec), &G.barA);
+}
+
+__device__ __forceinline__ void issue_b(KGroup& G, const Params& P, int64_t item) {
+  int64_t ch, c;
+  int h, b;
+  item_pos(P.a.g, item, ch, c, h, b);
+  mbar_arrive_expect_tx(&G.barB, 5 * tma::kTileBytes);
+#pragma unroll
+  for (int t = 0; t < 5; ++t) tma::load_tile(G.raw[t], &P.in[t], h, static_cast<int>(c * L), b, &G.barB);
+}
 
 __device__ __forceinline__ uint32_t to_tf32(float x) {
   uint32_t r;
@@ -545,18 +577,6 @@ __device__ __forceinline__ void mm16_tf32(float (&acc)[2][4], FA A, FB B, int la
   }
 }
 
-__device__ __forceinline__ void issue(KGroup& G, int rb, const Params& P, int64_t item) {
-  const Geom& g = P.a.g;
-  const int64_t ch = item / g.nchunk, c = item % g.nchunk;
-  const int h = static_cast<int>(g.h0 + ch % g.hc), b = static_cast<int>(ch / g.hc);
-  const bool next = c + 1 < g.nchunk;
-  mbar_arrive_expect_tx(&G.bar[rb], 7 * tma::kTileBytes + sizeof(rec::XRec) + (next ? 8192 : 0));
-#pragma unroll
-  for (int t = 0; t < 7; ++t) tma::load_tile(G.raw[rb][t], &P.maps[t], h, static_cast<int>(c * L), b, &G.bar[rb]);
-  bulk_g2s(&G.x[rb], rec::xrec(P.work, ch, g.nchunk, c), sizeof(rec::XRec), &G.bar[rb]);
-  if (next) bulk_g2s(G.Snext, rec::xrec(P.work, ch, g.nchunk, c + 1)->S, 8192, &G.bar[rb]);
-}
-
 __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   KGroup& G = *reinterpret_cast<KGroup*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
@@ -564,37 +584,40 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
   const int tid = threadIdx.x, lane = tid & 31, gw = tid >> 5, gq = lane >> 2, q = lane & 3;
   const int j0 = 16 * gw;
   if (tid == 0) {
-    for (int i = 0; i < NR; ++i) mbar_init(&G.bar[i], 1);
+    mbar_init(&G.barA, 1);
+    mbar_init(&G.barB, 1);
     mbar_fence_init();
   }
   __syncthreads();
-  const int64_t nchunk = p.g.nchunk, T = p.g.T, ts = p.g.tstride();
+  const int64_t nchunk = p.g.nchunk;
   const int64_t total = p.g.chains() * nchunk;
-  if (tid == 0)
-    for (int i = 0; i < NR; ++i)
-      if (blockIdx.x + static_cast<int64_t>(i) * gridDim.x < total) issue(G, i, P, blockIdx.x + static_cast<int64_t>(i) * gridDim.x);
+  // thread 0's count of part A / part B loads issued and of their completions seen
+  int64_t issued_a = 0, issued_b = 0, seen_a = 0, seen_b = 0;
+  if (tid == 0 && blockIdx.x < total) {
+    issue_a(G, P, blockIdx.x);
+    issue_b(G, P, blockIdx.x);
+    issued_a = issued_b = 1;
+  }
+  const bf16* raw_r = G.raw[0];
+  const bf16* raw_k = G.raw[2];
+  const bf16* raw_a = G.raw[3];
+  const bf16* raw_b = G.raw[4];
+  const bf16* raw_v = G.raw[5];
+  const bf16* raw_dy = G.raw[6];
+  rec::XRec& xr = G.x;
   int64_t j = 0;
   for (;; ++j) {
     const int64_t item = blockIdx.x + j * gridDim.x;
     if (item >= total) break;
-    const int rb = static_cast<int>(j % NR);
-    bool ok = mbar_wait(&G.bar[rb], static_cast<uint32_t>((j / NR) & 1));
+    const int64_t next = item + gridDim.x;
+    const uint32_t ph = static_cast<uint32_t>(j & 1);
+    bool ok = mbar_wait(&G.barA, ph);  // v, dy, XRec
+    seen_a += ok;
     ok = __syncthreads_and(ok);
     if (!ok) break;
-    const int64_t ch = item / nchunk, c = item % nchunk;
-    const int64_t cbase = p.g.base(ch);
-    const bf16* raw_r = G.raw[rb][0];
-    const bf16* raw_k = G.raw[rb][2];
-    const bf16* raw_a = G.raw[rb][3];
-    const bf16* raw_b = G.raw[rb][4];
-    const bf16* raw_v = G.raw[rb][5];
-    const bf16* raw_dy = G.raw[rb][6];
-    rec::XRec& xr = G.x[rb];
-    float(*dcum)[kN] = reinterpret_cast<float(*)[kN]>(&xr.S[0]);
-    float(*dcumx)[kN] = dcum + L;
-    Tile& dQyb = *reinterpret_cast<Tile*>(&xr.G[0]);
-    Tile& dW2b = *(&dQyb + 1);
-    Tile& dwt = *(&dQyb + 2);
+    int64_t ch, c;
+    int hh, bb;
+    item_pos(p.g, item, ch, c, hh, bb);
 
     // ---- row sums over the 64 state rows (own columns), and the key side ----
     //   dW = dSA S, dQy = dY S, dBb = SA G'', dKb = V G'';  dP = lower(dY V^T) (warp 2),
@@ -626,27 +649,54 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
       store_acc_bf16(&G.dPb[0][0], LDS, 0, 0, dp[0], lane);
       store_acc_bf16(&G.dPb[0][0], LDS, 0, 8, dp[1], lane);
     }
-    {  // lam dll = colsum(G'' o S'), S' = start state of the next chunk (rows 16gw.., cols 2lane, 2lane+1)
+    {  // colsum(G'' o S) over rows 16gw.. for columns 2 lane, 2 lane + 1
       float2 acc = make_float2(0.f, 0.f);
-      if (c + 1 < nchunk) {
 #pragma unroll 4
-        for (int i = 16 * gw; i < 16 * gw + 16; ++i) {
-          const int o = Swz64{}(i, 2 * lane);
-          const float2 gv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xr.G[o]));
-          const float2 sv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&G.Snext[o]));
-          acc.x += gv.x * sv.x;
-          acc.y += gv.y * sv.y;
-        }
+      for (int i = 16 * gw; i < 16 * gw + 16; ++i) {
+        const int o = Swz64{}(i, 2 * lane);
+        const float2 gv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xr.G[o]));
+        const float2 sv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xr.S[o]));
+        acc.x += gv.x * sv.x;
+        acc.y += gv.y * sv.y;
       }
       *reinterpret_cast<float2*>(&G.dllp[gw][2 * lane]) = acc;
     }
-    ks::decays<true>(raw_r, G.raw[rb][1], raw_k, raw_a, raw_b, G.At, G.Rt, G.Kb, G.Bb, G.lam,
-                     G.cum, G.sig, tid);
-    __syncthreads();  // XRec S and G and the next chunk's state free from here on
+    ok = mbar_wait(&G.barB, ph);  // r, w, k, a, b
+    seen_b += ok;
+    if (ok)
+      ks::decays<true>(raw_r, G.raw[1], raw_k, raw_a, raw_b, G.At, G.Rt, G.Kb, G.Bb, G.lam,
+                       G.cum, G.sig, tid);
+    ok = __syncthreads_and(ok);  // v, dy and the XRec are free from here on
+    if (!ok) break;
+    if (tid == 0 && next < total) {
+      issue_a(G, P, next);
+      ++issued_a;
+    }
     ks::grams(G.At, G.Rt, G.Bb, G.Kb, G.Ga, G.Bm, G.Cm, G.Dm, gw, lane);
-    if (tid < kN) G.dll[tid] = G.dllp[0][tid] + G.dllp[1][tid] + G.dllp[2][tid] + G.dllp[3][tid];
-    store_acc_bf16(&dQyb[0][0], LD, 0, j0, dQy[0], lane);
-    store_acc_bf16(&dQyb[0][0], LD, 0, j0 + 8, dQy[1], lane);
+    {  // dll = colsum(G'' o S') / lam = colsum(G'' o S) + colsum(Bb o SA G'') + colsum(Kb o V G'')
+      float v[4];  // columns j0 + 8 nt + 2q + x, as v[2 nt + x]; rows gq, gq + 8 of this lane
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const int jj = j0 + 8 * nt + 2 * q + x;
+          v[2 * nt + x] = __bfloat162float(G.Bb[gq][jj]) * dBp[nt][x] + __bfloat162float(G.Kb[gq][jj]) * dKp[nt][x] +
+                          __bfloat162float(G.Bb[gq + 8][jj]) * dBp[nt][2 + x] +
+                          __bfloat162float(G.Kb[gq + 8][jj]) * dKp[nt][2 + x];
+        }
+#pragma unroll
+      for (int m = 4; m < 32; m <<= 1)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], m);
+      if (gq == 0)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int jj = j0 + 8 * (i >> 1) + 2 * q + (i & 1);
+          G.dll[jj] = G.dllp[0][jj] + G.dllp[1][jj] + G.dllp[2][jj] + G.dllp[3][jj] + v[i];
+        }
+    }
+    store_acc_bf16(&G.dQyb[0][0], LD, 0, j0, dQy[0], lane);
+    store_acc_bf16(&G.dQyb[0][0], LD, 0, j0 + 8, dQy[1], lane);
     __syncthreads();
     if (gw == 0) ks::inverse(G.Ga, G.Tf, G.Mf, G.Ti, lane);
     __syncthreads();
@@ -654,15 +704,15 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     __syncthreads();  // W, Q ready
 
     // ---- dW += Cm^T dQy (own columns) ----
-    mm16<true, true, 1>(dW, &G.Cm[0][0], Padded{LDS}, &dQyb[0][0], Padded{LD}, j0, lane);
-    store_acc_bf16(&dW2b[0][0], LD, 0, j0, dW[0], lane);
-    store_acc_bf16(&dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
+    mm16<true, true, 1>(dW, &G.Cm[0][0], Padded{LDS}, &G.dQyb[0][0], Padded{LD}, j0, lane);
+    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW[0], lane);
+    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
     __syncthreads();
 
     // ---- 16x16 pieces ----
     if (gw == 0) {  // dCm = lower(dQy W^T + dP Q^T)
       float dcm[2][4] = {};
-      mm16<false, false, 4>(dcm, &dQyb[0][0], Padded{LD}, &G.W[0][0], Padded{LD}, 0, lane);
+      mm16<false, false, 4>(dcm, &G.dQyb[0][0], Padded{LD}, &G.W[0][0], Padded{LD}, 0, lane);
       mm16<false, false, 1>(dcm, &G.dPb[0][0], Padded{LDS}, &G.Q[0][0], Padded{LDS}, 0, lane);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
@@ -679,13 +729,13 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
       store_acc_bf16(&G.dQ2b[0][0], LDS, 0, 8, dq[1], lane);
       __syncwarp();
       float dti[2][4] = {};
-      mm16<false, false, 4>(dti, &dW2b[0][0], Padded{LD}, &G.At[0][0], Padded{LD}, 0, lane);
+      mm16<false, false, 4>(dti, &G.dW2b[0][0], Padded{LD}, &G.At[0][0], Padded{LD}, 0, lane);
       mm16<false, false, 1>(dti, &G.dQ2b[0][0], Padded{LDS}, &G.Bm[0][0], Padded{LDS}, 0, lane);
       store_acc_f32(&G.dTf[0][0], L + 1, 0, 0, dti[0], lane);
       store_acc_f32(&G.dTf[0][0], L + 1, 0, 8, dti[1], lane);
     }
     float dAt[2][4] = {};  // Ti^T dW (own columns)
-    mm16<true, true, 1>(dAt, &G.Ti[0][0], Padded{LDS}, &dW2b[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dAt, &G.Ti[0][0], Padded{LDS}, &G.dW2b[0][0], Padded{LD}, j0, lane);
     __syncthreads();
     // dA = strict(Ti^T dTi Ti^T) with tf32 operands on warp 0; dBm = strict(Ti^T dQ) on warp 1
     if (gw == 0) {
@@ -732,21 +782,19 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     mm16<true, true, 1>(dKb, &G.dPb[0][0], Padded{LDS}, &G.Rt[0][0], Padded{LD}, j0, lane);
     mm16<false, true, 1>(dRt, &G.dCmb[0][0], Padded{LDS}, &G.Bb[0][0], Padded{LD}, j0, lane);
     mm16<false, true, 1>(dRt, &G.dPb[0][0], Padded{LDS}, &G.Kb[0][0], Padded{LD}, j0, lane);
-    bf16* dap = static_cast<bf16*>(p.da);
-    bf16* drp = static_cast<bf16*>(p.dr);
-    bf16* dkp = static_cast<bf16*>(p.dk);
-    bf16* dbp = static_cast<bf16*>(p.db);
+    // outputs in place of the inputs they replace (same thread, same element):
+    // dr -> r, dk -> k, da -> a, db -> b tiles; dw -> the w tile below
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const int t = gq + 8 * hf, jj = j0 + 8 * nt + 2 * q;
+        const int t = gq + 8 * hf, jj = j0 + 8 * nt + 2 * q, o = tma::swz(t, jj);
         const float2 cm = *reinterpret_cast<const float2*>(&G.cum[t][jj]);
         const float2 sg = *reinterpret_cast<const float2*>(&G.sig[t][jj]);
-        const float2 rr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_r + tma::swz(t, jj)));
-        const float2 kk = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_k + tma::swz(t, jj)));
-        const float2 aa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_a + tma::swz(t, jj)));
-        const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_b + tma::swz(t, jj)));
+        const float2 rr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_r + o));
+        const float2 kk = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_k + o));
+        const float2 aa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_a + o));
+        const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_b + o));
         const float cmv[2] = {cm.x, cm.y}, sgv[2] = {sg.x, sg.y};
         const float rv[2] = {rr.x, rr.y}, kv[2] = {kk.x, kk.y}, av[2] = {aa.x, aa.y}, bv[2] = {bb.x, bb.y};
         float oda[2], odr[2], odk[2], odb[2];
@@ -760,17 +808,13 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
           odr[x] = drt * Lam;
           odk[x] = dkb * iLam;
           odb[x] = dbb * iLam;
-          dcum[t][jj + x] = drt * rv[x] * Lam - dkb * kv[x] * iLam - dbb * bv[x] * iLam;
-          dcumx[t][jj + x] = dat * av[x] * Lamx;
+          G.dcum[t][jj + x] = drt * rv[x] * Lam - dkb * kv[x] * iLam - dbb * bv[x] * iLam;
+          G.dcumx[t][jj + x] = dat * av[x] * Lamx;
         }
-        const int64_t tg = c * L + t;
-        if (tg < T) {
-          const int64_t o = cbase + tg * ts + jj;
-          *reinterpret_cast<__nv_bfloat162*>(dap + o) = __floats2bfloat162_rn(oda[0], oda[1]);
-          *reinterpret_cast<__nv_bfloat162*>(drp + o) = __floats2bfloat162_rn(odr[0], odr[1]);
-          *reinterpret_cast<__nv_bfloat162*>(dkp + o) = __floats2bfloat162_rn(odk[0], odk[1]);
-          *reinterpret_cast<__nv_bfloat162*>(dbp + o) = __floats2bfloat162_rn(odb[0], odb[1]);
-        }
+        *reinterpret_cast<__nv_bfloat162*>(G.raw[3] + o) = __floats2bfloat162_rn(oda[0], oda[1]);
+        *reinterpret_cast<__nv_bfloat162*>(G.raw[0] + o) = __floats2bfloat162_rn(odr[0], odr[1]);
+        *reinterpret_cast<__nv_bfloat162*>(G.raw[2] + o) = __floats2bfloat162_rn(odk[0], odk[1]);
+        *reinterpret_cast<__nv_bfloat162*>(G.raw[4] + o) = __floats2bfloat162_rn(odb[0], odb[1]);
       }
     __syncwarp();
     if (lane < 16) {  // reverse scans along t of column j
@@ -778,31 +822,35 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
       float s1 = 0.f, s2 = 0.f;
 #pragma unroll
       for (int t = L - 1; t >= 0; --t) {
-        float dc = dcum[t][jj];
-        if (t == L - 1) dc += G.dll[jj] / G.lam[jj];  // the XRec holds colsum(G'' o S') = lam dll
+        float dc = G.dcum[t][jj];
+        if (t == L - 1) dc += G.dll[jj];
         s1 += dc;
         const float dlw = s1 + s2;
-        s2 += dcumx[t][jj];
+        s2 += G.dcumx[t][jj];
         const float sg = G.sig[t][jj];
-        dwt[t][jj] = __float2bfloat16_rn(dlw * kWScale * sg * (1.0f - sg));
+        G.raw[1][tma::swz(t, jj)] = __float2bfloat16_rn(dlw * kWScale * sg * (1.0f - sg));
       }
     }
+    fence_proxy_async();  // the output tiles are read by the TMA stores below
     __syncthreads();
-    {  // dw tile: 16 rows x 8 pieces of 16 bytes
-      const int t = tid >> 3, part = tid & 7;
-      const int64_t tg = c * L + t;
-      if (tg < T)
-        *reinterpret_cast<uint4*>(static_cast<bf16*>(p.dw) + cbase + tg * ts + part * 8) =
-            *reinterpret_cast<const uint4*>(&dwt[t][part * 8]);
+    if (tid == 0) {
+      const int order[5] = {0, 1, 2, 3, 4};  // dr, dw, dk, da, db
+#pragma unroll
+      for (int i = 0; i < 5; ++i) tma::store_tile(&P.out[i], G.raw[order[i]], 0, hh, static_cast<int>(c * L), bb);
+      bulk_commit();
+      bulk_wait_read();
+      if (next < total) {
+        issue_b(G, P, next);
+        ++issued_b;
+      }
     }
-    fence_proxy_async();  // generic writes to the XRec scratch before the next bulk load lands there
-    __syncthreads();  // raw, XRec and scratch free
-    if (tid == 0 && item + NR * static_cast<int64_t>(gridDim.x) < total)
-      issue(G, rb, P, item + NR * static_cast<int64_t>(gridDim.x));
   }
-  if (tid == 0)  // after a timeout, let loads in flight land before the CTA exits
-    for (int64_t jj = j; jj < j + NR; ++jj)
-      if (blockIdx.x + jj * gridDim.x < total) mbar_wait(&G.bar[jj % NR], static_cast<uint32_t>((jj / NR) & 1));
+  if (tid == 0) {
+    // after a timeout, let loads still in flight land before the CTA exits
+    if (issued_a > seen_a) mbar_wait(&G.barA, static_cast<uint32_t>((issued_a - 1) & 1));
+    if (issued_b > seen_b) mbar_wait(&G.barB, static_cast<uint32_t>((issued_b - 1) & 1));
+    bulk_wait_all();
+  }
 }
 
 }  // namespace kb
@@ -844,7 +892,10 @@ cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
   K.work = work;
   const void* src[7] = {p.r, p.w, p.k, p.a, p.b, p.v, p.dy};
   for (int t = 0; t < 7; ++t)
-    if (!tma::encode_bhtn(&K.maps[t], src[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
+    if (!tma::encode_bhtn(&K.in[t], src[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
+  const void* dst[5] = {p.dr, p.dw, p.dk, p.da, p.db};
+  for (int t = 0; t < 5; ++t)
+    if (!tma::encode_bhtn(&K.out[t], dst[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
   const size_t ksmem = sizeof(kb::KGroup) + 1024;
   e = cudaFuncSetAttribute(kb::keyside_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)ksmem);
