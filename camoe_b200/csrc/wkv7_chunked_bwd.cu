@@ -498,18 +498,11 @@ struct alignas(1024) KGroup {
   float lam[kN], cum[L][kN], sig[L][kN];
   float dllp[4][kN], dll[kN];
   bf16 dPb[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
-  union {
-    struct {  // key-side recompute and the 16 x 16 pieces
-      Tile W;
-      Tile16 Bm, Cm, Dm, Ti, Q, P;
-      float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
-      bf16 dQ2b[L][LDS];
-      float dTf[L][L + 1];
-    };
-    struct {  // column phase and the reverse scans
-      float dcum[L][kN], dcumx[L][kN];
-    };
-  };
+  Tile W;
+  Tile16 Bm, Cm, Dm, Ti, Q, P;
+  float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
+  bf16 dQ2b[L][LDS];
+  float dTf[L][L + 1];
   uint64_t barA, barB;
 };
 
@@ -783,7 +776,9 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     mm16<false, true, 1>(dRt, &G.dCmb[0][0], Padded{LDS}, &G.Bb[0][0], Padded{LD}, j0, lane);
     mm16<false, true, 1>(dRt, &G.dPb[0][0], Padded{LDS}, &G.Kb[0][0], Padded{LD}, j0, lane);
     // outputs in place of the inputs they replace (same thread, same element):
-    // dr -> r, dk -> k, da -> a, db -> b tiles; dw -> the w tile below
+    // dr -> r, dk -> k, da -> a, db -> b tiles; dw -> the w tile.  This lane
+    // holds rows gq (hf 0) and gq + 8 (hf 1) of columns j0 + 8 nt + 2q + x.
+    float u[2][2][2], cx[2][2][2], sgs[2][2][2];  // [nt][x][hf]: dcum + dcumx, dcumx, sig
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -808,29 +803,57 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
           odr[x] = drt * Lam;
           odk[x] = dkb * iLam;
           odb[x] = dbb * iLam;
-          G.dcum[t][jj + x] = drt * rv[x] * Lam - dkb * kv[x] * iLam - dbb * bv[x] * iLam;
-          G.dcumx[t][jj + x] = dat * av[x] * Lamx;
+          const float dcx = dat * av[x] * Lamx;
+          cx[nt][x][hf] = dcx;
+          u[nt][x][hf] = drt * rv[x] * Lam - dkb * kv[x] * iLam - dbb * bv[x] * iLam + dcx;
+          sgs[nt][x][hf] = sgv[x];
         }
         *reinterpret_cast<__nv_bfloat162*>(G.raw[3] + o) = __floats2bfloat162_rn(oda[0], oda[1]);
         *reinterpret_cast<__nv_bfloat162*>(G.raw[0] + o) = __floats2bfloat162_rn(odr[0], odr[1]);
         *reinterpret_cast<__nv_bfloat162*>(G.raw[2] + o) = __floats2bfloat162_rn(odk[0], odk[1]);
         *reinterpret_cast<__nv_bfloat162*>(G.raw[4] + o) = __floats2bfloat162_rn(odb[0], odb[1]);
       }
-    __syncwarp();
-    if (lane < 16) {  // reverse scans along t of column j
-      const int jj = j0 + lane;
-      float s1 = 0.f, s2 = 0.f;
+    // reverse scans along t: dlw_s = sum_{t>=s} (dcum_t + dcumx_t) - dcumx_s, with dll
+    // added at the last step; rows gq + 8 hf sit in the 8 lanes of equal q (lane stride 4)
+    if (gq == 7)
 #pragma unroll
-      for (int t = L - 1; t >= 0; --t) {
-        float dc = G.dcum[t][jj];
-        if (t == L - 1) dc += G.dll[jj];
-        s1 += dc;
-        const float dlw = s1 + s2;
-        s2 += G.dcumx[t][jj];
-        const float sg = G.sig[t][jj];
-        G.raw[1][tma::swz(t, jj)] = __float2bfloat16_rn(dlw * kWScale * sg * (1.0f - sg));
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) u[nt][x][1] += G.dll[j0 + 8 * nt + 2 * q + x];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        float s1 = u[nt][x][1];  // suffix over rows 8..15
+#pragma unroll
+        for (int d = 1; d < 8; d <<= 1) {
+          const float y = __shfl_down_sync(0xffffffffu, s1, 4 * d);
+          if (gq + d < 8) s1 += y;
+        }
+        const float tot1 = __shfl_sync(0xffffffffu, s1, q);
+        float s0 = u[nt][x][0];  // suffix over rows 0..7
+#pragma unroll
+        for (int d = 1; d < 8; d <<= 1) {
+          const float y = __shfl_down_sync(0xffffffffu, s0, 4 * d);
+          if (gq + d < 8) s0 += y;
+        }
+        s0 += tot1;
+        u[nt][x][0] = s0 - cx[nt][x][0];
+        u[nt][x][1] = s1 - cx[nt][x][1];
       }
-    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int t = gq + 8 * hf, jj = j0 + 8 * nt + 2 * q;
+        float dwv[2];
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float sg = sgs[nt][x][hf];
+          dwv[x] = u[nt][x][hf] * kWScale * sg * (1.0f - sg);
+        }
+        *reinterpret_cast<__nv_bfloat162*>(G.raw[1] + tma::swz(t, jj)) = __floats2bfloat162_rn(dwv[0], dwv[1]);
+      }
     fence_proxy_async();  // the output tiles are read by the TMA stores below
     __syncthreads();
     if (tid == 0) {
