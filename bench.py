@@ -45,6 +45,23 @@ FWD_BYTES, BWD_BYTES = 6 * 2 + 2 + 4, 7 * 2 + 6 * 2
 FALLBACK_HBM_GBS = 6650.0
 
 
+def profiled_traffic(workload: str, kernels: list[str]):
+    """DRAM bytes (read + write) per launch of `kernels`, summed, from the committed
+    ncu launch-list summary of this workload (profiles/launches_<workload>.md), or
+    None when there is no such capture."""
+    path = os.path.join(ROOT, "profiles", f"launches_{workload}.md")
+    try:
+        with open(path) as f:
+            line = next(l for l in f if l.startswith("traffic-per-launch-bytes:"))
+    except (OSError, StopIteration):
+        return None
+    per = dict(kv.split("=") for kv in line.split(":", 1)[1].split())
+    try:
+        return sum(int(per[k]) for k in kernels)
+    except KeyError:
+        return None
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -261,11 +278,19 @@ def main():
     step_gbs = (FWD_BYTES + BWD_BYTES) * elems / (step_ms / 1e3) / 1e9
     kname = {"fwd": "forward (keyside_kernel + value_fwd_kernel)",
              "bwd": "backward (value_bwd_kernel + keyside_bwd_kernel)"}[kern]
+    traffic = None
     if args.algo == "scan":
         kname = f"scan_{kern}_kernel"
+    else:
+        traffic = profiled_traffic(args.workload,
+                                   ["value_bwd_kernel", "keyside_bwd_kernel"] if kern == "bwd"
+                                   else ["keyside_kernel", "value_fwd_kernel"])
     roofline = {"bound": "hbm", "kernel": kname, "achieved": achieved,
                 "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": None, "algorithmic_bytes_per_launch": k_bytes,
+                "traffic": traffic,
+                "traffic_source": (f"profiles/launches_{args.workload}.md (ncu dram__bytes_read.sum"
+                                   " + dram__bytes_write.sum per launch)") if traffic else None,
+                "algorithmic_bytes_per_launch": k_bytes,
                 "launch_ms": k_ms, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
                 "step_achieved": step_gbs, "step_frac": step_gbs / hbm,
                 "bytes_per_element": {"fwd": FWD_BYTES, "bwd": BWD_BYTES}}
