@@ -321,7 +321,13 @@ def main():
 
 def measure_e2e(args, xs, dy, dev, stream, world, local):
     """Same metric through the public autograd API with host buffers: every step
-    copies the inputs from pinned host memory and reads every output back."""
+    copies its inputs from pinned host memory and reads every output back.
+
+    Steps are pipelined as an input pipeline would run them: step k+1's inputs go
+    host -> device on one copy stream (into the other of two device buffers) and
+    step k's outputs go device -> host on a second copy stream while the op runs
+    on the compute stream, so both PCIe directions overlap the compute.  The timed
+    region starts before the first input copy and ends after the last output copy."""
     from camoe_b200 import backbone
 
     os.environ.setdefault("CAMOE_WKV7_ALGO", args.algo)
@@ -332,25 +338,52 @@ def measure_e2e(args, xs, dy, dev, stream, world, local):
                             pin_memory=True) for i in range(n_out)]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = sum(t.numel() * t.element_size() for t in host_out)
+    bufs = [[torch.empty_like(h, device=dev) for h in host_in] for _ in range(2)]
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    freed = [torch.cuda.Event(), torch.cuda.Event()]  # compute done with buffer b
+    landed = [torch.cuda.Event(), torch.cuda.Event()]  # inputs of buffer b on the device
+    computed = torch.cuda.Event()
 
-    def one():
-        d = [h.to(dev, non_blocking=True) for h in host_in]
-        ins = [t.requires_grad_(True) for t in d[:6]]
+    def copy_in(k):
+        b = k % 2
+        with torch.cuda.stream(up):
+            if k >= 2:
+                up.wait_event(freed[b])
+            for d, h in zip(bufs[b], host_in):
+                d.copy_(h, non_blocking=True)
+            landed[b].record(up)
+
+    def step(k, last):
+        b = k % 2
+        stream.wait_event(landed[b])
+        ins = [t.detach().requires_grad_(True) for t in bufs[b][:6]]
         y, sa = backbone.RWKV7_ClampW.apply(*ins)
-        torch.autograd.backward([y], [d[6]])
+        torch.autograd.backward([y], [bufs[b][6]])
         outs = [y, sa] + [t.grad for t in ins]
-        for h, o in zip(host_out, outs):
-            h.copy_(o, non_blocking=True)
+        freed[b].record(stream)
+        if not last:
+            copy_in(k + 1)
+        computed.record(stream)
+        with torch.cuda.stream(down):
+            down.wait_event(computed)
+            for h, o in zip(host_out, outs):
+                h.copy_(o, non_blocking=True)
+                o.record_stream(down)
+
+    def run(n):
+        copy_in(0)
+        for k in range(n):
+            step(k, k == n - 1)
 
     steps = max(3, min(args.steps, 20))
-    for _ in range(2):
-        one()
+    run(2)
     torch.cuda.synchronize(dev)
     barrier(world, local)
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s0.record(stream)
-    for _ in range(steps):
-        one()
+    up.wait_stream(stream)
+    run(steps)
+    stream.wait_stream(down)
     s1.record(stream)
     torch.cuda.synchronize(dev)
     barrier(world, local)
@@ -358,7 +391,9 @@ def measure_e2e(args, xs, dy, dev, stream, world, local):
     tokens = xs[0].shape[0] * xs[0].shape[1] * world * steps
     return {"value": tokens / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": steps,
-            "api": "camoe_b200.backbone.RWKV7_ClampW.apply + autograd backward"}
+            "api": "camoe_b200.backbone.RWKV7_ClampW.apply + autograd backward",
+            "pipelining": "inputs of step k+1 and outputs of step k copied on two streams "
+                          "while step k computes"}
 
 
 if __name__ == "__main__":
