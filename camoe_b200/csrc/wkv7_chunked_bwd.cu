@@ -555,18 +555,16 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// acc (16 x 16) = A (16 x 16) B (16 x 16) with tf32 operands, one warp;
+// acc (16 x 8 at columns n0) = A (16 x 16) B (16 x 16) with tf32 operands, one warp;
 // A(m, k) and B(k, n) are element accessors.
 template <typename FA, typename FB>
-__device__ __forceinline__ void mm16_tf32(float (&acc)[2][4], FA A, FB B, int lane) {
+__device__ __forceinline__ void mm8_tf32(float (&acc)[4], FA A, FB B, int n0, int lane) {
   const int g = lane >> 2, q = lane & 3;
 #pragma unroll
   for (int k0 = 0; k0 < 16; k0 += 8) {
     const uint32_t a[4] = {to_tf32(A(g, k0 + q)), to_tf32(A(g + 8, k0 + q)),
                            to_tf32(A(g, k0 + q + 4)), to_tf32(A(g + 8, k0 + q + 4))};
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-      mma_tf32(acc[nt], a, to_tf32(B(k0 + q, 8 * nt + g)), to_tf32(B(k0 + q + 4, 8 * nt + g)));
+    mma_tf32(acc, a, to_tf32(B(k0 + q, n0 + g)), to_tf32(B(k0 + q + 4, n0 + g)));
   }
 }
 
@@ -691,16 +689,22 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     store_acc_bf16(&G.dQyb[0][0], LD, 0, j0, dQy[0], lane);
     store_acc_bf16(&G.dQyb[0][0], LD, 0, j0 + 8, dQy[1], lane);
     __syncthreads();
-    if (gw == 0) ks::inverse(G.Ga, G.Tf, G.Mf, G.Ti, lane);
+    // ---- inverse (warp 0) | dW += Cm^T dQy, own columns (warps 1-3) ----
+    if (gw == 0) {
+      ks::inverse(G.Ga, G.Tf, G.Mf, G.Ti, lane);
+    } else {
+      mm16<true, true, 1>(dW, &G.Cm[0][0], Padded{LDS}, &G.dQyb[0][0], Padded{LD}, j0, lane);
+      store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW[0], lane);
+      store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
+    }
     __syncthreads();
+    if (gw == 0) {
+      mm16<true, true, 1>(dW, &G.Cm[0][0], Padded{LDS}, &G.dQyb[0][0], Padded{LD}, j0, lane);
+      store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW[0], lane);
+      store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
+    }
     ks::w_and_q(G.Ti, G.At, G.Bm, G.W, G.Q, gw, lane);
-    __syncthreads();  // W, Q ready
-
-    // ---- dW += Cm^T dQy (own columns) ----
-    mm16<true, true, 1>(dW, &G.Cm[0][0], Padded{LDS}, &G.dQyb[0][0], Padded{LD}, j0, lane);
-    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW[0], lane);
-    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
-    __syncthreads();
+    __syncthreads();  // W, Q and dW ready
 
     // ---- 16x16 pieces ----
     if (gw == 0) {  // dCm = lower(dQy W^T + dP Q^T)
@@ -730,26 +734,26 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     float dAt[2][4] = {};  // Ti^T dW (own columns)
     mm16<true, true, 1>(dAt, &G.Ti[0][0], Padded{LDS}, &G.dW2b[0][0], Padded{LD}, j0, lane);
     __syncthreads();
-    // dA = strict(Ti^T dTi Ti^T) with tf32 operands on warp 0; dBm = strict(Ti^T dQ) on warp 1
-    if (gw == 0) {
-      float m1[2][4] = {};  // M1 = dTi Ti^T
-      mm16_tf32(m1, [&](int m, int k) { return G.dTf[m][k]; },
-                [&](int k, int n) { return G.Tf[n][k]; }, lane);
-      store_acc_f32(&G.Ga[0][0], L + 1, 0, 0, m1[0], lane);  // Ga is free after the inverse
-      store_acc_f32(&G.Ga[0][0], L + 1, 0, 8, m1[1], lane);
+    // dA = strict(Ti^T dTi Ti^T) with tf32 operands, columns 0-7 on warp 0 and 8-15 on
+    // warp 2 (a column block of dA needs only that block of M1 = dTi Ti^T);
+    // dBm = strict(Ti^T dQ) on warp 1; every warp also forms the column products
+    // that need neither.
+    if (gw == 0 || gw == 2) {
+      const int n0 = gw == 0 ? 0 : 8;
+      float m1[4] = {};
+      mm8_tf32(m1, [&](int m, int k) { return G.dTf[m][k]; },
+               [&](int k, int n) { return G.Tf[n][k]; }, n0, lane);
+      store_acc_f32(&G.Ga[0][0], L + 1, 0, n0, m1, lane);  // Ga is free after the inverse
       __syncwarp();
-      float da[2][4] = {};  // dA = Ti^T M1
-      mm16_tf32(da, [&](int m, int k) { return G.Tf[k][m]; },
-                [&](int k, int n) { return G.Ga[k][n]; }, lane);
+      float da[4] = {};
+      mm8_tf32(da, [&](int m, int k) { return G.Tf[k][m]; },
+               [&](int k, int n) { return G.Ga[k][n]; }, n0, lane);
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
-          if (u >= t) da[nt][e] = 0.f;
-        }
-      store_acc_bf16(&G.dAb[0][0], LDS, 0, 0, da[0], lane);
-      store_acc_bf16(&G.dAb[0][0], LDS, 0, 8, da[1], lane);
+      for (int e = 0; e < 4; ++e) {
+        const int t = gq + (e >= 2 ? 8 : 0), u = n0 + 2 * q + (e & 1);
+        if (u >= t) da[e] = 0.f;
+      }
+      store_acc_bf16(&G.dAb[0][0], LDS, 0, n0, da, lane);
     } else if (gw == 1) {
       float dbm[2][4] = {};
       mm16<true, true, 1>(dbm, &G.Ti[0][0], Padded{LDS}, &G.dQ2b[0][0], Padded{LDS}, 0, lane);
@@ -763,18 +767,18 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
       store_acc_bf16(&G.dBmb[0][0], LDS, 0, 0, dbm[0], lane);
       store_acc_bf16(&G.dBmb[0][0], LDS, 0, 8, dbm[1], lane);
     }
-    __syncthreads();
-
-    // ---- column-indexed gradients (own columns) ----
-    mm16<false, true, 1>(dAt, &G.dAb[0][0], Padded{LDS}, &G.Bb[0][0], Padded{LD}, j0, lane);
-    mm16<false, true, 1>(dAt, &G.dBmb[0][0], Padded{LDS}, &G.Kb[0][0], Padded{LD}, j0, lane);
     float dBb[2][4] = {}, dKb[2][4] = {}, dRt[2][4] = {};
-    mm16<true, true, 1>(dBb, &G.dAb[0][0], Padded{LDS}, &G.At[0][0], Padded{LD}, j0, lane);
     mm16<true, true, 1>(dBb, &G.dCmb[0][0], Padded{LDS}, &G.Rt[0][0], Padded{LD}, j0, lane);
-    mm16<true, true, 1>(dKb, &G.dBmb[0][0], Padded{LDS}, &G.At[0][0], Padded{LD}, j0, lane);
     mm16<true, true, 1>(dKb, &G.dPb[0][0], Padded{LDS}, &G.Rt[0][0], Padded{LD}, j0, lane);
     mm16<false, true, 1>(dRt, &G.dCmb[0][0], Padded{LDS}, &G.Bb[0][0], Padded{LD}, j0, lane);
     mm16<false, true, 1>(dRt, &G.dPb[0][0], Padded{LDS}, &G.Kb[0][0], Padded{LD}, j0, lane);
+    __syncthreads();
+
+    // ---- column-indexed gradients that need dA, dBm (own columns) ----
+    mm16<false, true, 1>(dAt, &G.dAb[0][0], Padded{LDS}, &G.Bb[0][0], Padded{LD}, j0, lane);
+    mm16<false, true, 1>(dAt, &G.dBmb[0][0], Padded{LDS}, &G.Kb[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dBb, &G.dAb[0][0], Padded{LDS}, &G.At[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dKb, &G.dBmb[0][0], Padded{LDS}, &G.At[0][0], Padded{LD}, j0, lane);
     // outputs in place of the inputs they replace (same thread, same element):
     // dr -> r, dk -> k, da -> a, db -> b tiles; dw -> the w tile.  This lane
     // holds rows gq (hf 0) and gq + 8 (hf 1) of columns j0 + 8 nt + 2q + x.
