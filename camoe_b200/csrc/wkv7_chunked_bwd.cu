@@ -655,7 +655,8 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     ok = mbar_wait(&G.barB, ph);  // r, w, k, a, b
     seen_b += ok;
     if (ok)
-      ks::decays<true>(raw_r, G.raw[1], raw_k, raw_a, raw_b, G.At, G.Rt, G.Kb, G.Bb, G.lam,
+      ks::decays<true>(raw_r, G.raw[1], raw_k, raw_a, raw_b, &G.At[0][0], &G.Rt[0][0], Padded{LD},
+                       &G.Kb[0][0], &G.Bb[0][0], Padded{LD}, G.lam,
                        G.cum, G.sig, tid);
     ok = __syncthreads_and(ok);  // v, dy and the XRec are free from here on
     if (!ok) break;
@@ -663,7 +664,8 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
       issue_a(G, P, next);
       ++issued_a;
     }
-    ks::grams(G.At, G.Rt, G.Bb, G.Kb, G.Ga, G.Bm, G.Cm, G.Dm, gw, lane);
+    ks::grams(&G.At[0][0], &G.Rt[0][0], Padded{LD}, &G.Bb[0][0], &G.Kb[0][0], Padded{LD}, G.Ga,
+              G.Bm, G.Cm, G.Dm, gw, lane);
     {  // dll = colsum(G'' o S') / lam = colsum(G'' o S) + colsum(Bb o SA G'') + colsum(Kb o V G'')
       float v[4];  // columns j0 + 8 nt + 2q + x, as v[2 nt + x]; rows gq, gq + 8 of this lane
 #pragma unroll
@@ -703,7 +705,8 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
       store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW[0], lane);
       store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
     }
-    ks::w_and_q(G.Ti, G.At, G.Bm, G.W, G.Q, gw, lane);
+    ks::w_and_q(G.Ti, &G.At[0][0], Padded{LD}, G.Bm, &G.W[0][0], Padded{LD}, &G.Q[0][0],
+                Padded{LDS}, gw, lane);
     __syncthreads();  // W, Q and dW ready
 
     // ---- 16x16 pieces ----

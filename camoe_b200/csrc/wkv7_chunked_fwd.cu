@@ -208,21 +208,24 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_fwd_kernel(const __grid_c
       if (ok && c >= NS) ok = mbar_wait(&sm.empty[s], static_cast<uint32_t>((c / NS - 1) & 1));
       ok = named_sync_and(bar_id, 128, ok);  // the group leaves together on a timeout
       if (!ok) break;
-      ks::decays<true>(raw[R_R], raw[R_W], raw[R_K], raw[R_A], raw[R_B], sc.At, sc.Rt, sl.Kb,
-                       sl.Bb, sl.lam, nullptr, nullptr, gtid);
+      ks::decays<true>(raw[R_R], raw[R_W], raw[R_K], raw[R_A], raw[R_B], &sc.At[0][0], &sc.Rt[0][0],
+                       Padded{LD}, &sl.Kb[0][0], &sl.Bb[0][0], Padded{LD}, sl.lam, nullptr, nullptr, gtid);
       {  // v tile -> slot, un-swizzled (one 16-byte piece per thread)
         const int u = gtid >> 3, part = gtid & 7;
         *reinterpret_cast<uint4*>(&sl.v[u][part * 8]) =
             *reinterpret_cast<const uint4*>(&raw[R_V][tma::swz(u, part * 8)]);
       }
       named_sync(bar_id, 128);
-      ks::grams(sc.At, sc.Rt, sl.Bb, sl.Kb, sc.Ga, sc.Bm, sc.Cm, sc.Dm, gw, lane);
+      ks::grams(&sc.At[0][0], &sc.Rt[0][0], Padded{LD}, &sl.Bb[0][0], &sl.Kb[0][0], Padded{LD}, sc.Ga,
+                sc.Bm, sc.Cm, sc.Dm, gw, lane);
       named_sync(bar_id, 128);
       if (gw == 0) ks::inverse(sc.Ga, sc.Tf, sc.Mf, sc.Ti, lane);
       named_sync(bar_id, 128);
-      ks::w_and_q(sc.Ti, sc.At, sc.Bm, sl.W, sl.Q, gw, lane);
+      ks::w_and_q(sc.Ti, &sc.At[0][0], Padded{LD}, sc.Bm, &sl.W[0][0], Padded{LD}, &sl.Q[0][0],
+                  Padded{LDS}, gw, lane);
       named_sync(bar_id, 128);
-      ks::qy_and_p(sc.Cm, sl.W, sc.Rt, sl.Q, sc.Dm, sl.Qy, sl.P, gw, lane);
+      ks::qy_and_p(sc.Cm, &sl.W[0][0], Padded{LD}, &sc.Rt[0][0], Padded{LD}, &sl.Q[0][0], Padded{LDS},
+                   sc.Dm, &sl.Qy[0][0], Padded{LD}, &sl.P[0][0], Padded{LDS}, gw, lane);
       named_sync(bar_id, 128);
       if (gtid == 0) mbar_arrive(&sm.full[s]);
       if (gtid == 0 && k + NRAW < nk)
@@ -261,9 +264,9 @@ constexpr int NR = 2;  // input buffers per group
 
 struct alignas(1024) Group {
   bf16 raw[NR][5][L * kN];  // r, w, k, a, b tiles as landed by TMA (1 KiB aligned)
-  rec::KeyRec out;          // staging of the record for the bulk store
-  Tile At, Rt, W, Qy, Bb, Kb;
-  Tile16 Bm, Cm, Dm, Ti, Q, P;
+  rec::KeyRec out;          // the record, written in place (swizzled layouts), then bulk-stored
+  Tile At, Rt;
+  Tile16 Bm, Cm, Dm, Ti;
   float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
   float lam[kN];
   uint64_t rawbar[NR];
@@ -306,42 +309,24 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
     if (item >= total) break;
     const int rb = static_cast<int>(j % NR);
     bool ok = mbar_wait(&G.rawbar[rb], static_cast<uint32_t>((j / NR) & 1));
+    if (gtid == 0) bulk_wait_read();  // the previous record has left `out`
     ok = named_sync_and(bar_id, 128, ok);
     if (!ok) break;
-    ks::decays<true>(G.raw[rb][0], G.raw[rb][1], G.raw[rb][2], G.raw[rb][3], G.raw[rb][4], G.At,
-                     G.Rt, G.Kb, G.Bb, G.lam, nullptr, nullptr, gtid);
+    rec::KeyRec& o = G.out;
+    ks::decays<true>(G.raw[rb][0], G.raw[rb][1], G.raw[rb][2], G.raw[rb][3], G.raw[rb][4],
+                     &G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Kb, o.Bb, Swz64{}, o.lam, nullptr,
+                     nullptr, gtid);
     named_sync(bar_id, 128);
     if (gtid == 0 && item + NR * ngroups < total) issue(G, rb, P, item + NR * ngroups);
-    ks::grams(G.At, G.Rt, G.Bb, G.Kb, G.Ga, G.Bm, G.Cm, G.Dm, gw, lane);
+    ks::grams(&G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Bb, o.Kb, Swz64{}, G.Ga, G.Bm, G.Cm, G.Dm,
+              gw, lane);
     named_sync(bar_id, 128);
     if (gw == 0) ks::inverse(G.Ga, G.Tf, G.Mf, G.Ti, lane);
     named_sync(bar_id, 128);
-    ks::w_and_q(G.Ti, G.At, G.Bm, G.W, G.Q, gw, lane);
+    ks::w_and_q(G.Ti, &G.At[0][0], Padded{LD}, G.Bm, o.W, Swz64{}, o.Q, Swz16{}, gw, lane);
     named_sync(bar_id, 128);
-    ks::qy_and_p(G.Cm, G.W, G.Rt, G.Q, G.Dm, G.Qy, G.P, gw, lane);
-    if (gtid == 0) bulk_wait_read();  // the previous record has left `out`
-    named_sync(bar_id, 128);
-    // pack W, Qy, Bb, Kb, Q, P, lam into the record (16-byte pieces, swizzled layouts)
-    for (int pc = gtid; pc < 592; pc += 128) {
-      uint4 v;
-      void* dst;
-      if (pc < 512) {
-        const int t = pc >> 7, r = (pc >> 3) & 15, k = pc & 7;
-        const Tile& src = t == 0 ? G.W : t == 1 ? G.Qy : t == 2 ? G.Bb : G.Kb;
-        bf16* d = t == 0 ? G.out.W : t == 1 ? G.out.Qy : t == 2 ? G.out.Bb : G.out.Kb;
-        v = *reinterpret_cast<const uint4*>(&src[r][8 * k]);
-        dst = d + Swz64{}(r, 8 * k);
-      } else if (pc < 576) {
-        const int t = (pc - 512) >> 5, r = ((pc - 512) >> 1) & 15, k = pc & 1;
-        const Tile16& src = t == 0 ? G.Q : G.P;
-        v = *reinterpret_cast<const uint4*>(&src[r][8 * k]);
-        dst = (t == 0 ? G.out.Q : G.out.P) + Swz16{}(r, 8 * k);
-      } else {
-        v = *reinterpret_cast<const uint4*>(&G.lam[4 * (pc - 576)]);
-        dst = &G.out.lam[4 * (pc - 576)];
-      }
-      *reinterpret_cast<uint4*>(dst) = v;
-    }
+    ks::qy_and_p(G.Cm, o.W, Swz64{}, &G.Rt[0][0], Padded{LD}, o.Q, Swz16{}, G.Dm, o.Qy, Swz64{},
+                 o.P, Swz16{}, gw, lane);
     fence_proxy_async();
     named_sync(bar_id, 128);
     if (gtid == 0) {

@@ -37,10 +37,11 @@ __device__ __forceinline__ int raw_idx(int u, int j) {
   return SWZ ? tma::swz(u, j) : u * LD + j;
 }
 
-template <bool SWZ>
+// At, Rt are written through layout lar, Kb, Bb through layout lkb (16 x 64 bf16).
+template <bool SWZ, typename LAR, typename LKB>
 __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf16* kk,
-                                       const bf16* aa, const bf16* bb, Tile& At, Tile& Rt,
-                                       Tile& Kb, Tile& Bb, float* lam, float (*cum_out)[kN],
+                                       const bf16* aa, const bf16* bb, bf16* At, bf16* Rt, LAR lar,
+                                       bf16* Kb, bf16* Bb, LKB lkb, float* lam, float (*cum_out)[kN],
                                        float (*sig_out)[kN], int gtid) {
   const int p = gtid >> 2, tq = gtid & 3, j = 2 * p;
   const int lane = gtid & 31;
@@ -86,10 +87,10 @@ __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf1
     const float2 k = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kk + o));
     const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(aa + o));
     const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bb + o));
-    *reinterpret_cast<__nv_bfloat162*>(&At[u][j]) = __floats2bfloat162_rn(a.x * px0, a.y * px1);
-    *reinterpret_cast<__nv_bfloat162*>(&Rt[u][j]) = __floats2bfloat162_rn(r.x * L0, r.y * L1);
-    *reinterpret_cast<__nv_bfloat162*>(&Kb[u][j]) = __floats2bfloat162_rn(k.x * i0, k.y * i1);
-    *reinterpret_cast<__nv_bfloat162*>(&Bb[u][j]) = __floats2bfloat162_rn(b.x * i0, b.y * i1);
+    *reinterpret_cast<__nv_bfloat162*>(At + lar(u, j)) = __floats2bfloat162_rn(a.x * px0, a.y * px1);
+    *reinterpret_cast<__nv_bfloat162*>(Rt + lar(u, j)) = __floats2bfloat162_rn(r.x * L0, r.y * L1);
+    *reinterpret_cast<__nv_bfloat162*>(Kb + lkb(u, j)) = __floats2bfloat162_rn(k.x * i0, k.y * i1);
+    *reinterpret_cast<__nv_bfloat162*>(Bb + lkb(u, j)) = __floats2bfloat162_rn(b.x * i0, b.y * i1);
     px0 = L0;
     px1 = L1;
   }
@@ -99,17 +100,18 @@ __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf1
 // Phase 2 (tensor cores): the four 16x16 Gram blocks, warp gw computes block gw:
 //   0: Ga = strict(At Bb^T) (fp32)   1: Bm = strict(At Kb^T)
 //   2: Cm = lower(Rt Bb^T)           3: Dm = lower(Rt Kb^T)
-__device__ __forceinline__ void grams(const Tile& At, const Tile& Rt, const Tile& Bb,
-                                      const Tile& Kb, float (*Ga)[L + 1], Tile16& Bm, Tile16& Cm,
-                                      Tile16& Dm, int gw, int lane) {
-  const bf16* Am = (gw >> 1) ? &Rt[0][0] : &At[0][0];
-  const bf16* Bn = (gw & 1) ? &Kb[0][0] : &Bb[0][0];
+template <typename LAR, typename LKB>
+__device__ __forceinline__ void grams(const bf16* At, const bf16* Rt, LAR lar, const bf16* Bb,
+                                      const bf16* Kb, LKB lkb, float (*Ga)[L + 1], Tile16& Bm,
+                                      Tile16& Cm, Tile16& Dm, int gw, int lane) {
+  const bf16* Am = (gw >> 1) ? Rt : At;
+  const bf16* Bn = (gw & 1) ? Kb : Bb;
   float acc[2][4] = {};
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
     uint32_t a[4], b[4];
-    lda_rowmajor(a, Am, LD, 0, kk * 16, lane);
-    ldb_nk(b, Bn, LD, 0, kk * 16, lane);
+    lda_rm(a, Am, lar, 0, kk * 16, lane);
+    ldb_nk(b, Bn, lkb, 0, kk * 16, lane);
     mma16816(acc[0], a, b[0], b[1]);
     mma16816(acc[1], a, b[2], b[3]);
   }
@@ -180,60 +182,65 @@ __device__ __forceinline__ void inverse(const float (*Ga)[L + 1], float (*Tf)[L 
 }
 
 // Phase 4a: W = Ti At (warp gw: columns 16gw..16gw+15); Q = Ti Bm (warp 3).
-__device__ __forceinline__ void w_and_q(const Tile16& Ti, const Tile& At, const Tile16& Bm,
-                                        Tile& W, Tile16& Q, int gw, int lane) {
+// At is read through lar, W written through lw, Q through lq.
+template <typename LAR, typename LW, typename LQ>
+__device__ __forceinline__ void w_and_q(const Tile16& Ti, const bf16* At, LAR lar, const Tile16& Bm,
+                                        bf16* W, LW lw, bf16* Q, LQ lq, int gw, int lane) {
   uint32_t a[4], b[4];
   lda_rowmajor(a, &Ti[0][0], LDS, 0, 0, lane);
-  ldb_kn(b, &At[0][0], LD, 16 * gw, 0, lane);
+  ldb_kn(b, At, lar, 16 * gw, 0, lane);
   float acc[2][4] = {};
   mma16816(acc[0], a, b[0], b[1]);
   mma16816(acc[1], a, b[2], b[3]);
-  store_acc_bf16(&W[0][0], LD, 0, 16 * gw, acc[0], lane);
-  store_acc_bf16(&W[0][0], LD, 0, 16 * gw + 8, acc[1], lane);
+  store_acc_lay(W, lw, 0, 16 * gw, acc[0], lane);
+  store_acc_lay(W, lw, 0, 16 * gw + 8, acc[1], lane);
   if (gw == 3) {
     float qa[2][4] = {};
     ldb_kn(b, &Bm[0][0], LDS, 0, 0, lane);
     mma16816(qa[0], a, b[0], b[1]);
     mma16816(qa[1], a, b[2], b[3]);
-    store_acc_bf16(&Q[0][0], LDS, 0, 0, qa[0], lane);
-    store_acc_bf16(&Q[0][0], LDS, 0, 8, qa[1], lane);
+    store_acc_lay(Q, lq, 0, 0, qa[0], lane);
+    store_acc_lay(Q, lq, 0, 8, qa[1], lane);
   }
 }
 
-// accumulator pair initialised from a bf16 [m][n] tile at (m0, n0)
-__device__ __forceinline__ void acc_from_bf16(float (&c)[4], const bf16* tile, int ld, int m0,
+// accumulator pair initialised from a bf16 tile (through layout lay) at (m0, n0)
+template <typename Lay>
+__device__ __forceinline__ void acc_from_bf16(float (&c)[4], const bf16* tile, Lay lay, int m0,
                                               int n0, int lane) {
   const int g = lane >> 2, q = lane & 3;
   const float2 lo = __bfloat1622float2(
-      *reinterpret_cast<const __nv_bfloat162*>(tile + (m0 + g) * ld + n0 + 2 * q));
+      *reinterpret_cast<const __nv_bfloat162*>(tile + lay(m0 + g, n0 + 2 * q)));
   const float2 hi = __bfloat1622float2(
-      *reinterpret_cast<const __nv_bfloat162*>(tile + (m0 + g + 8) * ld + n0 + 2 * q));
+      *reinterpret_cast<const __nv_bfloat162*>(tile + lay(m0 + g + 8, n0 + 2 * q)));
   c[0] = lo.x; c[1] = lo.y; c[2] = hi.x; c[3] = hi.y;
 }
 
 // Phase 4b: Qy = Rt + Cm W (warp gw: columns 16gw..); P = Cm Q + Dm (warp 2).
-__device__ __forceinline__ void qy_and_p(const Tile16& Cm, const Tile& W, const Tile& Rt,
-                                         const Tile16& Q, const Tile16& Dm, Tile& Qy, Tile16& P,
-                                         int gw, int lane) {
+// W is read through lw, Rt through lar, Q through lq; Qy written through lqy, P through lp.
+template <typename LW, typename LAR, typename LQ, typename LQY, typename LP>
+__device__ __forceinline__ void qy_and_p(const Tile16& Cm, const bf16* W, LW lw, const bf16* Rt,
+                                         LAR lar, const bf16* Q, LQ lq, const Tile16& Dm, bf16* Qy,
+                                         LQY lqy, bf16* P, LP lp, int gw, int lane) {
   uint32_t a[4], b[4];
   lda_rowmajor(a, &Cm[0][0], LDS, 0, 0, lane);
-  ldb_kn(b, &W[0][0], LD, 16 * gw, 0, lane);
+  ldb_kn(b, W, lw, 16 * gw, 0, lane);
   float acc[2][4];
-  acc_from_bf16(acc[0], &Rt[0][0], LD, 0, 16 * gw, lane);
-  acc_from_bf16(acc[1], &Rt[0][0], LD, 0, 16 * gw + 8, lane);
+  acc_from_bf16(acc[0], Rt, lar, 0, 16 * gw, lane);
+  acc_from_bf16(acc[1], Rt, lar, 0, 16 * gw + 8, lane);
   mma16816(acc[0], a, b[0], b[1]);
   mma16816(acc[1], a, b[2], b[3]);
-  store_acc_bf16(&Qy[0][0], LD, 0, 16 * gw, acc[0], lane);
-  store_acc_bf16(&Qy[0][0], LD, 0, 16 * gw + 8, acc[1], lane);
+  store_acc_lay(Qy, lqy, 0, 16 * gw, acc[0], lane);
+  store_acc_lay(Qy, lqy, 0, 16 * gw + 8, acc[1], lane);
   if (gw == 2) {
     float pa[2][4];
-    acc_from_bf16(pa[0], &Dm[0][0], LDS, 0, 0, lane);
-    acc_from_bf16(pa[1], &Dm[0][0], LDS, 0, 8, lane);
-    ldb_kn(b, &Q[0][0], LDS, 0, 0, lane);
+    acc_from_bf16(pa[0], &Dm[0][0], Padded{LDS}, 0, 0, lane);
+    acc_from_bf16(pa[1], &Dm[0][0], Padded{LDS}, 0, 8, lane);
+    ldb_kn(b, Q, lq, 0, 0, lane);
     mma16816(pa[0], a, b[0], b[1]);
     mma16816(pa[1], a, b[2], b[3]);
-    store_acc_bf16(&P[0][0], LDS, 0, 0, pa[0], lane);
-    store_acc_bf16(&P[0][0], LDS, 0, 8, pa[1], lane);
+    store_acc_lay(P, lp, 0, 0, pa[0], lane);
+    store_acc_lay(P, lp, 0, 8, pa[1], lane);
   }
 }
 
