@@ -488,10 +488,10 @@ constexpr int kThreads = 128;  // one group of 4 warps per CTA, 3 CTAs per SM
 // Inputs are single-buffered and loaded in two parts: v, dy and the XRec of
 // the next item as soon as the first phase of this one has consumed them
 // (part A), r, w, k, a, b once this item's outputs, staged in place in those
-// tiles, have been read by the TMA stores (part B).
+// tiles, have been copied out (part B).
 struct alignas(1024) KGroup {
   bf16 raw[7][L * kN];  // r, w, k, a, b, v, dy as landed by TMA (1 KiB aligned);
-                        // r, w, k, a, b then hold dr, dw, dk, da, db for the TMA stores
+                        // r, w, k, a, b then hold dr, dw, dk, da, db until copied out
   rec::XRec x;
   Tile dQyb, dW2b;
   Tile At, Rt, Bb, Kb;
@@ -507,8 +507,7 @@ struct alignas(1024) KGroup {
 };
 
 struct Params {
-  CUtensorMap in[7];   // r, w, k, a, b, v, dy
-  CUtensorMap out[5];  // dr, dw, dk, da, db
+  CUtensorMap in[7];  // r, w, k, a, b, v, dy
   BwdArgs a;
   void* work;
 };
@@ -861,25 +860,31 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
         }
         *reinterpret_cast<__nv_bfloat162*>(G.raw[1] + tma::swz(t, jj)) = __floats2bfloat162_rn(dwv[0], dwv[1]);
       }
-    fence_proxy_async();  // the output tiles are read by the TMA stores below
     __syncthreads();
-    if (tid == 0) {
-      const int order[5] = {0, 1, 2, 3, 4};  // dr, dw, dk, da, db
+    {  // output tiles -> global, one 16-byte piece of each tile per thread (rows past T skipped)
+      const int t = tid >> 3, k = tid & 7;
+      const int64_t tg = c * L + t;
+      if (tg < p.g.T) {
+        const int64_t off = p.g.base(ch) + tg * p.g.tstride() + 8 * k;
+        const int o = tma::swz(t, 8 * k);
+        bf16* const dst[5] = {static_cast<bf16*>(p.dr), static_cast<bf16*>(p.dw),
+                              static_cast<bf16*>(p.dk), static_cast<bf16*>(p.da),
+                              static_cast<bf16*>(p.db)};
 #pragma unroll
-      for (int i = 0; i < 5; ++i) tma::store_tile(&P.out[i], G.raw[order[i]], 0, hh, static_cast<int>(c * L), bb);
-      bulk_commit();
-      bulk_wait_read();
-      if (next < total) {
-        issue_b(G, P, next);
-        ++issued_b;
+        for (int i = 0; i < 5; ++i)
+          *reinterpret_cast<uint4*>(dst[i] + off) = *reinterpret_cast<const uint4*>(G.raw[i] + o);
       }
+    }
+    __syncthreads();  // r, w, k, a, b tiles free
+    if (tid == 0 && next < total) {
+      issue_b(G, P, next);
+      ++issued_b;
     }
   }
   if (tid == 0) {
     // after a timeout, let loads still in flight land before the CTA exits
     if (issued_a > seen_a) mbar_wait(&G.barA, static_cast<uint32_t>((issued_a - 1) & 1));
     if (issued_b > seen_b) mbar_wait(&G.barB, static_cast<uint32_t>((issued_b - 1) & 1));
-    bulk_wait_all();
   }
 }
 
@@ -923,9 +928,6 @@ cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
   const void* src[7] = {p.r, p.w, p.k, p.a, p.b, p.v, p.dy};
   for (int t = 0; t < 7; ++t)
     if (!tma::encode_bhtn(&K.in[t], src[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
-  const void* dst[5] = {p.dr, p.dw, p.dk, p.da, p.db};
-  for (int t = 0; t < 5; ++t)
-    if (!tma::encode_bhtn(&K.out[t], dst[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;
   const size_t ksmem = sizeof(kb::KGroup) + 1024;
   e = cudaFuncSetAttribute(kb::keyside_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)ksmem);
