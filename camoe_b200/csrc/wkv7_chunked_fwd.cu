@@ -264,7 +264,8 @@ constexpr int NR = 2;  // input buffers per group
 
 struct alignas(1024) Group {
   bf16 raw[NR][5][L * kN];  // r, w, k, a, b tiles as landed by TMA (1 KiB aligned)
-  rec::KeyRec out;          // the record, written in place (swizzled layouts), then bulk-stored
+  rec::KeyRec out[2];       // the record, written in place (swizzled layouts), then bulk-stored;
+                            // two, so the store of one overlaps the next item
   Tile At, Rt;
   Tile16 Bm, Cm, Dm, Ti;
   float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
@@ -309,10 +310,10 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
     if (item >= total) break;
     const int rb = static_cast<int>(j % NR);
     bool ok = mbar_wait(&G.rawbar[rb], static_cast<uint32_t>((j / NR) & 1));
-    if (gtid == 0) bulk_wait_read();  // the previous record has left `out`
+    if (gtid == 0) bulk_wait_read_n<1>();  // the record of item j - 2 has left out[j & 1]
     ok = named_sync_and(bar_id, 128, ok);
     if (!ok) break;
-    rec::KeyRec& o = G.out;
+    rec::KeyRec& o = G.out[j & 1];
     ks::decays<true>(G.raw[rb][0], G.raw[rb][1], G.raw[rb][2], G.raw[rb][3], G.raw[rb][4],
                      &G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Kb, o.Bb, Swz64{}, o.lam, nullptr,
                      nullptr, gtid);
@@ -331,7 +332,7 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
     named_sync(bar_id, 128);
     if (gtid == 0) {
       const int64_t ch = item / P.g.nchunk, c = item % P.g.nchunk;
-      bulk_s2g(rec::keyrec(P.ckpt, ch, P.g.nchunk, c), &G.out, sizeof(rec::KeyRec));
+      bulk_s2g(rec::keyrec(P.ckpt, ch, P.g.nchunk, c), &o, sizeof(rec::KeyRec));
       bulk_commit();
     }
   }
