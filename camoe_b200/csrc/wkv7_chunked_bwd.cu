@@ -63,7 +63,6 @@ namespace vb {
 //               and SA^T rows of the XRec.
 // A producer warp streams the inputs and a store warp writes the staged rows
 // and the dv tile with bulk copies, KEEP groups in flight.
-constexpr int NS = 4;    // input slots (power of two)
 constexpr int NX = 4;    // output stages (power of two)
 constexpr int KEEP = 2;  // store groups still reading shared memory, < NX
 
@@ -71,7 +70,7 @@ template <int RB>
 struct alignas(1024) Slot {
   bf16 v[L * kN];   // TMA 128-byte swizzled, all 64 columns
   bf16 dy[L * kN];  // TMA 128-byte swizzled
-  float dsa[L][kN];
+  float dsa[L][16 * RB];  // this CTA's columns of the external dSA (no swizzle)
   rec::KeyRec k;
   bf16 S[16 * RB * kN];  // Swz64: this CTA's rows of the state at the chunk start (even chunks >= 2)
 };
@@ -93,7 +92,10 @@ struct alignas(1024) Stage {
 
 template <int RB>
 struct Smem {
-  static constexpr int NG = RB == 4 ? 2 : 4;  // G'' / dSA ring (power of two)
+  // input slots and G'' / dSA ring entries (powers of two): eight slots keep the
+  // producer far enough ahead of the state warp, which holds two at a time
+  static constexpr int NS = RB == 4 ? 4 : 8;
+  static constexpr int NG = RB == 1 ? 4 : 2;
   Slot<RB> slot[NS];
   Stage<RB> st[NX];
   GPub<RB> gp[NG];
@@ -167,6 +169,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
   Smem<RB>& sm = *reinterpret_cast<Smem<RB>*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
   constexpr int NRG = 4 / RB;  // CTAs per chain
   constexpr int NG = Smem<RB>::NG;
+  constexpr int NS = Smem<RB>::NS;
   const BwdArgs& p = P.a;
   const int tid = threadIdx.x, lane = tid & 31, warp = role_warp<RB>(tid >> 5);
   const int64_t ch = blockIdx.x / NRG;
@@ -208,13 +211,13 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
         if (!ok) break;
         const bool with_state = c == lo && lo >= 2;
         const uint32_t bytes = sizeof(rec::KeyRec) + 2 * tma::kTileBytes +
-                               (has_dsa ? L * kN * 4 : 0) + (with_state ? 2048 * RB : 0);
+                               (has_dsa ? L * 64 * RB : 0) + (with_state ? 2048 * RB : 0);
         Slot<RB>& sl = sm.slot[s];
         mbar_arrive_expect_tx(&sm.full[s], bytes);
         bulk_g2s(&sl.k, rec::keyrec(const_cast<float*>(p.ckpt), ch, nchunk, c), sizeof(rec::KeyRec), &sm.full[s]);
         tma::load_tile(sl.v, &P.map_v, hh, c * L, bb, &sm.full[s]);
         tma::load_tile(sl.dy, &P.map_dy, hh, c * L, bb, &sm.full[s]);
-        if (has_dsa) tma::load_tile(&sl.dsa[0][0], &P.map_dsa, hh, c * L, bb, &sm.full[s]);
+        if (has_dsa) tma::load_tile_at(&sl.dsa[0][0], &P.map_dsa, row0, hh, c * L, bb, &sm.full[s]);
         if (with_state)
           bulk_g2s(sl.S, rec::state_ptr(const_cast<float*>(p.ckpt), chains, ch, nchunk, lo) + row0 * 128,
                    2048 * RB, &sm.full[s]);
@@ -288,7 +291,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          dsat[nt][e] = has_dsa ? sl.dsa[8 * nt + 2 * q + (e & 1)][i0 + g + (e >= 2 ? 8 : 0)] : 0.f;
+          dsat[nt][e] = has_dsa ? sl.dsa[8 * nt + 2 * q + (e & 1)][il + g + (e >= 2 ? 8 : 0)] : 0.f;
           dso[nt][e] = 0.f;
         }
       // G'' = G diag(lam)
@@ -915,7 +918,7 @@ cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
       !tma::encode_bhtn(&V.map_dy, p.dy, p.g.B, p.g.T, p.g.H) ||
       !tma::encode_bhtn_cols(&V.map_dv, p.dv, p.g.B, p.g.T, p.g.H, 16 * rb, false))
     return cudaErrorInvalidValue;
-  if (p.dsa != nullptr && !tma::encode_bhtn_f32(&V.map_dsa, p.dsa, p.g.B, p.g.T, p.g.H))
+  if (p.dsa != nullptr && !tma::encode_bhtn_cols(&V.map_dsa, p.dsa, p.g.B, p.g.T, p.g.H, 16 * rb, true))
     return cudaErrorInvalidValue;
   cudaError_t e = rb == 1 ? vb::launch<1>(V, p.g.chains(), stream)
                 : rb == 2 ? vb::launch<2>(V, p.g.chains(), stream)

@@ -6,8 +6,9 @@
 // 16 rows of 128 bytes.  Rows past T are out of bounds in the T dimension and
 // arrive zero-filled.  The box lands in shared memory with the 128-byte
 // swizzle: the 16-byte piece k of row r is stored at piece k ^ (r & 7), which
-// keeps row-parallel shared-memory reads free of bank conflicts.  Every load
-// starts at x = 0 (16-byte aligned) and never writes global memory.
+// keeps row-parallel shared-memory reads free of bank conflicts.  Loads start
+// at x = 0 or, for column-range boxes, at a column offset whose byte offset is
+// a multiple of 16; no load writes global memory.
 #pragma once
 
 #include <cuda.h>
@@ -44,6 +45,18 @@ __device__ __forceinline__ void load_tile(void* dst_smem, const CUtensorMap* map
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(h), "r"(t0), "r"(b), "r"(mb)
+      : "memory");
+}
+
+// Same with the box starting at column n0 (n0 x element size a multiple of 16 bytes).
+__device__ __forceinline__ void load_tile_at(void* dst_smem, const CUtensorMap* map, int n0, int h,
+                                             int t0, int b, uint64_t* bar) {
+  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem));
+  const uint32_t mb = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(n0), "r"(h), "r"(t0), "r"(b), "r"(mb)
       : "memory");
 }
 
