@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 3 * RB);
+      mbar_init(&sm.empty[s], 2 * RB);  // state and dV warps (see the G warp)
     }
     for (int x = 0; x < NG; ++x) {
       mbar_init(&sm.gfull[x], RB);
@@ -334,8 +334,9 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
       sta_rm(gp.dSAT, Swz16{}, il, 0, dsaA, lane);
       __syncwarp();
       if (lane == 0) {
+        // no release of slot s here: the dV warp releases it after waiting for
+        // this publication, which follows every read of the slot above
         mbar_arrive(&sm.gfull[xg]);
-        mbar_arrive(&sm.empty[s]);
       }
       if (!next_ready && !mbar_wait(&sm.full[sn], par(lin, NS))) return;
     }

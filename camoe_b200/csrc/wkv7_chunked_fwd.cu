@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 3 * RB);
+      mbar_init(&sm.empty[s], 2 * RB);  // Y and A warps (see the S warp)
     }
     for (int x = 0; x < NP; ++x) {
       mbar_init(&sm.pfull[x], RB);
@@ -520,8 +520,9 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
       for (int kk = 0; kk < 4; ++kk) sta_rm(sm.pub[xp].S, Swz64{}, il, 16 * kk, sA[kk], lane);
       __syncwarp();
       if (lane == 0) {
+        // no release of slot s here: the Y and A warps release it after waiting
+        // for this publication, which follows every read of the slot above
         mbar_arrive(&sm.pfull[xp]);
-        mbar_arrive(&sm.empty[s]);
       }
       if (!next_ready && !mbar_wait(&sm.full[sn], par(c + 1, NS))) return;
     }
