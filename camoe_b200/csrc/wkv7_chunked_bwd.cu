@@ -18,9 +18,9 @@
 // chunk (odd chunks).
 //
 // keyside_bwd_kernel (chunk-parallel, every SM): forms the row sums above from
-// the chunk's XRec, its v, dy tiles and the next chunk's start state (for
-// dll), recomputes the chunk's key side from r, w, k, a, b and turns both into
-// dr, dw, dk, da, db:
+// the chunk's XRec and its v, dy tiles, recomputes the decays and W, Q from
+// r, w, k, a, b and the forward's triangular record (Ti, Bm, Cm), and turns
+// both into dr, dw, dk, da, db:
 //     dW += Cm^T dQy,  dQ += Cm^T dP,  dCm = lower(dQy W^T + dP Q^T)
 //     dTi = dW At^T + dQ Bm^T,  dA = strict(Ti^T dTi Ti^T),  dBm = strict(Ti^T dQ)
 //     dAt = Ti^T dW + dA Bb + dBm Kb,   dRt = dQy + dCm Bb + dP Kb
@@ -503,8 +503,9 @@ struct alignas(1024) KGroup {
   float dllp[4][kN], dll[kN];
   bf16 dPb[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
   Tile W;
-  Tile16 Bm, Cm, Dm, Ti, Q, P;
-  float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
+  Tile16 Ti, Q;
+  alignas(16) rec::TriRec tri;  // Tf = Ti in fp32, Bm, Cm: from the forward, with part B
+  float Ga[L][L + 1];           // scratch of the dA product
   bf16 dQ2b[L][LDS];
   float dTf[L][L + 1];
   uint64_t barA, barB;
@@ -538,9 +539,11 @@ __device__ __forceinline__ void issue_b(KGroup& G, const Params& P, int64_t item
   int64_t ch, c;
   int h, b;
   item_pos(P.a.g, item, ch, c, h, b);
-  mbar_arrive_expect_tx(&G.barB, 5 * tma::kTileBytes);
+  mbar_arrive_expect_tx(&G.barB, 5 * tma::kTileBytes + sizeof(rec::TriRec));
 #pragma unroll
   for (int t = 0; t < 5; ++t) tma::load_tile(G.raw[t], &P.in[t], h, static_cast<int>(c * L), b, &G.barB);
+  bulk_g2s(&G.tri, rec::trirec(const_cast<float*>(P.a.ckpt), P.a.g.chains(), ch, P.a.g.nchunk, c),
+           sizeof(rec::TriRec), &G.barB);
 }
 
 __device__ __forceinline__ uint32_t to_tf32(float x) {
@@ -667,8 +670,8 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
       issue_a(G, P, next);
       ++issued_a;
     }
-    ks::grams(&G.At[0][0], &G.Rt[0][0], Padded{LD}, &G.Bb[0][0], &G.Kb[0][0], Padded{LD}, G.Ga,
-              G.Bm, G.Cm, G.Dm, gw, lane);
+    for (int e = tid; e < L * L; e += kThreads)  // Ti = bf16(Tf) for the bf16 products
+      G.Ti[e >> 4][e & 15] = __float2bfloat16_rn(G.tri.Tf[e >> 4][e & 15]);
     {  // dll = colsum(G'' o S') / lam = colsum(G'' o S) + colsum(Bb o SA G'') + colsum(Kb o V G'')
       float v[4];  // columns j0 + 8 nt + 2q + x, as v[2 nt + x]; rows gq, gq + 8 of this lane
 #pragma unroll
@@ -693,22 +696,13 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     }
     store_acc_bf16(&G.dQyb[0][0], LD, 0, j0, dQy[0], lane);
     store_acc_bf16(&G.dQyb[0][0], LD, 0, j0 + 8, dQy[1], lane);
+    __syncwarp();
+    // dW += Cm^T dQy (own columns of dQy, written by this warp)
+    mm16<true, true, 1>(dW, &G.tri.Cm[0][0], Padded{LDS}, &G.dQyb[0][0], Padded{LD}, j0, lane);
+    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW[0], lane);
+    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
     __syncthreads();
-    // ---- inverse (warp 0) | dW += Cm^T dQy, own columns (warps 1-3) ----
-    if (gw == 0) {
-      ks::inverse(G.Ga, G.Tf, G.Mf, G.Ti, lane);
-    } else {
-      mm16<true, true, 1>(dW, &G.Cm[0][0], Padded{LDS}, &G.dQyb[0][0], Padded{LD}, j0, lane);
-      store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW[0], lane);
-      store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
-    }
-    __syncthreads();
-    if (gw == 0) {
-      mm16<true, true, 1>(dW, &G.Cm[0][0], Padded{LDS}, &G.dQyb[0][0], Padded{LD}, j0, lane);
-      store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW[0], lane);
-      store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
-    }
-    ks::w_and_q(G.Ti, &G.At[0][0], Padded{LD}, G.Bm, &G.W[0][0], Padded{LD}, &G.Q[0][0],
+    ks::w_and_q(G.Ti, &G.At[0][0], Padded{LD}, G.tri.Bm, &G.W[0][0], Padded{LD}, &G.Q[0][0],
                 Padded{LDS}, gw, lane);
     __syncthreads();  // W, Q and dW ready
 
@@ -727,13 +721,13 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
       store_acc_bf16(&G.dCmb[0][0], LDS, 0, 0, dcm[0], lane);
       store_acc_bf16(&G.dCmb[0][0], LDS, 0, 8, dcm[1], lane);
     } else if (gw == 1) {  // dQ += Cm^T dP;  dTi = dW At^T + dQ Bm^T
-      mm16<true, true, 1>(dq, &G.Cm[0][0], Padded{LDS}, &G.dPb[0][0], Padded{LDS}, 0, lane);
+      mm16<true, true, 1>(dq, &G.tri.Cm[0][0], Padded{LDS}, &G.dPb[0][0], Padded{LDS}, 0, lane);
       store_acc_bf16(&G.dQ2b[0][0], LDS, 0, 0, dq[0], lane);
       store_acc_bf16(&G.dQ2b[0][0], LDS, 0, 8, dq[1], lane);
       __syncwarp();
       float dti[2][4] = {};
       mm16<false, false, 4>(dti, &G.dW2b[0][0], Padded{LD}, &G.At[0][0], Padded{LD}, 0, lane);
-      mm16<false, false, 1>(dti, &G.dQ2b[0][0], Padded{LDS}, &G.Bm[0][0], Padded{LDS}, 0, lane);
+      mm16<false, false, 1>(dti, &G.dQ2b[0][0], Padded{LDS}, &G.tri.Bm[0][0], Padded{LDS}, 0, lane);
       store_acc_f32(&G.dTf[0][0], L + 1, 0, 0, dti[0], lane);
       store_acc_f32(&G.dTf[0][0], L + 1, 0, 8, dti[1], lane);
     }
@@ -748,11 +742,11 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
       const int n0 = gw == 0 ? 0 : 8;
       float m1[4] = {};
       mm8_tf32(m1, [&](int m, int k) { return G.dTf[m][k]; },
-               [&](int k, int n) { return G.Tf[n][k]; }, n0, lane);
-      store_acc_f32(&G.Ga[0][0], L + 1, 0, n0, m1, lane);  // Ga is free after the inverse
+               [&](int k, int n) { return G.tri.Tf[n][k]; }, n0, lane);
+      store_acc_f32(&G.Ga[0][0], L + 1, 0, n0, m1, lane);
       __syncwarp();
       float da[4] = {};
-      mm8_tf32(da, [&](int m, int k) { return G.Tf[k][m]; },
+      mm8_tf32(da, [&](int m, int k) { return G.tri.Tf[k][m]; },
                [&](int k, int n) { return G.Ga[k][n]; }, n0, lane);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {

@@ -264,11 +264,14 @@ constexpr int NR = 2;  // input buffers per group
 
 struct alignas(1024) Group {
   bf16 raw[NR][5][L * kN];  // r, w, k, a, b tiles as landed by TMA (1 KiB aligned)
-  rec::KeyRec out[2];       // the record, written in place (swizzled layouts), then bulk-stored;
-                            // two, so the store of one overlaps the next item
+  struct Out {
+    rec::KeyRec k;
+    rec::TriRec t;
+  } out[2];                 // the records, written in place, then bulk-stored; two, so
+                            // the stores of one item overlap the next
   Tile At, Rt;
-  Tile16 Bm, Cm, Dm, Ti;
-  float Ga[L][L + 1], Tf[L][L + 1], Mf[8][9];
+  Tile16 Dm, Ti;
+  float Ga[L][L + 1], Mf[8][9];
   float lam[kN];
   uint64_t rawbar[NR];
 };
@@ -313,26 +316,28 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
     if (gtid == 0) bulk_wait_read_n<1>();  // the record of item j - 2 has left out[j & 1]
     ok = named_sync_and(bar_id, 128, ok);
     if (!ok) break;
-    rec::KeyRec& o = G.out[j & 1];
+    rec::KeyRec& o = G.out[j & 1].k;
+    rec::TriRec& tr = G.out[j & 1].t;
     ks::decays<true>(G.raw[rb][0], G.raw[rb][1], G.raw[rb][2], G.raw[rb][3], G.raw[rb][4],
                      &G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Kb, o.Bb, Swz64{}, o.lam, nullptr,
                      nullptr, gtid);
     named_sync(bar_id, 128);
     if (gtid == 0 && item + NR * ngroups < total) issue(G, rb, P, item + NR * ngroups);
-    ks::grams(&G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Bb, o.Kb, Swz64{}, G.Ga, G.Bm, G.Cm, G.Dm,
+    ks::grams(&G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Bb, o.Kb, Swz64{}, G.Ga, tr.Bm, tr.Cm, G.Dm,
               gw, lane);
     named_sync(bar_id, 128);
-    if (gw == 0) ks::inverse(G.Ga, G.Tf, G.Mf, G.Ti, lane);
+    if (gw == 0) ks::inverse(G.Ga, tr.Tf, G.Mf, G.Ti, lane);
     named_sync(bar_id, 128);
-    ks::w_and_q(G.Ti, &G.At[0][0], Padded{LD}, G.Bm, o.W, Swz64{}, o.Q, Swz16{}, gw, lane);
+    ks::w_and_q(G.Ti, &G.At[0][0], Padded{LD}, tr.Bm, o.W, Swz64{}, o.Q, Swz16{}, gw, lane);
     named_sync(bar_id, 128);
-    ks::qy_and_p(G.Cm, o.W, Swz64{}, &G.Rt[0][0], Padded{LD}, o.Q, Swz16{}, G.Dm, o.Qy, Swz64{},
+    ks::qy_and_p(tr.Cm, o.W, Swz64{}, &G.Rt[0][0], Padded{LD}, o.Q, Swz16{}, G.Dm, o.Qy, Swz64{},
                  o.P, Swz16{}, gw, lane);
     fence_proxy_async();
     named_sync(bar_id, 128);
     if (gtid == 0) {
       const int64_t ch = item / P.g.nchunk, c = item % P.g.nchunk;
       bulk_s2g(rec::keyrec(P.ckpt, ch, P.g.nchunk, c), &o, sizeof(rec::KeyRec));
+      bulk_s2g(rec::trirec(P.ckpt, P.g.chains(), ch, P.g.nchunk, c), &tr, sizeof(rec::TriRec));
       bulk_commit();
     }
   }

@@ -5,12 +5,14 @@
 // Checkpoint buffer (written by the forward, read by the backward), for
 // `chains` chains of `nchunk` 16-step chunks:
 //   [chains][nchunk] KeyRec      key-side matrices of every chunk
+//   [chains][nchunk] TriRec      the chunk's triangular inverse and two Gram
+//                                blocks, for the key-side backward
 //   [chains][nstate] state       bf16 64x64 state at the start of chunks
 //                                2, 4, 6, ... (rows of 128 bytes, 16-byte
 //                                pieces swizzled by row & 7)
 // nstate = (nchunk - 1) / 2; the state at the start of odd chunks is
 // recomputed from the preceding even one, chunk 0 starts from zero.  Per
-// chunk this is 9472 + 4096 bytes, below the 16 KiB per chunk of the
+// chunk this is 9472 + 2624 + 4096 bytes, below the 16 KiB per chunk of the
 // reference's [B, H, T/16, 64, 64] fp32 checkpoint tensor.
 //
 // Backward workspace: [chains][nchunk] XRec.
@@ -30,6 +32,16 @@ struct KeyRec {
 };
 static_assert(sizeof(KeyRec) == 9472, "KeyRec layout");
 
+// Ti = (I - A)^{-1} in fp32 (upper triangle zero), Bm = strict(At Kb^T) and
+// Cm = lower(Rt Bb^T) in bf16, in the padded shared-memory layouts of the
+// key-side kernels ([16][17] fp32, [16][24] bf16), so a bulk copy lands them
+// ready for use.
+struct TriRec {
+  float Tf[16][17];
+  bf16 Bm[16][24], Cm[16][24];
+};
+static_assert(sizeof(TriRec) == 2624, "TriRec layout");
+
 // What the value-side backward hands to the key-side backward for one chunk:
 // bf16 copies of the chunk's start state S, of G'' = dL/dS' diag(lam), of SA^T
 // and dSA^T (rows = state row i).
@@ -47,7 +59,7 @@ __host__ __device__ __forceinline__ int64_t nstate(int64_t nchunk) {
   return nchunk > 0 ? (nchunk - 1) / 2 : 0;
 }
 __host__ __device__ __forceinline__ size_t ckpt_bytes(int64_t chains, int64_t nchunk) {
-  return static_cast<size_t>(chains * nchunk) * sizeof(KeyRec) +
+  return static_cast<size_t>(chains * nchunk) * (sizeof(KeyRec) + sizeof(TriRec)) +
          static_cast<size_t>(chains * nstate(nchunk)) * kStateBytes;
 }
 __host__ __device__ __forceinline__ size_t work_bytes(int64_t chains, int64_t nchunk) {
@@ -56,10 +68,15 @@ __host__ __device__ __forceinline__ size_t work_bytes(int64_t chains, int64_t nc
 __device__ __forceinline__ KeyRec* keyrec(void* ckpt, int64_t ch, int64_t nchunk, int64_t c) {
   return reinterpret_cast<KeyRec*>(ckpt) + (ch * nchunk + c);
 }
+__device__ __forceinline__ TriRec* trirec(void* ckpt, int64_t chains, int64_t ch, int64_t nchunk,
+                                          int64_t c) {
+  char* base = reinterpret_cast<char*>(ckpt) + chains * nchunk * sizeof(KeyRec);
+  return reinterpret_cast<TriRec*>(base) + (ch * nchunk + c);
+}
 // state at the start of even chunk c >= 2
 __device__ __forceinline__ char* state_ptr(void* ckpt, int64_t chains, int64_t ch,
                                            int64_t nchunk, int64_t c) {
-  char* base = reinterpret_cast<char*>(ckpt) + chains * nchunk * sizeof(KeyRec);
+  char* base = reinterpret_cast<char*>(ckpt) + chains * nchunk * (sizeof(KeyRec) + sizeof(TriRec));
   return base + (ch * nstate(nchunk) + (c / 2 - 1)) * kStateBytes;
 }
 __device__ __forceinline__ XRec* xrec(void* work, int64_t ch, int64_t nchunk, int64_t c) {

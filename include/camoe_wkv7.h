@@ -123,7 +123,7 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v,
  * camoe_wkv7_bwd, with the state checkpoint kept in a library-owned device
  * array of CAMOE_WKV7_NOALLOC_SCRATCH_BYTES instead of a caller buffer.
  * Returns CAMOE_ERR_WORKSPACE when camoe_wkv7_ckpt_bytes() plus
- * camoe_wkv7_work_bytes() of the problem exceed that size (about 2000 chains x
+ * camoe_wkv7_work_bytes() of the problem exceed that size (about 1900 chains x
  * 16-step chunks for the chunked algorithm, 4096 for the scan).  The first
  * call on a device looks up the array's address (cudaGetSymbolAddress); make
  * it before any stream capture.  All calls share the array: calls whose work
