@@ -357,9 +357,13 @@ namespace vf {
 // over 4 / RB CTAs of RB row blocks.  Per row block:
 //   S warp   carries the fp32 state through the sequence (SA and the update:
 //            the critical path).  It loads all of a chunk's operand fragments
-//            before its mma chains and publishes the chunk's start state in a
-//            small ring only after them, so no shared-memory store sits in
-//            front of its loads; it issues no fence and no output store;
+//            before its mma chains and publishes the chunk's start state next
+//            to the chunk's inputs only after them, so no shared-memory store
+//            sits in front of its loads; it issues no fence, no output store
+//            and one mbarrier wait per chunk (each costs a round trip of
+//            about 50-120 cycles): the published state lives in the chunk's
+//            input slot, which is refilled only after the Y and A warps have
+//            released it, so no "buffer free" check is needed;
 //   Y warp   reads the published start state, forms Y and stages y and (even
 //            chunks) the checkpoint copy of the start state;
 //   A warp   the same for SA (recomputed with the S warp's operands and
@@ -367,9 +371,6 @@ namespace vf {
 // A producer warp streams each chunk's KeyRec and v tile; a store warp writes
 // the staged tiles (TMA tile stores, bulk copies) with KEEP groups in flight.
 constexpr int NS = 8;    // input slots (power of two)
-constexpr int NP = 4;    // start-state ring (power of two)
-constexpr int NX = 4;    // output stages (power of two)
-constexpr int KEEP = 2;  // store groups still reading shared memory, < NX
 
 struct alignas(1024) Slot {
   bf16 v[L * kN];  // v tile as landed by TMA (1 KiB aligned)
@@ -390,10 +391,14 @@ struct alignas(1024) Stage {
 
 template <int RB>
 struct Smem {
+  // output stages (power of two) and store groups left reading shared memory (< NX)
+  static constexpr int NX = RB == 4 ? 4 : 8;
+  static constexpr int KEEP = NX / 2;
   Slot slot[NS];
   Stage<RB> st[NX];
-  Pub<RB> pub[NP];
-  uint64_t full[NS], empty[NS], pfull[NP], pfree[NP], done[NX], sempty[NX];
+  Pub<RB> pub[NS];  // start state of the chunk in slot s
+  // inputs land two chunks at a time on one barrier (consumers wait once per pair)
+  uint64_t fullp[NS / 2], empty[NS], pfull[NS], done[NX], sempty[NX];
 };
 
 struct Params {
@@ -408,6 +413,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Smem<RB>& sm = *reinterpret_cast<Smem<RB>*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
   constexpr int NRG = 4 / RB;  // CTAs per chain
+  constexpr int NX = Smem<RB>::NX, KEEP = Smem<RB>::KEEP;
   const FwdArgs& p = P.a;
   const int tid = threadIdx.x, lane = tid & 31, warp = role_warp<RB>(tid >> 5);
   const int64_t ch = blockIdx.x / NRG;
@@ -416,13 +422,10 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&sm.full[s], 1);
+      if (s < NS / 2) mbar_init(&sm.fullp[s], 1);
       mbar_init(&sm.empty[s], 2 * RB);  // Y and A warps (see the S warp)
     }
-    for (int x = 0; x < NP; ++x) {
-      mbar_init(&sm.pfull[x], RB);
-      mbar_init(&sm.pfree[x], 2 * RB);
-    }
+    for (int x = 0; x < NS; ++x) mbar_init(&sm.pfull[x], RB);
     for (int x = 0; x < NX; ++x) {
       mbar_init(&sm.done[x], 2 * RB);
       mbar_init(&sm.sempty[x], 1);
@@ -435,16 +438,26 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
   if (warp == 3 * RB) {
     // ------------------------------ producer ------------------------------
     if (lane != 0) return;
-    int c = 0;
-    for (; c < nchunk; ++c) {
-      const int s = c & (NS - 1);
-      if (c >= NS && !mbar_wait(&sm.empty[s], par(c - NS, NS))) break;
-      mbar_arrive_expect_tx(&sm.full[s], sizeof(rec::KeyRec) + tma::kTileBytes);
-      bulk_g2s(&sm.slot[s].k, rec::keyrec(p.ckpt, ch, nchunk, c), sizeof(rec::KeyRec), &sm.full[s]);
-      tma::load_tile(sm.slot[s].v, &P.map_v, hh, c * L, bb, &sm.full[s]);
+    constexpr int NB = NS / 2;
+    int pc = 0;
+    bool ok = true;
+    for (; 2 * pc < nchunk && ok; ++pc) {
+      const int c0 = 2 * pc, n = nchunk - c0 < 2 ? nchunk - c0 : 2;
+      for (int k = 0; k < n && ok; ++k) {
+        const int c = c0 + k;
+        if (c >= NS) ok = mbar_wait(&sm.empty[c & (NS - 1)], par(c - NS, NS));
+      }
+      if (!ok) break;
+      uint64_t* bar = &sm.fullp[pc & (NB - 1)];
+      mbar_arrive_expect_tx(bar, n * (sizeof(rec::KeyRec) + tma::kTileBytes));
+      for (int k = 0; k < n; ++k) {
+        const int c = c0 + k, s = c & (NS - 1);
+        bulk_g2s(&sm.slot[s].k, rec::keyrec(p.ckpt, ch, nchunk, c), sizeof(rec::KeyRec), bar);
+        tma::load_tile(sm.slot[s].v, &P.map_v, hh, c * L, bb, bar);
+      }
     }
-    if (c < nchunk)  // stopped on a timeout: let the copies in flight land
-      for (int cc = c > NS ? c - NS : 0; cc < c; ++cc) mbar_wait(&sm.full[cc & (NS - 1)], par(cc, NS));
+    if (!ok)  // stopped on a timeout: let the copies in flight land
+      for (int pp = pc > NB ? pc - NB : 0; pp < pc; ++pp) mbar_wait(&sm.fullp[pp & (NB - 1)], par(pp, NB));
     return;
   }
 
@@ -478,12 +491,9 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
     for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
-    if (nchunk > 0 && !mbar_wait(&sm.full[0], 0)) return;
+    if (nchunk > 0 && !mbar_wait(&sm.fullp[0], 0)) return;
     for (int c = 0; c < nchunk; ++c) {
-      const int s = c & (NS - 1), xp = c & (NP - 1), sn = (c + 1) & (NS - 1);
-      // barrier tests for the end of this chunk and the next one, answered while the chunk computes
-      const bool next_ready = c + 1 >= nchunk || mbar_test(&sm.full[sn], par(c + 1, NS));
-      const bool pub_ready = c < NP || mbar_test(&sm.pfree[xp], par(c - NP, NP));
+      const int s = c & (NS - 1);
       const rec::KeyRec& kr = sm.slot[s].k;
       uint32_t bW[4][4], bQ[4], bB[4][4], bK[4][4], vA[4];
       float2 lam[8];
@@ -519,27 +529,26 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
       for (int nt = 0; nt < 8; ++nt) {
         S[nt][0] *= lam[nt].x; S[nt][1] *= lam[nt].y; S[nt][2] *= lam[nt].x; S[nt][3] *= lam[nt].y;
       }
-      // publish the chunk's start state
-      if (!pub_ready && !mbar_wait(&sm.pfree[xp], par(c - NP, NP))) return;
+      // publish the chunk's start state beside its inputs
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) sta_rm(sm.pub[xp].S, Swz64{}, il, 16 * kk, sA[kk], lane);
+      for (int kk = 0; kk < 4; ++kk) sta_rm(sm.pub[s].S, Swz64{}, il, 16 * kk, sA[kk], lane);
       __syncwarp();
       if (lane == 0) {
         // no release of slot s here: the Y and A warps release it after waiting
         // for this publication, which follows every read of the slot above
-        mbar_arrive(&sm.pfull[xp]);
+        mbar_arrive(&sm.pfull[s]);
       }
-      if (!next_ready && !mbar_wait(&sm.full[sn], par(c + 1, NS))) return;
+      if (c + 1 < nchunk && ((c + 1) & 1) == 0 &&
+          !mbar_wait(&sm.fullp[((c + 1) >> 1) & (NS / 2 - 1)], par((c + 1) >> 1, NS / 2)))
+        return;
     }
     return;
   }
 
   // ------------------------------ Y warp (role 1) / A warp (role 2) ------------------------------
-  if (nchunk > 0 && !mbar_wait(&sm.full[0], 0)) return;
   for (int c = 0; c < nchunk; ++c) {
-    const int s = c & (NS - 1), xp = c & (NP - 1), x = c & (NX - 1), sn = (c + 1) & (NS - 1);
-    const bool next_ready = c + 1 >= nchunk || mbar_test(&sm.full[sn], par(c + 1, NS));
-    const bool st_ready = c < NX || mbar_test(&sm.sempty[x], par(c - NX, NX));
+    const int s = c & (NS - 1), x = c & (NX - 1);
+    if ((c & 1) == 0 && !mbar_wait(&sm.fullp[(c >> 1) & (NS / 2 - 1)], par(c >> 1, NS / 2))) return;
     const rec::KeyRec& kr = sm.slot[s].k;
     uint32_t bM[4][4], bV[4], vA[4];
     const bf16* mk = role == 1 ? kr.Qy : kr.W;
@@ -547,16 +556,14 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
     for (int kk = 0; kk < 4; ++kk) ldb_nk(bM[kk], mk, Swz64{}, 0, 16 * kk, lane);
     ldb_nk(bV, role == 1 ? kr.P : kr.Q, Swz16{}, 0, 0, lane);
     lda_cm(vA, sm.slot[s].v, Swz64{}, i0, 0, lane);
-    if (!mbar_wait(&sm.pfull[xp], par(c, NP))) return;
+    if (!mbar_wait(&sm.pfull[s], par(c, NS))) return;
     uint32_t sA[4][4];
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) lda_rm(sA[kk], sm.pub[xp].S, Swz64{}, il, 16 * kk, lane);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.pfree[xp]);
+    for (int kk = 0; kk < 4; ++kk) lda_rm(sA[kk], sm.pub[s].S, Swz64{}, il, 16 * kk, lane);
     // role 1: Y = Qy S^T + P V;  role 2: SA = W S^T + Q V (the S warp's operands and order)
     float acc[2][4];
     mma_k64_k16(acc, sA, vA, bM, bV);
-    if (!st_ready && !mbar_wait(&sm.sempty[x], par(c - NX, NX))) return;
+    if (c >= NX && !mbar_wait(&sm.sempty[x], par(c - NX, NX))) return;
     Stage<RB>& st = sm.st[x];
     if (role == 1) {
       uint32_t yA[4];
@@ -578,7 +585,6 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
       mbar_arrive(&sm.done[x]);
       mbar_arrive(&sm.empty[s]);
     }
-    if (!next_ready && !mbar_wait(&sm.full[sn], par(c + 1, NS))) return;
   }
 }
 
