@@ -370,7 +370,6 @@ namespace vf {
 //            order) and sa.
 // A producer warp streams each chunk's KeyRec and v tile; a store warp writes
 // the staged tiles (TMA tile stores, bulk copies) with KEEP groups in flight.
-constexpr int NS = 8;    // input slots (power of two)
 
 struct alignas(1024) Slot {
   bf16 v[L * kN];  // v tile as landed by TMA (1 KiB aligned)
@@ -391,8 +390,10 @@ struct alignas(1024) Stage {
 
 template <int RB>
 struct Smem {
-  // output stages (power of two) and store groups left reading shared memory (< NX)
-  static constexpr int NX = RB == 4 ? 4 : 8;
+  // input slots (even), output stages (power of two) and store groups left
+  // reading shared memory (< NX)
+  static constexpr int NS = RB == 4 ? 8 : 12;
+  static constexpr int NX = RB == 1 ? 8 : 4;
   static constexpr int KEEP = NX / 2;
   Slot slot[NS];
   Stage<RB> st[NX];
@@ -413,7 +414,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Smem<RB>& sm = *reinterpret_cast<Smem<RB>*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
   constexpr int NRG = 4 / RB;  // CTAs per chain
-  constexpr int NX = Smem<RB>::NX, KEEP = Smem<RB>::KEEP;
+  constexpr int NS = Smem<RB>::NS, NX = Smem<RB>::NX, KEEP = Smem<RB>::KEEP;
   const FwdArgs& p = P.a;
   const int tid = threadIdx.x, lane = tid & 31, warp = role_warp<RB>(tid >> 5);
   const int64_t ch = blockIdx.x / NRG;
@@ -445,19 +446,19 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
       const int c0 = 2 * pc, n = nchunk - c0 < 2 ? nchunk - c0 : 2;
       for (int k = 0; k < n && ok; ++k) {
         const int c = c0 + k;
-        if (c >= NS) ok = mbar_wait(&sm.empty[c & (NS - 1)], par(c - NS, NS));
+        if (c >= NS) ok = mbar_wait(&sm.empty[c % NS], par(c - NS, NS));
       }
       if (!ok) break;
-      uint64_t* bar = &sm.fullp[pc & (NB - 1)];
+      uint64_t* bar = &sm.fullp[pc % NB];
       mbar_arrive_expect_tx(bar, n * (sizeof(rec::KeyRec) + tma::kTileBytes));
       for (int k = 0; k < n; ++k) {
-        const int c = c0 + k, s = c & (NS - 1);
+        const int c = c0 + k, s = c % NS;
         bulk_g2s(&sm.slot[s].k, rec::keyrec(p.ckpt, ch, nchunk, c), sizeof(rec::KeyRec), bar);
         tma::load_tile(sm.slot[s].v, &P.map_v, hh, c * L, bb, bar);
       }
     }
     if (!ok)  // stopped on a timeout: let the copies in flight land
-      for (int pp = pc > NB ? pc - NB : 0; pp < pc; ++pp) mbar_wait(&sm.fullp[pp & (NB - 1)], par(pp, NB));
+      for (int pp = pc > NB ? pc - NB : 0; pp < pc; ++pp) mbar_wait(&sm.fullp[pp % NB], par(pp, NB));
     return;
   }
 
@@ -493,7 +494,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
       for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
     if (nchunk > 0 && !mbar_wait(&sm.fullp[0], 0)) return;
     for (int c = 0; c < nchunk; ++c) {
-      const int s = c & (NS - 1);
+      const int s = c % NS;
       const rec::KeyRec& kr = sm.slot[s].k;
       uint32_t bW[4][4], bQ[4], bB[4][4], bK[4][4], vA[4];
       float2 lam[8];
@@ -539,7 +540,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
         mbar_arrive(&sm.pfull[s]);
       }
       if (c + 1 < nchunk && ((c + 1) & 1) == 0 &&
-          !mbar_wait(&sm.fullp[((c + 1) >> 1) & (NS / 2 - 1)], par((c + 1) >> 1, NS / 2)))
+          !mbar_wait(&sm.fullp[((c + 1) >> 1) % (NS / 2)], par((c + 1) >> 1, NS / 2)))
         return;
     }
     return;
@@ -547,8 +548,8 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
 
   // ------------------------------ Y warp (role 1) / A warp (role 2) ------------------------------
   for (int c = 0; c < nchunk; ++c) {
-    const int s = c & (NS - 1), x = c & (NX - 1);
-    if ((c & 1) == 0 && !mbar_wait(&sm.fullp[(c >> 1) & (NS / 2 - 1)], par(c >> 1, NS / 2))) return;
+    const int s = c % NS, x = c & (NX - 1);
+    if ((c & 1) == 0 && !mbar_wait(&sm.fullp[(c >> 1) % (NS / 2)], par(c >> 1, NS / 2))) return;
     const rec::KeyRec& kr = sm.slot[s].k;
     uint32_t bM[4][4], bV[4], vA[4];
     const bf16* mk = role == 1 ? kr.Qy : kr.W;
