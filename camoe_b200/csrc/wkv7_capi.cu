@@ -70,7 +70,7 @@ void set_last_cuda_error(int e) { g_last_cuda_error = e; }
 
 extern "C" {
 
-int camoe_wkv7_version(void) { return 10000; }
+int camoe_wkv7_version(void) { return 10100; }
 
 const char* camoe_wkv7_strerror(int code) {
   switch (code) {
@@ -128,6 +128,50 @@ int camoe_wkv7_fwd(const void* r, const void* w, const void* k, const void* v, c
   p.y = y; p.sa = sa; p.ckpt = static_cast<float*>(ckpt);
   p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_fwd(p, s));
+  if (dtype == CAMOE_DTYPE_BF16) return cuda_status(camoe::scan::launch_fwd<camoe::bf16>(p, s));
+  return cuda_status(camoe::scan::launch_fwd<float>(p, s));
+}
+
+int camoe_wkv7_fwd_state(const void* r, const void* w, const void* k, const void* v,
+                         const void* a, const void* b, void* y, float* sa, const float* s0,
+                         float* s_out, int64_t B, int64_t T, int64_t H_total, int64_t h0,
+                         int64_t h_count, int N, int dtype, int algo, void* stream) {
+  int st = check_geometry(B, T, H_total, h0, h_count, N);
+  if (st != CAMOE_OK) return st;
+  int al = resolve_algo(dtype, algo);
+  if (al < 0) return CAMOE_ERR_UNSUPPORTED;
+  if (algo == CAMOE_ALGO_AUTO && T <= camoe::kChunk) al = CAMOE_ALGO_SCAN;  // decode steps
+  if (B * h_count == 0) return CAMOE_OK;
+  if ((s0 != nullptr && !aligned16(s0)) || (s_out != nullptr && !aligned16(s_out)))
+    return CAMOE_ERR_ALIGNMENT;
+  if (s0 != nullptr && s_out != nullptr && s0 != s_out) {
+    // the two [B, H_total, N, N] arrays must be the same or disjoint
+    const size_t bytes = static_cast<size_t>(B * H_total) * camoe::kN * camoe::kN * sizeof(float);
+    const uintptr_t x = reinterpret_cast<uintptr_t>(s0), z = reinterpret_cast<uintptr_t>(s_out);
+    if (x < z + bytes && z < x + bytes) return CAMOE_ERR_INVALID_ARG;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T == 0) {  // no step: the final state is the start state
+    if (s_out == nullptr || s_out == s0) return CAMOE_OK;
+    const size_t nn = static_cast<size_t>(camoe::kN) * camoe::kN * sizeof(float);
+    float* dst = s_out + h0 * camoe::kN * camoe::kN;
+    const size_t pitch = static_cast<size_t>(H_total) * nn, width = static_cast<size_t>(h_count) * nn;
+    if (s0 == nullptr)
+      return cuda_status(cudaMemset2DAsync(dst, pitch, 0, width, static_cast<size_t>(B), s));
+    return cuda_status(cudaMemcpy2DAsync(dst, pitch, s0 + h0 * camoe::kN * camoe::kN, pitch, width,
+                                         static_cast<size_t>(B), cudaMemcpyDeviceToDevice, s));
+  }
+  const void* ptrs[] = {r, w, k, v, a, b, y, sa};
+  for (const void* p : ptrs) {
+    if (p == nullptr) return CAMOE_ERR_INVALID_ARG;
+    if (!aligned16(p)) return CAMOE_ERR_ALIGNMENT;
+  }
+  camoe::FwdArgs p;
+  p.r = r; p.w = w; p.k = k; p.v = v; p.a = a; p.b = b;
+  p.y = y; p.sa = sa; p.ckpt = nullptr;
+  p.s0 = s0; p.sT = s_out;
+  p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk};
   if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_fwd(p, s));
   if (dtype == CAMOE_DTYPE_BF16) return cuda_status(camoe::scan::launch_fwd<camoe::bf16>(p, s));
   return cuda_status(camoe::scan::launch_fwd<float>(p, s));

@@ -122,11 +122,21 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_fwd_kernel(const __grid_c
   if (warp < 4) {
     // ------------------------------ value warps ------------------------------
     const int wq = warp, g = lane >> 2, q = lane & 3, i0 = 16 * wq;
-    float S[8][4];
+    float S[8][4];  // element (i0 + g (+8 for e >= 2), 8 nt + 2q + (e & 1))
+    if (p.s0 != nullptr) {
+      const float* s0 = p.s0 + p.g.state_off(ch) + (i0 + g) * kN + 2 * q;
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 8; ++nt) {
+        const float2 lo = *reinterpret_cast<const float2*>(s0 + 8 * nt);
+        const float2 hi = *reinterpret_cast<const float2*>(s0 + 8 * kN + 8 * nt);
+        S[nt][0] = lo.x; S[nt][1] = lo.y; S[nt][2] = hi.x; S[nt][3] = hi.y;
+      }
+    } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
+    }
     bf16* yp = static_cast<bf16*>(p.y);
     for (int64_t c = 0; c < nchunk; ++c) {
       const int s = static_cast<int>(c % NS);
@@ -188,6 +198,14 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_fwd_kernel(const __grid_c
           }
         }
     }
+    if (p.sT != nullptr) {  // after a timed-out wait this is the state reached so far
+      float* sT = p.sT + p.g.state_off(ch) + (i0 + g) * kN + 2 * q;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        *reinterpret_cast<float2*>(sT + 8 * nt) = make_float2(S[nt][0], S[nt][1]);
+        *reinterpret_cast<float2*>(sT + 8 * kN + 8 * nt) = make_float2(S[nt][2], S[nt][3]);
+      }
+    }
   } else {
     // ------------------------------ key groups ------------------------------
     const int grp = (warp - 4) >> 2, gw = (warp - 4) & 3, gtid = tid - 128 - 128 * grp;
@@ -208,8 +226,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_fwd_kernel(const __grid_c
       if (ok && c >= NS) ok = mbar_wait(&sm.empty[s], static_cast<uint32_t>((c / NS - 1) & 1));
       ok = named_sync_and(bar_id, 128, ok);  // the group leaves together on a timeout
       if (!ok) break;
+      const int nvalid = T - c * L < L ? static_cast<int>(T - c * L) : L;
       ks::decays<true>(raw[R_R], raw[R_W], raw[R_K], raw[R_A], raw[R_B], &sc.At[0][0], &sc.Rt[0][0],
-                       Padded{LD}, &sl.Kb[0][0], &sl.Bb[0][0], Padded{LD}, sl.lam, nullptr, nullptr, gtid);
+                       Padded{LD}, &sl.Kb[0][0], &sl.Bb[0][0], Padded{LD}, sl.lam, nullptr, nullptr, gtid,
+                       nvalid);
       {  // v tile -> slot, un-swizzled (one 16-byte piece per thread)
         const int u = gtid >> 3, part = gtid & 7;
         *reinterpret_cast<uint4*>(&sl.v[u][part * 8]) =

@@ -32,6 +32,10 @@ struct Geom {
   }
   // stride between consecutive time steps of one chain, in elements
   __host__ __device__ int64_t tstride() const { return H * kN; }
+  // offset of element (0, 0) of chain `ch`'s N x N state in a [B, H, N, N] array
+  __host__ __device__ int64_t state_off(int64_t ch) const {
+    return ((ch / hc) * H + h0 + ch % hc) * kN * kN;
+  }
 };
 
 struct FwdArgs {
@@ -40,6 +44,12 @@ struct FwdArgs {
   float* sa;
   float* ckpt;  // may be null
   Geom g;
+  // start state (null = zero) and final state (null = not stored) of every
+  // chain, fp32 [B, H, N, N] with element ((b*H + h)*N + i)*N + j = S[i][j];
+  // sT may equal s0 (each element is read before it is overwritten, by the
+  // same thread).  Only the inference forward (ckpt == null) takes them.
+  const float* s0 = nullptr;
+  float* sT = nullptr;
 };
 
 struct BwdArgs {

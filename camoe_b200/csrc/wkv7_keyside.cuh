@@ -30,7 +30,9 @@ using Tile16 = bf16[L][LDS];
 // lam (the decay over the whole chunk) = Lam of the last step.
 // Thread layout: p = gtid / 4, tq = gtid % 4 (quarter lanes adjacent).
 // With `cum_out`/`sig_out` non-null, the fp32 prefixes and sigmoids are kept
-// for the backward.  The input tiles are 16 x 64 bf16, either row-major with
+// for the backward.  Steps u >= nvalid (past the end of a sequence whose
+// length is not a multiple of L) get lw = 0, so lam is the decay over the
+// steps that exist and a final state taken after the chunk is exact.  The input tiles are 16 x 64 bf16, either row-major with
 // stride LD (SWZ = false) or as landed by a swizzled TMA load (SWZ = true).
 template <bool SWZ>
 __device__ __forceinline__ int raw_idx(int u, int j) {
@@ -42,7 +44,7 @@ template <bool SWZ, typename LAR, typename LKB>
 __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf16* kk,
                                        const bf16* aa, const bf16* bb, bf16* At, bf16* Rt, LAR lar,
                                        bf16* Kb, bf16* Bb, LKB lkb, float* lam, float (*cum_out)[kN],
-                                       float (*sig_out)[kN], int gtid) {
+                                       float (*sig_out)[kN], int gtid, int nvalid = L) {
   const int p = gtid >> 2, tq = gtid & 3, j = 2 * p;
   const int lane = gtid & 31;
   float lw0[4], lw1[4], c0[4], c1[4];
@@ -54,8 +56,8 @@ __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf1
     const float s0 = __fdividef(1.0f, 1.0f + __expf(-x.x));
     const float s1 = __fdividef(1.0f, 1.0f + __expf(-x.y));
     if (sig_out != nullptr) *reinterpret_cast<float2*>(&sig_out[u][j]) = make_float2(s0, s1);
-    lw0[e] = kWScale * s0;
-    lw1[e] = kWScale * s1;
+    lw0[e] = u < nvalid ? kWScale * s0 : 0.f;
+    lw1[e] = u < nvalid ? kWScale * s1 : 0.f;
     run0 += lw0[e];
     run1 += lw1[e];
     c0[e] = run0;

@@ -74,18 +74,30 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
   const int64_t nchunk = p.g.nchunk;
 
   float S[16];
+  if (p.s0 != nullptr) {  // start state: row i, columns 16q..16q+15
+    const float4* src = reinterpret_cast<const float4*>(p.s0 + p.g.state_off(ch) + i * kN + q * 16);
 #pragma unroll
-  for (int jj = 0; jj < 16; ++jj) S[jj] = 0.f;
+    for (int m = 0; m < 4; ++m) {
+      const float4 x = src[m];
+      S[4 * m] = x.x; S[4 * m + 1] = x.y; S[4 * m + 2] = x.z; S[4 * m + 3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) S[jj] = 0.f;
+  }
 
   fwd_issue(sm, 0, p, ch, 0, rg);
   cp_async_commit();
   for (int64_t c = 0; c < nchunk; ++c) {
     const int buf = c & 1;
+    // steps of this chunk inside the sequence (the rest are never applied,
+    // so the final state is the state after step T - 1)
+    const int nu = p.g.T - c * kChunk < kChunk ? static_cast<int>(p.g.T - c * kChunk) : kChunk;
     if (c + 1 < nchunk) fwd_issue(sm, buf ^ 1, p, ch, c + 1, rg);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    for (int idx = tid; idx < kChunk * kN; idx += kFwdThreads) {
+    for (int idx = tid; idx < nu * kN; idx += kFwdThreads) {
       const int u = idx / kN, j = idx % kN;
       sm.r[u][j] = to_f32(sm.raw[buf][0][u][j]);
       sm.w[u][j] = expf(kWScale / (1.0f + expf(-to_f32(sm.raw[buf][1][u][j]))));
@@ -93,7 +105,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
       sm.a[u][j] = to_f32(sm.raw[buf][3][u][j]);
       sm.b[u][j] = to_f32(sm.raw[buf][4][u][j]);
     }
-    for (int idx = tid; idx < kChunk * kRows; idx += kFwdThreads)
+    for (int idx = tid; idx < nu * kRows; idx += kFwdThreads)
       sm.v[idx / kRows][idx % kRows] = to_f32(sm.rawv[buf][idx / kRows][idx % kRows]);
     __syncthreads();
 
@@ -104,7 +116,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
     }
 
 #pragma unroll 1
-    for (int u = 0; u < kChunk; ++u) {
+    for (int u = 0; u < nu; ++u) {
       const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * 16]);
       float s0 = 0.f, s1 = 0.f;
 #pragma unroll
@@ -156,6 +168,143 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
         *reinterpret_cast<float4*>(p.sa + o) = *reinterpret_cast<const float4*>(&sm.sa[u][part * 4]);
       }
     }
+  }
+  if (p.sT != nullptr) {
+    float4* dst = reinterpret_cast<float4*>(p.sT + p.g.state_off(ch) + i * kN + q * 16);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) dst[m] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// decode step (step_fwd_kernel): a few steps from a stored state, no
+// checkpoint.  The cost is the state itself (16 KiB read and 16 KiB written
+// per chain), so the kernel is laid out for HBM: 4 CTAs of 128 threads per
+// chain (16 rows each), 8 threads per row, thread o of row i holding
+// S[i][4o + 32m .. 4o + 32m + 3] for m = 0, 1.  Each warp load or store
+// instruction then moves 4 whole 128-byte lines (4 rows x 8 threads x 16 B),
+// and the row sums (sa = S a, y = S r) take three xor-shuffles.  Per step the
+// CTA stages r, decay(w), k, a, b and its 16 values of v in shared memory
+// (double-buffered, one barrier per step), the next step's inputs already
+// loaded into registers; the arithmetic is the scan's
+// (camoe/cuda/rwkv7_clampw.cu:48-63).
+
+constexpr int kStepRows = 16;
+constexpr int kStepTpr = 8;                          // threads per row
+constexpr int kStepThreads = kStepRows * kStepTpr;   // 128
+constexpr int kStepCtas = kN / kStepRows;            // CTAs per chain
+constexpr int kStepLoaders = 5 * kN / 4 + kStepRows / 4;  // threads that load 4 inputs each (84)
+
+// thread tid < 80 loads 4 consecutive columns of r, w, k, a, b (tensor tid / 16);
+// threads 80..83 load 4 consecutive rows of this CTA's slice of v.  `src` is
+// the thread's element at step 0; step t is t * tstride further.
+template <typename Tin>
+__device__ __forceinline__ void step_load(float (&x)[4], const Tin* src) {
+  if constexpr (sizeof(Tin) == 4) {
+    const float4 v = *reinterpret_cast<const float4*>(src);
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(src);
+    const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    x[0] = lo.x; x[1] = lo.y; x[2] = hi.x; x[3] = hi.y;
+  }
+}
+
+template <typename Tin>
+__global__ void __launch_bounds__(kStepThreads, 12) step_fwd_kernel(FwdArgs p) {
+  __shared__ __align__(16) float xin[2][5][kN];  // r, decay, k, a, b
+  __shared__ __align__(16) float vin[2][kStepRows];
+  const int tid = threadIdx.x, rl = tid >> 3, o = tid & 7;
+  const unsigned ch = blockIdx.x / kStepCtas, hc = static_cast<unsigned>(p.g.hc);
+  const int rg = static_cast<int>(blockIdx.x % kStepCtas);
+  const int i = rg * kStepRows + rl;
+  const int64_t T = p.g.T, ts = p.g.tstride();
+  // chain (b, h): one 32-bit division (the grid is below 2^31 chains)
+  const unsigned bb = ch / hc;
+  const int64_t hh = p.g.h0 + (ch - bb * hc);
+  const int64_t cbase = (static_cast<int64_t>(bb) * T * p.g.H + hh) * kN;  // element (t=0, i=0)
+  const int64_t srow = ((static_cast<int64_t>(bb) * p.g.H + hh) * kN + i) * kN + 4 * o;
+
+  const Tin* src = nullptr;
+  if (tid < kStepLoaders) {
+    const int tens = tid < 80 ? tid >> 4 : 5;
+    const int col = tid < 80 ? 4 * (tid & 15) : rg * kStepRows + 4 * (tid - 80);
+    const void* base = tens == 0 ? p.r : tens == 1 ? p.w : tens == 2 ? p.k : tens == 3 ? p.a
+                     : tens == 4 ? p.b : p.v;
+    src = static_cast<const Tin*>(base) + cbase + col;
+  }
+  float x[4] = {0.f, 0.f, 0.f, 0.f};
+  if (src != nullptr) step_load<Tin>(x, src);
+  float S[8];  // S[4m + e] = S[i][4o + 32m + e]
+  if (p.s0 != nullptr) {
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const float4 v = *reinterpret_cast<const float4*>(p.s0 + srow + 32 * m);
+      S[4 * m] = v.x; S[4 * m + 1] = v.y; S[4 * m + 2] = v.z; S[4 * m + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) S[e] = 0.f;
+  }
+  Tin* yo = static_cast<Tin*>(p.y) + cbase + i;
+  float* sao = p.sa + cbase + i;
+
+  for (int64_t t = 0; t < T; ++t) {
+    const int buf = static_cast<int>(t & 1);
+    if (tid < 80) {
+      const int tens = tid >> 4, col = 4 * (tid & 15);
+      if (tens == 1) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = expf(kWScale / (1.0f + expf(-x[e])));
+      }
+      *reinterpret_cast<float4*>(&xin[buf][tens][col]) = make_float4(x[0], x[1], x[2], x[3]);
+    } else if (tid < kStepLoaders) {
+      *reinterpret_cast<float4*>(&vin[buf][4 * (tid - 80)]) = make_float4(x[0], x[1], x[2], x[3]);
+    }
+    __syncthreads();
+    if (src != nullptr && t + 1 < T) step_load<Tin>(x, src + (t + 1) * ts);
+
+    float sa = 0.f, y0 = 0.f, y1 = 0.f;
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const float4 av = *reinterpret_cast<const float4*>(&xin[buf][3][4 * o + 32 * m]);
+      sa += S[4 * m] * av.x + S[4 * m + 1] * av.y + S[4 * m + 2] * av.z + S[4 * m + 3] * av.w;
+    }
+    sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+    sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+    sa += __shfl_xor_sync(0xffffffffu, sa, 4);
+    const float vi = vin[buf][rl];
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const int c = 4 * o + 32 * m;
+      const float4 wv = *reinterpret_cast<const float4*>(&xin[buf][1][c]);
+      const float4 bv = *reinterpret_cast<const float4*>(&xin[buf][4][c]);
+      const float4 kv = *reinterpret_cast<const float4*>(&xin[buf][2][c]);
+      const float4 rv = *reinterpret_cast<const float4*>(&xin[buf][0][c]);
+      const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
+      const float ka[4] = {kv.x, kv.y, kv.z, kv.w}, ra[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float sv = S[4 * m + e] * wa[e] + (sa * ba[e] + ka[e] * vi);
+        S[4 * m + e] = sv;
+        if (e & 1) y1 += sv * ra[e]; else y0 += sv * ra[e];
+      }
+    }
+    float y = y0 + y1;
+    y += __shfl_xor_sync(0xffffffffu, y, 1);
+    y += __shfl_xor_sync(0xffffffffu, y, 2);
+    y += __shfl_xor_sync(0xffffffffu, y, 4);
+    if (o == 0) {
+      yo[t * ts] = from_f32<Tin>(y);
+      sao[t * ts] = sa;
+    }
+  }
+  if (p.sT != nullptr) {
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+      *reinterpret_cast<float4*>(p.sT + srow + 32 * m) =
+          make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
   }
 }
 
@@ -432,6 +581,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdArgs p) {
 
 template <typename Tin>
 cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
+  if (p.ckpt == nullptr && p.g.T <= kChunk) {  // a few steps without checkpoint: decode
+    step_fwd_kernel<Tin><<<(unsigned)(p.g.chains() * kStepCtas), kStepThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+  }
   const size_t smem = sizeof(FwdSmem<Tin>);
   cudaError_t e = cudaFuncSetAttribute(scan_fwd_kernel<Tin>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

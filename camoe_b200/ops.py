@@ -90,6 +90,58 @@ def wkv7_forward(r, w, k, v, a, b, *, algo="auto", save_ckpt: bool = True, h0: i
     return y, sa, ckpt
 
 
+def _check_state(s, B, H, device, name):
+    if s.dtype != torch.float32 or tuple(s.shape) != (B, H, HEAD_SIZE, HEAD_SIZE) \
+            or not s.is_contiguous() or s.device != device:
+        raise ValueError(f"{name} must be a contiguous float32 [B, H, {HEAD_SIZE}, {HEAD_SIZE}] "
+                         f"tensor on {device}, got {tuple(s.shape)} {s.dtype} on {s.device}")
+
+
+def wkv7_forward_state(r, w, k, v, a, b, state=None, *, algo="auto", h0: int = 0,
+                       h_count: int | None = None, y=None, sa=None, out_state=None,
+                       inplace: bool = False, zero_rest=False):
+    """Stateful inference forward: every chain starts from ``state`` ([B, H, 64, 64]
+    fp32, element [b, h, i, j] = S[i][j] with i the value index; None = zero) and
+    its state after the last step is returned.  With ``inplace`` the final state
+    overwrites ``state``; otherwise it goes to ``out_state`` (allocated when not
+    given).  Any T.  Returns (y, sa, final_state)."""
+    _check_inputs((r, w, k, v, a, b), "rwkvab")
+    B, T, H, N = r.shape
+    hc = H - h0 if h_count is None else h_count
+    if state is not None:
+        _check_state(state, B, H, r.device, "state")
+    if inplace:
+        if state is None:
+            raise ValueError("inplace needs a state tensor")
+        out_state = state
+    elif out_state is None:
+        out_state = (torch.zeros if zero_rest else torch.empty)(B, H, N, N, dtype=torch.float32,
+                                                                device=r.device)
+    else:
+        _check_state(out_state, B, H, r.device, "out_state")
+    alloc = torch.zeros if zero_rest else torch.empty
+    if y is None:
+        y = alloc(B, T, H, N, dtype=r.dtype, device=r.device)
+    if sa is None:
+        sa = alloc(B, T, H, N, dtype=torch.float32, device=r.device)
+    st = _lib.lib().camoe_wkv7_fwd_state(
+        r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(),
+        y.data_ptr(), sa.data_ptr(), None if state is None else state.data_ptr(),
+        out_state.data_ptr(), B, T, H, h0, hc, N, dtype_code(r.dtype), algo_code(algo),
+        _stream_ptr(r.device))
+    check(st)
+    return y, sa, out_state
+
+
+def wkv7_decode_step(r, w, k, v, a, b, state):
+    """One generated token for every sequence: inputs [B, H, 64] (or [B, 1, H, 64]),
+    ``state`` [B, H, 64, 64] fp32 updated in place.  Returns (y, sa) shaped like r."""
+    shape = r.shape
+    xs = [x.reshape(x.shape[0], 1, x.shape[-2], x.shape[-1]) for x in (r, w, k, v, a, b)]
+    y, sa, _ = wkv7_forward_state(*xs, state, inplace=True)
+    return y.reshape(shape), sa.reshape(shape)
+
+
 def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
                   h_count: int | None = None, grads=None, zero_rest=False, work=None):
     """Backward.  ``dsa`` (fp32) may be None.  Returns (dr, dw, dk, dv, da, db).

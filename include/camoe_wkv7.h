@@ -111,6 +111,25 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v,
                    int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
                    int algo, void* stream);
 
+/* Stateful forward, for inference and decoding: camoe_wkv7_fwd without a
+ * checkpoint, but every chain starts from the state s0 instead of zero and
+ * its state after step T-1 is written to s_out.  s0 and s_out are fp32
+ * [B, H_total, N, N] arrays, element ((b*H_total + h)*N + i)*N + j = S[i][j]
+ * (i the value index, j the key index); the heads [h0, h0 + h_count) are
+ * read and written in place.  s0 = NULL starts from the zero state (then
+ * y and sa equal camoe_wkv7_fwd's), s_out = NULL skips the store, and
+ * s_out == s0 updates the state in place (a partial overlap is
+ * CAMOE_ERR_INVALID_ARG).  Any T >= 0: a forward over steps [0, T1) followed
+ * by one over [T1, T) from its s_out gives the y and sa of one forward over
+ * [0, T).  AUTO runs the per-step decode kernel for T <= 16 (any dtype),
+ * else CHUNKED for bf16 and SCAN for fp32.  No gradient flows through the
+ * states.  No counterpart in the reference, which recomputes the whole
+ * prefix for every generated token (eval.py:212, camoe/wrapper.py:203-223). */
+int camoe_wkv7_fwd_state(const void* r, const void* w, const void* k, const void* v,
+                         const void* a, const void* b, void* y, float* sa, const float* s0,
+                         float* s_out, int64_t B, int64_t T, int64_t H_total, int64_t h0,
+                         int64_t h_count, int N, int dtype, int algo, void* stream);
+
 /* Size of the library-owned checkpoint scratch used by
  * camoe_wkv7_fwd_bwd_noalloc (64 MiB per GPU that loads the library). */
 #define CAMOE_WKV7_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)

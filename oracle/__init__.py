@@ -6,7 +6,7 @@ CPU baseline).  The ``camoe_b200`` product path never imports it.
 
 Contents:
 
-* ``fwd`` / ``bwd`` — ctypes bindings of ``wkv7_oracle.c`` (a plain-C
+* ``fwd`` / ``bwd`` / ``fwd_state`` — ctypes bindings of ``wkv7_oracle.c`` (a plain-C
   restatement of ``camoe/backbone.py:264-294`` and of the gradient formulas of
   ``camoe/cuda/rwkv7_clampw.cu:83-170``), in float64 (ground truth) or float32
   (reference precision), OpenMP over (batch, head) chains.
@@ -54,6 +54,9 @@ def _load():
         g = getattr(lib, f"wkv7_oracle_bwd_{suf}")
         g.argtypes = [i64] * 5 + [fp] * 14 + [ci]
         g.restype = ci
+        h = getattr(lib, f"wkv7_oracle_fwd_state_{suf}")
+        h.argtypes = [i64] * 4 + [fp] * 10 + [ci]
+        h.restype = ci
     lib.wkv7_oracle_decay.argtypes = [ctypes.c_double]
     lib.wkv7_oracle_decay.restype = ctypes.c_double
     _lib = lib
@@ -87,6 +90,22 @@ def fwd(r, w, k, v, a, b, precision: str = "f64", threads: int | None = None):
     return y, sa
 
 
+def fwd_state(r, w, k, v, a, b, s0=None, precision: str = "f64", threads: int | None = None):
+    """Forward from the start state ``s0`` ([B,H,N,N], element [b,h,i,j] = S[i][j]
+    with i the value index; None = zero).  Returns (y, sa, s_final) float32."""
+    r, w, k, v, a, b = (_f32(x) for x in (r, w, k, v, a, b))
+    B, T, H, N = r.shape
+    s0 = None if s0 is None else _f32(s0).reshape(B, H, N, N)
+    y = np.empty_like(r)
+    sa = np.empty_like(r)
+    sT = np.empty((B, H, N, N), dtype=np.float32)
+    fn = getattr(_load(), f"wkv7_oracle_fwd_state_{precision}")
+    rc = fn(B, T, H, N, *map(_ptr, (r, w, k, v, a, b, s0, y, sa, sT)), threads or default_threads())
+    if rc != 0:
+        raise RuntimeError(f"oracle stateful forward failed with code {rc}")
+    return y, sa, sT
+
+
 def bwd(r, w, k, v, a, b, dy, dsa=None, precision: str = "f64", ckpt: int = 64,
         threads: int | None = None):
     """Exact gradients (dr, dw, dk, dv, da, db) of sum(dy*y) + sum(dsa*sa), float32."""
@@ -106,10 +125,11 @@ def decay(w_in: float) -> float:
     return _load().wkv7_oracle_decay(float(w_in))
 
 
-def torch_reference(r, w, k, v, a, b, dy=None, dsa=None):
+def torch_reference(r, w, k, v, a, b, dy=None, dsa=None, s0=None):
     """Float64 torch restatement of camoe/backbone.py:264-294 returning (y, sa);
     with dy given, also the six input gradients from autograd (sa-gradient dsa
-    optional).  Small sizes only: it loops over time in Python."""
+    optional).  ``s0`` ([B,H,N,N], default zero) is the start state.  Small
+    sizes only: it loops over time in Python."""
     import torch
 
     xs = [torch.as_tensor(np.asarray(_f32(x)), dtype=torch.float64).requires_grad_(dy is not None)
@@ -117,7 +137,8 @@ def torch_reference(r, w, k, v, a, b, dy=None, dsa=None):
     rr, ww, kk, vv, aa, bb = xs
     B, T, H, N = rr.shape
     dec = torch.exp(W_SCALE / (1.0 + torch.exp(-ww)))
-    S = torch.zeros(B, H, N, N, dtype=torch.float64)
+    S = torch.zeros(B, H, N, N, dtype=torch.float64) if s0 is None else \
+        torch.as_tensor(_f32(s0), dtype=torch.float64).reshape(B, H, N, N)
     ys, sas = [], []
     for t in range(T):
         sa = (S * aa[:, t].unsqueeze(-2)).sum(-1)

@@ -43,9 +43,11 @@
 #define DEFINE_ORACLE(REAL, SUF, EXPF)                                                        \
 static void chain_fwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t b, int64_t h,           \
         const float* r, const float* wi, const float* k, const float* v, const float* a,      \
-        const float* bb, float* y, float* sa_out, REAL* S, REAL* sa, REAL* wv)                \
+        const float* bb, float* y, float* sa_out, REAL* S, REAL* sa, REAL* wv,                \
+        const float* s0, float* sT)                                                            \
 {                                                                                              \
-    memset(S, 0, sizeof(REAL) * N * N);                                                        \
+    if (s0) for (int64_t e = 0; e < N * N; ++e) S[e] = (REAL)s0[e];                            \
+    else memset(S, 0, sizeof(REAL) * N * N);                                                   \
     for (int64_t t = 0; t < T; ++t) {                                                          \
         const int64_t base = ((b * T + t) * H + h) * N;                                        \
         for (int64_t j = 0; j < N; ++j)                                                        \
@@ -69,6 +71,7 @@ static void chain_fwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t b, int64_t 
             if (sa_out) sa_out[base + i] = (float)sai;                                         \
         }                                                                                      \
     }                                                                                          \
+    if (sT) for (int64_t e = 0; e < N * N; ++e) sT[e] = (float)S[e];                           \
 }                                                                                              \
                                                                                                \
 /* one forward step S <- S diag(w) + sa b^T + v k^T, returning sa = S a */                     \
@@ -203,7 +206,32 @@ int wkv7_oracle_fwd_##SUF(int64_t B, int64_t T, int64_t H, int64_t N,           
         REAL* S = (REAL*)malloc(sizeof(REAL) * (size_t)N * N);                                 \
         REAL* sab = (REAL*)malloc(sizeof(REAL) * (size_t)N * 2);                               \
         if (!S || !sab) { free(S); free(sab); err = ORACLE_ERR_NOMEM; continue; }              \
-        chain_fwd_##SUF(T, H, N, c / H, c % H, r, w, k, v, a, b, y, sa, S, sab, sab + N);      \
+        chain_fwd_##SUF(T, H, N, c / H, c % H, r, w, k, v, a, b, y, sa, S, sab, sab + N,       \
+                        NULL, NULL);                                                           \
+        free(S); free(sab);                                                                    \
+    }                                                                                          \
+    return err;                                                                                \
+}                                                                                              \
+                                                                                               \
+/* Forward from a given start state: s0 (NULL = zero) and the final state sT  \
+ * (NULL = not returned) are [B, H, N, N] with element ((b*H + h)*N + i)*N + j \
+ * = S[i][j].  The reference has no stateful call; this is the same         \
+ * recurrence with S_{-1} = s0 instead of 0, which makes a forward over     \
+ * [0, T1) followed by one over [T1, T) from its final state equal a single \
+ * forward over [0, T). */                                                     \
+int wkv7_oracle_fwd_state_##SUF(int64_t B, int64_t T, int64_t H, int64_t N,                   \
+        const float* r, const float* w, const float* k, const float* v, const float* a,       \
+        const float* b, const float* s0, float* y, float* sa, float* sT, int nthreads)         \
+{                                                                                              \
+    if (B < 0 || T < 0 || H < 0 || N <= 0) return ORACLE_ERR_ARG;                              \
+    int err = ORACLE_OK;                                                                       \
+    _Pragma("omp parallel for schedule(dynamic) num_threads(nthreads > 0 ? nthreads : 1)")     \
+    for (int64_t c = 0; c < B * H; ++c) {                                                      \
+        REAL* S = (REAL*)malloc(sizeof(REAL) * (size_t)N * N);                                 \
+        REAL* sab = (REAL*)malloc(sizeof(REAL) * (size_t)N * 2);                               \
+        if (!S || !sab) { free(S); free(sab); err = ORACLE_ERR_NOMEM; continue; }              \
+        chain_fwd_##SUF(T, H, N, c / H, c % H, r, w, k, v, a, b, y, sa, S, sab, sab + N,       \
+                        s0 ? s0 + c * N * N : NULL, sT ? sT + c * N * N : NULL);               \
         free(S); free(sab);                                                                    \
     }                                                                                          \
     return err;                                                                                \

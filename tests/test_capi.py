@@ -105,6 +105,33 @@ def test_bwd_argument_errors_need_no_device():
     assert bwd(B=0) == _lib.OK
 
 
+def test_fwd_state_argument_errors_need_no_device():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+
+    def fst(s0=ctypes.c_void_p(1 << 20), s_out=ctypes.c_void_p(1 << 30), ptr=p, **kw):
+        g = dict(B=2, T=32, H=4, h0=0, hc=4, N=64, dtype=0, algo=0)
+        g.update(kw)
+        return lib.camoe_wkv7_fwd_state(ptr, ptr, ptr, ptr, ptr, ptr, ptr, ptr, s0, s_out,
+                                        g["B"], g["T"], g["H"], g["h0"], g["hc"], g["N"],
+                                        g["dtype"], g["algo"], None)
+
+    assert fst(N=32) == _lib.ERR_UNSUPPORTED
+    assert fst(dtype=1, algo=2) == _lib.ERR_UNSUPPORTED
+    assert fst(H=2, h0=1, hc=2) == _lib.ERR_INVALID_ARG
+    assert fst(s0=ctypes.c_void_p(1 << 20 | 8)) == _lib.ERR_ALIGNMENT
+    assert fst(s_out=ctypes.c_void_p(1 << 30 | 4)) == _lib.ERR_ALIGNMENT
+    # partially overlapping start and final state arrays (2*4*16 KiB each)
+    assert fst(s_out=ctypes.c_void_p((1 << 20) + 4096)) == _lib.ERR_INVALID_ARG
+    assert fst(s0=ctypes.c_void_p((1 << 30) - 16384)) == _lib.ERR_INVALID_ARG
+    assert fst(ptr=ctypes.c_void_p(0)) == _lib.ERR_INVALID_ARG
+    assert fst(ptr=ctypes.c_void_p(24)) == _lib.ERR_ALIGNMENT
+    # nothing to do: no device call
+    assert fst(B=0) == _lib.OK
+    assert fst(T=0, s_out=ctypes.c_void_p(1 << 20)) == _lib.OK   # in place, no step
+    assert fst(T=0, s_out=None) == _lib.OK
+
+
 def test_error_raises_camoe_error():
     with pytest.raises(_lib.CamoeError) as ei:
         _lib.check(_lib.ERR_ALIGNMENT)

@@ -85,3 +85,37 @@ def test_oracle_chains_are_independent():
     y1, sa1 = oracle.fwd(*one)
     np.testing.assert_array_equal(y[1:2, :, 2:3], y1)
     np.testing.assert_array_equal(sa[1:2, :, 2:3], sa1)
+
+
+def test_oracle_state_forward_zero_start_equals_fwd():
+    inp = make_inputs(2, 37, 3, seed=5)
+    xs = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    y, sa = oracle.fwd(*xs)
+    y1, sa1, sT = oracle.fwd_state(*xs)
+    assert np.array_equal(y, y1) and np.array_equal(sa, sa1)
+    assert sT.shape == (2, 3, 64, 64) and np.isfinite(sT).all()
+
+
+def test_oracle_state_forward_against_torch_with_start_state():
+    """The start state enters the recurrence as S_{-1}: checked against the
+    independent float64 torch restatement."""
+    inp = make_inputs(2, 24, 2, seed=6)
+    xs = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    s0 = np.random.default_rng(6).standard_normal((2, 2, 64, 64)).astype(np.float32)
+    y, sa, _ = oracle.fwd_state(*xs, s0=s0)
+    yt, sat = oracle.torch_reference(*xs, s0=s0)
+    assert nrel(y, yt) < 1e-6 and nrel(sa, sat) < 1e-6
+
+
+@pytest.mark.parametrize("T1", [1, 16, 23])
+def test_oracle_state_split_identity(T1):
+    """A forward over [0, T1) then over [T1, T) from its final state equals one
+    forward over [0, T)."""
+    inp = make_inputs(2, 40, 3, seed=7)
+    xs = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    y, sa, sT = oracle.fwd_state(*xs)
+    ya, saa, s1 = oracle.fwd_state(*[x[:, :T1] for x in xs])
+    yb, sab, s2 = oracle.fwd_state(*[x[:, T1:] for x in xs], s0=s1)
+    assert nrel(np.concatenate([ya, yb], 1), y) < 1e-5
+    assert nrel(np.concatenate([saa, sab], 1), sa) < 1e-5
+    assert nrel(s2, sT) < 1e-5
