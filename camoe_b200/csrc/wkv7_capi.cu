@@ -18,6 +18,7 @@ cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream);
 size_t ckpt_bytes(int64_t chains, int64_t T);
 size_t work_bytes(int64_t chains, int64_t T);
+size_t infer_bytes(int64_t chains, int64_t T);
 }  // namespace chunked
 }  // namespace camoe
 
@@ -133,16 +134,34 @@ int camoe_wkv7_fwd(const void* r, const void* w, const void* k, const void* v, c
   return cuda_status(camoe::scan::launch_fwd<float>(p, s));
 }
 
+// algorithm of a stateful forward: AUTO picks the decode-step kernel for T <= 16
+int resolve_state_algo(int dtype, int algo, int64_t T) {
+  const int al = resolve_algo(dtype, algo);
+  if (al >= 0 && algo == CAMOE_ALGO_AUTO && T <= camoe::kChunk) return CAMOE_ALGO_SCAN;
+  return al;
+}
+
+size_t camoe_wkv7_state_work_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype,
+                                   int algo) {
+  const int al = resolve_state_algo(dtype, algo, T);
+  if (al != CAMOE_ALGO_CHUNKED || N != camoe::kN || B < 0 || T < 0 || h_count < 0) return 0;
+  return camoe::chunked::infer_bytes(B * h_count, T);
+}
+
 int camoe_wkv7_fwd_state(const void* r, const void* w, const void* k, const void* v,
                          const void* a, const void* b, void* y, float* sa, const float* s0,
-                         float* s_out, int64_t B, int64_t T, int64_t H_total, int64_t h0,
-                         int64_t h_count, int N, int dtype, int algo, void* stream) {
+                         float* s_out, void* work, size_t work_bytes, int64_t B, int64_t T,
+                         int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
+                         void* stream) {
   int st = check_geometry(B, T, H_total, h0, h_count, N);
   if (st != CAMOE_OK) return st;
-  int al = resolve_algo(dtype, algo);
+  const int al = resolve_state_algo(dtype, algo, T);
   if (al < 0) return CAMOE_ERR_UNSUPPORTED;
-  if (algo == CAMOE_ALGO_AUTO && T <= camoe::kChunk) al = CAMOE_ALGO_SCAN;  // decode steps
   if (B * h_count == 0) return CAMOE_OK;
+  if (work != nullptr && al == CAMOE_ALGO_CHUNKED) {
+    if (!aligned16(work)) return CAMOE_ERR_ALIGNMENT;
+    if (work_bytes < camoe::chunked::infer_bytes(B * h_count, T)) return CAMOE_ERR_WORKSPACE;
+  }
   if ((s0 != nullptr && !aligned16(s0)) || (s_out != nullptr && !aligned16(s_out)))
     return CAMOE_ERR_ALIGNMENT;
   if (s0 != nullptr && s_out != nullptr && s0 != s_out) {
@@ -171,6 +190,7 @@ int camoe_wkv7_fwd_state(const void* r, const void* w, const void* k, const void
   p.r = r; p.w = w; p.k = k; p.v = v; p.a = a; p.b = b;
   p.y = y; p.sa = sa; p.ckpt = nullptr;
   p.s0 = s0; p.sT = s_out;
+  p.work = al == CAMOE_ALGO_CHUNKED ? work : nullptr;
   p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk};
   if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_fwd(p, s));
   if (dtype == CAMOE_DTYPE_BF16) return cuda_status(camoe::scan::launch_fwd<camoe::bf16>(p, s));

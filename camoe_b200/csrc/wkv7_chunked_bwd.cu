@@ -898,6 +898,10 @@ size_t ckpt_bytes(int64_t chains, int64_t T) {
   return rec::ckpt_bytes(chains, (T + kChunk - 1) / kChunk);
 }
 
+size_t infer_bytes(int64_t chains, int64_t T) {
+  return rec::infer_bytes(chains, (T + kChunk - 1) / kChunk);
+}
+
 size_t work_bytes(int64_t chains, int64_t T) {
   return rec::work_bytes(chains, (T + kChunk - 1) / kChunk);
 }

@@ -299,7 +299,8 @@ struct alignas(1024) Group {
 struct Params {
   CUtensorMap maps[5];  // r, w, k, a, b
   Geom g;
-  void* ckpt;
+  void* ckpt;        // record base: KeyRec array, then TriRec array
+  bool tri = true;   // store the TriRecs (only the backward reads them)
 };
 
 __device__ __forceinline__ void issue(Group& G, int rb, const Params& P, int64_t item) {
@@ -338,9 +339,12 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
     if (!ok) break;
     rec::KeyRec& o = G.out[j & 1].k;
     rec::TriRec& tr = G.out[j & 1].t;
+    const int64_t ch = item / P.g.nchunk, c = item - ch * P.g.nchunk;
+    // steps past T (a ragged last chunk) do not decay the state
+    const int nvalid = P.g.T - c * L < L ? static_cast<int>(P.g.T - c * L) : L;
     ks::decays<true>(G.raw[rb][0], G.raw[rb][1], G.raw[rb][2], G.raw[rb][3], G.raw[rb][4],
                      &G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Kb, o.Bb, Swz64{}, o.lam, nullptr,
-                     nullptr, gtid);
+                     nullptr, gtid, nvalid);
     named_sync(bar_id, 128);
     if (gtid == 0 && item + NR * ngroups < total) issue(G, rb, P, item + NR * ngroups);
     ks::grams(&G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Bb, o.Kb, Swz64{}, G.Ga, tr.Bm, tr.Cm, G.Dm,
@@ -355,9 +359,8 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
     fence_proxy_async();
     named_sync(bar_id, 128);
     if (gtid == 0) {
-      const int64_t ch = item / P.g.nchunk, c = item % P.g.nchunk;
       bulk_s2g(rec::keyrec(P.ckpt, ch, P.g.nchunk, c), &o, sizeof(rec::KeyRec));
-      bulk_s2g(rec::trirec(P.ckpt, P.g.chains(), ch, P.g.nchunk, c), &tr, sizeof(rec::TriRec));
+      if (P.tri) bulk_s2g(rec::trirec(P.ckpt, P.g.chains(), ch, P.g.nchunk, c), &tr, sizeof(rec::TriRec));
       bulk_commit();
     }
   }
@@ -456,6 +459,10 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
   __syncthreads();
 
   const int hh = static_cast<int>(p.g.h0 + ch % p.g.hc), bb = static_cast<int>(ch / p.g.hc);
+  // records come from the checkpoint (training) or the workspace (inference);
+  // only a checkpoint receives the bf16 states for the backward
+  void* const recs = p.ckpt != nullptr ? static_cast<void*>(p.ckpt) : p.work;
+  const bool states = p.ckpt != nullptr;
   if (warp == 3 * RB) {
     // ------------------------------ producer ------------------------------
     if (lane != 0) return;
@@ -473,7 +480,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
       mbar_arrive_expect_tx(bar, n * (sizeof(rec::KeyRec) + tma::kTileBytes));
       for (int k = 0; k < n; ++k) {
         const int c = c0 + k, s = c % NS;
-        bulk_g2s(&sm.slot[s].k, rec::keyrec(p.ckpt, ch, nchunk, c), sizeof(rec::KeyRec), bar);
+        bulk_g2s(&sm.slot[s].k, rec::keyrec(recs, ch, nchunk, c), sizeof(rec::KeyRec), bar);
         tma::load_tile(sm.slot[s].v, &P.map_v, hh, c * L, bb, bar);
       }
     }
@@ -492,7 +499,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
       const Stage<RB>& st = sm.st[x];
       tma::store_tile(&P.map_sa, &st.sa[0][0], row0, hh, c * L, bb);
       tma::store_tile(&P.map_y, &st.y[0][0], row0, hh, c * L, bb);
-      if (c >= 2 && (c & 1) == 0)
+      if (states && c >= 2 && (c & 1) == 0)
         bulk_s2g(rec::state_ptr(p.ckpt, chains, ch, nchunk, c) + row0 * 128, st.S, 2048 * RB);
       bulk_commit();
       bulk_wait_read_n<KEEP>();
@@ -507,11 +514,21 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
   const int g = lane >> 2, q = lane & 3;
   if (role == 0) {
     // ------------------------------ S warp: the state recurrence ------------------------------
-    float S[8][4];
+    float S[8][4];  // element (i0 + g (+8 for e >= 2), 8 nt + 2q + (e & 1))
+    if (p.s0 != nullptr) {
+      const float* s0 = p.s0 + p.g.state_off(ch) + (i0 + g) * kN + 2 * q;
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 8; ++nt) {
+        const float2 lo = *reinterpret_cast<const float2*>(s0 + 8 * nt);
+        const float2 hi = *reinterpret_cast<const float2*>(s0 + 8 * kN + 8 * nt);
+        S[nt][0] = lo.x; S[nt][1] = lo.y; S[nt][2] = hi.x; S[nt][3] = hi.y;
+      }
+    } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
+    }
     if (nchunk > 0 && !mbar_wait(&sm.fullp[0], 0)) return;
     for (int c = 0; c < nchunk; ++c) {
       const int s = c % NS;
@@ -563,6 +580,14 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
           !mbar_wait(&sm.fullp[((c + 1) >> 1) % (NS / 2)], par((c + 1) >> 1, NS / 2)))
         return;
     }
+    if (p.sT != nullptr) {
+      float* sT = p.sT + p.g.state_off(ch) + (i0 + g) * kN + 2 * q;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        *reinterpret_cast<float2*>(sT + 8 * nt) = make_float2(S[nt][0], S[nt][1]);
+        *reinterpret_cast<float2*>(sT + 8 * kN + 8 * nt) = make_float2(S[nt][2], S[nt][3]);
+      }
+    }
     return;
   }
 
@@ -590,7 +615,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
       uint32_t yA[4];
       acc_to_a(yA, acc[0], acc[1]);
       sta_cm(&st.y[0][0], Padded{16 * RB}, il, 0, yA, lane);
-      if (c >= 2 && (c & 1) == 0)
+      if (states && c >= 2 && (c & 1) == 0)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) sta_rm(st.S, Swz64{}, il, 16 * kk, sA[kk], lane);
     } else {
@@ -630,7 +655,7 @@ unsigned int fwd_timeouts() {
 }
 
 cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
-  if (p.ckpt == nullptr) {  // inference: one fused kernel, nothing stored
+  if (p.ckpt == nullptr && p.work == nullptr) {  // inference: one fused kernel, nothing stored
     fwd::Params P;
     P.a = p;
     const void* src[fwd::kNumRaw] = {p.r, p.w, p.k, p.a, p.b, p.v};
@@ -643,10 +668,12 @@ cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
     fwd::chunked_fwd_kernel<<<(unsigned)p.g.chains(), fwd::kThreads, smem, stream>>>(P);
     return cudaGetLastError();
   }
-  // training: key-side records over all SMs, then the sequential value pass
+  // key-side records over all SMs, then the sequential value pass (training:
+  // into the checkpoint, with TriRecs and states; inference: into the workspace)
   ka::Params K;
   K.g = p.g;
-  K.ckpt = p.ckpt;
+  K.ckpt = p.ckpt != nullptr ? static_cast<void*>(p.ckpt) : p.work;
+  K.tri = p.ckpt != nullptr;
   const void* ksrc[5] = {p.r, p.w, p.k, p.a, p.b};
   for (int t = 0; t < 5; ++t)
     if (!tma::encode_bhtn(&K.maps[t], ksrc[t], p.g.B, p.g.T, p.g.H)) return cudaErrorInvalidValue;

@@ -50,6 +50,9 @@ struct FwdArgs {
   // same thread).  Only the inference forward (ckpt == null) takes them.
   const float* s0 = nullptr;
   float* sT = nullptr;
+  // inference forward only: with a workspace the chunked path runs as two
+  // kernels (key-side records into `work`, then the value pass), else fused
+  void* work = nullptr;
 };
 
 struct BwdArgs {

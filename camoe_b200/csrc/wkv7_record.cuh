@@ -62,6 +62,10 @@ __host__ __device__ __forceinline__ size_t ckpt_bytes(int64_t chains, int64_t nc
   return static_cast<size_t>(chains * nchunk) * (sizeof(KeyRec) + sizeof(TriRec)) +
          static_cast<size_t>(chains * nstate(nchunk)) * kStateBytes;
 }
+// inference forward through the two-kernel path: the KeyRecs only
+__host__ __device__ __forceinline__ size_t infer_bytes(int64_t chains, int64_t nchunk) {
+  return static_cast<size_t>(chains * nchunk) * sizeof(KeyRec);
+}
 __host__ __device__ __forceinline__ size_t work_bytes(int64_t chains, int64_t nchunk) {
   return static_cast<size_t>(chains * nchunk) * sizeof(XRec);
 }

@@ -97,17 +97,42 @@ def _check_state(s, B, H, device, name):
                          f"tensor on {device}, got {tuple(s.shape)} {s.dtype} on {s.device}")
 
 
+def state_work_bytes(B: int, T: int, h_count: int, dtype: torch.dtype, algo="auto") -> int:
+    return int(_lib.lib().camoe_wkv7_state_work_bytes(B, T, h_count, HEAD_SIZE,
+                                                      dtype_code(dtype), algo_code(algo)))
+
+
+def _use_workspace(work, chains: int, device: torch.device) -> bool:
+    if work is None or isinstance(work, str):
+        # "auto": the fused kernel runs one CTA per chain, so with fewer chains
+        # than about 3/4 of the SMs the two-kernel path (key side over every SM)
+        # is faster: B200, T=4096, 64 chains 192 us vs 316 us; 128 chains at
+        # T=1024 the fused kernel wins, 87 us vs 96 us
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        return 4 * chains < 3 * sms
+    return bool(work)
+
+
 def wkv7_forward_state(r, w, k, v, a, b, state=None, *, algo="auto", h0: int = 0,
                        h_count: int | None = None, y=None, sa=None, out_state=None,
-                       inplace: bool = False, zero_rest=False):
+                       inplace: bool = False, zero_rest=False, work="auto"):
     """Stateful inference forward: every chain starts from ``state`` ([B, H, 64, 64]
     fp32, element [b, h, i, j] = S[i][j] with i the value index; None = zero) and
     its state after the last step is returned.  With ``inplace`` the final state
     overwrites ``state``; otherwise it goes to ``out_state`` (allocated when not
-    given).  Any T.  Returns (y, sa, final_state)."""
+    given).  Any T.  ``work``: a uint8 workspace tensor, True / False to allocate
+    one or run without, or "auto" (a workspace when there are fewer chains than
+    3/4 of the SM count).  Returns (y, sa, final_state)."""
     _check_inputs((r, w, k, v, a, b), "rwkvab")
     B, T, H, N = r.shape
     hc = H - h0 if h_count is None else h_count
+    wneed = state_work_bytes(B, T, hc, r.dtype, algo)
+    if isinstance(work, torch.Tensor):
+        wt = work
+    elif wneed > 0 and _use_workspace(work, B * hc, r.device):
+        wt = torch.empty(wneed, dtype=torch.uint8, device=r.device)
+    else:
+        wt = None
     if state is not None:
         _check_state(state, B, H, r.device, "state")
     if inplace:
@@ -127,8 +152,9 @@ def wkv7_forward_state(r, w, k, v, a, b, state=None, *, algo="auto", h0: int = 0
     st = _lib.lib().camoe_wkv7_fwd_state(
         r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(),
         y.data_ptr(), sa.data_ptr(), None if state is None else state.data_ptr(),
-        out_state.data_ptr(), B, T, H, h0, hc, N, dtype_code(r.dtype), algo_code(algo),
-        _stream_ptr(r.device))
+        out_state.data_ptr(), None if wt is None else wt.data_ptr(),
+        0 if wt is None else wt.numel() * wt.element_size(), B, T, H, h0, hc, N,
+        dtype_code(r.dtype), algo_code(algo), _stream_ptr(r.device))
     check(st)
     return y, sa, out_state
 

@@ -122,13 +122,23 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v,
  * CAMOE_ERR_INVALID_ARG).  Any T >= 0: a forward over steps [0, T1) followed
  * by one over [T1, T) from its s_out gives the y and sa of one forward over
  * [0, T).  AUTO runs the per-step decode kernel for T <= 16 (any dtype),
- * else CHUNKED for bf16 and SCAN for fp32.  No gradient flows through the
- * states.  No counterpart in the reference, which recomputes the whole
- * prefix for every generated token (eval.py:212, camoe/wrapper.py:203-223). */
+ * else CHUNKED for bf16 and SCAN for fp32.  CHUNKED with work = NULL runs one
+ * fused kernel per chain; with a workspace of camoe_wkv7_state_work_bytes()
+ * bytes it runs the key-side pass over all SMs first (faster when there are
+ * fewer chains than about 3/4 of the SM count); other algorithms ignore work.
+ * No gradient flows through the states.  No counterpart in the reference,
+ * which recomputes the whole prefix for every generated token (eval.py:212,
+ * camoe/wrapper.py:203-223). */
 int camoe_wkv7_fwd_state(const void* r, const void* w, const void* k, const void* v,
                          const void* a, const void* b, void* y, float* sa, const float* s0,
-                         float* s_out, int64_t B, int64_t T, int64_t H_total, int64_t h0,
-                         int64_t h_count, int N, int dtype, int algo, void* stream);
+                         float* s_out, void* work, size_t work_bytes, int64_t B, int64_t T,
+                         int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
+                         void* stream);
+
+/* Bytes of the optional workspace of camoe_wkv7_fwd_state (0 when its
+ * algorithm takes none). */
+size_t camoe_wkv7_state_work_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype,
+                                   int algo);
 
 /* Size of the library-owned checkpoint scratch used by
  * camoe_wkv7_fwd_bwd_noalloc (64 MiB per GPU that loads the library). */

@@ -109,12 +109,13 @@ def test_fwd_state_argument_errors_need_no_device():
     lib = _lib.lib()
     p = ctypes.c_void_p(16)
 
-    def fst(s0=ctypes.c_void_p(1 << 20), s_out=ctypes.c_void_p(1 << 30), ptr=p, **kw):
+    def fst(s0=ctypes.c_void_p(1 << 20), s_out=ctypes.c_void_p(1 << 30), ptr=p, work=None,
+            wbytes=0, **kw):
         g = dict(B=2, T=32, H=4, h0=0, hc=4, N=64, dtype=0, algo=0)
         g.update(kw)
         return lib.camoe_wkv7_fwd_state(ptr, ptr, ptr, ptr, ptr, ptr, ptr, ptr, s0, s_out,
-                                        g["B"], g["T"], g["H"], g["h0"], g["hc"], g["N"],
-                                        g["dtype"], g["algo"], None)
+                                        work, wbytes, g["B"], g["T"], g["H"], g["h0"], g["hc"],
+                                        g["N"], g["dtype"], g["algo"], None)
 
     assert fst(N=32) == _lib.ERR_UNSUPPORTED
     assert fst(dtype=1, algo=2) == _lib.ERR_UNSUPPORTED
@@ -126,6 +127,13 @@ def test_fwd_state_argument_errors_need_no_device():
     assert fst(s0=ctypes.c_void_p((1 << 30) - 16384)) == _lib.ERR_INVALID_ARG
     assert fst(ptr=ctypes.c_void_p(0)) == _lib.ERR_INVALID_ARG
     assert fst(ptr=ctypes.c_void_p(24)) == _lib.ERR_ALIGNMENT
+    need = lib.camoe_wkv7_state_work_bytes(2, 32, 4, 64, 0, 0)
+    assert need == 2 * 4 * 2 * 9472      # one key-side record per chunk and chain
+    assert lib.camoe_wkv7_state_work_bytes(2, 16, 4, 64, 0, 0) == 0      # decode kernel
+    assert lib.camoe_wkv7_state_work_bytes(2, 32, 4, 64, 1, 0) == 0      # fp32 scan
+    assert lib.camoe_wkv7_state_work_bytes(2, 16, 4, 64, 0, 2) > 0       # forced chunked
+    assert fst(work=ctypes.c_void_p(1 << 40), wbytes=need - 1) == _lib.ERR_WORKSPACE
+    assert fst(work=ctypes.c_void_p((1 << 40) + 8), wbytes=need) == _lib.ERR_ALIGNMENT
     # nothing to do: no device call
     assert fst(B=0) == _lib.OK
     assert fst(T=0, s_out=ctypes.c_void_p(1 << 20)) == _lib.OK   # in place, no step

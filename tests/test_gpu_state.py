@@ -22,9 +22,13 @@ from helpers import TOL_BF16, TOL_FP32, nrel
 pytestmark = pytest.mark.gpu
 
 NAMES = ("r", "w", "k", "v", "a", "b")
-PATHS = [(torch.float32, "scan"), (torch.bfloat16, "scan"), (torch.bfloat16, "chunked"),
-         (torch.float32, "auto"), (torch.bfloat16, "auto")]
-PATH_IDS = ["fp32-scan", "bf16-scan", "bf16-chunked", "fp32-auto", "bf16-auto"]
+# (dtype, algo, work): work False = the fused chunked kernel, True = the
+# key-side pass into a workspace, then the value pass
+PATHS = [(torch.float32, "scan", False), (torch.bfloat16, "scan", False),
+         (torch.bfloat16, "chunked", False), (torch.bfloat16, "chunked", True),
+         (torch.float32, "auto", "auto"), (torch.bfloat16, "auto", "auto")]
+PATH_IDS = ["fp32-scan", "bf16-scan", "bf16-chunked-fused", "bf16-chunked-work", "fp32-auto",
+            "bf16-auto"]
 
 # (B, T, H, seed): decode steps (T <= 16 runs the step kernel under scan/auto),
 # ragged and whole chunks, and a multi-chunk prefill
@@ -69,40 +73,44 @@ def check(got, want, tol, label):
     assert not bad, f"{label}: errors above {tol}: {bad} (all: {errs})"
 
 
-@pytest.mark.parametrize("dtype,algo", PATHS, ids=PATH_IDS)
+@pytest.mark.parametrize("dtype,algo,work", PATHS, ids=PATH_IDS)
 @pytest.mark.parametrize("shape", list(SHAPES), ids=list(SHAPES))
-def test_state_matches_oracle(shape, dtype, algo):
+def test_state_matches_oracle(shape, dtype, algo, work):
     B, T, H, seed = SHAPES[shape]
     inp = make_inputs(B, T, H, seed=seed)
     s0 = start_state(B, H, seed)
     want = oracle.fwd_state(*rounded(inp, dtype), s0=s0)
-    y, sa, sT = ops.wkv7_forward_state(*to_dev(inp, dtype), torch.from_numpy(s0).cuda(), algo=algo)
+    y, sa, sT = ops.wkv7_forward_state(*to_dev(inp, dtype), torch.from_numpy(s0).cuda(), algo=algo,
+                                       work=work)
     torch.cuda.synchronize()
     got = [y.float().cpu().numpy(), sa.cpu().numpy(), sT.cpu().numpy()]
     check(got, want, tol_for(dtype), f"{shape} {dtype} {algo}")
 
 
-@pytest.mark.parametrize("dtype,algo", PATHS[:3], ids=PATH_IDS[:3])
-def test_zero_state_equals_stateless_forward(dtype, algo):
+@pytest.mark.parametrize("dtype,algo,work", PATHS[:4], ids=PATH_IDS[:4])
+def test_zero_state_equals_stateless_forward(dtype, algo, work):
     """s0 = None gives bit-for-bit the outputs of camoe_wkv7_fwd (same kernels)."""
     for (B, T, H) in ((2, 40, 3), (1, 7, 2), (2, 128, 16)):
         xs = to_dev(make_inputs(B, T, H, seed=T), dtype)
-        y0, sa0, _ = ops.wkv7_forward(*xs, algo=algo, save_ckpt=False)
-        y1, sa1, sT = ops.wkv7_forward_state(*xs, None, algo=algo)
+        # the workspace path runs the training forward's kernels
+        y0, sa0, _ = ops.wkv7_forward(*xs, algo=algo, save_ckpt=work is True)
+        y1, sa1, sT = ops.wkv7_forward_state(*xs, None, algo=algo, work=work)
         torch.cuda.synchronize()
         assert torch.equal(y0, y1) and torch.equal(sa0, sa1)
         assert torch.isfinite(sT).all()
 
 
-@pytest.mark.parametrize("dtype,algo", PATHS[:3], ids=PATH_IDS[:3])
-def test_split_sequence_equals_one_pass(dtype, algo):
+@pytest.mark.parametrize("dtype,algo,work", PATHS[:4], ids=PATH_IDS[:4])
+def test_split_sequence_equals_one_pass(dtype, algo, work):
     """Forward over [0, T1) then over [T1, T) from its final state equals one
     forward over [0, T) (outputs within tolerance of the one-pass oracle)."""
     B, T, H, T1 = 2, 96, 3, 48
     inp = make_inputs(B, T, H, seed=21)
     xs = to_dev(inp, dtype)
-    ya, saa, s1 = ops.wkv7_forward_state(*[x[:, :T1].contiguous() for x in xs], None, algo=algo)
-    yb, sab, s2 = ops.wkv7_forward_state(*[x[:, T1:].contiguous() for x in xs], s1, algo=algo)
+    ya, saa, s1 = ops.wkv7_forward_state(*[x[:, :T1].contiguous() for x in xs], None, algo=algo,
+                                         work=work)
+    yb, sab, s2 = ops.wkv7_forward_state(*[x[:, T1:].contiguous() for x in xs], s1, algo=algo,
+                                         work=work)
     torch.cuda.synchronize()
     want = oracle.fwd_state(*rounded(inp, dtype))
     got = [torch.cat([ya, yb], 1).float().cpu().numpy(), torch.cat([saa, sab], 1).cpu().numpy(),
@@ -131,30 +139,30 @@ def test_prefill_then_decode_loop(dtype):
     check(got, [yw[:, T0:], saw[:, T0:], sw], tol_for(dtype), f"decode {dtype}")
 
 
-@pytest.mark.parametrize("dtype,algo", PATHS[:3], ids=PATH_IDS[:3])
-def test_inplace_equals_out_of_place(dtype, algo):
+@pytest.mark.parametrize("dtype,algo,work", PATHS[:4], ids=PATH_IDS[:4])
+def test_inplace_equals_out_of_place(dtype, algo, work):
     B, T, H = 2, 33, 4
     xs = to_dev(make_inputs(B, T, H, seed=41), dtype)
     s0 = torch.from_numpy(start_state(B, H, 41)).cuda()
-    y0, sa0, s_out = ops.wkv7_forward_state(*xs, s0, algo=algo)
+    y0, sa0, s_out = ops.wkv7_forward_state(*xs, s0, algo=algo, work=work)
     s_in = s0.clone()
-    y1, sa1, s_same = ops.wkv7_forward_state(*xs, s_in, algo=algo, inplace=True)
+    y1, sa1, s_same = ops.wkv7_forward_state(*xs, s_in, algo=algo, inplace=True, work=work)
     torch.cuda.synchronize()
     assert s_same.data_ptr() == s_in.data_ptr()
     assert torch.equal(y0, y1) and torch.equal(sa0, sa1) and torch.equal(s_out, s_in)
 
 
-@pytest.mark.parametrize("dtype,algo", PATHS[:3], ids=PATH_IDS[:3])
-def test_head_range_touches_only_its_states(dtype, algo):
+@pytest.mark.parametrize("dtype,algo,work", PATHS[:4], ids=PATH_IDS[:4])
+def test_head_range_touches_only_its_states(dtype, algo, work):
     """A head slice [h0, h0 + hc) reads and writes only those heads' states,
     and its outputs equal the full run's bit for bit."""
     B, T, H, h0, hc = 2, 40, 6, 2, 3
     xs = to_dev(make_inputs(B, T, H, seed=51), dtype)
     s0 = torch.from_numpy(start_state(B, H, 51)).cuda()
-    yf, saf, sf = ops.wkv7_forward_state(*xs, s0, algo=algo)
+    yf, saf, sf = ops.wkv7_forward_state(*xs, s0, algo=algo, work=work)
     out = torch.full_like(s0, 7.0)
     y, sa, _ = ops.wkv7_forward_state(*xs, s0, algo=algo, h0=h0, h_count=hc, out_state=out,
-                                      zero_rest=True)
+                                      zero_rest=True, work=work)
     torch.cuda.synchronize()
     sl = slice(h0, h0 + hc)
     assert torch.equal(out[:, sl], sf[:, sl])
