@@ -20,7 +20,7 @@ OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_SHAPE, ERR_ALIGNMENT, ERR_WORKSPACE, E
 EXPORTS = ("camoe_wkv7_version", "camoe_wkv7_strerror", "camoe_wkv7_last_cuda_error",
            "camoe_wkv7_device_errors", "camoe_wkv7_ckpt_bytes", "camoe_wkv7_work_bytes",
            "camoe_wkv7_fwd", "camoe_wkv7_bwd", "camoe_wkv7_fwd_state",
-           "camoe_wkv7_state_work_bytes")
+           "camoe_wkv7_state_work_bytes", "camoe_wkv7_wind_fwd", "camoe_wkv7_wind_bwd")
 
 
 class CamoeError(RuntimeError):
@@ -63,6 +63,11 @@ def lib() -> ctypes.CDLL:
     l.camoe_wkv7_state_work_bytes.argtypes = [i64, i64, i64, ci, ci, ci]
     l.camoe_wkv7_bwd.restype = ci
     l.camoe_wkv7_bwd.argtypes = [vp] * 9 + [sz, vp, sz] + [vp] * 6 + [i64] * 5 + [ci, ci, ci, vp]
+    # the wind op's entry points take the ClampW ones' argument types
+    l.camoe_wkv7_wind_fwd.restype = ci
+    l.camoe_wkv7_wind_fwd.argtypes = l.camoe_wkv7_fwd.argtypes
+    l.camoe_wkv7_wind_bwd.restype = ci
+    l.camoe_wkv7_wind_bwd.argtypes = l.camoe_wkv7_bwd.argtypes
     _lib = l
     return l
 

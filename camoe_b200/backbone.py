@@ -75,6 +75,33 @@ class RWKV7_ClampW(torch.autograd.Function):
         return grads
 
 
+class WindBackstepping(torch.autograd.Function):
+    """y, sa = WindBackstepping.apply(w, q, k, v, z, a): the reference's
+    wind_backstepping op (decay exp(-exp(w)), camoe/cuda/wkv7_cuda.cu; bound
+    by camoe/cuda/wkv7_op.cpp:18-21, no Python wrapper in the reference) as an
+    autograd Function on [B, T, H, 64] tensors, gradients of y and sa."""
+
+    @staticmethod
+    def forward(ctx, w, q, k, v, z, a):
+        assert q.shape[1] % CHUNK_LEN == 0
+        assert all(i.is_contiguous() for i in [w, q, k, v, z, a]), "wind kernel needs contiguous tensors"
+        y, sa, ckpt = ops.wkv7_forward(q, w, k, v, z, a, algo=_ALGO,
+                                       save_ckpt=any(ctx.needs_input_grad), decay="wind")
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(w, q, k, v, z, a, ckpt)
+        return y, sa
+
+    @staticmethod
+    def backward(ctx, dy, dsa):
+        w, q, k, v, z, a, ckpt = ctx.saved_tensors
+        dy = torch.zeros_like(q) if dy is None else dy.contiguous()
+        if dsa is not None:
+            dsa = dsa.to(torch.float32).contiguous()
+        dq, dw, dk, dv, dz, da = ops.wkv7_backward(q, w, k, v, z, a, dy, dsa, ckpt, algo=_ALGO,
+                                                   decay="wind")
+        return dw, dq, dk, dv, dz, da
+
+
 def _run_cuda(r, w, k, v, a, b):
     B, T, HC = r.shape
     H = HC // HEAD_SIZE
@@ -117,6 +144,40 @@ def _register_torch_ops():
     lib.impl("forward", fwd_impl, "CUDA")
     lib.impl("backward", bwd_impl, "CUDA")
     _TORCH_LIB = lib
+    _register_wind_ops()
+
+
+_WIND_LIB = None
+
+
+def _register_wind_ops():
+    """torch.ops.wind_backstepping.forward/backward with the reference's
+    arguments (camoe/cuda/wkv7_op.cpp:18-21): (w, q, k, v, z, a) inputs,
+    outputs preallocated and written in place, ``s`` the checkpoint buffer."""
+    global _WIND_LIB
+    if _WIND_LIB is not None:
+        return
+    try:
+        lib = torch.library.Library("wind_backstepping", "DEF")
+    except RuntimeError:  # namespace already defined
+        return
+    lib.define("forward(Tensor w, Tensor q, Tensor k, Tensor v, Tensor z, Tensor a, "
+               "Tensor(a!) y, Tensor(b!) s, Tensor(c!) sa) -> ()")
+    lib.define("backward(Tensor w, Tensor q, Tensor k, Tensor v, Tensor z, Tensor a, Tensor dy, "
+               "Tensor s, Tensor sa, Tensor(a!) dw, Tensor(b!) dq, Tensor(c!) dk, Tensor(d!) dv, "
+               "Tensor(e!) dz, Tensor(f!) da) -> ()")
+
+    def fwd_impl(w, q, k, v, z, a, y, s, sa):
+        ops.wkv7_forward(q, w, k, v, z, a, algo=_ALGO, y=y, sa=sa, ckpt=s.view(torch.uint8),
+                         decay="wind")
+
+    def bwd_impl(w, q, k, v, z, a, dy, s, sa, dw, dq, dk, dv, dz, da):
+        ops.wkv7_backward(q, w, k, v, z, a, dy, None, s.view(torch.uint8), algo=_ALGO,
+                          grads=(dq, dw, dk, dv, dz, da), decay="wind")
+
+    lib.impl("forward", fwd_impl, "CUDA")
+    lib.impl("backward", bwd_impl, "CUDA")
+    _WIND_LIB = lib
 
 
 def init_rwkv7_cuda():

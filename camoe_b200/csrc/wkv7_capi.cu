@@ -37,6 +37,13 @@ int resolve_algo(int dtype, int algo) {
   return -1;
 }
 
+// algorithm of a stateful forward: AUTO picks the decode-step kernel for T <= 16
+int resolve_state_algo(int dtype, int algo, int64_t T) {
+  const int al = resolve_algo(dtype, algo);
+  if (al >= 0 && algo == CAMOE_ALGO_AUTO && T <= camoe::kChunk) return CAMOE_ALGO_SCAN;
+  return al;
+}
+
 size_t required_ckpt(int64_t B, int64_t T, int64_t hc, int algo) {
   const int64_t chains = B * hc;
   if (algo == CAMOE_ALGO_CHUNKED) return camoe::chunked::ckpt_bytes(chains, T);
@@ -106,10 +113,14 @@ size_t camoe_wkv7_work_bytes(int64_t B, int64_t T, int64_t h_count, int N, int d
   return required_work(B, T, h_count, al);
 }
 
-int camoe_wkv7_fwd(const void* r, const void* w, const void* k, const void* v, const void* a,
-                   const void* b, void* y, float* sa, void* ckpt, size_t ckpt_bytes, int64_t B,
-                   int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
-                   int algo, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int fwd_impl(const void* r, const void* w, const void* k, const void* v, const void* a,
+             const void* b, void* y, float* sa, void* ckpt, size_t ckpt_bytes, int64_t B,
+             int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
+             void* stream, int decay) {
   int st = check_geometry(B, T, H_total, h0, h_count, N);
   if (st != CAMOE_OK) return st;
   const int al = resolve_algo(dtype, algo);
@@ -127,18 +138,32 @@ int camoe_wkv7_fwd(const void* r, const void* w, const void* k, const void* v, c
   camoe::FwdArgs p;
   p.r = r; p.w = w; p.k = k; p.v = v; p.a = a; p.b = b;
   p.y = y; p.sa = sa; p.ckpt = static_cast<float*>(ckpt);
-  p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk};
+  p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk, decay};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_fwd(p, s));
   if (dtype == CAMOE_DTYPE_BF16) return cuda_status(camoe::scan::launch_fwd<camoe::bf16>(p, s));
   return cuda_status(camoe::scan::launch_fwd<float>(p, s));
 }
 
-// algorithm of a stateful forward: AUTO picks the decode-step kernel for T <= 16
-int resolve_state_algo(int dtype, int algo, int64_t T) {
-  const int al = resolve_algo(dtype, algo);
-  if (al >= 0 && algo == CAMOE_ALGO_AUTO && T <= camoe::kChunk) return CAMOE_ALGO_SCAN;
-  return al;
+}  // namespace
+
+extern "C" {
+
+int camoe_wkv7_fwd(const void* r, const void* w, const void* k, const void* v, const void* a,
+                   const void* b, void* y, float* sa, void* ckpt, size_t ckpt_bytes, int64_t B,
+                   int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
+                   int algo, void* stream) {
+  return fwd_impl(r, w, k, v, a, b, y, sa, ckpt, ckpt_bytes, B, T, H_total, h0, h_count, N, dtype,
+                  algo, stream, camoe::kDecayClampW);
+}
+
+int camoe_wkv7_wind_fwd(const void* w, const void* q, const void* k, const void* v,
+                        const void* z, const void* a, void* y, float* sa, void* ckpt,
+                        size_t ckpt_bytes, int64_t B, int64_t T, int64_t H_total, int64_t h0,
+                        int64_t h_count, int N, int dtype, int algo, void* stream) {
+  // the wind op's (w, q, z, a) are the ClampW op's (w, r, a, b)
+  return fwd_impl(q, w, k, v, z, a, y, sa, ckpt, ckpt_bytes, B, T, H_total, h0, h_count, N, dtype,
+                  algo, stream, camoe::kDecayWind);
 }
 
 size_t camoe_wkv7_state_work_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype,
@@ -197,11 +222,15 @@ int camoe_wkv7_fwd_state(const void* r, const void* w, const void* k, const void
   return cuda_status(camoe::scan::launch_fwd<float>(p, s));
 }
 
-int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v, const void* a,
-                   const void* b, const void* dy, const float* dsa, const void* ckpt,
-                   size_t ckpt_bytes, void* work, size_t work_bytes, void* dr, void* dw, void* dk,
-                   void* dv, void* da, void* db, int64_t B, int64_t T, int64_t H_total,
-                   int64_t h0, int64_t h_count, int N, int dtype, int algo, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int bwd_impl(const void* r, const void* w, const void* k, const void* v, const void* a,
+             const void* b, const void* dy, const float* dsa, const void* ckpt, size_t ckpt_bytes,
+             void* work, size_t work_bytes, void* dr, void* dw, void* dk, void* dv, void* da,
+             void* db, int64_t B, int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N,
+             int dtype, int algo, void* stream, int decay) {
   int st = check_geometry(B, T, H_total, h0, h_count, N);
   if (st != CAMOE_OK) return st;
   const int al = resolve_algo(dtype, algo);
@@ -229,11 +258,34 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v, c
   p.r = r; p.w = w; p.k = k; p.v = v; p.a = a; p.b = b; p.dy = dy;
   p.dsa = dsa; p.ckpt = static_cast<const float*>(ckpt);
   p.dr = dr; p.dw = dw; p.dk = dk; p.dv = dv; p.da = da; p.db = db;
-  p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk};
+  p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk, decay};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_bwd(p, work, s));
   if (dtype == CAMOE_DTYPE_BF16) return cuda_status(camoe::scan::launch_bwd<camoe::bf16>(p, s));
   return cuda_status(camoe::scan::launch_bwd<float>(p, s));
+}
+
+}  // namespace
+
+extern "C" {
+
+int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v, const void* a,
+                   const void* b, const void* dy, const float* dsa, const void* ckpt,
+                   size_t ckpt_bytes, void* work, size_t work_bytes, void* dr, void* dw, void* dk,
+                   void* dv, void* da, void* db, int64_t B, int64_t T, int64_t H_total,
+                   int64_t h0, int64_t h_count, int N, int dtype, int algo, void* stream) {
+  return bwd_impl(r, w, k, v, a, b, dy, dsa, ckpt, ckpt_bytes, work, work_bytes, dr, dw, dk, dv,
+                  da, db, B, T, H_total, h0, h_count, N, dtype, algo, stream, camoe::kDecayClampW);
+}
+
+int camoe_wkv7_wind_bwd(const void* w, const void* q, const void* k, const void* v,
+                        const void* z, const void* a, const void* dy, const float* dsa,
+                        const void* ckpt, size_t ckpt_bytes, void* work, size_t work_bytes,
+                        void* dw, void* dq, void* dk, void* dv, void* dz, void* da, int64_t B,
+                        int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
+                        int algo, void* stream) {
+  return bwd_impl(q, w, k, v, z, a, dy, dsa, ckpt, ckpt_bytes, work, work_bytes, dq, dw, dk, dv,
+                  dz, da, B, T, H_total, h0, h_count, N, dtype, algo, stream, camoe::kDecayWind);
 }
 
 }  // extern "C"

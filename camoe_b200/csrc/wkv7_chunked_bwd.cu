@@ -499,7 +499,7 @@ struct alignas(1024) KGroup {
   rec::XRec x;
   Tile dQyb, dW2b;
   Tile At, Rt, Bb, Kb;
-  float lam[kN], cum[L][kN], sig[L][kN];
+  float lam[kN], cum[L][kN], lw[L][kN];
   float dllp[4][kN], dll[kN];
   bf16 dPb[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
   Tile W;
@@ -663,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     if (ok)
       ks::decays<true>(raw_r, G.raw[1], raw_k, raw_a, raw_b, &G.At[0][0], &G.Rt[0][0], Padded{LD},
                        &G.Kb[0][0], &G.Bb[0][0], Padded{LD}, G.lam,
-                       G.cum, G.sig, tid);
+                       G.cum, G.lw, tid, p.g.decay);
     ok = __syncthreads_and(ok);  // v, dy and the XRec are free from here on
     if (!ok) break;
     if (tid == 0 && next < total) {
@@ -782,25 +782,25 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     // outputs in place of the inputs they replace (same thread, same element):
     // dr -> r, dk -> k, da -> a, db -> b tiles; dw -> the w tile.  This lane
     // holds rows gq (hf 0) and gq + 8 (hf 1) of columns j0 + 8 nt + 2q + x.
-    float u[2][2][2], cx[2][2][2], sgs[2][2][2];  // [nt][x][hf]: dcum + dcumx, dcumx, sig
+    float u[2][2][2], cx[2][2][2], lws[2][2][2];  // [nt][x][hf]: dcum + dcumx, dcumx, lw
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const int t = gq + 8 * hf, jj = j0 + 8 * nt + 2 * q, o = tma::swz(t, jj);
         const float2 cm = *reinterpret_cast<const float2*>(&G.cum[t][jj]);
-        const float2 sg = *reinterpret_cast<const float2*>(&G.sig[t][jj]);
+        const float2 lg = *reinterpret_cast<const float2*>(&G.lw[t][jj]);
         const float2 rr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_r + o));
         const float2 kk = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_k + o));
         const float2 aa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_a + o));
         const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_b + o));
-        const float cmv[2] = {cm.x, cm.y}, sgv[2] = {sg.x, sg.y};
+        const float cmv[2] = {cm.x, cm.y}, lwv[2] = {lg.x, lg.y};
         const float rv[2] = {rr.x, rr.y}, kv[2] = {kk.x, kk.y}, av[2] = {aa.x, aa.y}, bv[2] = {bb.x, bb.y};
         float oda[2], odr[2], odk[2], odb[2];
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           const int e = 2 * hf + x;
-          const float Lam = __expf(cmv[x]), Lamx = __expf(cmv[x] - kWScale * sgv[x]), iLam = __expf(-cmv[x]);
+          const float Lam = __expf(cmv[x]), Lamx = __expf(cmv[x] - lwv[x]), iLam = __expf(-cmv[x]);
           const float dat = dAt[nt][e], drt = dRt[nt][e] + dQy[nt][e];
           const float dbb = dBb[nt][e] + dBp[nt][e], dkb = dKb[nt][e] + dKp[nt][e];
           oda[x] = dat * Lamx;
@@ -810,7 +810,7 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
           const float dcx = dat * av[x] * Lamx;
           cx[nt][x][hf] = dcx;
           u[nt][x][hf] = drt * rv[x] * Lam - dkb * kv[x] * iLam - dbb * bv[x] * iLam + dcx;
-          sgs[nt][x][hf] = sgv[x];
+          lws[nt][x][hf] = lwv[x];
         }
         *reinterpret_cast<__nv_bfloat162*>(G.raw[3] + o) = __floats2bfloat162_rn(oda[0], oda[1]);
         *reinterpret_cast<__nv_bfloat162*>(G.raw[0] + o) = __floats2bfloat162_rn(odr[0], odr[1]);
@@ -852,10 +852,7 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
         const int t = gq + 8 * hf, jj = j0 + 8 * nt + 2 * q;
         float dwv[2];
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const float sg = sgs[nt][x][hf];
-          dwv[x] = u[nt][x][hf] * kWScale * sg * (1.0f - sg);
-        }
+        for (int x = 0; x < 2; ++x) dwv[x] = u[nt][x][hf] * dlog_decay(lws[nt][x][hf], p.g.decay);
         *reinterpret_cast<__nv_bfloat162*>(G.raw[1] + tma::swz(t, jj)) = __floats2bfloat162_rn(dwv[0], dwv[1]);
       }
     __syncthreads();
@@ -907,6 +904,7 @@ size_t work_bytes(int64_t chains, int64_t T) {
 }
 
 cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
+  if (!tma::bind_context()) return cudaErrorNoDevice;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int rb = rows_per_cta(p.g.chains(), sms);

@@ -2,7 +2,8 @@
 // accumulation and fp32 state), the bf16 path of the operator.
 //
 // Per chain (b, h), chunks of L = 16 steps are processed in order.  With the
-// log-decay lw = -e^{-1/2} sigmoid(w_in) (camoe/cuda/rwkv7_clampw.cu:42),
+// log-decay lw = -e^{-1/2} sigmoid(w_in) (camoe/cuda/rwkv7_clampw.cu:42; or
+// -exp(w_in) for the wind_backstepping decay, camoe/cuda/wkv7_cuda.cu:21),
 // cum_t = sum_{s<=t} lw_s inside the chunk, Lam = exp(cum) and lam = Lam_{L-1},
 // the 16 steps of
 //     S_t = S_{t-1} (diag w_t + a_t b_t^T) + v_t k_t^T,  y_t = S_t r_t,  sa_t = S_{t-1} a_t
@@ -18,7 +19,10 @@
 // (the WY / UT-transform form of chunked delta-rule recurrences, e.g. Yang et
 // al. 2024, "Parallelizing Linear Transformers with the Delta Rule over
 // Sequence Length").  ClampW bounds every decay below by exp(-e^{-1/2}) =
-// 0.545, so 1/Lam <= 0.545^-16 ~ 1.6e4: nothing over- or underflows.
+// 0.545, so 1/Lam <= 0.545^-16 ~ 1.6e4: nothing over- or underflows.  The
+// wind decay has no such bound; RWKV-7's time mix feeds it w_in <= -1/2
+// (the same 0.545 bound), and fp32 1/Lam stays finite while the chunk's
+// summed -lw stays below 88 (w_in up to about 1.7 in every step).
 //
 // One CTA per chain, 12 warps in three roles:
 //   value warps 0-3   own state rows 16w..16w+15 as mma accumulators for the
@@ -229,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_fwd_kernel(const __grid_c
       const int nvalid = T - c * L < L ? static_cast<int>(T - c * L) : L;
       ks::decays<true>(raw[R_R], raw[R_W], raw[R_K], raw[R_A], raw[R_B], &sc.At[0][0], &sc.Rt[0][0],
                        Padded{LD}, &sl.Kb[0][0], &sl.Bb[0][0], Padded{LD}, sl.lam, nullptr, nullptr, gtid,
-                       nvalid);
+                       p.g.decay, nvalid);
       {  // v tile -> slot, un-swizzled (one 16-byte piece per thread)
         const int u = gtid >> 3, part = gtid & 7;
         *reinterpret_cast<uint4*>(&sl.v[u][part * 8]) =
@@ -339,12 +343,15 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
     if (!ok) break;
     rec::KeyRec& o = G.out[j & 1].k;
     rec::TriRec& tr = G.out[j & 1].t;
-    const int64_t ch = item / P.g.nchunk, c = item - ch * P.g.nchunk;
     // steps past T (a ragged last chunk) do not decay the state
-    const int nvalid = P.g.T - c * L < L ? static_cast<int>(P.g.T - c * L) : L;
+    int nvalid = L;
+    if ((P.g.T & (L - 1)) != 0) {
+      const int64_t c = item % P.g.nchunk;
+      if (c == P.g.nchunk - 1) nvalid = static_cast<int>(P.g.T - c * L);
+    }
     ks::decays<true>(G.raw[rb][0], G.raw[rb][1], G.raw[rb][2], G.raw[rb][3], G.raw[rb][4],
                      &G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Kb, o.Bb, Swz64{}, o.lam, nullptr,
-                     nullptr, gtid, nvalid);
+                     nullptr, gtid, P.g.decay, nvalid);
     named_sync(bar_id, 128);
     if (gtid == 0 && item + NR * ngroups < total) issue(G, rb, P, item + NR * ngroups);
     ks::grams(&G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Bb, o.Kb, Swz64{}, G.Ga, tr.Bm, tr.Cm, G.Dm,
@@ -359,6 +366,7 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
     fence_proxy_async();
     named_sync(bar_id, 128);
     if (gtid == 0) {
+      const int64_t ch = item / P.g.nchunk, c = item - ch * P.g.nchunk;
       bulk_s2g(rec::keyrec(P.ckpt, ch, P.g.nchunk, c), &o, sizeof(rec::KeyRec));
       if (P.tri) bulk_s2g(rec::trirec(P.ckpt, P.g.chains(), ch, P.g.nchunk, c), &tr, sizeof(rec::TriRec));
       bulk_commit();
@@ -655,6 +663,7 @@ unsigned int fwd_timeouts() {
 }
 
 cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
+  if (!tma::bind_context()) return cudaErrorNoDevice;
   if (p.ckpt == nullptr && p.work == nullptr) {  // inference: one fused kernel, nothing stored
     fwd::Params P;
     P.a = p;

@@ -13,12 +13,32 @@ constexpr int kChunk = 16;  // steps per chunk / checkpoint interval
 // camoe/cuda/rwkv7_clampw.cu:16,42.
 constexpr float kWScale = -0.6065306597126334f;
 
+// Decay transforms w = exp(lw(w_in)) of the two reference ops:
+//   ClampW             lw = -e^{-1/2} sigmoid(w_in)   camoe/cuda/rwkv7_clampw.cu:42
+//   wind_backstepping  lw = -exp(w_in)                camoe/cuda/wkv7_cuda.cu:21,66-67
+enum : int { kDecayClampW = 0, kDecayWind = 1 };
+
+__device__ __forceinline__ float log_decay(float x, int kind) {
+  return kind == kDecayWind ? -expf(x) : kWScale / (1.0f + expf(-x));
+}
+// fast-math form, for the chunked kernels (bf16 operands)
+__device__ __forceinline__ float log_decay_fast(float x, int kind) {
+  return kind == kDecayWind ? -__expf(x) : kWScale * __fdividef(1.0f, 1.0f + __expf(-x));
+}
+// d lw / d w_in, written in terms of lw: ClampW kWScale s (1 - s) with
+// s = lw / kWScale; wind -exp(w_in) = lw
+__device__ __forceinline__ float dlog_decay(float lw, int kind) {
+  return kind == kDecayWind ? lw : lw * (1.0f - lw * (1.0f / kWScale));
+}
+
 using bf16 = __nv_bfloat16;
 
-// Geometry of one call: heads [h0, h0 + hc) of [B, T, H, kN] arrays.
+// Geometry of one call: heads [h0, h0 + hc) of [B, T, H, kN] arrays, and
+// the decay transform (kDecayClampW or kDecayWind) the call applies.
 struct Geom {
   int64_t B, T, H, h0, hc;
   int64_t nchunk;  // ceil(T / kChunk)
+  int decay = kDecayClampW;
   __host__ __device__ int64_t chains() const { return B * hc; }
   // offset of element (t, i) of chain `ch`
   __device__ __forceinline__ int64_t off(int64_t ch, int64_t t, int i) const {

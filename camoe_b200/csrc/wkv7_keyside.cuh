@@ -24,12 +24,12 @@ using Tile = bf16[L][LD];
 using Tile16 = bf16[L][LDS];
 
 // Phase 1 (SIMT): per column pair (2p, 2p+1) and time quarter tq, the
-// log-decays lw = -e^{-1/2} sigmoid(w_in), their inclusive prefix cum inside
+// log-decays lw = log_decay(w_in, kind), their inclusive prefix cum inside
 // the chunk (scan over the 4 quarter lanes), Lam = exp(cum), and the scaled
 // operands At = a exp(cum - lw), Rt = r Lam, Kb = k / Lam, Bb = b / Lam.
 // lam (the decay over the whole chunk) = Lam of the last step.
 // Thread layout: p = gtid / 4, tq = gtid % 4 (quarter lanes adjacent).
-// With `cum_out`/`sig_out` non-null, the fp32 prefixes and sigmoids are kept
+// With `cum_out`/`lw_out` non-null, the fp32 prefixes and log-decays are kept
 // for the backward.  Steps u >= nvalid (past the end of a sequence whose
 // length is not a multiple of L) get lw = 0, so lam is the decay over the
 // steps that exist and a final state taken after the chunk is exact.  The input tiles are 16 x 64 bf16, either row-major with
@@ -44,20 +44,35 @@ template <bool SWZ, typename LAR, typename LKB>
 __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf16* kk,
                                        const bf16* aa, const bf16* bb, bf16* At, bf16* Rt, LAR lar,
                                        bf16* Kb, bf16* Bb, LKB lkb, float* lam, float (*cum_out)[kN],
-                                       float (*sig_out)[kN], int gtid, int nvalid = L) {
+                                       float (*lw_out)[kN], int gtid, int kind, int nvalid = L) {
   const int p = gtid >> 2, tq = gtid & 3, j = 2 * p;
   const int lane = gtid & 31;
   float lw0[4], lw1[4], c0[4], c1[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ww + raw_idx<SWZ>(4 * tq + e, j)));
+    lw0[e] = x.x;
+    lw1[e] = x.y;
+  }
+  if (kind == kDecayWind) {  // uniform branch: one transform per call
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      lw0[e] = -__expf(lw0[e]);
+      lw1[e] = -__expf(lw1[e]);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      lw0[e] = kWScale * __fdividef(1.0f, 1.0f + __expf(-lw0[e]));
+      lw1[e] = kWScale * __fdividef(1.0f, 1.0f + __expf(-lw1[e]));
+    }
+  }
   float run0 = 0.f, run1 = 0.f;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const int u = 4 * tq + e;
-    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ww + raw_idx<SWZ>(u, j)));
-    const float s0 = __fdividef(1.0f, 1.0f + __expf(-x.x));
-    const float s1 = __fdividef(1.0f, 1.0f + __expf(-x.y));
-    if (sig_out != nullptr) *reinterpret_cast<float2*>(&sig_out[u][j]) = make_float2(s0, s1);
-    lw0[e] = u < nvalid ? kWScale * s0 : 0.f;
-    lw1[e] = u < nvalid ? kWScale * s1 : 0.f;
+    if (u >= nvalid) lw0[e] = lw1[e] = 0.f;
+    if (lw_out != nullptr) *reinterpret_cast<float2*>(&lw_out[u][j]) = make_float2(lw0[e], lw1[e]);
     run0 += lw0[e];
     run1 += lw1[e];
     c0[e] = run0;

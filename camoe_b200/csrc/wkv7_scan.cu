@@ -7,7 +7,7 @@
 // combine row sums (sa = S a, y = S r) with two xor-shuffles.  Chunks of 16
 // steps of r, w, k, a, b (and the CTA's slice of v) are streamed into shared
 // memory with cp.async, double-buffered, and converted once per chunk
-// (decay w = exp(-e^{-1/2} sigmoid(w_in)) computed there).  The state at the
+// (decay w = exp(log_decay(w_in)) computed there, ClampW or wind).  The state at the
 // start of every chunk is the checkpoint, stored row-major in fp32.
 //
 // Backward (scan_bwd_kernel): one CTA of 256 threads per chain (row i =
@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
     for (int idx = tid; idx < nu * kN; idx += kFwdThreads) {
       const int u = idx / kN, j = idx % kN;
       sm.r[u][j] = to_f32(sm.raw[buf][0][u][j]);
-      sm.w[u][j] = expf(kWScale / (1.0f + expf(-to_f32(sm.raw[buf][1][u][j]))));
+      sm.w[u][j] = expf(log_decay(to_f32(sm.raw[buf][1][u][j]), p.g.decay));
       sm.k[u][j] = to_f32(sm.raw[buf][2][u][j]);
       sm.a[u][j] = to_f32(sm.raw[buf][3][u][j]);
       sm.b[u][j] = to_f32(sm.raw[buf][4][u][j]);
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kStepThreads, 8) step_fwd_kernel(FwdArgs p) {
       const int tens = tid >> 4, col = 4 * (tid & 15);
       if (tens == 1) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) x[e] = expf(kWScale / (1.0f + expf(-x[e])));
+        for (int e = 0; e < 4; ++e) x[e] = expf(log_decay(x[e], p.g.decay));
       }
       *reinterpret_cast<float4*>(&xin[buf][tens][col]) = make_float4(x[0], x[1], x[2], x[3]);
     } else if (tid < kStepLoaders) {
@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kStepThreads, 8) step_fwd_kernel(FwdArgs p) {
 
 struct BwdSmem {
   float S[kHalf + 1][kN][kN];  // states of one half chunk, columns xor-swizzled by row
-  float r[kChunk][kN], w[kChunk][kN], sig[kChunk][kN], k[kChunk][kN], a[kChunk][kN],
+  float r[kChunk][kN], w[kChunk][kN], dlw[kChunk][kN], k[kChunk][kN], a[kChunk][kN],
       b[kChunk][kN], v[kChunk][kN], dy[kChunk][kN], dsa[kChunk][kN];
   float sa[kChunk][kN];
   float red[kBwdThreads / 32][320];  // per-warp partial column sums
@@ -381,17 +381,18 @@ __device__ __forceinline__ void bwd_prefetch(Prefetch<Tin>& pf, const BwdArgs& p
 }
 
 template <typename Tin>
-__device__ __forceinline__ void bwd_stage(BwdSmem& sm, const Prefetch<Tin>& pf) {
+__device__ __forceinline__ void bwd_stage(BwdSmem& sm, const Prefetch<Tin>& pf, int kind) {
   const int u = threadIdx.x >> 4, j = (threadIdx.x & 15) * 4;
   *reinterpret_cast<float4*>(&sm.r[u][j]) = pf.x[0];
   const float wi[4] = {pf.x[1].x, pf.x[1].y, pf.x[1].z, pf.x[1].w};
-  float sg[4], wd[4];
+  float dl[4], wd[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    sg[e] = 1.0f / (1.0f + expf(-wi[e]));
-    wd[e] = expf(kWScale / (1.0f + expf(-wi[e])));
+    const float lw = log_decay(wi[e], kind);
+    dl[e] = dlog_decay(lw, kind);
+    wd[e] = expf(lw);
   }
-  *reinterpret_cast<float4*>(&sm.sig[u][j]) = make_float4(sg[0], sg[1], sg[2], sg[3]);
+  *reinterpret_cast<float4*>(&sm.dlw[u][j]) = make_float4(dl[0], dl[1], dl[2], dl[3]);
   *reinterpret_cast<float4*>(&sm.w[u][j]) = make_float4(wd[0], wd[1], wd[2], wd[3]);
   *reinterpret_cast<float4*>(&sm.k[u][j]) = pf.x[2];
   *reinterpret_cast<float4*>(&sm.v[u][j]) = pf.x[3];
@@ -511,10 +512,7 @@ __device__ __forceinline__ void bwd_step(BwdSmem& sm, int u, int st, int sp, int
     const int ln = pidx / 10, s = pidx % 10, qq = ln & 3, rb = ln >> 2;
     const int m = 40 * ((rb >> 2) & 1) + 20 * ((rb >> 1) & 1) + 10 * (rb & 1) + s;
     const int quant = m >> 4, j = qq * 16 + (m & 15);
-    if (quant == 1) {
-      const float sg = sm.sig[u][j];
-      acc = kWScale * acc * sm.w[u][j] * sg * (1.0f - sg);
-    }
+    if (quant == 1) acc = acc * sm.w[u][j] * sm.dlw[u][j];  // dw_in = dL/dw * w * dlw/dw_in
     sm.out[quant][u][j] = acc;
   }
   __syncthreads();
@@ -536,7 +534,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdArgs p) {
   if (nchunk > 0) bwd_prefetch<Tin>(pf, p, ch, nchunk - 1);
   for (int64_t c = nchunk - 1; c >= 0; --c) {
     __syncthreads();
-    bwd_stage<Tin>(sm, pf);
+    bwd_stage<Tin>(sm, pf, p.g.decay);
     if (c > 0) bwd_prefetch<Tin>(pf, p, ch, c - 1);
     if (c > 0) {
       const float4* src = reinterpret_cast<const float4*>(p.ckpt + ((ch * nchunk + c) * kN + i) * kN + q * 16);

@@ -31,6 +31,11 @@ EncodeFn encode_fn() {
 
 }  // namespace
 
+bool bind_context() {
+  int dev = 0;
+  return cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess;
+}
+
 bool encode_bhtn(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H) {
   const EncodeFn fn = encode_fn();
   if (fn == nullptr || B <= 0 || T <= 0 || H <= 0) return false;

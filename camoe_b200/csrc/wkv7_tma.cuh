@@ -26,6 +26,13 @@ __host__ __device__ __forceinline__ int swz(int r, int c) {
   return r * 64 + ((((c >> 3) ^ (r & 7))) << 3) + (c & 7);
 }
 
+// Make the calling thread's current device's primary context current for the
+// driver before tensor maps are encoded (cuTensorMapEncodeTiled is a driver
+// call and fails on a thread with no current context, e.g. a framework's
+// backward worker thread that has launched nothing yet).  Returns false when
+// the runtime has no usable device.
+bool bind_context();
+
 // Encode the (N, H, T, B) map of a bf16 [B, T, H, 64] array; returns false on failure.
 bool encode_bhtn(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H);
 // Same for an fp32 array, without swizzle: a chunk lands as a plain [16][64] fp32 tile.

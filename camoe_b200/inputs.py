@@ -16,10 +16,13 @@ NAMES = ("r", "w", "k", "v", "a", "b")
 
 def make_inputs(B: int, T: int, H: int, N: int = 64, seed: int = 0, w_mu: float = 0.0,
                 w_sigma: float = 1.0, dtype: torch.dtype = torch.float32,
-                device: str | torch.device = "cpu", with_dsa: bool = False) -> dict:
+                device: str | torch.device = "cpu", with_dsa: bool = False,
+                decay: str = "clampw") -> dict:
     """Return dict(r, w, k, v, a, b, dy[, dsa]) of [B, T, H, N] contiguous tensors.
 
     ``w`` is the raw decay input w_in (the op applies exp(-e^{-1/2} sigmoid(w_in))).
+    With ``decay="wind"`` it is -softplus(-x) - 1/2 of the same draw x, the input
+    RWKV-7's time mix gives a decay exp(-exp(w_in)) (camoe/backbone.py:326).
     Values are drawn in float32 on the CPU and then cast, so every dtype and
     device sees the same numbers up to rounding.
     """
@@ -31,6 +34,8 @@ def make_inputs(B: int, T: int, H: int, N: int = 64, seed: int = 0, w_mu: float 
 
     r, k, v, u, dy, w_in, kk = (randn() for _ in range(7))
     w_in = w_mu + w_sigma * w_in
+    if decay == "wind":
+        w_in = -torch.nn.functional.softplus(-w_in) - 0.5
     kk = torch.nn.functional.normalize(kk.view(B, T, H, N), dim=-1, p=2.0)
     a = -kk
     b = kk * torch.sigmoid(u.view(B, T, H, N))

@@ -62,9 +62,17 @@ def work_bytes(B: int, T: int, h_count: int, dtype: torch.dtype, algo="auto") ->
                                                 algo_code(algo)))
 
 
+DECAYS = ("clampw", "wind")
+
+
 def wkv7_forward(r, w, k, v, a, b, *, algo="auto", save_ckpt: bool = True, h0: int = 0,
-                 h_count: int | None = None, y=None, sa=None, ckpt=None, zero_rest=False):
-    """Forward.  Returns (y, sa, ckpt); ckpt is None when save_ckpt is False."""
+                 h_count: int | None = None, y=None, sa=None, ckpt=None, zero_rest=False,
+                 decay: str = "clampw"):
+    """Forward.  Returns (y, sa, ckpt); ckpt is None when save_ckpt is False.
+    ``decay="wind"`` runs the wind_backstepping op (decay exp(-exp(w))), whose
+    (q, z, a) are passed here as (r, a, b)."""
+    if decay not in DECAYS:
+        raise ValueError(f"decay must be one of {DECAYS}, got {decay!r}")
     _check_inputs((r, w, k, v, a, b), "rwkvab")
     B, T, H, N = r.shape
     hc = H - h0 if h_count is None else h_count
@@ -82,10 +90,13 @@ def wkv7_forward(r, w, k, v, a, b, *, algo="auto", save_ckpt: bool = True, h0: i
             nbytes = ckpt.numel() * ckpt.element_size()
     else:
         ckpt = None
-    st = _lib.lib().camoe_wkv7_fwd(
-        r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(),
-        y.data_ptr(), sa.data_ptr(), None if ckpt is None else ckpt.data_ptr(), nbytes,
-        B, T, H, h0, hc, N, dtype_code(r.dtype), algo_code(algo), _stream_ptr(r.device))
+    if decay == "wind":  # the wind op's argument order: (w, q, k, v, z, a)
+        fn, ins = _lib.lib().camoe_wkv7_wind_fwd, (w, r, k, v, a, b)
+    else:
+        fn, ins = _lib.lib().camoe_wkv7_fwd, (r, w, k, v, a, b)
+    st = fn(*(x.data_ptr() for x in ins),
+            y.data_ptr(), sa.data_ptr(), None if ckpt is None else ckpt.data_ptr(), nbytes,
+            B, T, H, h0, hc, N, dtype_code(r.dtype), algo_code(algo), _stream_ptr(r.device))
     check(st)
     return y, sa, ckpt
 
@@ -169,9 +180,13 @@ def wkv7_decode_step(r, w, k, v, a, b, state):
 
 
 def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
-                  h_count: int | None = None, grads=None, zero_rest=False, work=None):
+                  h_count: int | None = None, grads=None, zero_rest=False, work=None,
+                  decay: str = "clampw"):
     """Backward.  ``dsa`` (fp32) may be None.  Returns (dr, dw, dk, dv, da, db).
-    ``work`` is the scratch workspace (allocated here when not given)."""
+    ``work`` is the scratch workspace (allocated here when not given).  ``decay``
+    as in wkv7_forward (the gradients keep the (r, w, k, v, a, b) order)."""
+    if decay not in DECAYS:
+        raise ValueError(f"decay must be one of {DECAYS}, got {decay!r}")
     _check_inputs((r, w, k, v, a, b, dy), "rwkvab" + "y")
     B, T, H, N = r.shape
     hc = H - h0 if h_count is None else h_count
@@ -187,12 +202,16 @@ def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
     if work is None and wneed > 0:
         work = torch.empty(wneed, dtype=torch.uint8, device=r.device)
     wbytes = 0 if work is None else work.numel() * work.element_size()
-    st = _lib.lib().camoe_wkv7_bwd(
-        r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(),
-        dy.data_ptr(), None if dsa is None else dsa.data_ptr(),
-        None if ckpt is None else ckpt.data_ptr(), nbytes,
-        None if work is None else work.data_ptr(), wbytes,
-        *(g.data_ptr() for g in grads), B, T, H, h0, hc, N, dtype_code(r.dtype),
-        algo_code(algo), _stream_ptr(r.device))
+    dr, dw, dk, dv, da, db = grads
+    if decay == "wind":  # (w, q, k, v, z, a) in, (dw, dq, dk, dv, dz, da) out
+        fn, ins, outs = _lib.lib().camoe_wkv7_wind_bwd, (w, r, k, v, a, b), (dw, dr, dk, dv, da, db)
+    else:
+        fn, ins, outs = _lib.lib().camoe_wkv7_bwd, (r, w, k, v, a, b), (dr, dw, dk, dv, da, db)
+    st = fn(*(x.data_ptr() for x in ins),
+            dy.data_ptr(), None if dsa is None else dsa.data_ptr(),
+            None if ckpt is None else ckpt.data_ptr(), nbytes,
+            None if work is None else work.data_ptr(), wbytes,
+            *(g.data_ptr() for g in outs), B, T, H, h0, hc, N, dtype_code(r.dtype),
+            algo_code(algo), _stream_ptr(r.device))
     check(st)
     return grads

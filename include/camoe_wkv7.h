@@ -111,6 +111,29 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v,
                    int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
                    int algo, void* stream);
 
+/* The reference's second WKV-7 op, wind_backstepping (camoe/cuda/wkv7_cuda.cu,
+ * wkv7_cuda_fp32.cu; bound by camoe/cuda/wkv7_op.cpp:5-21), in its own
+ * argument order: forward(w, q, k, v, z, a) with decay exp(-exp(w)) in place
+ * of ClampW's exp(-e^{-1/2} sigmoid(w)); q, z, a play the roles of ClampW's
+ * r, a, b.  Same shapes, dtypes, checkpoint and workspace sizes, algorithms
+ * and status codes as camoe_wkv7_fwd / camoe_wkv7_bwd.  The decay is not
+ * clamped: the chunked algorithm is exact for w <= -1/2 (decays >= 0.545,
+ * as RWKV-7's time mix produces them) and stays finite while a 16-step
+ * chunk's summed exp(w) stays below about 88; SCAN takes any w.  The
+ * reference's backward reverses the state through 1/decay
+ * (wkv7_cuda.cu:91-94); this one recomputes it forward from checkpoints. */
+int camoe_wkv7_wind_fwd(const void* w, const void* q, const void* k, const void* v,
+                        const void* z, const void* a, void* y, float* sa, void* ckpt,
+                        size_t ckpt_bytes, int64_t B, int64_t T, int64_t H_total, int64_t h0,
+                        int64_t h_count, int N, int dtype, int algo, void* stream);
+
+int camoe_wkv7_wind_bwd(const void* w, const void* q, const void* k, const void* v,
+                        const void* z, const void* a, const void* dy, const float* dsa,
+                        const void* ckpt, size_t ckpt_bytes, void* work, size_t work_bytes,
+                        void* dw, void* dq, void* dk, void* dv, void* dz, void* da, int64_t B,
+                        int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
+                        int algo, void* stream);
+
 /* Stateful forward, for inference and decoding: camoe_wkv7_fwd without a
  * checkpoint, but every chain starts from the state s0 instead of zero and
  * its state after step T-1 is written to s_out.  s0 and s_out are fp32

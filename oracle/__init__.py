@@ -10,9 +10,9 @@ Contents:
   restatement of ``camoe/backbone.py:264-294`` and of the gradient formulas of
   ``camoe/cuda/rwkv7_clampw.cu:83-170``), in float64 (ground truth) or float32
   (reference precision), OpenMP over (batch, head) chains.
-* ``RefOp`` — the reference's own ClampW CUDA op, compiled by
-  ``oracle/Makefile`` from the reference's sources into ``oracle/_ref/``; the
-  GPU parity tests call it with device pointers.
+* ``RefOp`` — the reference's own ClampW (or wind_backstepping) CUDA op,
+  compiled by ``oracle/Makefile`` from the reference's sources into
+  ``oracle/_ref/``; the GPU parity tests call it with device pointers.
 * ``torch_reference`` — a float64 torch restatement of the same recurrence
   whose gradients come from autograd; an independent cross-check of ``bwd``.
 """
@@ -49,13 +49,13 @@ def _load():
     i64, fp, ci = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int
     for suf in ("f64", "f32"):
         f = getattr(lib, f"wkv7_oracle_fwd_{suf}")
-        f.argtypes = [i64] * 4 + [fp] * 8 + [ci]
+        f.argtypes = [i64] * 4 + [fp] * 8 + [ci, ci]
         f.restype = ci
         g = getattr(lib, f"wkv7_oracle_bwd_{suf}")
-        g.argtypes = [i64] * 5 + [fp] * 14 + [ci]
+        g.argtypes = [i64] * 5 + [fp] * 14 + [ci, ci]
         g.restype = ci
         h = getattr(lib, f"wkv7_oracle_fwd_state_{suf}")
-        h.argtypes = [i64] * 4 + [fp] * 10 + [ci]
+        h.argtypes = [i64] * 4 + [fp] * 10 + [ci, ci]
         h.restype = ci
     lib.wkv7_oracle_decay.argtypes = [ctypes.c_double]
     lib.wkv7_oracle_decay.restype = ctypes.c_double
@@ -77,20 +77,28 @@ def default_threads() -> int:
     return max(1, len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count() or 1)
 
 
-def fwd(r, w, k, v, a, b, precision: str = "f64", threads: int | None = None):
-    """Forward recurrence.  Inputs [B,T,H,N] (numpy or torch); returns (y, sa) float32."""
+DECAYS = {"clampw": 0, "wind": 1}
+
+
+def fwd(r, w, k, v, a, b, precision: str = "f64", threads: int | None = None,
+        decay: str = "clampw"):
+    """Forward recurrence.  Inputs [B,T,H,N] (numpy or torch); returns (y, sa) float32.
+    ``decay="wind"`` applies the wind_backstepping decay exp(-exp(w)) (then r, a,
+    b are that op's q, z, a)."""
     r, w, k, v, a, b = (_f32(x) for x in (r, w, k, v, a, b))
     B, T, H, N = r.shape
     y = np.empty_like(r)
     sa = np.empty_like(r)
     fn = getattr(_load(), f"wkv7_oracle_fwd_{precision}")
-    rc = fn(B, T, H, N, *map(_ptr, (r, w, k, v, a, b, y, sa)), threads or default_threads())
+    rc = fn(B, T, H, N, *map(_ptr, (r, w, k, v, a, b, y, sa)), DECAYS[decay],
+            threads or default_threads())
     if rc != 0:
         raise RuntimeError(f"oracle forward failed with code {rc}")
     return y, sa
 
 
-def fwd_state(r, w, k, v, a, b, s0=None, precision: str = "f64", threads: int | None = None):
+def fwd_state(r, w, k, v, a, b, s0=None, precision: str = "f64", threads: int | None = None,
+              decay: str = "clampw"):
     """Forward from the start state ``s0`` ([B,H,N,N], element [b,h,i,j] = S[i][j]
     with i the value index; None = zero).  Returns (y, sa, s_final) float32."""
     r, w, k, v, a, b = (_f32(x) for x in (r, w, k, v, a, b))
@@ -100,14 +108,15 @@ def fwd_state(r, w, k, v, a, b, s0=None, precision: str = "f64", threads: int | 
     sa = np.empty_like(r)
     sT = np.empty((B, H, N, N), dtype=np.float32)
     fn = getattr(_load(), f"wkv7_oracle_fwd_state_{precision}")
-    rc = fn(B, T, H, N, *map(_ptr, (r, w, k, v, a, b, s0, y, sa, sT)), threads or default_threads())
+    rc = fn(B, T, H, N, *map(_ptr, (r, w, k, v, a, b, s0, y, sa, sT)), DECAYS[decay],
+            threads or default_threads())
     if rc != 0:
         raise RuntimeError(f"oracle stateful forward failed with code {rc}")
     return y, sa, sT
 
 
 def bwd(r, w, k, v, a, b, dy, dsa=None, precision: str = "f64", ckpt: int = 64,
-        threads: int | None = None):
+        threads: int | None = None, decay: str = "clampw"):
     """Exact gradients (dr, dw, dk, dv, da, db) of sum(dy*y) + sum(dsa*sa), float32."""
     r, w, k, v, a, b, dy = (_f32(x) for x in (r, w, k, v, a, b, dy))
     dsa = None if dsa is None else _f32(dsa)
@@ -115,7 +124,7 @@ def bwd(r, w, k, v, a, b, dy, dsa=None, precision: str = "f64", ckpt: int = 64,
     outs = [np.empty_like(r) for _ in range(6)]
     fn = getattr(_load(), f"wkv7_oracle_bwd_{precision}")
     rc = fn(B, T, H, N, ckpt, *map(_ptr, (r, w, k, v, a, b, dy, dsa)), *map(_ptr, outs),
-            threads or default_threads())
+            DECAYS[decay], threads or default_threads())
     if rc != 0:
         raise RuntimeError(f"oracle backward failed with code {rc}")
     return tuple(outs)
@@ -125,7 +134,7 @@ def decay(w_in: float) -> float:
     return _load().wkv7_oracle_decay(float(w_in))
 
 
-def torch_reference(r, w, k, v, a, b, dy=None, dsa=None, s0=None):
+def torch_reference(r, w, k, v, a, b, dy=None, dsa=None, s0=None, decay: str = "clampw"):
     """Float64 torch restatement of camoe/backbone.py:264-294 returning (y, sa);
     with dy given, also the six input gradients from autograd (sa-gradient dsa
     optional).  ``s0`` ([B,H,N,N], default zero) is the start state.  Small
@@ -136,7 +145,7 @@ def torch_reference(r, w, k, v, a, b, dy=None, dsa=None, s0=None):
           for x in (r, w, k, v, a, b)]
     rr, ww, kk, vv, aa, bb = xs
     B, T, H, N = rr.shape
-    dec = torch.exp(W_SCALE / (1.0 + torch.exp(-ww)))
+    dec = torch.exp(-torch.exp(ww)) if decay == "wind" else torch.exp(W_SCALE / (1.0 + torch.exp(-ww)))
     S = torch.zeros(B, H, N, N, dtype=torch.float64) if s0 is None else \
         torch.as_tensor(_f32(s0), dtype=torch.float64).reshape(B, H, N, N)
     ys, sas = [], []
@@ -158,36 +167,49 @@ def torch_reference(r, w, k, v, a, b, dy=None, dsa=None, s0=None):
 
 
 class RefOp:
-    """The reference's ClampW CUDA op (built from its sources into oracle/_ref/),
-    called with device pointers.  It launches on the legacy default stream and
-    validates nothing, so callers synchronise and pass T % 16 == 0."""
+    """The reference's ClampW CUDA op, or with ``decay="wind"`` its
+    wind_backstepping op (built from its sources into oracle/_ref/), called with
+    device pointers.  Arguments are in the ClampW order (r, w, k, v, a, b) for
+    both; the wind op's own order (w, q, k, v, z, a) is applied here.  It
+    launches on the legacy default stream and validates nothing, so callers
+    synchronise and pass T % 16 == 0."""
 
-    def __init__(self, fp32: bool = False):
-        name = "librwkv7_clampw_ref_fp32.so" if fp32 else "librwkv7_clampw_ref_bf16.so"
-        path = os.path.join(_REF_DIR, name)
+    _NAMES = {("clampw", False): "librwkv7_clampw_ref_bf16.so",
+              ("clampw", True): "librwkv7_clampw_ref_fp32.so",
+              ("wind", False): "libwind_ref_bf16.so", ("wind", True): "libwind_ref_fp32.so"}
+
+    def __init__(self, fp32: bool = False, decay: str = "clampw"):
+        path = os.path.join(_REF_DIR, self._NAMES[(decay, fp32)])
         if not os.path.exists(path):
             raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
+        self.wind = decay == "wind"
         self.lib = ctypes.CDLL(path)
         ci, fp = ctypes.c_int, ctypes.c_void_p
-        self.lib.ref_clampw_fwd.argtypes = [ci] * 3 + [fp] * 9
-        self.lib.ref_clampw_fwd.restype = ci
-        self.lib.ref_clampw_bwd.argtypes = [ci] * 3 + [fp] * 15
-        self.lib.ref_clampw_bwd.restype = ci
+        pre = "ref_wind" if self.wind else "ref_clampw"
+        self._fwd = getattr(self.lib, pre + "_fwd")
+        self._bwd = getattr(self.lib, pre + "_bwd")
+        self._fwd.argtypes = [ci] * 3 + [fp] * 9
+        self._fwd.restype = ci
+        self._bwd.argtypes = [ci] * 3 + [fp] * 15
+        self._bwd.restype = ci
 
     @staticmethod
-    def available(fp32: bool = False) -> bool:
-        name = "librwkv7_clampw_ref_fp32.so" if fp32 else "librwkv7_clampw_ref_bf16.so"
-        return os.path.exists(os.path.join(_REF_DIR, name))
+    def available(fp32: bool = False, decay: str = "clampw") -> bool:
+        return os.path.exists(os.path.join(_REF_DIR, RefOp._NAMES[(decay, fp32)]))
 
     def forward(self, r, w, k, v, a, b, y, s, sa):
         B, T, H, _ = r.shape
-        rc = self.lib.ref_clampw_fwd(B, T, H, *[x.data_ptr() for x in (r, w, k, v, a, b, y, s, sa)])
+        ins = (w, r, k, v, a, b) if self.wind else (r, w, k, v, a, b)
+        rc = self._fwd(B, T, H, *[x.data_ptr() for x in ins + (y, s, sa)])
         if rc != 0:
             raise RuntimeError(f"reference forward failed: cuda error {rc}")
 
     def backward(self, r, w, k, v, a, b, dy, s, sa, dr, dw, dk, dv, da, db):
         B, T, H, _ = r.shape
-        ptrs = [x.data_ptr() for x in (r, w, k, v, a, b, dy, s, sa, dr, dw, dk, dv, da, db)]
-        rc = self.lib.ref_clampw_bwd(B, T, H, *ptrs)
+        if self.wind:
+            ptrs = (w, r, k, v, a, b, dy, s, sa, dw, dr, dk, dv, da, db)
+        else:
+            ptrs = (r, w, k, v, a, b, dy, s, sa, dr, dw, dk, dv, da, db)
+        rc = self._bwd(B, T, H, *[x.data_ptr() for x in ptrs])
         if rc != 0:
             raise RuntimeError(f"reference backward failed: cuda error {rc}")

@@ -5,7 +5,10 @@
  *
  * Restated from the reference:
  *   decay        w = exp(W_SCALE * sigmoid(w_in)), W_SCALE = -exp(-1/2)
- *                (camoe/cuda/rwkv7_clampw.cu:16,42; camoe/backbone.py:20,272)
+ *                (camoe/cuda/rwkv7_clampw.cu:16,42; camoe/backbone.py:20,272);
+ *                with decay = 1, the wind_backstepping op's w = exp(-exp(w_in))
+ *                (camoe/cuda/wkv7_cuda.cu:21,66-67), whose recurrence is the
+ *                same with (q, z, a) in the roles of (r, a, b)
  *   forward      sa_t = S_{t-1} a_t
  *                S_t  = S_{t-1} diag(w_t) + sa_t b_t^T + v_t k_t^T
  *                y_t  = S_t r_t,  S_{-1} = 0
@@ -41,17 +44,32 @@
 /* Body, instantiated once for double (_f64) and once for float (_f32). */
 /* ------------------------------------------------------------------ */
 #define DEFINE_ORACLE(REAL, SUF, EXPF)                                                        \
+/* log-decay lw(w_in): ClampW -e^{-1/2} sigmoid(w_in) (rwkv7_clampw.cu:42),                  \
+ * wind_backstepping -exp(w_in) (wkv7_cuda.cu:21) */                                           \
+static REAL logdecay_##SUF(REAL x, int decay)                                                  \
+{                                                                                              \
+    return decay ? -EXPF(x) : (REAL)W_SCALE_D / ((REAL)1 + EXPF(-x));                          \
+}                                                                                              \
+/* d lw / d w_in: ClampW W_SCALE s (1 - s) (rwkv7_clampw.cu:99-100,147),                      \
+ * wind -exp(w_in) (wkv7_cuda.cu:66,108) */                                                    \
+static REAL dlogdecay_##SUF(REAL x, int decay)                                                 \
+{                                                                                              \
+    if (decay) return -EXPF(x);                                                                \
+    const REAL sg = (REAL)1 / ((REAL)1 + EXPF(-x));                                            \
+    return (REAL)W_SCALE_D * sg * ((REAL)1 - sg);                                              \
+}                                                                                              \
+                                                                                               \
 static void chain_fwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t b, int64_t h,           \
         const float* r, const float* wi, const float* k, const float* v, const float* a,      \
         const float* bb, float* y, float* sa_out, REAL* S, REAL* sa, REAL* wv,                \
-        const float* s0, float* sT)                                                            \
+        const float* s0, float* sT, int decay)                                                 \
 {                                                                                              \
     if (s0) for (int64_t e = 0; e < N * N; ++e) S[e] = (REAL)s0[e];                            \
     else memset(S, 0, sizeof(REAL) * N * N);                                                   \
     for (int64_t t = 0; t < T; ++t) {                                                          \
         const int64_t base = ((b * T + t) * H + h) * N;                                        \
         for (int64_t j = 0; j < N; ++j)                                                        \
-            wv[j] = EXPF((REAL)W_SCALE_D / ((REAL)1 + EXPF(-(REAL)wi[base + j])));            \
+            wv[j] = EXPF(logdecay_##SUF((REAL)wi[base + j], decay));            \
         for (int64_t i = 0; i < N; ++i) {                                                      \
             REAL acc = 0;                                                                      \
             const REAL* Si = S + i * N;                                                        \
@@ -96,7 +114,7 @@ static void step_##SUF(int64_t N, const REAL* wv, const float* k, const float* v
 static int chain_bwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t ck, int64_t b, int64_t h, \
         const float* r, const float* wi, const float* k, const float* v, const float* a,      \
         const float* bb, const float* dy, const float* dsa_ext,                               \
-        float* dr, float* dw, float* dk, float* dv, float* da, float* db)                     \
+        float* dr, float* dw, float* dk, float* dv, float* da, float* db, int decay)          \
 {                                                                                              \
     const int64_t nck = (T + ck - 1) / ck;                                                     \
     const int64_t NN = N * N;                                                                  \
@@ -120,7 +138,7 @@ static int chain_bwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t ck, int64_t 
         for (int64_t t = c * ck; t < t1; ++t) {                                                \
             const int64_t base = ((b * T + t) * H + h) * N;                                    \
             for (int64_t j = 0; j < N; ++j)                                                    \
-                wtmp[j] = EXPF((REAL)W_SCALE_D / ((REAL)1 + EXPF(-(REAL)wi[base + j])));      \
+                wtmp[j] = EXPF(logdecay_##SUF((REAL)wi[base + j], decay));      \
             step_##SUF(N, wtmp, k + base, v + base, a + base, bb + base, Sbuf,                 \
                        Sbuf + NN, satmp);                                                      \
             memcpy(Sbuf, Sbuf + NN, sizeof(REAL) * NN);                                        \
@@ -134,7 +152,7 @@ static int chain_bwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t ck, int64_t 
         for (int64_t u = 0; u < len; ++u) {                                                    \
             const int64_t base = ((b * T + t0 + u) * H + h) * N;                               \
             for (int64_t j = 0; j < N; ++j)                                                    \
-                wbuf[u * N + j] = EXPF((REAL)W_SCALE_D / ((REAL)1 + EXPF(-(REAL)wi[base + j]))); \
+                wbuf[u * N + j] = EXPF(logdecay_##SUF((REAL)wi[base + j], decay)); \
             step_##SUF(N, wbuf + u * N, k + base, v + base, a + base, bb + base,               \
                        Sbuf + u * NN, Sbuf + (u + 1) * NN, sabuf + u * N);                     \
         }                                                                                      \
@@ -176,8 +194,7 @@ static int chain_bwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t ck, int64_t 
                     ab += g * sat[i];                                                          \
                     aa += dsa[i] * Sp[i * N + j];                                              \
                 }                                                                              \
-                const REAL sg = (REAL)1 / ((REAL)1 + EXPF(-(REAL)wi[base + j]));               \
-                dw[base + j] = (float)((REAL)W_SCALE_D * aw * wt[j] * sg * ((REAL)1 - sg));    \
+                dw[base + j] = (float)(aw * wt[j] * dlogdecay_##SUF((REAL)wi[base + j], decay)); \
                 dk[base + j] = (float)ak;                                                      \
                 db[base + j] = (float)ab;                                                      \
                 da[base + j] = (float)aa;                                                      \
@@ -197,7 +214,7 @@ static int chain_bwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t ck, int64_t 
                                                                                                \
 int wkv7_oracle_fwd_##SUF(int64_t B, int64_t T, int64_t H, int64_t N,                         \
         const float* r, const float* w, const float* k, const float* v, const float* a,       \
-        const float* b, float* y, float* sa, int nthreads)                                     \
+        const float* b, float* y, float* sa, int decay, int nthreads)                          \
 {                                                                                              \
     if (B < 0 || T < 0 || H < 0 || N <= 0) return ORACLE_ERR_ARG;                              \
     int err = ORACLE_OK;                                                                       \
@@ -207,7 +224,7 @@ int wkv7_oracle_fwd_##SUF(int64_t B, int64_t T, int64_t H, int64_t N,           
         REAL* sab = (REAL*)malloc(sizeof(REAL) * (size_t)N * 2);                               \
         if (!S || !sab) { free(S); free(sab); err = ORACLE_ERR_NOMEM; continue; }              \
         chain_fwd_##SUF(T, H, N, c / H, c % H, r, w, k, v, a, b, y, sa, S, sab, sab + N,       \
-                        NULL, NULL);                                                           \
+                        NULL, NULL, decay);                                                    \
         free(S); free(sab);                                                                    \
     }                                                                                          \
     return err;                                                                                \
@@ -221,7 +238,8 @@ int wkv7_oracle_fwd_##SUF(int64_t B, int64_t T, int64_t H, int64_t N,           
  * forward over [0, T). */                                                     \
 int wkv7_oracle_fwd_state_##SUF(int64_t B, int64_t T, int64_t H, int64_t N,                   \
         const float* r, const float* w, const float* k, const float* v, const float* a,       \
-        const float* b, const float* s0, float* y, float* sa, float* sT, int nthreads)         \
+        const float* b, const float* s0, float* y, float* sa, float* sT, int decay,            \
+        int nthreads)                                                                          \
 {                                                                                              \
     if (B < 0 || T < 0 || H < 0 || N <= 0) return ORACLE_ERR_ARG;                              \
     int err = ORACLE_OK;                                                                       \
@@ -231,7 +249,7 @@ int wkv7_oracle_fwd_state_##SUF(int64_t B, int64_t T, int64_t H, int64_t N,     
         REAL* sab = (REAL*)malloc(sizeof(REAL) * (size_t)N * 2);                               \
         if (!S || !sab) { free(S); free(sab); err = ORACLE_ERR_NOMEM; continue; }              \
         chain_fwd_##SUF(T, H, N, c / H, c % H, r, w, k, v, a, b, y, sa, S, sab, sab + N,       \
-                        s0 ? s0 + c * N * N : NULL, sT ? sT + c * N * N : NULL);               \
+                        s0 ? s0 + c * N * N : NULL, sT ? sT + c * N * N : NULL, decay);        \
         free(S); free(sab);                                                                    \
     }                                                                                          \
     return err;                                                                                \
@@ -240,14 +258,15 @@ int wkv7_oracle_fwd_state_##SUF(int64_t B, int64_t T, int64_t H, int64_t N,     
 int wkv7_oracle_bwd_##SUF(int64_t B, int64_t T, int64_t H, int64_t N, int64_t ckpt,           \
         const float* r, const float* w, const float* k, const float* v, const float* a,       \
         const float* b, const float* dy, const float* dsa,                                    \
-        float* dr, float* dw, float* dk, float* dv, float* da, float* db, int nthreads)       \
+        float* dr, float* dw, float* dk, float* dv, float* da, float* db, int decay,           \
+        int nthreads)                                                                          \
 {                                                                                              \
     if (B < 0 || T < 0 || H < 0 || N <= 0 || ckpt <= 0) return ORACLE_ERR_ARG;                 \
     int err = ORACLE_OK;                                                                       \
     _Pragma("omp parallel for schedule(dynamic) num_threads(nthreads > 0 ? nthreads : 1)")     \
     for (int64_t c = 0; c < B * H; ++c) {                                                      \
         int e = chain_bwd_##SUF(T, H, N, ckpt, c / H, c % H, r, w, k, v, a, b, dy, dsa,        \
-                                dr, dw, dk, dv, da, db);                                       \
+                                dr, dw, dk, dv, da, db, decay);                                \
         if (e) err = e;                                                                        \
     }                                                                                          \
     return err;                                                                                \

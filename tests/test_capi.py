@@ -24,6 +24,26 @@ def test_header_declares_expected_entry_points():
         assert n in names
 
 
+def header_param_counts():
+    src = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(camoe_wkv7_\w+)\s*\(([^)]*)\)\s*;", src):
+        params = params.strip()
+        out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_bindings_declare_the_header_argument_counts():
+    """Every function the ctypes binding calls has argtypes of the header's arity
+    (an unset argtypes would pass 64-bit pointers and sizes as C ints)."""
+    lib = _lib.lib()
+    counts = header_param_counts()
+    for name in _lib.EXPORTS:
+        f = getattr(lib, name)
+        assert f.argtypes is not None, name
+        assert len(f.argtypes) == counts[name], name
+
+
 def test_library_exports_every_header_function():
     lib = _lib.lib()
     for name in header_functions():

@@ -130,3 +130,41 @@ def test_empty_inputs():
         y, sa, ck = ops.wkv7_forward(*xs)
         g = ops.wkv7_backward(*xs, torch.zeros_like(xs[0]), None, ck)
         assert y.shape == (B, T, H, 64) and all(t.shape == (B, T, H, 64) for t in g)
+
+
+@pytest.mark.parametrize("decay", ["clampw", "wind"])
+def test_first_call_on_a_fresh_thread(decay):
+    """The op's first CUDA call on a thread (as on a framework's backward worker
+    thread, before anything else there touched the device) gives the main
+    thread's results: the chunked path binds the device's context before it
+    encodes its TMA descriptors.  All buffers come from the main thread."""
+    import threading
+
+    B, T, H = 2, 64, 3
+    inp = make_inputs(B, T, H, 64, seed=12, decay=decay)
+    xs = [inp[n].to(torch.bfloat16).cuda() for n in NAMES]
+    dy = inp["dy"].to(torch.bfloat16).cuda()
+    y0, sa0, ck0 = ops.wkv7_forward(*xs, decay=decay)
+    g0 = ops.wkv7_backward(*xs, dy, None, ck0, decay=decay)
+    y, sa, ck = torch.empty_like(y0), torch.empty_like(sa0), torch.empty_like(ck0)
+    grads = tuple(torch.empty_like(g) for g in g0)
+    work = torch.empty(max(ops.work_bytes(B, T, H, torch.bfloat16), 16), dtype=torch.uint8,
+                       device="cuda")
+    torch.cuda.synchronize()
+    errors = []
+
+    def run():
+        try:
+            ops.wkv7_forward(*xs, y=y, sa=sa, ckpt=ck, decay=decay)
+            ops.wkv7_backward(*xs, dy, None, ck, grads=grads, work=work, decay=decay)
+        except Exception as e:  # reported on the main thread
+            errors.append(e)
+
+    th = threading.Thread(target=run)
+    th.start()
+    th.join()
+    torch.cuda.synchronize()
+    assert not errors, errors
+    assert torch.equal(y, y0) and torch.equal(sa, sa0)
+    for g, w in zip(grads, g0):
+        assert torch.equal(g, w)

@@ -119,3 +119,26 @@ def test_oracle_state_split_identity(T1):
     assert nrel(np.concatenate([ya, yb], 1), y) < 1e-5
     assert nrel(np.concatenate([saa, sab], 1), sa) < 1e-5
     assert nrel(s2, sT) < 1e-5
+
+
+def test_oracle_wind_decay_against_torch_autograd():
+    """The wind_backstepping decay exp(-exp(w)) (camoe/cuda/wkv7_cuda.cu:21,66-67,108):
+    forward and all six gradients of the C oracle against float64 torch autograd."""
+    inp = make_inputs(1, 40, 2, seed=8, decay="wind", with_dsa=True)
+    xs = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    y, sa = oracle.fwd(*xs, decay="wind")
+    grads = oracle.bwd(*xs, inp["dy"], inp["dsa"], decay="wind", ckpt=16)
+    ref = oracle.torch_reference(*xs, dy=inp["dy"], dsa=inp["dsa"], decay="wind")
+    for name, got, want in zip(("y", "sa") + GRADS, (y, sa) + grads, ref):
+        assert nrel(got, want) < 1e-6, name
+    # the decay differs from ClampW's on the same inputs
+    y_c, _ = oracle.fwd(*xs)
+    assert nrel(y_c, y) > 1e-3
+
+
+def test_wind_inputs_are_in_the_bounded_decay_range():
+    inp = make_inputs(2, 64, 4, seed=9, decay="wind", w_sigma=3.0)
+    assert float(inp["w"].max()) <= -0.5
+    lo = math.exp(-math.exp(-0.5))
+    dec = np.exp(-np.exp(inp["w"].numpy().astype(np.float64)))
+    assert dec.min() >= lo - 1e-12 and dec.max() < 1
