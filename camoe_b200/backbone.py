@@ -17,7 +17,10 @@ Same module-level names and call contract:
   reference's ``backward(ctx, dy)`` cannot be called by autograd for a
   two-output Function);
 * ``RUN_CUDA_RWKV7(r, w, k, v, a, b)`` on ``[B, T, C]`` tensors returning
-  ``(y, sa)`` in the caller's dtype (camoe/backbone.py:104-121).
+  ``(y, sa)`` in the caller's dtype (camoe/backbone.py:104-121);
+* the reference's second op, ``torch.ops.wind_backstepping.forward/backward``
+  (camoe/cuda/wkv7_op.cpp:18-21, decay exp(-exp(w))), registered by
+  ``init_rwkv7_cuda`` too, and ``WindBackstepping``, its autograd Function.
 
 Environment flags read by ``init_rwkv7_cuda`` as in the reference:
 ``CAMOE_FORCE_FP32_KERNEL=1`` selects fp32 inputs and the fp32-exact scan.
