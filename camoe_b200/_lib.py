@@ -23,6 +23,12 @@ EXPORTS = ("camoe_wkv7_version", "camoe_wkv7_strerror", "camoe_wkv7_last_cuda_er
            "camoe_wkv7_state_work_bytes", "camoe_wkv7_wind_fwd", "camoe_wkv7_wind_bwd")
 
 
+# include/camoe_timemix.h: fused elementwise kernels of the time mix
+TM_EXPORTS = ("camoe_tm_work_bytes", "camoe_tm_mix_fwd", "camoe_tm_mix_bwd", "camoe_tm_prep_fwd",
+              "camoe_tm_prep_bwd", "camoe_tm_post_fwd", "camoe_tm_post_bwd", "camoe_tm_lnsa_fwd",
+              "camoe_tm_lnsa_bwd")
+
+
 class CamoeError(RuntimeError):
     """A non-zero status from the C ABI."""
 
@@ -63,6 +69,18 @@ def lib() -> ctypes.CDLL:
     l.camoe_wkv7_state_work_bytes.argtypes = [i64, i64, i64, ci, ci, ci]
     l.camoe_wkv7_bwd.restype = ci
     l.camoe_wkv7_bwd.argtypes = [vp] * 9 + [sz, vp, sz] + [vp] * 6 + [i64] * 5 + [ci, ci, ci, vp]
+    l.camoe_tm_work_bytes.restype = sz
+    l.camoe_tm_work_bytes.argtypes = [i64] * 3
+    l.camoe_tm_mix_fwd.argtypes = [vp, ci, vp, vp] + [i64] * 3 + [vp]
+    l.camoe_tm_mix_bwd.argtypes = [vp, ci, vp, vp, vp, vp, vp, sz] + [i64] * 3 + [vp]
+    l.camoe_tm_prep_fwd.argtypes = [vp] * 12 + [i64] * 3 + [vp]
+    l.camoe_tm_prep_bwd.argtypes = [vp] * 26 + [sz] + [i64] * 3 + [vp]
+    l.camoe_tm_post_fwd.argtypes = [vp] * 9 + [i64] * 3 + [vp]
+    l.camoe_tm_post_bwd.argtypes = [vp] * 16 + [sz] + [i64] * 3 + [vp]
+    l.camoe_tm_lnsa_fwd.argtypes = [vp] * 4 + [i64] * 3 + [vp]
+    l.camoe_tm_lnsa_bwd.argtypes = [vp] * 6 + [sz] + [i64] * 3 + [vp]
+    for n in TM_EXPORTS[1:]:
+        getattr(l, n).restype = ci
     # the wind op's entry points take the ClampW ones' argument types
     l.camoe_wkv7_wind_fwd.restype = ci
     l.camoe_wkv7_wind_fwd.argtypes = l.camoe_wkv7_fwd.argtypes

@@ -8,26 +8,28 @@ import pytest
 
 from camoe_b200 import _lib
 
-HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
-                      "include", "camoe_wkv7.h")
+INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+HEADER = os.path.join(INCLUDE, "camoe_wkv7.h")
+HEADERS = [os.path.join(INCLUDE, h) for h in ("camoe_wkv7.h", "camoe_timemix.h")]
+
+
+def _sources():
+    return "\n".join(re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S) for h in HEADERS)
 
 
 def header_functions():
-    src = open(HEADER).read()
-    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(camoe_wkv7_\w+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b(camoe_(?:wkv7|tm)_\w+)\s*\(", _sources())))
 
 
 def test_header_declares_expected_entry_points():
     names = header_functions()
-    for n in _lib.EXPORTS:
+    for n in _lib.EXPORTS + _lib.TM_EXPORTS:
         assert n in names
 
 
 def header_param_counts():
-    src = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
     out = {}
-    for name, params in re.findall(r"\b(camoe_wkv7_\w+)\s*\(([^)]*)\)\s*;", src):
+    for name, params in re.findall(r"\b(camoe_(?:wkv7|tm)_\w+)\s*\(([^)]*)\)\s*;", _sources()):
         params = params.strip()
         out[name] = 0 if params in ("", "void") else params.count(",") + 1
     return out
@@ -38,7 +40,7 @@ def test_bindings_declare_the_header_argument_counts():
     (an unset argtypes would pass 64-bit pointers and sizes as C ints)."""
     lib = _lib.lib()
     counts = header_param_counts()
-    for name in _lib.EXPORTS:
+    for name in _lib.EXPORTS + _lib.TM_EXPORTS:
         f = getattr(lib, name)
         assert f.argtypes is not None, name
         assert len(f.argtypes) == counts[name], name
