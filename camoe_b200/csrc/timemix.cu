@@ -3,16 +3,22 @@
 //
 // Each kernel is one pass over HBM for what the reference runs as chains of
 // eager PyTorch ops (each a separate read and write of [B, T, C] tensors).
-// Layout: one CTA of C/2 threads owns whole rows (one time step of one
-// sequence); thread i holds columns 2i and 2i+1 (bf16x2 / float2 accesses,
-// each warp one coalesced 128-byte line per bf16 tensor), so warp w is head w
-// and the per-head sums (key normalisation, GroupNorm, the bonus term) are
-// warp shuffles; the LayerNorm over C adds one shared-memory step.  CTAs walk
-// work items of kRows consecutive steps of one sequence (the token shift
-// reads the previous step from registers).  Parameter gradients are summed
-// over a CTA's rows in registers, written as one partial row per CTA and
-// added by partial_reduce_kernel in a fixed order (deterministic).
-// All arithmetic is fp32; activations are stored in bf16.
+// Layout: one CTA owns one row (one time step of one sequence) at a time.
+// In mix_fwd, post and lnsa the CTA has C/8 threads and thread i holds
+// columns 8i..8i+7 (one 16-byte access per bf16 tensor, two per fp32 one), so
+// a head (64 columns) is 8 adjacent threads and a per-head sum (GroupNorm,
+// the bonus term) is three xor-shuffles; the LayerNorm over C adds one
+// shared-memory step.  mix_bwd and prep, which keep the most values live per
+// column (six mixes and their gradient sums; fifteen input tensors), use C/2
+// threads of two columns each (warp = head) so that they fit in 64 registers
+// at full occupancy: measured faster than eight columns on B200.
+// CTAs walk work items of kRows consecutive steps of one sequence (the token
+// shift takes the neighbouring step from registers), U rows in flight per
+// thread: the loads of U rows are issued before any of them is used.
+// Per-column parameters too many for registers live in shared memory.
+// Parameter gradients are summed over a CTA's rows in registers, written as
+// one partial row per CTA and added by partial_reduce_kernel in a fixed
+// order (deterministic).  All arithmetic is fp32; activations are bf16.
 #include <initializer_list>
 
 #include "camoe_timemix.h"
@@ -23,9 +29,10 @@ void set_last_cuda_error(int e);  // wkv7_capi.cu: reported by camoe_wkv7_last_c
 
 namespace tm {
 
-constexpr int kRows = 4;      // time steps per work item (small items balance the one wave)
+constexpr int kRows = 4;       // time steps per work item (small items balance the one wave)
 constexpr int kMaxGrid = 1024;
 constexpr int kMaxParams = 6;  // parameter vectors of the backward with the most (mix)
+constexpr int V = 8;           // columns per thread
 
 struct Shape {
   int64_t B, T, C;
@@ -33,21 +40,49 @@ struct Shape {
   __host__ __device__ int64_t items() const { return B * nblk; }
 };
 
-__device__ __forceinline__ float2 ld2(const bf16* p) {
-  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+// 8 bf16 <-> 8 floats
+__device__ __forceinline__ uint4 ldv(const bf16* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ void unpack(const uint4& u, float (&f)[V]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
 }
-__device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
-__device__ __forceinline__ void st2(bf16* p, float a, float b) {
-  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+__device__ __forceinline__ void ld8(const bf16* p, float (&f)[V]) { unpack(ldv(p), f); }
+__device__ __forceinline__ void ld8(const float* p, float (&f)[V]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
-__device__ __forceinline__ void st2(float* p, float a, float b) {
-  *reinterpret_cast<float2*>(p) = make_float2(a, b);
+__device__ __forceinline__ void st8(bf16* p, const float (&f)[V]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void st8(float* p, const float (&f)[V]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
 }
 
-__device__ __forceinline__ float warp_sum(float x) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+// lanes of this thread's warp that exist (the last warp of a CTA of C/8 < 32
+// threads, or of C/8 not a multiple of 32, is partial)
+__device__ __forceinline__ unsigned warp_lanes() {
+  const unsigned n = blockDim.x - (threadIdx.x & ~31u);
+  return n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
+}
+// sum over the 8 threads of a head
+__device__ __forceinline__ float head_sum(float x, unsigned m) {
+  x += __shfl_xor_sync(m, x, 1);
+  x += __shfl_xor_sync(m, x, 2);
+  x += __shfl_xor_sync(m, x, 4);
   return x;
+}
+__device__ __forceinline__ float sum8(const float (&a)[V]) {
+  return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
 }
 
 __device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
@@ -62,11 +97,26 @@ __device__ __forceinline__ void item_rows(const Shape& S, int64_t item, int64_t&
   t1 = t0 + kRows < S.T ? t0 + kRows : S.T;
 }
 
-// -------------------------------------------------------------------------
-// Every kernel walks its item's rows U at a time: the loads of U rows are
-// issued before any of them is used (U independent rows in flight per
-// thread), then the rows are computed and stored.
+// Two-columns-per-thread kernels (CTA of C/2 threads, warp = head): the
+// layout of the kernels with the most live values per column, where eight
+// columns per thread would cost occupancy.
+__device__ __forceinline__ float2 ld2(const bf16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+__device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ void st2(bf16* p, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+}
+__device__ __forceinline__ void st2(float* p, float a, float b) {
+  *reinterpret_cast<float2*>(p) = make_float2(a, b);
+}
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
 
+// -------------------------------------------------------------------------
 // token shift and mixes (backbone.py:316-323):
 //   xx = shift(x) - x;  x_m = x + xx * mix_m
 struct Out6 {
@@ -77,37 +127,47 @@ struct In6 {
 };
 
 template <typename Tx>
-__global__ void __launch_bounds__(1024) mix_fwd_kernel(const Tx* __restrict__ x,
-                                                       const float* __restrict__ mix, Out6 out,
-                                                       Shape S) {
-  constexpr int U = 2;
-  const int c = 2 * threadIdx.x;
+__global__ void __launch_bounds__(256) mix_fwd_kernel(const Tx* __restrict__ x,
+                                                      const float* __restrict__ mix, Out6 out,
+                                                      Shape S) {
+  const int c = V * threadIdx.x;
   const int64_t C = S.C;
-  float m0[6], m1[6];
+  float mx[6][V];
 #pragma unroll
-  for (int m = 0; m < 6; ++m) {
-    m0[m] = mix[m * C + c];
-    m1[m] = mix[m * C + c + 1];
-  }
+  for (int m = 0; m < 6; ++m) ld8(mix + m * C + c, mx[m]);
   for (int64_t item = blockIdx.x; item < S.items(); item += gridDim.x) {
     int64_t b, t0, t1;
     item_rows(S, item, b, t0, t1);
-    float2 xp = t0 > 0 ? ld2(x + (b * S.T + t0 - 1) * C + c) : make_float2(0.f, 0.f);
-    for (int64_t tb = t0; tb < t1; tb += U) {
-      const int nu = t1 - tb < U ? static_cast<int>(t1 - tb) : U;
-      const int64_t o0 = (b * S.T + tb) * C + c;
-      float2 xc[U];
+    float xp[V];
+    if (t0 > 0) {
+      ld8(x + (b * S.T + t0 - 1) * C + c, xp);
+    } else {
 #pragma unroll
-      for (int u = 0; u < U; ++u) xc[u] = ld2(x + o0 + (u < nu ? u : nu - 1) * C);
+      for (int e = 0; e < V; ++e) xp[e] = 0.f;
+    }
+    float xc[kRows][V];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const float dx0 = xp.x - xc[u].x, dx1 = xp.y - xc[u].y;
-        if (u < nu)
+    for (int u = 0; u < kRows; ++u) {  // rows past the item repeat its last one
+      const int64_t t = t0 + u < t1 ? t0 + u : t1 - 1;
+      ld8(x + (b * S.T + t) * C + c, xc[u]);
+    }
 #pragma unroll
-          for (int m = 0; m < 6; ++m)
-            st2(out.p[m] + o0 + u * C, xc[u].x + dx0 * m0[m], xc[u].y + dx1 * m1[m]);
-        xp = xc[u];
+    for (int u = 0; u < kRows; ++u) {
+      float d[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) d[e] = xp[e] - xc[u][e];
+      if (t0 + u < t1) {
+        const int64_t o = (b * S.T + t0 + u) * C + c;
+#pragma unroll
+        for (int m = 0; m < 6; ++m) {
+          float y[V];
+#pragma unroll
+          for (int e = 0; e < V; ++e) y[e] = xc[u][e] + d[e] * mx[m][e];
+          st8(out.p[m] + o, y);
+        }
       }
+#pragma unroll
+      for (int e = 0; e < V; ++e) xp[e] = xc[u][e];
     }
   }
 }
@@ -335,35 +395,50 @@ struct Post {
   const float *rk, *gamma, *beta;
 };
 
-__global__ void __launch_bounds__(1024) post_fwd_kernel(Post p, bf16* __restrict__ z, Shape S) {
-  constexpr int U = 4;
-  const int c = 2 * threadIdx.x;
+__global__ void __launch_bounds__(256) post_fwd_kernel(Post p, bf16* __restrict__ z, Shape S) {
+  constexpr int U = 2;
+  const int c = V * threadIdx.x;
   const int64_t C = S.C;
-  const float2 gm = ld2(p.gamma + c), bt = ld2(p.beta + c), rk = ld2(p.rk + c);
+  const unsigned lanes = warp_lanes();
+  float gm[V], bt[V], rk[V];
+  ld8(p.gamma + c, gm);
+  ld8(p.beta + c, bt);
+  ld8(p.rk + c, rk);
   for (int64_t item = blockIdx.x; item < S.items(); item += gridDim.x) {
     int64_t b, t0, t1;
     item_rows(S, item, b, t0, t1);
     for (int64_t tb = t0; tb < t1; tb += U) {
-      const int nu = t1 - tb < U ? static_cast<int>(t1 - tb) : U;
-      const int64_t o0 = (b * S.T + tb) * C + c;
-      float2 y[U], r[U], ko[U], vo[U], g[U];
+      uint4 y[U], r[U], ko[U], vo[U], g[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t o = o0 + (u < nu ? u : nu - 1) * C;  // rows past the item repeat its last one
-        y[u] = ld2(p.y + o); r[u] = ld2(p.r + o); ko[u] = ld2(p.ko + o); vo[u] = ld2(p.vo + o);
-        g[u] = ld2(p.g + o);
+      for (int u = 0; u < U; ++u) {  // rows past the item repeat its last one
+        const int64_t o = (b * S.T + (tb + u < t1 ? tb + u : t1 - 1)) * C + c;
+        y[u] = ldv(p.y + o); r[u] = ldv(p.r + o); ko[u] = ldv(p.ko + o); vo[u] = ldv(p.vo + o);
+        g[u] = ldv(p.g + o);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        {
-          const float mean = warp_sum(y[u].x + y[u].y) * (1.f / 64.f);
-          const float d0 = y[u].x - mean, d1 = y[u].y - mean;
-          const float rstd = rsqrtf(warp_sum(d0 * d0 + d1 * d1) * (1.f / 64.f) + 64e-5f);
-          const float s = warp_sum(r[u].x * ko[u].x * rk.x + r[u].y * ko[u].y * rk.y);
-          const float x0 = d0 * rstd * gm.x + bt.x + s * vo[u].x;
-          const float x1 = d1 * rstd * gm.y + bt.y + s * vo[u].y;
-          if (u < nu) st2(z + o0 + u * C, x0 * g[u].x, x1 * g[u].y);
+        float yf[V], rf[V], kf[V], sr = 0.f;
+        unpack(y[u], yf);
+        unpack(r[u], rf);
+        unpack(ko[u], kf);
+#pragma unroll
+        for (int e = 0; e < V; ++e) sr += rf[e] * kf[e] * rk[e];
+        const float mean = head_sum(sum8(yf), lanes) * (1.f / 64.f);
+        float vs = 0.f;
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          yf[e] -= mean;
+          vs += yf[e] * yf[e];
         }
+        const float rstd = rsqrtf(head_sum(vs, lanes) * (1.f / 64.f) + 64e-5f);
+        const float s = head_sum(sr, lanes);
+        if (tb + u >= t1) continue;
+        float vf[V], gf[V];
+        unpack(vo[u], vf);
+        unpack(g[u], gf);
+#pragma unroll
+        for (int e = 0; e < V; ++e) yf[e] = (yf[e] * rstd * gm[e] + bt[e] + s * vf[e]) * gf[e];
+        st8(z + (b * S.T + tb + u) * C + c, yf);
       }
     }
   }
@@ -374,210 +449,249 @@ struct PostBwd {
   bf16 *dy, *dr, *dk, *dv, *dg;
 };
 
-__global__ void __launch_bounds__(1024) post_bwd_kernel(Post p, PostBwd q, float* __restrict__ part,
-                                                        Shape S) {
-  constexpr int U = 2;
-  const int c = 2 * threadIdx.x;
+__global__ void __launch_bounds__(256) post_bwd_kernel(Post p, PostBwd q, float* __restrict__ part,
+                                                       Shape S) {
+  const int c = V * threadIdx.x;
   const int64_t C = S.C;
-  const float2 gm = ld2(p.gamma + c), bt = ld2(p.beta + c), rk = ld2(p.rk + c);
-  float acc[3][2] = {};  // gamma, beta, r_k
+  const unsigned lanes = warp_lanes();
+  float gm[V], rk[V];
+  ld8(p.gamma + c, gm);
+  ld8(p.rk + c, rk);
+  float acc[3][V];  // gamma, beta, r_k
+#pragma unroll
+  for (int k = 0; k < 3; ++k)
+#pragma unroll
+    for (int e = 0; e < V; ++e) acc[k][e] = 0.f;
   for (int64_t item = blockIdx.x; item < S.items(); item += gridDim.x) {
     int64_t b, t0, t1;
     item_rows(S, item, b, t0, t1);
-    for (int64_t tb = t0; tb < t1; tb += U) {
-      const int nu = t1 - tb < U ? static_cast<int>(t1 - tb) : U;
-      const int64_t o0 = (b * S.T + tb) * C + c;
-      float2 y[U], r[U], ko[U], vo[U], g[U], dz[U];
+    for (int64_t t = t0; t < t1; ++t) {
+      const int64_t o = (b * S.T + t) * C + c;
+      const uint4 yp = ldv(p.y + o), rp = ldv(p.r + o), kp = ldv(p.ko + o), vp = ldv(p.vo + o);
+      const uint4 gp = ldv(p.g + o), dzp = ldv(q.dz + o);
+      float yn[V], rf[V], kf[V], sr = 0.f;
+      unpack(yp, yn);
+      unpack(rp, rf);
+      unpack(kp, kf);
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t o = o0 + (u < nu ? u : nu - 1) * C;  // rows past the item repeat its last one
-        y[u] = ld2(p.y + o); r[u] = ld2(p.r + o); ko[u] = ld2(p.ko + o); vo[u] = ld2(p.vo + o);
-        g[u] = ld2(p.g + o);
-        dz[u] = ld2(q.dz + o);
-        if (u >= nu) dz[u] = make_float2(0.f, 0.f);  // contributes nothing to the parameter sums
-      }
+      for (int e = 0; e < V; ++e) sr += rf[e] * kf[e] * rk[e];
+      const float mean = head_sum(sum8(yn), lanes) * (1.f / 64.f);
+      float vs = 0.f;
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t o = o0 + u * C;
-        const bool live = u < nu;
-        const float mean = warp_sum(y[u].x + y[u].y) * (1.f / 64.f);
-        const float d0 = y[u].x - mean, d1 = y[u].y - mean;
-        const float rstd = rsqrtf(warp_sum(d0 * d0 + d1 * d1) * (1.f / 64.f) + 64e-5f);
-        const float s = warp_sum(r[u].x * ko[u].x * rk.x + r[u].y * ko[u].y * rk.y);
-        const float yn0 = d0 * rstd, yn1 = d1 * rstd;
-        const float xa0 = yn0 * gm.x + bt.x + s * vo[u].x, xa1 = yn1 * gm.y + bt.y + s * vo[u].y;
-        const float dx0 = dz[u].x * g[u].x, dx1 = dz[u].y * g[u].y;  // d x_att
-        if (live) st2(q.dg + o, dz[u].x * xa0, dz[u].y * xa1);
-        acc[0][0] += dx0 * yn0;
-        acc[0][1] += dx1 * yn1;
-        acc[1][0] += dx0;
-        acc[1][1] += dx1;
-        const float dn0 = dx0 * gm.x, dn1 = dx1 * gm.y;  // d yn
-        const float m1 = warp_sum(dn0 + dn1) * (1.f / 64.f);
-        const float m2 = warp_sum(dn0 * yn0 + dn1 * yn1) * (1.f / 64.f);
-        const float ds = warp_sum(dx0 * vo[u].x + dx1 * vo[u].y);
-        if (live) {
-          st2(q.dy + o, rstd * (dn0 - m1 - yn0 * m2), rstd * (dn1 - m1 - yn1 * m2));
-          // bonus s v': dv' = dx s, ds = <dx, v'>, s = sum r k' r_k
-          st2(q.dv + o, dx0 * s, dx1 * s);
-          st2(q.dr + o, ds * ko[u].x * rk.x, ds * ko[u].y * rk.y);
-          st2(q.dk + o, ds * r[u].x * rk.x, ds * r[u].y * rk.y);
-        }
-        acc[2][0] += ds * r[u].x * ko[u].x;
-        acc[2][1] += ds * r[u].y * ko[u].y;
+      for (int e = 0; e < V; ++e) {
+        yn[e] -= mean;
+        vs += yn[e] * yn[e];
       }
+      const float rstd = rsqrtf(head_sum(vs, lanes) * (1.f / 64.f) + 64e-5f);
+      const float s = head_sum(sr, lanes);
+      float vf[V], gf[V], dz[V], bt[V];
+      unpack(vp, vf);
+      unpack(gp, gf);
+      unpack(dzp, dz);
+      ld8(p.beta + c, bt);
+      float dxa[V], m1 = 0.f, m2 = 0.f, dsv = 0.f;
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        yn[e] *= rstd;
+        const float xa = yn[e] * gm[e] + bt[e] + s * vf[e];
+        dxa[e] = dz[e] * gf[e];             // d x_att
+        gf[e] = dz[e] * xa;                 // dg (gf reused)
+        acc[0][e] += dxa[e] * yn[e];
+        acc[1][e] += dxa[e];
+        const float dn = dxa[e] * gm[e];    // d yn
+        m1 += dn;
+        m2 += dn * yn[e];
+        dsv += dxa[e] * vf[e];
+      }
+      st8(q.dg + o, gf);
+      m1 = head_sum(m1, lanes) * (1.f / 64.f);
+      m2 = head_sum(m2, lanes) * (1.f / 64.f);
+      const float ds = head_sum(dsv, lanes);  // bonus s v': ds = <dx, v'>, s = sum r k' r_k
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        dz[e] = rstd * (dxa[e] * gm[e] - m1 - yn[e] * m2);  // dy (dz reused)
+        vf[e] = dxa[e] * s;                                 // dv'
+        acc[2][e] += ds * rf[e] * kf[e];
+      }
+      st8(q.dy + o, dz);
+      st8(q.dv + o, vf);
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        const float dr = ds * kf[e] * rk[e], dk = ds * rf[e] * rk[e];
+        rf[e] = dr;
+        kf[e] = dk;
+      }
+      st8(q.dr + o, rf);
+      st8(q.dk + o, kf);
     }
   }
   float* pp = part + static_cast<int64_t>(blockIdx.x) * 3 * C;
 #pragma unroll
-  for (int k = 0; k < 3; ++k) st2(pp + k * C + c, acc[k][0], acc[k][1]);
+  for (int k = 0; k < 3; ++k) st8(pp + k * C + c, acc[k]);
 }
 
 // -------------------------------------------------------------------------
 // state representation (backbone.py:348): LayerNorm over C, eps 1e-5.  The
-// U rows of an iteration share each CTA-wide reduction (one barrier for all).
+// CTA is the row; the U rows of an iteration share each CTA-wide sum.
 template <int U>
-__device__ __forceinline__ void block_sum_rows(float (&v)[U][2], float (*red)[32][U][2], int& buf) {
-  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+__device__ __forceinline__ void row_sums(float (&v)[U][2], float2 (*red)[8][U], int& buf,
+                                         unsigned lanes) {
+  const int warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;  // nw <= 8 (C <= 2048)
+  const int lane = threadIdx.x & 31, n = __popc(lanes);  // a partial last warp has n < 32 lanes
+  // lane 0 of each warp collects its warp's sum (shuffles from lanes past n are not used)
 #pragma unroll
-  for (int u = 0; u < U; ++u) {
-    v[u][0] = warp_sum(v[u][0]);
-    v[u][1] = warp_sum(v[u][1]);
-  }
-  if ((threadIdx.x & 31) == 0)
+  for (int u = 0; u < U; ++u)
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      red[buf][warp][u][0] = v[u][0];
-      red[buf][warp][u][1] = v[u][1];
-    }
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float t = __shfl_down_sync(lanes, v[u][j], o);
+        if (lane + o < n) v[u][j] += t;
+      }
+  if (lane == 0)
+#pragma unroll
+    for (int u = 0; u < U; ++u) red[buf][warp][u] = make_float2(v[u][0], v[u][1]);
   __syncthreads();
-  // lane l takes warp l's partials (nw <= 32), then one more warp sum
-  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int u = 0; u < U; ++u) {
-    const float2 x = lane < nw ? *reinterpret_cast<const float2*>(&red[buf][lane][u][0])
-                               : make_float2(0.f, 0.f);
-    v[u][0] = warp_sum(x.x);
-    v[u][1] = warp_sum(x.y);
+    float2 t = red[buf][0][u];
+    for (int w = 1; w < nw; ++w) {
+      const float2 x = red[buf][w][u];
+      t.x += x.x;
+      t.y += x.y;
+    }
+    v[u][0] = t.x;
+    v[u][1] = t.y;
   }
   buf ^= 1;
 }
 
-__global__ void __launch_bounds__(1024) lnsa_fwd_kernel(const float* __restrict__ sa,
-                                                        const float* __restrict__ wt,
-                                                        const float* __restrict__ bs,
-                                                        float* __restrict__ out, Shape S) {
-  constexpr int U = 4;
-  __shared__ __align__(8) float red[2][32][U][2];
+__global__ void __launch_bounds__(256) lnsa_fwd_kernel(const float* __restrict__ sa,
+                                                       const float* __restrict__ wt,
+                                                       const float* __restrict__ bs,
+                                                       float* __restrict__ out, Shape S) {
+  constexpr int U = kRows;
+  __shared__ float2 red[2][8][U];
   int buf = 0;
-  const int c = 2 * threadIdx.x;
+  const int c = V * threadIdx.x;
   const int64_t C = S.C;
+  const unsigned lanes = warp_lanes();
   const float invC = 1.0f / static_cast<float>(C);
-  const float2 w = ld2(wt + c), bb = ld2(bs + c);
   for (int64_t item = blockIdx.x; item < S.items(); item += gridDim.x) {
     int64_t b, t0, t1;
     item_rows(S, item, b, t0, t1);
-    for (int64_t tb = t0; tb < t1; tb += U) {
-      const int nu = t1 - tb < U ? static_cast<int>(t1 - tb) : U;
-      const int64_t o0 = (b * S.T + tb) * C + c;
-      float2 x[U];
-      float s[U][2];
+    float x[U][V], s[U][2];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        x[u] = u < nu ? ld2(sa + o0 + u * C) : make_float2(0.f, 0.f);
-        s[u][0] = x[u].x + x[u].y;
-        s[u][1] = 0.f;
-      }
-      block_sum_rows<U>(s, red, buf);  // mean, then the variance about it (two passes)
-      float d[U][2];
+    for (int u = 0; u < U; ++u) {  // rows past the item repeat its last one
+      ld8(sa + (b * S.T + (t0 + u < t1 ? t0 + u : t1 - 1)) * C + c, x[u]);
+      s[u][0] = sum8(x[u]);
+      s[u][1] = 0.f;
+    }
+    row_sums<U>(s, red, buf, lanes);  // mean
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const float mean = s[u][0] * invC;
-        d[u][0] = x[u].x - mean;
-        d[u][1] = x[u].y - mean;
-        s[u][0] = d[u][0] * d[u][0] + d[u][1] * d[u][1];
-        s[u][1] = 0.f;
-      }
-      block_sum_rows<U>(s, red, buf);
+    for (int u = 0; u < U; ++u) {
+      const float mean = s[u][0] * invC;
+      float q = 0.f;
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        if (u < nu) {
-          const float rstd = rsqrtf(s[u][0] * invC + 1e-5f);
-          st2(out + o0 + u * C, d[u][0] * rstd * w.x + bb.x, d[u][1] * rstd * w.y + bb.y);
-        }
+      for (int e = 0; e < V; ++e) {
+        x[u][e] -= mean;
+        q += x[u][e] * x[u][e];
       }
+      s[u][0] = q;
+    }
+    row_sums<U>(s, red, buf, lanes);  // variance about the mean (two passes)
+    float w[V], bb[V];
+    ld8(wt + c, w);
+    ld8(bs + c, bb);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (t0 + u >= t1) continue;
+      const float rstd = rsqrtf(s[u][0] * invC + 1e-5f);
+      float y[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) y[e] = x[u][e] * rstd * w[e] + bb[e];
+      st8(out + (b * S.T + t0 + u) * C + c, y);
     }
   }
 }
 
-__global__ void __launch_bounds__(1024) lnsa_bwd_kernel(const float* __restrict__ dout,
-                                                        const float* __restrict__ sa,
-                                                        const float* __restrict__ wt,
-                                                        float* __restrict__ dsa,
-                                                        float* __restrict__ part, Shape S) {
-  constexpr int U = 4;
-  __shared__ __align__(8) float red[2][32][U][2];
+__global__ void __launch_bounds__(256) lnsa_bwd_kernel(const float* __restrict__ dout,
+                                                       const float* __restrict__ sa,
+                                                       const float* __restrict__ wt,
+                                                       float* __restrict__ dsa,
+                                                       float* __restrict__ part, Shape S) {
+  constexpr int U = 2;
+  __shared__ float2 red[2][8][U];
   int buf = 0;
-  const int c = 2 * threadIdx.x;
+  const int c = V * threadIdx.x;
   const int64_t C = S.C;
+  const unsigned lanes = warp_lanes();
   const float invC = 1.0f / static_cast<float>(C);
-  const float2 w = ld2(wt + c);
-  float acc[2][2] = {};  // weight, bias
+  float w[V], acc[2][V];  // weight, bias
+  ld8(wt + c, w);
+#pragma unroll
+  for (int e = 0; e < V; ++e) acc[0][e] = acc[1][e] = 0.f;
   for (int64_t item = blockIdx.x; item < S.items(); item += gridDim.x) {
     int64_t b, t0, t1;
     item_rows(S, item, b, t0, t1);
     for (int64_t tb = t0; tb < t1; tb += U) {
-      const int nu = t1 - tb < U ? static_cast<int>(t1 - tb) : U;
-      const int64_t o0 = (b * S.T + tb) * C + c;
-      float2 x[U], g[U];
-      float s[U][2];
+      float x[U][V], g[U][V], s[U][2];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        x[u] = u < nu ? ld2(sa + o0 + u * C) : make_float2(0.f, 0.f);
-        g[u] = u < nu ? ld2(dout + o0 + u * C) : make_float2(0.f, 0.f);
-        s[u][0] = x[u].x + x[u].y;
+      for (int u = 0; u < U; ++u) {  // rows past the item repeat its last one, with g = 0
+        const int64_t o = (b * S.T + (tb + u < t1 ? tb + u : t1 - 1)) * C + c;
+        ld8(sa + o, x[u]);
+        ld8(dout + o, g[u]);
+        if (tb + u >= t1)
+#pragma unroll
+          for (int e = 0; e < V; ++e) g[u][e] = 0.f;
+        s[u][0] = sum8(x[u]);
         s[u][1] = 0.f;
       }
-      block_sum_rows<U>(s, red, buf);  // mean
-      float d[U][2];
+      row_sums<U>(s, red, buf, lanes);  // mean
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const float mean = s[u][0] * invC;
-        d[u][0] = x[u].x - mean;
-        d[u][1] = x[u].y - mean;
-        s[u][0] = d[u][0] * d[u][0] + d[u][1] * d[u][1];
-        s[u][1] = 0.f;
+        float q = 0.f;
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          x[u][e] -= mean;
+          q += x[u][e] * x[u][e];
+        }
+        s[u][0] = q;
       }
-      block_sum_rows<U>(s, red, buf);  // variance
-      float xn[U][2], dn[U][2], rstd[U];
+      row_sums<U>(s, red, buf, lanes);  // variance
+      float rstd[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         rstd[u] = rsqrtf(s[u][0] * invC + 1e-5f);
-        xn[u][0] = d[u][0] * rstd[u];
-        xn[u][1] = d[u][1] * rstd[u];
-        dn[u][0] = g[u].x * w.x;
-        dn[u][1] = g[u].y * w.y;
-        acc[0][0] += g[u].x * xn[u][0];   // rows past nu have g = 0
-        acc[0][1] += g[u].y * xn[u][1];
-        acc[1][0] += g[u].x;
-        acc[1][1] += g[u].y;
-        s[u][0] = dn[u][0] + dn[u][1];
-        s[u][1] = dn[u][0] * xn[u][0] + dn[u][1] * xn[u][1];
+        float m1 = 0.f, m2 = 0.f;
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          x[u][e] *= rstd[u];                  // xn
+          acc[0][e] += g[u][e] * x[u][e];
+          acc[1][e] += g[u][e];
+          g[u][e] *= w[e];                     // d xn
+          m1 += g[u][e];
+          m2 += g[u][e] * x[u][e];
+        }
+        s[u][0] = m1;
+        s[u][1] = m2;
       }
-      block_sum_rows<U>(s, red, buf);
+      row_sums<U>(s, red, buf, lanes);
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        if (u < nu) {
-          const float m1 = s[u][0] * invC, m2 = s[u][1] * invC;
-          st2(dsa + o0 + u * C, rstd[u] * (dn[u][0] - m1 - xn[u][0] * m2),
-              rstd[u] * (dn[u][1] - m1 - xn[u][1] * m2));
-        }
+        if (tb + u >= t1) continue;
+        const float m1 = s[u][0] * invC, m2 = s[u][1] * invC;
+        float d[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) d[e] = rstd[u] * (g[u][e] - m1 - x[u][e] * m2);
+        st8(dsa + (b * S.T + tb + u) * C + c, d);
       }
     }
   }
   float* pp = part + static_cast<int64_t>(blockIdx.x) * 2 * C;
-  st2(pp + c, acc[0][0], acc[0][1]);
-  st2(pp + C + c, acc[1][0], acc[1][1]);
+  st8(pp + c, acc[0]);
+  st8(pp + C + c, acc[1]);
 }
 
 // out[i] = sum over g < G of part[g * n + i].  Block (32, 8): 32 consecutive
@@ -612,13 +726,18 @@ int check_shape(int64_t B, int64_t T, int64_t C) {
   return 0;
 }
 
-// CTAs to launch: as many as fit on the device at once (CTAs of C/2 threads),
+// CTAs to launch: as many as fit on the device at once (CTAs of `threads`,
+// C/8 by default),
 // at most one per work item and kMaxGrid
 template <typename K>
-int grid_for(K kernel, const Shape& S) {
+int grid_for(K kernel, const Shape& S, size_t smem = 0, int threads = 0) {
+  if (threads == 0) threads = static_cast<int>(S.C / V);
+  // launches above the default 48 KiB of dynamic shared memory need the opt-in
+  if (smem > (48u << 10))
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   int dev = 0, sms = 148, per_sm = 1;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, static_cast<int>(S.C / 2), 0) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) !=
           cudaSuccess || per_sm < 1)
     per_sm = 1;
   int64_t g = static_cast<int64_t>(sms) * per_sm;
@@ -708,9 +827,9 @@ int camoe_tm_mix_fwd(const void* x, int x_dtype, const float* mix, void* const* 
                              : camoe::tm::grid_for(camoe::tm::mix_fwd_kernel<float>, S);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (x_dtype == 0)
-    camoe::tm::mix_fwd_kernel<bf16><<<G, static_cast<unsigned>(C / 2), 0, s>>>(static_cast<const bf16*>(x), mix, o, S);
+    camoe::tm::mix_fwd_kernel<bf16><<<G, static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(static_cast<const bf16*>(x), mix, o, S);
   else
-    camoe::tm::mix_fwd_kernel<float><<<G, static_cast<unsigned>(C / 2), 0, s>>>(static_cast<const float*>(x), mix, o, S);
+    camoe::tm::mix_fwd_kernel<float><<<G, static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(static_cast<const float*>(x), mix, o, S);
   return camoe::tm::status(cudaGetLastError());
 }
 
@@ -729,15 +848,16 @@ int camoe_tm_mix_bwd(const void* x, int x_dtype, const float* mix, const void* c
   if ((st = check_work(S, work, work_bytes)) != 0) return st;
   camoe::tm::In6 d;
   for (int m = 0; m < 6; ++m) d.p[m] = static_cast<const bf16*>(dout[m]);
-  const int G = x_dtype == 0 ? camoe::tm::grid_for(camoe::tm::mix_bwd_kernel<bf16>, S)
-                             : camoe::tm::grid_for(camoe::tm::mix_bwd_kernel<float>, S);
+  const int threads = static_cast<int>(C / 2);  // two columns per thread
+  const int G = x_dtype == 0 ? camoe::tm::grid_for(camoe::tm::mix_bwd_kernel<bf16>, S, 0, threads)
+                             : camoe::tm::grid_for(camoe::tm::mix_bwd_kernel<float>, S, 0, threads);
   float* part = static_cast<float*>(work);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (x_dtype == 0)
-    camoe::tm::mix_bwd_kernel<bf16><<<G, static_cast<unsigned>(C / 2), 0, s>>>(
+    camoe::tm::mix_bwd_kernel<bf16><<<G, threads, 0, s>>>(
         static_cast<const bf16*>(x), mix, d, static_cast<bf16*>(dx), part, S);
   else
-    camoe::tm::mix_bwd_kernel<float><<<G, static_cast<unsigned>(C / 2), 0, s>>>(
+    camoe::tm::mix_bwd_kernel<float><<<G, threads, 0, s>>>(
         static_cast<const float*>(x), mix, d, static_cast<float*>(dx), part, S);
   if ((st = camoe::tm::status(cudaGetLastError())) != 0) return st;
   return camoe::tm::reduce(part, G, 6 * C, dmix, s);
@@ -758,7 +878,9 @@ int camoe_tm_prep_fwd(const void* wl, const void* k, const void* v, const void* 
   p.par = params;
   p.w = static_cast<bf16*>(w_op); p.ko = static_cast<bf16*>(k_op); p.vo = static_cast<bf16*>(v_op);
   p.a = static_cast<bf16*>(a_op); p.b = static_cast<bf16*>(b_op);
-  camoe::tm::prep_fwd_kernel<<<camoe::tm::grid_for(camoe::tm::prep_fwd_kernel, S), static_cast<unsigned>(C / 2), 0,
+  const int threads = static_cast<int>(C / 2);  // two columns per thread
+  camoe::tm::prep_fwd_kernel<<<camoe::tm::grid_for(camoe::tm::prep_fwd_kernel, S, 0, threads),
+                               threads, 0,
                                static_cast<cudaStream_t>(stream)>>>(p, S);
   return camoe::tm::status(cudaGetLastError());
 }
@@ -799,10 +921,11 @@ int camoe_tm_prep_bwd(const void* dr_op, const void* dr_epi, const void* dw_op,
   p.dr = static_cast<bf16*>(dr); p.dwl = static_cast<bf16*>(dwl); p.dk = static_cast<bf16*>(dk);
   p.dv = static_cast<bf16*>(dv); p.dvl = static_cast<bf16*>(dvl); p.dal = static_cast<bf16*>(dal);
   p.dvf = static_cast<bf16*>(dv_first);
-  const int G = camoe::tm::grid_for(camoe::tm::prep_bwd_kernel, S);
+  const int threads = static_cast<int>(C / 2);  // two columns per thread
+  const int G = camoe::tm::grid_for(camoe::tm::prep_bwd_kernel, S, 0, threads);
   float* part = static_cast<float*>(work);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  camoe::tm::prep_bwd_kernel<<<G, static_cast<unsigned>(C / 2), 0, s>>>(p, part, S);
+  camoe::tm::prep_bwd_kernel<<<G, threads, 0, s>>>(p, part, S);
   if ((st = camoe::tm::status(cudaGetLastError())) != 0) return st;
   return camoe::tm::reduce(part, G, 5 * C, dparams, s);
 }
@@ -816,7 +939,7 @@ int camoe_tm_post_fwd(const void* y, const void* r, const void* k_op, const void
   camoe::tm::Post p{static_cast<const bf16*>(y), static_cast<const bf16*>(r),
                     static_cast<const bf16*>(k_op), static_cast<const bf16*>(v_op),
                     static_cast<const bf16*>(g), r_k, gamma, beta};
-  camoe::tm::post_fwd_kernel<<<camoe::tm::grid_for(camoe::tm::post_fwd_kernel, S), static_cast<unsigned>(C / 2), 0,
+  camoe::tm::post_fwd_kernel<<<camoe::tm::grid_for(camoe::tm::post_fwd_kernel, S), static_cast<unsigned>(C / camoe::tm::V), 0,
                                static_cast<cudaStream_t>(stream)>>>(p, static_cast<bf16*>(z), S);
   return camoe::tm::status(cudaGetLastError());
 }
@@ -844,7 +967,7 @@ int camoe_tm_post_bwd(const void* dz, const void* y, const void* r, const void* 
   const int G = camoe::tm::grid_for(camoe::tm::post_bwd_kernel, S);
   float* part = static_cast<float*>(work);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  camoe::tm::post_bwd_kernel<<<G, static_cast<unsigned>(C / 2), 0, s>>>(p, q, part, S);
+  camoe::tm::post_bwd_kernel<<<G, static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(p, q, part, S);
   if ((st = camoe::tm::status(cudaGetLastError())) != 0) return st;
   return camoe::tm::reduce(part, G, 3 * C, dparams, s);
 }
@@ -854,7 +977,7 @@ int camoe_tm_lnsa_fwd(const float* sa, const float* weight, const float* bias, f
   int st = precheck(B, T, C, {sa, weight, bias, out}, {});
   if (st != 0) return st < 0 ? 0 : st;
   const Shape S = make_shape(B, T, C);
-  camoe::tm::lnsa_fwd_kernel<<<camoe::tm::grid_for(camoe::tm::lnsa_fwd_kernel, S), static_cast<unsigned>(C / 2), 0,
+  camoe::tm::lnsa_fwd_kernel<<<camoe::tm::grid_for(camoe::tm::lnsa_fwd_kernel, S), static_cast<unsigned>(C / camoe::tm::V), 0,
                                static_cast<cudaStream_t>(stream)>>>(sa, weight, bias, out, S);
   return camoe::tm::status(cudaGetLastError());
 }
@@ -873,7 +996,7 @@ int camoe_tm_lnsa_bwd(const float* dout, const float* sa, const float* weight, f
   const int G = camoe::tm::grid_for(camoe::tm::lnsa_bwd_kernel, S);
   float* part = static_cast<float*>(work);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  camoe::tm::lnsa_bwd_kernel<<<G, static_cast<unsigned>(C / 2), 0, s>>>(dout, sa, weight, dsa, part, S);
+  camoe::tm::lnsa_bwd_kernel<<<G, static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(dout, sa, weight, dsa, part, S);
   if ((st = camoe::tm::status(cudaGetLastError())) != 0) return st;
   return camoe::tm::reduce(part, G, 2 * C, dparams, s);
 }
