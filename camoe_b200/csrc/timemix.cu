@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(256) lnsa_bwd_kernel(const float* __restrict__
                                                        const float* __restrict__ wt,
                                                        float* __restrict__ dsa,
                                                        float* __restrict__ part, Shape S) {
-  constexpr int U = 2;
+  constexpr int U = 4;
   __shared__ float2 red[2][8][U];
   int buf = 0;
   const int c = V * threadIdx.x;
