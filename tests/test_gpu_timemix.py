@@ -62,7 +62,8 @@ def close(got, want, tol, name):
     assert e < tol, f"{name}: {e:.3g} >= {tol}"
 
 
-SHAPES = [(2, 40, 128), (1, 17, 1024), (3, 16, 2048), (1, 5, 64)]
+# C = 320: 40 threads of 8 columns (a full warp and a partial one), 160 of 2
+SHAPES = [(2, 40, 128), (1, 17, 1024), (3, 16, 2048), (1, 5, 64), (2, 9, 320)]
 
 
 @pytest.mark.parametrize("xdt", [BF, torch.float32], ids=["bf16", "fp32"])
