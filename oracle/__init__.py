@@ -1,8 +1,8 @@
 """CPU oracle for the WKV-7 ClampW recurrence — TEST INFRASTRUCTURE ONLY.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
-``bench.py`` may import this package, and only as the checker (or as the timed
-CPU baseline).  The ``camoe_b200`` product path never imports it.
+``bench.py`` may import this package, and only as the result to compare against
+(or as the timed CPU baseline).  The ``camoe_b200`` product path never imports it.
 
 Contents:
 

@@ -1,7 +1,7 @@
 /*
  * CPU oracle for the WKV-7 ClampW recurrence.  TEST INFRASTRUCTURE ONLY:
- * tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use it as
- * the checker; nothing in the camoe_b200 product path links or calls it.
+ * tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg compare
+ * against it; nothing in the camoe_b200 product path links or calls it.
  *
  * Restated from the reference:
  *   decay        w = exp(W_SCALE * sigmoid(w_in)), W_SCALE = -exp(-1/2)
