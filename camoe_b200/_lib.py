@@ -24,7 +24,8 @@ EXPORTS = ("camoe_wkv7_version", "camoe_wkv7_strerror", "camoe_wkv7_last_cuda_er
 
 
 # include/camoe_timemix.h: fused elementwise kernels of the time mix
-TM_EXPORTS = ("camoe_tm_work_bytes", "camoe_tm_mix_fwd", "camoe_tm_mix_bwd", "camoe_tm_prep_fwd",
+TM_EXPORTS = ("camoe_tm_work_bytes", "camoe_tm_mix_fwd", "camoe_tm_mix_fwd_prev",
+              "camoe_tm_mix_bwd", "camoe_tm_prep_fwd",
               "camoe_tm_prep_bwd", "camoe_tm_post_fwd", "camoe_tm_post_bwd", "camoe_tm_lnsa_fwd",
               "camoe_tm_lnsa_bwd")
 
@@ -72,6 +73,7 @@ def lib() -> ctypes.CDLL:
     l.camoe_tm_work_bytes.restype = sz
     l.camoe_tm_work_bytes.argtypes = [i64] * 3
     l.camoe_tm_mix_fwd.argtypes = [vp, ci, vp, vp] + [i64] * 3 + [vp]
+    l.camoe_tm_mix_fwd_prev.argtypes = [vp, ci, vp, vp, vp] + [i64] * 3 + [vp]
     l.camoe_tm_mix_bwd.argtypes = [vp, ci, vp, vp, vp, vp, vp, sz] + [i64] * 3 + [vp]
     l.camoe_tm_prep_fwd.argtypes = [vp] * 12 + [i64] * 3 + [vp]
     l.camoe_tm_prep_bwd.argtypes = [vp] * 26 + [sz] + [i64] * 3 + [vp]

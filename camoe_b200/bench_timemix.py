@@ -11,6 +11,9 @@ Prints JSON lines:
   ``eager_forward``, the unfused baseline) under bf16 autocast, with this
   package's WKV-7 op behind ``RUN_CUDA_RWKV7`` in both, so the difference is
   the fusion of everything around the op.
+* ``decode``: one generated token through one layer with the state carried
+  (``RWKV7TimeMix.forward_state``), against re-running the layer over the
+  whole context as the reference's generation loop does (B=64 sequences).
 * ``kernel``: each fused kernel alone, CUDA-event time per launch (L2 flushed
   before each) against its algorithmic bytes (each input read once, each
   output written once) and the measured HBM bandwidth.
@@ -139,6 +142,36 @@ def bench_layer(B, T, C, layer, steps):
             "speedup": round(eager / fused, 2), "speedup_graph": round(eager_g / fused_g, 2)}
 
 
+def bench_decode(B, ctx, C, layer, steps):
+    """Per generated token, one time-mix layer: forward_state on one step with
+    the carried state (eager, and replayed from a CUDA graph), against what the
+    reference's generation loop does per token, a forward over the whole
+    context (eval.py:212)."""
+    torch.manual_seed(0)
+    m = timemix.RWKV7TimeMix(C, 12, layer).cuda()
+    x = torch.randn(B, ctx, C, device="cuda", dtype=BF)
+    vf = None if layer == 0 else torch.randn(B, ctx, C, device="cuda", dtype=BF)
+    with torch.no_grad():
+        _, _, _, state = m.forward_state(x, vf)
+    x1 = x[:, -1:].contiguous()
+    v1 = None if vf is None else vf[:, -1:].contiguous()
+    holder = {"s": state}
+
+    def token():
+        o, _, _, holder["s"] = m.forward_state(x1, v1, holder["s"])
+
+    step_ms = time_ms(token, steps)
+    step_graph_ms = time_graph_ms(token, steps)
+    with torch.no_grad():
+        full_ms = time_ms(lambda: m(x, vf), max(3, steps // 10))
+    return {"workload": f"time mix layer {layer} decode: B={B} context {ctx} C={C}, bf16, "
+                        "one generated token",
+            "metric": "decode_ms_per_token",
+            "stateful": {"ms": round(step_ms, 4), "graph_ms": round(step_graph_ms, 4)},
+            "rerun_context": {"ms": round(full_ms, 3)},
+            "speedup_graph": round(full_ms / step_graph_ms, 1)}
+
+
 def bench_kernels(B, T, C, steps):
     L = _lib.lib()
     n = B * T * C
@@ -205,6 +238,7 @@ def main():
     args = ap.parse_args()
     if not args.no_layer:
         print(json.dumps(bench_layer(args.batch, args.seq, args.embd, args.layer, args.steps)))
+        print(json.dumps(bench_decode(64, args.seq, args.embd, args.layer, 5 * args.steps)))
     for line in bench_kernels(args.batch, args.seq, args.embd, args.steps):
         print(json.dumps(line))
 

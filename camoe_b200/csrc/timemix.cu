@@ -126,8 +126,11 @@ struct In6 {
   const bf16* p[6];
 };
 
+// x_prev (nullable): [B, C], the step before step 0 of each sequence (the
+// token-shift state of a stateful call); zero when null, as in the reference
 template <typename Tx>
 __global__ void __launch_bounds__(256) mix_fwd_kernel(const Tx* __restrict__ x,
+                                                      const Tx* __restrict__ x_prev,
                                                       const float* __restrict__ mix, Out6 out,
                                                       Shape S) {
   const int c = V * threadIdx.x;
@@ -141,6 +144,8 @@ __global__ void __launch_bounds__(256) mix_fwd_kernel(const Tx* __restrict__ x,
     float xp[V];
     if (t0 > 0) {
       ld8(x + (b * S.T + t0 - 1) * C + c, xp);
+    } else if (x_prev != nullptr) {
+      ld8(x_prev + b * C + c, xp);
     } else {
 #pragma unroll
       for (int e = 0; e < V; ++e) xp[e] = 0.f;
@@ -816,8 +821,13 @@ size_t camoe_tm_work_bytes(int64_t B, int64_t T, int64_t C) {
 
 int camoe_tm_mix_fwd(const void* x, int x_dtype, const float* mix, void* const* out, int64_t B,
                      int64_t T, int64_t C, void* stream) {
+  return camoe_tm_mix_fwd_prev(x, x_dtype, nullptr, mix, out, B, T, C, stream);
+}
+
+int camoe_tm_mix_fwd_prev(const void* x, int x_dtype, const void* x_prev, const float* mix,
+                          void* const* out, int64_t B, int64_t T, int64_t C, void* stream) {
   if (out == nullptr) return 1;
-  int st = precheck(B, T, C, {x, mix, out[0], out[1], out[2], out[3], out[4], out[5]}, {});
+  int st = precheck(B, T, C, {x, mix, out[0], out[1], out[2], out[3], out[4], out[5]}, {x_prev});
   if (st != 0) return st < 0 ? 0 : st;
   if (x_dtype != 0 && x_dtype != 1) return 2;
   const Shape S = make_shape(B, T, C);
@@ -827,9 +837,11 @@ int camoe_tm_mix_fwd(const void* x, int x_dtype, const float* mix, void* const* 
                              : camoe::tm::grid_for(camoe::tm::mix_fwd_kernel<float>, S);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (x_dtype == 0)
-    camoe::tm::mix_fwd_kernel<bf16><<<G, static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(static_cast<const bf16*>(x), mix, o, S);
+    camoe::tm::mix_fwd_kernel<bf16><<<G, static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(
+        static_cast<const bf16*>(x), static_cast<const bf16*>(x_prev), mix, o, S);
   else
-    camoe::tm::mix_fwd_kernel<float><<<G, static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(static_cast<const float*>(x), mix, o, S);
+    camoe::tm::mix_fwd_kernel<float><<<G, static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(
+        static_cast<const float*>(x), static_cast<const float*>(x_prev), mix, o, S);
   return camoe::tm::status(cudaGetLastError());
 }
 

@@ -262,3 +262,72 @@ class RWKV7TimeMix(nn.Module):
         if self.layer_id == 0:
             v_first = v
         return out, v_first, srep
+
+    @torch.no_grad()
+    def forward_state(self, x: torch.Tensor, v_first: torch.Tensor | None = None, state=None):
+        """Inference over steps [t0, t0 + T) of each sequence, carrying the
+        layer's state across calls, so that generating a token costs one step
+        instead of a pass over the whole context (the reference re-runs the
+        prefix for every token, eval.py:212).  ``state`` is None at t0 = 0 or
+        the (x_prev, wkv) returned by the previous call: x_prev [B, C] the last
+        step of x (the token shift's input), wkv [B, H, 64, 64] fp32 the WKV
+        state.  Returns (out, v_first, state_representation, new_state); the
+        outputs equal ``forward`` over the concatenated steps.  ``v_first``
+        (layers > 0) covers the same steps as x."""
+        B, T, C = x.shape
+        H = C // HEAD_SIZE
+        dev = x.device
+        L = _lib.lib()
+        st = _stream(x)
+        x = x.contiguous()
+        code = {_BF: 0, torch.float32: 1}.get(x.dtype)
+        if code is None:
+            raise TypeError(f"time-mix input must be bfloat16 or float32, got {x.dtype}")
+        x_prev, wkv = (None, None) if state is None else state
+        if x_prev is not None:
+            x_prev = x_prev.to(x.dtype).contiguous()
+            if tuple(x_prev.shape) != (B, C):
+                raise ValueError(f"state x_prev must be [B, C] = [{B}, {C}]")
+        mix = torch.cat([getattr(self, n).view(1, C) for n in
+                         ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g")]).float().contiguous()
+        xs = [torch.empty(B, T, C, dtype=_BF, device=dev) for _ in range(6)]
+        ptrs = (ctypes.c_void_p * 6)(*[t.data_ptr() for t in xs])
+        check(L.camoe_tm_mix_fwd_prev(_p(x), code, _p(x_prev), _p(mix), ptrs, B, T, C, st))
+        xr, xw, xk, xv, xa, xg = xs
+        W = (lambda m: m.weight.to(_BF))
+        P = (lambda t: t.to(_BF))
+        r = F.linear(xr, W(self.receptance)).contiguous()
+        k = F.linear(xk, W(self.key)).contiguous()
+        v = F.linear(xv, W(self.value)).contiguous()
+        wl = (torch.tanh(xw @ P(self.w1)) @ P(self.w2)).contiguous()
+        al = ((xa @ P(self.a1)) @ P(self.a2)).contiguous()
+        g = (torch.sigmoid(xg @ P(self.g1)) @ P(self.g2)).contiguous()
+        if self.layer_id == 0:
+            vl = vf = None
+        else:
+            if v_first is None:
+                raise ValueError("layers after the first need v_first")
+            vl = ((xv @ P(self.v1)) @ P(self.v2)).contiguous()
+            vf = v_first.to(_BF).contiguous()
+        prep_par = torch.cat([t.view(1, C) for t in (self.w0, self.v0, self.a0, self.k_k,
+                                                      self.k_a)]).float().contiguous()
+        op_in = [torch.empty(B, T, C, dtype=_BF, device=dev) for _ in range(5)]
+        check(L.camoe_tm_prep_fwd(_p(wl), _p(k), _p(v), _p(vl), _p(al), _p(vf), _p(prep_par),
+                                  *[_p(t) for t in op_in], B, T, C, st))
+        w_op, k_op, v_op, a_op, b_op = op_in
+        as4 = (lambda t: t.view(B, T, H, HEAD_SIZE))
+        y, sa, wkv_new = ops.wkv7_forward_state(as4(r), as4(w_op), as4(k_op), as4(v_op),
+                                                as4(a_op), as4(b_op), wkv, algo=self.algo)
+        y, sa = y.view(B, T, C), sa.view(B, T, C)
+        # fp32 parameter copies held here until the launches are queued
+        ln_w, ln_b, r_k, gx, bx = (t.float().contiguous() for t in (
+            self.ln_sa.weight, self.ln_sa.bias, self.r_k, self.ln_x.weight, self.ln_x.bias))
+        srep = torch.empty(B, T, C, dtype=torch.float32, device=dev)
+        check(L.camoe_tm_lnsa_fwd(_p(sa), _p(ln_w), _p(ln_b), _p(srep), B, T, C, st))
+        z = torch.empty(B, T, C, dtype=_BF, device=dev)
+        check(L.camoe_tm_post_fwd(_p(y), _p(r), _p(k_op), _p(v_op), _p(g), _p(r_k), _p(gx),
+                                  _p(bx), _p(z), B, T, C, st))
+        out = F.linear(z, W(self.output))
+        if self.layer_id == 0:
+            v_first = v
+        return out, v_first, srep, (x[:, -1].contiguous(), wkv_new)

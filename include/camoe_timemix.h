@@ -43,6 +43,12 @@ size_t camoe_tm_work_bytes(int64_t B, int64_t T, int64_t C);
 int camoe_tm_mix_fwd(const void* x, int x_dtype, const float* mix, void* const* out, int64_t B,
                      int64_t T, int64_t C, void* stream);
 
+/* camoe_tm_mix_fwd with the step before step 0 of each sequence given:
+ * x_prev is [B, C] of x_dtype (the last step of the previous call, for a
+ * time mix carried across calls); NULL means zero, as camoe_tm_mix_fwd. */
+int camoe_tm_mix_fwd_prev(const void* x, int x_dtype, const void* x_prev, const float* mix,
+                          void* const* out, int64_t B, int64_t T, int64_t C, void* stream);
+
 /* Backward of camoe_tm_mix_fwd: dout[m] (bf16) -> dx (x_dtype), dmix [6][C]. */
 int camoe_tm_mix_bwd(const void* x, int x_dtype, const float* mix, const void* const* dout,
                      void* dx, float* dmix, void* work, size_t work_bytes, int64_t B, int64_t T,

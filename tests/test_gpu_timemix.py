@@ -362,3 +362,33 @@ def test_layer_replays_from_a_cuda_graph():
     torch.cuda.synchronize()
     close(res["out"], out0, 1e-3, "graph out")
     close(x.grad, gx0, 1e-3, "graph dx")
+
+
+@pytest.mark.parametrize("layer_id", [0, 2])
+def test_forward_state_prefill_then_decode_equals_one_pass(layer_id):
+    """RWKV7TimeMix.forward_state: a 32-step prefill, then 16 single-token calls
+    carrying (x_prev, wkv), give forward()'s outputs over all 48 steps."""
+    B, T0, n, C = 2, 32, 16, 256
+    torch.manual_seed(11)
+    m = timemix.RWKV7TimeMix(C, 4, layer_id).cuda()
+    with torch.no_grad():  # non-zero LoRA inputs and output projection
+        for name in ("w1", "a1", "v1", "g1"):
+            getattr(m, name).normal_(0, 0.1)
+        m.output.weight.normal_(0, C ** -0.5)
+    x = torch.randn(B, T0 + n, C, device="cuda", dtype=BF)
+    vf = None if layer_id == 0 else torch.randn(B, T0 + n, C, device="cuda", dtype=BF)
+    with torch.no_grad():
+        out, vf_out, srep = m(x, vf)
+    o1, v1, s1, state = m.forward_state(x[:, :T0], None if vf is None else vf[:, :T0])
+    outs, srs, vfs = [o1], [s1], [v1]
+    for t in range(T0, T0 + n):
+        o, v_, s_, state = m.forward_state(x[:, t:t + 1], None if vf is None else vf[:, t:t + 1],
+                                           state)
+        outs.append(o)
+        srs.append(s_)
+        vfs.append(v_)
+    torch.cuda.synchronize()
+    close(torch.cat(outs, 1), out, 2e-2, "out")
+    close(torch.cat(srs, 1), srep, 2e-2, "state_representation")
+    close(torch.cat(vfs, 1), vf_out, 2e-2, "v_first")
+    assert state[0].shape == (B, C) and state[1].shape == (B, C // 64, 64, 64)
