@@ -71,6 +71,9 @@ def test_timemix_abi_rejects_bad_arguments_without_a_device():
     assert L.camoe_tm_mix_fwd(None, 0, p, outs, 2, 40, 128, None) == _lib.ERR_INVALID_ARG
     assert L.camoe_tm_mix_fwd(ctypes.c_void_p(24), 0, p, outs, 2, 40, 128, None) == _lib.ERR_ALIGNMENT
     assert L.camoe_tm_mix_fwd(p, 0, p, outs, 0, 40, 128, None) == _lib.OK   # empty: no launch
+    # the carried token-shift row is optional but must be aligned when given
+    assert L.camoe_tm_mix_fwd_prev(p, 0, ctypes.c_void_p(40), p, outs, 2, 40, 128, None) == _lib.ERR_ALIGNMENT
+    assert L.camoe_tm_mix_fwd_prev(p, 0, None, p, outs, 0, 40, 128, None) == _lib.OK
     assert L.camoe_tm_lnsa_fwd(p, p, p, p, -1, 4, 128, None) == _lib.ERR_INVALID_ARG
     # prep: value-residual inputs come as a pair
     assert L.camoe_tm_prep_fwd(p, p, p, p, p, None, p, p, p, p, p, p, 2, 40, 128, None) == _lib.ERR_INVALID_ARG
