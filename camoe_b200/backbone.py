@@ -18,6 +18,9 @@ Same module-level names and call contract:
   two-output Function);
 * ``RUN_CUDA_RWKV7(r, w, k, v, a, b)`` on ``[B, T, C]`` tensors returning
   ``(y, sa)`` in the caller's dtype (camoe/backbone.py:104-121);
+* ``RWKV7_ClampW_State`` — the same op over a piece of a longer sequence:
+  start state in, final state out, gradients through both (no counterpart in
+  the reference, whose op always starts from zero);
 * the reference's second op, ``torch.ops.wind_backstepping.forward/backward``
   (camoe/cuda/wkv7_op.cpp:18-21, decay exp(-exp(w))), registered by
   ``init_rwkv7_cuda`` too, and ``WindBackstepping``, its autograd Function.
@@ -103,6 +106,44 @@ class WindBackstepping(torch.autograd.Function):
         dq, dw, dk, dv, dz, da = ops.wkv7_backward(q, w, k, v, z, a, dy, dsa, ckpt, algo=_ALGO,
                                                    decay="wind")
         return dw, dq, dk, dv, dz, da
+
+
+class RWKV7_ClampW_State(torch.autograd.Function):
+    """y, sa, sT = RWKV7_ClampW_State.apply(r, w, k, v, a, b, s0): the ClampW op
+    over one piece of a longer sequence, starting from the state ``s0``
+    ([B, H, 64, 64] fp32, element [b, h, i, j] = S[i][j], i the value index)
+    and returning its final state ``sT``, differentiable in all seven inputs.
+    Carrying ``sT`` into the next piece (detached or not) trains over
+    sequences longer than one call (truncated BPTT).  T must be a multiple of
+    16.  The reference has no carried state: its op always starts from zero
+    (camoe/cuda/rwkv7_clampw.cu:28)."""
+
+    @staticmethod
+    def forward(ctx, r, w, k, v, a, b, s0):
+        B, T, H, C = r.shape
+        assert T % CHUNK_LEN == 0
+        assert all(i.is_contiguous() for i in [r, w, k, v, a, b, s0]), \
+            "RWKV7 kernel needs contiguous tensors"
+        sT = torch.empty_like(s0)
+        needs_ckpt = any(ctx.needs_input_grad)
+        y, sa, ckpt = ops.wkv7_forward(r, w, k, v, a, b, algo=_ALGO, save_ckpt=needs_ckpt,
+                                       s0=s0, s_out=sT)
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(r, w, k, v, a, b, s0, ckpt)
+        return y, sa, sT
+
+    @staticmethod
+    def backward(ctx, dy, dsa, dsT):
+        r, w, k, v, a, b, s0, ckpt = ctx.saved_tensors
+        dy = torch.zeros_like(r) if dy is None else dy.to(r.dtype).contiguous()
+        if dsa is not None:
+            dsa = dsa.to(torch.float32).contiguous()
+        if dsT is not None:
+            dsT = dsT.to(torch.float32).contiguous()
+        ds0 = torch.empty_like(s0)
+        grads = ops.wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, algo=_ALGO, s0=s0,
+                                  ds_out=dsT, ds0=ds0)
+        return tuple(grads) + (ds0,)
 
 
 def _run_cuda(r, w, k, v, a, b):

@@ -1,6 +1,8 @@
 // C ABI of the WKV-7 ClampW operator (declared in include/camoe_wkv7.h):
 // argument validation, algorithm selection and kernel dispatch.  Nothing here
 // allocates or synchronises; every launch goes to the caller's stream.
+#include <initializer_list>
+
 #include "camoe_wkv7.h"
 #include "wkv7_common.cuh"
 
@@ -117,10 +119,24 @@ size_t camoe_wkv7_work_bytes(int64_t B, int64_t T, int64_t h_count, int N, int d
 
 namespace {
 
+// the [B, H_total, N, N] state arrays of a call, when given, must be aligned
+// and the sequence a whole number of chunks (a ragged last chunk would put
+// the final state mid-chunk)
+int check_carry(int64_t T, std::initializer_list<const void*> states) {
+  bool any = false;
+  for (const void* p : states) {
+    if (p == nullptr) continue;
+    any = true;
+    if (!aligned16(p)) return CAMOE_ERR_ALIGNMENT;
+  }
+  if (any && T % camoe::kChunk != 0) return CAMOE_ERR_SHAPE;
+  return CAMOE_OK;
+}
+
 int fwd_impl(const void* r, const void* w, const void* k, const void* v, const void* a,
              const void* b, void* y, float* sa, void* ckpt, size_t ckpt_bytes, int64_t B,
              int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
-             void* stream, int decay) {
+             void* stream, int decay, const float* s0 = nullptr, float* sT = nullptr) {
   int st = check_geometry(B, T, H_total, h0, h_count, N);
   if (st != CAMOE_OK) return st;
   const int al = resolve_algo(dtype, algo);
@@ -135,9 +151,11 @@ int fwd_impl(const void* r, const void* w, const void* k, const void* v, const v
     if (!aligned16(ckpt)) return CAMOE_ERR_ALIGNMENT;
     if (ckpt_bytes < required_ckpt(B, T, h_count, al)) return CAMOE_ERR_WORKSPACE;
   }
+  if ((st = check_carry(T, {s0, sT})) != CAMOE_OK) return st;
   camoe::FwdArgs p;
   p.r = r; p.w = w; p.k = k; p.v = v; p.a = a; p.b = b;
   p.y = y; p.sa = sa; p.ckpt = static_cast<float*>(ckpt);
+  p.s0 = s0; p.sT = sT;
   p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk, decay};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_fwd(p, s));
@@ -230,7 +248,8 @@ int bwd_impl(const void* r, const void* w, const void* k, const void* v, const v
              const void* b, const void* dy, const float* dsa, const void* ckpt, size_t ckpt_bytes,
              void* work, size_t work_bytes, void* dr, void* dw, void* dk, void* dv, void* da,
              void* db, int64_t B, int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N,
-             int dtype, int algo, void* stream, int decay) {
+             int dtype, int algo, void* stream, int decay, const float* s0 = nullptr,
+             const float* dsT = nullptr, float* ds0 = nullptr) {
   int st = check_geometry(B, T, H_total, h0, h_count, N);
   if (st != CAMOE_OK) return st;
   const int al = resolve_algo(dtype, algo);
@@ -254,10 +273,12 @@ int bwd_impl(const void* r, const void* w, const void* k, const void* v, const v
     if (!aligned16(work)) return CAMOE_ERR_ALIGNMENT;
     if (work_bytes < wneed) return CAMOE_ERR_WORKSPACE;
   }
+  if ((st = check_carry(T, {s0, dsT, ds0})) != CAMOE_OK) return st;
   camoe::BwdArgs p;
   p.r = r; p.w = w; p.k = k; p.v = v; p.a = a; p.b = b; p.dy = dy;
   p.dsa = dsa; p.ckpt = static_cast<const float*>(ckpt);
   p.dr = dr; p.dw = dw; p.dk = dk; p.dv = dv; p.da = da; p.db = db;
+  p.s0 = s0; p.dsT = dsT; p.ds0 = ds0;
   p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk, decay};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_bwd(p, work, s));
@@ -269,6 +290,18 @@ int bwd_impl(const void* r, const void* w, const void* k, const void* v, const v
 
 extern "C" {
 
+int camoe_wkv7_fwd_carry(const void* r, const void* w, const void* k, const void* v,
+                         const void* a, const void* b, void* y, float* sa, const float* s0,
+                         float* s_out, void* ckpt, size_t ckpt_bytes, int64_t B, int64_t T,
+                         int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
+                         void* stream) {
+  // an empty sequence would have to pass the state through unchanged; the
+  // carried calls want at least one chunk
+  if (T == 0 && (s0 != nullptr || s_out != nullptr)) return CAMOE_ERR_SHAPE;
+  return fwd_impl(r, w, k, v, a, b, y, sa, ckpt, ckpt_bytes, B, T, H_total, h0, h_count, N, dtype,
+                  algo, stream, camoe::kDecayClampW, s0, s_out);
+}
+
 int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v, const void* a,
                    const void* b, const void* dy, const float* dsa, const void* ckpt,
                    size_t ckpt_bytes, void* work, size_t work_bytes, void* dr, void* dw, void* dk,
@@ -276,6 +309,19 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v, c
                    int64_t h0, int64_t h_count, int N, int dtype, int algo, void* stream) {
   return bwd_impl(r, w, k, v, a, b, dy, dsa, ckpt, ckpt_bytes, work, work_bytes, dr, dw, dk, dv,
                   da, db, B, T, H_total, h0, h_count, N, dtype, algo, stream, camoe::kDecayClampW);
+}
+
+int camoe_wkv7_bwd_carry(const void* r, const void* w, const void* k, const void* v,
+                         const void* a, const void* b, const void* dy, const float* dsa,
+                         const float* s0, const float* ds_out, float* ds0, const void* ckpt,
+                         size_t ckpt_bytes, void* work, size_t work_bytes, void* dr, void* dw,
+                         void* dk, void* dv, void* da, void* db, int64_t B, int64_t T,
+                         int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
+                         void* stream) {
+  if (T == 0 && (s0 != nullptr || ds_out != nullptr || ds0 != nullptr)) return CAMOE_ERR_SHAPE;
+  return bwd_impl(r, w, k, v, a, b, dy, dsa, ckpt, ckpt_bytes, work, work_bytes, dr, dw, dk, dv,
+                  da, db, B, T, H_total, h0, h_count, N, dtype, algo, stream, camoe::kDecayClampW,
+                  s0, ds_out, ds0);
 }
 
 int camoe_wkv7_wind_bwd(const void* w, const void* q, const void* k, const void* v,

@@ -256,11 +256,21 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
   const int q = lane & 3, g = lane >> 2;
   if (role == 0) {
     // ------------------------------ G warp: the gradient recurrence ------------------------------
-    float G[8][4];  // dL/dS' of the chunk being processed
+    float G[8][4];  // dL/dS' of the chunk being processed: element (i0 + g (+8), 8 nt + 2q (+1))
+    if (p.dsT != nullptr) {  // the gradient of the final state enters at the last chunk
+      const float* src = p.dsT + p.g.state_off(ch) + (i0 + g) * kN + 2 * q;
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 8; ++nt) {
+        const float2 lo = *reinterpret_cast<const float2*>(src + 8 * nt);
+        const float2 hi = *reinterpret_cast<const float2*>(src + 8 * kN + 8 * nt);
+        G[nt][0] = lo.x; G[nt][1] = lo.y; G[nt][2] = hi.x; G[nt][3] = hi.y;
+      }
+    } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) G[nt][e] = 0.f;
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) G[nt][e] = 0.f;
+    }
     if (nchunk > 0) {
       const int li0 = load_idx(nchunk, nchunk - 1);
       if (!mbar_wait(&sm.full[li0 & (NS - 1)], par(li0, NS))) return;
@@ -339,6 +349,14 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
         mbar_arrive(&sm.gfull[xg]);
       }
       if (!next_ready && !mbar_wait(&sm.full[sn], par(lin, NS))) return;
+    }
+    if (p.ds0 != nullptr) {  // after chunk 0, G is the gradient of the start state
+      float* dst = p.ds0 + p.g.state_off(ch) + (i0 + g) * kN + 2 * q;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        *reinterpret_cast<float2*>(dst + 8 * nt) = make_float2(G[nt][0], G[nt][1]);
+        *reinterpret_cast<float2*>(dst + 8 * kN + 8 * nt) = make_float2(G[nt][2], G[nt][3]);
+      }
     }
     return;
   }
@@ -419,6 +437,17 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
     if (lo >= 2) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) lda_rm(sLo[kk], slo.S, Swz64{}, il, 16 * kk, lane);
+    } else if (p.s0 != nullptr) {  // chunk 0 starts from the state carried in (bf16, as stored)
+      const float* src = p.s0 + p.g.state_off(ch) + (i0 + g) * kN + 2 * q;
+      float Sf[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float2 a = *reinterpret_cast<const float2*>(src + 8 * nt);
+        const float2 c2 = *reinterpret_cast<const float2*>(src + 8 * kN + 8 * nt);
+        Sf[nt][0] = a.x; Sf[nt][1] = a.y; Sf[nt][2] = c2.x; Sf[nt][3] = c2.y;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) acc_to_a(sLo[kk], Sf[2 * kk], Sf[2 * kk + 1]);
     } else {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) sLo[kk][0] = sLo[kk][1] = sLo[kk][2] = sLo[kk][3] = 0u;

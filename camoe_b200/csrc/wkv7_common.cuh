@@ -81,6 +81,13 @@ struct BwdArgs {
   const float* ckpt;  // written by the matching forward
   void *dr, *dw, *dk, *dv, *da, *db;
   Geom g;
+  // a sequence carried in from a previous call (T a multiple of kChunk): the
+  // start state the forward was given (null = zero), the gradient of the final
+  // state (null = zero), and where to write the gradient of the start state
+  // (null = not wanted); [B, H, N, N] fp32 like FwdArgs::s0
+  const float* s0 = nullptr;
+  const float* dsT = nullptr;
+  float* ds0 = nullptr;
 };
 
 __device__ __forceinline__ float to_f32(float x) { return x; }

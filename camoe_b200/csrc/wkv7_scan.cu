@@ -527,8 +527,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdArgs p) {
   const int64_t nchunk = p.g.nchunk;
 
   float dS[16], S0[16], S[16];
+  if (p.dsT != nullptr) {  // the gradient of the final state enters at the last step
+    const float4* src = reinterpret_cast<const float4*>(p.dsT + p.g.state_off(ch) + i * kN + q * 16);
 #pragma unroll
-  for (int jj = 0; jj < 16; ++jj) dS[jj] = 0.f;
+    for (int m = 0; m < 4; ++m) {
+      const float4 x = src[m];
+      dS[4 * m] = x.x; dS[4 * m + 1] = x.y; dS[4 * m + 2] = x.z; dS[4 * m + 3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) dS[jj] = 0.f;
+  }
 
   Prefetch<Tin> pf;
   if (nchunk > 0) bwd_prefetch<Tin>(pf, p, ch, nchunk - 1);
@@ -538,6 +547,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdArgs p) {
     if (c > 0) bwd_prefetch<Tin>(pf, p, ch, c - 1);
     if (c > 0) {
       const float4* src = reinterpret_cast<const float4*>(p.ckpt + ((ch * nchunk + c) * kN + i) * kN + q * 16);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float4 x = src[m];
+        S0[4 * m] = x.x; S0[4 * m + 1] = x.y; S0[4 * m + 2] = x.z; S0[4 * m + 3] = x.w;
+      }
+    } else if (p.s0 != nullptr) {  // chunk 0 starts from the state carried in
+      const float4* src = reinterpret_cast<const float4*>(p.s0 + p.g.state_off(ch) + i * kN + q * 16);
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
         const float4 x = src[m];
@@ -595,6 +611,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdArgs p) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[e] = from_f32<Tin>(s[e]);
     }
+  }
+  if (p.ds0 != nullptr) {  // after chunk 0, dS is the gradient of the start state
+    float4* dst = reinterpret_cast<float4*>(p.ds0 + p.g.state_off(ch) + i * kN + q * 16);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) dst[m] = make_float4(dS[4 * m], dS[4 * m + 1], dS[4 * m + 2], dS[4 * m + 3]);
   }
 }
 

@@ -65,12 +65,25 @@ def work_bytes(B: int, T: int, h_count: int, dtype: torch.dtype, algo="auto") ->
 DECAYS = ("clampw", "wind")
 
 
+def _check_carry(states, B, H, device, decay):
+    given = {n: s for n, s in states.items() if s is not None}
+    if given and decay != "clampw":
+        raise ValueError("carried states are supported for the ClampW decay only")
+    for n, s in given.items():
+        _check_state(s, B, H, device, n)
+    return bool(given)
+
+
 def wkv7_forward(r, w, k, v, a, b, *, algo="auto", save_ckpt: bool = True, h0: int = 0,
                  h_count: int | None = None, y=None, sa=None, ckpt=None, zero_rest=False,
-                 decay: str = "clampw"):
+                 decay: str = "clampw", s0=None, s_out=None):
     """Forward.  Returns (y, sa, ckpt); ckpt is None when save_ckpt is False.
     ``decay="wind"`` runs the wind_backstepping op (decay exp(-exp(w))), whose
-    (q, z, a) are passed here as (r, a, b)."""
+    (q, z, a) are passed here as (r, a, b).
+
+    Training across calls (ClampW, T a multiple of 16): ``s0`` ([B, H, 64, 64]
+    fp32) is the state the sequence starts from and ``s_out`` receives its
+    final state; the checkpoint then serves ``wkv7_backward(..., s0=s0)``."""
     if decay not in DECAYS:
         raise ValueError(f"decay must be one of {DECAYS}, got {decay!r}")
     _check_inputs((r, w, k, v, a, b), "rwkvab")
@@ -90,12 +103,21 @@ def wkv7_forward(r, w, k, v, a, b, *, algo="auto", save_ckpt: bool = True, h0: i
             nbytes = ckpt.numel() * ckpt.element_size()
     else:
         ckpt = None
+    carry = _check_carry({"s0": s0, "s_out": s_out}, B, H, r.device, decay)
+    ptr = (lambda t: None if t is None else t.data_ptr())
+    if carry:
+        st = _lib.lib().camoe_wkv7_fwd_carry(
+            *(x.data_ptr() for x in (r, w, k, v, a, b)), y.data_ptr(), sa.data_ptr(), ptr(s0),
+            ptr(s_out), ptr(ckpt), nbytes, B, T, H, h0, hc, N, dtype_code(r.dtype),
+            algo_code(algo), _stream_ptr(r.device))
+        check(st)
+        return y, sa, ckpt
     if decay == "wind":  # the wind op's argument order: (w, q, k, v, z, a)
         fn, ins = _lib.lib().camoe_wkv7_wind_fwd, (w, r, k, v, a, b)
     else:
         fn, ins = _lib.lib().camoe_wkv7_fwd, (r, w, k, v, a, b)
     st = fn(*(x.data_ptr() for x in ins),
-            y.data_ptr(), sa.data_ptr(), None if ckpt is None else ckpt.data_ptr(), nbytes,
+            y.data_ptr(), sa.data_ptr(), ptr(ckpt), nbytes,
             B, T, H, h0, hc, N, dtype_code(r.dtype), algo_code(algo), _stream_ptr(r.device))
     check(st)
     return y, sa, ckpt
@@ -181,10 +203,15 @@ def wkv7_decode_step(r, w, k, v, a, b, state):
 
 def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
                   h_count: int | None = None, grads=None, zero_rest=False, work=None,
-                  decay: str = "clampw"):
+                  decay: str = "clampw", s0=None, ds_out=None, ds0=None):
     """Backward.  ``dsa`` (fp32) may be None.  Returns (dr, dw, dk, dv, da, db).
     ``work`` is the scratch workspace (allocated here when not given).  ``decay``
-    as in wkv7_forward (the gradients keep the (r, w, k, v, a, b) order)."""
+    as in wkv7_forward (the gradients keep the (r, w, k, v, a, b) order).
+
+    Training across calls (ClampW, T a multiple of 16): ``s0`` is the start
+    state the forward was given, ``ds_out`` the gradient of its final state
+    (None = zero) and ``ds0`` ([B, H, 64, 64] fp32) receives the gradient of
+    the start state."""
     if decay not in DECAYS:
         raise ValueError(f"decay must be one of {DECAYS}, got {decay!r}")
     _check_inputs((r, w, k, v, a, b, dy), "rwkvab" + "y")
@@ -203,6 +230,15 @@ def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
         work = torch.empty(wneed, dtype=torch.uint8, device=r.device)
     wbytes = 0 if work is None else work.numel() * work.element_size()
     dr, dw, dk, dv, da, db = grads
+    if _check_carry({"s0": s0, "ds_out": ds_out, "ds0": ds0}, B, H, r.device, decay):
+        ptr = (lambda t: None if t is None else t.data_ptr())
+        st = _lib.lib().camoe_wkv7_bwd_carry(
+            *(x.data_ptr() for x in (r, w, k, v, a, b)), dy.data_ptr(), ptr(dsa), ptr(s0),
+            ptr(ds_out), ptr(ds0), ptr(ckpt), nbytes, ptr(work), wbytes,
+            *(g.data_ptr() for g in grads), B, T, H, h0, hc, N, dtype_code(r.dtype),
+            algo_code(algo), _stream_ptr(r.device))
+        check(st)
+        return grads
     if decay == "wind":  # (w, q, k, v, z, a) in, (dw, dq, dk, dv, dz, da) out
         fn, ins, outs = _lib.lib().camoe_wkv7_wind_bwd, (w, r, k, v, a, b), (dw, dr, dk, dv, da, db)
     else:

@@ -111,6 +111,32 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v,
                    int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
                    int algo, void* stream);
 
+/* Training across calls (a long sequence processed in pieces with the
+ * state carried between them): camoe_wkv7_fwd and camoe_wkv7_bwd with the
+ * state arrays of camoe_wkv7_fwd_state ([B, H_total, N, N] fp32, element
+ * ((b*H_total + h)*N + i)*N + j = S[i][j]).  The forward starts every chain
+ * from s0 (NULL = zero) and writes its final state to s_out (NULL = not
+ * stored).  The backward takes the same s0, the gradient of the final state
+ * ds_out (NULL = zero), and writes the gradient of the start state to ds0
+ * (NULL = not wanted), besides the six input gradients; so the backward of a
+ * later piece hands its ds0 to the earlier piece as ds_out.  T must be a
+ * positive multiple of 16 when any state array is given (else
+ * CAMOE_ERR_SHAPE).  No counterpart in the reference, whose op always starts
+ * from the zero state (camoe/cuda/rwkv7_clampw.cu:28). */
+int camoe_wkv7_fwd_carry(const void* r, const void* w, const void* k, const void* v,
+                         const void* a, const void* b, void* y, float* sa, const float* s0,
+                         float* s_out, void* ckpt, size_t ckpt_bytes, int64_t B, int64_t T,
+                         int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
+                         void* stream);
+
+int camoe_wkv7_bwd_carry(const void* r, const void* w, const void* k, const void* v,
+                         const void* a, const void* b, const void* dy, const float* dsa,
+                         const float* s0, const float* ds_out, float* ds0, const void* ckpt,
+                         size_t ckpt_bytes, void* work, size_t work_bytes, void* dr, void* dw,
+                         void* dk, void* dv, void* da, void* db, int64_t B, int64_t T,
+                         int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
+                         void* stream);
+
 /* The reference's second WKV-7 op, wind_backstepping (camoe/cuda/wkv7_cuda.cu,
  * wkv7_cuda_fp32.cu; bound by camoe/cuda/wkv7_op.cpp:5-21), in its own
  * argument order: forward(w, q, k, v, z, a) with decay exp(-exp(w)) in place

@@ -6,7 +6,7 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
 
 Contents:
 
-* ``fwd`` / ``bwd`` / ``fwd_state`` — ctypes bindings of ``wkv7_oracle.c`` (a plain-C
+* ``fwd`` / ``bwd`` / ``fwd_state`` / ``bwd_state`` — ctypes bindings of ``wkv7_oracle.c`` (a plain-C
   restatement of ``camoe/backbone.py:264-294`` and of the gradient formulas of
   ``camoe/cuda/rwkv7_clampw.cu:83-170``), in float64 (ground truth) or float32
   (reference precision), OpenMP over (batch, head) chains.
@@ -54,6 +54,9 @@ def _load():
         g = getattr(lib, f"wkv7_oracle_bwd_{suf}")
         g.argtypes = [i64] * 5 + [fp] * 14 + [ci, ci]
         g.restype = ci
+        gs = getattr(lib, f"wkv7_oracle_bwd_state_{suf}")
+        gs.argtypes = [i64] * 5 + [fp] * 17 + [ci, ci]
+        gs.restype = ci
         h = getattr(lib, f"wkv7_oracle_fwd_state_{suf}")
         h.argtypes = [i64] * 4 + [fp] * 10 + [ci, ci]
         h.restype = ci
@@ -130,11 +133,33 @@ def bwd(r, w, k, v, a, b, dy, dsa=None, precision: str = "f64", ckpt: int = 64,
     return tuple(outs)
 
 
+def bwd_state(r, w, k, v, a, b, dy, dsa=None, s0=None, dsT=None, precision: str = "f64",
+              ckpt: int = 64, threads: int | None = None, decay: str = "clampw"):
+    """``bwd`` for a sequence carried across calls: the forward started from
+    ``s0`` ([B,H,N,N], None = zero) and ``dsT`` is the gradient of its final
+    state (None = zero).  Returns (dr, dw, dk, dv, da, db, ds0), ds0 the
+    gradient of the start state."""
+    r, w, k, v, a, b, dy = (_f32(x) for x in (r, w, k, v, a, b, dy))
+    B, T, H, N = r.shape
+    dsa = None if dsa is None else _f32(dsa)
+    s0 = None if s0 is None else _f32(s0).reshape(B, H, N, N)
+    dsT = None if dsT is None else _f32(dsT).reshape(B, H, N, N)
+    outs = [np.empty_like(r) for _ in range(6)]
+    ds0 = np.empty((B, H, N, N), dtype=np.float32)
+    fn = getattr(_load(), f"wkv7_oracle_bwd_state_{precision}")
+    rc = fn(B, T, H, N, ckpt, *map(_ptr, (r, w, k, v, a, b, dy, dsa, s0, dsT, ds0)),
+            *map(_ptr, outs), DECAYS[decay], threads or default_threads())
+    if rc != 0:
+        raise RuntimeError(f"oracle backward failed with code {rc}")
+    return tuple(outs) + (ds0,)
+
+
 def decay(w_in: float) -> float:
     return _load().wkv7_oracle_decay(float(w_in))
 
 
-def torch_reference(r, w, k, v, a, b, dy=None, dsa=None, s0=None, decay: str = "clampw"):
+def torch_reference(r, w, k, v, a, b, dy=None, dsa=None, s0=None, decay: str = "clampw",
+                    dsT=None):
     """Float64 torch restatement of camoe/backbone.py:264-294 returning (y, sa);
     with dy given, also the six input gradients from autograd (sa-gradient dsa
     optional).  ``s0`` ([B,H,N,N], default zero) is the start state.  Small
@@ -146,8 +171,9 @@ def torch_reference(r, w, k, v, a, b, dy=None, dsa=None, s0=None, decay: str = "
     rr, ww, kk, vv, aa, bb = xs
     B, T, H, N = rr.shape
     dec = torch.exp(-torch.exp(ww)) if decay == "wind" else torch.exp(W_SCALE / (1.0 + torch.exp(-ww)))
-    S = torch.zeros(B, H, N, N, dtype=torch.float64) if s0 is None else \
-        torch.as_tensor(_f32(s0), dtype=torch.float64).reshape(B, H, N, N)
+    S0 = None if s0 is None else torch.as_tensor(_f32(s0), dtype=torch.float64).reshape(
+        B, H, N, N).requires_grad_(dy is not None)
+    S = torch.zeros(B, H, N, N, dtype=torch.float64) if S0 is None else S0
     ys, sas = [], []
     for t in range(T):
         sa = (S * aa[:, t].unsqueeze(-2)).sum(-1)
@@ -162,7 +188,9 @@ def torch_reference(r, w, k, v, a, b, dy=None, dsa=None, s0=None, decay: str = "
     loss = (y * torch.as_tensor(_f32(dy), dtype=torch.float64)).sum()
     if dsa is not None:
         loss = loss + (sa * torch.as_tensor(_f32(dsa), dtype=torch.float64)).sum()
-    grads = torch.autograd.grad(loss, xs)
+    if dsT is not None:
+        loss = loss + (S * torch.as_tensor(_f32(dsT), dtype=torch.float64).reshape(B, H, N, N)).sum()
+    grads = torch.autograd.grad(loss, xs + ([S0] if S0 is not None else []))
     return (y.detach().numpy(), sa.detach().numpy()) + tuple(g.numpy() for g in grads)
 
 

@@ -114,7 +114,8 @@ static void step_##SUF(int64_t N, const REAL* wv, const float* k, const float* v
 static int chain_bwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t ck, int64_t b, int64_t h, \
         const float* r, const float* wi, const float* k, const float* v, const float* a,      \
         const float* bb, const float* dy, const float* dsa_ext,                               \
-        float* dr, float* dw, float* dk, float* dv, float* da, float* db, int decay)          \
+        float* dr, float* dw, float* dk, float* dv, float* da, float* db, int decay,           \
+        const float* s0, const float* dsT, float* ds0)                                         \
 {                                                                                              \
     const int64_t nck = (T + ck - 1) / ck;                                                     \
     const int64_t NN = N * N;                                                                  \
@@ -131,7 +132,9 @@ static int chain_bwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t ck, int64_t 
         free(satmp); return ORACLE_ERR_NOMEM;                                                  \
     }                                                                                          \
     /* forward pass keeping the state at the start of every checkpoint interval */             \
-    memset(Sbuf, 0, sizeof(REAL) * NN);                                                        \
+    if (s0) for (int64_t e = 0; e < NN; ++e) Sbuf[e] = (REAL)s0[e];                            \
+    else memset(Sbuf, 0, sizeof(REAL) * NN);                                                   \
+    if (dsT) for (int64_t e = 0; e < NN; ++e) dS[e] = (REAL)dsT[e];                            \
     for (int64_t c = 0; c < nck; ++c) {                                                        \
         memcpy(ckpt + c * NN, Sbuf, sizeof(REAL) * NN);                                        \
         const int64_t t1 = (c + 1) * ck < T ? (c + 1) * ck : T;                                \
@@ -207,6 +210,7 @@ static int chain_bwd_##SUF(int64_t T, int64_t H, int64_t N, int64_t ck, int64_t 
             }                                                                                  \
         }                                                                                      \
     }                                                                                          \
+    if (ds0) for (int64_t e = 0; e < NN; ++e) ds0[e] = (float)dS[e];                           \
     free(ckpt); free(Sbuf); free(sabuf); free(wbuf); free(dS); free(dsa); free(wtmp);         \
     free(satmp);                                                                               \
     return ORACLE_OK;                                                                          \
@@ -266,7 +270,28 @@ int wkv7_oracle_bwd_##SUF(int64_t B, int64_t T, int64_t H, int64_t N, int64_t ck
     _Pragma("omp parallel for schedule(dynamic) num_threads(nthreads > 0 ? nthreads : 1)")     \
     for (int64_t c = 0; c < B * H; ++c) {                                                      \
         int e = chain_bwd_##SUF(T, H, N, ckpt, c / H, c % H, r, w, k, v, a, b, dy, dsa,        \
-                                dr, dw, dk, dv, da, db, decay);                                \
+                                dr, dw, dk, dv, da, db, decay, NULL, NULL, NULL);              \
+        if (e) err = e;                                                                        \
+    }                                                                                          \
+    return err;                                                                                \
+}                                                                                              \
+                                                                                               \
+/* Backward of a sequence carried across calls: s0 the start state of the    \
+ * forward, dsT the gradient of its final state (NULL = zero), ds0 receives   \
+ * the gradient of the start state (all [B, H, N, N], NULL allowed). */         \
+int wkv7_oracle_bwd_state_##SUF(int64_t B, int64_t T, int64_t H, int64_t N, int64_t ckpt,     \
+        const float* r, const float* w, const float* k, const float* v, const float* a,       \
+        const float* b, const float* dy, const float* dsa, const float* s0, const float* dsT,  \
+        float* ds0, float* dr, float* dw, float* dk, float* dv, float* da, float* db,          \
+        int decay, int nthreads)                                                               \
+{                                                                                              \
+    if (B < 0 || T < 0 || H < 0 || N <= 0 || ckpt <= 0) return ORACLE_ERR_ARG;                 \
+    int err = ORACLE_OK;                                                                       \
+    _Pragma("omp parallel for schedule(dynamic) num_threads(nthreads > 0 ? nthreads : 1)")     \
+    for (int64_t c = 0; c < B * H; ++c) {                                                      \
+        int e = chain_bwd_##SUF(T, H, N, ckpt, c / H, c % H, r, w, k, v, a, b, dy, dsa,        \
+                                dr, dw, dk, dv, da, db, decay, s0 ? s0 + c * N * N : NULL,     \
+                                dsT ? dsT + c * N * N : NULL, ds0 ? ds0 + c * N * N : NULL);   \
         if (e) err = e;                                                                        \
     }                                                                                          \
     return err;                                                                                \

@@ -162,6 +162,38 @@ def test_fwd_state_argument_errors_need_no_device():
     assert fst(T=0, s_out=None) == _lib.OK
 
 
+def test_carry_argument_errors_need_no_device():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+    s = ctypes.c_void_p(1 << 30)
+
+    def fc(s0=s, s_out=None, **kw):
+        g = dict(B=1, T=32, H=1, h0=0, hc=1, N=64, dtype=0, algo=0)
+        g.update(kw)
+        return lib.camoe_wkv7_fwd_carry(p, p, p, p, p, p, p, p, s0, s_out, None, 0, g["B"],
+                                        g["T"], g["H"], g["h0"], g["hc"], g["N"], g["dtype"],
+                                        g["algo"], None)
+
+    def bc(s0=s, ds_out=None, ds0=None, **kw):
+        g = dict(B=1, T=32, H=1, h0=0, hc=1, N=64, dtype=0, algo=0)
+        g.update(kw)
+        return lib.camoe_wkv7_bwd_carry(p, p, p, p, p, p, p, None, s0, ds_out, ds0, p, 1 << 40,
+                                        p, 1 << 40, p, p, p, p, p, p, g["B"], g["T"], g["H"],
+                                        g["h0"], g["hc"], g["N"], g["dtype"], g["algo"], None)
+
+    assert fc(T=40) == _lib.ERR_SHAPE                 # not a whole number of chunks
+    assert fc(T=0) == _lib.ERR_SHAPE                  # nothing to carry the state through
+    assert fc(s0=ctypes.c_void_p((1 << 30) + 4)) == _lib.ERR_ALIGNMENT
+    assert fc(s0=None, s_out=ctypes.c_void_p(8)) == _lib.ERR_ALIGNMENT
+    assert fc(N=32) == _lib.ERR_UNSUPPORTED
+    assert fc(B=0) == _lib.OK
+    assert bc(T=24) == _lib.ERR_SHAPE
+    assert bc(s0=None, ds0=s, T=0) == _lib.ERR_SHAPE
+    assert bc(ds_out=ctypes.c_void_p(40)) == _lib.ERR_ALIGNMENT
+    assert bc(ds0=ctypes.c_void_p(4)) == _lib.ERR_ALIGNMENT
+    assert bc(hc=0) == _lib.OK
+
+
 def test_error_raises_camoe_error():
     with pytest.raises(_lib.CamoeError) as ei:
         _lib.check(_lib.ERR_ALIGNMENT)

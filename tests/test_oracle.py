@@ -142,3 +142,39 @@ def test_wind_inputs_are_in_the_bounded_decay_range():
     lo = math.exp(-math.exp(-0.5))
     dec = np.exp(-np.exp(inp["w"].numpy().astype(np.float64)))
     assert dec.min() >= lo - 1e-12 and dec.max() < 1
+
+
+def test_oracle_state_gradients_against_torch_autograd():
+    """The backward of a sequence carried across calls: with a start state and
+    a gradient of the final state, all six gradients and the gradient of the
+    start state against float64 torch autograd."""
+    inp = make_inputs(2, 24, 2, seed=9, with_dsa=True)
+    xs = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    g = np.random.default_rng(9)
+    s0 = g.standard_normal((2, 2, 64, 64)).astype(np.float32)
+    dsT = g.standard_normal((2, 2, 64, 64)).astype(np.float32)
+    got = oracle.bwd_state(*xs, inp["dy"], inp["dsa"], s0=s0, dsT=dsT, ckpt=8)
+    want = oracle.torch_reference(*xs, dy=inp["dy"], dsa=inp["dsa"], s0=s0, dsT=dsT)[2:]
+    for name, a, b in zip(GRADS + ("ds0",), got, want):
+        assert nrel(a, b) < 1e-6, name
+    # without states it is bwd
+    plain = oracle.bwd(*xs, inp["dy"], inp["dsa"])
+    zero = oracle.bwd_state(*xs, inp["dy"], inp["dsa"])
+    for a, b in zip(plain, zero[:6]):
+        assert np.array_equal(a, b)
+
+
+def test_oracle_state_gradient_split_identity():
+    """Gradients of one pass over [0, T) equal those of [0, T1) and [T1, T)
+    with the state carried forward and its gradient carried back."""
+    T, T1 = 48, 16
+    inp = make_inputs(1, T, 2, seed=10)
+    xs = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    full = oracle.bwd(*xs, inp["dy"])
+    first = [x[:, :T1] for x in xs]
+    second = [x[:, T1:] for x in xs]
+    _, _, s1 = oracle.fwd_state(*first)
+    g2 = oracle.bwd_state(*second, inp["dy"][:, T1:], s0=s1)
+    g1 = oracle.bwd_state(*first, inp["dy"][:, :T1], dsT=g2[6])
+    for name, f, a, b in zip(GRADS, full, g1[:6], g2[:6]):
+        assert nrel(np.concatenate([a, b], 1), f) < 1e-5, name
