@@ -255,10 +255,15 @@ int bwd_impl(const void* r, const void* w, const void* k, const void* v, const v
   const int al = resolve_algo(dtype, algo);
   if (al < 0) return CAMOE_ERR_UNSUPPORTED;
   if (B * h_count == 0 || T == 0) return CAMOE_OK;
-  const void* ptrs[] = {r, w, k, v, a, b, dy, dr, dw, dk, dv, da, db};
-  for (const void* p : ptrs) {
-    if (p == nullptr) return CAMOE_ERR_INVALID_ARG;
-    if (!aligned16(p)) return CAMOE_ERR_ALIGNMENT;
+  // dv and ds0 only: the chunked path with a start-state gradient may leave
+  // the five key-side gradients null (its key-side pass is then skipped)
+  const bool key_null = dr == nullptr && dw == nullptr && dk == nullptr && da == nullptr &&
+                        db == nullptr;
+  const bool ds0_only = key_null && ds0 != nullptr && al == CAMOE_ALGO_CHUNKED;
+  const void* ptrs[] = {r, w, k, v, a, b, dy, dv, dr, dw, dk, da, db};
+  for (int i = 0; i < (ds0_only ? 8 : 13); ++i) {
+    if (ptrs[i] == nullptr) return CAMOE_ERR_INVALID_ARG;
+    if (!aligned16(ptrs[i])) return CAMOE_ERR_ALIGNMENT;
   }
   if (dsa != nullptr && !aligned16(dsa)) return CAMOE_ERR_ALIGNMENT;
   const size_t need = required_ckpt(B, T, h_count, al);

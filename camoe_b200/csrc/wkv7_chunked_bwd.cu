@@ -951,6 +951,10 @@ cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
                           : vb::launch<4>(V, p.g.chains(), stream);
   if (e != cudaSuccess) return e;
 
+  // a carried backward that wants only dv and the start-state gradient
+  // (dr, dw, dk, da, db all null) needs no key-side pass
+  if (p.dr == nullptr && p.dw == nullptr && p.dk == nullptr && p.da == nullptr && p.db == nullptr)
+    return cudaGetLastError();
   kb::Params K;
   K.a = p;
   K.work = work;

@@ -203,7 +203,8 @@ def wkv7_decode_step(r, w, k, v, a, b, state):
 
 def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
                   h_count: int | None = None, grads=None, zero_rest=False, work=None,
-                  decay: str = "clampw", s0=None, ds_out=None, ds0=None):
+                  decay: str = "clampw", s0=None, ds_out=None, ds0=None,
+                  ds0_only: bool = False):
     """Backward.  ``dsa`` (fp32) may be None.  Returns (dr, dw, dk, dv, da, db).
     ``work`` is the scratch workspace (allocated here when not given).  ``decay``
     as in wkv7_forward (the gradients keep the (r, w, k, v, a, b) order).
@@ -211,7 +212,9 @@ def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
     Training across calls (ClampW, T a multiple of 16): ``s0`` is the start
     state the forward was given, ``ds_out`` the gradient of its final state
     (None = zero) and ``ds0`` ([B, H, 64, 64] fp32) receives the gradient of
-    the start state."""
+    the start state.  ``ds0_only`` (chunked path, ``ds0`` given) computes only
+    ``ds0`` and dv, skipping the key-side pass; the other five gradients are
+    left unwritten."""
     if decay not in DECAYS:
         raise ValueError(f"decay must be one of {DECAYS}, got {decay!r}")
     _check_inputs((r, w, k, v, a, b, dy), "rwkvab" + "y")
@@ -230,13 +233,18 @@ def wkv7_backward(r, w, k, v, a, b, dy, dsa, ckpt, *, algo="auto", h0: int = 0,
         work = torch.empty(wneed, dtype=torch.uint8, device=r.device)
     wbytes = 0 if work is None else work.numel() * work.element_size()
     dr, dw, dk, dv, da, db = grads
+    if ds0_only and ds0 is None:
+        raise ValueError("ds0_only needs ds0")
     if _check_carry({"s0": s0, "ds_out": ds_out, "ds0": ds0}, B, H, r.device, decay):
         ptr = (lambda t: None if t is None else t.data_ptr())
+        outs = [g.data_ptr() for g in grads]
+        if ds0_only:
+            outs = [None, None, None, outs[3], None, None]
         st = _lib.lib().camoe_wkv7_bwd_carry(
             *(x.data_ptr() for x in (r, w, k, v, a, b)), dy.data_ptr(), ptr(dsa), ptr(s0),
             ptr(ds_out), ptr(ds0), ptr(ckpt), nbytes, ptr(work), wbytes,
-            *(g.data_ptr() for g in grads), B, T, H, h0, hc, N, dtype_code(r.dtype),
-            algo_code(algo), _stream_ptr(r.device))
+            *outs, B, T, H, h0, hc, N, dtype_code(r.dtype), algo_code(algo),
+            _stream_ptr(r.device))
         check(st)
         return grads
     if decay == "wind":  # (w, q, k, v, z, a) in, (dw, dq, dk, dv, dz, da) out

@@ -119,7 +119,10 @@ int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v,
  * stored).  The backward takes the same s0, the gradient of the final state
  * ds_out (NULL = zero), and writes the gradient of the start state to ds0
  * (NULL = not wanted), besides the six input gradients; so the backward of a
- * later piece hands its ds0 to the earlier piece as ds_out.  T must be a
+ * later piece hands its ds0 to the earlier piece as ds_out.  With
+ * CAMOE_ALGO_CHUNKED (or AUTO on bf16) and ds0 given, dr, dw, dk, da and db
+ * may all be NULL: only dv and ds0 are then computed, and the key-side pass,
+ * about 60% of the backward, is skipped.  T must be a
  * positive multiple of 16 when any state array is given (else
  * CAMOE_ERR_SHAPE).  No counterpart in the reference, whose op always starts
  * from the zero state (camoe/cuda/rwkv7_clampw.cu:28). */
@@ -135,6 +138,24 @@ int camoe_wkv7_bwd_carry(const void* r, const void* w, const void* k, const void
                          size_t ckpt_bytes, void* work, size_t work_bytes, void* dr, void* dw,
                          void* dk, void* dv, void* da, void* db, int64_t B, int64_t T,
                          int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
+                         void* stream);
+
+/* Joins the segments of chains cut in time into P pieces of equal length.
+ * states, trans and local are [B*P, H_total, N, N] fp32 arrays (segment g of
+ * sequence b at index b*P + g, element as in camoe_wkv7_fwd_state); only the
+ * heads [h0, h0 + h_count) are read or written.  trans holds every segment's
+ * transition A (its final state from an identity start with v = 0).
+ *   backward = 0: local = C, each segment's final state from a zero start;
+ *     states[b, 0] is given and states[b, g] = states[b, g-1] A_{g-1} + C_{g-1}
+ *     is written for g = 1 .. P-1 (the start state of every segment).
+ *   backward = 1: local = D, each segment's start-state gradient with no
+ *     gradient at its end; states[b, P-1] is given and
+ *     states[b, g-1] = states[b, g] A_g^T + D_g is written for g = P-1 .. 1
+ *     (the gradient of every segment's final state).
+ * One launch on `stream`.  No counterpart in the reference, whose op runs each
+ * chain from t = 0 to T in one sequential pass (camoe/cuda/rwkv7_clampw.cu:36). */
+int camoe_wkv7_seg_chain(float* states, const float* trans, const float* local, int64_t B,
+                         int64_t P, int64_t H_total, int64_t h0, int64_t h_count, int backward,
                          void* stream);
 
 /* The reference's second WKV-7 op, wind_backstepping (camoe/cuda/wkv7_cuda.cu,

@@ -193,6 +193,35 @@ def test_carry_argument_errors_need_no_device():
     assert bc(ds0=ctypes.c_void_p(4)) == _lib.ERR_ALIGNMENT
     assert bc(hc=0) == _lib.OK
 
+    def key_null(ds0, dtype, algo):
+        n = None
+        return lib.camoe_wkv7_bwd_carry(p, p, p, p, p, p, p, None, s, None, ds0, p, 1 << 40, p,
+                                        1 << 40, n, n, n, p, n, n, 1, 32, 1, 0, 1, 64, dtype,
+                                        algo, None)
+
+    # dv and ds0 only: chunked path with ds0 given; the scan or no ds0 need all six
+    assert key_null(None, 0, 2) == _lib.ERR_INVALID_ARG
+    assert key_null(s, 1, 0) == _lib.ERR_INVALID_ARG      # fp32 resolves to the scan
+    assert key_null(s, 0, 1) == _lib.ERR_INVALID_ARG
+
+
+def test_seg_chain_argument_errors_need_no_device():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+
+    def sc(st=p, tr=p, lo=p, B=2, P=4, H=4, h0=0, hc=4, backward=0):
+        return lib.camoe_wkv7_seg_chain(st, tr, lo, B, P, H, h0, hc, backward, None)
+
+    assert sc(P=0) == _lib.ERR_INVALID_ARG
+    assert sc(h0=2, hc=3) == _lib.ERR_INVALID_ARG         # head range past H_total
+    assert sc(backward=2) == _lib.ERR_INVALID_ARG
+    assert sc(tr=None) == _lib.ERR_INVALID_ARG
+    assert sc(lo=ctypes.c_void_p(40)) == _lib.ERR_ALIGNMENT
+    # nothing to chain: no device call
+    assert sc(P=1) == _lib.OK
+    assert sc(B=0) == _lib.OK
+    assert sc(hc=0) == _lib.OK
+
 
 def test_error_raises_camoe_error():
     with pytest.raises(_lib.CamoeError) as ei:

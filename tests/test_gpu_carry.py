@@ -118,6 +118,27 @@ def test_split_gradients_equal_one_pass(dtype, algo):
     assert nrel(torch.cat([saa, sab], 1).cpu().numpy(), sa.cpu().numpy()) < tol
 
 
+def test_ds0_only_skips_the_key_side():
+    """ds0_only (chunked): ds0 and dv bit for bit those of the full carried
+    backward; the other five gradient buffers are not written."""
+    B, T, H = 2, 96, 3
+    inp = make_inputs(B, T, H, seed=12)
+    xs = [inp[n].to(torch.bfloat16).cuda() for n in NAMES]
+    dy = inp["dy"].to(torch.bfloat16).cuda()
+    s0, dsT = (torch.from_numpy(x).cuda() for x in states(B, H, 12))
+    y, sa, ck = ops.wkv7_forward(*xs, algo="chunked", s0=s0)
+    full0 = torch.empty_like(s0)
+    g_full = ops.wkv7_backward(*xs, dy, None, ck, algo="chunked", s0=s0, ds_out=dsT, ds0=full0)
+    only0 = torch.empty_like(s0)
+    marks = tuple(torch.full_like(xs[0], 3.0) for _ in range(6))
+    ops.wkv7_backward(*xs, dy, None, ck, algo="chunked", s0=s0, ds_out=dsT, ds0=only0,
+                      grads=marks, ds0_only=True)
+    torch.cuda.synchronize()
+    assert torch.equal(only0, full0) and torch.equal(marks[3], g_full[3])
+    for i in (0, 1, 2, 4, 5):
+        assert (marks[i] == 3.0).all()
+
+
 @pytest.mark.parametrize("dtype,algo", PATHS, ids=PATH_IDS)
 def test_zero_state_is_the_plain_op(dtype, algo):
     """s0 = 0 and ds_out = 0 give the plain op's outputs and gradients."""
