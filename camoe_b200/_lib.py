@@ -21,7 +21,8 @@ EXPORTS = ("camoe_wkv7_version", "camoe_wkv7_strerror", "camoe_wkv7_last_cuda_er
            "camoe_wkv7_device_errors", "camoe_wkv7_ckpt_bytes", "camoe_wkv7_work_bytes",
            "camoe_wkv7_fwd", "camoe_wkv7_bwd", "camoe_wkv7_fwd_state",
            "camoe_wkv7_state_work_bytes", "camoe_wkv7_wind_fwd", "camoe_wkv7_wind_bwd",
-           "camoe_wkv7_fwd_carry", "camoe_wkv7_bwd_carry", "camoe_wkv7_seg_chain")
+           "camoe_wkv7_fwd_carry", "camoe_wkv7_bwd_carry", "camoe_wkv7_seg_chain",
+           "camoe_wkv7_fwd_value")
 
 
 # include/camoe_timemix.h: fused elementwise kernels of the time mix
@@ -77,6 +78,8 @@ def lib() -> ctypes.CDLL:
     l.camoe_wkv7_bwd_carry.restype = ci
     l.camoe_wkv7_bwd_carry.argtypes = [vp] * 12 + [sz, vp, sz] + [vp] * 6 + [i64] * 5 + \
         [ci, ci, ci, vp]
+    l.camoe_wkv7_fwd_value.restype = ci
+    l.camoe_wkv7_fwd_value.argtypes = [vp] * 11 + [sz] + [i64] * 5 + [ci, ci, vp]
     l.camoe_wkv7_seg_chain.restype = ci
     l.camoe_wkv7_seg_chain.argtypes = [vp] * 3 + [i64] * 5 + [ci, vp]
     l.camoe_tm_work_bytes.argtypes = [i64] * 3

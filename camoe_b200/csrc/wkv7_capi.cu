@@ -136,7 +136,8 @@ int check_carry(int64_t T, std::initializer_list<const void*> states) {
 int fwd_impl(const void* r, const void* w, const void* k, const void* v, const void* a,
              const void* b, void* y, float* sa, void* ckpt, size_t ckpt_bytes, int64_t B,
              int64_t T, int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
-             void* stream, int decay, const float* s0 = nullptr, float* sT = nullptr) {
+             void* stream, int decay, const float* s0 = nullptr, float* sT = nullptr,
+             bool records_ready = false) {
   int st = check_geometry(B, T, H_total, h0, h_count, N);
   if (st != CAMOE_OK) return st;
   const int al = resolve_algo(dtype, algo);
@@ -156,6 +157,7 @@ int fwd_impl(const void* r, const void* w, const void* k, const void* v, const v
   p.r = r; p.w = w; p.k = k; p.v = v; p.a = a; p.b = b;
   p.y = y; p.sa = sa; p.ckpt = static_cast<float*>(ckpt);
   p.s0 = s0; p.sT = sT;
+  p.records_ready = records_ready;
   p.g = camoe::Geom{B, T, H_total, h0, h_count, (T + camoe::kChunk - 1) / camoe::kChunk, decay};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (al == CAMOE_ALGO_CHUNKED) return cuda_status(camoe::chunked::launch_fwd(p, s));
@@ -305,6 +307,18 @@ int camoe_wkv7_fwd_carry(const void* r, const void* w, const void* k, const void
   if (T == 0 && (s0 != nullptr || s_out != nullptr)) return CAMOE_ERR_SHAPE;
   return fwd_impl(r, w, k, v, a, b, y, sa, ckpt, ckpt_bytes, B, T, H_total, h0, h_count, N, dtype,
                   algo, stream, camoe::kDecayClampW, s0, s_out);
+}
+
+int camoe_wkv7_fwd_value(const void* r, const void* w, const void* k, const void* v,
+                         const void* a, const void* b, void* y, float* sa, const float* s0,
+                         float* s_out, void* ckpt, size_t ckpt_bytes, int64_t B, int64_t T,
+                         int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
+                         void* stream) {
+  if (T == 0 && (s0 != nullptr || s_out != nullptr)) return CAMOE_ERR_SHAPE;
+  if (dtype != CAMOE_DTYPE_BF16) return CAMOE_ERR_UNSUPPORTED;
+  if (ckpt == nullptr) return CAMOE_ERR_INVALID_ARG;
+  return fwd_impl(r, w, k, v, a, b, y, sa, ckpt, ckpt_bytes, B, T, H_total, h0, h_count, N, dtype,
+                  CAMOE_ALGO_CHUNKED, stream, camoe::kDecayClampW, s0, s_out, true);
 }
 
 int camoe_wkv7_bwd(const void* r, const void* w, const void* k, const void* v, const void* a,

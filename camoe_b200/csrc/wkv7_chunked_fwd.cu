@@ -695,16 +695,18 @@ cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
       !tma::encode_bhtn_cols(&V.map_y, p.y, p.g.B, p.g.T, p.g.H, 16 * rb, false) ||
       !tma::encode_bhtn_cols(&V.map_sa, p.sa, p.g.B, p.g.T, p.g.H, 16 * rb, true))
     return cudaErrorInvalidValue;
-  const size_t ksmem = ka::kGroups * sizeof(ka::Group) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(ka::keyside_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ksmem);
-  if (e != cudaSuccess) return e;
-  const int64_t items = p.g.chains() * p.g.nchunk;
-  const int64_t want = (items + ka::kGroups - 1) / ka::kGroups;
-  const int64_t kgrid = want < 2LL * sms ? want : 2LL * sms;
-  ka::keyside_kernel<<<(unsigned)kgrid, ka::kThreads, ksmem, stream>>>(K);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  if (!(p.records_ready && p.ckpt != nullptr)) {
+    const size_t ksmem = ka::kGroups * sizeof(ka::Group) + 1024;
+    cudaError_t e = cudaFuncSetAttribute(ka::keyside_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ksmem);
+    if (e != cudaSuccess) return e;
+    const int64_t items = p.g.chains() * p.g.nchunk;
+    const int64_t want = (items + ka::kGroups - 1) / ka::kGroups;
+    const int64_t kgrid = want < 2LL * sms ? want : 2LL * sms;
+    ka::keyside_kernel<<<(unsigned)kgrid, ka::kThreads, ksmem, stream>>>(K);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
 
   return rb == 1 ? vf::launch<1>(V, p.g.chains(), stream)
        : rb == 2 ? vf::launch<2>(V, p.g.chains(), stream)

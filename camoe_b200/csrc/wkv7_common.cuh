@@ -67,12 +67,16 @@ struct FwdArgs {
   // start state (null = zero) and final state (null = not stored) of every
   // chain, fp32 [B, H, N, N] with element ((b*H + h)*N + i)*N + j = S[i][j];
   // sT may equal s0 (each element is read before it is overwritten, by the
-  // same thread).  Only the inference forward (ckpt == null) takes them.
+  // same thread).  The inference forward (ckpt == null) and the carried
+  // training forward take them.
   const float* s0 = nullptr;
   float* sT = nullptr;
   // inference forward only: with a workspace the chunked path runs as two
   // kernels (key-side records into `work`, then the value pass), else fused
   void* work = nullptr;
+  // chunked training forward: the key-side records in ckpt were written by an
+  // earlier forward of the same r, w, k, a, b and geometry; run the value pass only
+  bool records_ready = false;
 };
 
 struct BwdArgs {

@@ -123,6 +123,29 @@ def wkv7_forward(r, w, k, v, a, b, *, algo="auto", save_ckpt: bool = True, h0: i
     return y, sa, ckpt
 
 
+def wkv7_forward_value(r, w, k, v, a, b, ckpt, *, h0: int = 0, h_count: int | None = None,
+                       y=None, sa=None, s0=None, s_out=None):
+    """The value pass of a chunked training forward alone (bf16): ``ckpt``
+    holds the key-side records an earlier ``wkv7_forward`` of the same r, w,
+    k, a, b (and geometry) wrote; ``v`` and the start state ``s0`` may differ.
+    Writes y, sa, ``s_out`` and the checkpoint's states.  Returns (y, sa)."""
+    _check_inputs((r, w, k, v, a, b), "rwkvab")
+    B, T, H, N = r.shape
+    hc = H - h0 if h_count is None else h_count
+    _check_carry({"s0": s0, "s_out": s_out}, B, H, r.device, "clampw")
+    if y is None:
+        y = torch.empty_like(r)
+    if sa is None:
+        sa = torch.empty(B, T, H, N, dtype=torch.float32, device=r.device)
+    ptr = (lambda t: None if t is None else t.data_ptr())
+    st = _lib.lib().camoe_wkv7_fwd_value(
+        *(x.data_ptr() for x in (r, w, k, v, a, b)), y.data_ptr(), sa.data_ptr(), ptr(s0),
+        ptr(s_out), ckpt.data_ptr(), ckpt.numel() * ckpt.element_size(), B, T, H, h0, hc, N,
+        dtype_code(r.dtype), _stream_ptr(r.device))
+    check(st)
+    return y, sa
+
+
 def _check_state(s, B, H, device, name):
     if s.dtype != torch.float32 or tuple(s.shape) != (B, H, HEAD_SIZE, HEAD_SIZE) \
             or not s.is_contiguous() or s.device != device:

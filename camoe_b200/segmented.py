@@ -10,8 +10,10 @@ no copy -- joined through their states.  The state map of a segment is
 affine, S_end = S_start A + C, so
 
 1. every segment's transition A (its final state from an identity start with
-   v = 0) and its final state C from a zero start come from two stateful
-   forwards over all segments at once (``ops.wkv7_forward_state``);
+   v = 0) and its final state C from a zero start come from two forwards over
+   all segments at once (on the chunked path the key-side pass, which does not
+   depend on v or the start state, runs once for these and step 3:
+   ``camoe_wkv7_fwd_value``);
 2. the start states S_g = S_{g-1} A_{g-1} + C_{g-1}, S_0 = s0, come from one
    launch that chains the P - 1 products per chain (``camoe_wkv7_seg_chain``);
 3. the training forward of every segment starts from its S_g
@@ -111,6 +113,11 @@ def wkv7_forward_segmented(r, w, k, v, a, b, segments: int, *, h0: int = 0,
     sv = starts.view(B, P, H, N, N)
     if s0 is not None:
         sv[:, 0, hs] = s0[:, hs]
+    fin = _states(BP, H, dev) if s_out is not None else None
+    # the chunked path runs the key-side pass once, into the checkpoint, and
+    # the value pass three times over it
+    chunked = r.dtype == torch.bfloat16 and algo in ("auto", "chunked")
+    ckpt = None
     if P > 1:
         # 1. transitions (identity start, v = 0) and zero-start final states
         local = _states(BP, H, dev)
@@ -118,18 +125,26 @@ def wkv7_forward_segmented(r, w, k, v, a, b, segments: int, *, h0: int = 0,
         eye[:, hs] = torch.eye(N, device=dev)
         vz = torch.empty_like(v)
         vz[:, :, hs].zero_()
-        ops.wkv7_forward_state(xs[0], xs[1], xs[2], _view(vz, P), xs[4], xs[5], eye, algo=algo,
-                               h0=h0, h_count=hc, y=yv, sa=sav, out_state=trans)
+        xz = (xs[0], xs[1], xs[2], _view(vz, P), xs[4], xs[5])
+        if chunked:
+            _, _, ckpt = ops.wkv7_forward(*xz, algo=algo, h0=h0, h_count=hc, y=yv, sa=sav, s0=eye,
+                                          s_out=trans)
+            ops.wkv7_forward_value(*xs, ckpt, h0=h0, h_count=hc, y=yv, sa=sav, s_out=local)
+        else:
+            ops.wkv7_forward_state(*xz, eye, algo=algo, h0=h0, h_count=hc, y=yv, sa=sav,
+                                   out_state=trans)
+            ops.wkv7_forward_state(*xs, None, algo=algo, h0=h0, h_count=hc, y=yv, sa=sav,
+                                   out_state=local)
         del vz, eye
-        ops.wkv7_forward_state(*xs, None, algo=algo, h0=h0, h_count=hc, y=yv, sa=sav,
-                               out_state=local)
         # 2. the start state of every segment
         seg_chain(starts, trans, local, B, P, h0, hc, backward=False)
         del local
     # 3. the training forward of every segment from its start state
-    fin = _states(BP, H, dev) if s_out is not None else None
-    _, _, ckpt = ops.wkv7_forward(*xs, algo=algo, h0=h0, h_count=hc, y=yv, sa=sav, s0=starts,
-                                  s_out=fin)
+    if ckpt is not None:
+        ops.wkv7_forward_value(*xs, ckpt, h0=h0, h_count=hc, y=yv, sa=sav, s0=starts, s_out=fin)
+    else:
+        _, _, ckpt = ops.wkv7_forward(*xs, algo=algo, h0=h0, h_count=hc, y=yv, sa=sav,
+                                      s0=starts, s_out=fin)
     if s_out is not None:
         s_out[:, hs] = fin.view(B, P, H, N, N)[:, P - 1, hs]
     saved = Saved(xs, (B, T, H, N), P, h0, hc, starts, trans, ckpt, algo)

@@ -132,6 +132,20 @@ int camoe_wkv7_fwd_carry(const void* r, const void* w, const void* k, const void
                          int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype, int algo,
                          void* stream);
 
+/* The value pass of camoe_wkv7_fwd_carry alone (bf16, chunked): the
+ * key-side records in ckpt (which depend on r, w, k, a and b only) were
+ * written by an earlier camoe_wkv7_fwd_carry or camoe_wkv7_fwd of the same r,
+ * w, k, a, b and geometry into the same ckpt, and are reused; v, s0 may
+ * differ.  Writes y, sa, s_out and the checkpoint's states, so the ckpt then
+ * serves the backward of this call.  Several forwards over one sequence that
+ * differ only in v or the start state (camoe_b200/segmented.py) run the
+ * key-side pass once. */
+int camoe_wkv7_fwd_value(const void* r, const void* w, const void* k, const void* v,
+                         const void* a, const void* b, void* y, float* sa, const float* s0,
+                         float* s_out, void* ckpt, size_t ckpt_bytes, int64_t B, int64_t T,
+                         int64_t H_total, int64_t h0, int64_t h_count, int N, int dtype,
+                         void* stream);
+
 int camoe_wkv7_bwd_carry(const void* r, const void* w, const void* k, const void* v,
                          const void* a, const void* b, const void* dy, const float* dsa,
                          const float* s0, const float* ds_out, float* ds0, const void* ckpt,

@@ -205,6 +205,22 @@ def test_carry_argument_errors_need_no_device():
     assert key_null(s, 0, 1) == _lib.ERR_INVALID_ARG
 
 
+def test_fwd_value_argument_errors_need_no_device():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+
+    def fv(ckpt=p, nbytes=1 << 40, s0=None, dtype=0, T=32, B=1):
+        return lib.camoe_wkv7_fwd_value(p, p, p, p, p, p, p, p, s0, None, ckpt, nbytes, B, T, 1,
+                                        0, 1, 64, dtype, None)
+
+    assert fv(dtype=1) == _lib.ERR_UNSUPPORTED       # chunked records are bf16 only
+    assert fv(ckpt=None) == _lib.ERR_INVALID_ARG     # the records live in the checkpoint
+    assert fv(nbytes=100) == _lib.ERR_WORKSPACE
+    assert fv(T=0, s0=p) == _lib.ERR_SHAPE
+    assert fv(T=24, s0=p) == _lib.ERR_SHAPE
+    assert fv(B=0) == _lib.OK
+
+
 def test_seg_chain_argument_errors_need_no_device():
     lib = _lib.lib()
     p = ctypes.c_void_p(16)

@@ -139,6 +139,29 @@ def test_ds0_only_skips_the_key_side():
         assert (marks[i] == 3.0).all()
 
 
+def test_value_pass_reuses_the_key_side_records():
+    """camoe_wkv7_fwd_value over a checkpoint written by a forward with another
+    v and start state gives bit for bit the outputs, final state and (through
+    the backward) gradients of a full forward with its own v and start state."""
+    B, T, H = 2, 96, 3
+    inp = make_inputs(B, T, H, seed=13)
+    xs = [inp[n].to(torch.bfloat16).cuda() for n in NAMES]
+    dy = inp["dy"].to(torch.bfloat16).cuda()
+    s0, _ = (torch.from_numpy(x).cuda() for x in states(B, H, 13))
+    other = list(xs)
+    other[3] = (xs[3].float() * -0.5).to(torch.bfloat16)
+    s_a, s_b = torch.empty_like(s0), torch.empty_like(s0)
+    y0, sa0, ck0 = ops.wkv7_forward(*xs, algo="chunked", s0=s0, s_out=s_a)
+    _, _, ck1 = ops.wkv7_forward(*other, algo="chunked")
+    y1, sa1 = ops.wkv7_forward_value(*xs, ck1, s0=s0, s_out=s_b)
+    g0 = ops.wkv7_backward(*xs, dy, None, ck0, algo="chunked", s0=s0)
+    g1 = ops.wkv7_backward(*xs, dy, None, ck1, algo="chunked", s0=s0)
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1) and torch.equal(sa0, sa1) and torch.equal(s_a, s_b)
+    for a, b_ in zip(g0, g1):
+        assert torch.equal(a, b_)
+
+
 @pytest.mark.parametrize("dtype,algo", PATHS, ids=PATH_IDS)
 def test_zero_state_is_the_plain_op(dtype, algo):
     """s0 = 0 and ds_out = 0 give the plain op's outputs and gradients."""
