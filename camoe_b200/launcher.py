@@ -57,17 +57,35 @@ def plan_shards(B: int, H: int, world: int) -> list[Shard]:
     raise ValueError(f"cannot split B={B} x H={H} chains evenly over {world} ranks")
 
 
-def cuda_shard_fn(inputs: dict, shard: Shard, device: torch.device) -> dict:
-    """Forward + backward of one shard on `device` through the C ABI (head range in place)."""
-    from . import ops
+def cuda_shard_fn(inputs: dict, shard: Shard, device: torch.device, segments="auto") -> dict:
+    """Forward + backward of one shard on `device` through the C ABI (head range
+    in place).  A shard of few long chains (bf16) runs time-segmented
+    (camoe_b200.segmented): ``segments`` "auto" picks the count from the
+    chain count, the length and the SM count; an int forces it."""
+    from . import ops, segmented
 
     sl = slice(shard.b0, shard.b1)
     xs = [inputs[n][sl].to(device) for n in NAMES]
     dy = inputs["dy"][sl].to(device)
     dsa = inputs["dsa"][sl].to(device) if inputs.get("dsa") is not None else None
     hc = shard.h1 - shard.h0
-    y, sa, ck = ops.wkv7_forward(*xs, h0=shard.h0, h_count=hc, zero_rest=True)
-    grads = ops.wkv7_backward(*xs, dy, dsa, ck, h0=shard.h0, h_count=hc, zero_rest=True)
+    T = xs[0].shape[1]
+    P = segments
+    if segments == "auto":
+        P = 1
+        if xs[0].dtype == torch.bfloat16:
+            sms = torch.cuda.get_device_properties(device).multi_processor_count
+            P = segmented.auto_segments(shard.chains, T, sms)
+    if P > 1:
+        y = torch.zeros_like(xs[0])
+        sa = torch.zeros(xs[0].shape, dtype=torch.float32, device=device)
+        grads = tuple(torch.zeros_like(xs[0]) for _ in range(6))
+        _, _, saved = segmented.wkv7_forward_segmented(*xs, P, h0=shard.h0, h_count=hc, y=y,
+                                                       sa=sa)
+        segmented.wkv7_backward_segmented(saved, dy, dsa, grads=grads)
+    else:
+        y, sa, ck = ops.wkv7_forward(*xs, h0=shard.h0, h_count=hc, zero_rest=True)
+        grads = ops.wkv7_backward(*xs, dy, dsa, ck, h0=shard.h0, h_count=hc, zero_rest=True)
     torch.cuda.synchronize(device)
     hs = slice(shard.h0, shard.h1)
     out = {"y": y, "sa": sa}

@@ -59,6 +59,20 @@ class Saved:
     algo: str
 
 
+def auto_segments(chains: int, T: int, sms: int, min_len: int = 2048) -> int:
+    """Segments per chain: the largest power of two P with 2 * chains * P <=
+    sms (up to sms / 2 chain segments the value passes run two CTAs per
+    segment, one per SM, so every segment still gets its SMs) and segments of
+    at least ``min_len`` steps (below that the three forward passes cost more
+    than the parallelism gains); 1 when the chains already fill the GPU.
+    B200 (148 SMs), the long-context share of 8 chains at T=65536: P = 8,
+    measured fastest of 4, 8 and 16."""
+    P = 1
+    while 2 * chains * 2 * P <= sms and T % (16 * 2 * P) == 0 and T // (2 * P) >= min_len:
+        P *= 2
+    return P
+
+
 def _view(x: torch.Tensor, P: int) -> torch.Tensor:
     B, T, H, N = x.shape
     return x.view(B * P, T // P, H, N)

@@ -25,3 +25,17 @@ def test_launcher_matches_single_process(B, H):
     torch.cuda.synchronize()
     for n, want in zip(launcher.OUT_NAMES, (y, sa) + tuple(g)):
         np.testing.assert_array_equal(full[n].float().numpy(), want.float().cpu().numpy(), err_msg=n)
+
+
+def test_segmented_shard_matches_one_pass():
+    """cuda_shard_fn with a forced segment count on a head-group shard: the
+    same outputs as the one-pass shard within the bf16 tolerance."""
+    from helpers import TOL_BF16, nrel
+    inp = make_inputs(1, 512, 4, 64, seed=10, with_dsa=True, dtype=torch.bfloat16)
+    inp["dsa"] = inp["dsa"].float()
+    shard = launcher.Shard(0, 1, 1, 3)
+    dev = torch.device("cuda", 0)
+    one = launcher.cuda_shard_fn(inp, shard, dev, segments=1)
+    seg = launcher.cuda_shard_fn(inp, shard, dev, segments=4)
+    for n in launcher.OUT_NAMES:
+        assert nrel(seg[n].float().numpy(), one[n].float().numpy()) < TOL_BF16, n

@@ -51,6 +51,17 @@ def test_plan_shards():
         launcher.plan_shards(3, 5, 2)
 
 
+def test_auto_segments():
+    from camoe_b200.segmented import auto_segments
+    assert auto_segments(8, 65536, 148) == 8      # long-context share: 64 segments, 128 CTAs
+    assert auto_segments(16, 65536, 148) == 4
+    assert auto_segments(64, 65536, 148) == 1     # the chains fill the GPU already
+    assert auto_segments(64, 4096, 148) == 1
+    assert auto_segments(8, 4096, 148) == 2       # segments of at least 2048 steps
+    assert auto_segments(8, 2048, 148) == 1
+    assert auto_segments(1, 65536 + 16, 148) == 1  # T must split into whole chunks
+
+
 @pytest.mark.parametrize("B,H", [(2, 2), (1, 4)], ids=["batch-shards", "head-groups"])
 def test_two_ranks_gloo_match_single_process(B, H):
     inp = make_inputs(B, 32, H, 64, seed=3, with_dsa=True)
