@@ -178,3 +178,25 @@ def test_oracle_state_gradient_split_identity():
     g1 = oracle.bwd_state(*first, inp["dy"][:, :T1], dsT=g2[6])
     for name, f, a, b in zip(GRADS, full, g1[:6], g2[:6]):
         assert nrel(np.concatenate([a, b], 1), f) < 1e-5, name
+
+
+def test_oracle_segment_map_is_affine():
+    """The algebra of the time-segmented path, on the oracle: a stretch's final
+    state is S_end = s0 A + C, with A the final state from the identity with
+    v = 0 and C the final state from zero; its start-state gradient is
+    ds0 = dsT A^T + D, with D the start-state gradient when dsT = 0."""
+    inp = make_inputs(1, 40, 2, seed=11)
+    xs = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
+    g = np.random.default_rng(11)
+    s0 = g.standard_normal((1, 2, 64, 64)).astype(np.float32)
+    dsT = g.standard_normal((1, 2, 64, 64)).astype(np.float32)
+    eye = np.broadcast_to(np.eye(64, dtype=np.float32), (1, 2, 64, 64)).copy()
+    xz = list(xs)
+    xz[3] = np.zeros_like(xs[3])
+    A = oracle.fwd_state(*xz, s0=eye)[2].astype(np.float64)
+    C = oracle.fwd_state(*xs)[2].astype(np.float64)
+    S = oracle.fwd_state(*xs, s0=s0)[2]
+    assert nrel(S, s0.astype(np.float64) @ A + C) < 1e-6
+    D = oracle.bwd_state(*xs, inp["dy"], s0=s0)[6].astype(np.float64)
+    ds0 = oracle.bwd_state(*xs, inp["dy"], s0=s0, dsT=dsT)[6]
+    assert nrel(ds0, dsT.astype(np.float64) @ np.swapaxes(A, -1, -2) + D) < 1e-6
