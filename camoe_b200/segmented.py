@@ -63,14 +63,17 @@ def auto_segments(chains: int, T: int, sms: int, min_len: int = 2048) -> int:
     """Segments per chain: the largest power of two P with 2 * chains * P <=
     sms (up to sms / 2 chain segments the value passes run two CTAs per
     segment, one per SM, so every segment still gets its SMs) and segments of
-    at least ``min_len`` steps (below that the three forward passes cost more
-    than the parallelism gains); 1 when the chains already fill the GPU.
-    B200 (148 SMs), the long-context share of 8 chains at T=65536: P = 8,
-    measured fastest of 4, 8 and 16."""
+    at least ``min_len`` steps; 1 when that P is below 4.  The segmented step
+    walks 3/P of the chain's chunks in value forwards and 2/P in value
+    backwards, at two CTAs per segment, against all of them once each at up
+    to four CTAs per chain in one pass; per chunk on B200 that is
+    (3 x 0.41 + 2 x 0.52) / P us against 0.34 + 0.43 us, a gain only from
+    P > 2.9.  B200 (148 SMs), the long-context share of 8 chains at
+    T=65536: P = 8, measured fastest of 4, 8 and 16."""
     P = 1
     while 2 * chains * 2 * P <= sms and T % (16 * 2 * P) == 0 and T // (2 * P) >= min_len:
         P *= 2
-    return P
+    return P if P >= 4 else 1
 
 
 def _view(x: torch.Tensor, P: int) -> torch.Tensor:

@@ -57,7 +57,9 @@ def test_auto_segments():
     assert auto_segments(16, 65536, 148) == 4
     assert auto_segments(64, 65536, 148) == 1     # the chains fill the GPU already
     assert auto_segments(64, 4096, 148) == 1
-    assert auto_segments(8, 4096, 148) == 2       # segments of at least 2048 steps
+    assert auto_segments(32, 65536, 148) == 1     # P = 2 would be slower than one pass
+    assert auto_segments(8, 8192, 148) == 4       # segments of at least 2048 steps
+    assert auto_segments(8, 4096, 148) == 1
     assert auto_segments(8, 2048, 148) == 1
     assert auto_segments(1, 65536 + 16, 148) == 1  # T must split into whole chunks
 
