@@ -234,5 +234,4 @@ class SegmentedClampW(torch.autograd.Function):
         if dsa is not None:
             dsa = dsa.to(torch.float32).contiguous()
         grads = wkv7_backward_segmented(saved, dy, dsa)
-        del ctx.saved
         return tuple(grads) + (None,)
