@@ -13,6 +13,14 @@ larger than the 126 MB L2, so no flush is needed between steps.
 For N > 1 run one process per GPU under torch.distributed.run; the reported
 time is the max over ranks of the CUDA-event time of the K timed steps.
 
+``--split`` (strong scaling) takes the workload as the whole problem and
+splits its B x H chains over the ranks as camoe_b200.launcher does (batch
+shards, else (batch, head-group) shards read in place through the head
+range); a shard of few long chains runs time-segmented
+(camoe_b200.segmented.auto_segments).  E.g. ``--workload long_b2_t65536
+--split`` under 8 ranks: 8 chains of 65536 steps per GPU.  Inputs are drawn on
+the GPU from a seeded generator.
+
 ``--impl reference`` times the CPU oracle port of the reference's recurrence
 (fp32, every host thread) on a bounded sample of the same workload; it prints
 the same JSON line with "impl": "reference".
@@ -190,6 +198,104 @@ def run_reference(args, wl, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_split(args, wl, world, rank, local):
+    """Strong scaling: the workload is the whole problem, split over the ranks."""
+    import torch.nn.functional as F
+
+    from camoe_b200 import launcher, segmented
+
+    dev = torch.device("cuda", local)
+    B, T, H, N = wl["B"], wl["T"], wl["H"], wl["N"]
+    sh = launcher.plan_shards(B, H, world)[rank]
+    nb, hc = sh.b1 - sh.b0, sh.h1 - sh.h0
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    shp = (nb, T, H, N)
+    r, k, v, u, dy, w, kk = (torch.randn(shp, generator=gen, device=dev) for _ in range(7))
+    w = wl["w_mu"] + wl["w_sigma"] * w
+    kk = F.normalize(kk, dim=-1, p=2.0)
+    xs = [t.to(torch.bfloat16).contiguous() for t in (r, w, k, v, -kk, kk * torch.sigmoid(u))]
+    dy = dy.to(torch.bfloat16)
+    del r, k, v, u, w, kk
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    P = segmented.auto_segments(nb * hc, T, sms) if args.segments == "auto" else int(args.segments)
+    y = torch.zeros_like(xs[0])
+    sa = torch.zeros(xs[0].shape, dtype=torch.float32, device=dev)
+    grads = tuple(torch.zeros_like(xs[0]) for _ in range(6))
+    ckpt = torch.empty(max(ops.ckpt_bytes(nb, T, hc, torch.bfloat16), 16), dtype=torch.uint8,
+                       device=dev)
+    work = torch.empty(max(ops.work_bytes(nb, T, hc, torch.bfloat16), 16), dtype=torch.uint8,
+                       device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        if P > 1:
+            _, _, saved = segmented.wkv7_forward_segmented(*xs, P, h0=sh.h0, h_count=hc, y=y,
+                                                           sa=sa)
+            if ev is not None:
+                ev[1].record(stream)
+            segmented.wkv7_backward_segmented(saved, dy, grads=grads)
+        else:
+            ops.wkv7_forward(*xs, h0=sh.h0, h_count=hc, y=y, sa=sa, ckpt=ckpt)
+            if ev is not None:
+                ev[1].record(stream)
+            ops.wkv7_backward(*xs, dy, None, ckpt, h0=sh.h0, h_count=hc, grads=grads, work=work)
+        if ev is not None:
+            ev[2].record(stream)
+
+    clocks = ClockSampler(local)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world, local)
+    torch.cuda.synchronize(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for kk_ in range(args.steps):
+        step(evs[kk_])
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world, local)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    ms = max_over_ranks(start.elapsed_time(end), world, local)
+    fwd_ms = max_over_ranks(sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps, world, local)
+    bwd_ms = max_over_ranks(sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps, world, local)
+    step_ms = ms / args.steps
+    value = B * T * args.steps / (ms / 1e3)
+    hbm, peak_kind = peaks()
+    shard_elems = nb * T * hc * N
+    step_gbs = (FWD_BYTES + BWD_BYTES) * shard_elems / (step_ms / 1e3) / 1e9
+    bwd_gbs = BWD_BYTES * shard_elems / (bwd_ms / 1e3) / 1e9
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded randn drawn on the GPU)",
+                "config": {"workload": f"{args.workload} split: B={B} T={T} H={H} N={N} bf16 "
+                                       f"WKV-7 ClampW fwd+bwd over {world} GPU(s), {nb} "
+                                       f"sequence(s) x {hc} heads per GPU",
+                           "model": "WKV-7 ClampW op", "global_batch": B, "seq_len": T,
+                           "heads": H, "head_size": N, "segments_per_chain": P,
+                           "parallelism": f"{world} (batch, head-group) shards, no collective",
+                           "l2": "inputs larger than L2, no flush",
+                           "w_in": f"N({wl['w_mu']},{wl['w_sigma']})"},
+                "roofline": {"bound": "hbm", "kernel": "backward of one GPU's shard",
+                             "achieved": bwd_gbs, "peak": hbm, "peak_kind": peak_kind,
+                             "unit": "GB/s", "frac": bwd_gbs / hbm, "traffic": None,
+                             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "step_achieved": step_gbs,
+                             "step_frac": step_gbs / hbm},
+                "clocks": clk,
+                "gpu_launches": (9 if P > 1 else 4) * args.steps,
+                "tokens_per_s_per_gpu": value / world}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def config_of(args, wl, world):
     return {"workload": f"{args.workload}: B={wl['B']}/GPU T={wl['T']} H={wl['H']} N={wl['N']} "
                         f"bf16 WKV-7 ClampW fwd+bwd", "model": "WKV-7 ClampW op",
@@ -209,6 +315,9 @@ def main():
     ap.add_argument("--algo", default="auto", choices=["auto", "scan", "chunked"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--split", action="store_true",
+                    help="strong scaling: split the workload's chains over the ranks")
+    ap.add_argument("--segments", default="auto", help="with --split: segments per chain")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload]
@@ -220,6 +329,9 @@ def main():
         return
 
     world, rank, local = dist_setup(args)
+    if args.split:
+        run_split(args, wl, world, rank, local)
+        return
     dev = torch.device("cuda", local)
     B, T, H, N = wl["B"], wl["T"], wl["H"], wl["N"]
     inp = make_inputs(B, T, H, N, seed=1000 + rank, w_mu=wl["w_mu"], w_sigma=wl["w_sigma"],
