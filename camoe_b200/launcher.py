@@ -108,6 +108,9 @@ def _worker(rank, world, port, backend, inputs, shards, shard_fn, results, timeo
             device = torch.device("cuda", rank)
         else:
             device = torch.device("cpu")
+            # one node: gloo on the loopback device, so that its choice of
+            # interface does not depend on the host name resolving
+            os.environ.setdefault("GLOO_SOCKET_IFNAME", "lo")
         dist.init_process_group(backend, init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                                 world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
         out = shard_fn(inputs, shards[rank], device)
