@@ -20,7 +20,8 @@ from __future__ import annotations
 import datetime
 import os
 import queue
-import socket
+import shutil
+import tempfile
 import traceback
 from dataclasses import dataclass
 
@@ -93,13 +94,7 @@ def cuda_shard_fn(inputs: dict, shard: Shard, device: torch.device, segments="au
     return {n: t[:, :, hs].cpu() for n, t in out.items()}
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _worker(rank, world, port, backend, inputs, shards, shard_fn, results, timeout_s):
+def _worker(rank, world, init_method, backend, inputs, shards, shard_fn, results, timeout_s):
     import torch.distributed as dist
     try:
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -111,7 +106,7 @@ def _worker(rank, world, port, backend, inputs, shards, shard_fn, results, timeo
             # one node: gloo on the loopback device, so that its choice of
             # interface does not depend on the host name resolving
             os.environ.setdefault("GLOO_SOCKET_IFNAME", "lo")
-        dist.init_process_group(backend, init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+        dist.init_process_group(backend, init_method=init_method, rank=rank,
                                 world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
         out = shard_fn(inputs, shards[rank], device)
         dist.barrier()  # every rank finished its shard
@@ -135,9 +130,11 @@ def run(inputs: dict, world: int, backend: str = "nccl", shard_fn=None,
     fn = shard_fn or cuda_shard_fn
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, backend, inputs, shards, fn,
-                                                 results, timeout), daemon=True)
+    # rendezvous through a file in a private directory: no port to race for
+    rdv_dir = tempfile.mkdtemp(prefix="camoe_rdv_")
+    init_method = "file://" + os.path.join(rdv_dir, "store")
+    procs = [ctx.Process(target=_worker, args=(r, world, init_method, backend, inputs, shards,
+                                                 fn, results, timeout), daemon=True)
              for r in range(world)]
     for p in procs:
         p.start()
@@ -161,6 +158,7 @@ def run(inputs: dict, world: int, backend: str = "nccl", shard_fn=None,
             if p.is_alive():
                 p.kill()
                 p.join(timeout=5.0)
+        shutil.rmtree(rdv_dir, ignore_errors=True)
     if errors:
         rank, tb = errors[0]
         raise RuntimeError(f"rank {rank} failed:\n{tb}")
