@@ -16,8 +16,10 @@
 // problem fits the array; otherwise CAMOE_ERR_WORKSPACE), then, on its first
 // call on a device, looks up the array's device address with
 // cudaGetSymbolAddress while that device is current (make that first call
-// before any stream capture), then launches the existing forward and backward
-// kernels on `stream` with the array as their checkpoint.
+// before any stream capture; the address is kept for the life of the process,
+// so it is stale after a cudaDeviceReset of that device), then launches the
+// existing forward and backward kernels on `stream` with the array as their
+// checkpoint.
 //
 // The array is shared by every call and keeps the last call's contents.
 // Nothing in it needs to start at zero: the forward writes every checkpoint
@@ -99,6 +101,14 @@ extern "C" int camoe_wkv7_fwd_bwd_noalloc(
     if (!aligned16(p)) return CAMOE_ERR_ALIGNMENT;
   }
   if (dsa != nullptr && !aligned16(dsa)) return CAMOE_ERR_ALIGNMENT;
+  // Every algorithm needs more than 4 KiB per chain and 16-step chunk, so a
+  // problem with more chain-chunks than the scratch holds 4 KiB pieces cannot
+  // fit.  Rejecting those first keeps the byte counts below from overflowing
+  // (B * h_count < 2^31 and nchunk <= 2^14 / chains bound every product).
+  const int64_t chains = B * h_count;
+  const int64_t nchunk = T / camoe::kChunk + (T % camoe::kChunk != 0 ? 1 : 0);
+  if (nchunk > static_cast<int64_t>(CAMOE_WKV7_NOALLOC_SCRATCH_BYTES / 4096) / chains)
+    return CAMOE_ERR_WORKSPACE;
   // the scratch holds the checkpoint, then the backward workspace
   const size_t need = camoe_wkv7_ckpt_bytes(B, T, h_count, N, dtype, al);
   const size_t wneed = camoe_wkv7_work_bytes(B, T, h_count, N, dtype, al);

@@ -22,6 +22,7 @@ import os
 import queue
 import shutil
 import tempfile
+import time
 import traceback
 from dataclasses import dataclass
 
@@ -94,6 +95,19 @@ def cuda_shard_fn(inputs: dict, shard: Shard, device: torch.device, segments="au
     return {n: t[:, :, hs].cpu() for n, t in out.items()}
 
 
+def _to_wire(t: torch.Tensor):
+    """(bf16 flag, numpy array) of a CPU tensor; bf16 travels as its int16 bit pattern."""
+    t = t.contiguous()
+    if t.dtype == torch.bfloat16:
+        return True, t.view(torch.int16).numpy()
+    return False, t.numpy()
+
+
+def _from_wire(is_bf16: bool, a) -> torch.Tensor:
+    t = torch.from_numpy(a)
+    return t.view(torch.bfloat16) if is_bf16 else t
+
+
 def _worker(rank, world, init_method, backend, inputs, shards, shard_fn, results, timeout_s):
     import torch.distributed as dist
     try:
@@ -110,7 +124,9 @@ def _worker(rank, world, init_method, backend, inputs, shards, shard_fn, results
                                 world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
         out = shard_fn(inputs, shards[rank], device)
         dist.barrier()  # every rank finished its shard
-        results.put((rank, "ok", out))
+        # plain arrays, pickled by value: a tensor would travel as a shared-memory
+        # handle that the parent can no longer open once this process has exited
+        results.put((rank, "ok", {n: _to_wire(t) for n, t in out.items()}))
         dist.destroy_process_group()
     except Exception:  # reported to the parent, which raises
         results.put((rank, "error", traceback.format_exc()))
@@ -139,16 +155,19 @@ def run(inputs: dict, world: int, backend: str = "nccl", shard_fn=None,
     for p in procs:
         p.start()
     got, errors = {}, []
-    deadline = timeout + 10.0
+    # one deadline for the whole job, not one per result
+    limit = timeout + 10.0
+    deadline = time.monotonic() + limit
     try:
         while len(got) + len(errors) < world:
             try:
-                rank, status, payload = results.get(timeout=deadline)
+                left = max(deadline - time.monotonic(), 0.0)
+                rank, status, payload = results.get(timeout=left)
             except queue.Empty:
                 raise TimeoutError(f"ranks {sorted(set(range(world)) - set(got))} did not finish "
-                                   f"within {deadline:.0f} s")
+                                   f"within {limit:.0f} s")
             if status == "ok":
-                got[rank] = payload
+                got[rank] = {n: _from_wire(*x) for n, x in payload.items()}
             else:
                 errors.append((rank, payload))
                 break

@@ -239,8 +239,10 @@ size_t camoe_wkv7_state_work_bytes(int64_t B, int64_t T, int64_t h_count, int N,
  * camoe_wkv7_work_bytes() of the problem exceed that size (about 1900 chains x
  * 16-step chunks for the chunked algorithm, 4096 for the scan).  The first
  * call on a device looks up the array's address (cudaGetSymbolAddress); make
- * it before any stream capture.  All calls share the array: calls whose work
- * overlaps on the GPU race. */
+ * it before any stream capture.  That address is cached for the life of the
+ * process and does not survive a cudaDeviceReset of the device: do not call
+ * this entry point on a device after resetting it.  All calls share the
+ * array: calls whose work overlaps on the GPU race. */
 int camoe_wkv7_fwd_bwd_noalloc(const void* r, const void* w, const void* k, const void* v,
                                const void* a, const void* b, const void* dy, const float* dsa,
                                void* y, float* sa, void* dr, void* dw, void* dk, void* dv,

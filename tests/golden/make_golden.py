@@ -3,6 +3,10 @@
 Runs the reference's own CPU recurrence ``RWKV7_TimeMix._run_torch_fallback``
 (camoe/backbone.py:250-294, imported from the reference checkout) in float32
 and takes the six input gradients from torch.autograd through it.  The
+recurrence computes ``sa`` at every step (camoe/backbone.py:284) but returns
+only y, so ``sa`` is captured from the reference's own calls: a
+TorchFunctionMode records the result of every ``Tensor.sum(dim=-1)`` made
+inside the function, which per step are sa_t (:284) and then y_t (:290).  The
 reference has no tests or stored vectors for this op, so these fixtures are
 what pins the oracle (tests/test_oracle.py) to the reference's behaviour.
 
@@ -18,6 +22,7 @@ import sys
 
 import numpy as np
 import torch
+from torch.overrides import TorchFunctionMode
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
@@ -40,6 +45,21 @@ def input_digest(inp: dict) -> str:
     return h.hexdigest()
 
 
+class RowSumRecorder(TorchFunctionMode):
+    """Records the output of every ``Tensor.sum(dim=-1)`` call made under it."""
+
+    def __init__(self):
+        super().__init__()
+        self.sums = []
+
+    def __torch_function__(self, func, types, args=(), kwargs=None):
+        kwargs = kwargs or {}
+        out = func(*args, **kwargs)
+        if func is torch.Tensor.sum and kwargs.get("dim") == -1:
+            self.sums.append(out.detach().clone())
+        return out
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     sys.path.insert(0, ref_root)
@@ -51,9 +71,15 @@ def main():
         inp = make_inputs(B, T, H, N, seed=seed, w_mu=mu, w_sigma=sig)
         xs = [inp[n].reshape(B, T, H * N).clone().requires_grad_(True)
               for n in ("r", "w", "k", "v", "a", "b")]
-        y = RWKV7_TimeMix._run_torch_fallback(*xs, H, N)
+        rec = RowSumRecorder()
+        with rec:
+            y = RWKV7_TimeMix._run_torch_fallback(*xs, H, N)
+        assert len(rec.sums) == 2 * T, "expected the sa and y row sums of every step"
+        sa = torch.stack(rec.sums[0::2], dim=1)  # [B, T, H, N]: sa_t of :284
+        y_rows = torch.stack(rec.sums[1::2], dim=1)  # y_t of :290, a check of the capture
+        assert torch.equal(y_rows.reshape(B, T, H * N), y.detach())
         (y * inp["dy"].reshape(B, T, H * N)).sum().backward()
-        out = {"y": y.detach().reshape(B, T, H, N).numpy()}
+        out = {"y": y.detach().reshape(B, T, H, N).numpy(), "sa": sa.numpy()}
         for n, x in zip(("dr", "dw", "dk", "dv", "da", "db"), xs):
             out[n] = x.grad.reshape(B, T, H, N).numpy()
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"),

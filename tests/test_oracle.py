@@ -28,11 +28,13 @@ def test_oracle_matches_reference_golden(path, precision):
     z, inp = load_golden(path)
     assert input_digest(inp) == str(z["input_sha256"]), "input generator drifted"
     args = [inp[n] for n in ("r", "w", "k", "v", "a", "b")]
-    y, _ = oracle.fwd(*args, precision=precision)
+    y, sa = oracle.fwd(*args, precision=precision)
     grads = oracle.bwd(*args, inp["dy"], precision=precision, ckpt=16)
-    # the golden values are float32 autograd through a float32 loop
+    # the golden values are float32 autograd through a float32 loop; sa is the
+    # reference's own per-step row sum (camoe/backbone.py:284), captured
     tol = 2e-5
     assert nrel(y, z["y"]) < tol
+    assert nrel(sa, z["sa"]) < tol
     for n, g in zip(GRADS, grads):
         assert nrel(g, z[n]) < tol, n
 
