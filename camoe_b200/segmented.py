@@ -85,6 +85,44 @@ def _states(BP: int, H: int, device) -> torch.Tensor:
     return torch.zeros(BP, H, HEAD_SIZE, HEAD_SIZE, dtype=torch.float32, device=device)
 
 
+class Buffers:
+    """Device buffers of a segmented forward + backward, allocated and filled
+    once so that a step launches only the op's kernels and the two chain
+    kernels: no allocation and no fill or copy kernels (unless a start state,
+    a final-state gradient, ``s_out`` or ``ds0`` is passed, which are copied).
+    Every step overwrites them, so one Buffers serves one forward/backward pair
+    at a time, in stream order.
+
+    Holds, for B sequences of T steps cut into P segments (heads [h0, h0 +
+    h_count) of H): the segments' start states (row 0 kept at zero), their
+    transitions and zero-start final states, the identity start of the
+    transition pass, v = 0 over the head range, the end-state gradients (the
+    last kept at zero), and the checkpoint and backward workspace."""
+
+    def __init__(self, B: int, T: int, H: int, P: int, *, h0: int = 0,
+                 h_count: int | None = None, device=None, dtype=torch.bfloat16, algo="auto"):
+        hc = H - h0 if h_count is None else h_count
+        N = HEAD_SIZE
+        BP, Ts = B * P, T // P
+        self.key = (B, T, H, P, h0, hc, dtype, algo)
+        self.starts, self.trans, self.local = (_states(BP, H, device) for _ in range(3))
+        self.ends = _states(BP, H, device)
+        self.eye = _states(BP, H, device)
+        self.eye[:, h0:h0 + hc] = torch.eye(N, device=device)
+        self.vz = torch.zeros(BP, Ts, H, N, dtype=dtype, device=device)
+        self.ckpt = torch.empty(max(ops.ckpt_bytes(BP, Ts, hc, dtype, algo), 16),
+                                dtype=torch.uint8, device=device)
+        self.work = torch.empty(max(ops.work_bytes(BP, Ts, hc, dtype, algo), 16),
+                                dtype=torch.uint8, device=device)
+        self.starts_dirty = False  # row 0 of starts holds a start state, not zero
+        self.ends_dirty = False    # the last row of ends holds a gradient, not zero
+
+    def check(self, B, T, H, P, h0, hc, dtype, algo):
+        if (B, T, H, P, h0, hc, dtype, algo) != self.key:
+            raise ValueError(f"Buffers made for {self.key}, called with "
+                             f"{(B, T, H, P, h0, hc, dtype, algo)}")
+
+
 def seg_chain(states, trans, local, B: int, P: int, h0: int, h_count: int, backward: bool):
     """camoe_wkv7_seg_chain on [B*P, H, 64, 64] fp32 tensors (see the header)."""
     for t, n in ((states, "states"), (trans, "trans"), (local, "local")):
@@ -100,12 +138,13 @@ def seg_chain(states, trans, local, B: int, P: int, h0: int, h_count: int, backw
 
 def wkv7_forward_segmented(r, w, k, v, a, b, segments: int, *, h0: int = 0,
                            h_count: int | None = None, s0=None, s_out=None, y=None, sa=None,
-                           algo="auto"):
+                           algo="auto", bufs: Buffers | None = None):
     """Training forward with every chain cut into ``segments`` pieces of equal
     length (T a multiple of 16 x segments).  ``s0`` ([B, H, 64, 64] fp32, None
     = zero) is the state the sequences start from and ``s_out`` receives their
-    final states.  Heads [h0, h0 + h_count) are processed, in place.  Returns
-    (y, sa, saved); ``saved`` feeds ``wkv7_backward_segmented``."""
+    final states.  Heads [h0, h0 + h_count) are processed, in place.  ``bufs``
+    (a ``Buffers`` of the same geometry) replaces every per-call allocation and
+    fill.  Returns (y, sa, saved); ``saved`` feeds ``wkv7_backward_segmented``."""
     _check_inputs((r, w, k, v, a, b), NAMES)
     B, T, H, N = r.shape
     P = int(segments)
@@ -126,53 +165,65 @@ def wkv7_forward_segmented(r, w, k, v, a, b, segments: int, *, h0: int = 0,
     xs = tuple(_view(x, P) for x in (r, w, k, v, a, b))
     yv, sav = _view(y, P), _view(sa, P)
     BP = B * P
-    starts, trans = _states(BP, H, dev), _states(BP, H, dev)
+    if bufs is not None:
+        bufs.check(B, T, H, P, h0, hc, r.dtype, algo)
+        starts, trans = bufs.starts, bufs.trans
+    else:
+        starts, trans = _states(BP, H, dev), _states(BP, H, dev)
     sv = starts.view(B, P, H, N, N)
     if s0 is not None:
         sv[:, 0, hs] = s0[:, hs]
+        if bufs is not None:
+            bufs.starts_dirty = True
+    elif bufs is not None and bufs.starts_dirty:
+        sv[:, 0, hs] = 0.0
+        bufs.starts_dirty = False
     fin = _states(BP, H, dev) if s_out is not None else None
     # the chunked path runs the key-side pass once, into the checkpoint, and
     # the value pass three times over it
     chunked = r.dtype == torch.bfloat16 and algo in ("auto", "chunked")
-    ckpt = None
+    ckpt = None if bufs is None else bufs.ckpt
     if P > 1:
         # 1. transitions (identity start, v = 0) and zero-start final states
-        local = _states(BP, H, dev)
-        eye = _states(BP, H, dev)
-        eye[:, hs] = torch.eye(N, device=dev)
-        vz = torch.empty_like(v)
-        vz[:, :, hs].zero_()
-        xz = (xs[0], xs[1], xs[2], _view(vz, P), xs[4], xs[5])
+        if bufs is not None:
+            local, eye, vzv = bufs.local, bufs.eye, bufs.vz
+        else:
+            local = _states(BP, H, dev)
+            eye = _states(BP, H, dev)
+            eye[:, hs] = torch.eye(N, device=dev)
+            vz = torch.empty_like(v)
+            vz[:, :, hs].zero_()
+            vzv = _view(vz, P)
+        xz = (xs[0], xs[1], xs[2], vzv, xs[4], xs[5])
         if chunked:
             _, _, ckpt = ops.wkv7_forward(*xz, algo=algo, h0=h0, h_count=hc, y=yv, sa=sav, s0=eye,
-                                          s_out=trans)
+                                          s_out=trans, ckpt=ckpt)
             ops.wkv7_forward_value(*xs, ckpt, h0=h0, h_count=hc, y=yv, sa=sav, s_out=local)
         else:
             ops.wkv7_forward_state(*xz, eye, algo=algo, h0=h0, h_count=hc, y=yv, sa=sav,
                                    out_state=trans)
             ops.wkv7_forward_state(*xs, None, algo=algo, h0=h0, h_count=hc, y=yv, sa=sav,
                                    out_state=local)
-        del vz, eye
         # 2. the start state of every segment
         seg_chain(starts, trans, local, B, P, h0, hc, backward=False)
-        del local
     # 3. the training forward of every segment from its start state
-    if ckpt is not None:
+    if chunked and P > 1:
         ops.wkv7_forward_value(*xs, ckpt, h0=h0, h_count=hc, y=yv, sa=sav, s0=starts, s_out=fin)
     else:
         _, _, ckpt = ops.wkv7_forward(*xs, algo=algo, h0=h0, h_count=hc, y=yv, sa=sav,
-                                      s0=starts, s_out=fin)
+                                      s0=starts, s_out=fin, ckpt=ckpt)
     if s_out is not None:
         s_out[:, hs] = fin.view(B, P, H, N, N)[:, P - 1, hs]
     saved = Saved(xs, (B, T, H, N), P, h0, hc, starts, trans, ckpt, algo)
     return y, sa, saved
 
 
-def wkv7_backward_segmented(saved: Saved, dy, dsa=None, *, ds_out=None, ds0=None, grads=None):
+def wkv7_backward_segmented(saved: Saved, dy, dsa=None, *, ds_out=None, ds0=None, grads=None,
+                            bufs: Buffers | None = None):
     """Backward of ``wkv7_forward_segmented``.  ``dsa`` (fp32) may be None;
     ``ds_out`` is the gradient of the final states (None = zero) and ``ds0``
-    ([B, H, 64, 64] fp32) receives the gradient of the start states.
-    Returns (dr, dw, dk, dv, da, db)."""
+    ([B, H, 64, 64] fp32) receives the gradient of the start states.  ``bufs``
+    as in the forward.  Returns (dr, dw, dk, dv, da, db)."""
     B, T, H, N = saved.shape
     P, h0, hc = saved.segments, saved.h0, saved.h_count
     hs = slice(h0, h0 + hc)
@@ -192,20 +243,28 @@ def wkv7_backward_segmented(saved: Saved, dy, dsa=None, *, ds_out=None, ds0=None
     dyv = _view(dy, P)
     dsav = None if dsa is None else _view(dsa, P)
     BP, Ts = B * P, T // P
-    wneed = ops.work_bytes(BP, Ts, hc, ref.dtype, saved.algo)
-    work = torch.empty(max(wneed, 16), dtype=torch.uint8, device=dev) if wneed > 0 else None
-    ends = _states(BP, H, dev)
+    if bufs is not None:
+        bufs.check(B, T, H, P, h0, hc, ref.dtype, saved.algo)
+        work, ends = bufs.work, bufs.ends
+    else:
+        wneed = ops.work_bytes(BP, Ts, hc, ref.dtype, saved.algo)
+        work = torch.empty(max(wneed, 16), dtype=torch.uint8, device=dev) if wneed > 0 else None
+        ends = _states(BP, H, dev)
     if ds_out is not None:
         ends.view(B, P, H, N, N)[:, P - 1, hs] = ds_out[:, hs]
+        if bufs is not None:
+            bufs.ends_dirty = True
+    elif bufs is not None and bufs.ends_dirty:
+        ends.view(B, P, H, N, N)[:, P - 1, hs] = 0.0
+        bufs.ends_dirty = False
     kw = dict(algo=saved.algo, h0=h0, h_count=hc, grads=gv, work=work, s0=saved.starts)
     if P > 1:
         # start-state gradients with no gradient at the segment ends (the value
         # pass alone on the chunked path), then the end gradients
-        local = _states(BP, H, dev)
+        local = bufs.local if bufs is not None else _states(BP, H, dev)
         chunked = ref.dtype == torch.bfloat16 and saved.algo in ("auto", "chunked")
         ops.wkv7_backward(*saved.xs, dyv, dsav, saved.ckpt, ds0=local, ds0_only=chunked, **kw)
         seg_chain(ends, saved.trans, local, B, P, h0, hc, backward=True)
-        del local
     first = _states(BP, H, dev) if ds0 is not None else None
     ops.wkv7_backward(*saved.xs, dyv, dsav, saved.ckpt, ds_out=ends, ds0=first, **kw)
     if ds0 is not None:

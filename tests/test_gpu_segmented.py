@@ -174,3 +174,36 @@ def test_autograd_function_equals_rwkv7_clampw():
     assert nrel(np_of(y1.detach()), np_of(y0.detach())) < TOL_BF16
     for n, a, b_ in zip(GRADS, leaves[1], leaves[0]):
         assert nrel(np_of(a.grad), np_of(b_.grad)) < TOL_BF16, n
+
+
+@pytest.mark.parametrize("dtype,algo", PATHS, ids=PATH_IDS)
+def test_preallocated_buffers_are_bit_identical_over_consecutive_steps(dtype, algo):
+    """segmented.Buffers (no allocation or fill inside a step) gives the
+    per-call allocations' results bit for bit, over consecutive steps that
+    alternate a start state / final-state gradient with none (the kept-zero
+    rows of the buffers must be restored)."""
+    B, T, H, P, h0, hc = 2, 256, 5, 4, 1, 3
+    inp = make_inputs(B, T, H, seed=71, with_dsa=True)
+    xs = [inp[n].to(dtype).cuda() for n in NAMES]
+    dy = inp["dy"].to(dtype).cuda()
+    dsa = inp["dsa"].cuda()
+    g = torch.Generator().manual_seed(72)
+    s0 = (0.3 * torch.randn(B, H, 64, 64, generator=g)).cuda()
+    dso = (0.3 * torch.randn(B, H, 64, 64, generator=g)).cuda()
+    bufs = segmented.Buffers(B, T, H, P, h0=h0, h_count=hc, device=xs[0].device, dtype=dtype,
+                             algo=algo)
+    for with_state in (True, False, True, False):
+        st = dict(s0=s0) if with_state else {}
+        ds = dict(ds_out=dso) if with_state else {}
+        outs = []
+        for b in (None, bufs):
+            y = torch.zeros_like(xs[0])
+            sa = torch.zeros(xs[0].shape, dtype=torch.float32, device="cuda")
+            grads = tuple(torch.zeros_like(xs[0]) for _ in range(6))
+            _, _, saved = segmented.wkv7_forward_segmented(*xs, P, h0=h0, h_count=hc, y=y, sa=sa,
+                                                           algo=algo, bufs=b, **st)
+            segmented.wkv7_backward_segmented(saved, dy, dsa, grads=grads, bufs=b, **ds)
+            outs.append((y, sa) + grads)
+        torch.cuda.synchronize()
+        for name, a, c in zip(("y", "sa") + GRADS, *outs):
+            assert torch.equal(a, c), (name, with_state)
