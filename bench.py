@@ -199,11 +199,11 @@ def count_launches(fn, dev) -> dict:
         return {"own": None, "source": f"unavailable: {type(e).__name__}: {e}"}
 
 
-def timed_blocks(step, K, dev, stream, world, local, min_blocks, min_total_s):
+def timed_blocks(step, K, dev, stream, world, local, min_blocks, min_total_s, phases=True):
     """Run blocks of exactly K steps, each bracketed by barrier + synchronize and
-    timed with CUDA events on `stream`.  `step(ev)` records ev[0..2] around its
-    forward and backward when ev is given.  Returns (block ms list (max over
-    ranks), mean fwd ms, mean bwd ms)."""
+    timed with CUDA events on `stream`.  With `phases`, `step(ev)` records
+    ev[0..2] around its forward and backward.  Returns (block ms list (max over
+    ranks), mean fwd ms, mean bwd ms; the last two None without phases)."""
     blocks, fwd, bwd = [], [], []
     t_start = time.perf_counter()
     while True:
@@ -214,19 +214,22 @@ def timed_blocks(step, K, dev, stream, world, local, min_blocks, min_total_s):
         torch.cuda.synchronize(dev)
         start.record(stream)
         for k in range(K):
-            step(evs[k])
+            step(evs[k] if phases else None)
         end.record(stream)
         torch.cuda.synchronize(dev)
         barrier(world, local)
         torch.cuda.synchronize(dev)
         blocks.append(start.elapsed_time(end))
-        fwd += [e[0].elapsed_time(e[1]) for e in evs]
-        bwd += [e[1].elapsed_time(e[2]) for e in evs]
+        if phases:
+            fwd += [e[0].elapsed_time(e[1]) for e in evs]
+            bwd += [e[1].elapsed_time(e[2]) for e in evs]
         # every rank takes the same decision: on the max over ranks of the elapsed time
         elapsed = max_over_ranks(time.perf_counter() - t_start, world, local)
         if len(blocks) >= min_blocks and elapsed >= min_total_s:
             break
     blocks = [max_over_ranks(b, world, local) for b in blocks]
+    if not phases:
+        return blocks, None, None
     return (blocks, max_over_ranks(statistics.fmean(fwd), world, local),
             max_over_ranks(statistics.fmean(bwd), world, local))
 
@@ -459,8 +462,8 @@ def run_long_share(args, wl, dev):
         for _ in range(args.warmup):
             step()
         launches = count_launches(step, dev)
-        blocks, _, _ = timed_blocks(lambda ev=None: step(), args.steps, dev, stream, 1, 0,
-                                    args.blocks, args.min_timed_s)
+        blocks, _, _ = timed_blocks(step, args.steps, dev, stream, 1, 0, args.blocks,
+                                    args.min_timed_s, phases=False)
         ms = statistics.median(blocks) / args.steps
         gbs = (FWD_BYTES + BWD_BYTES) * elems / (ms / 1e3) / 1e9
         print(json.dumps({
