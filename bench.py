@@ -63,7 +63,12 @@ NAMES = ("r", "w", "k", "v", "a", "b")
 # gradients.
 FWD_BYTES, BWD_BYTES = 6 * 2 + 2 + 4, 7 * 2 + 6 * 2
 FALLBACK_HBM_GBS = 6650.0
-OTHER_WORKLOADS = ("decode_b1024_h16", "timemix_b8_t1024_c1024")
+OTHER_WORKLOADS = ("decode_b1024_h16", "timemix_b8_t1024_c1024", "train_step_c4")
+# the op's calls in one train step of the 0.4B CaMoE configuration: 12 RWKV-7
+# layers at C=1024, B=8 sequences of T=1024; each layer's attention stage runs
+# under activation checkpointing (camoe/system.py:317-324), so the op runs a
+# forward, a recompute forward and a backward per layer
+C4 = dict(layers=12, B=8, T=1024, H=16, N=64)
 # kernels of this repository (their names all sit in the camoe namespace)
 OWN_KERNEL_TAG = "camoe::"
 
@@ -520,7 +525,8 @@ def run_op(args, wl, world, rank, local):
 
     for _ in range(args.warmup):
         step()
-    launches = count_launches(step, dev)
+    launches = {"own": 4 if args.algo != "scan" else 2, "source": "static (--no-trace)"} \
+        if args.no_trace else count_launches(step, dev)
     clocks = ClockSampler(local)
     blocks, fwd_ms, bwd_ms = timed_blocks(step, args.steps, dev, stream, world, local,
                                           args.blocks, args.min_timed_s)
@@ -742,6 +748,121 @@ def bench_prefill(B, T, H, reps):
     return out
 
 
+def op_share_c4(fwd, bwd, steps, warmup):
+    """Time `steps` train steps' worth of op calls (C4): per layer fwd(l) twice
+    (forward, recompute) then bwd(l), layers in order forward and reverse in
+    backward as autograd runs them.  CUDA events on the current stream."""
+    L = C4["layers"]
+
+    def step():
+        for l in range(L):
+            fwd(l)
+        for l in reversed(range(L)):
+            fwd(l)  # the activation-checkpoint recompute of layer l
+            bwd(l)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    tokens = C4["B"] * C4["T"]
+    return {"ms_per_step": ms, "tokens_per_s": tokens / (ms / 1e3)}
+
+
+def c4_inputs(dt, dev):
+    B, T, H, N = C4["B"], C4["T"], C4["H"], C4["N"]
+    layers = []
+    for l in range(C4["layers"]):
+        inp = make_inputs(B, T, H, N, seed=100 + l, dtype=dt)
+        layers.append(([inp[n].to(dev) for n in NAMES], inp["dy"].to(dev)))
+    return layers
+
+
+def run_train_step_c4(args):
+    """Our op on the call pattern of one 0.4B CaMoE train step (C4), bf16
+    through the chunked kernels and fp32 through the scan."""
+    dev = torch.device("cuda", 0)
+    B, T, H, N = C4["B"], C4["T"], C4["H"], C4["N"]
+    for dt in (torch.bfloat16, torch.float32):
+        layers = c4_inputs(dt, dev)
+        state = []
+        for xs, dy in layers:
+            y, sa, ck = ops.wkv7_forward(*xs)
+            g = ops.wkv7_backward(*xs, dy, sa, ck)
+            state.append((y, sa, ck, g))
+        work = torch.empty(max(ops.work_bytes(B, T, H, dt), 16), dtype=torch.uint8, device=dev)
+
+        def fwd(l):
+            xs, _ = layers[l]
+            y, sa, ck, _ = state[l]
+            ops.wkv7_forward(*xs, y=y, sa=sa, ckpt=ck)
+
+        def bwd(l):
+            xs, dy = layers[l]
+            _, sa, ck, g = state[l]
+            # the dsa the layer's ln_sa sends back is an input of the backward
+            ops.wkv7_backward(*xs, dy, sa, ck, grads=g, work=work)
+
+        r = op_share_c4(fwd, bwd, max(args.steps // 4, 3), 2)
+        print(json.dumps({
+            "workload": f"train_step_c4 op share: {C4['layers']} layers x (forward, recompute "
+                        f"forward, backward with dsa), B={B} T={T} H={H} N={N}, "
+                        f"{str(dt).split('.')[-1]} inputs",
+            "metric": "camoe_c4_op_tokens_per_s", "impl": "ours",
+            "algo": "chunked" if dt == torch.bfloat16 else "scan", **r}), flush=True)
+        del layers, state, work
+        torch.cuda.empty_cache()
+
+
+def reference_train_step_c4(args):
+    """The reference's own CUDA op (oracle/_ref) on the same call pattern (C4);
+    its backward takes no dsa (camoe/cuda/rwkv7_clampw.cpp:19-23)."""
+    import oracle
+
+    dev = torch.device("cuda", 0)
+    B, T, H, N = C4["B"], C4["T"], C4["H"], C4["N"]
+    for fp32 in (False, True):
+        dt = torch.float32 if fp32 else torch.bfloat16
+        if not oracle.RefOp.available(fp32=fp32):
+            print(json.dumps({"workload": "train_step_c4 op share", "impl": "reference",
+                              "unavailable": "oracle/_ref not built"}), flush=True)
+            continue
+        op = oracle.RefOp(fp32=fp32)
+        layers = c4_inputs(dt, dev)
+        state = []
+        for xs, _ in layers:
+            state.append((torch.empty_like(xs[0]),
+                          torch.empty(B, H, T // 16, N, N, dtype=torch.float32, device=dev),
+                          torch.empty(xs[0].shape, dtype=torch.float32, device=dev),
+                          [torch.empty_like(xs[0]) for _ in range(6)]))
+
+        def fwd(l):
+            y, s, sa, _ = state[l]
+            op.forward(*layers[l][0], y, s, sa)
+
+        def bwd(l):
+            y, s, sa, g = state[l]
+            op.backward(*layers[l][0], layers[l][1], s, sa, *g)
+
+        # it launches on the legacy default stream, which the events also use
+        r = op_share_c4(fwd, bwd, 2, 1)
+        print(json.dumps({
+            "workload": f"train_step_c4 op share: {C4['layers']} layers x (forward, recompute "
+                        f"forward, backward), B={B} T={T} H={H} N={N}, "
+                        f"{str(dt).split('.')[-1]} inputs",
+            "metric": "camoe_c4_op_tokens_per_s", "impl": "reference",
+            "source": "camoe/cuda/rwkv7_clampw.cu built from the reference's sources", **r}),
+            flush=True)
+        del layers, state
+        torch.cuda.empty_cache()
+
+
 def run_decode(args):
     for dt in (torch.bfloat16, torch.float32):
         print(json.dumps(bench_decode(1024, 16, dt, 50, 10)), flush=True)
@@ -926,6 +1047,8 @@ def main():
     ap.add_argument("--algo", default="auto", choices=["auto", "scan", "chunked"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-trace", action="store_true",
+                    help="skip the traced launch count (e.g. under ncu, which owns the counters)")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="--impl reference: skip timing the reference's CUDA op")
     ap.add_argument("--split", action="store_true",
@@ -940,7 +1063,11 @@ def main():
 
     if args.workload in OTHER_WORKLOADS:
         torch.cuda.set_device(0)
-        {"decode_b1024_h16": run_decode, "timemix_b8_t1024_c1024": run_timemix}[args.workload](args)
+        if args.workload == "train_step_c4" and args.impl == "reference":
+            reference_train_step_c4(args)
+            return
+        {"decode_b1024_h16": run_decode, "timemix_b8_t1024_c1024": run_timemix,
+         "train_step_c4": run_train_step_c4}[args.workload](args)
         return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":

@@ -22,7 +22,9 @@ EXPORTS = ("camoe_wkv7_version", "camoe_wkv7_strerror", "camoe_wkv7_last_cuda_er
            "camoe_wkv7_fwd", "camoe_wkv7_bwd", "camoe_wkv7_fwd_state",
            "camoe_wkv7_state_work_bytes", "camoe_wkv7_wind_fwd", "camoe_wkv7_wind_bwd",
            "camoe_wkv7_fwd_carry", "camoe_wkv7_bwd_carry", "camoe_wkv7_seg_chain",
-           "camoe_wkv7_fwd_value")
+           "camoe_wkv7_fwd_value", "camoe_wkv7_test_hooks")
+# the kernels' default wait limit (clock cycles), restored by tests that lower it
+DEFAULT_WAIT_LIMIT = 2000000000
 
 
 # include/camoe_timemix.h: fused elementwise kernels of the time mix
@@ -80,6 +82,8 @@ def lib() -> ctypes.CDLL:
         [ci, ci, ci, vp]
     l.camoe_wkv7_fwd_value.restype = ci
     l.camoe_wkv7_fwd_value.argtypes = [vp] * 11 + [sz] + [i64] * 5 + [ci, ci, vp]
+    l.camoe_wkv7_test_hooks.restype = ci
+    l.camoe_wkv7_test_hooks.argtypes = [ctypes.c_longlong, ci]
     l.camoe_wkv7_seg_chain.restype = ci
     l.camoe_wkv7_seg_chain.argtypes = [vp] * 3 + [i64] * 5 + [ci, vp]
     l.camoe_tm_work_bytes.argtypes = [i64] * 3

@@ -16,6 +16,8 @@ cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream);
 namespace chunked {
 unsigned int fwd_timeouts();
 unsigned int bwd_timeouts();
+cudaError_t fwd_test_hooks(long long wait_limit_cycles, int skip_pair);
+cudaError_t bwd_test_hooks(long long wait_limit_cycles);
 cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream);
 size_t ckpt_bytes(int64_t chains, int64_t T);
@@ -101,6 +103,15 @@ unsigned int camoe_wkv7_device_errors(void) {
   const unsigned int a = camoe::chunked::fwd_timeouts(), b = camoe::chunked::bwd_timeouts();
   if (a == ~0u || b == ~0u) return ~0u;
   return a + b;
+}
+
+int camoe_wkv7_test_hooks(long long wait_limit_cycles, int skip_pair) {
+  // at most the kernels' default limit (kWaitLimitCycles of wkv7_sync.cuh)
+  if (wait_limit_cycles < 1000 || wait_limit_cycles > 2000000000LL || skip_pair < -1)
+    return CAMOE_ERR_INVALID_ARG;
+  cudaError_t e = camoe::chunked::fwd_test_hooks(wait_limit_cycles, skip_pair);
+  if (e == cudaSuccess) e = camoe::chunked::bwd_test_hooks(wait_limit_cycles);
+  return cuda_status(e);
 }
 
 size_t camoe_wkv7_ckpt_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype, int algo) {

@@ -920,6 +920,11 @@ unsigned int bwd_timeouts() {
   return n;
 }
 
+// test hook: the wait limit of this file's kernels
+cudaError_t bwd_test_hooks(long long wait_limit_cycles) {
+  return cudaMemcpyToSymbol(g_wkv7_wait_limit, &wait_limit_cycles, sizeof(long long));
+}
+
 size_t ckpt_bytes(int64_t chains, int64_t T) {
   return rec::ckpt_bytes(chains, (T + kChunk - 1) / kChunk);
 }

@@ -438,6 +438,11 @@ struct Params {
   FwdArgs a;
 };
 
+// Test hook (camoe_wkv7_test_hooks): the producer never issues the loads of
+// this chunk pair, so every role's next wait runs out and the kernel returns
+// with the timeouts counted.  -1 (the default) withholds nothing.
+static __device__ int g_test_skip_pair = -1;
+
 __device__ __forceinline__ uint32_t par(int idx, int n) { return static_cast<uint32_t>((idx / n) & 1); }
 
 template <int RB>
@@ -475,6 +480,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
     // ------------------------------ producer ------------------------------
     if (lane != 0) return;
     constexpr int NB = NS / 2;
+    const int skip = *static_cast<volatile int*>(&g_test_skip_pair);
     int pc = 0;
     bool ok = true;
     for (; 2 * pc < nchunk && ok; ++pc) {
@@ -484,6 +490,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
         if (c >= NS) ok = mbar_wait(&sm.empty[c % NS], par(c - NS, NS));
       }
       if (!ok) break;
+      if (pc == skip) continue;  // test hook: this pair never arrives
       uint64_t* bar = &sm.fullp[pc % NB];
       mbar_arrive_expect_tx(bar, n * (sizeof(rec::KeyRec) + tma::kTileBytes));
       for (int k = 0; k < n; ++k) {
@@ -492,7 +499,11 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
         tma::load_tile(sm.slot[s].v, &P.map_v, hh, c * L, bb, bar);
       }
     }
-    if (!ok)  // stopped on a timeout: let the copies in flight land
+    // stopped on a timeout, or a pair withheld (the consumers then stop early):
+    // let the copies in flight land.  Pairs older than the last NB were
+    // consumed before their slots were refilled; the withheld pair's wait runs
+    // out (bounded) since nothing arrives on it.
+    if (!ok || skip >= 0)
       for (int pp = pc > NB ? pc - NB : 0; pp < pc; ++pp) mbar_wait(&sm.fullp[pp % NB], par(pp, NB));
     return;
   }
@@ -660,6 +671,14 @@ unsigned int fwd_timeouts() {
   unsigned int n = 0;
   if (cudaMemcpyFromSymbol(&n, g_wkv7_timeouts, sizeof(n)) != cudaSuccess) return ~0u;
   return n;
+}
+
+// test hook: the wait limit of this file's kernels, and the chunk pair whose
+// loads value_fwd_kernel's producer withholds (-1: none)
+cudaError_t fwd_test_hooks(long long wait_limit_cycles, int skip_pair) {
+  cudaError_t e = cudaMemcpyToSymbol(g_wkv7_wait_limit, &wait_limit_cycles, sizeof(long long));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(vf::g_test_skip_pair, &skip_pair, sizeof(int));
+  return e;
 }
 
 cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {

@@ -1,8 +1,8 @@
 // mbarrier, named-barrier and bulk-copy helpers with bounded waits.
 //
 // Every wait on an mbarrier gives up after kWaitLimitCycles (about a second
-// at 1.9 GHz), counts the event in g_wkv7_timeouts and reports failure, so a
-// logic error can never leave a GPU spinning.  Callers stop their loops on a
+// at 1.9 GHz; g_wkv7_wait_limit), counts the event in g_wkv7_timeouts and
+// reports failure, so a logic error can never leave a GPU spinning.  Callers stop their loops on a
 // failed wait.  The counter is per translation unit (static); each kernel
 // file exposes a host reader, summed by camoe_wkv7_device_errors().
 #pragma once
@@ -14,6 +14,11 @@ namespace camoe {
 static __device__ unsigned int g_wkv7_timeouts = 0;
 
 constexpr long long kWaitLimitCycles = 2000000000LL;
+// The limit in force (per translation unit, like the counter).  Only the
+// test hook camoe_wkv7_test_hooks lowers it, to make a withheld arrival time
+// out within milliseconds; it is read only once a wait has already failed its
+// first try, so the fast path does not load it.
+static __device__ long long g_wkv7_wait_limit = kWaitLimitCycles;
 
 __device__ __forceinline__ uint32_t sm_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -67,9 +72,10 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
+  const long long limit = *static_cast<volatile long long*>(&g_wkv7_wait_limit);
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       atomicAdd(&g_wkv7_timeouts, 1u);
       return false;
     }

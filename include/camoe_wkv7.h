@@ -224,6 +224,18 @@ int camoe_wkv7_fwd_state(const void* r, const void* w, const void* k, const void
 size_t camoe_wkv7_state_work_bytes(int64_t B, int64_t T, int64_t h_count, int N, int dtype,
                                    int algo);
 
+/* Test hook for the bounded device waits; no counterpart in the reference.
+ * Every wait of the chunked kernels on a pipeline barrier gives up after a
+ * limit (by default 2e9 clock cycles, about a second), counts the event in
+ * camoe_wkv7_device_errors() and makes the kernel's roles return.  This call
+ * sets that limit (1000 .. 2e9 cycles) for later launches on the current
+ * device, and with skip_pair >= 0 makes the forward's value pass withhold
+ * the loads of that pair of 16-step chunks, so that its waits run out: a test
+ * that failure detection returns instead of hanging.  skip_pair = -1 with
+ * the default limit restores normal operation.  Returns CAMOE_ERR_INVALID_ARG
+ * for a limit or pair outside those ranges.  Not for production use. */
+int camoe_wkv7_test_hooks(long long wait_limit_cycles, int skip_pair);
+
 /* Size of the library-owned checkpoint scratch used by
  * camoe_wkv7_fwd_bwd_noalloc (64 MiB per GPU that loads the library). */
 #define CAMOE_WKV7_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)

@@ -243,3 +243,11 @@ def test_error_raises_camoe_error():
     with pytest.raises(_lib.CamoeError) as ei:
         _lib.check(_lib.ERR_ALIGNMENT)
     assert ei.value.status == _lib.ERR_ALIGNMENT
+
+
+def test_test_hooks_reject_out_of_range_arguments():
+    """The wait-limit hook validates before touching any device state."""
+    lib = _lib.lib()
+    assert lib.camoe_wkv7_test_hooks(999, -1) == _lib.ERR_INVALID_ARG
+    assert lib.camoe_wkv7_test_hooks(_lib.DEFAULT_WAIT_LIMIT + 1, -1) == _lib.ERR_INVALID_ARG
+    assert lib.camoe_wkv7_test_hooks(_lib.DEFAULT_WAIT_LIMIT, -2) == _lib.ERR_INVALID_ARG
