@@ -528,7 +528,7 @@ struct alignas(1024) KGroup {
   rec::XRec x;
   Tile dQyb, dW2b;
   Tile At, Rt, Bb, Kb;
-  float lam[kN], cum[L][kN], lw[L][kN];
+  float lam[kN], cum[L][ks::LDF], lw[L][ks::LDF];
   float dllp[4][kN], dll[kN];
   bf16 dPb[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
   Tile W;

@@ -22,6 +22,11 @@ constexpr int LDS = 24;    // padded row stride of 16 x 16 bf16 tiles
 
 using Tile = bf16[L][LD];
 using Tile16 = bf16[L][LDS];
+// row stride of the fp32 16 x 64 prefix and log-decay tiles the backward keeps:
+// 72 floats put the rows t, t + 1, t + 2, t + 3 read by one half-warp's float2
+// loads (rows of 8 threads apart, columns 2q) on distinct banks (64 would map
+// every row to the same banks)
+constexpr int LDF = kN + 8;
 
 // Phase 1 (SIMT): per column pair (2p, 2p+1) and time quarter tq, the
 // log-decays lw = log_decay(w_in, kind), their inclusive prefix cum inside
@@ -43,8 +48,8 @@ __device__ __forceinline__ int raw_idx(int u, int j) {
 template <bool SWZ, typename LAR, typename LKB>
 __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf16* kk,
                                        const bf16* aa, const bf16* bb, bf16* At, bf16* Rt, LAR lar,
-                                       bf16* Kb, bf16* Bb, LKB lkb, float* lam, float (*cum_out)[kN],
-                                       float (*lw_out)[kN], int gtid, int kind, int nvalid = L) {
+                                       bf16* Kb, bf16* Bb, LKB lkb, float* lam, float (*cum_out)[LDF],
+                                       float (*lw_out)[LDF], int gtid, int kind, int nvalid = L) {
   const int p = gtid >> 2, tq = gtid & 3, j = 2 * p;
   const int lane = gtid & 31;
   float lw0[4], lw1[4], c0[4], c1[4];

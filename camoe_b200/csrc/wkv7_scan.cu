@@ -10,16 +10,22 @@
 // (decay w = exp(log_decay(w_in)) computed there, ClampW or wind).  The state at the
 // start of every chunk is the checkpoint, stored row-major in fp32.
 //
-// Backward (scan_bwd_kernel): one CTA of 256 threads per chain (row i =
-// tid/4, column quarter q = tid%4), walking chunks in reverse.  Each chunk's
-// states are recomputed forward from its checkpoint into shared memory (two
-// halves of 8 steps so 9 states fit), never reversed through 1/w as
-// camoe/cuda/rwkv7_clampw.cu:133 does.  Per step the row sums (dsa = dS b,
-// dv = dS k) use shuffles; the five column sums over the 64 rows (dr, dw, dk,
-// db, da) use a shuffle reduce-scatter over the 8 rows of a warp and a
-// shared-memory pass over the 8 warps.  The per-element formulas are those
-// of camoe/cuda/rwkv7_clampw.cu:123-168, plus the external sa-gradient.
+// Backward (scan_bwd_kernel): one cluster of two 128-thread CTAs per chain,
+// each owning 32 rows of dS (row i = 32 rank + tid/4, column quarter q =
+// tid%4), walking chunks in reverse.  Each chunk's states are recomputed
+// forward from its checkpoint into shared memory (two halves of 8 steps so 9
+// states fit), never reversed through 1/w as camoe/cuda/rwkv7_clampw.cu:133
+// does.  Per step the row sums (dsa = dS b, dv = dS k) use shuffles; the five
+// column sums over the rows (dr, dw, dk, db, da) use a shuffle reduce-scatter
+// over the 8 rows of a warp and a shared-memory pass over the 4 warps, and the
+// two CTAs' sums are added once per chunk through distributed shared memory.
+// The per-element formulas are those of camoe/cuda/rwkv7_clampw.cu:123-168,
+// plus the external sa-gradient.
+#include <cooperative_groups.h>
+
 #include "wkv7_common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace camoe {
 namespace scan {
@@ -27,7 +33,6 @@ namespace scan {
 constexpr int kRows = 16;                 // forward: state rows per CTA
 constexpr int kFwdThreads = kRows * 4;    // forward: 4 threads per row
 constexpr int kRowGroups = kN / kRows;    // forward: CTAs per chain
-constexpr int kBwdThreads = kN * 4;       // backward: whole chain per CTA
 constexpr int kHalf = kChunk / 2;         // backward: states held per half chunk
 
 template <typename Tin>
@@ -331,22 +336,48 @@ __global__ void __launch_bounds__(kStepThreads, 8) step_fwd_kernel(FwdArgs p) {
 
 // ---------------------------------------------------------------------------
 // backward
+//
+// A chain's 64 rows of dS are independent recurrences (row i of the update
+// dS <- dS (diag w + a b^T)^T + dy r^T only reads row i), so each chain is a
+// cluster of two CTAs of 32 rows: 128 CTAs for the 64 chains of a 4-sequence
+// shard instead of 64.  Every per-step output indexed by the key column j (dr,
+// dw, dk, db, da) is a sum over all 64 rows: each CTA forms the sum over its
+// own 32 rows per step (warp shuffles, then shared memory over its 4 warps)
+// into a partial-sum buffer, and once per chunk, after a cluster barrier, each
+// CTA adds its peer's partials for its half of the columns (read through
+// distributed shared memory) and writes the outputs.  The partial buffers are
+// double-buffered by chunk parity, so one cluster barrier per chunk keeps a
+// buffer from being refilled while the peer still reads it.  dv (a sum over
+// j, within a row) needs no exchange.
 
+// ROWS = 32: a cluster of two CTAs per chain; ROWS = 64: one CTA per chain
+// (taken when two CTAs per chain would not fit the SMs in one wave).
+template <int ROWS>
+struct BwdCfg {
+  static constexpr int kCtas = kN / ROWS;        // CTAs per chain (one cluster)
+  static constexpr int kThreads = ROWS * 4;      // 4 threads per row
+  static constexpr int kWarps = kThreads / 32;
+  static constexpr int kParts = kCtas > 1 ? 2 : 1;  // partial-sum buffers (by chunk parity)
+};
+
+template <int ROWS>
 struct BwdSmem {
-  float S[kHalf + 1][kN][kN];  // states of one half chunk, columns xor-swizzled by row
-  float r[kChunk][kN], w[kChunk][kN], dlw[kChunk][kN], k[kChunk][kN], a[kChunk][kN],
-      b[kChunk][kN], v[kChunk][kN], dy[kChunk][kN], dsa[kChunk][kN];
-  float sa[kChunk][kN];
-  float red[kBwdThreads / 32][320];  // per-warp partial column sums
-  float out[6][kChunk][kN];          // dr, dw, dk, db, da, dv of the chunk
+  float S[kHalf + 1][ROWS][kN];  // own rows' states of one half chunk, columns xor-swizzled by row
+  float r[kChunk][kN], w[kChunk][kN], dlw[kChunk][kN], k[kChunk][kN], a[kChunk][kN], b[kChunk][kN];
+  float v[kChunk][ROWS], dy[kChunk][ROWS], dsa[kChunk][ROWS], sa[kChunk][ROWS];
+  float red[BwdCfg<ROWS>::kWarps][320];           // per-warp partial column sums of one step
+  float part[BwdCfg<ROWS>::kParts][5][kChunk][kN];  // own rows' column sums (dr, dw, dk, db, da)
+  float dv[kChunk][ROWS];                          // dv of the own rows
 };
 
 // physical column of element (i, j) in BwdSmem::S (keeps 4-column groups contiguous)
 __device__ __forceinline__ int swz(int i, int j) { return j ^ ((i & 7) << 2); }
 
-template <typename Tin>
-struct Prefetch {  // one thread's share (4 consecutive columns of one step) of a chunk
-  float4 x[8];     // r, w, k, v, a, b, dy, dsa
+template <typename Tin, int ROWS>
+struct Prefetch {  // one thread's share of a chunk's inputs
+  static constexpr int kC = 256 / (4 * ROWS);  // column slots per thread (16 steps x 16 groups)
+  float4 c[5][kC];   // r, w, k, a, b: steps u + (ROWS / 4) h, columns 4 jq .. 4 jq + 3
+  float4 o[3];       // v, dy, dsa: step u2, own rows 4 iq .. 4 iq + 3
 };
 
 template <typename Tin>
@@ -363,47 +394,59 @@ __device__ __forceinline__ float4 load4(const void* base, int64_t off, bool ok) 
   }
 }
 
-template <typename Tin>
-__device__ __forceinline__ void bwd_prefetch(Prefetch<Tin>& pf, const BwdArgs& p, int64_t ch,
-                                             int64_t c) {
-  const int u = threadIdx.x >> 4, j = (threadIdx.x & 15) * 4;
-  const int64_t t = c * kChunk + u;
-  const bool ok = t < p.g.T;
-  const int64_t o = ok ? p.g.off(ch, t, j) : 0;
-  pf.x[0] = load4<Tin>(p.r, o, ok);
-  pf.x[1] = load4<Tin>(p.w, o, ok);
-  pf.x[2] = load4<Tin>(p.k, o, ok);
-  pf.x[3] = load4<Tin>(p.v, o, ok);
-  pf.x[4] = load4<Tin>(p.a, o, ok);
-  pf.x[5] = load4<Tin>(p.b, o, ok);
-  pf.x[6] = load4<Tin>(p.dy, o, ok);
-  pf.x[7] = (p.dsa != nullptr) ? load4<float>(p.dsa, o, ok) : make_float4(0.f, 0.f, 0.f, 0.f);
-}
-
-template <typename Tin>
-__device__ __forceinline__ void bwd_stage(BwdSmem& sm, const Prefetch<Tin>& pf, int kind) {
-  const int u = threadIdx.x >> 4, j = (threadIdx.x & 15) * 4;
-  *reinterpret_cast<float4*>(&sm.r[u][j]) = pf.x[0];
-  const float wi[4] = {pf.x[1].x, pf.x[1].y, pf.x[1].z, pf.x[1].w};
-  float dl[4], wd[4];
+template <typename Tin, int ROWS>
+__device__ __forceinline__ void bwd_prefetch(Prefetch<Tin, ROWS>& pf, const BwdArgs& p, int64_t ch,
+                                             int64_t c, int row0) {
+  const int tid = threadIdx.x;
+  const void* src[5] = {p.r, p.w, p.k, p.a, p.b};
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float lw = log_decay(wi[e], kind);
-    dl[e] = dlog_decay(lw, kind);
-    wd[e] = expf(lw);
+  for (int h = 0; h < Prefetch<Tin, ROWS>::kC; ++h) {
+    const int u = (tid >> 4) + (ROWS / 4) * h, j = (tid & 15) * 4;
+    const int64_t t = c * kChunk + u;
+    const bool ok = t < p.g.T;
+    const int64_t o = ok ? p.g.off(ch, t, j) : 0;
+#pragma unroll
+    for (int n = 0; n < 5; ++n) pf.c[n][h] = load4<Tin>(src[n], o, ok);
   }
-  *reinterpret_cast<float4*>(&sm.dlw[u][j]) = make_float4(dl[0], dl[1], dl[2], dl[3]);
-  *reinterpret_cast<float4*>(&sm.w[u][j]) = make_float4(wd[0], wd[1], wd[2], wd[3]);
-  *reinterpret_cast<float4*>(&sm.k[u][j]) = pf.x[2];
-  *reinterpret_cast<float4*>(&sm.v[u][j]) = pf.x[3];
-  *reinterpret_cast<float4*>(&sm.a[u][j]) = pf.x[4];
-  *reinterpret_cast<float4*>(&sm.b[u][j]) = pf.x[5];
-  *reinterpret_cast<float4*>(&sm.dy[u][j]) = pf.x[6];
-  *reinterpret_cast<float4*>(&sm.dsa[u][j]) = pf.x[7];
+  const int u2 = tid / (ROWS / 4), i4 = row0 + (tid % (ROWS / 4)) * 4;
+  const int64_t t2 = c * kChunk + u2;
+  const bool ok2 = t2 < p.g.T;
+  const int64_t o2 = ok2 ? p.g.off(ch, t2, i4) : 0;
+  pf.o[0] = load4<Tin>(p.v, o2, ok2);
+  pf.o[1] = load4<Tin>(p.dy, o2, ok2);
+  pf.o[2] = (p.dsa != nullptr) ? load4<float>(p.dsa, o2, ok2) : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-// one forward step of row i (columns q*16..q*16+15); returns sa_i
-__device__ __forceinline__ float fwd_step(const BwdSmem& sm, int u, int i, int q, float* S) {
+template <typename Tin, int ROWS>
+__device__ __forceinline__ void bwd_stage(BwdSmem<ROWS>& sm, const Prefetch<Tin, ROWS>& pf, int kind) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int h = 0; h < Prefetch<Tin, ROWS>::kC; ++h) {
+    const int u = (tid >> 4) + (ROWS / 4) * h, j = (tid & 15) * 4;
+    *reinterpret_cast<float4*>(&sm.r[u][j]) = pf.c[0][h];
+    const float wi[4] = {pf.c[1][h].x, pf.c[1][h].y, pf.c[1][h].z, pf.c[1][h].w};
+    float dl[4], wd[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lw = log_decay(wi[e], kind);
+      dl[e] = dlog_decay(lw, kind);
+      wd[e] = expf(lw);
+    }
+    *reinterpret_cast<float4*>(&sm.dlw[u][j]) = make_float4(dl[0], dl[1], dl[2], dl[3]);
+    *reinterpret_cast<float4*>(&sm.w[u][j]) = make_float4(wd[0], wd[1], wd[2], wd[3]);
+    *reinterpret_cast<float4*>(&sm.k[u][j]) = pf.c[2][h];
+    *reinterpret_cast<float4*>(&sm.a[u][j]) = pf.c[3][h];
+    *reinterpret_cast<float4*>(&sm.b[u][j]) = pf.c[4][h];
+  }
+  const int u2 = tid / (ROWS / 4), il4 = (tid % (ROWS / 4)) * 4;
+  *reinterpret_cast<float4*>(&sm.v[u2][il4]) = pf.o[0];
+  *reinterpret_cast<float4*>(&sm.dy[u2][il4]) = pf.o[1];
+  *reinterpret_cast<float4*>(&sm.dsa[u2][il4]) = pf.o[2];
+}
+
+// one forward step of own row il (columns q*16..q*16+15); returns sa of the row
+template <int ROWS>
+__device__ __forceinline__ float fwd_step(const BwdSmem<ROWS>& sm, int u, int il, int q, float* S) {
   const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * 16]);
   float s0 = 0.f, s1 = 0.f;
 #pragma unroll
@@ -415,7 +458,7 @@ __device__ __forceinline__ float fwd_step(const BwdSmem& sm, int u, int i, int q
   float sa = s0 + s1;
   sa += __shfl_xor_sync(0xffffffffu, sa, 1);
   sa += __shfl_xor_sync(0xffffffffu, sa, 2);
-  const float vi = sm.v[u][i];
+  const float vi = sm.v[u][il];
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
     const float4 wv = reinterpret_cast<const float4*>(&sm.w[u][q * 16])[m];
@@ -429,28 +472,32 @@ __device__ __forceinline__ float fwd_step(const BwdSmem& sm, int u, int i, int q
   return sa;
 }
 
-__device__ __forceinline__ void store_state(BwdSmem& sm, int slot, int i, int q, const float* S) {
+template <int ROWS>
+__device__ __forceinline__ void store_state(BwdSmem<ROWS>& sm, int slot, int il, int q, const float* S) {
 #pragma unroll
   for (int m = 0; m < 4; ++m)
-    *reinterpret_cast<float4*>(&sm.S[slot][i][swz(i, q * 16 + 4 * m)]) =
+    *reinterpret_cast<float4*>(&sm.S[slot][il][swz(il, q * 16 + 4 * m)]) =
         make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
 }
 
-__device__ __forceinline__ void load_state(const BwdSmem& sm, int slot, int i, int q, float* S) {
+template <int ROWS>
+__device__ __forceinline__ void load_state(const BwdSmem<ROWS>& sm, int slot, int il, int q, float* S) {
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
-    const float4 x = *reinterpret_cast<const float4*>(&sm.S[slot][i][swz(i, q * 16 + 4 * m)]);
+    const float4 x = *reinterpret_cast<const float4*>(&sm.S[slot][il][swz(il, q * 16 + 4 * m)]);
     S[4 * m] = x.x; S[4 * m + 1] = x.y; S[4 * m + 2] = x.z; S[4 * m + 3] = x.w;
   }
 }
 
-// one reverse step u with S_t in slot st and S_{t-1} in slot sp
-__device__ __forceinline__ void bwd_step(BwdSmem& sm, int u, int st, int sp, int i, int q,
-                                         int lane, int warp, float* dS) {
+// one reverse step u of own row il, with S_t in slot st and S_{t-1} in slot sp;
+// the own rows' column sums go to part[pb]
+template <int ROWS>
+__device__ __forceinline__ void bwd_step(BwdSmem<ROWS>& sm, int u, int st, int sp, int il, int q,
+                                         int lane, int warp, int pb, float* dS) {
   float Sc[16], Sp[16];
-  load_state(sm, st, i, q, Sc);
-  load_state(sm, sp, i, q, Sp);
-  const float dyi = sm.dy[u][i], vi = sm.v[u][i], sai = sm.sa[u][i];
+  load_state(sm, st, il, q, Sc);
+  load_state(sm, sp, il, q, Sp);
+  const float dyi = sm.dy[u][il], vi = sm.v[u][il], sai = sm.sa[u][il];
   float dsa0 = 0.f, dsa1 = 0.f, dv0 = 0.f, dv1 = 0.f;
 #pragma unroll
   for (int jj = 0; jj < 16; ++jj) {
@@ -464,23 +511,23 @@ __device__ __forceinline__ void bwd_step(BwdSmem& sm, int u, int st, int sp, int
   dv += __shfl_xor_sync(0xffffffffu, dv, 1);
   dsa += __shfl_xor_sync(0xffffffffu, dsa, 2);
   dv += __shfl_xor_sync(0xffffffffu, dv, 2);
-  dsa += sm.dsa[u][i];
+  dsa += sm.dsa[u][il];
 
   float x[80];
 #pragma unroll
   for (int jj = 0; jj < 16; ++jj) {
-    x[jj] = Sc[jj] * dyi;       // dr
-    x[16 + jj] = dS[jj] * Sp[jj];  // dw (before the sigmoid chain factor)
-    x[32 + jj] = dS[jj] * vi;   // dk
-    x[48 + jj] = dS[jj] * sai;  // db
-    x[64 + jj] = dsa * Sp[jj];  // da
+    x[jj] = Sc[jj] * dyi;          // dr
+    x[16 + jj] = dS[jj] * Sp[jj];  // dw (before the decay's chain factor)
+    x[32 + jj] = dS[jj] * vi;      // dk
+    x[48 + jj] = dS[jj] * sai;     // db
+    x[64 + jj] = dsa * Sp[jj];     // da
   }
 #pragma unroll
   for (int jj = 0; jj < 16; ++jj) {
     const int j = q * 16 + jj;
     dS[jj] = dS[jj] * sm.w[u][j] + dsa * sm.a[u][j];
   }
-  if (q == 0) sm.out[5][u][i] = dv;
+  if (q == 0) sm.dv[u][il] = dv;
 
   // reduce-scatter the 80 partials over the 8 rows of this warp (lane bits 4,3,2)
   const bool h4 = lane & 16, h3 = lane & 8, h2 = lane & 4;
@@ -505,26 +552,32 @@ __device__ __forceinline__ void bwd_step(BwdSmem& sm, int u, int st, int sp, int
 #pragma unroll
   for (int s = 0; s < 10; ++s) sm.red[warp][lane * 10 + s] = x[s];
   __syncthreads();
-  for (int pidx = threadIdx.x; pidx < 320; pidx += kBwdThreads) {
+  for (int pidx = threadIdx.x; pidx < 320; pidx += BwdCfg<ROWS>::kThreads) {
     float acc = 0.f;
 #pragma unroll
-    for (int wv = 0; wv < kBwdThreads / 32; ++wv) acc += sm.red[wv][pidx];
+    for (int wv = 0; wv < BwdCfg<ROWS>::kWarps; ++wv) acc += sm.red[wv][pidx];
     const int ln = pidx / 10, s = pidx % 10, qq = ln & 3, rb = ln >> 2;
     const int m = 40 * ((rb >> 2) & 1) + 20 * ((rb >> 1) & 1) + 10 * (rb & 1) + s;
-    const int quant = m >> 4, j = qq * 16 + (m & 15);
-    if (quant == 1) acc = acc * sm.w[u][j] * sm.dlw[u][j];  // dw_in = dL/dw * w * dlw/dw_in
-    sm.out[quant][u][j] = acc;
+    sm.part[pb][m >> 4][u][qq * 16 + (m & 15)] = acc;
   }
   __syncthreads();
 }
 
-template <typename Tin>
-__global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdArgs p) {
+template <typename Tin, int ROWS>
+__global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
+    __launch_bounds__(BwdCfg<ROWS>::kThreads, 1) scan_bwd_kernel(BwdArgs p) {
+  using Cfg = BwdCfg<ROWS>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  BwdSmem& sm = *reinterpret_cast<BwdSmem*>(smem_raw);
-  const int tid = threadIdx.x, i = tid >> 2, q = tid & 3, lane = tid & 31, warp = tid >> 5;
-  const int64_t ch = blockIdx.x;
+  BwdSmem<ROWS>& sm = *reinterpret_cast<BwdSmem<ROWS>*>(smem_raw);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int tid = threadIdx.x, il = tid >> 2, q = tid & 3, lane = tid & 31, warp = tid >> 5;
+  // this CTA's rows, and the columns whose outputs it writes
+  const int rank = Cfg::kCtas > 1 ? static_cast<int>(cluster.block_rank()) : 0;
+  const int64_t ch = blockIdx.x / Cfg::kCtas;
+  const int row0 = rank * ROWS, i = row0 + il;
   const int64_t nchunk = p.g.nchunk;
+  // the peer's partial sums, in its shared memory (a cluster of two)
+  const BwdSmem<ROWS>* peer = Cfg::kCtas > 1 ? cluster.map_shared_rank(&sm, rank ^ 1) : nullptr;
 
   float dS[16], S0[16], S[16];
   if (p.dsT != nullptr) {  // the gradient of the final state enters at the last step
@@ -539,12 +592,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdArgs p) {
     for (int jj = 0; jj < 16; ++jj) dS[jj] = 0.f;
   }
 
-  Prefetch<Tin> pf;
-  if (nchunk > 0) bwd_prefetch<Tin>(pf, p, ch, nchunk - 1);
+  Prefetch<Tin, ROWS> pf;
+  if (nchunk > 0) bwd_prefetch<Tin, ROWS>(pf, p, ch, nchunk - 1, row0);
   for (int64_t c = nchunk - 1; c >= 0; --c) {
+    const int pb = Cfg::kParts > 1 ? static_cast<int>(c & 1) : 0;
     __syncthreads();
-    bwd_stage<Tin>(sm, pf, p.g.decay);
-    if (c > 0) bwd_prefetch<Tin>(pf, p, ch, c - 1);
+    bwd_stage<Tin, ROWS>(sm, pf, p.g.decay);
+    if (c > 0) bwd_prefetch<Tin, ROWS>(pf, p, ch, c - 1, row0);
     if (c > 0) {
       const float4* src = reinterpret_cast<const float4*>(p.ckpt + ((ch * nchunk + c) * kN + i) * kN + q * 16);
 #pragma unroll
@@ -570,46 +624,66 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdArgs p) {
     for (int jj = 0; jj < 16; ++jj) S[jj] = S0[jj];
 #pragma unroll 1
     for (int u = 0; u < kHalf; ++u) {
-      const float sa = fwd_step(sm, u, i, q, S);
-      if (q == 0) sm.sa[u][i] = sa;
+      const float sa = fwd_step(sm, u, il, q, S);
+      if (q == 0) sm.sa[u][il] = sa;
     }
-    store_state(sm, 0, i, q, S);
+    store_state(sm, 0, il, q, S);
 #pragma unroll 1
     for (int u = kHalf; u < kChunk; ++u) {
-      const float sa = fwd_step(sm, u, i, q, S);
-      if (q == 0) sm.sa[u][i] = sa;
-      store_state(sm, u - kHalf + 1, i, q, S);
+      const float sa = fwd_step(sm, u, il, q, S);
+      if (q == 0) sm.sa[u][il] = sa;
+      store_state(sm, u - kHalf + 1, il, q, S);
     }
     __syncthreads();
 #pragma unroll 1
-    for (int u = kChunk - 1; u >= kHalf; --u) bwd_step(sm, u, u - kHalf + 1, u - kHalf, i, q, lane, warp, dS);
+    for (int u = kChunk - 1; u >= kHalf; --u)
+      bwd_step(sm, u, u - kHalf + 1, u - kHalf, il, q, lane, warp, pb, dS);
 
     // first half
 #pragma unroll
     for (int jj = 0; jj < 16; ++jj) S[jj] = S0[jj];
-    store_state(sm, 0, i, q, S);
+    store_state(sm, 0, il, q, S);
 #pragma unroll 1
     for (int u = 0; u < kHalf; ++u) {
-      fwd_step(sm, u, i, q, S);
-      store_state(sm, u + 1, i, q, S);
+      fwd_step(sm, u, il, q, S);
+      store_state(sm, u + 1, il, q, S);
     }
     __syncthreads();
 #pragma unroll 1
-    for (int u = kHalf - 1; u >= 0; --u) bwd_step(sm, u, u + 1, u, i, q, lane, warp, dS);
+    for (int u = kHalf - 1; u >= 0; --u) bwd_step(sm, u, u + 1, u, il, q, lane, warp, pb, dS);
 
-    // write the chunk's gradients: thread -> (tensor, step, 4 columns)
-    for (int idx = tid; idx < 6 * kChunk * (kN / 4); idx += kBwdThreads) {
-      const int tens = idx / (kChunk * (kN / 4)), rem = idx % (kChunk * (kN / 4));
-      const int u = rem / (kN / 4), j = (rem % (kN / 4)) * 4;
+    // both CTAs' column sums of this chunk are complete (and visible across the
+    // cluster); with one CTA per chain the block barrier of the last step suffices
+    if (Cfg::kCtas > 1) cluster.sync();
+    // this CTA writes the columns [ROWS rank, ROWS rank + ROWS): thread -> (tensor, step, 4 columns)
+    for (int idx = tid; idx < 5 * kChunk * (ROWS / 4); idx += Cfg::kThreads) {
+      const int tens = idx / (kChunk * (ROWS / 4)), rem = idx % (kChunk * (ROWS / 4));
+      const int u = rem / (ROWS / 4), j = row0 + (rem % (ROWS / 4)) * 4;
       const int64_t t = c * kChunk + u;
       if (t >= p.g.T) continue;
-      // out[] order: dr, dw, dk, db, da, dv
-      void* dst = tens == 0 ? p.dr : tens == 1 ? p.dw : tens == 2 ? p.dk : tens == 3 ? p.db
-                : tens == 4 ? p.da : p.dv;
+      const float4 own = *reinterpret_cast<const float4*>(&sm.part[pb][tens][u][j]);
+      float s[4] = {own.x, own.y, own.z, own.w};
+      if (Cfg::kCtas > 1) {
+        const float4 oth = *reinterpret_cast<const float4*>(&peer->part[pb][tens][u][j]);
+        s[0] += oth.x; s[1] += oth.y; s[2] += oth.z; s[3] += oth.w;
+      }
+      if (tens == 1)  // dw_in = dL/dw * w * dlw/dw_in
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[e] *= sm.w[u][j + e] * sm.dlw[u][j + e];
+      // part[] order: dr, dw, dk, db, da
+      void* dst = tens == 0 ? p.dr : tens == 1 ? p.dw : tens == 2 ? p.dk : tens == 3 ? p.db : p.da;
       Tin* o = static_cast<Tin*>(dst) + p.g.off(ch, t, j);
-      const float* s = &sm.out[tens][u][j];
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[e] = from_f32<Tin>(s[e]);
+    }
+    {  // dv of the own rows: thread -> (step, 4 rows)
+      const int u = tid / (ROWS / 4), j = (tid % (ROWS / 4)) * 4;
+      const int64_t t = c * kChunk + u;
+      if (t < p.g.T) {
+        Tin* o = static_cast<Tin*>(p.dv) + p.g.off(ch, t, row0 + j);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = from_f32<Tin>(sm.dv[u][j + e]);
+      }
     }
   }
   if (p.ds0 != nullptr) {  // after chunk 0, dS is the gradient of the start state
@@ -617,6 +691,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdArgs p) {
 #pragma unroll
     for (int m = 0; m < 4; ++m) dst[m] = make_float4(dS[4 * m], dS[4 * m + 1], dS[4 * m + 2], dS[4 * m + 3]);
   }
+  // the peer may still be reading this CTA's partial sums of the last chunk
+  if (Cfg::kCtas > 1) cluster.sync();
 }
 
 template <typename Tin>
@@ -634,14 +710,26 @@ cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-template <typename Tin>
-cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream) {
-  const size_t smem = sizeof(BwdSmem);
-  cudaError_t e = cudaFuncSetAttribute(scan_bwd_kernel<Tin>,
+template <typename Tin, int ROWS>
+cudaError_t launch_bwd_rows(const BwdArgs& p, cudaStream_t stream) {
+  using Cfg = BwdCfg<ROWS>;
+  const size_t smem = sizeof(BwdSmem<ROWS>);
+  cudaError_t e = cudaFuncSetAttribute(scan_bwd_kernel<Tin, ROWS>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  scan_bwd_kernel<Tin><<<(unsigned)p.g.chains(), kBwdThreads, smem, stream>>>(p);
+  // Cfg::kCtas CTAs per chain, one cluster (the cluster shape is compiled in)
+  scan_bwd_kernel<Tin, ROWS><<<(unsigned)(p.g.chains() * Cfg::kCtas), Cfg::kThreads, smem, stream>>>(p);
   return cudaGetLastError();
+}
+
+// Two 32-row CTAs per chain while they fit the SMs in one wave (a CTA holds
+// an SM: 151 KB of shared memory), else one 64-row CTA per chain.
+template <typename Tin>
+cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return p.g.chains() * 2 <= sms ? launch_bwd_rows<Tin, 32>(p, stream)
+                                 : launch_bwd_rows<Tin, 64>(p, stream);
 }
 
 template cudaError_t launch_fwd<float>(const FwdArgs&, cudaStream_t);
