@@ -529,7 +529,7 @@ struct alignas(1024) KGroup {
   Tile dQyb, dW2b;
   Tile At, Rt, Bb, Kb;
   float lam[kN], cum[L][ks::LDF], lw[L][ks::LDF];
-  float dllp[4][kN], dll[kN];
+  float dllp[1][kN], dll[kN];  // colsum(G'' o S) (own columns per warp), then dll
   bf16 dPb[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
   Tile W;
   Tile16 Ti, Q;
@@ -645,47 +645,70 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     int hh, bb;
     item_pos(p.g, item, ch, c, hh, bb);
 
-    // ---- row sums over the 64 state rows (own columns), and the key side ----
-    //   dW = dSA S, dQy = dY S, dBb = SA G'', dKb = V G'';  dP = lower(dY V^T) (warp 2),
-    //   dQ = strict(dSA V^T) (warp 1, kept in registers), lam dll (16 rows per warp)
+    // ---- row sums over the 64 state rows (own columns j0 .. j0 + 15), and the key side ----
+    //   dW = dSA S, dQy = dY S, dBb = SA G'', dKb = V G'', and colsum(G'' o S) as the
+    //   diagonal of G''^T S; dQ = strict(dSA V^T) (warp 1, kept in registers),
+    //   dP = lower(dY V^T) (warp 2).  One pass over the 64 rows in k-steps of 16:
+    //   the S and G'' fragments of a k-step serve every product that needs them.
     float dW[2][4] = {}, dQy[2][4] = {}, dBp[2][4] = {}, dKp[2][4] = {}, dq[2][4] = {};
-    mm16<true, true, 4>(dW, xr.dSAT, Swz16{}, xr.S, Swz64{}, j0, lane);
-    mm16<false, true, 4>(dQy, raw_dy, Swz64{}, xr.S, Swz64{}, j0, lane);
-    mm16<true, true, 4>(dBp, xr.SAT, Swz16{}, xr.G, Swz64{}, j0, lane);
-    mm16<false, true, 4>(dKp, raw_v, Swz64{}, xr.G, Swz64{}, j0, lane);
-    if (gw == 1) {
-      mm16<true, false, 4>(dq, xr.dSAT, Swz16{}, raw_v, Swz64{}, 0, lane);
+    {
+      float dd[2][4] = {}, dp[2][4] = {};
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t bS[4], bG[4], aD[4], aY[4], aA[4], aV[4], aT[4];
+        ldb_kn(bS, xr.S, Swz64{}, j0, 16 * kk, lane);
+        ldb_kn(bG, xr.G, Swz64{}, j0, 16 * kk, lane);
+        lda_cm(aD, xr.dSAT, Swz16{}, 0, 16 * kk, lane);   // dSA (t x i)
+        lda_rm(aY, raw_dy, Swz64{}, 0, 16 * kk, lane);    // dY
+        lda_cm(aA, xr.SAT, Swz16{}, 0, 16 * kk, lane);    // SA
+        lda_rm(aV, raw_v, Swz64{}, 0, 16 * kk, lane);     // V
+        lda_cm(aT, xr.G, Swz64{}, j0, 16 * kk, lane);     // G''^T (own columns as rows)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
-          if (u >= t) dq[nt][e] = 0.f;
+        for (int nt = 0; nt < 2; ++nt) {
+          mma16816(dW[nt], aD, bS[2 * nt], bS[2 * nt + 1]);
+          mma16816(dQy[nt], aY, bS[2 * nt], bS[2 * nt + 1]);
+          mma16816(dBp[nt], aA, bG[2 * nt], bG[2 * nt + 1]);
+          mma16816(dKp[nt], aV, bG[2 * nt], bG[2 * nt + 1]);
+          mma16816(dd[nt], aT, bS[2 * nt], bS[2 * nt + 1]);
         }
-    } else if (gw == 2) {
-      float dp[2][4] = {};
-      mm16<false, false, 4>(dp, raw_dy, Swz64{}, raw_v, Swz64{}, 0, lane);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
-          if (u > t) dp[nt][e] = 0.f;
+        if (gw == 1 || gw == 2) {  // V^T as the B operand (k = i, n = s)
+          uint32_t bV[4];
+          ldb_nk(bV, raw_v, Swz64{}, 0, 16 * kk, lane);
+          if (gw == 1) {
+            mma16816(dq[0], aD, bV[0], bV[1]);
+            mma16816(dq[1], aD, bV[2], bV[3]);
+          } else {
+            mma16816(dp[0], aY, bV[0], bV[1]);
+            mma16816(dp[1], aY, bV[2], bV[3]);
+          }
         }
-      store_acc_bf16(&G.dPb[0][0], LDS, 0, 0, dp[0], lane);
-      store_acc_bf16(&G.dPb[0][0], LDS, 0, 8, dp[1], lane);
-    }
-    {  // colsum(G'' o S) over rows 16gw.. for columns 2 lane, 2 lane + 1
-      float2 acc = make_float2(0.f, 0.f);
-#pragma unroll 4
-      for (int i = 16 * gw; i < 16 * gw + 16; ++i) {
-        const int o = Swz64{}(i, 2 * lane);
-        const float2 gv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xr.G[o]));
-        const float2 sv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xr.S[o]));
-        acc.x += gv.x * sv.x;
-        acc.y += gv.y * sv.y;
       }
-      *reinterpret_cast<float2*>(&G.dllp[gw][2 * lane]) = acc;
+      if (gw == 1) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
+            if (u >= t) dq[nt][e] = 0.f;
+          }
+      } else if (gw == 2) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
+            if (u > t) dp[nt][e] = 0.f;
+          }
+        store_acc_bf16(&G.dPb[0][0], LDS, 0, 0, dp[0], lane);
+        store_acc_bf16(&G.dPb[0][0], LDS, 0, 8, dp[1], lane);
+      }
+      // diagonal of the 16 x 16 block G''^T S: lanes with gq / 2 == q hold columns
+      // j0 + gq (tile 0) and j0 + 8 + gq (tile 1)
+      if ((gq >> 1) == q) {
+        const bool x = gq & 1;  // selects, not an index: keeps dd in registers
+        G.dllp[0][j0 + gq] = x ? dd[0][1] : dd[0][0];
+        G.dllp[0][j0 + 8 + gq] = x ? dd[1][3] : dd[1][2];
+      }
     }
     ok = mbar_wait(&G.barB, ph);  // r, w, k, a, b
     seen_b += ok;
@@ -720,7 +743,7 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int jj = j0 + 8 * (i >> 1) + 2 * q + (i & 1);
-          G.dll[jj] = G.dllp[0][jj] + G.dllp[1][jj] + G.dllp[2][jj] + G.dllp[3][jj] + v[i];
+          G.dll[jj] = G.dllp[0][jj] + v[i];
         }
     }
     store_acc_bf16(&G.dQyb[0][0], LD, 0, j0, dQy[0], lane);
