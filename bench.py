@@ -491,7 +491,7 @@ def timing_note(blocks, K):
 
 def config_of(args, wl, world):
     return {"workload": f"{args.workload}: B={wl['B']}/GPU T={wl['T']} H={wl['H']} N={wl['N']} "
-                        f"bf16 WKV-7 ClampW fwd+bwd", "model": "WKV-7 ClampW op",
+                        f"{args.dtype} WKV-7 ClampW fwd+bwd", "model": "WKV-7 ClampW op",
             "global_batch": wl["B"] * world, "seq_len": wl["T"], "heads": wl["H"],
             "head_size": wl["N"], "parallelism": f"dp{world} (batch shards, no collective)",
             "algo": args.algo, "l2": "inputs larger than L2 (7 x 32 MiB per step), no flush",
@@ -501,15 +501,16 @@ def config_of(args, wl, world):
 def run_op(args, wl, world, rank, local):
     dev = torch.device("cuda", local)
     B, T, H, N = wl["B"], wl["T"], wl["H"], wl["N"]
+    dt = torch.float32 if args.dtype == "fp32" else torch.bfloat16
     inp = make_inputs(B, T, H, N, seed=1000 + rank, w_mu=wl["w_mu"], w_sigma=wl["w_sigma"],
-                      dtype=torch.bfloat16)
+                      dtype=dt)
     xs = [inp[n].to(dev) for n in NAMES]
     dy = inp["dy"].to(dev)
     stream = torch.cuda.current_stream(dev)
 
     # preallocated outputs: the timed step is exactly one fwd + one bwd call
     y, sa, ckpt = ops.wkv7_forward(*xs, algo=args.algo)
-    wb = ops.work_bytes(B, T, H, torch.bfloat16, args.algo)
+    wb = ops.work_bytes(B, T, H, dt, args.algo)
     work = torch.empty(max(wb, 16), dtype=torch.uint8, device=dev)
     grads = ops.wkv7_backward(*xs, dy, None, ckpt, algo=args.algo, work=work)
 
@@ -525,7 +526,8 @@ def run_op(args, wl, world, rank, local):
 
     for _ in range(args.warmup):
         step()
-    launches = {"own": 4 if args.algo != "scan" else 2, "source": "static (--no-trace)"} \
+    scan = args.algo == "scan" or dt == torch.float32
+    launches = {"own": 2 if scan else 4, "source": "static (--no-trace)"} \
         if args.no_trace else count_launches(step, dev)
     clocks = ClockSampler(local)
     blocks, fwd_ms, bwd_ms = timed_blocks(step, args.steps, dev, stream, world, local,
@@ -539,13 +541,15 @@ def run_op(args, wl, world, rank, local):
     hbm, peak_kind = peaks()
     kern = "bwd" if bwd_ms >= fwd_ms else "fwd"
     k_ms = bwd_ms if kern == "bwd" else fwd_ms
-    k_bytes = (BWD_BYTES if kern == "bwd" else FWD_BYTES) * elems
+    # fp32 inputs and outputs (sa is fp32 either way) double the bf16 element bytes
+    fwd_b, bwd_b = (FWD_BYTES, BWD_BYTES) if dt == torch.bfloat16 else (6 * 4 + 4 + 4, 13 * 4)
+    k_bytes = (bwd_b if kern == "bwd" else fwd_b) * elems
     achieved = k_bytes / (k_ms / 1e3) / 1e9
-    step_gbs = (FWD_BYTES + BWD_BYTES) * elems / (step_ms / 1e3) / 1e9
+    step_gbs = (fwd_b + bwd_b) * elems / (step_ms / 1e3) / 1e9
     kname = {"fwd": "forward (keyside_kernel + value_fwd_kernel)",
              "bwd": "backward (value_bwd_kernel + keyside_bwd_kernel)"}[kern]
     traffic = None
-    if args.algo == "scan":
+    if scan:
         kname = f"scan_{kern}_kernel"
     else:
         traffic = profiled_traffic(args.workload,
@@ -559,10 +563,10 @@ def run_op(args, wl, world, rank, local):
                 "algorithmic_bytes_per_launch": k_bytes,
                 "launch_ms": k_ms, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
                 "step_achieved": step_gbs, "step_frac": step_gbs / hbm,
-                "bytes_per_element": {"fwd": FWD_BYTES, "bwd": BWD_BYTES}}
+                "bytes_per_element": {"fwd": fwd_b, "bwd": bwd_b}}
 
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and dt == torch.bfloat16:  # the autograd API's default (bf16) path
         e2e = measure_e2e(args, xs, dy, dev, stream, world, local)
 
     cb = None
@@ -574,8 +578,8 @@ def run_op(args, wl, world, rank, local):
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "bf16", "data": "synthetic (seeded randn, distributions of the op's "
-                                         "workloads)",
+                "dtype": args.dtype, "data": "synthetic (seeded randn, distributions of the "
+                                             "op's workloads)",
                 "config": config_of(args, wl, world), "roofline": roofline,
                 "timing": timing_note(blocks, args.steps),
                 "cpu_baseline": cb, "clocks": clk, "e2e": e2e,
@@ -1045,6 +1049,8 @@ def main():
     ap.add_argument("--workload", default="shard_b4_t4096",
                     choices=sorted(WORKLOADS) + list(OTHER_WORKLOADS))
     ap.add_argument("--algo", default="auto", choices=["auto", "scan", "chunked"])
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"],
+                    help="input dtype of the op workloads (fp32 runs the fp32-exact scan)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-trace", action="store_true",
