@@ -142,15 +142,22 @@ __device__ __forceinline__ void sa_of(float (&sat)[2][4], const rec::KeyRec& kr,
   mma_k64_k16(sat, sA, vA, bW, bQ);
 }
 
-// State warp, one chunk (processing index pi): stage its S and SA^T rows.
+// Whether chunk c's start state goes into its hand-off record: the key-side
+// backward takes the states of even chunks >= 2 from the checkpoint instead,
+// where the forward stored the same bf16 values in the same layout.
+__device__ __forceinline__ bool record_state(int64_t c) { return c < 2 || (c & 1) != 0; }
+
+// State warp, one chunk c (processing index pi): stage its SA^T rows, and its
+// S rows when they go into the record.
 template <int RB>
-__device__ __forceinline__ bool s_chunk(Smem<RB>& sm, int pi, int s, const uint32_t (&sA)[4][4],
+__device__ __forceinline__ bool s_chunk(Smem<RB>& sm, int pi, int c, int s, const uint32_t (&sA)[4][4],
                                         const float (&sat)[2][4], int il, int lane) {
   const int x = pi & (NX - 1);
   if (pi >= NX && !mbar_wait(&sm.sempty[x], par(pi - NX, NX))) return false;
   Stage<RB>& st = sm.st[x];
+  if (record_state(c))
 #pragma unroll
-  for (int kk = 0; kk < 4; ++kk) sta_rm(st.S, Swz64{}, il, 16 * kk, sA[kk], lane);
+    for (int kk = 0; kk < 4; ++kk) sta_rm(st.S, Swz64{}, il, 16 * kk, sA[kk], lane);
   uint32_t saA[4];
   acc_to_a(saA, sat[0], sat[1]);
   sta_rm(st.SAT, Swz16{}, il, 0, saA, lane);
@@ -238,7 +245,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
       if (!mbar_wait(&sm.sfull[x], par(pi, NX))) break;
       const Stage<RB>& st = sm.st[x];
       rec::XRec* xr = rec::xrec(P.work, ch, nchunk, c);
-      bulk_s2g(xr->S + row0 * kN, st.S, 2048 * RB);
+      if (record_state(c)) bulk_s2g(xr->S + row0 * kN, st.S, 2048 * RB);
       bulk_s2g(xr->G + row0 * kN, st.G, 2048 * RB);
       bulk_s2g(xr->SAT + row0 * L, st.SAT, 512 * RB);
       bulk_s2g(xr->dSAT + row0 * L, st.dSAT, 512 * RB);
@@ -496,9 +503,9 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_bwd_kernel(const _
       lda_cm(vHi, shi.v, Swz64{}, i0, 0, lane);
       float satHi[2][4];
       sa_of(satHi, shi.k, sHi, vHi, lane);
-      if (!s_chunk(sm, nchunk - 1 - hi, s_hi, sHi, satHi, il, lane)) return;
+      if (!s_chunk(sm, nchunk - 1 - hi, hi, s_hi, sHi, satHi, il, lane)) return;
     }
-    if (!s_chunk(sm, nchunk - 1 - lo, s_lo, sLo, satLo, il, lane)) return;
+    if (!s_chunk(sm, nchunk - 1 - lo, lo, s_lo, sLo, satLo, il, lane)) return;
   }
 }
 
@@ -516,22 +523,29 @@ cudaError_t launch(const Params& V, int64_t chains, cudaStream_t stream) {
 
 namespace kb {
 
-constexpr int kThreads = 128;  // one group of 4 warps per CTA, 3 CTAs per SM
+constexpr int kThreads = 128;  // one group of 4 warps per CTA, 4 CTAs per SM
 
-// Inputs are single-buffered and loaded in two parts: v, dy and the XRec of
-// the next item as soon as the first phase of this one has consumed them
-// (part A), r, w, k, a, b once this item's outputs, staged in place in those
-// tiles, have been copied out (part B).
+// Inputs are single-buffered: v, dy and the XRec (part A), and r, w, k, a, b
+// (part B) of the next item are loaded once this item's outputs, staged in
+// place in the r, w, k, a, b tiles, have been copied out; the record's space
+// serves as scratch in between.  Four CTAs per SM cover each other's loads.
 struct alignas(1024) KGroup {
   bf16 raw[7][L * kN];  // r, w, k, a, b, v, dy as landed by TMA (1 KiB aligned);
                         // r, w, k, a, b then hold dr, dw, dk, da, db until copied out
-  rec::XRec x;
-  Tile dQyb, dW2b;
-  Tile At, Rt, Bb, Kb;
+  // The hand-off record is read only by the row sums; the tiles of the later
+  // phases reuse its space (54 KB per CTA: four CTAs per SM)
+  union Shared {
+    rec::XRec x;
+    struct Scratch {
+      Tile dQyb, dW2b;
+      Tile At, Rt, Bb, Kb;
+      Tile W;
+      bf16 dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
+    } s;
+  } u;
   float lam[kN], cum[L][ks::LDF], lw[L][ks::LDF];
   float dllp[1][kN], dll[kN];  // colsum(G'' o S) (own columns per warp), then dll
-  bf16 dPb[L][LDS], dCmb[L][LDS], dAb[L][LDS], dBmb[L][LDS];
-  Tile W;
+  bf16 dPb[L][LDS];
   Tile16 Ti, Q;
   alignas(16) rec::TriRec tri;  // Tf = Ti in fp32, Bm, Cm: from the forward, with part B
   float Ga[L][L + 1];           // scratch of the dA product
@@ -539,6 +553,10 @@ struct alignas(1024) KGroup {
   float dTf[L][L + 1];
   uint64_t barA, barB;
 };
+
+// four CTAs per SM: each takes its dynamic shared memory (the struct plus 1 KiB
+// of alignment slack) and 1 KiB the runtime reserves, out of 228 KiB
+static_assert(4 * (sizeof(KGroup) + 2048) <= 228 * 1024, "keyside_bwd: four CTAs per SM");
 
 struct Params {
   CUtensorMap in[7];  // r, w, k, a, b, v, dy
@@ -561,7 +579,15 @@ __device__ __forceinline__ void issue_a(KGroup& G, const Params& P, int64_t item
   mbar_arrive_expect_tx(&G.barA, 2 * tma::kTileBytes + sizeof(rec::XRec));
   tma::load_tile(G.raw[5], &P.in[5], h, static_cast<int>(c * L), b, &G.barA);
   tma::load_tile(G.raw[6], &P.in[6], h, static_cast<int>(c * L), b, &G.barA);
-  bulk_g2s(&G.x, rec::xrec(P.work, ch, P.a.g.nchunk, c), sizeof(rec::XRec), &G.barA);
+  const rec::XRec* xr = rec::xrec(P.work, ch, P.a.g.nchunk, c);
+  if (vb::record_state(c)) {
+    bulk_g2s(&G.u.x, xr, sizeof(rec::XRec), &G.barA);
+  } else {  // the start state from the checkpoint, the rest of the record from the workspace
+    constexpr uint32_t kS = sizeof(rec::XRec::S);
+    bulk_g2s(G.u.x.S, rec::state_ptr(const_cast<float*>(P.a.ckpt), P.a.g.chains(), ch,
+                                     P.a.g.nchunk, c), kS, &G.barA);
+    bulk_g2s(G.u.x.G, xr->G, sizeof(rec::XRec) - kS, &G.barA);
+  }
 }
 
 __device__ __forceinline__ void issue_b(KGroup& G, const Params& P, int64_t item) {
@@ -603,7 +629,7 @@ __device__ __forceinline__ void mm8_tf32(float (&acc)[4], FA A, FB B, int n0, in
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(kThreads, 4) keyside_bwd_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   KGroup& G = *reinterpret_cast<KGroup*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
   const BwdArgs& p = P.a;
@@ -630,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
   const bf16* raw_b = G.raw[4];
   const bf16* raw_v = G.raw[5];
   const bf16* raw_dy = G.raw[6];
-  rec::XRec& xr = G.x;
+  rec::XRec& xr = G.u.x;
   int64_t j = 0;
   for (;; ++j) {
     const int64_t item = blockIdx.x + j * gridDim.x;
@@ -712,16 +738,14 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
     }
     ok = mbar_wait(&G.barB, ph);  // r, w, k, a, b
     seen_b += ok;
-    if (ok)
-      ks::decays<true>(raw_r, G.raw[1], raw_k, raw_a, raw_b, &G.At[0][0], &G.Rt[0][0], Padded{LD},
-                       &G.Kb[0][0], &G.Bb[0][0], Padded{LD}, G.lam,
-                       G.cum, G.lw, tid, p.g.decay);
-    ok = __syncthreads_and(ok);  // v, dy and the XRec are free from here on
+    // every warp's row sums are done: v, dy and the hand-off record are dead,
+    // and the scratch tiles may overwrite the record
+    ok = __syncthreads_and(ok);
     if (!ok) break;
-    if (tid == 0 && next < total) {
-      issue_a(G, P, next);
-      ++issued_a;
-    }
+    ks::decays<true>(raw_r, G.raw[1], raw_k, raw_a, raw_b, &G.u.s.At[0][0], &G.u.s.Rt[0][0],
+                     Padded{LD}, &G.u.s.Kb[0][0], &G.u.s.Bb[0][0], Padded{LD}, G.lam, G.cum, G.lw,
+                     tid, p.g.decay);
+    __syncthreads();
     for (int e = tid; e < L * L; e += kThreads)  // Ti = bf16(Tf) for the bf16 products
       G.Ti[e >> 4][e & 15] = __float2bfloat16_rn(G.tri.Tf[e >> 4][e & 15]);
     {  // dll = colsum(G'' o S') / lam = colsum(G'' o S) + colsum(Bb o SA G'') + colsum(Kb o V G'')
@@ -731,9 +755,9 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           const int jj = j0 + 8 * nt + 2 * q + x;
-          v[2 * nt + x] = __bfloat162float(G.Bb[gq][jj]) * dBp[nt][x] + __bfloat162float(G.Kb[gq][jj]) * dKp[nt][x] +
-                          __bfloat162float(G.Bb[gq + 8][jj]) * dBp[nt][2 + x] +
-                          __bfloat162float(G.Kb[gq + 8][jj]) * dKp[nt][2 + x];
+          v[2 * nt + x] = __bfloat162float(G.u.s.Bb[gq][jj]) * dBp[nt][x] + __bfloat162float(G.u.s.Kb[gq][jj]) * dKp[nt][x] +
+                          __bfloat162float(G.u.s.Bb[gq + 8][jj]) * dBp[nt][2 + x] +
+                          __bfloat162float(G.u.s.Kb[gq + 8][jj]) * dKp[nt][2 + x];
         }
 #pragma unroll
       for (int m = 4; m < 32; m <<= 1)
@@ -746,22 +770,22 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
           G.dll[jj] = G.dllp[0][jj] + v[i];
         }
     }
-    store_acc_bf16(&G.dQyb[0][0], LD, 0, j0, dQy[0], lane);
-    store_acc_bf16(&G.dQyb[0][0], LD, 0, j0 + 8, dQy[1], lane);
+    store_acc_bf16(&G.u.s.dQyb[0][0], LD, 0, j0, dQy[0], lane);
+    store_acc_bf16(&G.u.s.dQyb[0][0], LD, 0, j0 + 8, dQy[1], lane);
     __syncwarp();
     // dW += Cm^T dQy (own columns of dQy, written by this warp)
-    mm16<true, true, 1>(dW, &G.tri.Cm[0][0], Padded{LDS}, &G.dQyb[0][0], Padded{LD}, j0, lane);
-    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0, dW[0], lane);
-    store_acc_bf16(&G.dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
+    mm16<true, true, 1>(dW, &G.tri.Cm[0][0], Padded{LDS}, &G.u.s.dQyb[0][0], Padded{LD}, j0, lane);
+    store_acc_bf16(&G.u.s.dW2b[0][0], LD, 0, j0, dW[0], lane);
+    store_acc_bf16(&G.u.s.dW2b[0][0], LD, 0, j0 + 8, dW[1], lane);
     __syncthreads();
-    ks::w_and_q(G.Ti, &G.At[0][0], Padded{LD}, G.tri.Bm, &G.W[0][0], Padded{LD}, &G.Q[0][0],
+    ks::w_and_q(G.Ti, &G.u.s.At[0][0], Padded{LD}, G.tri.Bm, &G.u.s.W[0][0], Padded{LD}, &G.Q[0][0],
                 Padded{LDS}, gw, lane);
     __syncthreads();  // W, Q and dW ready
 
     // ---- 16x16 pieces ----
     if (gw == 0) {  // dCm = lower(dQy W^T + dP Q^T)
       float dcm[2][4] = {};
-      mm16<false, false, 4>(dcm, &G.dQyb[0][0], Padded{LD}, &G.W[0][0], Padded{LD}, 0, lane);
+      mm16<false, false, 4>(dcm, &G.u.s.dQyb[0][0], Padded{LD}, &G.u.s.W[0][0], Padded{LD}, 0, lane);
       mm16<false, false, 1>(dcm, &G.dPb[0][0], Padded{LDS}, &G.Q[0][0], Padded{LDS}, 0, lane);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
@@ -770,21 +794,21 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
           const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
           if (u > t) dcm[nt][e] = 0.f;
         }
-      store_acc_bf16(&G.dCmb[0][0], LDS, 0, 0, dcm[0], lane);
-      store_acc_bf16(&G.dCmb[0][0], LDS, 0, 8, dcm[1], lane);
+      store_acc_bf16(&G.u.s.dCmb[0][0], LDS, 0, 0, dcm[0], lane);
+      store_acc_bf16(&G.u.s.dCmb[0][0], LDS, 0, 8, dcm[1], lane);
     } else if (gw == 1) {  // dQ += Cm^T dP;  dTi = dW At^T + dQ Bm^T
       mm16<true, true, 1>(dq, &G.tri.Cm[0][0], Padded{LDS}, &G.dPb[0][0], Padded{LDS}, 0, lane);
       store_acc_bf16(&G.dQ2b[0][0], LDS, 0, 0, dq[0], lane);
       store_acc_bf16(&G.dQ2b[0][0], LDS, 0, 8, dq[1], lane);
       __syncwarp();
       float dti[2][4] = {};
-      mm16<false, false, 4>(dti, &G.dW2b[0][0], Padded{LD}, &G.At[0][0], Padded{LD}, 0, lane);
+      mm16<false, false, 4>(dti, &G.u.s.dW2b[0][0], Padded{LD}, &G.u.s.At[0][0], Padded{LD}, 0, lane);
       mm16<false, false, 1>(dti, &G.dQ2b[0][0], Padded{LDS}, &G.tri.Bm[0][0], Padded{LDS}, 0, lane);
       store_acc_f32(&G.dTf[0][0], L + 1, 0, 0, dti[0], lane);
       store_acc_f32(&G.dTf[0][0], L + 1, 0, 8, dti[1], lane);
     }
     float dAt[2][4] = {};  // Ti^T dW (own columns)
-    mm16<true, true, 1>(dAt, &G.Ti[0][0], Padded{LDS}, &G.dW2b[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dAt, &G.Ti[0][0], Padded{LDS}, &G.u.s.dW2b[0][0], Padded{LD}, j0, lane);
     __syncthreads();
     // dA = strict(Ti^T dTi Ti^T) with tf32 operands, columns 0-7 on warp 0 and 8-15 on
     // warp 2 (a column block of dA needs only that block of M1 = dTi Ti^T);
@@ -805,7 +829,7 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
         const int t = gq + (e >= 2 ? 8 : 0), u = n0 + 2 * q + (e & 1);
         if (u >= t) da[e] = 0.f;
       }
-      store_acc_bf16(&G.dAb[0][0], LDS, 0, n0, da, lane);
+      store_acc_bf16(&G.u.s.dAb[0][0], LDS, 0, n0, da, lane);
     } else if (gw == 1) {
       float dbm[2][4] = {};
       mm16<true, true, 1>(dbm, &G.Ti[0][0], Padded{LDS}, &G.dQ2b[0][0], Padded{LDS}, 0, lane);
@@ -816,21 +840,21 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
           const int t = gq + (e >= 2 ? 8 : 0), u = 8 * nt + 2 * q + (e & 1);
           if (u >= t) dbm[nt][e] = 0.f;
         }
-      store_acc_bf16(&G.dBmb[0][0], LDS, 0, 0, dbm[0], lane);
-      store_acc_bf16(&G.dBmb[0][0], LDS, 0, 8, dbm[1], lane);
+      store_acc_bf16(&G.u.s.dBmb[0][0], LDS, 0, 0, dbm[0], lane);
+      store_acc_bf16(&G.u.s.dBmb[0][0], LDS, 0, 8, dbm[1], lane);
     }
     float dBb[2][4] = {}, dKb[2][4] = {}, dRt[2][4] = {};
-    mm16<true, true, 1>(dBb, &G.dCmb[0][0], Padded{LDS}, &G.Rt[0][0], Padded{LD}, j0, lane);
-    mm16<true, true, 1>(dKb, &G.dPb[0][0], Padded{LDS}, &G.Rt[0][0], Padded{LD}, j0, lane);
-    mm16<false, true, 1>(dRt, &G.dCmb[0][0], Padded{LDS}, &G.Bb[0][0], Padded{LD}, j0, lane);
-    mm16<false, true, 1>(dRt, &G.dPb[0][0], Padded{LDS}, &G.Kb[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dBb, &G.u.s.dCmb[0][0], Padded{LDS}, &G.u.s.Rt[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dKb, &G.dPb[0][0], Padded{LDS}, &G.u.s.Rt[0][0], Padded{LD}, j0, lane);
+    mm16<false, true, 1>(dRt, &G.u.s.dCmb[0][0], Padded{LDS}, &G.u.s.Bb[0][0], Padded{LD}, j0, lane);
+    mm16<false, true, 1>(dRt, &G.dPb[0][0], Padded{LDS}, &G.u.s.Kb[0][0], Padded{LD}, j0, lane);
     __syncthreads();
 
     // ---- column-indexed gradients that need dA, dBm (own columns) ----
-    mm16<false, true, 1>(dAt, &G.dAb[0][0], Padded{LDS}, &G.Bb[0][0], Padded{LD}, j0, lane);
-    mm16<false, true, 1>(dAt, &G.dBmb[0][0], Padded{LDS}, &G.Kb[0][0], Padded{LD}, j0, lane);
-    mm16<true, true, 1>(dBb, &G.dAb[0][0], Padded{LDS}, &G.At[0][0], Padded{LD}, j0, lane);
-    mm16<true, true, 1>(dKb, &G.dBmb[0][0], Padded{LDS}, &G.At[0][0], Padded{LD}, j0, lane);
+    mm16<false, true, 1>(dAt, &G.u.s.dAb[0][0], Padded{LDS}, &G.u.s.Bb[0][0], Padded{LD}, j0, lane);
+    mm16<false, true, 1>(dAt, &G.u.s.dBmb[0][0], Padded{LDS}, &G.u.s.Kb[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dBb, &G.u.s.dAb[0][0], Padded{LDS}, &G.u.s.At[0][0], Padded{LD}, j0, lane);
+    mm16<true, true, 1>(dKb, &G.u.s.dBmb[0][0], Padded{LDS}, &G.u.s.At[0][0], Padded{LD}, j0, lane);
     // outputs in place of the inputs they replace (same thread, same element):
     // dr -> r, dk -> k, da -> a, db -> b tiles; dw -> the w tile.  This lane
     // holds rows gq (hf 0) and gq + 8 (hf 1) of columns j0 + 8 nt + 2q + x.
@@ -922,8 +946,10 @@ __global__ void __launch_bounds__(kThreads, 3) keyside_bwd_kernel(const __grid_c
           *reinterpret_cast<uint4*>(dst[i] + off) = *reinterpret_cast<const uint4*>(G.raw[i] + o);
       }
     }
-    __syncthreads();  // r, w, k, a, b tiles free
+    __syncthreads();  // every tile and the scratch free: load the next item
     if (tid == 0 && next < total) {
+      issue_a(G, P, next);
+      ++issued_a;
       issue_b(G, P, next);
       ++issued_b;
     }
@@ -994,7 +1020,7 @@ cudaError_t launch_bwd(const BwdArgs& p, void* work, cudaStream_t stream) {
                            (int)ksmem);
   if (e != cudaSuccess) return e;
   const int64_t items = p.g.chains() * p.g.nchunk;
-  const int64_t kgrid = items < 3LL * sms ? items : 3LL * sms;  // 3 CTAs per SM
+  const int64_t kgrid = items < 4LL * sms ? items : 4LL * sms;  // 4 CTAs per SM
   kb::keyside_bwd_kernel<<<(unsigned)kgrid, kb::kThreads, ksmem, stream>>>(K);
   return cudaGetLastError();
 }

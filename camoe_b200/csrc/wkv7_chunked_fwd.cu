@@ -393,12 +393,14 @@ namespace vf {
 //            sits in front of its loads; it issues no fence, no output store
 //            and one mbarrier wait per chunk (each costs a round trip of
 //            about 50-120 cycles): the published state lives in the chunk's
-//            input slot, which is refilled only after the Y and A warps have
-//            released it, so no "buffer free" check is needed;
+//            input slot, which is refilled only after the Y warp has
+//            released it, so no "buffer free" check is needed.  It writes sa
+//            straight from its accumulators to global memory (store
+//            instructions, off its dependency chain): staging sa through a
+//            second consumer warp cost that warp a recomputation of SA on the
+//            SMSPs the Y warps use, which then set the pace;
 //   Y warp   reads the published start state, forms Y and stages y and (even
-//            chunks) the checkpoint copy of the start state;
-//   A warp   the same for SA (recomputed with the S warp's operands and
-//            order) and sa.
+//            chunks) the checkpoint copy of the start state.
 // A producer warp streams each chunk's KeyRec and v tile; a store warp writes
 // the staged tiles (TMA tile stores, bulk copies) with KEEP groups in flight.
 
@@ -414,8 +416,7 @@ struct alignas(128) Pub {
 
 template <int RB>
 struct alignas(1024) Stage {
-  float sa[L][16 * RB];  // [t][i] of this CTA's rows (TMA store)
-  bf16 y[L][16 * RB];    // [t][i] (TMA store)
+  bf16 y[L][16 * RB];    // [t][i] of this CTA's rows (TMA store)
   bf16 S[16 * RB * kN];  // Swz64 rows: checkpoint copy of the start state
 };
 
@@ -434,7 +435,7 @@ struct Smem {
 };
 
 struct Params {
-  CUtensorMap map_v, map_y, map_sa;
+  CUtensorMap map_v, map_y;
   FwdArgs a;
 };
 
@@ -446,13 +447,15 @@ static __device__ int g_test_skip_pair = -1;
 __device__ __forceinline__ uint32_t par(int idx, int n) { return static_cast<uint32_t>((idx / n) & 1); }
 
 template <int RB>
-__global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(32 * (2 * RB + 2), 1) value_fwd_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Smem<RB>& sm = *reinterpret_cast<Smem<RB>*>(smem_raw + ((1024u - (sm_addr(smem_raw) & 1023u)) & 1023u));
   constexpr int NRG = 4 / RB;  // CTAs per chain
   constexpr int NS = Smem<RB>::NS, NX = Smem<RB>::NX, KEEP = Smem<RB>::KEEP;
   const FwdArgs& p = P.a;
-  const int tid = threadIdx.x, lane = tid & 31, warp = role_warp<RB>(tid >> 5);
+  // warps [S x RB][Y x RB][producer][store]: with RB == 2 the two S warps run on
+  // SMSPs 0 and 1 beside the light producer and store warps, the Y warps on 2, 3
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t ch = blockIdx.x / NRG;
   const int row0 = 16 * RB * static_cast<int>(blockIdx.x % NRG);
   const int nchunk = static_cast<int>(p.g.nchunk);
@@ -460,11 +463,11 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       if (s < NS / 2) mbar_init(&sm.fullp[s], 1);
-      mbar_init(&sm.empty[s], 2 * RB);  // Y and A warps (see the S warp)
+      mbar_init(&sm.empty[s], RB);  // the Y warps (see the S warp)
     }
     for (int x = 0; x < NS; ++x) mbar_init(&sm.pfull[x], RB);
     for (int x = 0; x < NX; ++x) {
-      mbar_init(&sm.done[x], 2 * RB);
+      mbar_init(&sm.done[x], RB);
       mbar_init(&sm.sempty[x], 1);
     }
     mbar_fence_init();
@@ -476,7 +479,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
   // only a checkpoint receives the bf16 states for the backward
   void* const recs = p.ckpt != nullptr ? static_cast<void*>(p.ckpt) : p.work;
   const bool states = p.ckpt != nullptr;
-  if (warp == 3 * RB) {
+  if (warp == 2 * RB) {
     // ------------------------------ producer ------------------------------
     if (lane != 0) return;
     constexpr int NB = NS / 2;
@@ -508,7 +511,7 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
     return;
   }
 
-  if (warp == 3 * RB + 1) {
+  if (warp == 2 * RB + 1) {
     // ------------------------------ store warp ------------------------------
     if (lane != 0) return;
     const int64_t chains = p.g.chains();
@@ -516,7 +519,6 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
       const int x = c & (NX - 1);
       if (!mbar_wait(&sm.done[x], par(c, NX))) break;
       const Stage<RB>& st = sm.st[x];
-      tma::store_tile(&P.map_sa, &st.sa[0][0], row0, hh, c * L, bb);
       tma::store_tile(&P.map_y, &st.y[0][0], row0, hh, c * L, bb);
       if (states && c >= 2 && (c & 1) == 0)
         bulk_s2g(rec::state_ptr(p.ckpt, chains, ch, nchunk, c) + row0 * 128, st.S, 2048 * RB);
@@ -548,6 +550,9 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
 #pragma unroll
         for (int e = 0; e < 4; ++e) S[nt][e] = 0.f;
     }
+    // sa element (t, i) of this warp's rows goes to sa_row[t * ts + i]
+    float* const sa_row = p.sa + p.g.base(ch) + i0 + g;
+    const int64_t ts = p.g.tstride(), T = p.g.T;
     if (nchunk > 0 && !mbar_wait(&sm.fullp[0], 0)) return;
     for (int c = 0; c < nchunk; ++c) {
       const int s = c % NS;
@@ -582,6 +587,14 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
         mma16816(S[2 * m], saA, bB[m][0], bB[m][1]);
         mma16816(S[2 * m + 1], saA, bB[m][2], bB[m][3]);
       }
+      // sa of the chunk: element (t = 16c + 8 nt + 2q + (e & 1), i = i0 + g (+8 for e >= 2))
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int64_t t = static_cast<int64_t>(c) * L + 8 * nt + 2 * q + (e & 1);
+          if (t < T) sa_row[t * ts + (e >= 2 ? 8 : 0)] = sa[nt][e];
+        }
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         S[nt][0] *= lam[nt].x; S[nt][1] *= lam[nt].y; S[nt][2] *= lam[nt].x; S[nt][3] *= lam[nt].y;
@@ -591,8 +604,8 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
       for (int kk = 0; kk < 4; ++kk) sta_rm(sm.pub[s].S, Swz64{}, il, 16 * kk, sA[kk], lane);
       __syncwarp();
       if (lane == 0) {
-        // no release of slot s here: the Y and A warps release it after waiting
-        // for this publication, which follows every read of the slot above
+        // no release of slot s here: the Y warps release it after waiting for
+        // this publication, which follows every read of the slot above
         mbar_arrive(&sm.pfull[s]);
       }
       if (c + 1 < nchunk && ((c + 1) & 1) == 0 &&
@@ -610,40 +623,31 @@ __global__ void __launch_bounds__(32 * (3 * RB + 2), 1) value_fwd_kernel(const _
     return;
   }
 
-  // ------------------------------ Y warp (role 1) / A warp (role 2) ------------------------------
+  // ------------------------------ Y warp (role 1) ------------------------------
   for (int c = 0; c < nchunk; ++c) {
     const int s = c % NS, x = c & (NX - 1);
     if ((c & 1) == 0 && !mbar_wait(&sm.fullp[(c >> 1) % (NS / 2)], par(c >> 1, NS / 2))) return;
     const rec::KeyRec& kr = sm.slot[s].k;
     uint32_t bM[4][4], bV[4], vA[4];
-    const bf16* mk = role == 1 ? kr.Qy : kr.W;
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) ldb_nk(bM[kk], mk, Swz64{}, 0, 16 * kk, lane);
-    ldb_nk(bV, role == 1 ? kr.P : kr.Q, Swz16{}, 0, 0, lane);
+    for (int kk = 0; kk < 4; ++kk) ldb_nk(bM[kk], kr.Qy, Swz64{}, 0, 16 * kk, lane);
+    ldb_nk(bV, kr.P, Swz16{}, 0, 0, lane);
     lda_cm(vA, sm.slot[s].v, Swz64{}, i0, 0, lane);
     if (!mbar_wait(&sm.pfull[s], par(c, NS))) return;
     uint32_t sA[4][4];
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) lda_rm(sA[kk], sm.pub[s].S, Swz64{}, il, 16 * kk, lane);
-    // role 1: Y = Qy S^T + P V;  role 2: SA = W S^T + Q V (the S warp's operands and order)
+    // Y = Qy S^T + P V
     float acc[2][4];
     mma_k64_k16(acc, sA, vA, bM, bV);
     if (c >= NX && !mbar_wait(&sm.sempty[x], par(c - NX, NX))) return;
     Stage<RB>& st = sm.st[x];
-    if (role == 1) {
-      uint32_t yA[4];
-      acc_to_a(yA, acc[0], acc[1]);
-      sta_cm(&st.y[0][0], Padded{16 * RB}, il, 0, yA, lane);
-      if (states && c >= 2 && (c & 1) == 0)
+    uint32_t yA[4];
+    acc_to_a(yA, acc[0], acc[1]);
+    sta_cm(&st.y[0][0], Padded{16 * RB}, il, 0, yA, lane);
+    if (states && c >= 2 && (c & 1) == 0)
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) sta_rm(st.S, Swz64{}, il, 16 * kk, sA[kk], lane);
-    } else {
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          st.sa[8 * nt + 2 * q + (e & 1)][il + g + (e >= 2 ? 8 : 0)] = acc[nt][e];
-    }
+      for (int kk = 0; kk < 4; ++kk) sta_rm(st.S, Swz64{}, il, 16 * kk, sA[kk], lane);
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) {
@@ -659,7 +663,7 @@ cudaError_t launch(const Params& V, int64_t chains, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(value_fwd_kernel<RB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  value_fwd_kernel<RB><<<static_cast<unsigned>(chains * (4 / RB)), 32 * (3 * RB + 2), smem, stream>>>(V);
+  value_fwd_kernel<RB><<<static_cast<unsigned>(chains * (4 / RB)), 32 * (2 * RB + 2), smem, stream>>>(V);
   return cudaGetLastError();
 }
 
@@ -711,8 +715,7 @@ cudaError_t launch_fwd(const FwdArgs& p, cudaStream_t stream) {
   vf::Params V;
   V.a = p;
   if (!tma::encode_bhtn(&V.map_v, p.v, p.g.B, p.g.T, p.g.H) ||
-      !tma::encode_bhtn_cols(&V.map_y, p.y, p.g.B, p.g.T, p.g.H, 16 * rb, false) ||
-      !tma::encode_bhtn_cols(&V.map_sa, p.sa, p.g.B, p.g.T, p.g.H, 16 * rb, true))
+      !tma::encode_bhtn_cols(&V.map_y, p.y, p.g.B, p.g.T, p.g.H, 16 * rb, false))
     return cudaErrorInvalidValue;
   if (!(p.records_ready && p.ckpt != nullptr)) {
     const size_t ksmem = ka::kGroups * sizeof(ka::Group) + 1024;
