@@ -3,21 +3,22 @@
 //
 // Forward (scan_fwd_kernel): the state rows are independent recurrences that
 // share the transition, so a chain's 64 rows are split over 4 CTAs of 16
-// rows; 4 threads own one row (16 state columns each in registers) and
-// combine row sums (sa = S a, y = S r) with two xor-shuffles.  Chunks of 16
+// rows; 8 threads own one row (8 state columns each in registers, 4 warps per
+// CTA so each SMSP switches between warps of the latency-bound step loop) and
+// combine row sums (sa = S a, y = S r) with three xor-shuffles.  Chunks of 16
 // steps of r, w, k, a, b (and the CTA's slice of v) are streamed into shared
 // memory with cp.async, double-buffered, and converted once per chunk
 // (decay w = exp(log_decay(w_in)) computed there, ClampW or wind).  The state at the
 // start of every chunk is the checkpoint, stored row-major in fp32.
 //
-// Backward (scan_bwd_kernel): one cluster of two 128-thread CTAs per chain,
-// each owning 32 rows of dS (row i = 32 rank + tid/4, column quarter q =
-// tid%4), walking chunks in reverse.  Each chunk's states are recomputed
+// Backward (scan_bwd_kernel): one cluster of two 256-thread CTAs per chain,
+// each owning 32 rows of dS (row i = 32 rank + tid/8, eight columns 8q..8q+7
+// with q = tid%8), walking chunks in reverse.  Each chunk's states are recomputed
 // forward from its checkpoint into shared memory (two halves of 8 steps so 9
 // states fit), never reversed through 1/w as camoe/cuda/rwkv7_clampw.cu:133
 // does.  Per step the row sums (dsa = dS b, dv = dS k) use shuffles; the five
 // column sums over the rows (dr, dw, dk, db, da) use a shuffle reduce-scatter
-// over the 8 rows of a warp and a shared-memory pass over the 4 warps, and the
+// over the 4 rows of a warp and a shared-memory pass over the 8 warps, and the
 // two CTAs' sums are added once per chunk through distributed shared memory.
 // The per-element formulas are those of camoe/cuda/rwkv7_clampw.cu:123-168,
 // plus the external sa-gradient.
@@ -31,7 +32,9 @@ namespace camoe {
 namespace scan {
 
 constexpr int kRows = 16;                 // forward: state rows per CTA
-constexpr int kFwdThreads = kRows * 4;    // forward: 4 threads per row
+constexpr int kFwdTpr = 8;                // forward: threads per row (8 columns each)
+constexpr int kFwdCols = kN / kFwdTpr;
+constexpr int kFwdThreads = kRows * kFwdTpr;
 constexpr int kRowGroups = kN / kRows;    // forward: CTAs per chain
 constexpr int kHalf = kChunk / 2;         // backward: states held per half chunk
 
@@ -68,27 +71,35 @@ __device__ __forceinline__ void fwd_issue(FwdSmem<Tin>& sm, int buf, const FwdAr
   }
 }
 
+// sum over the TPR threads of a row (the low lane bits)
+template <int TPR>
+__device__ __forceinline__ float row_sum(float x) {
+#pragma unroll
+  for (int d = 1; d < TPR; d <<= 1) x += __shfl_xor_sync(0xffffffffu, x, d);
+  return x;
+}
+
 template <typename Tin>
 __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   FwdSmem<Tin>& sm = *reinterpret_cast<FwdSmem<Tin>*>(smem_raw);
-  const int tid = threadIdx.x, rl = tid >> 2, q = tid & 3;
+  const int tid = threadIdx.x, rl = tid / kFwdTpr, q = tid % kFwdTpr;
   const int64_t ch = blockIdx.x / kRowGroups;
   const int rg = blockIdx.x % kRowGroups;
   const int i = rg * kRows + rl;
   const int64_t nchunk = p.g.nchunk;
 
-  float S[16];
-  if (p.s0 != nullptr) {  // start state: row i, columns 16q..16q+15
-    const float4* src = reinterpret_cast<const float4*>(p.s0 + p.g.state_off(ch) + i * kN + q * 16);
+  float S[kFwdCols];
+  if (p.s0 != nullptr) {  // start state: row i, columns 8q..8q+7
+    const float4* src = reinterpret_cast<const float4*>(p.s0 + p.g.state_off(ch) + i * kN + q * kFwdCols);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
+    for (int m = 0; m < kFwdCols / 4; ++m) {
       const float4 x = src[m];
       S[4 * m] = x.x; S[4 * m + 1] = x.y; S[4 * m + 2] = x.z; S[4 * m + 3] = x.w;
     }
   } else {
 #pragma unroll
-    for (int jj = 0; jj < 16; ++jj) S[jj] = 0.f;
+    for (int jj = 0; jj < kFwdCols; ++jj) S[jj] = 0.f;
   }
 
   fwd_issue(sm, 0, p, ch, 0, rg);
@@ -115,32 +126,31 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
     __syncthreads();
 
     if (p.ckpt != nullptr && c > 0) {
-      float4* dst = reinterpret_cast<float4*>(p.ckpt + ((ch * nchunk + c) * kN + i) * kN + q * 16);
+      float4* dst = reinterpret_cast<float4*>(p.ckpt + ((ch * nchunk + c) * kN + i) * kN + q * kFwdCols);
 #pragma unroll
-      for (int m = 0; m < 4; ++m) dst[m] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+      for (int m = 0; m < kFwdCols / 4; ++m)
+        dst[m] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
     }
 
 #pragma unroll 1
     for (int u = 0; u < nu; ++u) {
-      const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * 16]);
+      const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * kFwdCols]);
       float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-      for (int m = 0; m < 4; m += 2) {
+      for (int m = 0; m < kFwdCols / 4; m += 2) {
         const float4 x = a4[m], z = a4[m + 1];
         s0 += S[4 * m] * x.x + S[4 * m + 1] * x.y + S[4 * m + 2] * x.z + S[4 * m + 3] * x.w;
         s1 += S[4 * m + 4] * z.x + S[4 * m + 5] * z.y + S[4 * m + 6] * z.z + S[4 * m + 7] * z.w;
       }
-      float sa = s0 + s1;
-      sa += __shfl_xor_sync(0xffffffffu, sa, 1);
-      sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+      const float sa = row_sum<kFwdTpr>(s0 + s1);
       const float vi = sm.v[u][rl];
-      const float4* w4 = reinterpret_cast<const float4*>(&sm.w[u][q * 16]);
-      const float4* b4 = reinterpret_cast<const float4*>(&sm.b[u][q * 16]);
-      const float4* k4 = reinterpret_cast<const float4*>(&sm.k[u][q * 16]);
-      const float4* r4 = reinterpret_cast<const float4*>(&sm.r[u][q * 16]);
+      const float4* w4 = reinterpret_cast<const float4*>(&sm.w[u][q * kFwdCols]);
+      const float4* b4 = reinterpret_cast<const float4*>(&sm.b[u][q * kFwdCols]);
+      const float4* k4 = reinterpret_cast<const float4*>(&sm.k[u][q * kFwdCols]);
+      const float4* r4 = reinterpret_cast<const float4*>(&sm.r[u][q * kFwdCols]);
       float y0 = 0.f, y1 = 0.f;
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
+      for (int m = 0; m < kFwdCols / 4; ++m) {
         const float4 wv = w4[m], bv = b4[m], kv = k4[m], rv = r4[m];
         const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
         const float ka[4] = {kv.x, kv.y, kv.z, kv.w}, ra[4] = {rv.x, rv.y, rv.z, rv.w};
@@ -151,17 +161,15 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
           if (e & 1) y1 += s * ra[e]; else y0 += s * ra[e];
         }
       }
-      float y = y0 + y1;
-      y += __shfl_xor_sync(0xffffffffu, y, 1);
-      y += __shfl_xor_sync(0xffffffffu, y, 2);
+      const float y = row_sum<kFwdTpr>(y0 + y1);
       if (q == 0) {
         sm.y[u][rl] = y;
         sm.sa[u][rl] = sa;
       }
     }
     __syncthreads();
-    // write y, sa of this chunk: thread -> (step u, 4 consecutive rows)
-    {
+    // write y, sa of this chunk: thread -> (step u, 4 consecutive rows), 16 x 4 of them
+    if (tid < kChunk * (kRows / 4)) {
       const int u = tid >> 2, part = tid & 3;
       const int64_t t = c * kChunk + u;
       if (t < p.g.T) {
@@ -175,9 +183,10 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
     }
   }
   if (p.sT != nullptr) {
-    float4* dst = reinterpret_cast<float4*>(p.sT + p.g.state_off(ch) + i * kN + q * 16);
+    float4* dst = reinterpret_cast<float4*>(p.sT + p.g.state_off(ch) + i * kN + q * kFwdCols);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) dst[m] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+    for (int m = 0; m < kFwdCols / 4; ++m)
+      dst[m] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
   }
 }
 
@@ -342,7 +351,7 @@ __global__ void __launch_bounds__(kStepThreads, 8) step_fwd_kernel(FwdArgs p) {
 // cluster of two CTAs of 32 rows: 128 CTAs for the 64 chains of a 4-sequence
 // shard instead of 64.  Every per-step output indexed by the key column j (dr,
 // dw, dk, db, da) is a sum over all 64 rows: each CTA forms the sum over its
-// own 32 rows per step (warp shuffles, then shared memory over its 4 warps)
+// own 32 rows per step (warp shuffles, then shared memory over its 8 warps)
 // into a partial-sum buffer, and once per chunk, after a cluster barrier, each
 // CTA adds its peer's partials for its half of the columns (read through
 // distributed shared memory) and writes the outputs.  The partial buffers are
@@ -350,14 +359,21 @@ __global__ void __launch_bounds__(kStepThreads, 8) step_fwd_kernel(FwdArgs p) {
 // buffer from being refilled while the peer still reads it.  dv (a sum over
 // j, within a row) needs no exchange.
 
-// ROWS = 32: a cluster of two CTAs per chain; ROWS = 64: one CTA per chain
-// (taken when two CTAs per chain would not fit the SMs in one wave).
+// ROWS = 32: a cluster of two CTAs per chain, eight threads per row (8
+// columns each): 16 warps per chain, so that every SMSP has two warps of the
+// latency-bound step loop to switch between, and the per-step partial sums
+// double-buffered (one block barrier per step).  ROWS = 64: one CTA per chain
+// (taken when two CTAs per chain would not fit the SMs in one wave), four
+// threads per row and one partial-sum buffer, to fit its shared memory.
 template <int ROWS>
 struct BwdCfg {
   static constexpr int kCtas = kN / ROWS;        // CTAs per chain (one cluster)
-  static constexpr int kThreads = ROWS * 4;      // 4 threads per row
+  static constexpr int kTpr = ROWS == 32 ? 8 : 4;   // threads per state row
+  static constexpr int kCols = kN / kTpr;           // columns per thread
+  static constexpr int kThreads = ROWS * kTpr;
   static constexpr int kWarps = kThreads / 32;
-  static constexpr int kParts = kCtas > 1 ? 2 : 1;  // partial-sum buffers (by chunk parity)
+  static constexpr int kRed = ROWS == 32 ? 2 : 1;   // per-step partial-sum buffers
+  static constexpr int kParts = kCtas > 1 ? 2 : 1;  // per-chunk partial-sum buffers (by parity)
 };
 
 template <int ROWS>
@@ -365,19 +381,26 @@ struct BwdSmem {
   float S[kHalf + 1][ROWS][kN];  // own rows' states of one half chunk, columns xor-swizzled by row
   float r[kChunk][kN], w[kChunk][kN], dlw[kChunk][kN], k[kChunk][kN], a[kChunk][kN], b[kChunk][kN];
   float v[kChunk][ROWS], dy[kChunk][ROWS], dsa[kChunk][ROWS], sa[kChunk][ROWS];
-  float red[BwdCfg<ROWS>::kWarps][320];           // per-warp partial column sums of one step
+  // per-warp partial column sums of one step (with two buffers, by step parity)
+  float red[BwdCfg<ROWS>::kRed][BwdCfg<ROWS>::kWarps][320];
   float part[BwdCfg<ROWS>::kParts][5][kChunk][kN];  // own rows' column sums (dr, dw, dk, db, da)
   float dv[kChunk][ROWS];                          // dv of the own rows
 };
 
+// both fit the 227 KB of dynamic shared memory a CTA may have
+static_assert(sizeof(BwdSmem<32>) <= 227 * 1024 && sizeof(BwdSmem<64>) <= 227 * 1024,
+              "scan backward shared memory");
+
 // physical column of element (i, j) in BwdSmem::S (keeps 4-column groups contiguous)
 __device__ __forceinline__ int swz(int i, int j) { return j ^ ((i & 7) << 2); }
 
+// A chunk's inputs in 16-byte pieces: r, w, k, a, b as 16 steps x 16 groups of
+// 4 columns (threads tid < 256 take one group), v, dy, dsa as 16 steps x
+// ROWS / 4 groups of 4 own rows (threads tid < 4 ROWS take one).
 template <typename Tin, int ROWS>
-struct Prefetch {  // one thread's share of a chunk's inputs
-  static constexpr int kC = 256 / (4 * ROWS);  // column slots per thread (16 steps x 16 groups)
-  float4 c[5][kC];   // r, w, k, a, b: steps u + (ROWS / 4) h, columns 4 jq .. 4 jq + 3
-  float4 o[3];       // v, dy, dsa: step u2, own rows 4 iq .. 4 iq + 3
+struct Prefetch {
+  float4 c[5];  // r, w, k, a, b of the thread's column group
+  float4 o[3];  // v, dy, dsa of the thread's row group
 };
 
 template <typename Tin>
@@ -398,33 +421,33 @@ template <typename Tin, int ROWS>
 __device__ __forceinline__ void bwd_prefetch(Prefetch<Tin, ROWS>& pf, const BwdArgs& p, int64_t ch,
                                              int64_t c, int row0) {
   const int tid = threadIdx.x;
-  const void* src[5] = {p.r, p.w, p.k, p.a, p.b};
-#pragma unroll
-  for (int h = 0; h < Prefetch<Tin, ROWS>::kC; ++h) {
-    const int u = (tid >> 4) + (ROWS / 4) * h, j = (tid & 15) * 4;
+  if (tid < 256) {
+    const int u = tid >> 4, j = (tid & 15) * 4;
     const int64_t t = c * kChunk + u;
     const bool ok = t < p.g.T;
     const int64_t o = ok ? p.g.off(ch, t, j) : 0;
+    const void* src[5] = {p.r, p.w, p.k, p.a, p.b};
 #pragma unroll
-    for (int n = 0; n < 5; ++n) pf.c[n][h] = load4<Tin>(src[n], o, ok);
+    for (int n = 0; n < 5; ++n) pf.c[n] = load4<Tin>(src[n], o, ok);
   }
-  const int u2 = tid / (ROWS / 4), i4 = row0 + (tid % (ROWS / 4)) * 4;
-  const int64_t t2 = c * kChunk + u2;
-  const bool ok2 = t2 < p.g.T;
-  const int64_t o2 = ok2 ? p.g.off(ch, t2, i4) : 0;
-  pf.o[0] = load4<Tin>(p.v, o2, ok2);
-  pf.o[1] = load4<Tin>(p.dy, o2, ok2);
-  pf.o[2] = (p.dsa != nullptr) ? load4<float>(p.dsa, o2, ok2) : make_float4(0.f, 0.f, 0.f, 0.f);
+  if (tid < 4 * ROWS) {
+    const int u2 = tid / (ROWS / 4), i4 = row0 + (tid % (ROWS / 4)) * 4;
+    const int64_t t2 = c * kChunk + u2;
+    const bool ok2 = t2 < p.g.T;
+    const int64_t o2 = ok2 ? p.g.off(ch, t2, i4) : 0;
+    pf.o[0] = load4<Tin>(p.v, o2, ok2);
+    pf.o[1] = load4<Tin>(p.dy, o2, ok2);
+    pf.o[2] = (p.dsa != nullptr) ? load4<float>(p.dsa, o2, ok2) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 }
 
 template <typename Tin, int ROWS>
 __device__ __forceinline__ void bwd_stage(BwdSmem<ROWS>& sm, const Prefetch<Tin, ROWS>& pf, int kind) {
   const int tid = threadIdx.x;
-#pragma unroll
-  for (int h = 0; h < Prefetch<Tin, ROWS>::kC; ++h) {
-    const int u = (tid >> 4) + (ROWS / 4) * h, j = (tid & 15) * 4;
-    *reinterpret_cast<float4*>(&sm.r[u][j]) = pf.c[0][h];
-    const float wi[4] = {pf.c[1][h].x, pf.c[1][h].y, pf.c[1][h].z, pf.c[1][h].w};
+  if (tid < 256) {
+    const int u = tid >> 4, j = (tid & 15) * 4;
+    *reinterpret_cast<float4*>(&sm.r[u][j]) = pf.c[0];
+    const float wi[4] = {pf.c[1].x, pf.c[1].y, pf.c[1].z, pf.c[1].w};
     float dl[4], wd[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -434,36 +457,37 @@ __device__ __forceinline__ void bwd_stage(BwdSmem<ROWS>& sm, const Prefetch<Tin,
     }
     *reinterpret_cast<float4*>(&sm.dlw[u][j]) = make_float4(dl[0], dl[1], dl[2], dl[3]);
     *reinterpret_cast<float4*>(&sm.w[u][j]) = make_float4(wd[0], wd[1], wd[2], wd[3]);
-    *reinterpret_cast<float4*>(&sm.k[u][j]) = pf.c[2][h];
-    *reinterpret_cast<float4*>(&sm.a[u][j]) = pf.c[3][h];
-    *reinterpret_cast<float4*>(&sm.b[u][j]) = pf.c[4][h];
+    *reinterpret_cast<float4*>(&sm.k[u][j]) = pf.c[2];
+    *reinterpret_cast<float4*>(&sm.a[u][j]) = pf.c[3];
+    *reinterpret_cast<float4*>(&sm.b[u][j]) = pf.c[4];
   }
-  const int u2 = tid / (ROWS / 4), il4 = (tid % (ROWS / 4)) * 4;
-  *reinterpret_cast<float4*>(&sm.v[u2][il4]) = pf.o[0];
-  *reinterpret_cast<float4*>(&sm.dy[u2][il4]) = pf.o[1];
-  *reinterpret_cast<float4*>(&sm.dsa[u2][il4]) = pf.o[2];
+  if (tid < 4 * ROWS) {
+    const int u2 = tid / (ROWS / 4), il4 = (tid % (ROWS / 4)) * 4;
+    *reinterpret_cast<float4*>(&sm.v[u2][il4]) = pf.o[0];
+    *reinterpret_cast<float4*>(&sm.dy[u2][il4]) = pf.o[1];
+    *reinterpret_cast<float4*>(&sm.dsa[u2][il4]) = pf.o[2];
+  }
 }
 
-// one forward step of own row il (columns q*16..q*16+15); returns sa of the row
+// one forward step of own row il (its kCols columns from q*kCols); returns sa of the row
 template <int ROWS>
 __device__ __forceinline__ float fwd_step(const BwdSmem<ROWS>& sm, int u, int il, int q, float* S) {
-  const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * 16]);
+  constexpr int kCols = BwdCfg<ROWS>::kCols;
+  const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * kCols]);
   float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-  for (int m = 0; m < 4; m += 2) {
+  for (int m = 0; m < kCols / 4; m += 2) {
     const float4 x = a4[m], z = a4[m + 1];
     s0 += S[4 * m] * x.x + S[4 * m + 1] * x.y + S[4 * m + 2] * x.z + S[4 * m + 3] * x.w;
     s1 += S[4 * m + 4] * z.x + S[4 * m + 5] * z.y + S[4 * m + 6] * z.z + S[4 * m + 7] * z.w;
   }
-  float sa = s0 + s1;
-  sa += __shfl_xor_sync(0xffffffffu, sa, 1);
-  sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+  const float sa = row_sum<BwdCfg<ROWS>::kTpr>(s0 + s1);
   const float vi = sm.v[u][il];
 #pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const float4 wv = reinterpret_cast<const float4*>(&sm.w[u][q * 16])[m];
-    const float4 bv = reinterpret_cast<const float4*>(&sm.b[u][q * 16])[m];
-    const float4 kv = reinterpret_cast<const float4*>(&sm.k[u][q * 16])[m];
+  for (int m = 0; m < kCols / 4; ++m) {
+    const float4 wv = reinterpret_cast<const float4*>(&sm.w[u][q * kCols])[m];
+    const float4 bv = reinterpret_cast<const float4*>(&sm.b[u][q * kCols])[m];
+    const float4 kv = reinterpret_cast<const float4*>(&sm.k[u][q * kCols])[m];
     const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
     const float ka[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
@@ -474,17 +498,19 @@ __device__ __forceinline__ float fwd_step(const BwdSmem<ROWS>& sm, int u, int il
 
 template <int ROWS>
 __device__ __forceinline__ void store_state(BwdSmem<ROWS>& sm, int slot, int il, int q, const float* S) {
+  constexpr int kCols = BwdCfg<ROWS>::kCols;
 #pragma unroll
-  for (int m = 0; m < 4; ++m)
-    *reinterpret_cast<float4*>(&sm.S[slot][il][swz(il, q * 16 + 4 * m)]) =
+  for (int m = 0; m < kCols / 4; ++m)
+    *reinterpret_cast<float4*>(&sm.S[slot][il][swz(il, q * kCols + 4 * m)]) =
         make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
 }
 
 template <int ROWS>
 __device__ __forceinline__ void load_state(const BwdSmem<ROWS>& sm, int slot, int il, int q, float* S) {
+  constexpr int kCols = BwdCfg<ROWS>::kCols;
 #pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const float4 x = *reinterpret_cast<const float4*>(&sm.S[slot][il][swz(il, q * 16 + 4 * m)]);
+  for (int m = 0; m < kCols / 4; ++m) {
+    const float4 x = *reinterpret_cast<const float4*>(&sm.S[slot][il][swz(il, q * kCols + 4 * m)]);
     S[4 * m] = x.x; S[4 * m + 1] = x.y; S[4 * m + 2] = x.z; S[4 * m + 3] = x.w;
   }
 }
@@ -494,83 +520,82 @@ __device__ __forceinline__ void load_state(const BwdSmem<ROWS>& sm, int slot, in
 template <int ROWS>
 __device__ __forceinline__ void bwd_step(BwdSmem<ROWS>& sm, int u, int st, int sp, int il, int q,
                                          int lane, int warp, int pb, float* dS) {
-  float Sc[16], Sp[16];
+  using Cfg = BwdCfg<ROWS>;
+  constexpr int kCols = Cfg::kCols, kX = 5 * kCols;
+  // lane bits above the row's threads: rows of the warp (two or three levels)
+  constexpr int kLevels = Cfg::kTpr == 8 ? 2 : 3;
+  float Sc[kCols], Sp[kCols];
   load_state(sm, st, il, q, Sc);
   load_state(sm, sp, il, q, Sp);
   const float dyi = sm.dy[u][il], vi = sm.v[u][il], sai = sm.sa[u][il];
   float dsa0 = 0.f, dsa1 = 0.f, dv0 = 0.f, dv1 = 0.f;
 #pragma unroll
-  for (int jj = 0; jj < 16; ++jj) {
-    const int j = q * 16 + jj;
+  for (int jj = 0; jj < kCols; ++jj) {
+    const int j = q * kCols + jj;
     dS[jj] += dyi * sm.r[u][j];
     if (jj & 1) { dsa1 += dS[jj] * sm.b[u][j]; dv1 += dS[jj] * sm.k[u][j]; }
     else { dsa0 += dS[jj] * sm.b[u][j]; dv0 += dS[jj] * sm.k[u][j]; }
   }
-  float dsa = dsa0 + dsa1, dv = dv0 + dv1;
-  dsa += __shfl_xor_sync(0xffffffffu, dsa, 1);
-  dv += __shfl_xor_sync(0xffffffffu, dv, 1);
-  dsa += __shfl_xor_sync(0xffffffffu, dsa, 2);
-  dv += __shfl_xor_sync(0xffffffffu, dv, 2);
-  dsa += sm.dsa[u][il];
+  const float dsa = row_sum<Cfg::kTpr>(dsa0 + dsa1) + sm.dsa[u][il];
+  const float dv = row_sum<Cfg::kTpr>(dv0 + dv1);
 
-  float x[80];
+  float x[kX];
 #pragma unroll
-  for (int jj = 0; jj < 16; ++jj) {
-    x[jj] = Sc[jj] * dyi;          // dr
-    x[16 + jj] = dS[jj] * Sp[jj];  // dw (before the decay's chain factor)
-    x[32 + jj] = dS[jj] * vi;      // dk
-    x[48 + jj] = dS[jj] * sai;     // db
-    x[64 + jj] = dsa * Sp[jj];     // da
+  for (int jj = 0; jj < kCols; ++jj) {
+    x[jj] = Sc[jj] * dyi;                // dr
+    x[kCols + jj] = dS[jj] * Sp[jj];     // dw (before the decay's chain factor)
+    x[2 * kCols + jj] = dS[jj] * vi;     // dk
+    x[3 * kCols + jj] = dS[jj] * sai;    // db
+    x[4 * kCols + jj] = dsa * Sp[jj];    // da
   }
 #pragma unroll
-  for (int jj = 0; jj < 16; ++jj) {
-    const int j = q * 16 + jj;
+  for (int jj = 0; jj < kCols; ++jj) {
+    const int j = q * kCols + jj;
     dS[jj] = dS[jj] * sm.w[u][j] + dsa * sm.a[u][j];
   }
   if (q == 0) sm.dv[u][il] = dv;
 
-  // reduce-scatter the 80 partials over the 8 rows of this warp (lane bits 4,3,2)
-  const bool h4 = lane & 16, h3 = lane & 8, h2 = lane & 4;
+  // reduce-scatter the partials over the rows of this warp: at each level the
+  // lanes whose row bit is set keep the upper half of x, the others the lower
 #pragma unroll
-  for (int m = 0; m < 40; ++m) {
-    const float send = h4 ? x[m] : x[m + 40];
-    const float keep = h4 ? x[m + 40] : x[m];
-    x[m] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  for (int lv = 0; lv < kLevels; ++lv) {
+    const int bit = 16 >> lv, half = kX >> (lv + 1);
+    const bool hi = lane & bit;
+#pragma unroll
+    for (int m = 0; m < half; ++m) {
+      const float send = hi ? x[m] : x[m + half];
+      const float keep = hi ? x[m + half] : x[m];
+      x[m] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+    }
   }
+  float* red = sm.red[Cfg::kRed == 2 ? (u & 1) : 0][0];
 #pragma unroll
-  for (int m = 0; m < 20; ++m) {
-    const float send = h3 ? x[m] : x[m + 20];
-    const float keep = h3 ? x[m + 20] : x[m];
-    x[m] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-#pragma unroll
-  for (int m = 0; m < 10; ++m) {
-    const float send = h2 ? x[m] : x[m + 10];
-    const float keep = h2 ? x[m + 10] : x[m];
-    x[m] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-#pragma unroll
-  for (int s = 0; s < 10; ++s) sm.red[warp][lane * 10 + s] = x[s];
+  for (int s = 0; s < 10; ++s) red[warp * 320 + lane * 10 + s] = x[s];
   __syncthreads();
-  for (int pidx = threadIdx.x; pidx < 320; pidx += BwdCfg<ROWS>::kThreads) {
+  // lane ln = TPR rb + q holds 10 values m = s + sum over levels of the row
+  // bit times that level's half, of quantity m / kCols at column q kCols + m % kCols
+  for (int pidx = threadIdx.x; pidx < 320; pidx += Cfg::kThreads) {
     float acc = 0.f;
 #pragma unroll
-    for (int wv = 0; wv < BwdCfg<ROWS>::kWarps; ++wv) acc += sm.red[wv][pidx];
-    const int ln = pidx / 10, s = pidx % 10, qq = ln & 3, rb = ln >> 2;
-    const int m = 40 * ((rb >> 2) & 1) + 20 * ((rb >> 1) & 1) + 10 * (rb & 1) + s;
-    sm.part[pb][m >> 4][u][qq * 16 + (m & 15)] = acc;
+    for (int wv = 0; wv < Cfg::kWarps; ++wv) acc += red[wv * 320 + pidx];
+    const int ln = pidx / 10, qq = ln % Cfg::kTpr, rb = ln / Cfg::kTpr;
+    int m = pidx % 10;
+#pragma unroll
+    for (int lv = 0; lv < kLevels; ++lv) m += ((rb >> (kLevels - 1 - lv)) & 1) * (kX >> (lv + 1));
+    sm.part[pb][m / kCols][u][qq * kCols + m % kCols] = acc;
   }
-  __syncthreads();
+  if (Cfg::kRed == 1) __syncthreads();  // red is refilled by the next step
 }
 
 template <typename Tin, int ROWS>
 __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
     __launch_bounds__(BwdCfg<ROWS>::kThreads, 1) scan_bwd_kernel(BwdArgs p) {
   using Cfg = BwdCfg<ROWS>;
+  constexpr int kCols = Cfg::kCols;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BwdSmem<ROWS>& sm = *reinterpret_cast<BwdSmem<ROWS>*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
-  const int tid = threadIdx.x, il = tid >> 2, q = tid & 3, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, il = tid / Cfg::kTpr, q = tid % Cfg::kTpr, lane = tid & 31, warp = tid >> 5;
   // this CTA's rows, and the columns whose outputs it writes
   const int rank = Cfg::kCtas > 1 ? static_cast<int>(cluster.block_rank()) : 0;
   const int64_t ch = blockIdx.x / Cfg::kCtas;
@@ -579,17 +604,17 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
   // the peer's partial sums, in its shared memory (a cluster of two)
   const BwdSmem<ROWS>* peer = Cfg::kCtas > 1 ? cluster.map_shared_rank(&sm, rank ^ 1) : nullptr;
 
-  float dS[16], S0[16], S[16];
+  float dS[kCols], S0[kCols], S[kCols];
   if (p.dsT != nullptr) {  // the gradient of the final state enters at the last step
-    const float4* src = reinterpret_cast<const float4*>(p.dsT + p.g.state_off(ch) + i * kN + q * 16);
+    const float4* src = reinterpret_cast<const float4*>(p.dsT + p.g.state_off(ch) + i * kN + q * kCols);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
+    for (int m = 0; m < kCols / 4; ++m) {
       const float4 x = src[m];
       dS[4 * m] = x.x; dS[4 * m + 1] = x.y; dS[4 * m + 2] = x.z; dS[4 * m + 3] = x.w;
     }
   } else {
 #pragma unroll
-    for (int jj = 0; jj < 16; ++jj) dS[jj] = 0.f;
+    for (int jj = 0; jj < kCols; ++jj) dS[jj] = 0.f;
   }
 
   Prefetch<Tin, ROWS> pf;
@@ -600,28 +625,28 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
     bwd_stage<Tin, ROWS>(sm, pf, p.g.decay);
     if (c > 0) bwd_prefetch<Tin, ROWS>(pf, p, ch, c - 1, row0);
     if (c > 0) {
-      const float4* src = reinterpret_cast<const float4*>(p.ckpt + ((ch * nchunk + c) * kN + i) * kN + q * 16);
+      const float4* src = reinterpret_cast<const float4*>(p.ckpt + ((ch * nchunk + c) * kN + i) * kN + q * kCols);
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
+      for (int m = 0; m < kCols / 4; ++m) {
         const float4 x = src[m];
         S0[4 * m] = x.x; S0[4 * m + 1] = x.y; S0[4 * m + 2] = x.z; S0[4 * m + 3] = x.w;
       }
     } else if (p.s0 != nullptr) {  // chunk 0 starts from the state carried in
-      const float4* src = reinterpret_cast<const float4*>(p.s0 + p.g.state_off(ch) + i * kN + q * 16);
+      const float4* src = reinterpret_cast<const float4*>(p.s0 + p.g.state_off(ch) + i * kN + q * kCols);
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
+      for (int m = 0; m < kCols / 4; ++m) {
         const float4 x = src[m];
         S0[4 * m] = x.x; S0[4 * m + 1] = x.y; S0[4 * m + 2] = x.z; S0[4 * m + 3] = x.w;
       }
     } else {
 #pragma unroll
-      for (int jj = 0; jj < 16; ++jj) S0[jj] = 0.f;
+      for (int jj = 0; jj < kCols; ++jj) S0[jj] = 0.f;
     }
     __syncthreads();
 
     // second half: advance to the middle, keep states of steps kHalf..kChunk-1
 #pragma unroll
-    for (int jj = 0; jj < 16; ++jj) S[jj] = S0[jj];
+    for (int jj = 0; jj < kCols; ++jj) S[jj] = S0[jj];
 #pragma unroll 1
     for (int u = 0; u < kHalf; ++u) {
       const float sa = fwd_step(sm, u, il, q, S);
@@ -641,7 +666,7 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
 
     // first half
 #pragma unroll
-    for (int jj = 0; jj < 16; ++jj) S[jj] = S0[jj];
+    for (int jj = 0; jj < kCols; ++jj) S[jj] = S0[jj];
     store_state(sm, 0, il, q, S);
 #pragma unroll 1
     for (int u = 0; u < kHalf; ++u) {
@@ -653,8 +678,8 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
     for (int u = kHalf - 1; u >= 0; --u) bwd_step(sm, u, u + 1, u, il, q, lane, warp, pb, dS);
 
     // both CTAs' column sums of this chunk are complete (and visible across the
-    // cluster); with one CTA per chain the block barrier of the last step suffices
-    if (Cfg::kCtas > 1) cluster.sync();
+    // cluster; with one CTA per chain, across the CTA)
+    if (Cfg::kCtas > 1) cluster.sync(); else __syncthreads();
     // this CTA writes the columns [ROWS rank, ROWS rank + ROWS): thread -> (tensor, step, 4 columns)
     for (int idx = tid; idx < 5 * kChunk * (ROWS / 4); idx += Cfg::kThreads) {
       const int tens = idx / (kChunk * (ROWS / 4)), rem = idx % (kChunk * (ROWS / 4));
@@ -676,7 +701,7 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[e] = from_f32<Tin>(s[e]);
     }
-    {  // dv of the own rows: thread -> (step, 4 rows)
+    if (tid < 4 * ROWS) {  // dv of the own rows: thread -> (step, 4 rows), 16 x ROWS / 4 of them
       const int u = tid / (ROWS / 4), j = (tid % (ROWS / 4)) * 4;
       const int64_t t = c * kChunk + u;
       if (t < p.g.T) {
@@ -687,9 +712,9 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
     }
   }
   if (p.ds0 != nullptr) {  // after chunk 0, dS is the gradient of the start state
-    float4* dst = reinterpret_cast<float4*>(p.ds0 + p.g.state_off(ch) + i * kN + q * 16);
+    float4* dst = reinterpret_cast<float4*>(p.ds0 + p.g.state_off(ch) + i * kN + q * kCols);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) dst[m] = make_float4(dS[4 * m], dS[4 * m + 1], dS[4 * m + 2], dS[4 * m + 3]);
+    for (int m = 0; m < kCols / 4; ++m) dst[m] = make_float4(dS[4 * m], dS[4 * m + 1], dS[4 * m + 2], dS[4 * m + 3]);
   }
   // the peer may still be reading this CTA's partial sums of the last chunk
   if (Cfg::kCtas > 1) cluster.sync();
@@ -723,7 +748,7 @@ cudaError_t launch_bwd_rows(const BwdArgs& p, cudaStream_t stream) {
 }
 
 // Two 32-row CTAs per chain while they fit the SMs in one wave (a CTA holds
-// an SM: 151 KB of shared memory), else one 64-row CTA per chain.
+// an SM: 166 KB of shared memory), else one 64-row CTA per chain.
 template <typename Tin>
 cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream) {
   int dev = 0, sms = 148;
