@@ -12,10 +12,11 @@
 // (dll is d(lam) * lam: lam scales the chunk's end state S').
 //
 // value_bwd_kernel (chunks in reverse, one to four CTAs per chain): carries G
-// through the recurrence, writing dv and, per chunk, a rec::XRec (bf16 S, G'',
-// SA^T, dSA^T) to the workspace; the state at the start of every chunk comes
-// from the checkpoint (even chunks) or is recomputed from the preceding even
-// chunk (odd chunks).
+// through the recurrence, writing dv and, per chunk, a rec::XRec (bf16 G'',
+// SA^T, dSA^T, and the start state S where the forward checkpoint lacks it)
+// to the workspace; the state at the start of every chunk comes from the
+// checkpoint (even chunks) or is recomputed from the preceding even chunk
+// (odd chunks).
 //
 // keyside_bwd_kernel (chunk-parallel, every SM): forms the row sums above from
 // the chunk's XRec and its v, dy tiles, recomputes the decays and W, Q from
@@ -59,8 +60,10 @@ namespace vb {
 //               loads; no fences, no output stores;
 //   dV warp     reads them, forms dV and stages dv and the G'', dSA^T rows of
 //               the chunk's XRec;
-//   state warp  start states (checkpointed or recomputed), SA; stages the S
-//               and SA^T rows of the XRec.
+//   state warp  start states (checkpointed or recomputed), SA; stages the
+//               SA^T rows of the XRec and, for chunks 0, 1 and the odd ones,
+//               its S rows (the key-side backward reads the other chunks'
+//               start states from the forward checkpoint).
 // A producer warp streams the inputs and a store warp writes the staged rows
 // and the dv tile with bulk copies, KEEP groups in flight.
 constexpr int NX = 4;    // output stages (power of two)

@@ -44,7 +44,9 @@ static_assert(sizeof(TriRec) == 2624, "TriRec layout");
 
 // What the value-side backward hands to the key-side backward for one chunk:
 // bf16 copies of the chunk's start state S, of G'' = dL/dS' diag(lam), of SA^T
-// and dSA^T (rows = state row i).
+// and dSA^T (rows = state row i).  S is written only for chunks 0, 1 and the
+// odd chunks; for even chunks from 2 on the space stays unwritten and the
+// reader takes the start state from the forward's state checkpoint instead.
 struct XRec {
   bf16 S[64 * 64];     // Swz64 layout over 64 rows
   bf16 G[64 * 64];     // Swz64

@@ -14,9 +14,10 @@
 // Backward (scan_bwd_kernel): one cluster of two 256-thread CTAs per chain,
 // each owning 32 rows of dS (row i = 32 rank + tid/8, eight columns 8q..8q+7
 // with q = tid%8), walking chunks in reverse.  Each chunk's states are recomputed
-// forward from its checkpoint into shared memory (two halves of 8 steps so 9
-// states fit), never reversed through 1/w as camoe/cuda/rwkv7_clampw.cu:133
-// does.  Per step the row sums (dsa = dS b, dv = dS k) use shuffles; the five
+// forward from its checkpoint into shared memory (all 16 in one pass; with one
+// 64-row CTA per chain, two halves of 8 steps so 9 states fit), never reversed
+// through 1/w as camoe/cuda/rwkv7_clampw.cu:133 does.  Per step the row sums
+// (dsa = dS b, dv = dS k) use shuffles; the five
 // column sums over the rows (dr, dw, dk, db, da) use a shuffle reduce-scatter
 // over the 4 rows of a warp and a shared-memory pass over the 8 warps, and the
 // two CTAs' sums are added once per chunk through distributed shared memory.
@@ -35,6 +36,7 @@ constexpr int kRows = 16;                 // forward: state rows per CTA
 constexpr int kFwdTpr = 8;                // forward: threads per row (8 columns each)
 constexpr int kFwdCols = kN / kFwdTpr;
 constexpr int kFwdThreads = kRows * kFwdTpr;
+static_assert(kFwdCols == 8, "dot8 and the group flip take eight columns per thread");
 constexpr int kRowGroups = kN / kRows;    // forward: CTAs per chain
 constexpr int kHalf = kChunk / 2;         // backward: states held per half chunk
 
@@ -47,27 +49,28 @@ struct FwdSmem {
   float y[kChunk][kRows], sa[kChunk][kRows];
 };
 
+// one chunk's copies, element (t, j) of the chain at cb + t * ts + j
 template <typename Tin>
-__device__ __forceinline__ void fwd_issue(FwdSmem<Tin>& sm, int buf, const FwdArgs& p,
-                                          int64_t ch, int64_t c, int rg) {
+__device__ __forceinline__ void fwd_issue(FwdSmem<Tin>& sm, int buf, const FwdArgs& p, int64_t cb,
+                                          int64_t ts, int64_t c, int rg) {
   constexpr int V = 16 / sizeof(Tin);  // elements per 16-byte copy
   constexpr int PR = kN / V;           // copies per 64-wide row
   constexpr int VR = kRows / V;        // copies per v slice row
   const int64_t t0 = c * kChunk;
-  for (int idx = threadIdx.x; idx < 5 * kChunk * PR; idx += kFwdThreads) {
-    const int tens = idx / (kChunk * PR), rem = idx % (kChunk * PR);
-    const int u = rem / PR, part = rem % PR;
-    const Tin* src = static_cast<const Tin*>(tens == 0 ? p.r : tens == 1 ? p.w : tens == 2 ? p.k
-                                             : tens == 3 ? p.a : p.b);
+  const Tin* src[5] = {static_cast<const Tin*>(p.r), static_cast<const Tin*>(p.w), static_cast<const Tin*>(p.k),
+                       static_cast<const Tin*>(p.a), static_cast<const Tin*>(p.b)};
+  for (int idx = threadIdx.x; idx < kChunk * PR; idx += kFwdThreads) {
+    const int u = idx / PR, part = idx % PR;
     const bool ok = t0 + u < p.g.T;
-    cp_async16(&sm.raw[buf][tens][u][part * V], src + (ok ? p.g.off(ch, t0 + u, part * V) : 0), ok);
+    const int64_t o = ok ? cb + (t0 + u) * ts + part * V : 0;
+#pragma unroll
+    for (int tens = 0; tens < 5; ++tens) cp_async16(&sm.raw[buf][tens][u][part * V], src[tens] + o, ok);
   }
   for (int idx = threadIdx.x; idx < kChunk * VR; idx += kFwdThreads) {
     const int u = idx / VR, part = idx % VR;
     const bool ok = t0 + u < p.g.T;
-    const Tin* src = static_cast<const Tin*>(p.v);
-    cp_async16(&sm.rawv[buf][u][part * V],
-               src + (ok ? p.g.off(ch, t0 + u, rg * kRows + part * V) : 0), ok);
+    const int64_t o = ok ? cb + (t0 + u) * ts + rg * kRows + part * V : 0;
+    cp_async16(&sm.rawv[buf][u][part * V], static_cast<const Tin*>(p.v) + o, ok);
   }
 }
 
@@ -79,22 +82,40 @@ __device__ __forceinline__ float row_sum(float x) {
   return x;
 }
 
+// this thread's part of a row dot product: its kFwdCols state columns times a
+// shared-memory row segment (two FMA chains).  Register group m holds column
+// group m ^ sw, sw = 1 for the upper four threads of a row, so that the eight
+// threads of a row (a quarter warp) read eight different bank groups.
+__device__ __forceinline__ float dot8(const float (&S)[kFwdCols], const float* x, int sw) {
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int m = 0; m < kFwdCols / 4; m += 2) {
+    const float4 e = x4[m ^ sw], f = x4[(m + 1) ^ sw];
+    s0 += S[4 * m] * e.x + S[4 * m + 1] * e.y + S[4 * m + 2] * e.z + S[4 * m + 3] * e.w;
+    s1 += S[4 * m + 4] * f.x + S[4 * m + 5] * f.y + S[4 * m + 6] * f.z + S[4 * m + 7] * f.w;
+  }
+  return s0 + s1;
+}
+
 template <typename Tin>
 __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   FwdSmem<Tin>& sm = *reinterpret_cast<FwdSmem<Tin>*>(smem_raw);
   const int tid = threadIdx.x, rl = tid / kFwdTpr, q = tid % kFwdTpr;
+  const int sw = q >= kFwdTpr / 2 ? 1 : 0;  // register group m = column group m ^ sw
   const int64_t ch = blockIdx.x / kRowGroups;
   const int rg = blockIdx.x % kRowGroups;
   const int i = rg * kRows + rl;
   const int64_t nchunk = p.g.nchunk;
+  const int64_t cb = p.g.base(ch), ts = p.g.tstride();
 
   float S[kFwdCols];
   if (p.s0 != nullptr) {  // start state: row i, columns 8q..8q+7
     const float4* src = reinterpret_cast<const float4*>(p.s0 + p.g.state_off(ch) + i * kN + q * kFwdCols);
 #pragma unroll
     for (int m = 0; m < kFwdCols / 4; ++m) {
-      const float4 x = src[m];
+      const float4 x = src[m ^ sw];
       S[4 * m] = x.x; S[4 * m + 1] = x.y; S[4 * m + 2] = x.z; S[4 * m + 3] = x.w;
     }
   } else {
@@ -102,14 +123,14 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
     for (int jj = 0; jj < kFwdCols; ++jj) S[jj] = 0.f;
   }
 
-  fwd_issue(sm, 0, p, ch, 0, rg);
+  fwd_issue(sm, 0, p, cb, ts, 0, rg);
   cp_async_commit();
   for (int64_t c = 0; c < nchunk; ++c) {
     const int buf = c & 1;
     // steps of this chunk inside the sequence (the rest are never applied,
     // so the final state is the state after step T - 1)
     const int nu = p.g.T - c * kChunk < kChunk ? static_cast<int>(p.g.T - c * kChunk) : kChunk;
-    if (c + 1 < nchunk) fwd_issue(sm, buf ^ 1, p, ch, c + 1, rg);
+    if (c + 1 < nchunk) fwd_issue(sm, buf ^ 1, p, cb, ts, c + 1, rg);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
@@ -129,43 +150,43 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
       float4* dst = reinterpret_cast<float4*>(p.ckpt + ((ch * nchunk + c) * kN + i) * kN + q * kFwdCols);
 #pragma unroll
       for (int m = 0; m < kFwdCols / 4; ++m)
-        dst[m] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+        dst[m ^ sw] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
     }
 
+    // y_u = S_u r_u and sa_{u+1} = S_u a_{u+1} both read only S_u, so their
+    // row sums run interleaved: one shuffle chain per step instead of two
+    // (sa holds the whole row's sum at the top of every step)
+    float sa = row_sum<kFwdTpr>(dot8(S, &sm.a[0][q * kFwdCols], sw));
 #pragma unroll 1
     for (int u = 0; u < nu; ++u) {
-      const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * kFwdCols]);
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int m = 0; m < kFwdCols / 4; m += 2) {
-        const float4 x = a4[m], z = a4[m + 1];
-        s0 += S[4 * m] * x.x + S[4 * m + 1] * x.y + S[4 * m + 2] * x.z + S[4 * m + 3] * x.w;
-        s1 += S[4 * m + 4] * z.x + S[4 * m + 5] * z.y + S[4 * m + 6] * z.z + S[4 * m + 7] * z.w;
-      }
-      const float sa = row_sum<kFwdTpr>(s0 + s1);
       const float vi = sm.v[u][rl];
       const float4* w4 = reinterpret_cast<const float4*>(&sm.w[u][q * kFwdCols]);
       const float4* b4 = reinterpret_cast<const float4*>(&sm.b[u][q * kFwdCols]);
       const float4* k4 = reinterpret_cast<const float4*>(&sm.k[u][q * kFwdCols]);
-      const float4* r4 = reinterpret_cast<const float4*>(&sm.r[u][q * kFwdCols]);
-      float y0 = 0.f, y1 = 0.f;
 #pragma unroll
       for (int m = 0; m < kFwdCols / 4; ++m) {
-        const float4 wv = w4[m], bv = b4[m], kv = k4[m], rv = r4[m];
+        const float4 wv = w4[m ^ sw], bv = b4[m ^ sw], kv = k4[m ^ sw];
         const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
-        const float ka[4] = {kv.x, kv.y, kv.z, kv.w}, ra[4] = {rv.x, rv.y, rv.z, rv.w};
+        const float ka[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float s = S[4 * m + e] * wa[e] + (sa * ba[e] + ka[e] * vi);
-          S[4 * m + e] = s;
-          if (e & 1) y1 += s * ra[e]; else y0 += s * ra[e];
-        }
+        for (int e = 0; e < 4; ++e) S[4 * m + e] = S[4 * m + e] * wa[e] + (sa * ba[e] + ka[e] * vi);
       }
-      const float y = row_sum<kFwdTpr>(y0 + y1);
+      // the last step of the chunk reads a row of a again (its sum is unused)
+      const int un = u + 1 < nu ? u + 1 : u;
+      float y = dot8(S, &sm.r[u][q * kFwdCols], sw);
+      float sn = dot8(S, &sm.a[un][q * kFwdCols], sw);
+#pragma unroll
+      for (int d = 1; d < kFwdTpr; d <<= 1) {
+        const float yo = __shfl_xor_sync(0xffffffffu, y, d);
+        const float so = __shfl_xor_sync(0xffffffffu, sn, d);
+        y += yo;
+        sn += so;
+      }
       if (q == 0) {
         sm.y[u][rl] = y;
         sm.sa[u][rl] = sa;
       }
+      sa = sn;
     }
     __syncthreads();
     // write y, sa of this chunk: thread -> (step u, 4 consecutive rows), 16 x 4 of them
@@ -173,7 +194,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
       const int u = tid >> 2, part = tid & 3;
       const int64_t t = c * kChunk + u;
       if (t < p.g.T) {
-        const int64_t o = p.g.off(ch, t, rg * kRows + part * 4);
+        const int64_t o = cb + t * ts + rg * kRows + part * 4;
         const float* ys = &sm.y[u][part * 4];
         Tin* yo = static_cast<Tin*>(p.y) + o;
 #pragma unroll
@@ -186,7 +207,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
     float4* dst = reinterpret_cast<float4*>(p.sT + p.g.state_off(ch) + i * kN + q * kFwdCols);
 #pragma unroll
     for (int m = 0; m < kFwdCols / 4; ++m)
-      dst[m] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+      dst[m ^ sw] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
   }
 }
 
@@ -374,11 +395,16 @@ struct BwdCfg {
   static constexpr int kWarps = kThreads / 32;
   static constexpr int kRed = ROWS == 32 ? 2 : 1;   // per-step partial-sum buffers
   static constexpr int kParts = kCtas > 1 ? 2 : 1;  // per-chunk partial-sum buffers (by parity)
+  // 32 rows: all 16 states of a chunk fit in shared memory (the 17th, the end
+  // state, stays in registers), one forward pass per chunk; 64 rows: two
+  // halves of 8 steps, 9 states each (24 forward steps per chunk)
+  static constexpr bool kWhole = ROWS == 32;
+  static constexpr int kSlots = kWhole ? kChunk : kHalf + 1;
 };
 
 template <int ROWS>
 struct BwdSmem {
-  float S[kHalf + 1][ROWS][kN];  // own rows' states of one half chunk, columns xor-swizzled by row
+  float S[BwdCfg<ROWS>::kSlots][ROWS][kN];  // own rows' states, in the threads' order (slot4)
   float r[kChunk][kN], w[kChunk][kN], dlw[kChunk][kN], k[kChunk][kN], a[kChunk][kN], b[kChunk][kN];
   float v[kChunk][ROWS], dy[kChunk][ROWS], dsa[kChunk][ROWS], sa[kChunk][ROWS];
   // per-warp partial column sums of one step (with two buffers, by step parity)
@@ -391,8 +417,42 @@ struct BwdSmem {
 static_assert(sizeof(BwdSmem<32>) <= 227 * 1024 && sizeof(BwdSmem<64>) <= 227 * 1024,
               "scan backward shared memory");
 
-// physical column of element (i, j) in BwdSmem::S (keeps 4-column groups contiguous)
-__device__ __forceinline__ int swz(int i, int j) { return j ^ ((i & 7) << 2); }
+// Column order of a thread's registers, and where its reduced column sums go.
+// The five column sums of a step are reduce-scattered over the rows of a warp
+// (the lane bits above a row's threads; 2 levels for 8 threads per row, 3 for
+// 4).  For the top log2(kCols / 4) levels a thread holds its 4-column groups in
+// an order permuted by its row bits (register group g holds column group
+// g ^ perm), so at those levels every lane keeps its first half of groups and
+// adds its partner's second half, which holds the same columns: no selects.
+// The last level splits the remaining 5 x 4 values by a select on the lane bit.
+// The upper half of a row's threads also flip the lowest group bit: the eight
+// lanes of a quarter warp then read a shared row's 16-byte pieces from eight
+// different bank groups (with the natural order, threads q and q + kTpr / 2 of
+// a row hit the same banks).  Partners share q, so the pairing is unchanged.
+template <int ROWS>
+struct Lanes {
+  using Cfg = BwdCfg<ROWS>;
+  static constexpr int kG = Cfg::kCols / 4;                 // 4-column groups per thread
+  static constexpr int kP = kG == 2 ? 1 : 2;                // select-free levels
+  static constexpr int kLevels = Cfg::kTpr == 8 ? 2 : 3;    // row bits within a warp
+  static constexpr int kSelBit = 16 >> kP;                  // lane bit of the select level
+  static_assert((kG == 2 || kG == 4) && kLevels == kP + 1, "one select level after the permuted ones");
+  static_assert(Cfg::kThreads <= 320 && 2 * Cfg::kThreads >= 320, "one or two sums per thread");
+  __device__ __forceinline__ static int perm(int lane) {
+    int pm = 0;
+#pragma unroll
+    for (int lv = 0; lv < kP; ++lv) pm += ((lane >> (4 - lv)) & 1) * (kG >> (lv + 1));
+    return pm ^ ((lane % Cfg::kTpr) >= Cfg::kTpr / 2 ? 1 : 0);
+  }
+  // offset in part[pb] (quantity, step 0, column) of reduced value pidx, which
+  // lane pidx % 32 of every warp holds in its slot pidx / 32
+  __device__ __forceinline__ static int part_off(int pidx) {
+    const int ln = pidx & 31, k = pidx >> 5;
+    const int f = k + ((ln & kSelBit) ? 10 : 0), quant = f >> 2, e = f & 3;
+    const int col = (ln % Cfg::kTpr) * Cfg::kCols + 4 * perm(ln) + e;
+    return quant * kChunk * kN + col;
+  }
+};
 
 // A chunk's inputs in 16-byte pieces: r, w, k, a, b as 16 steps x 16 groups of
 // 4 columns (threads tid < 256 take one group), v, dy, dsa as 16 steps x
@@ -418,14 +478,14 @@ __device__ __forceinline__ float4 load4(const void* base, int64_t off, bool ok) 
 }
 
 template <typename Tin, int ROWS>
-__device__ __forceinline__ void bwd_prefetch(Prefetch<Tin, ROWS>& pf, const BwdArgs& p, int64_t ch,
-                                             int64_t c, int row0) {
+__device__ __forceinline__ void bwd_prefetch(Prefetch<Tin, ROWS>& pf, const BwdArgs& p, int64_t cb,
+                                             int64_t ts, int64_t c, int row0) {
   const int tid = threadIdx.x;
   if (tid < 256) {
     const int u = tid >> 4, j = (tid & 15) * 4;
     const int64_t t = c * kChunk + u;
     const bool ok = t < p.g.T;
-    const int64_t o = ok ? p.g.off(ch, t, j) : 0;
+    const int64_t o = ok ? cb + t * ts + j : 0;
     const void* src[5] = {p.r, p.w, p.k, p.a, p.b};
 #pragma unroll
     for (int n = 0; n < 5; ++n) pf.c[n] = load4<Tin>(src[n], o, ok);
@@ -434,7 +494,7 @@ __device__ __forceinline__ void bwd_prefetch(Prefetch<Tin, ROWS>& pf, const BwdA
     const int u2 = tid / (ROWS / 4), i4 = row0 + (tid % (ROWS / 4)) * 4;
     const int64_t t2 = c * kChunk + u2;
     const bool ok2 = t2 < p.g.T;
-    const int64_t o2 = ok2 ? p.g.off(ch, t2, i4) : 0;
+    const int64_t o2 = ok2 ? cb + t2 * ts + i4 : 0;
     pf.o[0] = load4<Tin>(p.v, o2, ok2);
     pf.o[1] = load4<Tin>(p.dy, o2, ok2);
     pf.o[2] = (p.dsa != nullptr) ? load4<float>(p.dsa, o2, ok2) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -469,120 +529,148 @@ __device__ __forceinline__ void bwd_stage(BwdSmem<ROWS>& sm, const Prefetch<Tin,
   }
 }
 
-// one forward step of own row il (its kCols columns from q*kCols); returns sa of the row
+// one forward step of own row il (its kCols columns from q*kCols, register
+// group g holding column group g ^ pm); returns sa of the row
 template <int ROWS>
-__device__ __forceinline__ float fwd_step(const BwdSmem<ROWS>& sm, int u, int il, int q, float* S) {
-  constexpr int kCols = BwdCfg<ROWS>::kCols;
+__device__ __forceinline__ float fwd_step(const BwdSmem<ROWS>& sm, int u, int il, int q, int pm, float* S) {
+  constexpr int kCols = BwdCfg<ROWS>::kCols, kG = Lanes<ROWS>::kG;
   const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * kCols]);
   float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-  for (int m = 0; m < kCols / 4; m += 2) {
-    const float4 x = a4[m], z = a4[m + 1];
-    s0 += S[4 * m] * x.x + S[4 * m + 1] * x.y + S[4 * m + 2] * x.z + S[4 * m + 3] * x.w;
-    s1 += S[4 * m + 4] * z.x + S[4 * m + 5] * z.y + S[4 * m + 6] * z.z + S[4 * m + 7] * z.w;
+  for (int g = 0; g < kG; g += 2) {
+    const float4 x = a4[g ^ pm], z = a4[(g + 1) ^ pm];
+    s0 += S[4 * g] * x.x + S[4 * g + 1] * x.y + S[4 * g + 2] * x.z + S[4 * g + 3] * x.w;
+    s1 += S[4 * g + 4] * z.x + S[4 * g + 5] * z.y + S[4 * g + 6] * z.z + S[4 * g + 7] * z.w;
   }
   const float sa = row_sum<BwdCfg<ROWS>::kTpr>(s0 + s1);
   const float vi = sm.v[u][il];
+  const float4* w4 = reinterpret_cast<const float4*>(&sm.w[u][q * kCols]);
+  const float4* b4 = reinterpret_cast<const float4*>(&sm.b[u][q * kCols]);
+  const float4* k4 = reinterpret_cast<const float4*>(&sm.k[u][q * kCols]);
 #pragma unroll
-  for (int m = 0; m < kCols / 4; ++m) {
-    const float4 wv = reinterpret_cast<const float4*>(&sm.w[u][q * kCols])[m];
-    const float4 bv = reinterpret_cast<const float4*>(&sm.b[u][q * kCols])[m];
-    const float4 kv = reinterpret_cast<const float4*>(&sm.k[u][q * kCols])[m];
+  for (int g = 0; g < kG; ++g) {
+    const float4 wv = w4[g ^ pm], bv = b4[g ^ pm], kv = k4[g ^ pm];
     const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
     const float ka[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) S[4 * m + e] = S[4 * m + e] * wa[e] + (sa * ba[e] + ka[e] * vi);
+    for (int e = 0; e < 4; ++e) S[4 * g + e] = S[4 * g + e] * wa[e] + (sa * ba[e] + ka[e] * vi);
   }
   return sa;
 }
 
+// A thread's state slot holds only its own registers, so its layout is free:
+// float4 (row il, group g, thread q) at ((il kG + g) kTpr + q) ^ 4 (il & 1), which
+// gives the eight lanes of a quarter warp (one row of 8 threads, or two rows of
+// 4) eight different bank groups.
+template <int ROWS>
+__device__ __forceinline__ int slot4(int il, int g, int q) {
+  return ((il * Lanes<ROWS>::kG + g) * BwdCfg<ROWS>::kTpr + q) ^ (4 * (il & 1));
+}
+
 template <int ROWS>
 __device__ __forceinline__ void store_state(BwdSmem<ROWS>& sm, int slot, int il, int q, const float* S) {
-  constexpr int kCols = BwdCfg<ROWS>::kCols;
+  float4* dst = reinterpret_cast<float4*>(&sm.S[slot][0][0]);
 #pragma unroll
-  for (int m = 0; m < kCols / 4; ++m)
-    *reinterpret_cast<float4*>(&sm.S[slot][il][swz(il, q * kCols + 4 * m)]) =
-        make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+  for (int g = 0; g < Lanes<ROWS>::kG; ++g)
+    dst[slot4<ROWS>(il, g, q)] = make_float4(S[4 * g], S[4 * g + 1], S[4 * g + 2], S[4 * g + 3]);
 }
 
 template <int ROWS>
 __device__ __forceinline__ void load_state(const BwdSmem<ROWS>& sm, int slot, int il, int q, float* S) {
-  constexpr int kCols = BwdCfg<ROWS>::kCols;
+  const float4* src = reinterpret_cast<const float4*>(&sm.S[slot][0][0]);
 #pragma unroll
-  for (int m = 0; m < kCols / 4; ++m) {
-    const float4 x = *reinterpret_cast<const float4*>(&sm.S[slot][il][swz(il, q * kCols + 4 * m)]);
-    S[4 * m] = x.x; S[4 * m + 1] = x.y; S[4 * m + 2] = x.z; S[4 * m + 3] = x.w;
+  for (int g = 0; g < Lanes<ROWS>::kG; ++g) {
+    const float4 x = src[slot4<ROWS>(il, g, q)];
+    S[4 * g] = x.x; S[4 * g + 1] = x.y; S[4 * g + 2] = x.z; S[4 * g + 3] = x.w;
   }
 }
 
-// one reverse step u of own row il, with S_t in slot st and S_{t-1} in slot sp;
-// the own rows' column sums go to part[pb]
+// one reverse step u of own row il, with the thread's columns of S_t in Sc and
+// of S_{t-1} in Sp (register group g = column group g ^ pm); the own rows'
+// column sums go to part[pb], the thread's one or two of them at offsets d0, d1
 template <int ROWS>
-__device__ __forceinline__ void bwd_step(BwdSmem<ROWS>& sm, int u, int st, int sp, int il, int q,
-                                         int lane, int warp, int pb, float* dS) {
+__device__ __forceinline__ void bwd_step(BwdSmem<ROWS>& sm, int u, const float* Sc, const float* Sp, int il,
+                                         int q, int pm, int lane, int warp, int pb, int d0, int d1,
+                                         float* dS) {
   using Cfg = BwdCfg<ROWS>;
-  constexpr int kCols = Cfg::kCols, kX = 5 * kCols;
-  // lane bits above the row's threads: rows of the warp (two or three levels)
-  constexpr int kLevels = Cfg::kTpr == 8 ? 2 : 3;
-  float Sc[kCols], Sp[kCols];
-  load_state(sm, st, il, q, Sc);
-  load_state(sm, sp, il, q, Sp);
+  using Ln = Lanes<ROWS>;
+  constexpr int kCols = Cfg::kCols, kG = Ln::kG;
   const float dyi = sm.dy[u][il], vi = sm.v[u][il], sai = sm.sa[u][il];
+  const float4* r4 = reinterpret_cast<const float4*>(&sm.r[u][q * kCols]);
+  const float4* b4 = reinterpret_cast<const float4*>(&sm.b[u][q * kCols]);
+  const float4* k4 = reinterpret_cast<const float4*>(&sm.k[u][q * kCols]);
   float dsa0 = 0.f, dsa1 = 0.f, dv0 = 0.f, dv1 = 0.f;
 #pragma unroll
-  for (int jj = 0; jj < kCols; ++jj) {
-    const int j = q * kCols + jj;
-    dS[jj] += dyi * sm.r[u][j];
-    if (jj & 1) { dsa1 += dS[jj] * sm.b[u][j]; dv1 += dS[jj] * sm.k[u][j]; }
-    else { dsa0 += dS[jj] * sm.b[u][j]; dv0 += dS[jj] * sm.k[u][j]; }
+  for (int g = 0; g < kG; ++g) {
+    const float4 rv = r4[g ^ pm], bv = b4[g ^ pm], kv = k4[g ^ pm];
+    const float ra[4] = {rv.x, rv.y, rv.z, rv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
+    const float ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int jj = 4 * g + e;
+      dS[jj] += dyi * ra[e];
+      if (e & 1) { dsa1 += dS[jj] * ba[e]; dv1 += dS[jj] * ka[e]; }
+      else { dsa0 += dS[jj] * ba[e]; dv0 += dS[jj] * ka[e]; }
+    }
   }
   const float dsa = row_sum<Cfg::kTpr>(dsa0 + dsa1) + sm.dsa[u][il];
   const float dv = row_sum<Cfg::kTpr>(dv0 + dv1);
 
-  float x[kX];
+  // per column: dr, dw (before the decay's chain factor), dk, db, da
+  float x[5][kCols];
 #pragma unroll
   for (int jj = 0; jj < kCols; ++jj) {
-    x[jj] = Sc[jj] * dyi;                // dr
-    x[kCols + jj] = dS[jj] * Sp[jj];     // dw (before the decay's chain factor)
-    x[2 * kCols + jj] = dS[jj] * vi;     // dk
-    x[3 * kCols + jj] = dS[jj] * sai;    // db
-    x[4 * kCols + jj] = dsa * Sp[jj];    // da
+    x[0][jj] = Sc[jj] * dyi;
+    x[1][jj] = dS[jj] * Sp[jj];
+    x[2][jj] = dS[jj] * vi;
+    x[3][jj] = dS[jj] * sai;
+    x[4][jj] = dsa * Sp[jj];
   }
+  const float4* w4 = reinterpret_cast<const float4*>(&sm.w[u][q * kCols]);
+  const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * kCols]);
 #pragma unroll
-  for (int jj = 0; jj < kCols; ++jj) {
-    const int j = q * kCols + jj;
-    dS[jj] = dS[jj] * sm.w[u][j] + dsa * sm.a[u][j];
+  for (int g = 0; g < kG; ++g) {
+    const float4 wv = w4[g ^ pm], av = a4[g ^ pm];
+    const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dS[4 * g + e] = dS[4 * g + e] * wa[e] + dsa * aa[e];
   }
   if (q == 0) sm.dv[u][il] = dv;
 
-  // reduce-scatter the partials over the rows of this warp: at each level the
-  // lanes whose row bit is set keep the upper half of x, the others the lower
+  // reduce-scatter over the rows of this warp: permuted levels, then one select level
 #pragma unroll
-  for (int lv = 0; lv < kLevels; ++lv) {
-    const int bit = 16 >> lv, half = kX >> (lv + 1);
-    const bool hi = lane & bit;
+  for (int lv = 0; lv < Ln::kP; ++lv) {
+    const int bit = 16 >> lv, hc = 4 * (kG >> (lv + 1));
 #pragma unroll
-    for (int m = 0; m < half; ++m) {
-      const float send = hi ? x[m] : x[m + half];
-      const float keep = hi ? x[m + half] : x[m];
-      x[m] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
-    }
+    for (int n = 0; n < 5; ++n)
+#pragma unroll
+      for (int m = 0; m < hc; ++m) x[n][m] += __shfl_xor_sync(0xffffffffu, x[n][m + hc], bit);
   }
-  float* red = sm.red[Cfg::kRed == 2 ? (u & 1) : 0][0];
+  const bool hi = lane & Ln::kSelBit;
+  float* red = sm.red[Cfg::kRed == 2 ? (u & 1) : 0][warp];
 #pragma unroll
-  for (int s = 0; s < 10; ++s) red[warp * 320 + lane * 10 + s] = x[s];
+  for (int m = 0; m < 10; ++m) {
+    const float lo_v = x[m >> 2][m & 3], hi_v = x[(m + 10) >> 2][(m + 10) & 3];
+    const float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
+    red[m * 32 + lane] = keep + __shfl_xor_sync(0xffffffffu, send, Ln::kSelBit);
+  }
   __syncthreads();
-  // lane ln = TPR rb + q holds 10 values m = s + sum over levels of the row
-  // bit times that level's half, of quantity m / kCols at column q kCols + m % kCols
-  for (int pidx = threadIdx.x; pidx < 320; pidx += Cfg::kThreads) {
+  // sums over the warps: value pidx = tid (and tid + kThreads) of every warp's 320
+  const float* rd = sm.red[Cfg::kRed == 2 ? (u & 1) : 0][0];
+  float* part = &sm.part[pb][0][0][0] + u * kN;
+  {
+    const int pidx = threadIdx.x;
     float acc = 0.f;
 #pragma unroll
-    for (int wv = 0; wv < Cfg::kWarps; ++wv) acc += red[wv * 320 + pidx];
-    const int ln = pidx / 10, qq = ln % Cfg::kTpr, rb = ln / Cfg::kTpr;
-    int m = pidx % 10;
+    for (int wv = 0; wv < Cfg::kWarps; ++wv) acc += rd[wv * 320 + pidx];
+    part[d0] = acc;
+  }
+  if (threadIdx.x + Cfg::kThreads < 320) {
+    const int pidx = threadIdx.x + Cfg::kThreads;
+    float acc = 0.f;
 #pragma unroll
-    for (int lv = 0; lv < kLevels; ++lv) m += ((rb >> (kLevels - 1 - lv)) & 1) * (kX >> (lv + 1));
-    sm.part[pb][m / kCols][u][qq * kCols + m % kCols] = acc;
+    for (int wv = 0; wv < Cfg::kWarps; ++wv) acc += rd[wv * 320 + pidx];
+    part[d1] = acc;
   }
   if (Cfg::kRed == 1) __syncthreads();  // red is refilled by the next step
 }
@@ -603,14 +691,19 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
   const int64_t nchunk = p.g.nchunk;
   // the peer's partial sums, in its shared memory (a cluster of two)
   const BwdSmem<ROWS>* peer = Cfg::kCtas > 1 ? cluster.map_shared_rank(&sm, rank ^ 1) : nullptr;
+  // register group g holds column group g ^ pm; this thread's per-step sums go to d0, d1
+  const int pm = Lanes<ROWS>::perm(lane);
+  const int d0 = Lanes<ROWS>::part_off(tid);
+  const int d1 = tid + Cfg::kThreads < 320 ? Lanes<ROWS>::part_off(tid + Cfg::kThreads) : 0;
+  const int64_t cb = p.g.base(ch), ts = p.g.tstride();
 
   float dS[kCols], S0[kCols], S[kCols];
   if (p.dsT != nullptr) {  // the gradient of the final state enters at the last step
     const float4* src = reinterpret_cast<const float4*>(p.dsT + p.g.state_off(ch) + i * kN + q * kCols);
 #pragma unroll
-    for (int m = 0; m < kCols / 4; ++m) {
-      const float4 x = src[m];
-      dS[4 * m] = x.x; dS[4 * m + 1] = x.y; dS[4 * m + 2] = x.z; dS[4 * m + 3] = x.w;
+    for (int g = 0; g < kCols / 4; ++g) {
+      const float4 x = src[g ^ pm];
+      dS[4 * g] = x.x; dS[4 * g + 1] = x.y; dS[4 * g + 2] = x.z; dS[4 * g + 3] = x.w;
     }
   } else {
 #pragma unroll
@@ -618,25 +711,25 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
   }
 
   Prefetch<Tin, ROWS> pf;
-  if (nchunk > 0) bwd_prefetch<Tin, ROWS>(pf, p, ch, nchunk - 1, row0);
+  if (nchunk > 0) bwd_prefetch<Tin, ROWS>(pf, p, cb, ts, nchunk - 1, row0);
   for (int64_t c = nchunk - 1; c >= 0; --c) {
     const int pb = Cfg::kParts > 1 ? static_cast<int>(c & 1) : 0;
     __syncthreads();
     bwd_stage<Tin, ROWS>(sm, pf, p.g.decay);
-    if (c > 0) bwd_prefetch<Tin, ROWS>(pf, p, ch, c - 1, row0);
+    if (c > 0) bwd_prefetch<Tin, ROWS>(pf, p, cb, ts, c - 1, row0);
     if (c > 0) {
       const float4* src = reinterpret_cast<const float4*>(p.ckpt + ((ch * nchunk + c) * kN + i) * kN + q * kCols);
 #pragma unroll
-      for (int m = 0; m < kCols / 4; ++m) {
-        const float4 x = src[m];
-        S0[4 * m] = x.x; S0[4 * m + 1] = x.y; S0[4 * m + 2] = x.z; S0[4 * m + 3] = x.w;
+      for (int g = 0; g < kCols / 4; ++g) {
+        const float4 x = src[g ^ pm];
+        S0[4 * g] = x.x; S0[4 * g + 1] = x.y; S0[4 * g + 2] = x.z; S0[4 * g + 3] = x.w;
       }
     } else if (p.s0 != nullptr) {  // chunk 0 starts from the state carried in
       const float4* src = reinterpret_cast<const float4*>(p.s0 + p.g.state_off(ch) + i * kN + q * kCols);
 #pragma unroll
-      for (int m = 0; m < kCols / 4; ++m) {
-        const float4 x = src[m];
-        S0[4 * m] = x.x; S0[4 * m + 1] = x.y; S0[4 * m + 2] = x.z; S0[4 * m + 3] = x.w;
+      for (int g = 0; g < kCols / 4; ++g) {
+        const float4 x = src[g ^ pm];
+        S0[4 * g] = x.x; S0[4 * g + 1] = x.y; S0[4 * g + 2] = x.z; S0[4 * g + 3] = x.w;
       }
     } else {
 #pragma unroll
@@ -644,38 +737,69 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
     }
     __syncthreads();
 
-    // second half: advance to the middle, keep states of steps kHalf..kChunk-1
+    if constexpr (Cfg::kWhole) {
+      // one forward pass keeps S_0..S_15 in shared memory and S_16 in registers;
+      // the reverse walk hands each step's S_{t-1} on as the next step's S_t
 #pragma unroll
-    for (int jj = 0; jj < kCols; ++jj) S[jj] = S0[jj];
+      for (int jj = 0; jj < kCols; ++jj) S[jj] = S0[jj];
+      store_state(sm, 0, il, q, S);
 #pragma unroll 1
-    for (int u = 0; u < kHalf; ++u) {
-      const float sa = fwd_step(sm, u, il, q, S);
-      if (q == 0) sm.sa[u][il] = sa;
-    }
-    store_state(sm, 0, il, q, S);
+      for (int u = 0; u < kChunk; ++u) {
+        const float sa = fwd_step(sm, u, il, q, pm, S);
+        if (q == 0) sm.sa[u][il] = sa;
+        if (u + 1 < kChunk) store_state(sm, u + 1, il, q, S);
+      }
+      __syncthreads();
 #pragma unroll 1
-    for (int u = kHalf; u < kChunk; ++u) {
-      const float sa = fwd_step(sm, u, il, q, S);
-      if (q == 0) sm.sa[u][il] = sa;
-      store_state(sm, u - kHalf + 1, il, q, S);
-    }
-    __syncthreads();
+      for (int u = kChunk - 1; u >= 0; --u) {
+        float Sp[kCols];
+        load_state(sm, u, il, q, Sp);
+        bwd_step(sm, u, S, Sp, il, q, pm, lane, warp, pb, d0, d1, dS);
+#pragma unroll
+        for (int jj = 0; jj < kCols; ++jj) S[jj] = Sp[jj];
+      }
+    } else {
+      // second half: advance to the middle, keep states of steps kHalf..kChunk-1
+      float Sc[kCols], Sp[kCols];
+#pragma unroll
+      for (int jj = 0; jj < kCols; ++jj) S[jj] = S0[jj];
 #pragma unroll 1
-    for (int u = kChunk - 1; u >= kHalf; --u)
-      bwd_step(sm, u, u - kHalf + 1, u - kHalf, il, q, lane, warp, pb, dS);
+      for (int u = 0; u < kHalf; ++u) {
+        const float sa = fwd_step(sm, u, il, q, pm, S);
+        if (q == 0) sm.sa[u][il] = sa;
+      }
+      store_state(sm, 0, il, q, S);
+#pragma unroll 1
+      for (int u = kHalf; u < kChunk; ++u) {
+        const float sa = fwd_step(sm, u, il, q, pm, S);
+        if (q == 0) sm.sa[u][il] = sa;
+        store_state(sm, u - kHalf + 1, il, q, S);
+      }
+      __syncthreads();
+#pragma unroll 1
+      for (int u = kChunk - 1; u >= kHalf; --u) {
+        load_state(sm, u - kHalf + 1, il, q, Sc);
+        load_state(sm, u - kHalf, il, q, Sp);
+        bwd_step(sm, u, Sc, Sp, il, q, pm, lane, warp, pb, d0, d1, dS);
+      }
 
-    // first half
+      // first half
 #pragma unroll
-    for (int jj = 0; jj < kCols; ++jj) S[jj] = S0[jj];
-    store_state(sm, 0, il, q, S);
+      for (int jj = 0; jj < kCols; ++jj) S[jj] = S0[jj];
+      store_state(sm, 0, il, q, S);
 #pragma unroll 1
-    for (int u = 0; u < kHalf; ++u) {
-      fwd_step(sm, u, il, q, S);
-      store_state(sm, u + 1, il, q, S);
+      for (int u = 0; u < kHalf; ++u) {
+        fwd_step(sm, u, il, q, pm, S);
+        store_state(sm, u + 1, il, q, S);
+      }
+      __syncthreads();
+#pragma unroll 1
+      for (int u = kHalf - 1; u >= 0; --u) {
+        load_state(sm, u + 1, il, q, Sc);
+        load_state(sm, u, il, q, Sp);
+        bwd_step(sm, u, Sc, Sp, il, q, pm, lane, warp, pb, d0, d1, dS);
+      }
     }
-    __syncthreads();
-#pragma unroll 1
-    for (int u = kHalf - 1; u >= 0; --u) bwd_step(sm, u, u + 1, u, il, q, lane, warp, pb, dS);
 
     // both CTAs' column sums of this chunk are complete (and visible across the
     // cluster; with one CTA per chain, across the CTA)
@@ -697,7 +821,7 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
         for (int e = 0; e < 4; ++e) s[e] *= sm.w[u][j + e] * sm.dlw[u][j + e];
       // part[] order: dr, dw, dk, db, da
       void* dst = tens == 0 ? p.dr : tens == 1 ? p.dw : tens == 2 ? p.dk : tens == 3 ? p.db : p.da;
-      Tin* o = static_cast<Tin*>(dst) + p.g.off(ch, t, j);
+      Tin* o = static_cast<Tin*>(dst) + cb + t * ts + j;
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[e] = from_f32<Tin>(s[e]);
     }
@@ -705,7 +829,7 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
       const int u = tid / (ROWS / 4), j = (tid % (ROWS / 4)) * 4;
       const int64_t t = c * kChunk + u;
       if (t < p.g.T) {
-        Tin* o = static_cast<Tin*>(p.dv) + p.g.off(ch, t, row0 + j);
+        Tin* o = static_cast<Tin*>(p.dv) + cb + t * ts + row0 + j;
 #pragma unroll
         for (int e = 0; e < 4; ++e) o[e] = from_f32<Tin>(sm.dv[u][j + e]);
       }
@@ -714,7 +838,7 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
   if (p.ds0 != nullptr) {  // after chunk 0, dS is the gradient of the start state
     float4* dst = reinterpret_cast<float4*>(p.ds0 + p.g.state_off(ch) + i * kN + q * kCols);
 #pragma unroll
-    for (int m = 0; m < kCols / 4; ++m) dst[m] = make_float4(dS[4 * m], dS[4 * m + 1], dS[4 * m + 2], dS[4 * m + 3]);
+    for (int g = 0; g < kCols / 4; ++g) dst[g ^ pm] = make_float4(dS[4 * g], dS[4 * g + 1], dS[4 * g + 2], dS[4 * g + 3]);
   }
   // the peer may still be reading this CTA's partial sums of the last chunk
   if (Cfg::kCtas > 1) cluster.sync();
@@ -748,7 +872,7 @@ cudaError_t launch_bwd_rows(const BwdArgs& p, cudaStream_t stream) {
 }
 
 // Two 32-row CTAs per chain while they fit the SMs in one wave (a CTA holds
-// an SM: 166 KB of shared memory), else one 64-row CTA per chain.
+// an SM: 222 KB of shared memory), else one 64-row CTA per chain.
 template <typename Tin>
 cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream) {
   int dev = 0, sms = 148;
