@@ -567,18 +567,10 @@ struct Params {
   void* work;
 };
 
-__device__ __forceinline__ void item_pos(const Geom& g, int64_t item, int64_t& ch, int64_t& c, int& h,
-                                         int& b) {
-  ch = item / g.nchunk;
-  c = item % g.nchunk;
-  h = static_cast<int>(g.h0 + ch % g.hc);
-  b = static_cast<int>(ch / g.hc);
-}
-
-__device__ __forceinline__ void issue_a(KGroup& G, const Params& P, int64_t item) {
-  int64_t ch, c;
-  int h, b;
-  item_pos(P.a.g, item, ch, c, h, b);
+// loads of the item at walk position w
+__device__ __forceinline__ void issue_a(KGroup& G, const Params& P, const ItemWalk& w) {
+  const int64_t ch = w.ch, c = w.c;
+  const int h = w.head(P.a.g), b = static_cast<int>(w.b);
   mbar_arrive_expect_tx(&G.barA, 2 * tma::kTileBytes + sizeof(rec::XRec));
   tma::load_tile(G.raw[5], &P.in[5], h, static_cast<int>(c * L), b, &G.barA);
   tma::load_tile(G.raw[6], &P.in[6], h, static_cast<int>(c * L), b, &G.barA);
@@ -593,10 +585,9 @@ __device__ __forceinline__ void issue_a(KGroup& G, const Params& P, int64_t item
   }
 }
 
-__device__ __forceinline__ void issue_b(KGroup& G, const Params& P, int64_t item) {
-  int64_t ch, c;
-  int h, b;
-  item_pos(P.a.g, item, ch, c, h, b);
+__device__ __forceinline__ void issue_b(KGroup& G, const Params& P, const ItemWalk& w) {
+  const int64_t ch = w.ch, c = w.c;
+  const int h = w.head(P.a.g), b = static_cast<int>(w.b);
   mbar_arrive_expect_tx(&G.barB, 5 * tma::kTileBytes + sizeof(rec::TriRec));
 #pragma unroll
   for (int t = 0; t < 5; ++t) tma::load_tile(G.raw[t], &P.in[t], h, static_cast<int>(c * L), b, &G.barB);
@@ -648,9 +639,11 @@ __global__ void __launch_bounds__(kThreads, 4) keyside_bwd_kernel(const __grid_c
   const int64_t total = p.g.chains() * nchunk;
   // thread 0's count of part A / part B loads issued and of their completions seen
   int64_t issued_a = 0, issued_b = 0, seen_a = 0, seen_b = 0;
+  ItemWalk walk;  // this CTA's current item
+  walk.init(p.g, blockIdx.x, gridDim.x);
   if (tid == 0 && blockIdx.x < total) {
-    issue_a(G, P, blockIdx.x);
-    issue_b(G, P, blockIdx.x);
+    issue_a(G, P, walk);
+    issue_b(G, P, walk);
     issued_a = issued_b = 1;
   }
   const bf16* raw_r = G.raw[0];
@@ -670,9 +663,7 @@ __global__ void __launch_bounds__(kThreads, 4) keyside_bwd_kernel(const __grid_c
     seen_a += ok;
     ok = __syncthreads_and(ok);
     if (!ok) break;
-    int64_t ch, c;
-    int hh, bb;
-    item_pos(p.g, item, ch, c, hh, bb);
+    const int64_t c = walk.c;
 
     // ---- row sums over the 64 state rows (own columns j0 .. j0 + 15), and the key side ----
     //   dW = dSA S, dQy = dY S, dBb = SA G'', dKb = V G'', and colsum(G'' o S) as the
@@ -939,7 +930,7 @@ __global__ void __launch_bounds__(kThreads, 4) keyside_bwd_kernel(const __grid_c
       const int t = tid >> 3, k = tid & 7;
       const int64_t tg = c * L + t;
       if (tg < p.g.T) {
-        const int64_t off = p.g.base(ch) + tg * p.g.tstride() + 8 * k;
+        const int64_t off = walk.base(p.g) + tg * p.g.tstride() + 8 * k;
         const int o = tma::swz(t, 8 * k);
         bf16* const dst[5] = {static_cast<bf16*>(p.dr), static_cast<bf16*>(p.dw),
                               static_cast<bf16*>(p.dk), static_cast<bf16*>(p.da),
@@ -950,10 +941,11 @@ __global__ void __launch_bounds__(kThreads, 4) keyside_bwd_kernel(const __grid_c
       }
     }
     __syncthreads();  // every tile and the scratch free: load the next item
+    walk.next(p.g);
     if (tid == 0 && next < total) {
-      issue_a(G, P, next);
+      issue_a(G, P, walk);
       ++issued_a;
-      issue_b(G, P, next);
+      issue_b(G, P, walk);
       ++issued_b;
     }
   }

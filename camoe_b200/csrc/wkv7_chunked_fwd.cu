@@ -307,12 +307,12 @@ struct Params {
   bool tri = true;   // store the TriRecs (only the backward reads them)
 };
 
-__device__ __forceinline__ void issue(Group& G, int rb, const Params& P, int64_t item) {
-  const int64_t ch = item / P.g.nchunk, c = item % P.g.nchunk;
-  const int h = static_cast<int>(P.g.h0 + ch % P.g.hc), b = static_cast<int>(ch / P.g.hc);
+// loads of the item at walk position w into raw buffer rb
+__device__ __forceinline__ void issue(Group& G, int rb, const Params& P, const ItemWalk& w) {
+  const int h = w.head(P.g), b = static_cast<int>(w.b), t0 = static_cast<int>(w.c * L);
   mbar_arrive_expect_tx(&G.rawbar[rb], 5 * tma::kTileBytes);
 #pragma unroll
-  for (int t = 0; t < 5; ++t) tma::load_tile(G.raw[rb][t], &P.maps[t], h, static_cast<int>(c * L), b, &G.rawbar[rb]);
+  for (int t = 0; t < 5; ++t) tma::load_tile(G.raw[rb][t], &P.maps[t], h, t0, b, &G.rawbar[rb]);
 }
 
 __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant__ Params P) {
@@ -329,9 +329,15 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
   const int64_t total = P.g.chains() * P.g.nchunk;
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * kGroups + grp;
   const int64_t ngroups = static_cast<int64_t>(gridDim.x) * kGroups;
-  if (gtid == 0)
-    for (int i = 0; i < NR; ++i)
-      if (gid + i * ngroups < total) issue(G, i, P, gid + i * ngroups);
+  // cur: this group's current item; ahead: the item NR steps further, whose
+  // loads go out once the current item has released its raw buffer
+  ItemWalk cur, ahead;
+  cur.init(P.g, gid, ngroups);
+  ahead = cur;
+  for (int i = 0; i < NR; ++i) {
+    if (gtid == 0 && gid + i * ngroups < total) issue(G, i, P, ahead);
+    ahead.next(P.g);
+  }
   int64_t j = 0;
   for (;; ++j) {
     const int64_t item = gid + j * ngroups;
@@ -345,15 +351,13 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
     rec::TriRec& tr = G.out[j & 1].t;
     // steps past T (a ragged last chunk) do not decay the state
     int nvalid = L;
-    if ((P.g.T & (L - 1)) != 0) {
-      const int64_t c = item % P.g.nchunk;
-      if (c == P.g.nchunk - 1) nvalid = static_cast<int>(P.g.T - c * L);
-    }
+    if ((P.g.T & (L - 1)) != 0 && cur.c == P.g.nchunk - 1) nvalid = static_cast<int>(P.g.T - cur.c * L);
     ks::decays<true>(G.raw[rb][0], G.raw[rb][1], G.raw[rb][2], G.raw[rb][3], G.raw[rb][4],
                      &G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Kb, o.Bb, Swz64{}, o.lam, nullptr,
                      nullptr, gtid, P.g.decay, nvalid);
     named_sync(bar_id, 128);
-    if (gtid == 0 && item + NR * ngroups < total) issue(G, rb, P, item + NR * ngroups);
+    if (gtid == 0 && item + NR * ngroups < total) issue(G, rb, P, ahead);
+    ahead.next(P.g);
     ks::grams(&G.At[0][0], &G.Rt[0][0], Padded{LD}, o.Bb, o.Kb, Swz64{}, G.Ga, tr.Bm, tr.Cm, G.Dm,
               gw, lane);
     named_sync(bar_id, 128);
@@ -366,11 +370,11 @@ __global__ void __launch_bounds__(kThreads) keyside_kernel(const __grid_constant
     fence_proxy_async();
     named_sync(bar_id, 128);
     if (gtid == 0) {
-      const int64_t ch = item / P.g.nchunk, c = item - ch * P.g.nchunk;
-      bulk_s2g(rec::keyrec(P.ckpt, ch, P.g.nchunk, c), &o, sizeof(rec::KeyRec));
-      if (P.tri) bulk_s2g(rec::trirec(P.ckpt, P.g.chains(), ch, P.g.nchunk, c), &tr, sizeof(rec::TriRec));
+      bulk_s2g(rec::keyrec(P.ckpt, cur.ch, P.g.nchunk, cur.c), &o, sizeof(rec::KeyRec));
+      if (P.tri) bulk_s2g(rec::trirec(P.ckpt, P.g.chains(), cur.ch, P.g.nchunk, cur.c), &tr, sizeof(rec::TriRec));
       bulk_commit();
     }
+    cur.next(P.g);
   }
   if (gtid == 0) {
     bulk_wait_all();

@@ -58,6 +58,40 @@ struct Geom {
   }
 };
 
+// Position of a grid-stride walk over the (chain, chunk) items of a call,
+// item = ch * nchunk + c with ch = b * hc + hm.  The divisions happen once, in
+// init(); next() advances by the stride with one carry per level, so a loop
+// over items pays a few integer adds per item instead of 64-bit divisions.
+struct ItemWalk {
+  int64_t ch, c, b, hm;      // the current item
+  int64_t dch, dc, db, dhm;  // the stride in the same terms
+  __device__ __forceinline__ void init(const Geom& g, int64_t item, int64_t stride) {
+    ch = item / g.nchunk;
+    c = item - ch * g.nchunk;
+    b = ch / g.hc;
+    hm = ch - b * g.hc;
+    dch = stride / g.nchunk;
+    dc = stride - dch * g.nchunk;
+    db = dch / g.hc;
+    dhm = dch - db * g.hc;
+  }
+  __device__ __forceinline__ void next(const Geom& g) {
+    c += dc;
+    const int64_t carry = c >= g.nchunk ? 1 : 0;  // c, dc < nchunk: at most one wrap
+    c -= carry * g.nchunk;
+    ch += dch + carry;
+    hm += dhm + carry;
+    b += db;
+    if (hm >= g.hc) {  // hm, dhm < hc: at most one wrap
+      hm -= g.hc;
+      b += 1;
+    }
+  }
+  __device__ __forceinline__ int head(const Geom& g) const { return static_cast<int>(g.h0 + hm); }
+  // offset of element (0, 0) of the current chain, as Geom::base
+  __device__ __forceinline__ int64_t base(const Geom& g) const { return (b * g.T * g.H + g.h0 + hm) * kN; }
+};
+
 struct FwdArgs {
   const void *r, *w, *k, *v, *a, *b;
   void* y;

@@ -28,12 +28,17 @@ using Tile16 = bf16[L][LDS];
 // every row to the same banks)
 constexpr int LDF = kN + 8;
 
-// Phase 1 (SIMT): per column pair (2p, 2p+1) and time quarter tq, the
-// log-decays lw = log_decay(w_in, kind), their inclusive prefix cum inside
-// the chunk (scan over the 4 quarter lanes), Lam = exp(cum), and the scaled
-// operands At = a exp(cum - lw), Rt = r Lam, Kb = k / Lam, Bb = b / Lam.
-// lam (the decay over the whole chunk) = Lam of the last step.
-// Thread layout: p = gtid / 4, tq = gtid % 4 (quarter lanes adjacent).
+// Phase 1 (SIMT): per column pair (2p, 2p+1), the log-decays lw =
+// log_decay(w_in, kind), their inclusive prefix cum inside the chunk,
+// Lam = exp(cum), and the scaled operands At = a exp(cum - lw), Rt = r Lam,
+// Kb = k / Lam, Bb = b / Lam.  lam (the decay over the whole chunk) = Lam of
+// the last step.  Thread layout: p = gtid / 4, tq = gtid % 4 (the four lanes of
+// a column pair adjacent); lane tq owns rows 2tq, 2tq + 1 (first half) and
+// 8 + 2tq, 9 + 2tq (second half), so the four rows one instruction touches are
+// 2 apart, which puts them on different banks both in the swizzled TMA tiles
+// and in the padded tiles (rows 8 apart share banks in both).  The prefix is
+// two interleaved scans over the four lanes, one per half, the second offset
+// by the first half's total.
 // With `cum_out`/`lw_out` non-null, the fp32 prefixes and log-decays are kept
 // for the backward.  Steps u >= nvalid (past the end of a sequence whose
 // length is not a multiple of L) get lw = 0, so lam is the decay over the
@@ -52,10 +57,16 @@ __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf1
                                        float (*lw_out)[LDF], int gtid, int kind, int nvalid = L) {
   const int p = gtid >> 2, tq = gtid & 3, j = 2 * p;
   const int lane = gtid & 31;
-  float lw0[4], lw1[4], c0[4], c1[4];
+  // the lane's rows: e = 0, 1 first half, e = 2, 3 second half
+  int rows[4];
+  rows[0] = 2 * tq;
+  rows[1] = 2 * tq + 1;
+  rows[2] = 8 + 2 * tq;
+  rows[3] = 9 + 2 * tq;
+  float lw0[4], lw1[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ww + raw_idx<SWZ>(4 * tq + e, j)));
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ww + raw_idx<SWZ>(rows[e], j)));
     lw0[e] = x.x;
     lw1[e] = x.y;
   }
@@ -72,51 +83,63 @@ __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf1
       lw1[e] = kWScale * __fdividef(1.0f, 1.0f + __expf(-lw1[e]));
     }
   }
-  float run0 = 0.f, run1 = 0.f;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    const int u = 4 * tq + e;
-    if (u >= nvalid) lw0[e] = lw1[e] = 0.f;
-    if (lw_out != nullptr) *reinterpret_cast<float2*>(&lw_out[u][j]) = make_float2(lw0[e], lw1[e]);
-    run0 += lw0[e];
-    run1 += lw1[e];
-    c0[e] = run0;
-    c1[e] = run1;
+    if (rows[e] >= nvalid) lw0[e] = lw1[e] = 0.f;
+    if (lw_out != nullptr) *reinterpret_cast<float2*>(&lw_out[rows[e]][j]) = make_float2(lw0[e], lw1[e]);
   }
-  // exclusive prefix of the quarter totals over the 4 quarter lanes
-  float s0 = run0, s1 = run1;
+  // inclusive scans over the four lanes of the half totals (h: first half, g: second)
+  const float h0 = lw0[0] + lw0[1], h1 = lw1[0] + lw1[1];
+  const float g0 = lw0[2] + lw0[3], g1 = lw1[2] + lw1[3];
+  float sh0 = h0, sh1 = h1, sg0 = g0, sg1 = g1;
 #pragma unroll
   for (int d = 1; d < 4; d <<= 1) {
-    const float t0 = __shfl_up_sync(0xffffffffu, s0, d);
-    const float t1 = __shfl_up_sync(0xffffffffu, s1, d);
+    const float a0 = __shfl_up_sync(0xffffffffu, sh0, d);
+    const float a1 = __shfl_up_sync(0xffffffffu, sh1, d);
+    const float b0 = __shfl_up_sync(0xffffffffu, sg0, d);
+    const float b1 = __shfl_up_sync(0xffffffffu, sg1, d);
     if (tq >= d) {
-      s0 += t0;
-      s1 += t1;
+      sh0 += a0;
+      sh1 += a1;
+      sg0 += b0;
+      sg1 += b1;
     }
   }
-  const float off0 = s0 - run0, off1 = s1 - run1;
-  (void)lane;
-  float px0 = __expf(off0), px1 = __expf(off1);  // exp(cum) before the quarter's first step
+  // the first half's total sits in the pair's last lane
+  const int last = (lane & ~3) | 3;
+  const float tot0 = __shfl_sync(0xffffffffu, sh0, last), tot1 = __shfl_sync(0xffffffffu, sh1, last);
+  // cum before each half's first row of this lane
+  float off0[2], off1[2];
+  off0[0] = sh0 - h0;
+  off1[0] = sh1 - h1;
+  off0[1] = tot0 + sg0 - g0;
+  off1[1] = tot1 + sg1 - g1;
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int u = 4 * tq + e;
-    const float cu0 = off0 + c0[e], cu1 = off1 + c1[e];
-    if (cum_out != nullptr) *reinterpret_cast<float2*>(&cum_out[u][j]) = make_float2(cu0, cu1);
-    const float L0 = __expf(cu0), L1 = __expf(cu1);
-    const float i0 = __expf(-cu0), i1 = __expf(-cu1);
-    const int o = raw_idx<SWZ>(u, j);
-    const float2 r = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(rr + o));
-    const float2 k = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kk + o));
-    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(aa + o));
-    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bb + o));
-    *reinterpret_cast<__nv_bfloat162*>(At + lar(u, j)) = __floats2bfloat162_rn(a.x * px0, a.y * px1);
-    *reinterpret_cast<__nv_bfloat162*>(Rt + lar(u, j)) = __floats2bfloat162_rn(r.x * L0, r.y * L1);
-    *reinterpret_cast<__nv_bfloat162*>(Kb + lkb(u, j)) = __floats2bfloat162_rn(k.x * i0, k.y * i1);
-    *reinterpret_cast<__nv_bfloat162*>(Bb + lkb(u, j)) = __floats2bfloat162_rn(b.x * i0, b.y * i1);
-    px0 = L0;
-    px1 = L1;
+  for (int hf = 0; hf < 2; ++hf) {
+    float cu0 = off0[hf], cu1 = off1[hf];
+    float px0 = __expf(cu0), px1 = __expf(cu1);  // exp(cum) before the row
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      const int e = 2 * hf + x, u = rows[e];
+      cu0 += lw0[e];
+      cu1 += lw1[e];
+      if (cum_out != nullptr) *reinterpret_cast<float2*>(&cum_out[u][j]) = make_float2(cu0, cu1);
+      const float L0 = __expf(cu0), L1 = __expf(cu1);
+      const float i0 = __expf(-cu0), i1 = __expf(-cu1);
+      const int o = raw_idx<SWZ>(u, j);
+      const float2 r = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(rr + o));
+      const float2 k = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kk + o));
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(aa + o));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bb + o));
+      *reinterpret_cast<__nv_bfloat162*>(At + lar(u, j)) = __floats2bfloat162_rn(a.x * px0, a.y * px1);
+      *reinterpret_cast<__nv_bfloat162*>(Rt + lar(u, j)) = __floats2bfloat162_rn(r.x * L0, r.y * L1);
+      *reinterpret_cast<__nv_bfloat162*>(Kb + lkb(u, j)) = __floats2bfloat162_rn(k.x * i0, k.y * i1);
+      *reinterpret_cast<__nv_bfloat162*>(Bb + lkb(u, j)) = __floats2bfloat162_rn(b.x * i0, b.y * i1);
+      px0 = L0;
+      px1 = L1;
+    }
+    if (hf == 1 && tq == 3) *reinterpret_cast<float2*>(&lam[j]) = make_float2(px0, px1);  // row 15
   }
-  if (tq == 3) *reinterpret_cast<float2*>(&lam[j]) = make_float2(px0, px1);
 }
 
 // Phase 2 (tensor cores): the four 16x16 Gram blocks, warp gw computes block gw:
