@@ -3,9 +3,9 @@
 //
 // Forward (scan_fwd_kernel): the state rows are independent recurrences that
 // share the transition, so a chain's 64 rows are split over 4 CTAs of 16
-// rows; 8 threads own one row (8 state columns each in registers, 4 warps per
+// rows; 16 threads own one row (4 state columns each in registers, 8 warps per
 // CTA so each SMSP switches between warps of the latency-bound step loop) and
-// combine row sums (sa = S a, y = S r) with three xor-shuffles.  Chunks of 16
+// combine row sums (sa = S a, y = S r) with four xor-shuffles.  Chunks of 16
 // steps of r, w, k, a, b (and the CTA's slice of v) are streamed into shared
 // memory with cp.async, double-buffered, and converted once per chunk
 // (decay w = exp(log_decay(w_in)) computed there, ClampW or wind).  The state at the
@@ -33,10 +33,10 @@ namespace camoe {
 namespace scan {
 
 constexpr int kRows = 16;                 // forward: state rows per CTA
-constexpr int kFwdTpr = 8;                // forward: threads per row (8 columns each)
-constexpr int kFwdCols = kN / kFwdTpr;
+constexpr int kFwdTpr = 16;               // forward: threads per row
+constexpr int kFwdCols = kN / kFwdTpr;    // state columns per thread
 constexpr int kFwdThreads = kRows * kFwdTpr;
-static_assert(kFwdCols == 8, "dot8 and the group flip take eight columns per thread");
+static_assert(kFwdCols == 4 || kFwdCols == 8, "dot_cols takes one or two 4-column groups");
 constexpr int kRowGroups = kN / kRows;    // forward: CTAs per chain
 constexpr int kHalf = kChunk / 2;         // backward: states held per half chunk
 
@@ -84,18 +84,21 @@ __device__ __forceinline__ float row_sum(float x) {
 
 // this thread's part of a row dot product: its kFwdCols state columns times a
 // shared-memory row segment (two FMA chains).  Register group m holds column
-// group m ^ sw, sw = 1 for the upper four threads of a row, so that the eight
-// threads of a row (a quarter warp) read eight different bank groups.
-__device__ __forceinline__ float dot8(const float (&S)[kFwdCols], const float* x, int sw) {
+// group m ^ sw.  With 8 columns per thread, sw = 1 for the upper four threads
+// of a row, so that the eight threads of a row (a quarter warp) read eight
+// different bank groups; with 4 columns a quarter warp reads 128 contiguous
+// bytes and sw = 0.
+__device__ __forceinline__ float dot_cols(const float (&S)[kFwdCols], const float* x, int sw) {
   const float4* x4 = reinterpret_cast<const float4*>(x);
-  float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-  for (int m = 0; m < kFwdCols / 4; m += 2) {
-    const float4 e = x4[m ^ sw], f = x4[(m + 1) ^ sw];
-    s0 += S[4 * m] * e.x + S[4 * m + 1] * e.y + S[4 * m + 2] * e.z + S[4 * m + 3] * e.w;
-    s1 += S[4 * m + 4] * f.x + S[4 * m + 5] * f.y + S[4 * m + 6] * f.z + S[4 * m + 7] * f.w;
+  if constexpr (kFwdCols == 4) {
+    const float4 e = x4[0];
+    return (S[0] * e.x + S[1] * e.y) + (S[2] * e.z + S[3] * e.w);
+  } else {
+    const float4 e = x4[sw], f = x4[1 ^ sw];
+    const float s0 = S[0] * e.x + S[1] * e.y + S[2] * e.z + S[3] * e.w;
+    const float s1 = S[4] * f.x + S[5] * f.y + S[6] * f.z + S[7] * f.w;
+    return s0 + s1;
   }
-  return s0 + s1;
 }
 
 template <typename Tin>
@@ -103,7 +106,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   FwdSmem<Tin>& sm = *reinterpret_cast<FwdSmem<Tin>*>(smem_raw);
   const int tid = threadIdx.x, rl = tid / kFwdTpr, q = tid % kFwdTpr;
-  const int sw = q >= kFwdTpr / 2 ? 1 : 0;  // register group m = column group m ^ sw
+  const int sw = (kFwdCols == 8 && q >= kFwdTpr / 2) ? 1 : 0;  // register group m = column group m ^ sw
   const int64_t ch = blockIdx.x / kRowGroups;
   const int rg = blockIdx.x % kRowGroups;
   const int i = rg * kRows + rl;
@@ -156,7 +159,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
     // y_u = S_u r_u and sa_{u+1} = S_u a_{u+1} both read only S_u, so their
     // row sums run interleaved: one shuffle chain per step instead of two
     // (sa holds the whole row's sum at the top of every step)
-    float sa = row_sum<kFwdTpr>(dot8(S, &sm.a[0][q * kFwdCols], sw));
+    float sa = row_sum<kFwdTpr>(dot_cols(S, &sm.a[0][q * kFwdCols], sw));
 #pragma unroll 1
     for (int u = 0; u < nu; ++u) {
       const float vi = sm.v[u][rl];
@@ -173,8 +176,8 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
       }
       // the last step of the chunk reads a row of a again (its sum is unused)
       const int un = u + 1 < nu ? u + 1 : u;
-      float y = dot8(S, &sm.r[u][q * kFwdCols], sw);
-      float sn = dot8(S, &sm.a[un][q * kFwdCols], sw);
+      float y = dot_cols(S, &sm.r[u][q * kFwdCols], sw);
+      float sn = dot_cols(S, &sm.a[un][q * kFwdCols], sw);
 #pragma unroll
       for (int d = 1; d < kFwdTpr; d <<= 1) {
         const float yo = __shfl_xor_sync(0xffffffffu, y, d);
