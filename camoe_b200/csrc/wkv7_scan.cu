@@ -82,22 +82,32 @@ __device__ __forceinline__ float row_sum(float x) {
   return x;
 }
 
-// this thread's part of a row dot product: its kFwdCols state columns times a
-// shared-memory row segment (two FMA chains).  Register group m holds column
+// The per-thread column arrays are float2 pairs (pair 2g + h holds elements
+// 4g + 2h, 4g + 2h + 1 of register group g), so the elementwise work issues
+// as packed two-lane fp32 operations (__ffma2_rn, __fmul2_rn, __fadd2_rn:
+// each lane rounded as the scalar operation).
+__device__ __forceinline__ float2 bc2(float x) { return make_float2(x, x); }
+__device__ __forceinline__ float2 lo2(const float4& v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(const float4& v) { return make_float2(v.z, v.w); }
+
+// this thread's part of a row dot product: its kFwdCols state columns (as
+// pairs) times a shared-memory row segment.  Register group m holds column
 // group m ^ sw.  With 8 columns per thread, sw = 1 for the upper four threads
 // of a row, so that the eight threads of a row (a quarter warp) read eight
 // different bank groups; with 4 columns a quarter warp reads 128 contiguous
 // bytes and sw = 0.
-__device__ __forceinline__ float dot_cols(const float (&S)[kFwdCols], const float* x, int sw) {
+constexpr int kFwdPairs = kFwdCols / 2;
+__device__ __forceinline__ float dot_cols(const float2 (&S)[kFwdPairs], const float* x, int sw) {
   const float4* x4 = reinterpret_cast<const float4*>(x);
   if constexpr (kFwdCols == 4) {
     const float4 e = x4[0];
-    return (S[0] * e.x + S[1] * e.y) + (S[2] * e.z + S[3] * e.w);
+    const float2 acc = __ffma2_rn(S[1], hi2(e), __fmul2_rn(S[0], lo2(e)));
+    return acc.x + acc.y;
   } else {
     const float4 e = x4[sw], f = x4[1 ^ sw];
-    const float s0 = S[0] * e.x + S[1] * e.y + S[2] * e.z + S[3] * e.w;
-    const float s1 = S[4] * f.x + S[5] * f.y + S[6] * f.z + S[7] * f.w;
-    return s0 + s1;
+    const float2 a0 = __ffma2_rn(S[1], hi2(e), __fmul2_rn(S[0], lo2(e)));
+    const float2 a1 = __ffma2_rn(S[3], hi2(f), __fmul2_rn(S[2], lo2(f)));
+    return (a0.x + a0.y) + (a1.x + a1.y);
   }
 }
 
@@ -113,17 +123,18 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
   const int64_t nchunk = p.g.nchunk;
   const int64_t cb = p.g.base(ch), ts = p.g.tstride();
 
-  float S[kFwdCols];
-  if (p.s0 != nullptr) {  // start state: row i, columns 8q..8q+7
+  float2 S[kFwdPairs];
+  if (p.s0 != nullptr) {  // start state: row i, columns q kFwdCols .. q kFwdCols + kFwdCols - 1
     const float4* src = reinterpret_cast<const float4*>(p.s0 + p.g.state_off(ch) + i * kN + q * kFwdCols);
 #pragma unroll
     for (int m = 0; m < kFwdCols / 4; ++m) {
       const float4 x = src[m ^ sw];
-      S[4 * m] = x.x; S[4 * m + 1] = x.y; S[4 * m + 2] = x.z; S[4 * m + 3] = x.w;
+      S[2 * m] = lo2(x);
+      S[2 * m + 1] = hi2(x);
     }
   } else {
 #pragma unroll
-    for (int jj = 0; jj < kFwdCols; ++jj) S[jj] = 0.f;
+    for (int pp = 0; pp < kFwdPairs; ++pp) S[pp] = make_float2(0.f, 0.f);
   }
 
   fwd_issue(sm, 0, p, cb, ts, 0, rg);
@@ -153,7 +164,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
       float4* dst = reinterpret_cast<float4*>(p.ckpt + ((ch * nchunk + c) * kN + i) * kN + q * kFwdCols);
 #pragma unroll
       for (int m = 0; m < kFwdCols / 4; ++m)
-        dst[m ^ sw] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+        dst[m ^ sw] = make_float4(S[2 * m].x, S[2 * m].y, S[2 * m + 1].x, S[2 * m + 1].y);
     }
 
     // y_u = S_u r_u and sa_{u+1} = S_u a_{u+1} both read only S_u, so their
@@ -162,17 +173,15 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
     float sa = row_sum<kFwdTpr>(dot_cols(S, &sm.a[0][q * kFwdCols], sw));
 #pragma unroll 1
     for (int u = 0; u < nu; ++u) {
-      const float vi = sm.v[u][rl];
+      const float2 vi2 = bc2(sm.v[u][rl]), sa2 = bc2(sa);
       const float4* w4 = reinterpret_cast<const float4*>(&sm.w[u][q * kFwdCols]);
       const float4* b4 = reinterpret_cast<const float4*>(&sm.b[u][q * kFwdCols]);
       const float4* k4 = reinterpret_cast<const float4*>(&sm.k[u][q * kFwdCols]);
 #pragma unroll
       for (int m = 0; m < kFwdCols / 4; ++m) {
         const float4 wv = w4[m ^ sw], bv = b4[m ^ sw], kv = k4[m ^ sw];
-        const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
-        const float ka[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) S[4 * m + e] = S[4 * m + e] * wa[e] + (sa * ba[e] + ka[e] * vi);
+        S[2 * m] = __ffma2_rn(S[2 * m], lo2(wv), __ffma2_rn(sa2, lo2(bv), __fmul2_rn(lo2(kv), vi2)));
+        S[2 * m + 1] = __ffma2_rn(S[2 * m + 1], hi2(wv), __ffma2_rn(sa2, hi2(bv), __fmul2_rn(hi2(kv), vi2)));
       }
       // the last step of the chunk reads a row of a again (its sum is unused)
       const int un = u + 1 < nu ? u + 1 : u;
@@ -210,7 +219,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdArgs p) {
     float4* dst = reinterpret_cast<float4*>(p.sT + p.g.state_off(ch) + i * kN + q * kFwdCols);
 #pragma unroll
     for (int m = 0; m < kFwdCols / 4; ++m)
-      dst[m ^ sw] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+      dst[m ^ sw] = make_float4(S[2 * m].x, S[2 * m].y, S[2 * m + 1].x, S[2 * m + 1].y);
   }
 }
 
@@ -440,7 +449,7 @@ struct Lanes {
   static constexpr int kLevels = Cfg::kTpr == 8 ? 2 : 3;    // row bits within a warp
   static constexpr int kSelBit = 16 >> kP;                  // lane bit of the select level
   static_assert((kG == 2 || kG == 4) && kLevels == kP + 1, "one select level after the permuted ones");
-  static_assert(Cfg::kThreads <= 320 && 2 * Cfg::kThreads >= 320, "one or two sums per thread");
+  static_assert(Cfg::kThreads >= 160, "160 threads add the per-warp partial sums");
   __device__ __forceinline__ static int perm(int lane) {
     int pm = 0;
 #pragma unroll
@@ -535,28 +544,26 @@ __device__ __forceinline__ void bwd_stage(BwdSmem<ROWS>& sm, const Prefetch<Tin,
 // one forward step of own row il (its kCols columns from q*kCols, register
 // group g holding column group g ^ pm); returns sa of the row
 template <int ROWS>
-__device__ __forceinline__ float fwd_step(const BwdSmem<ROWS>& sm, int u, int il, int q, int pm, float* S) {
+__device__ __forceinline__ float fwd_step(const BwdSmem<ROWS>& sm, int u, int il, int q, int pm, float2* S) {
   constexpr int kCols = BwdCfg<ROWS>::kCols, kG = Lanes<ROWS>::kG;
   const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * kCols]);
-  float s0 = 0.f, s1 = 0.f;
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int g = 0; g < kG; g += 2) {
-    const float4 x = a4[g ^ pm], z = a4[(g + 1) ^ pm];
-    s0 += S[4 * g] * x.x + S[4 * g + 1] * x.y + S[4 * g + 2] * x.z + S[4 * g + 3] * x.w;
-    s1 += S[4 * g + 4] * z.x + S[4 * g + 5] * z.y + S[4 * g + 6] * z.z + S[4 * g + 7] * z.w;
+  for (int g = 0; g < kG; ++g) {
+    const float4 x = a4[g ^ pm];
+    acc0 = __ffma2_rn(S[2 * g], lo2(x), acc0);
+    acc1 = __ffma2_rn(S[2 * g + 1], hi2(x), acc1);
   }
-  const float sa = row_sum<BwdCfg<ROWS>::kTpr>(s0 + s1);
-  const float vi = sm.v[u][il];
+  const float sa = row_sum<BwdCfg<ROWS>::kTpr>((acc0.x + acc0.y) + (acc1.x + acc1.y));
+  const float2 sa2 = bc2(sa), vi2 = bc2(sm.v[u][il]);
   const float4* w4 = reinterpret_cast<const float4*>(&sm.w[u][q * kCols]);
   const float4* b4 = reinterpret_cast<const float4*>(&sm.b[u][q * kCols]);
   const float4* k4 = reinterpret_cast<const float4*>(&sm.k[u][q * kCols]);
 #pragma unroll
   for (int g = 0; g < kG; ++g) {
     const float4 wv = w4[g ^ pm], bv = b4[g ^ pm], kv = k4[g ^ pm];
-    const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
-    const float ka[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) S[4 * g + e] = S[4 * g + e] * wa[e] + (sa * ba[e] + ka[e] * vi);
+    S[2 * g] = __ffma2_rn(S[2 * g], lo2(wv), __ffma2_rn(sa2, lo2(bv), __fmul2_rn(lo2(kv), vi2)));
+    S[2 * g + 1] = __ffma2_rn(S[2 * g + 1], hi2(wv), __ffma2_rn(sa2, hi2(bv), __fmul2_rn(hi2(kv), vi2)));
   }
   return sa;
 }
@@ -571,109 +578,109 @@ __device__ __forceinline__ int slot4(int il, int g, int q) {
 }
 
 template <int ROWS>
-__device__ __forceinline__ void store_state(BwdSmem<ROWS>& sm, int slot, int il, int q, const float* S) {
+__device__ __forceinline__ void store_state(BwdSmem<ROWS>& sm, int slot, int il, int q, const float2* S) {
   float4* dst = reinterpret_cast<float4*>(&sm.S[slot][0][0]);
 #pragma unroll
   for (int g = 0; g < Lanes<ROWS>::kG; ++g)
-    dst[slot4<ROWS>(il, g, q)] = make_float4(S[4 * g], S[4 * g + 1], S[4 * g + 2], S[4 * g + 3]);
+    dst[slot4<ROWS>(il, g, q)] = make_float4(S[2 * g].x, S[2 * g].y, S[2 * g + 1].x, S[2 * g + 1].y);
 }
 
 template <int ROWS>
-__device__ __forceinline__ void load_state(const BwdSmem<ROWS>& sm, int slot, int il, int q, float* S) {
+__device__ __forceinline__ void load_state(const BwdSmem<ROWS>& sm, int slot, int il, int q, float2* S) {
   const float4* src = reinterpret_cast<const float4*>(&sm.S[slot][0][0]);
 #pragma unroll
   for (int g = 0; g < Lanes<ROWS>::kG; ++g) {
     const float4 x = src[slot4<ROWS>(il, g, q)];
-    S[4 * g] = x.x; S[4 * g + 1] = x.y; S[4 * g + 2] = x.z; S[4 * g + 3] = x.w;
+    S[2 * g] = lo2(x);
+    S[2 * g + 1] = hi2(x);
   }
 }
 
 // one reverse step u of own row il, with the thread's columns of S_t in Sc and
 // of S_{t-1} in Sp (register group g = column group g ^ pm); the own rows'
-// column sums go to part[pb], the thread's one or two of them at offsets d0, d1
+// column sums go to part[pb], threads below 160 writing two of them at d0, d1
 template <int ROWS>
-__device__ __forceinline__ void bwd_step(BwdSmem<ROWS>& sm, int u, const float* Sc, const float* Sp, int il,
+__device__ __forceinline__ void bwd_step(BwdSmem<ROWS>& sm, int u, const float2* Sc, const float2* Sp, int il,
                                          int q, int pm, int lane, int warp, int pb, int d0, int d1,
-                                         float* dS) {
+                                         float2* dS) {
   using Cfg = BwdCfg<ROWS>;
   using Ln = Lanes<ROWS>;
-  constexpr int kCols = Cfg::kCols, kG = Ln::kG;
-  const float dyi = sm.dy[u][il], vi = sm.v[u][il], sai = sm.sa[u][il];
+  constexpr int kCols = Cfg::kCols, kG = Ln::kG, kPairs = kCols / 2;
+  const float2 dy2 = bc2(sm.dy[u][il]), vi2 = bc2(sm.v[u][il]), sa2 = bc2(sm.sa[u][il]);
   const float4* r4 = reinterpret_cast<const float4*>(&sm.r[u][q * kCols]);
   const float4* b4 = reinterpret_cast<const float4*>(&sm.b[u][q * kCols]);
   const float4* k4 = reinterpret_cast<const float4*>(&sm.k[u][q * kCols]);
-  float dsa0 = 0.f, dsa1 = 0.f, dv0 = 0.f, dv1 = 0.f;
+  float2 dsa2 = make_float2(0.f, 0.f), dv2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int g = 0; g < kG; ++g) {
     const float4 rv = r4[g ^ pm], bv = b4[g ^ pm], kv = k4[g ^ pm];
-    const float ra[4] = {rv.x, rv.y, rv.z, rv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
-    const float ka[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int jj = 4 * g + e;
-      dS[jj] += dyi * ra[e];
-      if (e & 1) { dsa1 += dS[jj] * ba[e]; dv1 += dS[jj] * ka[e]; }
-      else { dsa0 += dS[jj] * ba[e]; dv0 += dS[jj] * ka[e]; }
-    }
+    dS[2 * g] = __ffma2_rn(dy2, lo2(rv), dS[2 * g]);
+    dS[2 * g + 1] = __ffma2_rn(dy2, hi2(rv), dS[2 * g + 1]);
+    dsa2 = __ffma2_rn(dS[2 * g], lo2(bv), dsa2);
+    dv2 = __ffma2_rn(dS[2 * g], lo2(kv), dv2);
+    dsa2 = __ffma2_rn(dS[2 * g + 1], hi2(bv), dsa2);
+    dv2 = __ffma2_rn(dS[2 * g + 1], hi2(kv), dv2);
   }
-  const float dsa = row_sum<Cfg::kTpr>(dsa0 + dsa1) + sm.dsa[u][il];
-  const float dv = row_sum<Cfg::kTpr>(dv0 + dv1);
+  const float dsa = row_sum<Cfg::kTpr>(dsa2.x + dsa2.y) + sm.dsa[u][il];
+  const float dv = row_sum<Cfg::kTpr>(dv2.x + dv2.y);
+  const float2 dsab = bc2(dsa);
 
-  // per column: dr, dw (before the decay's chain factor), dk, db, da
-  float x[5][kCols];
+  // per column pair: dr, dw (before the decay's chain factor), dk, db, da
+  float2 x[5][kPairs];
 #pragma unroll
-  for (int jj = 0; jj < kCols; ++jj) {
-    x[0][jj] = Sc[jj] * dyi;
-    x[1][jj] = dS[jj] * Sp[jj];
-    x[2][jj] = dS[jj] * vi;
-    x[3][jj] = dS[jj] * sai;
-    x[4][jj] = dsa * Sp[jj];
+  for (int pp = 0; pp < kPairs; ++pp) {
+    x[0][pp] = __fmul2_rn(Sc[pp], dy2);
+    x[1][pp] = __fmul2_rn(dS[pp], Sp[pp]);
+    x[2][pp] = __fmul2_rn(dS[pp], vi2);
+    x[3][pp] = __fmul2_rn(dS[pp], sa2);
+    x[4][pp] = __fmul2_rn(dsab, Sp[pp]);
   }
   const float4* w4 = reinterpret_cast<const float4*>(&sm.w[u][q * kCols]);
   const float4* a4 = reinterpret_cast<const float4*>(&sm.a[u][q * kCols]);
 #pragma unroll
   for (int g = 0; g < kG; ++g) {
     const float4 wv = w4[g ^ pm], av = a4[g ^ pm];
-    const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, aa[4] = {av.x, av.y, av.z, av.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) dS[4 * g + e] = dS[4 * g + e] * wa[e] + dsa * aa[e];
+    dS[2 * g] = __ffma2_rn(dS[2 * g], lo2(wv), __fmul2_rn(dsab, lo2(av)));
+    dS[2 * g + 1] = __ffma2_rn(dS[2 * g + 1], hi2(wv), __fmul2_rn(dsab, hi2(av)));
   }
   if (q == 0) sm.dv[u][il] = dv;
 
   // reduce-scatter over the rows of this warp: permuted levels, then one select level
 #pragma unroll
   for (int lv = 0; lv < Ln::kP; ++lv) {
-    const int bit = 16 >> lv, hc = 4 * (kG >> (lv + 1));
+    const int bit = 16 >> lv, hp = 2 * (kG >> (lv + 1));  // pairs kept
 #pragma unroll
     for (int n = 0; n < 5; ++n)
 #pragma unroll
-      for (int m = 0; m < hc; ++m) x[n][m] += __shfl_xor_sync(0xffffffffu, x[n][m + hc], bit);
+      for (int m = 0; m < hp; ++m) {
+        const float2 o = make_float2(__shfl_xor_sync(0xffffffffu, x[n][m + hp].x, bit),
+                                     __shfl_xor_sync(0xffffffffu, x[n][m + hp].y, bit));
+        x[n][m] = __fadd2_rn(x[n][m], o);
+      }
   }
+  // pairs 0..4 (values 0..9 of the lane's 5 x 4) stay on lanes without the
+  // select bit, pairs 5..9 on lanes with it; pair m of a lane (its values 2m,
+  // 2m + 1) lands at float2 m * 32 + lane of the warp's 160
   const bool hi = lane & Ln::kSelBit;
-  float* red = sm.red[Cfg::kRed == 2 ? (u & 1) : 0][warp];
+  float2* red = reinterpret_cast<float2*>(sm.red[Cfg::kRed == 2 ? (u & 1) : 0][warp]);
 #pragma unroll
-  for (int m = 0; m < 10; ++m) {
-    const float lo_v = x[m >> 2][m & 3], hi_v = x[(m + 10) >> 2][(m + 10) & 3];
-    const float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
-    red[m * 32 + lane] = keep + __shfl_xor_sync(0xffffffffu, send, Ln::kSelBit);
+  for (int m = 0; m < 5; ++m) {
+    const float2 lo_v = x[m >> 1][m & 1], hi_v = x[(m + 5) >> 1][(m + 5) & 1];
+    const float2 send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
+    const float2 o = make_float2(__shfl_xor_sync(0xffffffffu, send.x, Ln::kSelBit),
+                                 __shfl_xor_sync(0xffffffffu, send.y, Ln::kSelBit));
+    red[m * 32 + lane] = __fadd2_rn(keep, o);
   }
   __syncthreads();
-  // sums over the warps: value pidx = tid (and tid + kThreads) of every warp's 320
-  const float* rd = sm.red[Cfg::kRed == 2 ? (u & 1) : 0][0];
-  float* part = &sm.part[pb][0][0][0] + u * kN;
-  {
-    const int pidx = threadIdx.x;
-    float acc = 0.f;
+  // sums over the warps: threads 0..159 each add one float2 of every warp's 160
+  if (threadIdx.x < 160) {
+    const float2* rd = reinterpret_cast<const float2*>(sm.red[Cfg::kRed == 2 ? (u & 1) : 0][0]);
+    float2 acc = rd[threadIdx.x];
 #pragma unroll
-    for (int wv = 0; wv < Cfg::kWarps; ++wv) acc += rd[wv * 320 + pidx];
-    part[d0] = acc;
-  }
-  if (threadIdx.x + Cfg::kThreads < 320) {
-    const int pidx = threadIdx.x + Cfg::kThreads;
-    float acc = 0.f;
-#pragma unroll
-    for (int wv = 0; wv < Cfg::kWarps; ++wv) acc += rd[wv * 320 + pidx];
-    part[d1] = acc;
+    for (int wv = 1; wv < Cfg::kWarps; ++wv) acc = __fadd2_rn(acc, rd[wv * 160 + threadIdx.x]);
+    float* part = &sm.part[pb][0][0][0] + u * kN;
+    part[d0] = acc.x;
+    part[d1] = acc.y;
   }
   if (Cfg::kRed == 1) __syncthreads();  // red is refilled by the next step
 }
@@ -694,23 +701,27 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
   const int64_t nchunk = p.g.nchunk;
   // the peer's partial sums, in its shared memory (a cluster of two)
   const BwdSmem<ROWS>* peer = Cfg::kCtas > 1 ? cluster.map_shared_rank(&sm, rank ^ 1) : nullptr;
-  // register group g holds column group g ^ pm; this thread's per-step sums go to d0, d1
+  // register group g holds column group g ^ pm; threads below 160 add the
+  // per-warp sums of pair tid / 32 of lane tid % 32 (values 2 (tid / 32) and
+  // 2 (tid / 32) + 1 of that lane) and write them to d0, d1
   const int pm = Lanes<ROWS>::perm(lane);
-  const int d0 = Lanes<ROWS>::part_off(tid);
-  const int d1 = tid + Cfg::kThreads < 320 ? Lanes<ROWS>::part_off(tid + Cfg::kThreads) : 0;
+  const int d0 = tid < 160 ? Lanes<ROWS>::part_off(64 * (tid >> 5) + (tid & 31)) : 0;
+  const int d1 = tid < 160 ? Lanes<ROWS>::part_off(64 * (tid >> 5) + 32 + (tid & 31)) : 0;
   const int64_t cb = p.g.base(ch), ts = p.g.tstride();
 
-  float dS[kCols], S0[kCols], S[kCols];
+  constexpr int kPairs = kCols / 2;
+  float2 dS[kPairs], S0[kPairs], S[kPairs];
   if (p.dsT != nullptr) {  // the gradient of the final state enters at the last step
     const float4* src = reinterpret_cast<const float4*>(p.dsT + p.g.state_off(ch) + i * kN + q * kCols);
 #pragma unroll
     for (int g = 0; g < kCols / 4; ++g) {
       const float4 x = src[g ^ pm];
-      dS[4 * g] = x.x; dS[4 * g + 1] = x.y; dS[4 * g + 2] = x.z; dS[4 * g + 3] = x.w;
+      dS[2 * g] = lo2(x);
+      dS[2 * g + 1] = hi2(x);
     }
   } else {
 #pragma unroll
-    for (int jj = 0; jj < kCols; ++jj) dS[jj] = 0.f;
+    for (int pp = 0; pp < kPairs; ++pp) dS[pp] = make_float2(0.f, 0.f);
   }
 
   Prefetch<Tin, ROWS> pf;
@@ -725,18 +736,20 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
 #pragma unroll
       for (int g = 0; g < kCols / 4; ++g) {
         const float4 x = src[g ^ pm];
-        S0[4 * g] = x.x; S0[4 * g + 1] = x.y; S0[4 * g + 2] = x.z; S0[4 * g + 3] = x.w;
+        S0[2 * g] = lo2(x);
+        S0[2 * g + 1] = hi2(x);
       }
     } else if (p.s0 != nullptr) {  // chunk 0 starts from the state carried in
       const float4* src = reinterpret_cast<const float4*>(p.s0 + p.g.state_off(ch) + i * kN + q * kCols);
 #pragma unroll
       for (int g = 0; g < kCols / 4; ++g) {
         const float4 x = src[g ^ pm];
-        S0[4 * g] = x.x; S0[4 * g + 1] = x.y; S0[4 * g + 2] = x.z; S0[4 * g + 3] = x.w;
+        S0[2 * g] = lo2(x);
+        S0[2 * g + 1] = hi2(x);
       }
     } else {
 #pragma unroll
-      for (int jj = 0; jj < kCols; ++jj) S0[jj] = 0.f;
+      for (int pp = 0; pp < kPairs; ++pp) S0[pp] = make_float2(0.f, 0.f);
     }
     __syncthreads();
 
@@ -744,7 +757,7 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
       // one forward pass keeps S_0..S_15 in shared memory and S_16 in registers;
       // the reverse walk hands each step's S_{t-1} on as the next step's S_t
 #pragma unroll
-      for (int jj = 0; jj < kCols; ++jj) S[jj] = S0[jj];
+      for (int pp = 0; pp < kPairs; ++pp) S[pp] = S0[pp];
       store_state(sm, 0, il, q, S);
 #pragma unroll 1
       for (int u = 0; u < kChunk; ++u) {
@@ -755,17 +768,17 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
       __syncthreads();
 #pragma unroll 1
       for (int u = kChunk - 1; u >= 0; --u) {
-        float Sp[kCols];
+        float2 Sp[kPairs];
         load_state(sm, u, il, q, Sp);
         bwd_step(sm, u, S, Sp, il, q, pm, lane, warp, pb, d0, d1, dS);
 #pragma unroll
-        for (int jj = 0; jj < kCols; ++jj) S[jj] = Sp[jj];
+        for (int pp = 0; pp < kPairs; ++pp) S[pp] = Sp[pp];
       }
     } else {
       // second half: advance to the middle, keep states of steps kHalf..kChunk-1
-      float Sc[kCols], Sp[kCols];
+      float2 Sc[kPairs], Sp[kPairs];
 #pragma unroll
-      for (int jj = 0; jj < kCols; ++jj) S[jj] = S0[jj];
+      for (int pp = 0; pp < kPairs; ++pp) S[pp] = S0[pp];
 #pragma unroll 1
       for (int u = 0; u < kHalf; ++u) {
         const float sa = fwd_step(sm, u, il, q, pm, S);
@@ -788,7 +801,7 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
 
       // first half
 #pragma unroll
-      for (int jj = 0; jj < kCols; ++jj) S[jj] = S0[jj];
+      for (int pp = 0; pp < kPairs; ++pp) S[pp] = S0[pp];
       store_state(sm, 0, il, q, S);
 #pragma unroll 1
       for (int u = 0; u < kHalf; ++u) {
@@ -841,7 +854,8 @@ __global__ void __cluster_dims__(BwdCfg<ROWS>::kCtas, 1, 1)
   if (p.ds0 != nullptr) {  // after chunk 0, dS is the gradient of the start state
     float4* dst = reinterpret_cast<float4*>(p.ds0 + p.g.state_off(ch) + i * kN + q * kCols);
 #pragma unroll
-    for (int g = 0; g < kCols / 4; ++g) dst[g ^ pm] = make_float4(dS[4 * g], dS[4 * g + 1], dS[4 * g + 2], dS[4 * g + 3]);
+    for (int g = 0; g < kCols / 4; ++g)
+      dst[g ^ pm] = make_float4(dS[2 * g].x, dS[2 * g].y, dS[2 * g + 1].x, dS[2 * g + 1].y);
   }
   // the peer may still be reading this CTA's partial sums of the last chunk
   if (Cfg::kCtas > 1) cluster.sync();
