@@ -13,14 +13,15 @@
 //
 // Backward (scan_bwd_kernel): one cluster of two 256-thread CTAs per chain,
 // each owning 32 rows of dS (row i = 32 rank + tid/8, eight columns 8q..8q+7
-// with q = tid%8), walking chunks in reverse.  Each chunk's states are recomputed
-// forward from its checkpoint into shared memory (all 16 in one pass; with one
-// 64-row CTA per chain, two halves of 8 steps so 9 states fit), never reversed
-// through 1/w as camoe/cuda/rwkv7_clampw.cu:133 does.  Per step the row sums
-// (dsa = dS b, dv = dS k) use shuffles; the five
-// column sums over the rows (dr, dw, dk, db, da) use a shuffle reduce-scatter
-// over the 4 rows of a warp and a shared-memory pass over the 8 warps, and the
-// two CTAs' sums are added once per chunk through distributed shared memory.
+// with q = tid%8), walking chunks in reverse.  Each chunk's states are
+// recomputed forward from its checkpoint into shared memory (all 16 in one
+// pass; with one 64-row CTA per chain, two halves of 8 steps so 9 states fit),
+// never reversed through 1/w as camoe/cuda/rwkv7_clampw.cu:133 does.  Per step
+// the row sums (dsa = dS b, dv = dS k) use shuffles; the five column sums over
+// the rows (dr, dw, dk, db, da) use a shuffle reduce-scatter over the 4 rows of
+// a warp and a shared-memory pass over the 8 warps, and the two CTAs' sums are
+// added once per chunk through distributed shared memory.  The elementwise
+// work of both kernels runs as packed two-lane fp32 (float2) operations.
 // The per-element formulas are those of camoe/cuda/rwkv7_clampw.cu:123-168,
 // plus the external sa-gradient.
 #include <cooperative_groups.h>
