@@ -852,6 +852,7 @@ __global__ void __launch_bounds__(kThreads, 4) keyside_bwd_kernel(const __grid_c
     // outputs in place of the inputs they replace (same thread, same element):
     // dr -> r, dk -> k, da -> a, db -> b tiles; dw -> the w tile.  This lane
     // holds rows gq (hf 0) and gq + 8 (hf 1) of columns j0 + 8 nt + 2q + x.
+    // the column pair x = 0, 1 of each (nt, hf) runs as packed two-lane fp32
     float u[2][2][2], cx[2][2][2], lws[2][2][2];  // [nt][x][hf]: dcum + dcumx, dcumx, lw
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
@@ -860,32 +861,34 @@ __global__ void __launch_bounds__(kThreads, 4) keyside_bwd_kernel(const __grid_c
         const int t = gq + 8 * hf, jj = j0 + 8 * nt + 2 * q, o = tma::swz(t, jj);
         const float2 cm = *reinterpret_cast<const float2*>(&G.cum[t][jj]);
         const float2 lg = *reinterpret_cast<const float2*>(&G.lw[t][jj]);
-        const float2 rr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_r + o));
-        const float2 kk = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_k + o));
-        const float2 aa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_a + o));
-        const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw_b + o));
-        const float cmv[2] = {cm.x, cm.y}, lwv[2] = {lg.x, lg.y};
-        const float rv[2] = {rr.x, rr.y}, kv[2] = {kk.x, kk.y}, av[2] = {aa.x, aa.y}, bv[2] = {bb.x, bb.y};
-        float oda[2], odr[2], odk[2], odb[2];
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const int e = 2 * hf + x;
-          const float Lam = __expf(cmv[x]), Lamx = __expf(cmv[x] - lwv[x]), iLam = __expf(-cmv[x]);
-          const float dat = dAt[nt][e], drt = dRt[nt][e] + dQy[nt][e];
-          const float dbb = dBb[nt][e] + dBp[nt][e], dkb = dKb[nt][e] + dKp[nt][e];
-          oda[x] = dat * Lamx;
-          odr[x] = drt * Lam;
-          odk[x] = dkb * iLam;
-          odb[x] = dbb * iLam;
-          const float dcx = dat * av[x] * Lamx;
-          cx[nt][x][hf] = dcx;
-          u[nt][x][hf] = drt * rv[x] * Lam - dkb * kv[x] * iLam - dbb * bv[x] * iLam + dcx;
-          lws[nt][x][hf] = lwv[x];
-        }
-        *reinterpret_cast<__nv_bfloat162*>(G.raw[3] + o) = __floats2bfloat162_rn(oda[0], oda[1]);
-        *reinterpret_cast<__nv_bfloat162*>(G.raw[0] + o) = __floats2bfloat162_rn(odr[0], odr[1]);
-        *reinterpret_cast<__nv_bfloat162*>(G.raw[2] + o) = __floats2bfloat162_rn(odk[0], odk[1]);
-        *reinterpret_cast<__nv_bfloat162*>(G.raw[4] + o) = __floats2bfloat162_rn(odb[0], odb[1]);
+        const float2 rr = ks::ld_bf2(raw_r + o), kk = ks::ld_bf2(raw_k + o);
+        const float2 aa = ks::ld_bf2(raw_a + o), bb = ks::ld_bf2(raw_b + o);
+        const float2 Lam = ks::exp_pair(cm), iLam = ks::exp_pair(make_float2(-cm.x, -cm.y));
+        const float2 Lamx = ks::exp_pair(make_float2(cm.x - lg.x, cm.y - lg.y));
+        const int e = 2 * hf;
+        const float2 dat = make_float2(dAt[nt][e], dAt[nt][e + 1]);
+        const float2 drt = __fadd2_rn(make_float2(dRt[nt][e], dRt[nt][e + 1]), make_float2(dQy[nt][e], dQy[nt][e + 1]));
+        const float2 dbb = __fadd2_rn(make_float2(dBb[nt][e], dBb[nt][e + 1]), make_float2(dBp[nt][e], dBp[nt][e + 1]));
+        const float2 dkb = __fadd2_rn(make_float2(dKb[nt][e], dKb[nt][e + 1]), make_float2(dKp[nt][e], dKp[nt][e + 1]));
+        const float2 oda = __fmul2_rn(dat, Lamx), odr = __fmul2_rn(drt, Lam);
+        const float2 odk = __fmul2_rn(dkb, iLam), odb = __fmul2_rn(dbb, iLam);
+        const float2 dcx = __fmul2_rn(__fmul2_rn(dat, aa), Lamx);
+        // drt r Lam - dkb k iLam - dbb b iLam + dcx
+        const float2 t1 = __fmul2_rn(__fmul2_rn(drt, rr), Lam);
+        const float2 t2 = __fmul2_rn(__fmul2_rn(dkb, kk), iLam);
+        const float2 t3 = __fmul2_rn(__fmul2_rn(dbb, bb), iLam);
+        const float2 uu = __fadd2_rn(__fadd2_rn(__fadd2_rn(t1, make_float2(-t2.x, -t2.y)),
+                                                make_float2(-t3.x, -t3.y)), dcx);
+        cx[nt][0][hf] = dcx.x;
+        cx[nt][1][hf] = dcx.y;
+        u[nt][0][hf] = uu.x;
+        u[nt][1][hf] = uu.y;
+        lws[nt][0][hf] = lg.x;
+        lws[nt][1][hf] = lg.y;
+        *reinterpret_cast<__nv_bfloat162*>(G.raw[3] + o) = __floats2bfloat162_rn(oda.x, oda.y);
+        *reinterpret_cast<__nv_bfloat162*>(G.raw[0] + o) = __floats2bfloat162_rn(odr.x, odr.y);
+        *reinterpret_cast<__nv_bfloat162*>(G.raw[2] + o) = __floats2bfloat162_rn(odk.x, odk.y);
+        *reinterpret_cast<__nv_bfloat162*>(G.raw[4] + o) = __floats2bfloat162_rn(odb.x, odb.y);
       }
     // reverse scans along t: dlw_s = sum_{t>=s} (dcum_t + dcumx_t) - dcumx_s, with dll
     // added at the last step; rows gq + 8 hf sit in the 8 lanes of equal q (lane stride 4)

@@ -49,7 +49,14 @@ __device__ __forceinline__ int raw_idx(int u, int j) {
   return SWZ ? tma::swz(u, j) : u * LD + j;
 }
 
+__device__ __forceinline__ float2 exp_pair(float2 x) { return make_float2(__expf(x.x), __expf(x.y)); }
+__device__ __forceinline__ float2 ld_bf2(const bf16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+
 // At, Rt are written through layout lar, Kb, Bb through layout lkb (16 x 64 bf16).
+// The two columns of a pair run as packed two-lane fp32 operations
+// (__fmul2_rn, __fadd2_rn: each lane rounded as the scalar operation).
 template <bool SWZ, typename LAR, typename LKB>
 __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf16* kk,
                                        const bf16* aa, const bf16* bb, bf16* At, bf16* Rt, LAR lar,
@@ -63,82 +70,64 @@ __device__ __forceinline__ void decays(const bf16* rr, const bf16* ww, const bf1
   rows[1] = 2 * tq + 1;
   rows[2] = 8 + 2 * tq;
   rows[3] = 9 + 2 * tq;
-  float lw0[4], lw1[4];
+  float2 lw[4];  // log-decays of the column pair, per row
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ww + raw_idx<SWZ>(rows[e], j)));
-    lw0[e] = x.x;
-    lw1[e] = x.y;
-  }
+  for (int e = 0; e < 4; ++e) lw[e] = ld_bf2(ww + raw_idx<SWZ>(rows[e], j));
   if (kind == kDecayWind) {  // uniform branch: one transform per call
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      lw0[e] = -__expf(lw0[e]);
-      lw1[e] = -__expf(lw1[e]);
-    }
+    for (int e = 0; e < 4; ++e) lw[e] = __fmul2_rn(exp_pair(lw[e]), make_float2(-1.f, -1.f));
   } else {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      lw0[e] = kWScale * __fdividef(1.0f, 1.0f + __expf(-lw0[e]));
-      lw1[e] = kWScale * __fdividef(1.0f, 1.0f + __expf(-lw1[e]));
+      const float2 den = __fadd2_rn(exp_pair(make_float2(-lw[e].x, -lw[e].y)), make_float2(1.f, 1.f));
+      lw[e] = __fmul2_rn(make_float2(__fdividef(1.0f, den.x), __fdividef(1.0f, den.y)),
+                         make_float2(kWScale, kWScale));
     }
   }
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    if (rows[e] >= nvalid) lw0[e] = lw1[e] = 0.f;
-    if (lw_out != nullptr) *reinterpret_cast<float2*>(&lw_out[rows[e]][j]) = make_float2(lw0[e], lw1[e]);
+    if (rows[e] >= nvalid) lw[e] = make_float2(0.f, 0.f);
+    if (lw_out != nullptr) *reinterpret_cast<float2*>(&lw_out[rows[e]][j]) = lw[e];
   }
   // inclusive scans over the four lanes of the half totals (h: first half, g: second)
-  const float h0 = lw0[0] + lw0[1], h1 = lw1[0] + lw1[1];
-  const float g0 = lw0[2] + lw0[3], g1 = lw1[2] + lw1[3];
-  float sh0 = h0, sh1 = h1, sg0 = g0, sg1 = g1;
+  const float2 h = __fadd2_rn(lw[0], lw[1]), gs = __fadd2_rn(lw[2], lw[3]);
+  float2 sh = h, sg = gs;
 #pragma unroll
   for (int d = 1; d < 4; d <<= 1) {
-    const float a0 = __shfl_up_sync(0xffffffffu, sh0, d);
-    const float a1 = __shfl_up_sync(0xffffffffu, sh1, d);
-    const float b0 = __shfl_up_sync(0xffffffffu, sg0, d);
-    const float b1 = __shfl_up_sync(0xffffffffu, sg1, d);
+    const float2 a = make_float2(__shfl_up_sync(0xffffffffu, sh.x, d), __shfl_up_sync(0xffffffffu, sh.y, d));
+    const float2 b = make_float2(__shfl_up_sync(0xffffffffu, sg.x, d), __shfl_up_sync(0xffffffffu, sg.y, d));
     if (tq >= d) {
-      sh0 += a0;
-      sh1 += a1;
-      sg0 += b0;
-      sg1 += b1;
+      sh = __fadd2_rn(sh, a);
+      sg = __fadd2_rn(sg, b);
     }
   }
   // the first half's total sits in the pair's last lane
   const int last = (lane & ~3) | 3;
-  const float tot0 = __shfl_sync(0xffffffffu, sh0, last), tot1 = __shfl_sync(0xffffffffu, sh1, last);
+  const float2 tot = make_float2(__shfl_sync(0xffffffffu, sh.x, last), __shfl_sync(0xffffffffu, sh.y, last));
   // cum before each half's first row of this lane
-  float off0[2], off1[2];
-  off0[0] = sh0 - h0;
-  off1[0] = sh1 - h1;
-  off0[1] = tot0 + sg0 - g0;
-  off1[1] = tot1 + sg1 - g1;
+  float2 off[2];
+  off[0] = make_float2(sh.x - h.x, sh.y - h.y);
+  off[1] = make_float2(tot.x + sg.x - gs.x, tot.y + sg.y - gs.y);
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf) {
-    float cu0 = off0[hf], cu1 = off1[hf];
-    float px0 = __expf(cu0), px1 = __expf(cu1);  // exp(cum) before the row
+    float2 cu = off[hf];
+    float2 px = exp_pair(cu);  // exp(cum) before the row
 #pragma unroll
     for (int x = 0; x < 2; ++x) {
       const int e = 2 * hf + x, u = rows[e];
-      cu0 += lw0[e];
-      cu1 += lw1[e];
-      if (cum_out != nullptr) *reinterpret_cast<float2*>(&cum_out[u][j]) = make_float2(cu0, cu1);
-      const float L0 = __expf(cu0), L1 = __expf(cu1);
-      const float i0 = __expf(-cu0), i1 = __expf(-cu1);
+      cu = __fadd2_rn(cu, lw[e]);
+      if (cum_out != nullptr) *reinterpret_cast<float2*>(&cum_out[u][j]) = cu;
+      const float2 Lc = exp_pair(cu), ic = exp_pair(make_float2(-cu.x, -cu.y));
       const int o = raw_idx<SWZ>(u, j);
-      const float2 r = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(rr + o));
-      const float2 k = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kk + o));
-      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(aa + o));
-      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bb + o));
-      *reinterpret_cast<__nv_bfloat162*>(At + lar(u, j)) = __floats2bfloat162_rn(a.x * px0, a.y * px1);
-      *reinterpret_cast<__nv_bfloat162*>(Rt + lar(u, j)) = __floats2bfloat162_rn(r.x * L0, r.y * L1);
-      *reinterpret_cast<__nv_bfloat162*>(Kb + lkb(u, j)) = __floats2bfloat162_rn(k.x * i0, k.y * i1);
-      *reinterpret_cast<__nv_bfloat162*>(Bb + lkb(u, j)) = __floats2bfloat162_rn(b.x * i0, b.y * i1);
-      px0 = L0;
-      px1 = L1;
+      const float2 r = ld_bf2(rr + o), k = ld_bf2(kk + o), a = ld_bf2(aa + o), b = ld_bf2(bb + o);
+      const float2 at = __fmul2_rn(a, px), rt = __fmul2_rn(r, Lc), kt = __fmul2_rn(k, ic), bt = __fmul2_rn(b, ic);
+      *reinterpret_cast<__nv_bfloat162*>(At + lar(u, j)) = __floats2bfloat162_rn(at.x, at.y);
+      *reinterpret_cast<__nv_bfloat162*>(Rt + lar(u, j)) = __floats2bfloat162_rn(rt.x, rt.y);
+      *reinterpret_cast<__nv_bfloat162*>(Kb + lkb(u, j)) = __floats2bfloat162_rn(kt.x, kt.y);
+      *reinterpret_cast<__nv_bfloat162*>(Bb + lkb(u, j)) = __floats2bfloat162_rn(bt.x, bt.y);
+      px = Lc;
     }
-    if (hf == 1 && tq == 3) *reinterpret_cast<float2*>(&lam[j]) = make_float2(px0, px1);  // row 15
+    if (hf == 1 && tq == 3) *reinterpret_cast<float2*>(&lam[j]) = px;  // row 15
   }
 }
 
