@@ -8,7 +8,8 @@
 // columns 8i..8i+7 (one 16-byte access per bf16 tensor, two per fp32 one), so
 // a head (64 columns) is 8 adjacent threads and a per-head sum (GroupNorm,
 // the bonus term) is three xor-shuffles; the LayerNorm over C adds one
-// shared-memory step.  mix_bwd and prep, which keep the most values live per
+// shared-memory step (lnsa for C > 1024; up to C = 1024 it runs one warp per
+// row, shuffles only, lnsa_*_rows_kernel).  mix_bwd and prep, which keep the most values live per
 // column (six mixes and their gradient sums; fifteen input tensors), use C/2
 // threads of two columns each (warp = head) so that they fit in 64 registers
 // at full occupancy: measured faster than eight columns on B200.
@@ -20,6 +21,7 @@
 // one partial row per CTA and added by partial_reduce_kernel in a fixed
 // order (deterministic).  All arithmetic is fp32; activations are bf16.
 #include <initializer_list>
+#include <type_traits>
 
 #include "camoe_timemix.h"
 #include "wkv7_common.cuh"
@@ -699,25 +701,188 @@ __global__ void __launch_bounds__(256) lnsa_bwd_kernel(const float* __restrict__
   st8(pp + C + c, acc[1]);
 }
 
-// out[i] = sum over g < G of part[g * n + i].  Block (32, 8): 32 consecutive
-// columns, 8 row strides; each thread sums g = ty, ty + 8, ..., then the 8
-// partial sums are added in order of ty (deterministic).
-__global__ void __launch_bounds__(256) partial_reduce_kernel(const float* __restrict__ part, int G,
-                                                             int64_t n, float* __restrict__ out) {
-  __shared__ float red[8][33];
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int64_t i = blockIdx.x * 32LL + tx;
-  float s = 0.f;
-  if (i < n)
-    for (int g = ty; g < G; g += 8) s += part[g * n + i];
-  red[ty][tx] = s;
-  __syncthreads();
-  if (ty == 0 && i < n) {
-    float t = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) t += red[j][tx];
-    out[i] = t;
+// LayerNorm of sa for C <= 1024 (C = 64 J): one warp per row, the CTA's eight
+// warps taking rows in turn (grid-strided), lane l holding the column pairs
+// 2(l + 32 j), j < J, so each load and store of a row is J coalesced 256-byte
+// warp accesses and every sum over the row is five xor-shuffles: no CTA
+// barrier couples the warps, which the C/8-thread layout above needs for each
+// of its row sums.  Weight and bias are staged once in shared memory.  Same
+// arithmetic as lnsa_fwd_kernel (two-pass variance, eps 1e-5).
+constexpr int kRowWarps = 8;  // warps of a row kernel's CTA
+
+template <int J>
+__global__ void __launch_bounds__(32 * kRowWarps) lnsa_fwd_rows_kernel(
+    const float* __restrict__ sa, const float* __restrict__ wt, const float* __restrict__ bs,
+    float* __restrict__ out, int64_t rows) {
+  constexpr int C = 64 * J, P = 32 * J;  // columns, column pairs
+  __shared__ float2 pw[P], pb[P];
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    pw[i] = reinterpret_cast<const float2*>(wt)[i];
+    pb[i] = reinterpret_cast<const float2*>(bs)[i];
   }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * kRowWarps;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kRowWarps + (threadIdx.x >> 5); r < rows;
+       r += step) {
+    const float2* src = reinterpret_cast<const float2*>(sa + r * C) + lane;
+    float2 x[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) x[j] = src[32 * j];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) s += x[j].x + x[j].y;
+    const float mean = warp_sum(s) * (1.0f / static_cast<float>(C));
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      x[j].x -= mean;
+      x[j].y -= mean;
+      q += x[j].x * x[j].x + x[j].y * x[j].y;
+    }
+    const float rstd = rsqrtf(warp_sum(q) * (1.0f / static_cast<float>(C)) + 1e-5f);
+    float2* dst = reinterpret_cast<float2*>(out + r * C) + lane;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const float2 w = pw[lane + 32 * j], b = pb[lane + 32 * j];
+      dst[32 * j] = make_float2(x[j].x * rstd * w.x + b.x, x[j].y * rstd * w.y + b.y);
+    }
+  }
+}
+
+// Backward of lnsa_fwd_rows_kernel, same layout.  Each warp adds its rows'
+// weight and bias gradients into its own slice of shared memory (a lane
+// touches only its own columns, so no barrier is needed per row); at the end
+// the CTA adds its eight slices in warp order into one partial row of part,
+// [weight C | bias C] as lnsa_bwd_kernel writes it.
+// Dynamic shared memory: lnsa_rows_smem(J) bytes.
+template <int J>
+__global__ void __launch_bounds__(32 * kRowWarps) lnsa_bwd_rows_kernel(
+    const float* __restrict__ dout, const float* __restrict__ sa, const float* __restrict__ wt,
+    float* __restrict__ dsa, float* __restrict__ part, int64_t rows) {
+  constexpr int C = 64 * J, P = 32 * J;
+  extern __shared__ float2 rsm[];  // weight [P], then per warp [weight grad P | bias grad P]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float2* pw = rsm;
+  float2* acc = rsm + P + warp * 2 * P;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) pw[i] = reinterpret_cast<const float2*>(wt)[i];
+  for (int i = threadIdx.x; i < kRowWarps * 2 * P; i += blockDim.x) rsm[P + i] = make_float2(0.f, 0.f);
+  __syncthreads();
+  const int64_t step = static_cast<int64_t>(gridDim.x) * kRowWarps;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kRowWarps + warp; r < rows; r += step) {
+    const float2* xs = reinterpret_cast<const float2*>(sa + r * C) + lane;
+    const float2* gs = reinterpret_cast<const float2*>(dout + r * C) + lane;
+    float2 x[J], g[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      x[j] = xs[32 * j];
+      g[j] = gs[32 * j];
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) s += x[j].x + x[j].y;
+    const float mean = warp_sum(s) * (1.0f / static_cast<float>(C));
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      x[j].x -= mean;
+      x[j].y -= mean;
+      q += x[j].x * x[j].x + x[j].y * x[j].y;
+    }
+    const float rstd = rsqrtf(warp_sum(q) * (1.0f / static_cast<float>(C)) + 1e-5f);
+    float m1 = 0.f, m2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int i = lane + 32 * j;
+      x[j].x *= rstd;  // xn
+      x[j].y *= rstd;
+      float2 aw = acc[i], ab = acc[P + i];
+      aw.x += g[j].x * x[j].x;
+      aw.y += g[j].y * x[j].y;
+      ab.x += g[j].x;
+      ab.y += g[j].y;
+      acc[i] = aw;
+      acc[P + i] = ab;
+      const float2 w = pw[i];
+      g[j].x *= w.x;  // d xn
+      g[j].y *= w.y;
+      m1 += g[j].x + g[j].y;
+      m2 += g[j].x * x[j].x + g[j].y * x[j].y;
+    }
+    m1 = warp_sum(m1) * (1.0f / static_cast<float>(C));
+    m2 = warp_sum(m2) * (1.0f / static_cast<float>(C));
+    float2* dst = reinterpret_cast<float2*>(dsa + r * C) + lane;
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+      dst[32 * j] = make_float2(rstd * (g[j].x - m1 - x[j].x * m2),
+                                rstd * (g[j].y - m1 - x[j].y * m2));
+  }
+  __syncthreads();
+  float2* pp = reinterpret_cast<float2*>(part) + static_cast<int64_t>(blockIdx.x) * 2 * P;
+  for (int i = threadIdx.x; i < 2 * P; i += blockDim.x) {
+    float2 t = rsm[P + i];
+#pragma unroll
+    for (int w = 1; w < kRowWarps; ++w) {
+      const float2 u = rsm[P + w * 2 * P + i];
+      t.x += u.x;
+      t.y += u.y;
+    }
+    pp[i] = t;
+  }
+}
+
+constexpr size_t lnsa_rows_smem(int J) {
+  return static_cast<size_t>(32 * J) * (1 + 2 * kRowWarps) * sizeof(float2);
+}
+
+__device__ __forceinline__ void add4(float4& a, const float4& b) {
+  a.x += b.x;
+  a.y += b.y;
+  a.z += b.z;
+  a.w += b.w;
+}
+
+// out[i] = sum over g < G of part[g * n + i], n a multiple of 4 (n4 = n / 4
+// float4 columns).  A block of 256 threads covers four float4 columns (16
+// floats) with 64 row strides: thread (c, r) adds rows r, r + 64, ... into four
+// accumulators (one per row stride of a 256-row pass, so four loads are in
+// flight), adds them in a fixed order, and the 64 row strides are then added
+// by a fixed tree in shared memory (deterministic for a given G).  n / 16
+// blocks keep every SM busy where one block of 32 columns per 32 floats left
+// most of them idle for the G ~ 1000 partial rows of a backward kernel.
+__global__ void __launch_bounds__(256) partial_reduce_kernel(const float4* __restrict__ part, int G,
+                                                             int64_t n4, float4* __restrict__ out) {
+  __shared__ float4 red[64][4];
+  const int c = threadIdx.x & 3, r = threadIdx.x >> 2;
+  const int64_t i = blockIdx.x * 4LL + c;
+  float4 a[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) a[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (i < n4) {
+    int g = r;
+    for (; g + 192 < G; g += 256)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) add4(a[k], part[static_cast<int64_t>(g + 64 * k) * n4 + i]);
+    // fewer than four strides left (g + 192 >= G)
+    if (g < G) add4(a[0], part[static_cast<int64_t>(g) * n4 + i]);
+    if (g + 64 < G) add4(a[1], part[static_cast<int64_t>(g + 64) * n4 + i]);
+    if (g + 128 < G) add4(a[2], part[static_cast<int64_t>(g + 128) * n4 + i]);
+  }
+  add4(a[0], a[1]);
+  add4(a[2], a[3]);
+  add4(a[0], a[2]);
+  red[r][c] = a[0];
+  __syncthreads();
+#pragma unroll
+  for (int h = 32; h > 0; h >>= 1) {
+    if (r < h) {
+      float4 t = red[r][c];
+      add4(t, red[r + h][c]);
+      red[r][c] = t;
+    }
+    __syncthreads();
+  }
+  if (r == 0 && i < n4) out[i] = red[0][c];
 }
 
 // ---------------------------------------------------------------------------
@@ -762,10 +927,31 @@ int status(cudaError_t e) {
   return 6;  // CAMOE_ERR_CUDA
 }
 
+// n is k * C, a multiple of 64; part (the workspace) and out are 16-byte aligned
 int reduce(const float* part, int G, int64_t n, float* out, cudaStream_t st) {
-  const int64_t blocks = (n + 31) / 32;
-  partial_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(part, G, n, out);
+  const int64_t n4 = n / 4, blocks = (n4 + 3) / 4;
+  partial_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      reinterpret_cast<const float4*>(part), G, n4, reinterpret_cast<float4*>(out));
   return status(cudaGetLastError());
+}
+
+// f(std::integral_constant<int, J>) for J = C / 64 in 1..16 (C <= 1024); false
+// for wider rows, which the C/8-thread kernels take
+template <typename F>
+bool with_pairs(int64_t C, F&& f) {
+  switch (C / 64) {
+#define CAMOE_TM_PAIRS(J) \
+    case J:               \
+      f(std::integral_constant<int, J>{}); \
+      return true;
+    CAMOE_TM_PAIRS(1) CAMOE_TM_PAIRS(2) CAMOE_TM_PAIRS(3) CAMOE_TM_PAIRS(4)
+    CAMOE_TM_PAIRS(5) CAMOE_TM_PAIRS(6) CAMOE_TM_PAIRS(7) CAMOE_TM_PAIRS(8)
+    CAMOE_TM_PAIRS(9) CAMOE_TM_PAIRS(10) CAMOE_TM_PAIRS(11) CAMOE_TM_PAIRS(12)
+    CAMOE_TM_PAIRS(13) CAMOE_TM_PAIRS(14) CAMOE_TM_PAIRS(15) CAMOE_TM_PAIRS(16)
+#undef CAMOE_TM_PAIRS
+    default:
+      return false;
+  }
 }
 
 }  // namespace tm
@@ -989,8 +1175,16 @@ int camoe_tm_lnsa_fwd(const float* sa, const float* weight, const float* bias, f
   int st = precheck(B, T, C, {sa, weight, bias, out}, {});
   if (st != 0) return st < 0 ? 0 : st;
   const Shape S = make_shape(B, T, C);
-  camoe::tm::lnsa_fwd_kernel<<<camoe::tm::grid_for(camoe::tm::lnsa_fwd_kernel, S), static_cast<unsigned>(C / camoe::tm::V), 0,
-                               static_cast<cudaStream_t>(stream)>>>(sa, weight, bias, out, S);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool rows = camoe::tm::with_pairs(C, [&](auto pairs) {
+    constexpr int J = decltype(pairs)::value;
+    const auto k = camoe::tm::lnsa_fwd_rows_kernel<J>;
+    const int G = camoe::tm::grid_for(k, S, 0, 32 * camoe::tm::kRowWarps);
+    k<<<G, 32 * camoe::tm::kRowWarps, 0, s>>>(sa, weight, bias, out, B * T);
+  });
+  if (!rows)
+    camoe::tm::lnsa_fwd_kernel<<<camoe::tm::grid_for(camoe::tm::lnsa_fwd_kernel, S),
+                                 static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(sa, weight, bias, out, S);
   return camoe::tm::status(cudaGetLastError());
 }
 
@@ -1005,10 +1199,20 @@ int camoe_tm_lnsa_bwd(const float* dout, const float* sa, const float* weight, f
   }
   const Shape S = make_shape(B, T, C);
   if ((st = check_work(S, work, work_bytes)) != 0) return st;
-  const int G = camoe::tm::grid_for(camoe::tm::lnsa_bwd_kernel, S);
   float* part = static_cast<float*>(work);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  camoe::tm::lnsa_bwd_kernel<<<G, static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(dout, sa, weight, dsa, part, S);
+  int G = 0;
+  const bool rows = camoe::tm::with_pairs(C, [&](auto pairs) {
+    constexpr int J = decltype(pairs)::value;
+    const auto k = camoe::tm::lnsa_bwd_rows_kernel<J>;
+    const size_t smem = camoe::tm::lnsa_rows_smem(J);
+    G = camoe::tm::grid_for(k, S, smem, 32 * camoe::tm::kRowWarps);
+    k<<<G, 32 * camoe::tm::kRowWarps, smem, s>>>(dout, sa, weight, dsa, part, B * T);
+  });
+  if (!rows) {
+    G = camoe::tm::grid_for(camoe::tm::lnsa_bwd_kernel, S);
+    camoe::tm::lnsa_bwd_kernel<<<G, static_cast<unsigned>(C / camoe::tm::V), 0, s>>>(dout, sa, weight, dsa, part, S);
+  }
   if ((st = camoe::tm::status(cudaGetLastError())) != 0) return st;
   return camoe::tm::reduce(part, G, 2 * C, dparams, s);
 }
