@@ -87,9 +87,18 @@ __device__ __forceinline__ float sum8(const float (&a)[V]) {
   return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
 }
 
-__device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
-// torch.nn.functional.softplus with its default threshold 20
-__device__ __forceinline__ float softplus(float z) { return z > 20.0f ? z : log1pf(expf(z)); }
+// The gates and the decay input end in bf16 (8 significant bits), so they
+// use the hardware's base-2 exponential and logarithm (__expf, __logf: a few
+// ulp) and an approximate reciprocal (__fdividef): an IEEE division or log1pf
+// takes ten to twenty instructions each, which left prep_fwd issue-bound at
+// about half of HBM bandwidth.  1 / (1 + inf) is 0, as the limit wants.
+__device__ __forceinline__ float sigm(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// torch's softplus with threshold 20; its error (a few ulp of __expf and
+// __logf, and below z = -16.6 a result of 0 where e^z < 6e-8) stays below
+// 1e-5 of the decay input -softplus(-u) - 1/2, which is rounded to bf16
+__device__ __forceinline__ float softplus(float z) { return z > 20.0f ? z : __logf(1.0f + __expf(z)); }
+// 1 / max(sqrt(ss), 1e-12): F.normalize's divisor, as one reciprocal square root
+__device__ __forceinline__ float inv_norm(float ss) { return rsqrtf(fmaxf(ss, 1e-24f)); }
 
 // rows [t0, t1) of sequence b for work item `item`
 __device__ __forceinline__ void item_rows(const Shape& S, int64_t item, int64_t& b, int64_t& t0,
@@ -275,7 +284,7 @@ __global__ void __launch_bounds__(1024) prep_fwd_kernel(PrepFwd p, Shape S) {
           }
           const float a_0 = sigm(a0.x + al[u].x), a_1 = sigm(a0.y + al[u].y);
           const float kr0 = k[u].x * kk_.x, kr1 = k[u].y * kk_.y;
-          const float inv = 1.0f / fmaxf(sqrtf(warp_sum(kr0 * kr0 + kr1 * kr1)), 1e-12f);
+          const float inv = inv_norm(warp_sum(kr0 * kr0 + kr1 * kr1));
           const float kn0 = kr0 * inv, kn1 = kr1 * inv;
           if (u >= nu) continue;
           st2(p.w + o, -softplus(-(w0.x + wl[u].x)) - 0.5f, -softplus(-(w0.y + wl[u].y)) - 0.5f);
@@ -348,9 +357,9 @@ __global__ void __launch_bounds__(1024) prep_bwd_kernel(PrepBwd p, float* __rest
         }
         const float a[2] = {sigm(a0.x + al[u].x), sigm(a0.y + al[u].y)};
         const float kr[2] = {kv[0] * kkv[0], kv[1] * kkv[1]};
-        const float nrm = sqrtf(warp_sum(kr[0] * kr[0] + kr[1] * kr[1]));
-        const float den = fmaxf(nrm, 1e-12f);
-        const float kn[2] = {kr[0] / den, kr[1] / den};
+        const float ss = warp_sum(kr[0] * kr[0] + kr[1] * kr[1]);
+        const float inv = inv_norm(ss);  // 1 / max(|kr|, 1e-12)
+        const float kn[2] = {kr[0] * inv, kr[1] * inv};
         const float gav[2] = {ga[u].x * on, ga[u].y * on}, gbv[2] = {gb[u].x * on, gb[u].y * on};
         float dkn[2], da[2], dk[2];
 #pragma unroll
@@ -365,7 +374,7 @@ __global__ void __launch_bounds__(1024) prep_bwd_kernel(PrepBwd p, float* __rest
         float dal[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const float dkr = nrm > 1e-12f ? (dkn[e] - kn[e] * dot) / den : dkn[e] / den;
+          const float dkr = (ss > 1e-24f ? dkn[e] - kn[e] * dot : dkn[e]) * inv;
           dk[e] += dkr * kkv[e];
           acc[3][e] += dkr * kv[e];
           dal[e] = da[e] * a[e] * (1.f - a[e]);
