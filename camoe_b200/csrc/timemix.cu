@@ -121,6 +121,8 @@ __device__ __forceinline__ void st2(bf16* p, float a, float b) {
 __device__ __forceinline__ void st2(float* p, float a, float b) {
   *reinterpret_cast<float2*>(p) = make_float2(a, b);
 }
+__device__ __forceinline__ float2 f2(const __nv_bfloat162& v) { return __bfloat1622float2(v); }
+__device__ __forceinline__ float2 f2(const float2& v) { return v; }
 __device__ __forceinline__ float warp_sum(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
@@ -189,59 +191,81 @@ __global__ void __launch_bounds__(256) mix_fwd_kernel(const Tx* __restrict__ x,
 }
 
 // dx[t] = sum_m dx_m[t] (1 - mix_m) + sum_m dx_m[t+1] mix_m;  dmix_m = sum_t dx_m[t] xx[t]
-// Rows are walked downwards (dx_m[t+1] is the previous row's).
+// With s[t] = sum_m dx_m[t] and q[t] = sum_m dx_m[t] mix_m this is
+// dx[t] = s[t] - q[t] + q[t+1]: rows are walked downwards carrying one q per
+// column instead of the six dx_m of the next row.  Each CTA takes a contiguous
+// range of work items (the walk goes down through it, so q carries from item to
+// item and is loaded only for the row after the range), which leaves the
+// registers for a whole item's rows, all of whose loads are issued before the
+// first is used.  The mixes sit in shared memory, each thread reading back its
+// own columns.
 template <typename Tx>
 __global__ void __launch_bounds__(1024) mix_bwd_kernel(const Tx* __restrict__ x,
                                                        const float* __restrict__ mix, In6 dout,
                                                        Tx* __restrict__ dx,
                                                        float* __restrict__ part, Shape S) {
-  constexpr int U = 2;
-  const int c = 2 * threadIdx.x;
+  using X2 = typename std::conditional<std::is_same<Tx, float>::value, float2, __nv_bfloat162>::type;
+  extern __shared__ float2 mxs[];  // [6][C / 2]: the mixes of each thread's columns
+  const int c = 2 * threadIdx.x, nt = blockDim.x;
   const int64_t C = S.C;
-  float a0[6], a1[6];
+  float2 acc[6];
 #pragma unroll
-  for (int m = 0; m < 6; ++m) a0[m] = a1[m] = 0.f;
-  for (int64_t item = blockIdx.x; item < S.items(); item += gridDim.x) {
+  for (int m = 0; m < 6; ++m) {
+    mxs[m * nt + threadIdx.x] = ld2(mix + m * C + c);
+    acc[m] = make_float2(0.f, 0.f);
+  }
+  const float2* mx = mxs + threadIdx.x;  // mx[m * nt]: read back by this thread only
+  const int64_t n = S.items();
+  const int64_t i0 = blockIdx.x * n / gridDim.x, i1 = (blockIdx.x + 1) * n / gridDim.x;
+  float2 qn = make_float2(0.f, 0.f);  // q of the row after the current item
+  for (int64_t item = i1 - 1; item >= i0; --item) {
     int64_t b, t0, t1;
     item_rows(S, item, b, t0, t1);
-    float2 dn[6];  // dx_m of the step after the current one
+    const int64_t o = (b * S.T + t0) * C + c;  // row t0, this thread's columns
+    if (t1 == S.T) {
+      qn = make_float2(0.f, 0.f);  // past the sequence's end
+    } else if (item == i1 - 1) {   // the row after the range: another CTA's
+      const int64_t on = o + (t1 - t0) * C;
 #pragma unroll
-    for (int m = 0; m < 6; ++m)
-      dn[m] = t1 < S.T ? ld2(dout.p[m] + (b * S.T + t1) * C + c) : make_float2(0.f, 0.f);
-    float2 xc = ld2(x + (b * S.T + t1 - 1) * C + c);
-    for (int64_t tb = t1 - 1; tb >= t0; tb -= U) {   // rows tb, tb - 1, ...
-      const int nu = tb - t0 + 1 < U ? static_cast<int>(tb - t0 + 1) : U;
-      const int64_t o0 = (b * S.T + tb) * C + c;
-      float2 d[U][6], xp[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int uu = u < nu ? u : nu - 1;  // rows past the item repeat its last one
-#pragma unroll
-        for (int m = 0; m < 6; ++m) d[u][m] = ld2(dout.p[m] + o0 - uu * C);
-        xp[u] = tb - uu > 0 ? ld2(x + o0 - (uu + 1) * C) : make_float2(0.f, 0.f);
+      for (int m = 0; m < 6; ++m) {
+        const float2 g = ld2(dout.p[m] + on), w = mx[m * nt];
+        qn.x += g.x * w.x;
+        qn.y += g.y * w.y;
       }
+    }  // else qn is the q of row t1, the last row walked in item + 1
+    __nv_bfloat162 d[kRows][6];  // rows past the item repeat its last one
+    X2 xr[kRows + 1];            // x[t0 - 1 + u], as loaded
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const float on = u < nu ? 1.f : 0.f;
-        const float xx0 = (xp[u].x - xc.x) * on, xx1 = (xp[u].y - xc.y) * on;
-        float g0 = 0.f, g1 = 0.f;
+    for (int u = 0; u < kRows; ++u) {
+      const int64_t ou = o + (t0 + u < t1 ? u : t1 - 1 - t0) * C;
 #pragma unroll
-        for (int m = 0; m < 6; ++m) {
-          const float mx0 = __ldg(mix + m * C + c), mx1 = __ldg(mix + m * C + c + 1);
-          g0 += d[u][m].x * (1.f - mx0) + dn[m].x * mx0;
-          g1 += d[u][m].y * (1.f - mx1) + dn[m].y * mx1;
-          a0[m] += d[u][m].x * xx0;
-          a1[m] += d[u][m].y * xx1;
-          dn[m] = d[u][m];
-        }
-        if (u < nu) st2(dx + o0 - u * C, g0, g1);
-        xc = xp[u];
+      for (int m = 0; m < 6; ++m) d[u][m] = *reinterpret_cast<const __nv_bfloat162*>(dout.p[m] + ou);
+      xr[u + 1] = *reinterpret_cast<const X2*>(x + ou);
+    }
+    if (t0 > 0) xr[0] = *reinterpret_cast<const X2*>(x + o - C);
+#pragma unroll
+    for (int u = kRows - 1; u >= 0; --u) {
+      if (t0 + u >= t1) continue;  // the same for the whole CTA
+      float2 s = make_float2(0.f, 0.f), q = make_float2(0.f, 0.f);
+      const float2 xa = u > 0 || t0 > 0 ? f2(xr[u]) : make_float2(0.f, 0.f), xb = f2(xr[u + 1]);
+      const float2 xx = make_float2(xa.x - xb.x, xa.y - xb.y);
+#pragma unroll
+      for (int m = 0; m < 6; ++m) {
+        const float2 g = __bfloat1622float2(d[u][m]), w = mx[m * nt];
+        s.x += g.x;
+        s.y += g.y;
+        q.x += g.x * w.x;
+        q.y += g.y * w.y;
+        acc[m].x += g.x * xx.x;
+        acc[m].y += g.y * xx.y;
       }
+      st2(dx + o + u * C, s.x - q.x + qn.x, s.y - q.y + qn.y);
+      qn = q;
     }
   }
   float* pp = part + static_cast<int64_t>(blockIdx.x) * 6 * C;
 #pragma unroll
-  for (int m = 0; m < 6; ++m) st2(pp + m * C + c, a0[m], a1[m]);
+  for (int m = 0; m < 6; ++m) st2(pp + m * C + c, acc[m].x, acc[m].y);
 }
 
 // -------------------------------------------------------------------------
@@ -1056,15 +1080,16 @@ int camoe_tm_mix_bwd(const void* x, int x_dtype, const float* mix, const void* c
   camoe::tm::In6 d;
   for (int m = 0; m < 6; ++m) d.p[m] = static_cast<const bf16*>(dout[m]);
   const int threads = static_cast<int>(C / 2);  // two columns per thread
-  const int G = x_dtype == 0 ? camoe::tm::grid_for(camoe::tm::mix_bwd_kernel<bf16>, S, 0, threads)
-                             : camoe::tm::grid_for(camoe::tm::mix_bwd_kernel<float>, S, 0, threads);
+  const size_t smem = 6 * static_cast<size_t>(C) * sizeof(float);  // the mixes, <= 48 KiB
+  const int G = x_dtype == 0 ? camoe::tm::grid_for(camoe::tm::mix_bwd_kernel<bf16>, S, smem, threads)
+                             : camoe::tm::grid_for(camoe::tm::mix_bwd_kernel<float>, S, smem, threads);
   float* part = static_cast<float*>(work);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (x_dtype == 0)
-    camoe::tm::mix_bwd_kernel<bf16><<<G, threads, 0, s>>>(
+    camoe::tm::mix_bwd_kernel<bf16><<<G, threads, smem, s>>>(
         static_cast<const bf16*>(x), mix, d, static_cast<bf16*>(dx), part, S);
   else
-    camoe::tm::mix_bwd_kernel<float><<<G, threads, 0, s>>>(
+    camoe::tm::mix_bwd_kernel<float><<<G, threads, smem, s>>>(
         static_cast<const float*>(x), mix, d, static_cast<float*>(dx), part, S);
   if ((st = camoe::tm::status(cudaGetLastError())) != 0) return st;
   return camoe::tm::reduce(part, G, 6 * C, dmix, s);
