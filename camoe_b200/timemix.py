@@ -9,7 +9,8 @@ What runs:
 
 * projections (receptance, key, value, output) and the LoRA products: bf16
   GEMMs (cuBLAS through torch), weights cast from the fp32 parameters per
-  call as autocast does; the two LoRA hidden activations (tanh for the decay,
+  call as autocast does, their gradients written by the GEMMs in fp32
+  (``MatmulBf16Fn``); the two LoRA hidden activations (tanh for the decay,
   sigmoid for the gate, on [B, T, D] with D <= 160) are torch ops;
 * everything else is four fused CUDA kernels (include/camoe_timemix.h), each
   one pass over HBM, and the WKV-7 op itself:
@@ -61,6 +62,34 @@ def _stream(t):
 def _work(B, T, C, device):
     n = int(_lib.lib().camoe_tm_work_bytes(B, T, C))
     return torch.empty(max(n, 16), dtype=torch.uint8, device=device), n
+
+
+class MatmulBf16Fn(torch.autograd.Function):
+    """x @ w (or x @ w^T for ``F.linear``'s layout) with the fp32 parameter w
+    cast to bf16 per call, as autocast casts it for the reference's
+    projections and LoRA products.  The backward has the GEMM write w's
+    gradient in fp32 directly (cuBLAS accumulates in fp32 either way), where
+    autocast's path writes it in bf16 and converts it with one more kernel per
+    weight; the input's gradient stays bf16."""
+
+    @staticmethod
+    def forward(ctx, x, w, transposed: bool):
+        wb = w.to(_BF)
+        ctx.transposed = transposed
+        ctx.save_for_backward(x, wb)
+        return x @ (wb.t() if transposed else wb)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, wb = ctx.saved_tensors
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = dy @ (wb if ctx.transposed else wb.t())
+        if ctx.needs_input_grad[1]:
+            x2, dy2 = x.reshape(-1, x.shape[-1]), dy.reshape(-1, dy.shape[-1])
+            dw = (torch.mm(dy2.t(), x2, out_dtype=torch.float32) if ctx.transposed
+                  else torch.mm(x2.t(), dy2, out_dtype=torch.float32))
+        return dx, dw, None
 
 
 class Mix6Fn(torch.autograd.Function):
@@ -239,26 +268,26 @@ class RWKV7TimeMix(nn.Module):
         mix = torch.cat([getattr(self, n).view(1, C) for n in
                          ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g")])
         xr, xw, xk, xv, xa, xg = Mix6Fn.apply(x, mix)
-        W = (lambda m: m.weight.to(_BF))
-        P = (lambda t: t.to(_BF))
-        r = F.linear(xr, W(self.receptance))
-        k = F.linear(xk, W(self.key))
-        v = F.linear(xv, W(self.value))
-        wl = torch.tanh(xw @ P(self.w1)) @ P(self.w2)
-        al = (xa @ P(self.a1)) @ P(self.a2)
-        g = torch.sigmoid(xg @ P(self.g1)) @ P(self.g2)
+        L = (lambda t, m: MatmulBf16Fn.apply(t, m.weight, True))  # F.linear(t, bf16(W))
+        P = (lambda t, w: MatmulBf16Fn.apply(t, w, False))         # t @ bf16(w)
+        r = L(xr, self.receptance)
+        k = L(xk, self.key)
+        v = L(xv, self.value)
+        wl = P(torch.tanh(P(xw, self.w1)), self.w2)
+        al = P(P(xa, self.a1), self.a2)
+        g = P(torch.sigmoid(P(xg, self.g1)), self.g2)
         if self.layer_id == 0:
             vl = vf = None
         else:
             if v_first is None:
                 raise ValueError("layers after the first need v_first")
-            vl = (xv @ P(self.v1)) @ P(self.v2)
+            vl = P(P(xv, self.v1), self.v2)
             vf = v_first.to(_BF)
         prep_par = torch.cat([t.view(1, C) for t in (self.w0, self.v0, self.a0, self.k_k, self.k_a)])
         z, srep = Wkv7BlockFn.apply(r, wl, k, v, vl, al, vf, g, prep_par, self.r_k,
                                     self.ln_x.weight, self.ln_x.bias, self.ln_sa.weight,
                                     self.ln_sa.bias, self.algo)
-        out = F.linear(z, W(self.output))
+        out = L(z, self.output)
         if self.layer_id == 0:
             v_first = v
         return out, v_first, srep
