@@ -31,7 +31,7 @@ DEFAULT_WAIT_LIMIT = 2000000000
 TM_EXPORTS = ("camoe_tm_work_bytes", "camoe_tm_mix_fwd", "camoe_tm_mix_fwd_prev",
               "camoe_tm_mix_bwd", "camoe_tm_prep_fwd",
               "camoe_tm_prep_bwd", "camoe_tm_post_fwd", "camoe_tm_post_bwd", "camoe_tm_lnsa_fwd",
-              "camoe_tm_lnsa_bwd")
+              "camoe_tm_lnsa_bwd", "camoe_tm_lora_work_bytes", "camoe_tm_lora_wgrad")
 
 
 class CamoeError(RuntimeError):
@@ -96,8 +96,11 @@ def lib() -> ctypes.CDLL:
     l.camoe_tm_post_bwd.argtypes = [vp] * 16 + [sz] + [i64] * 3 + [vp]
     l.camoe_tm_lnsa_fwd.argtypes = [vp] * 4 + [i64] * 3 + [vp]
     l.camoe_tm_lnsa_bwd.argtypes = [vp] * 6 + [sz] + [i64] * 3 + [vp]
+    l.camoe_tm_lora_wgrad.argtypes = [vp, vp, vp, ci, vp, sz] + [i64] * 3 + [vp]
     for n in TM_EXPORTS[1:]:
         getattr(l, n).restype = ci
+    l.camoe_tm_lora_work_bytes.restype = sz
+    l.camoe_tm_lora_work_bytes.argtypes = [i64] * 3
     # the wind op's entry points take the ClampW ones' argument types
     l.camoe_wkv7_wind_fwd.restype = ci
     l.camoe_wkv7_wind_fwd.argtypes = l.camoe_wkv7_fwd.argtypes

@@ -51,6 +51,21 @@ bool encode_bhtn(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_2d_sw128(CUtensorMap* map, const void* base, int64_t inner, int64_t rows,
+                     int box_rows) {
+  const EncodeFn fn = encode_fn();
+  if (fn == nullptr || inner < 64 || rows <= 0 || (inner * 2) % 16 != 0 || box_rows <= 0 ||
+      box_rows > 256)
+    return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 2};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estride[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool encode_bhtn_f32(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H) {
   const EncodeFn fn = encode_fn();
   if (fn == nullptr || B <= 0 || T <= 0 || H <= 0) return false;

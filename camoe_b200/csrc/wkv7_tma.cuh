@@ -44,6 +44,25 @@ bool encode_bhtn_f32(CUtensorMap* map, const void* base, int64_t B, int64_t T, i
 bool encode_bhtn_cols(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H,
                       int n_box, bool f32);
 
+// Map of a row-major bf16 [rows, inner] matrix with a {64, box_rows} box and
+// the 128-byte swizzle (each box lands as box_rows rows of 128 bytes, 16-byte
+// pieces XOR-swizzled by row % 8); boxes past either extent read zeros.
+// inner x 2 bytes must be a multiple of 16.
+bool encode_2d_sw128(CUtensorMap* map, const void* base, int64_t inner, int64_t rows,
+                     int box_rows);
+
+// Load the box at (x, y) of a 2-D map, completing on `bar`.
+__device__ __forceinline__ void load_2d(void* dst_smem, const CUtensorMap* map, int x, int y,
+                                        uint64_t* bar) {
+  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem));
+  const uint32_t mb = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mb)
+      : "memory");
+}
+
 __device__ __forceinline__ void load_tile(void* dst_smem, const CUtensorMap* map, int h,
                                           int t0, int b, uint64_t* bar) {
   const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem));

@@ -64,13 +64,49 @@ def _work(B, T, C, device):
     return torch.empty(max(n, 16), dtype=torch.uint8, device=device), n
 
 
+def lora_work_bytes(R: int, C: int, D: int) -> int:
+    """camoe_tm_lora_work_bytes(R, C, D) without the call: one fp32 [C, D] partial
+    sum per slice of 64-row stages, at most 16 slices (lora_tc.cu)."""
+    return min(16, max(1, -(-R // 64))) * C * D * 4
+
+
+def _weight_grad(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a^T b in fp32 for 2-D bf16 a [R, m], b [R, n]: the weight gradient of a
+    product.  Where one side is a LoRA rank (a multiple of 32 from 64 to 256)
+    and the other a multiple of 128, the tcgen05 kernel camoe_tm_lora_wgrad
+    reduces over the R rows (include/camoe_timemix.h); the square projections
+    stay with cuBLAS."""
+    R, m = a.shape
+    n = b.shape[1]
+    if a.is_cuda and a.dtype == _BF and b.dtype == _BF and R > 0:
+        rank = (lambda d: d % 32 == 0 and 64 <= d <= 256)
+        big = None
+        if m % 128 == 0 and rank(n):
+            big, thin, C, D, out_cd = a, b, m, n, 1   # [m][n] = [C][D]
+        elif n % 128 == 0 and rank(m):
+            big, thin, C, D, out_cd = b, a, n, m, 0   # [m][n] = [D][C]
+        if big is not None:
+            big, thin = big.contiguous(), thin.contiguous()
+            nw = lora_work_bytes(R, C, D)
+            # one allocation (host time counts when the step is dispatched eagerly):
+            # the partial sums, then the gradient
+            buf = torch.empty(nw + 4 * m * n, dtype=torch.uint8, device=a.device)
+            dw = buf[nw:].view(torch.float32).view(m, n)
+            check(_lib.lib().camoe_tm_lora_wgrad(big.data_ptr(), thin.data_ptr(), dw.data_ptr(),
+                                                 out_cd, buf.data_ptr(), nw, R, C, D,
+                                                 torch.cuda.current_stream(a.device).cuda_stream))
+            return dw
+    return torch.mm(a.t(), b, out_dtype=torch.float32)
+
+
 class MatmulBf16Fn(torch.autograd.Function):
     """x @ w (or x @ w^T for ``F.linear``'s layout) with the fp32 parameter w
     cast to bf16 per call, as autocast casts it for the reference's
-    projections and LoRA products.  The backward has the GEMM write w's
-    gradient in fp32 directly (cuBLAS accumulates in fp32 either way), where
-    autocast's path writes it in bf16 and converts it with one more kernel per
-    weight; the input's gradient stays bf16."""
+    projections and LoRA products.  The backward writes w's gradient in fp32
+    directly (``_weight_grad``: the LoRA ranks' tcgen05 kernel, else a cuBLAS
+    GEMM with fp32 output), where autocast's path writes it in bf16 and
+    converts it with one more kernel per weight; the input's gradient stays
+    bf16."""
 
     @staticmethod
     def forward(ctx, x, w, transposed: bool):
@@ -87,8 +123,7 @@ class MatmulBf16Fn(torch.autograd.Function):
             dx = dy @ (wb if ctx.transposed else wb.t())
         if ctx.needs_input_grad[1]:
             x2, dy2 = x.reshape(-1, x.shape[-1]), dy.reshape(-1, dy.shape[-1])
-            dw = (torch.mm(dy2.t(), x2, out_dtype=torch.float32) if ctx.transposed
-                  else torch.mm(x2.t(), dy2, out_dtype=torch.float32))
+            dw = _weight_grad(dy2, x2) if ctx.transposed else _weight_grad(x2, dy2)
         return dx, dw, None
 
 

@@ -100,6 +100,19 @@ int camoe_tm_lnsa_bwd(const float* dout, const float* sa, const float* weight, f
                       float* dparams, void* work, size_t work_bytes, int64_t B, int64_t T,
                       int64_t C, void* stream);
 
+/* Weight gradient of one LoRA product (camoe/backbone.py:326-341, x @ w1 and
+ * h @ w2, whose gradients the reference gets from autograd through cuBLAS):
+ * T[c][d] = sum over the R rows of big[r][c] thin[r][d], big an [R, C] and thin
+ * an [R, D] bf16 matrix (row-major, contiguous), written to dw (fp32) as [C][D]
+ * (out_cd = 1: the gradient of w1 [C, D] from x and dh) or [D][C] (out_cd = 0:
+ * the gradient of w2 [D, C] from h and dy).  C a multiple of 128, D a multiple
+ * of 32 from 64 to 256; the workspace holds camoe_tm_lora_work_bytes(R, C, D)
+ * bytes of per-slice partial sums, added in a fixed order (deterministic).
+ * Runs on the tcgen05 tensor cores (lora_tc.cu).  R = 0 writes zeros. */
+size_t camoe_tm_lora_work_bytes(int64_t R, int64_t C, int64_t D);
+int camoe_tm_lora_wgrad(const void* big, const void* thin, float* dw, int out_cd, void* work,
+                        size_t work_bytes, int64_t R, int64_t C, int64_t D, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

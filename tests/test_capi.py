@@ -251,3 +251,30 @@ def test_test_hooks_reject_out_of_range_arguments():
     assert lib.camoe_wkv7_test_hooks(999, -1) == _lib.ERR_INVALID_ARG
     assert lib.camoe_wkv7_test_hooks(_lib.DEFAULT_WAIT_LIMIT + 1, -1) == _lib.ERR_INVALID_ARG
     assert lib.camoe_wkv7_test_hooks(_lib.DEFAULT_WAIT_LIMIT, -2) == _lib.ERR_INVALID_ARG
+
+
+def test_lora_wgrad_argument_errors_need_no_device():
+    """Shape, null and alignment errors return before any CUDA call."""
+    lib = _lib.lib()
+    fake, odd = ctypes.c_void_p(1 << 20), ctypes.c_void_p((1 << 20) + 8)
+    call = (lambda big, thin, dw, out_cd, work, nw, R, C, D:
+            lib.camoe_tm_lora_wgrad(big, thin, dw, out_cd, work, nw, R, C, D, None))
+    assert lib.camoe_tm_lora_work_bytes(8192, 1024, 160) == 16 * 1024 * 160 * 4
+    assert lib.camoe_tm_lora_work_bytes(5, 128, 64) == 1 * 128 * 64 * 4
+    assert call(fake, fake, fake, 1, fake, 1 << 30, 64, 1024, 48) == _lib.ERR_UNSUPPORTED  # D % 32
+    assert call(fake, fake, fake, 1, fake, 1 << 30, 64, 1024, 32) == _lib.ERR_UNSUPPORTED  # D < 64
+    assert call(fake, fake, fake, 1, fake, 1 << 30, 64, 192, 64) == _lib.ERR_UNSUPPORTED   # C % 128
+    assert call(fake, fake, fake, 1, fake, 1 << 30, 64, 1024, 288) == _lib.ERR_UNSUPPORTED  # D > 256
+    assert call(fake, fake, fake, 2, fake, 1 << 30, 64, 1024, 64) == _lib.ERR_INVALID_ARG
+    assert call(None, fake, fake, 1, fake, 1 << 30, 64, 1024, 64) == _lib.ERR_INVALID_ARG
+    assert call(odd, fake, fake, 1, fake, 1 << 30, 64, 1024, 64) == _lib.ERR_ALIGNMENT
+    assert call(fake, fake, fake, 1, None, 1 << 30, 64, 1024, 64) == _lib.ERR_INVALID_ARG
+    assert call(fake, fake, fake, 1, fake, 16, 64, 1024, 64) == _lib.ERR_WORKSPACE
+
+
+def test_lora_work_bytes_matches_the_python_sizing():
+    from camoe_b200 import timemix
+    lib = _lib.lib()
+    for R in (1, 5, 63, 64, 65, 1000, 1024, 1025, 8192, 100000):
+        for C, D in ((1024, 64), (128, 160), (2048, 256)):
+            assert lib.camoe_tm_lora_work_bytes(R, C, D) == timemix.lora_work_bytes(R, C, D)

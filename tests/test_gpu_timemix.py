@@ -392,3 +392,44 @@ def test_forward_state_prefill_then_decode_equals_one_pass(layer_id):
     close(torch.cat(srs, 1), srep, 2e-2, "state_representation")
     close(torch.cat(vfs, 1), vf_out, 2e-2, "v_first")
     assert state[0].shape == (B, C) and state[1].shape == (B, C // 64, 64, 64)
+
+
+# R = 5 and 1000: ragged last stages (rows past R load as zeros); D = 96 and
+# 160 padded to 128 and 192 columns; D = 256 the largest rank; C = 128 one tile
+@pytest.mark.parametrize("R,C,D,out_cd", [(5, 128, 96, 0), (1000, 128, 64, 1),
+                                          (200, 256, 256, 1), (8192, 1024, 160, 1),
+                                          (8192, 1024, 64, 0)])
+def test_lora_wgrad(R, C, D, out_cd):
+    """camoe_tm_lora_wgrad (tcgen05) against the product in float64, bit-identical
+    on a second call (fixed-order reduction), and no bounded wait ran out."""
+    g = torch.Generator().manual_seed(R + D)
+    big = torch.randn(R, C, generator=g).to(BF).cuda()
+    thin = torch.randn(R, D, generator=g).to(BF).cuda()
+    L = _lib.lib()
+    errs = L.camoe_wkv7_device_errors()
+    nw = int(L.camoe_tm_lora_work_bytes(R, C, D))
+    work = torch.empty(max(nw, 16), dtype=torch.uint8, device="cuda")
+    outs = []
+    for _ in range(2):
+        dw = torch.full((C, D) if out_cd else (D, C), float("nan"), device="cuda")
+        assert L.camoe_tm_lora_wgrad(p(big), p(thin), p(dw), out_cd, p(work), nw, R, C, D,
+                                     stream()) == 0
+        outs.append(dw)
+    torch.cuda.synchronize()
+    want = big.double().t() @ thin.double()
+    close(outs[0], want if out_cd else want.t(), 1e-5, "dw")
+    assert torch.equal(outs[0], outs[1])
+    assert L.camoe_wkv7_device_errors() == errs
+
+
+def test_weight_grad_routes_lora_shapes():
+    """The time mix's weight gradients: LoRA shapes through the kernel, both
+    orientations, and a square projection and a rank of 32 through cuBLAS,
+    all against float64."""
+    g = torch.Generator().manual_seed(7)
+    for m, n in ((1024, 64), (160, 1024), (1024, 1024), (1024, 32)):
+        a = torch.randn(3000, m, generator=g).to(BF).cuda()
+        b = torch.randn(3000, n, generator=g).to(BF).cuda()
+        got = timemix._weight_grad(a, b)
+        assert got.dtype == torch.float32 and got.shape == (m, n)
+        close(got, a.double().t() @ b.double(), 1e-5, f"{m}x{n}")
