@@ -29,7 +29,8 @@ the segment counts).  Other workloads print their own lines:
 ``decode_b1024_h16`` (one generated token through the decode-step kernel,
 bf16 and fp32, and prefills from a start state), ``timemix_b8_t1024_c1024``
 (the fused time mix: layer forward+backward against the op-by-op layer, a
-stateful decode token, and each fused kernel alone against HBM bandwidth).
+stateful decode token, and each fused kernel, and the tcgen05 LoRA weight
+gradient per rank, alone against HBM bandwidth).
 
 ``--impl reference`` times the CPU oracle port of the reference's recurrence
 (fp32, every host thread) on a bounded sample of the same workload and prints
@@ -914,7 +915,8 @@ def run_timemix(args, B=8, T=1024, C=1024, layer=2, steps=20):
     replayed from a CUDA graph) against the same layer op by op; one decode token
     with the state carried against re-running the layer over the context (what
     the reference's generation loop does per token, eval.py:212); and each fused
-    kernel alone (L2 flushed before each launch) against HBM bandwidth."""
+    kernel, and the tcgen05 LoRA weight gradient per rank, alone (L2 flushed
+    before each launch) against HBM bandwidth."""
     import ctypes
 
     from camoe_b200 import _lib, backbone, timemix
@@ -1018,6 +1020,20 @@ def run_timemix(args, B=8, T=1024, C=1024, layer=2, steps=20):
         "lnsa_bwd": (lambda: L.camoe_tm_lnsa_bwd(P(dsrep), P(sa), P(par2[0]), P(dsa), P(dpar),
                                                  P(work), nw, B, T, C, st), 12 * n),
     }
+    # the LoRA weight gradients (tcgen05): bytes = the [R, C] and [R, D] bf16
+    # operands read once and the fp32 [C, D] gradient written once, R = B T
+    R = B * T
+    lw = {}
+    for D in sorted(set(timemix.lora_dims(C).values())):
+        if D % 32 or not 64 <= D <= 256:
+            continue
+        lw[D] = (torch.randn(R, D, device="cuda", dtype=BF), torch.empty(C, D, device="cuda"),
+                 int(L.camoe_tm_lora_work_bytes(R, C, D)))
+        lw[D] += (torch.empty(lw[D][2], dtype=torch.uint8, device="cuda"),)
+        calls[f"lora_wgrad_d{D}"] = (
+            (lambda D=D: L.camoe_tm_lora_wgrad(P(xk), P(lw[D][0]), P(lw[D][1]), 1, P(lw[D][3]),
+                                               lw[D][2], R, C, D, st)),
+            R * C * 2 + R * D * 2 + C * D * 4)
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB, twice the L2
     for name, (fn, nbytes) in calls.items():
         assert fn() == 0, name
