@@ -25,6 +25,7 @@
 
 #include "camoe_timemix.h"
 #include "wkv7_common.cuh"
+#include "wkv7_sync.cuh"
 
 namespace camoe {
 void set_last_cuda_error(int e);  // wkv7_capi.cu: reported by camoe_wkv7_last_cuda_error()
@@ -262,6 +263,134 @@ __global__ void __launch_bounds__(1024) mix_bwd_kernel(const Tx* __restrict__ x,
       st2(dx + o + u * C, s.x - q.x + qn.x, s.y - q.y + qn.y);
       qn = q;
     }
+  }
+  float* pp = part + static_cast<int64_t>(blockIdx.x) * 6 * C;
+#pragma unroll
+  for (int m = 0; m < 6; ++m) st2(pp + m * C + c, acc[m].x, acc[m].y);
+}
+
+// mix_bwd for bf16 x and C <= 1024 with its rows streamed through shared
+// memory: one producer thread copies each work item's rows (the six mix
+// gradients' rows t0..t1-1 and x's rows t0-1..t1-1, each a contiguous run of
+// one sequence) into a ring of kRingStages stages with 1-D bulk copies behind
+// mbarriers, and the C/2 consumer threads (two columns each, as in
+// mix_bwd_kernel) compute from there.  The loads in flight then no longer
+// need registers (the register-staged kernel waits on load latency with one
+// item per thread in flight); same arithmetic and item order as
+// mix_bwd_kernel.  Waits are bounded (wkv7_sync.cuh).
+constexpr int kRingStages = 3;
+
+__host__ __device__ inline size_t ring_stage_elems(int64_t C) {  // bf16 elements of a stage
+  return static_cast<size_t>(6 * kRows + kRows + 1) * static_cast<size_t>(C);
+}
+inline size_t ring_smem(int64_t C) {
+  return 6 * static_cast<size_t>(C) * sizeof(float) + kRingStages * ring_stage_elems(C) * sizeof(bf16) +
+         2 * kRingStages * sizeof(uint64_t);
+}
+
+__global__ void __launch_bounds__(544) mix_bwd_ring_kernel(const bf16* __restrict__ x,
+                                                           const float* __restrict__ mix, In6 dout,
+                                                           bf16* __restrict__ dx,
+                                                           float* __restrict__ part, Shape S) {
+  extern __shared__ __align__(16) unsigned char ring_raw[];
+  const int64_t C = S.C;
+  const int nt = static_cast<int>(C / 2), tid = threadIdx.x, lane = tid & 31;
+  const size_t se = ring_stage_elems(C);
+  float2* mxs = reinterpret_cast<float2*>(ring_raw);  // [6][nt]
+  bf16* stages = reinterpret_cast<bf16*>(ring_raw + 6 * C * sizeof(float));
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kRingStages * se);
+  uint64_t* empty = full + kRingStages;
+  if (tid == 0) {
+    for (int s = 0; s < kRingStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], static_cast<uint32_t>(nt / 32));  // one arrival per consumer warp
+    }
+    mbar_fence_init();
+  }
+  if (tid < nt)
+#pragma unroll
+    for (int m = 0; m < 6; ++m) mxs[m * nt + tid] = ld2(mix + m * C + 2 * tid);
+  __syncthreads();
+  const int64_t n = S.items();
+  const int64_t i0 = blockIdx.x * n / gridDim.x, i1 = (blockIdx.x + 1) * n / gridDim.x;
+  const uint32_t rowb = static_cast<uint32_t>(C * sizeof(bf16));
+
+  if (tid >= nt) {  // the producer warp: its first thread copies, item by item (downwards)
+    if (tid == nt) {
+      int64_t k = 0;
+      for (int64_t item = i1 - 1; item >= i0; --item, ++k) {
+        const int s = static_cast<int>(k % kRingStages);
+        if (k >= kRingStages &&
+            !mbar_wait(&empty[s], static_cast<uint32_t>((k / kRingStages - 1) & 1)))
+          break;
+        int64_t b, t0, t1;
+        item_rows(S, item, b, t0, t1);
+        const uint32_t rows = static_cast<uint32_t>(t1 - t0);
+        const int64_t row0 = b * S.T + t0;
+        mbar_arrive_expect_tx(&full[s], 6 * rows * rowb + (rows + (t0 > 0 ? 1u : 0u)) * rowb);
+        bf16* st = stages + s * se;
+#pragma unroll
+        for (int m = 0; m < 6; ++m)
+          bulk_g2s(st + m * kRows * C, dout.p[m] + row0 * C, rows * rowb, &full[s]);
+        if (t0 > 0)  // x[t0 - 1 .. t1 - 1] at rows 0 .. rows of the x block
+          bulk_g2s(st + 6 * kRows * C, x + (row0 - 1) * C, (rows + 1) * rowb, &full[s]);
+        else         // x[-1] is zero: rows 1 .. rows
+          bulk_g2s(st + (6 * kRows + 1) * C, x + row0 * C, rows * rowb, &full[s]);
+      }
+      // keep the CTA alive until every copy it issued has landed
+      for (int64_t j = k - 1; j >= 0 && j >= k - kRingStages; --j)
+        mbar_wait(&full[j % kRingStages], static_cast<uint32_t>((j / kRingStages) & 1));
+    }
+    return;
+  }
+
+  const int c = 2 * tid;
+  const float2* mx = mxs + tid;  // mx[m * nt]
+  float2 acc[6];
+#pragma unroll
+  for (int m = 0; m < 6; ++m) acc[m] = make_float2(0.f, 0.f);
+  float2 qn = make_float2(0.f, 0.f);  // q of the row after the current item
+  int64_t k = 0;
+  for (int64_t item = i1 - 1; item >= i0; --item, ++k) {
+    int64_t b, t0, t1;
+    item_rows(S, item, b, t0, t1);
+    const int64_t row0 = b * S.T + t0;
+    const int rows = static_cast<int>(t1 - t0);
+    if (t1 == S.T) {
+      qn = make_float2(0.f, 0.f);
+    } else if (item == i1 - 1) {  // the row after the range: another CTA's
+#pragma unroll
+      for (int m = 0; m < 6; ++m) {
+        const float2 g = ld2(dout.p[m] + (row0 + rows) * C + c), w = mx[m * nt];
+        qn.x += g.x * w.x;
+        qn.y += g.y * w.y;
+      }
+    }
+    const int s = static_cast<int>(k % kRingStages);
+    if (!mbar_wait(&full[s], static_cast<uint32_t>((k / kRingStages) & 1))) break;
+    const bf16* st = stages + s * se;
+#pragma unroll
+    for (int u = kRows - 1; u >= 0; --u) {
+      if (u >= rows) continue;  // the same for the whole CTA
+      const float2 xa = u > 0 || t0 > 0 ? ld2(st + (6 * kRows + u) * C + c) : make_float2(0.f, 0.f);
+      const float2 xb = ld2(st + (6 * kRows + u + 1) * C + c);
+      const float2 xx = make_float2(xa.x - xb.x, xa.y - xb.y);
+      float2 sm = make_float2(0.f, 0.f), q = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < 6; ++m) {
+        const float2 g = ld2(st + (m * kRows + u) * C + c), w = mx[m * nt];
+        sm.x += g.x;
+        sm.y += g.y;
+        q.x += g.x * w.x;
+        q.y += g.y * w.y;
+        acc[m].x += g.x * xx.x;
+        acc[m].y += g.y * xx.y;
+      }
+      st2(dx + (row0 + u) * C + c, sm.x - q.x + qn.x, sm.y - q.y + qn.y);
+      qn = q;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage
   }
   float* pp = part + static_cast<int64_t>(blockIdx.x) * 6 * C;
 #pragma unroll
@@ -988,6 +1117,12 @@ bool with_pairs(int64_t C, F&& f) {
 }
 
 }  // namespace tm
+
+unsigned int tm_timeouts() {  // the bounded waits of this file's ring kernel
+  unsigned int n = 0;
+  if (cudaMemcpyFromSymbol(&n, g_wkv7_timeouts, sizeof(n)) != cudaSuccess) return ~0u;
+  return n;
+}
 }  // namespace camoe
 
 using camoe::bf16;
@@ -1079,12 +1214,21 @@ int camoe_tm_mix_bwd(const void* x, int x_dtype, const float* mix, const void* c
   if ((st = check_work(S, work, work_bytes)) != 0) return st;
   camoe::tm::In6 d;
   for (int m = 0; m < 6; ++m) d.p[m] = static_cast<const bf16*>(dout[m]);
+  float* part = static_cast<float*>(work);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (x_dtype == 0 && C <= 1024) {  // rows streamed through shared memory
+    const int threads = static_cast<int>(C / 2) + 32;
+    const size_t smem = camoe::tm::ring_smem(C);
+    const int G = camoe::tm::grid_for(camoe::tm::mix_bwd_ring_kernel, S, smem, threads);
+    camoe::tm::mix_bwd_ring_kernel<<<G, threads, smem, s>>>(
+        static_cast<const bf16*>(x), mix, d, static_cast<bf16*>(dx), part, S);
+    if ((st = camoe::tm::status(cudaGetLastError())) != 0) return st;
+    return camoe::tm::reduce(part, G, 6 * C, dmix, s);
+  }
   const int threads = static_cast<int>(C / 2);  // two columns per thread
   const size_t smem = 6 * static_cast<size_t>(C) * sizeof(float);  // the mixes, <= 48 KiB
   const int G = x_dtype == 0 ? camoe::tm::grid_for(camoe::tm::mix_bwd_kernel<bf16>, S, smem, threads)
                              : camoe::tm::grid_for(camoe::tm::mix_bwd_kernel<float>, S, smem, threads);
-  float* part = static_cast<float*>(work);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (x_dtype == 0)
     camoe::tm::mix_bwd_kernel<bf16><<<G, threads, smem, s>>>(
         static_cast<const bf16*>(x), mix, d, static_cast<bf16*>(dx), part, S);

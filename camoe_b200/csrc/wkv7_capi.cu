@@ -14,6 +14,7 @@ template <typename Tin>
 cudaError_t launch_bwd(const BwdArgs& p, cudaStream_t stream);
 }  // namespace scan
 unsigned int lora_timeouts();  // lora_tc.cu
+unsigned int tm_timeouts();    // timemix.cu
 namespace chunked {
 unsigned int fwd_timeouts();
 unsigned int bwd_timeouts();
@@ -102,9 +103,9 @@ int camoe_wkv7_last_cuda_error(void) { return g_last_cuda_error; }
 
 unsigned int camoe_wkv7_device_errors(void) {
   const unsigned int a = camoe::chunked::fwd_timeouts(), b = camoe::chunked::bwd_timeouts();
-  const unsigned int c = camoe::lora_timeouts();
-  if (a == ~0u || b == ~0u || c == ~0u) return ~0u;
-  return a + b + c;
+  const unsigned int c = camoe::lora_timeouts(), d = camoe::tm_timeouts();
+  if (a == ~0u || b == ~0u || c == ~0u || d == ~0u) return ~0u;
+  return a + b + c + d;
 }
 
 int camoe_wkv7_test_hooks(long long wait_limit_cycles, int skip_pair) {
